@@ -1,0 +1,333 @@
+"""Benchmark of the packed-Q4 linear hot path on B200.
+
+Default workload (the metric's layer-stack config):
+the DiT-shaped stack of 24 blocks x {qkv 3072->9216, o 3072->3072 (+bias),
+up 3072->12288 (+bias, GELU-tanh), down 12288->3072 (+bias)} Q4 linears,
+block 128, M = 4352 tokens, activations renormalised per block.  One step =
+one DMD step's pass through the stack.  At N GPUs the stack is
+tensor-parallel (column-parallel qkv/up, row-parallel o/down with an NCCL
+all-reduce); total work is fixed, so scaling is "strong".
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Prints one JSON line (rank 0).  `value` = whole-job Q4-linear TFLOP/s with
+inputs resident in HBM; `e2e` = the same through the public API with the
+step's input copied from pinned host memory and the output read back inside
+the timed region.  `--impl reference` times the CPU restatement of the
+reference's q_matmul (oracle/, OpenMP on all host cores) on a bounded sample
+of the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+HIDDEN, QKV, MLP, BLOCKS, TOKENS, QBLOCK = 3072, 9216, 12288, 24, 4352, 128
+METRIC = "Q4 linear TFLOP/s, DiT layer stack (24 blocks x qkv/o/up/down, M=4352, block 128)"
+WORKLOAD = "dit_layer_stack_24x(qkv3072x9216,o3072x3072,up3072x12288+gelu,down12288x3072)_M4352_b128"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--blocks", type=int, default=BLOCKS)
+    ap.add_argument("--tokens", type=int, default=TOKENS)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def dist_env():
+    return int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1)), int(os.environ.get("LOCAL_RANK", 0))
+
+
+# ------------------------------------------------------------------ clocks
+
+class ClockSampler:
+    """nvidia-smi sampling of SM clocks and throttle reasons during the timed region."""
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines = []
+        self.thread = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except Exception:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        if self.thread:
+            self.thread.join(timeout=2)
+        sm, smax, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax.append(float(parts[2]))
+            except ValueError:
+                continue
+            for nm, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(smax) if smax else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ------------------------------------------------------------------ CPU baseline (oracle)
+
+def cpu_sample(tokens_sample: int, repeats: int, threads: int = 0):
+    """Time the CPU restatement of the reference q_matmul (dequantize + f32
+    SGEMM + epilogue, OpenMP) on one block's four linears at `tokens_sample`
+    rows.  Returns (TFLOP/s, seconds, threads)."""
+    import numpy as np
+
+    import oracle as O
+    rng = np.random.default_rng(0)
+    shapes = [(HIDDEN, QKV, 0, False), (HIDDEN, HIDDEN, 0, True), (HIDDEN, MLP, O.ACT_GELU_TANH, True),
+              (MLP, HIDDEN, 0, True)]
+    ws = []
+    for K, N, act, has_bias in shapes:
+        words = rng.integers(0, 2 ** 32, size=(K // 8, N), dtype=np.uint64).astype(np.uint32)
+        scales = rng.uniform(0.001, 0.02, size=(K // QBLOCK, N)).astype(np.float32)
+        bias = (rng.standard_normal(N) * 0.02).astype(np.float32) if has_bias else None
+        ws.append((words, scales, K, N, act, bias))
+    x = rng.standard_normal((tokens_sample, HIDDEN), dtype=np.float32)
+    flops = 0
+    t0 = time.perf_counter()
+    for _ in range(repeats):
+        h = x
+        for i, (words, scales, K, N, act, bias) in enumerate(ws):
+            inp = h if i != 1 else h[:, -HIDDEN:]
+            inp = np.ascontiguousarray(inp)
+            h = O.cpu_linear(words, scales, K, N, QBLOCK, O.LAYOUT_ROW, inp, bias, act, threads=threads)
+            flops += 2 * tokens_sample * K * N
+    dt = time.perf_counter() - t0
+    return flops / dt / 1e12, dt, O.cpu_threads() if threads <= 0 else threads
+
+
+def run_reference(args):
+    rank, world, _ = dist_env()
+    if rank != 0:
+        return
+    import oracle as O
+    O.build()
+    tokens_sample = 64
+    for _ in range(args.warmup):
+        cpu_sample(tokens_sample, 1)
+    vals, secs = [], 0.0
+    for _ in range(args.steps):
+        v, dt, thr = cpu_sample(tokens_sample, 1)
+        vals.append(v)
+        secs += dt
+    value = statistics.median(vals)
+    flops_step = (2 * TOKENS * (HIDDEN * QKV + HIDDEN * HIDDEN + HIDDEN * MLP + MLP * HIDDEN) * args.blocks)
+    sample = (f"one block's 4 linears (qkv/o/up+gelu/down, block 128) at {tokens_sample} of {TOKENS} tokens per step; "
+              "CPU restatement of the reference q_matmul (oracle/bq4_oracle.c: dequantize + AVX2 SGEMM, OpenMP)")
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": flops_step / (value * 1e12) * 1e3, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": WORKLOAD, "tokens": TOKENS, "blocks": args.blocks, "sampled_tokens": tokens_sample,
+                   "parallelism": "cpu"},
+        "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": thr, "kind": "port", "sample": sample},
+        "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": "reference NdArray q_matmul unavailable on this box (Rust toolchain absent); oracle port timed",
+    }))
+
+
+# ------------------------------------------------------------------ GPU arm
+
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+
+    from burn_image_b200 import _lib as L
+    from burn_image_b200 import tp
+
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    group = None
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    lib = L.lib()
+
+    stack = tp.DiTQ4Stack(args.blocks, HIDDEN, QKV, MLP, dev, seed=1, block=QBLOCK, group=group)
+    M = args.tokens
+    g = torch.Generator(device=dev).manual_seed(42)
+    x0 = torch.randn((M, HIDDEN), generator=g, device=dev)
+    flops_step = stack.flops_per_token() * M
+    stream = torch.cuda.current_stream(dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+
+    # warm-up
+    for _ in range(args.warmup):
+        stack.forward(x0)
+    barrier()
+
+    # ---- timed region: inputs resident in HBM, per-linear events for the roofline
+    events = []
+
+    def on_linear(name, start):
+        ev = torch.cuda.Event(enable_timing=True)
+        ev.record(stream)
+        if start:
+            events.append([name, ev, None])
+        else:
+            events[-1][2] = ev
+
+    clocks = ClockSampler(local)
+    clocks.start()
+    barrier()
+    lib.bq4_launch_count_reset()
+    t_start = torch.cuda.Event(enable_timing=True)
+    t_end = torch.cuda.Event(enable_timing=True)
+    torch.cuda.nvtx.range_push("timed")
+    t_start.record(stream)
+    for _ in range(args.steps):
+        y = stack.forward(x0, on_linear)
+    t_end.record(stream)
+    torch.cuda.nvtx.range_pop()
+    barrier()
+    launches = int(lib.bq4_launch_count())
+    clk = clocks.stop()
+    elapsed_ms = t_start.elapsed_time(t_end)
+    t = torch.tensor([elapsed_ms], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    elapsed_ms = t.item()
+    ms_step = elapsed_ms / args.steps
+    value = flops_step / (ms_step * 1e-3) / 1e12
+
+    # per-linear kernel time (convert + GEMM launch pair of bq4_linear), local rank
+    per = {}
+    for name, a, b in events:
+        per.setdefault(name, []).append(a.elapsed_time(b))
+    lin_ms = sum(sum(v) for v in per.values())
+    lin_flops = flops_step * args.steps / world  # this rank's share
+    achieved_tflops = lin_flops / (lin_ms * 1e-3) / 1e12
+
+    # ---- e2e: through the public API with host buffers
+    x_host = x0.cpu().pin_memory()
+    y_host = torch.empty((M, HIDDEN), dtype=torch.float32).pin_memory()
+    barrier()
+    e_start = torch.cuda.Event(enable_timing=True)
+    e_end = torch.cuda.Event(enable_timing=True)
+    e_start.record(stream)
+    for _ in range(args.steps):
+        xd = x_host.to(dev, non_blocking=True)
+        yd = stack.forward(xd)
+        y_host.copy_(yd, non_blocking=True)
+    e_end.record(stream)
+    barrier()
+    e_ms = e_start.elapsed_time(e_end)
+    t = torch.tensor([e_ms], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    e2e_value = flops_step / (t.item() / args.steps * 1e-3) / 1e12
+    assert torch.isfinite(y_host).all(), "non-finite output"
+
+    peaks = {}
+    try:
+        peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
+    except Exception:
+        pass
+    peak = peaks.get("bf16_tflops_sustained")
+    peak_src = "measured sustained bf16 (MEASURED_PEAKS.json)"
+    if peak is None:
+        peak, peak_src = 1400.0, "fallback sustained"
+    traffic = None
+    try:
+        tj = json.load(open(os.path.join(ROOT, "profiles", "traffic.json")))
+        traffic = tj.get(WORKLOAD if world == 1 else f"{WORKLOAD}_tp{world}")
+    except Exception:
+        pass
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        try:
+            import oracle as O
+            O.build()
+            v, dt, thr = cpu_sample(64, 2)
+            cpu = {"value": v, "unit": "TFLOP/s", "cores": thr, "kind": "port",
+                   "sample": f"one block's 4 linears at 64 of {M} tokens, x2 ({dt:.1f} s); CPU restatement of the "
+                             "reference q_matmul (dequantize + AVX2 SGEMM, OpenMP)"}
+        except Exception as e:  # pragma: no cover
+            cpu = {"value": None, "unit": "TFLOP/s", "cores": 0, "kind": "port", "sample": f"failed: {e}"}
+
+    if rank == 0:
+        out = {
+            "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "f16 operands, f32 accumulate (Q4 weights)", "data": "synthetic",
+            "config": {"workload": WORKLOAD, "tokens": M, "blocks": args.blocks, "block": QBLOCK,
+                       "parallelism": f"tp{world}" if world > 1 else "single",
+                       "l2": "inputs larger than L2 (1.44 GB of Q4 weights streamed per step)"},
+            "roofline": {"bound": "tensor", "achieved": achieved_tflops, "peak": peak, "unit": "TFLOP/s",
+                         "frac": achieved_tflops / peak, "traffic": traffic,
+                         "peak_source": peak_src,
+                         "kernel": "bq4_linear (convert_x + q4_gemm_kernel), CUDA events per call, rank 0"},
+            "per_linear_ms": {k: sum(v) / len(v) for k, v in per.items()},
+            "e2e": {"value": e2e_value, "unit": "TFLOP/s", "h2d_bytes_per_step": M * HIDDEN * 4,
+                    "d2h_bytes_per_step": M * HIDDEN * 4},
+            "gpu_launches": launches,
+            "clocks": clk,
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(out))
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

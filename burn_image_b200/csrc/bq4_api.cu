@@ -1,0 +1,513 @@
+// bq4_api.cu -- the extern "C" boundary of libbq4 (include/bq4.h).
+//
+// Host-side validation mirrors the reference's eligibility rules and error
+// behaviour (patches/burn-cubecl-0.21.0/src/ops/qtensor.rs:303-368), except
+// that failures return a status instead of panicking.  Nothing here computes
+// on the CPU: every numeric result comes from a CUDA kernel, and calls fail
+// with BQ4_EUNSUPPORTED on devices without the sm_100a kernels.
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <new>
+#include <vector>
+
+#include "bq4_internal.h"
+
+namespace bq4 {
+
+static thread_local char g_err[512] = "no error";
+static thread_local uint64_t g_launches = 0;
+
+bq4_status set_error(bq4_status code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_err, sizeof(g_err), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+bq4_status check_cuda(cudaError_t e, const char* what) {
+  if (e == cudaSuccess) return BQ4_OK;
+  return set_error(BQ4_ECUDA, "%s: %s (%s)", what, cudaGetErrorName(e), cudaGetErrorString(e));
+}
+
+void note_launch(uint64_t n) { g_launches += n; }
+
+bq4_status poll_device_error();
+
+namespace {
+
+bool valid_block(int32_t b) { return b == 8 || b == 16 || b == 32 || b == 64 || b == 128; }
+
+bq4_status check_geometry(int64_t K, int64_t N, int32_t block, int32_t layout) {
+  if (layout != BQ4_LAYOUT_COL && layout != BQ4_LAYOUT_ROW)
+    return set_error(BQ4_EINVAL_ARG, "layout %d is not BQ4_LAYOUT_COL/ROW", layout);
+  if (!valid_block(block))
+    return set_error(BQ4_EINVAL_BLOCK, "block %d not in {8,16,32,64,128}", block);
+  if (K <= 0 || N <= 0)
+    return set_error(BQ4_EINVAL_SHAPE, "K=%lld N=%lld must be positive", (long long)K, (long long)N);
+  if (K % 8 != 0) return set_error(BQ4_EINVAL_SHAPE, "K=%lld is not a multiple of 8", (long long)K);
+  if (K % block != 0)
+    return set_error(BQ4_EINVAL_BLOCK, "block %d does not divide K=%lld", block, (long long)K);
+  if (K > (int64_t)1 << 24 || N > (int64_t)1 << 24)
+    return set_error(BQ4_EINVAL_SHAPE, "K or N above 2^24");
+  return BQ4_OK;
+}
+
+bool is_device_ptr(const void* p) {
+  cudaPointerAttributes a;
+  if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+    cudaGetLastError();
+    return false;
+  }
+  return a.type == cudaMemoryTypeDevice || a.type == cudaMemoryTypeManaged;
+}
+
+struct DeviceGuard {
+  int prev = -1;
+  explicit DeviceGuard(int dev) {
+    cudaGetDevice(&prev);
+    if (prev != dev) cudaSetDevice(dev);
+  }
+  ~DeviceGuard() {
+    int cur = -1;
+    cudaGetDevice(&cur);
+    if (prev >= 0 && cur != prev) cudaSetDevice(prev);
+  }
+};
+
+bq4_status require_sm100(int device) {
+  if (!device_is_sm100(device))
+    return set_error(BQ4_EUNSUPPORTED,
+                     "device %d is not sm_100 (B200); libbq4 has no kernels for it", device);
+  return BQ4_OK;
+}
+
+bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+// Build a prepared weight for the (n0..n0+N, k0..k0+K) window of a source
+// tensor of extents src_N x src_K.
+bq4_status prepare_window(const uint32_t* words, const float* scales, int64_t src_K, int64_t src_N,
+                          int32_t block, int32_t layout, int64_t n0, int64_t N, int64_t k0,
+                          int64_t K, int32_t device, bq4_weight** out) {
+  if (!out) return set_error(BQ4_EINVAL_ARG, "out is NULL");
+  *out = nullptr;
+  if (!words || !scales) return set_error(BQ4_EINVAL_ARG, "packed_words/scales is NULL");
+  int ndev = 0;
+  if (cudaGetDeviceCount(&ndev) != cudaSuccess || device < 0 || device >= ndev) {
+    cudaGetLastError();
+    return set_error(BQ4_EINVAL_ARG, "device %d not present", device);
+  }
+  bq4_status st = require_sm100(device);
+  if (st) return st;
+  DeviceGuard guard(device);
+
+  bq4_weight* w = new (std::nothrow) bq4_weight();
+  if (!w) return set_error(BQ4_ECUDA, "host allocation failed");
+  w->K = K;
+  w->N = N;
+  w->block = block;
+  w->layout = layout;
+  w->device = device;
+  w->Kp = (K + kChunkK - 1) / kChunkK * kChunkK;
+  w->nkc = w->Kp / kChunkK;
+  w->nkb = w->Kp / block;
+  w->ntiles = (N + kTileN - 1) / kTileN;
+  w->Np = w->ntiles * kTileN;
+  w->q_bytes = (size_t)w->ntiles * w->nkc * 1024 * sizeof(uint32_t);
+  w->s_bytes = (size_t)w->ntiles * w->nkb * 128 * sizeof(float);
+
+  const size_t src_words = (size_t)src_N * (size_t)(src_K / 8);
+  const size_t src_scales = (size_t)src_N * (size_t)(src_K / block);
+  const uint32_t* dwords = words;
+  const float* dscales = scales;
+  void* tmp_w = nullptr;
+  void* tmp_s = nullptr;
+  cudaError_t e = cudaSuccess;
+  if (!is_device_ptr(words)) {
+    e = cudaMalloc(&tmp_w, src_words * 4);
+    if (e == cudaSuccess) e = cudaMemcpy(tmp_w, words, src_words * 4, cudaMemcpyHostToDevice);
+    dwords = static_cast<const uint32_t*>(tmp_w);
+  }
+  if (e == cudaSuccess && !is_device_ptr(scales)) {
+    e = cudaMalloc(&tmp_s, src_scales * 4);
+    if (e == cudaSuccess) e = cudaMemcpy(tmp_s, scales, src_scales * 4, cudaMemcpyHostToDevice);
+    dscales = static_cast<const float*>(tmp_s);
+  }
+  if (e == cudaSuccess) e = cudaMalloc(reinterpret_cast<void**>(&w->q), w->q_bytes);
+  if (e == cudaSuccess) e = cudaMalloc(reinterpret_cast<void**>(&w->s), w->s_bytes);
+  if (e == cudaSuccess)
+    e = launch_prepare(dwords, dscales, K, N, block, layout, n0, k0, src_N, src_K, w, nullptr);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(nullptr);
+  if (tmp_w) cudaFree(tmp_w);
+  if (tmp_s) cudaFree(tmp_s);
+  if (e != cudaSuccess) {
+    if (w->q) cudaFree(w->q);
+    if (w->s) cudaFree(w->s);
+    delete w;
+    return check_cuda(e, "bq4_weight_prepare");
+  }
+  *out = w;
+  return BQ4_OK;
+}
+
+bq4_status check_weight(const bq4_weight* w, const char* name) {
+  if (!w || !w->q || !w->s) return set_error(BQ4_EINVAL_ARG, "%s is NULL or freed", name);
+  return BQ4_OK;
+}
+
+bq4_status check_compute_args(const bq4_weight* w, const float* x, int64_t M, int64_t ldx,
+                              const float* y, void* workspace) {
+  if (!x || !y) return set_error(BQ4_EINVAL_ARG, "x/y is NULL");
+  if (M <= 0) return set_error(BQ4_EINVAL_SHAPE, "M=%lld must be positive", (long long)M);
+  if (ldx < w->K)
+    return set_error(BQ4_EINVAL_SHAPE, "ldx=%lld < K=%lld", (long long)ldx, (long long)w->K);
+  if (!aligned(x, 4) || !aligned(y, 4)) return set_error(BQ4_EALIGN, "x/y not 4-byte aligned");
+  if (!workspace) return set_error(BQ4_EWORKSPACE, "workspace is NULL");
+  if (!aligned(workspace, 256)) return set_error(BQ4_EALIGN, "workspace not 256-byte aligned");
+  return BQ4_OK;
+}
+
+}  // namespace
+}  // namespace bq4
+
+using namespace bq4;
+
+extern "C" {
+
+const char* bq4_version(void) { return "bq4 0.1.0 (sm_100a tcgen05)"; }
+
+const char* bq4_last_error_string(void) { return g_err; }
+
+uint64_t bq4_launch_count(void) { return g_launches; }
+void bq4_launch_count_reset(void) { g_launches = 0; }
+
+bq4_status bq4_poll_device_error(void) { return poll_device_error(); }
+
+bq4_status bq4_weight_prepare(const uint32_t* packed_words, const float* scales, int64_t K,
+                              int64_t N, int32_t block, bq4_layout layout, int32_t device,
+                              bq4_weight** out) {
+  bq4_status st = check_geometry(K, N, block, layout);
+  if (st) return st;
+  return prepare_window(packed_words, scales, K, N, block, layout, 0, N, 0, K, device, out);
+}
+
+bq4_status bq4_weight_prepare_shard(const uint32_t* packed_words, const float* scales, int64_t K,
+                                    int64_t N, int32_t block, bq4_layout layout, int32_t kind,
+                                    int32_t rank, int32_t size, int32_t device, bq4_weight** out) {
+  bq4_status st = check_geometry(K, N, block, layout);
+  if (st) return st;
+  if (size <= 0 || rank < 0 || rank >= size)
+    return set_error(BQ4_EINVAL_ARG, "rank %d / size %d invalid", rank, size);
+  if (kind == 0) {
+    if (N % size != 0)
+      return set_error(BQ4_EINVAL_SHAPE, "column shard: N=%lld not divisible by %d", (long long)N, size);
+    const int64_t n = N / size;
+    return prepare_window(packed_words, scales, K, N, block, layout, rank * n, n, 0, K, device, out);
+  }
+  if (kind == 1) {
+    if (K % size != 0 || (K / size) % block != 0 || (K / size) % 8 != 0)
+      return set_error(BQ4_EINVAL_BLOCK,
+                       "row shard: K=%lld over %d parts does not fall on block-%d boundaries",
+                       (long long)K, size, block);
+    const int64_t k = K / size;
+    return prepare_window(packed_words, scales, K, N, block, layout, 0, N, rank * k, k, device, out);
+  }
+  return set_error(BQ4_EINVAL_ARG, "shard kind %d not 0 (column) or 1 (row)", kind);
+}
+
+bq4_status bq4_weight_free(bq4_weight* w) {
+  if (!w) return BQ4_OK;
+  DeviceGuard guard(w->device);
+  cudaError_t e1 = w->q ? cudaFree(w->q) : cudaSuccess;
+  cudaError_t e2 = w->s ? cudaFree(w->s) : cudaSuccess;
+  w->q = nullptr;
+  w->s = nullptr;
+  delete w;
+  if (e1 != cudaSuccess) return check_cuda(e1, "bq4_weight_free");
+  return check_cuda(e2, "bq4_weight_free");
+}
+
+bq4_status bq4_weight_info(const bq4_weight* w, int64_t* K, int64_t* N, int32_t* block,
+                           int32_t* layout, size_t* device_bytes) {
+  bq4_status st = check_weight(w, "w");
+  if (st) return st;
+  if (K) *K = w->K;
+  if (N) *N = w->N;
+  if (block) *block = w->block;
+  if (layout) *layout = w->layout;
+  if (device_bytes) *device_bytes = w->q_bytes + w->s_bytes;
+  return BQ4_OK;
+}
+
+bq4_status bq4_linear_workspace_size(const bq4_weight* w, int64_t M, size_t* bytes) {
+  bq4_status st = check_weight(w, "w");
+  if (st) return st;
+  if (!bytes) return set_error(BQ4_EINVAL_ARG, "bytes is NULL");
+  GemmPlan plan;
+  st = plan_gemm(w, 1, M, w->device, &plan);
+  if (st) return st;
+  *bytes = plan.workspace_bytes;
+  return BQ4_OK;
+}
+
+bq4_status bq4_linear(const bq4_weight* w, const float* x, int64_t M, int64_t ldx,
+                      const float* bias, bq4_act act, const float* aux, float* y, void* workspace,
+                      size_t workspace_bytes, bq4_stream_t stream) {
+  bq4_status st = check_weight(w, "w");
+  if (st) return st;
+  if (act != BQ4_ACT_NONE && act != BQ4_ACT_GELU_TANH && act != BQ4_ACT_SILU)
+    return set_error(BQ4_EINVAL_ARG, "act %d unknown", (int)act);
+  st = check_compute_args(w, x, M, ldx, y, workspace);
+  if (st) return st;
+  GemmPlan plan;
+  st = plan_gemm(w, 1, M, w->device, &plan);
+  if (st) return st;
+  if (workspace_bytes < plan.workspace_bytes)
+    return set_error(BQ4_EWORKSPACE, "workspace %zu < required %zu bytes", workspace_bytes,
+                     plan.workspace_bytes);
+  DeviceGuard guard(w->device);
+  const bq4_weight* ws[1] = {w};
+  const float* b[1] = {bias};
+  return run_gemm(plan, ws, x, M, ldx, b, (int)act, aux, y, workspace,
+                  reinterpret_cast<cudaStream_t>(stream));
+}
+
+bq4_status bq4_linear_gated_workspace_size(const bq4_weight* gate, const bq4_weight* up, int64_t M,
+                                           size_t* bytes) {
+  bq4_status st = check_weight(gate, "gate");
+  if (st) return st;
+  st = check_weight(up, "up");
+  if (st) return st;
+  if (!bytes) return set_error(BQ4_EINVAL_ARG, "bytes is NULL");
+  GemmPlan plan;
+  st = plan_gemm(gate, 2, M, gate->device, &plan);
+  if (st) return st;
+  *bytes = plan.workspace_bytes;
+  return BQ4_OK;
+}
+
+bq4_status bq4_linear_gated(const bq4_weight* gate, const bq4_weight* up, const float* x,
+                            int64_t M, int64_t ldx, const float* gate_bias, const float* up_bias,
+                            float* y, void* workspace, size_t workspace_bytes,
+                            bq4_stream_t stream) {
+  bq4_status st = check_weight(gate, "gate");
+  if (st) return st;
+  st = check_weight(up, "up");
+  if (st) return st;
+  if (gate->K != up->K || gate->N != up->N || gate->block != up->block || gate->device != up->device)
+    return set_error(BQ4_EINVAL_SHAPE, "gate and up weights differ in K/N/block/device");
+  st = check_compute_args(gate, x, M, ldx, y, workspace);
+  if (st) return st;
+  GemmPlan plan;
+  st = plan_gemm(gate, 2, M, gate->device, &plan);
+  if (st) return st;
+  if (workspace_bytes < plan.workspace_bytes)
+    return set_error(BQ4_EWORKSPACE, "workspace %zu < required %zu bytes", workspace_bytes,
+                     plan.workspace_bytes);
+  DeviceGuard guard(gate->device);
+  const bq4_weight* ws[2] = {gate, up};
+  const float* b[2] = {gate_bias, up_bias};
+  return run_gemm(plan, ws, x, M, ldx, b, BQ4_ACT_NONE, nullptr, y, workspace,
+                  reinterpret_cast<cudaStream_t>(stream));
+}
+
+bq4_status bq4_dequant(const bq4_weight* w, float* out, bq4_layout out_layout, bq4_stream_t stream) {
+  bq4_status st = check_weight(w, "w");
+  if (st) return st;
+  if (!out) return set_error(BQ4_EINVAL_ARG, "out is NULL");
+  if (out_layout != BQ4_LAYOUT_COL && out_layout != BQ4_LAYOUT_ROW)
+    return set_error(BQ4_EINVAL_ARG, "out_layout %d", (int)out_layout);
+  DeviceGuard guard(w->device);
+  return check_cuda(launch_dequant_prepared(w, out, out_layout, reinterpret_cast<cudaStream_t>(stream)),
+                    "bq4_dequant");
+}
+
+bq4_status bq4_dequant_raw(const uint32_t* packed_words, const float* scales, int64_t K, int64_t N,
+                           int32_t block, bq4_layout layout, float* out, bq4_layout out_layout,
+                           bq4_stream_t stream) {
+  bq4_status st = check_geometry(K, N, block, layout);
+  if (st) return st;
+  if (!packed_words || !scales || !out) return set_error(BQ4_EINVAL_ARG, "NULL pointer");
+  if (out_layout != BQ4_LAYOUT_COL && out_layout != BQ4_LAYOUT_ROW)
+    return set_error(BQ4_EINVAL_ARG, "out_layout %d", (int)out_layout);
+  int dev = 0;
+  cudaGetDevice(&dev);
+  st = require_sm100(dev);
+  if (st) return st;
+  return check_cuda(launch_dequant_raw(packed_words, scales, K, N, block, layout, out, out_layout,
+                                       reinterpret_cast<cudaStream_t>(stream)),
+                    "bq4_dequant_raw");
+}
+
+// ------------------------------------------------------------ q_matmul mirror
+
+static bq4_status check_scheme(const bq4_quant_scheme* s) {
+  // patches/burn-cubecl-0.21.0/src/ops/qtensor.rs:304-323
+  if (!s) return set_error(BQ4_EINVAL_ARG, "scheme is NULL");
+  if (s->value != 0) return set_error(BQ4_EINVAL_ARG, "scheme value is not Q4S");
+  if (s->mode != 0) return set_error(BQ4_EINVAL_ARG, "scheme mode is not Symmetric");
+  if (s->param != 0) return set_error(BQ4_EINVAL_ARG, "scheme param is not F32");
+  if (s->store_packed_dim != 0 && s->store_packed_dim != 1)
+    return set_error(BQ4_EINVAL_ARG, "scheme store is not PackedU32(0|1)");
+  if (s->block_rank != 1 && s->block_rank != 2)
+    return set_error(BQ4_EINVAL_ARG, "scheme level is not Block([b]) or Block([b,1])");
+  if (!valid_block(s->block)) return set_error(BQ4_EINVAL_BLOCK, "block %d unsupported", s->block);
+  return BQ4_OK;
+}
+
+static void q_matmul_view(int64_t K, int64_t N, int32_t block, bq4_weight* w) {
+  memset(w, 0, sizeof(*w));
+  w->K = K;
+  w->N = N;
+  w->block = block;
+  w->Kp = (K + kChunkK - 1) / kChunkK * kChunkK;
+  w->nkc = w->Kp / kChunkK;
+  w->nkb = w->Kp / block;
+  w->ntiles = (N + kTileN - 1) / kTileN;
+  w->Np = w->ntiles * kTileN;
+  w->q_bytes = (size_t)w->ntiles * w->nkc * 1024 * 4;
+  w->s_bytes = (size_t)w->ntiles * w->nkb * 128 * 4;
+}
+
+bq4_status bq4_q_matmul_workspace_size(int64_t M, int64_t K, int64_t N, int32_t block, size_t* bytes) {
+  bq4_status st = check_geometry(K, N, block, BQ4_LAYOUT_ROW);
+  if (st) return st;
+  if (!bytes) return set_error(BQ4_EINVAL_ARG, "bytes is NULL");
+  bq4_weight w;
+  q_matmul_view(K, N, block, &w);
+  int dev = 0;
+  cudaGetDevice(&dev);
+  GemmPlan plan;
+  st = plan_gemm(&w, 1, M, dev, &plan);
+  if (st) return st;
+  *bytes = (w.q_bytes + 255) / 256 * 256 + (w.s_bytes + 255) / 256 * 256 + plan.workspace_bytes;
+  return BQ4_OK;
+}
+
+bq4_status bq4_q_matmul(const float* lhs, int64_t M, int64_t K, const uint32_t* rhs_values,
+                        const float* rhs_scales, int64_t N, const bq4_quant_scheme* scheme,
+                        float* out, void* workspace, size_t workspace_bytes, bq4_stream_t stream) {
+  bq4_status st = check_scheme(scheme);
+  if (st) return st;
+  // PackedU32(0) of the logical [K,N] rhs packs along N (the reference's
+  // Qwen weight is the transposed view of a [N,K] tensor packed along K);
+  // both reach the kernel as the matching physical layout.
+  const int32_t layout = scheme->store_packed_dim == 0 ? BQ4_LAYOUT_COL : BQ4_LAYOUT_ROW;
+  st = check_geometry(K, N, scheme->block, layout);
+  if (st) return st;
+  if (!rhs_values || !rhs_scales || !lhs || !out) return set_error(BQ4_EINVAL_ARG, "NULL pointer");
+  int dev = 0;
+  cudaGetDevice(&dev);
+  st = require_sm100(dev);
+  if (st) return st;
+  bq4_weight w;
+  q_matmul_view(K, N, scheme->block, &w);
+  w.layout = layout;
+  w.device = dev;
+  size_t need = 0;
+  st = bq4_q_matmul_workspace_size(M, K, N, scheme->block, &need);
+  if (st) return st;
+  if (!workspace || workspace_bytes < need)
+    return set_error(BQ4_EWORKSPACE, "workspace %zu < required %zu bytes", workspace_bytes, need);
+  if (!aligned(workspace, 256)) return set_error(BQ4_EALIGN, "workspace not 256-byte aligned");
+  uint8_t* p = static_cast<uint8_t*>(workspace);
+  w.q = reinterpret_cast<uint32_t*>(p);
+  p += (w.q_bytes + 255) / 256 * 256;
+  w.s = reinterpret_cast<float*>(p);
+  p += (w.s_bytes + 255) / 256 * 256;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  cudaError_t e = launch_prepare(rhs_values, rhs_scales, K, N, scheme->block, layout, 0, 0, N, K, &w, s);
+  if (e != cudaSuccess) return check_cuda(e, "q_matmul prepare");
+  GemmPlan plan;
+  st = plan_gemm(&w, 1, M, dev, &plan);
+  if (st) return st;
+  const bq4_weight* ws[1] = {&w};
+  const float* b[1] = {nullptr};
+  return run_gemm(plan, ws, lhs, M, K, b, BQ4_ACT_NONE, nullptr, out, p, s);
+}
+
+// ------------------------------------------------------------ host packers
+
+int32_t bq4_row_block_for(int64_t input) {
+  static const int32_t groups[5] = {128, 64, 32, 16, 8};
+  for (int i = 0; i < 5; ++i)
+    if (input > 0 && input % groups[i] == 0) return groups[i];
+  return 0;
+}
+
+static inline int8_t q4_quantize(float v, float inverse) {
+  float q = std::round(v * inverse);  // f32::round: half away from zero
+  if (q < -7.0f) q = -7.0f;
+  if (q > 7.0f) q = 7.0f;
+  return static_cast<int8_t>(q);
+}
+
+static inline float q4_scale(float alpha) {
+  return alpha == 0.0f ? 1.17549435e-38f /* f32::MIN_POSITIVE */ : alpha / 7.0f;
+}
+
+bq4_status bq4_quantize_col_block128(const float* values, int64_t rows, int64_t inner,
+                                     uint32_t* words, float* scales) {
+  // crates/burn_qwen3_vl/src/artifacts.rs:1301-1366
+  if (!values || !words || !scales) return set_error(BQ4_EINVAL_ARG, "NULL pointer");
+  if (rows <= 0 || inner <= 0 || inner % 128 != 0)
+    return set_error(BQ4_EINVAL_SHAPE, "inner dimension %lld is not divisible by 128", (long long)inner);
+  const int64_t total = rows * inner;
+  for (int64_t i = 0; i < total; ++i)
+    if (!std::isfinite(values[i])) return set_error(BQ4_ENONFINITE, "non-finite value at %lld", (long long)i);
+  for (int64_t blk = 0; blk < total / 128; ++blk) {
+    const float* v = values + blk * 128;
+    float alpha = 0.0f;
+    for (int i = 0; i < 128; ++i) alpha = std::fmax(alpha, std::fabs(v[i]));
+    const float sc = q4_scale(alpha);
+    scales[blk] = sc;
+    const float inverse = 1.0f / sc;
+    for (int wi = 0; wi < 16; ++wi) {
+      uint32_t word = 0;
+      for (int lane = 0; lane < 8; ++lane)
+        word |= (uint32_t)((uint8_t)q4_quantize(v[wi * 8 + lane], inverse) & 0x0f) << (lane * 4);
+      words[blk * 16 + wi] = word;
+    }
+  }
+  return BQ4_OK;
+}
+
+bq4_status bq4_quantize_row_up_to128(const float* values, int64_t input, int64_t output,
+                                     uint32_t* words, float* scales, int32_t* block_out) {
+  // crates/burn_boogu/src/artifacts.rs:7296-7385
+  if (!values || !words || !scales || !block_out) return set_error(BQ4_EINVAL_ARG, "NULL pointer");
+  if (input <= 0 || output <= 0 || output % 8 != 0)
+    return set_error(BQ4_EINVAL_SHAPE, "output width %lld is not divisible by 8", (long long)output);
+  const int32_t block = bq4_row_block_for(input);
+  if (!block)
+    return set_error(BQ4_EINVAL_BLOCK, "input width %lld has no supported exact block", (long long)input);
+  for (int64_t i = 0; i < input * output; ++i)
+    if (!std::isfinite(values[i])) return set_error(BQ4_ENONFINITE, "non-finite value at %lld", (long long)i);
+  std::vector<int8_t> q((size_t)(input * output));
+  for (int64_t kb = 0; kb < input / block; ++kb) {
+    const int64_t k0 = kb * block;
+    for (int64_t n = 0; n < output; ++n) {
+      float alpha = 0.0f;
+      for (int64_t k = k0; k < k0 + block; ++k) alpha = std::fmax(alpha, std::fabs(values[k * output + n]));
+      const float sc = q4_scale(alpha);
+      scales[kb * output + n] = sc;
+      const float inverse = 1.0f / sc;
+      for (int64_t k = k0; k < k0 + block; ++k) q[k * output + n] = q4_quantize(values[k * output + n], inverse);
+    }
+  }
+  for (int64_t kw = 0; kw < input / 8; ++kw)
+    for (int64_t n = 0; n < output; ++n) {
+      uint32_t word = 0;
+      for (int lane = 0; lane < 8; ++lane)
+        word |= (uint32_t)((uint8_t)q[(kw * 8 + lane) * output + n] & 0x0f) << (lane * 4);
+      words[kw * output + n] = word;
+    }
+  *block_out = block;
+  return BQ4_OK;
+}
+
+}  // extern "C"

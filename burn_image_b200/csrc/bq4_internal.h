@@ -1,0 +1,79 @@
+// bq4_internal.h -- definitions shared by the libbq4 translation units.
+#pragma once
+#include <cstddef>
+#include <cstdint>
+#include <cuda_runtime.h>
+
+#include "../../include/bq4.h"
+
+// Prepared ("re-laid-out") weight.  Device layout, chosen so that one
+// (out-feature tile, K chunk) of nibbles is one contiguous 4 KiB block that a
+// single 1-D bulk copy brings into shared memory, and so that 128 threads
+// read it with two fully coalesced 16-byte loads each:
+//
+//   q: u32 [ntiles][nkc][2][128][4]   tile = 128 output rows (n), chunk = 64 K
+//        half h, row r, word j hold K = 64*kc + 32*h + 8*j .. +7 of row n.
+//        Inside a word the nibbles are permuted so that bits [4p,4p+3] hold
+//        logical lane kPermLane[p] = {0,2,4,6,1,3,5,7}[p]: the pair
+//        ((w >> 4i) & 0x000F000F) is then (lane 2i, lane 2i+1), i.e. two
+//        consecutive K values land in the low/high halves of an f16x2.
+//   s: f32 [ntiles][nkb][128]          scale of (row, K block), 0 in padding
+//
+// N is padded to Np = 128*ntiles and K to Kp = 64*nkc with zero nibbles and
+// zero scales; nkb = Kp / block.
+struct bq4_weight {
+  int64_t K, N;
+  int64_t Kp, Np;
+  int64_t nkc, nkb, ntiles;
+  int32_t block;
+  int32_t layout;  // source layout (informational)
+  int32_t device;
+  uint32_t* q;
+  float* s;
+  size_t q_bytes, s_bytes;
+};
+
+namespace bq4 {
+
+constexpr int kTileN = 128;   // output features per tile (MMA M)
+constexpr int kChunkK = 64;   // K per pipeline stage (128 B of f16)
+
+// Error plumbing (thread-local message, see bq4_api.cu).
+bq4_status set_error(bq4_status code, const char* fmt, ...);
+bq4_status check_cuda(cudaError_t e, const char* what);
+void note_launch(uint64_t n = 1);
+
+// ------------------------------------------------------------ kernels (bq4_kernels.cu)
+cudaError_t launch_prepare(const uint32_t* words, const float* scales, int64_t K, int64_t N,
+                           int32_t block, int32_t layout, int64_t n0, int64_t k0,
+                           int64_t src_N, int64_t src_K, const bq4_weight* w, cudaStream_t s);
+cudaError_t launch_dequant_prepared(const bq4_weight* w, float* out, int32_t out_layout,
+                                    cudaStream_t s);
+cudaError_t launch_dequant_raw(const uint32_t* words, const float* scales, int64_t K, int64_t N,
+                               int32_t block, int32_t layout, float* out, int32_t out_layout,
+                               cudaStream_t s);
+// x f32 [M][ldx] -> xh f16 [M][Kp] (zero padded); also zeroes `counters`.
+cudaError_t launch_convert_x(const float* x, int64_t M, int64_t K, int64_t ldx, int64_t Kp,
+                             void* xh, int* counters, int ncounters, cudaStream_t s);
+
+// ------------------------------------------------------------ GEMM (bq4_gemm_sm100.cu)
+struct GemmPlan {
+  int nw;          // 1 = plain, 2 = gated (gate, up)
+  int bt;          // tokens per tile (MMA N): 64, 128 or 256
+  int mtiles, ntiles, ksplit, units, grid;
+  int stages, raw_stages;
+  size_t smem_bytes;
+  size_t xh_bytes, counter_bytes, partial_bytes;  // workspace pieces
+  size_t workspace_bytes;
+};
+
+bq4_status plan_gemm(const bq4_weight* w, int nw, int64_t M, int device, GemmPlan* plan);
+
+bq4_status run_gemm(const GemmPlan& plan, const bq4_weight* const* ws, const float* x, int64_t M,
+                    int64_t ldx, const float* const* bias, int act, const float* aux, float* y,
+                    void* workspace, cudaStream_t stream);
+
+int device_sm_count(int device);
+int device_is_sm100(int device);
+
+}  // namespace bq4

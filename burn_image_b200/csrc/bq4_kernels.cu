@@ -1,0 +1,221 @@
+// bq4_kernels.cu -- load-time re-layout, bit-exact dequantization and the
+// activation f32 -> f16 staging pass.  All HBM-bound byte work: 128-bit
+// accesses where the layout allows, grids sized in multiples of the SM count.
+#include <cuda_fp16.h>
+
+#include "bq4_internal.h"
+
+namespace bq4 {
+namespace {
+
+// Logical lane stored at nibble position p of a prepared word.
+__device__ __constant__ int kPermLane[8] = {0, 2, 4, 6, 1, 3, 5, 7};
+
+__device__ __forceinline__ int32_t nibble_s4(uint32_t word, int lane) {
+  // Sign-extend the 4-bit two's-complement value at bits [4*lane, 4*lane+3].
+  return static_cast<int32_t>(word << (28 - 4 * lane)) >> 28;
+}
+
+__device__ __forceinline__ uint32_t raw_word(const uint32_t* words, int32_t layout, int64_t n,
+                                             int64_t kw, int64_t src_N, int64_t src_KW) {
+  return layout == BQ4_LAYOUT_COL ? words[n * src_KW + kw] : words[kw * src_N + n];
+}
+
+__device__ __forceinline__ float raw_scale(const float* scales, int32_t layout, int64_t n,
+                                           int64_t kb, int64_t src_N, int64_t src_KB) {
+  return layout == BQ4_LAYOUT_COL ? scales[n * src_KB + kb] : scales[kb * src_N + n];
+}
+
+// One thread per prepared word.  The shard is rows [n0, n0+N) and K range
+// [k0, k0+K) of a source weight whose full extents are src_N x src_K.
+__global__ void prepare_q_kernel(const uint32_t* __restrict__ words, int32_t layout, int64_t N,
+                                 int64_t K, int64_t n0, int64_t k0, int64_t src_N, int64_t src_K,
+                                 int64_t nkc, int64_t total, uint32_t* __restrict__ out) {
+  const int64_t src_KW = src_K / 8;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t j = i & 3;
+    const int64_t r = (i >> 2) & 127;
+    const int64_t h = (i >> 9) & 1;
+    const int64_t kc = (i >> 10) % nkc;
+    const int64_t tile = (i >> 10) / nkc;
+    const int64_t n = tile * 128 + r;
+    const int64_t kw = kc * 8 + h * 4 + j;  // word index inside the shard
+    uint32_t v = 0;
+    if (n < N && kw * 8 < K) {
+      const uint32_t src = raw_word(words, layout, n0 + n, k0 / 8 + kw, src_N, src_KW);
+#pragma unroll
+      for (int p = 0; p < 8; ++p) v |= ((src >> (4 * kPermLane[p])) & 0xFu) << (4 * p);
+    }
+    out[i] = v;
+  }
+}
+
+__global__ void prepare_s_kernel(const float* __restrict__ scales, int32_t layout, int64_t N,
+                                 int64_t K, int32_t block, int64_t n0, int64_t k0, int64_t src_N,
+                                 int64_t src_K, int64_t nkb, int64_t total, float* __restrict__ out) {
+  const int64_t src_KB = src_K / block;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = i & 127;
+    const int64_t kb = (i >> 7) % nkb;
+    const int64_t tile = (i >> 7) / nkb;
+    const int64_t n = tile * 128 + r;
+    float v = 0.0f;
+    if (n < N && kb * block < K) v = raw_scale(scales, layout, n0 + n, k0 / block + kb, src_N, src_KB);
+    out[i] = v;
+  }
+}
+
+// Dequantize from the prepared layout.  One thread per output element of
+// the logical tensor: out_layout ROW -> [K][N], COL -> [N][K].
+__global__ void dequant_prepared_kernel(const uint32_t* __restrict__ q, const float* __restrict__ s,
+                                        int64_t K, int64_t N, int64_t nkc, int64_t nkb,
+                                        int32_t block, int32_t out_layout,
+                                        float* __restrict__ out) {
+  const int64_t total = K * N;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    int64_t k, n;
+    if (out_layout == BQ4_LAYOUT_ROW) {
+      k = i / N;
+      n = i - k * N;
+    } else {
+      n = i / K;
+      k = i - n * K;
+    }
+    const int64_t tile = n >> 7, r = n & 127;
+    const int64_t kc = k >> 6, within = k & 63;
+    const int64_t h = within >> 5, j = (within >> 3) & 3, lane = k & 7;
+    const uint32_t word = q[((((tile * nkc + kc) * 2 + h) * 128 + r) << 2) + j];
+    // logical lane -> stored position: pos = {0,4,1,5,2,6,3,7}[lane]
+    const int pos = (lane >> 1) + ((lane & 1) << 2);
+    const int32_t qv = nibble_s4(word, pos);
+    const float sc = s[(tile * nkb + k / block) * 128 + r];
+    out[i] = static_cast<float>(qv) * sc;
+  }
+}
+
+__global__ void dequant_raw_kernel(const uint32_t* __restrict__ words, const float* __restrict__ scales,
+                                   int64_t K, int64_t N, int32_t block, int32_t layout,
+                                   int32_t out_layout, float* __restrict__ out) {
+  const int64_t total = K * N;
+  const int64_t KW = K / 8, KB = K / block;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    int64_t k, n;
+    if (out_layout == BQ4_LAYOUT_ROW) {
+      k = i / N;
+      n = i - k * N;
+    } else {
+      n = i / K;
+      k = i - n * K;
+    }
+    const uint32_t word = raw_word(words, layout, n, k >> 3, N, KW);
+    const float sc = raw_scale(scales, layout, n, k / block, N, KB);
+    out[i] = static_cast<float>(nibble_s4(word, static_cast<int>(k & 7))) * sc;
+  }
+}
+
+// x f32 [M][ldx] -> xh f16 [M][Kp] with round-to-nearest-even, zero padding
+// K..Kp-1.  Each thread converts 8 consecutive K values into one 16-byte
+// store.  Block 0 also zeroes the split-K tile counters.
+__global__ void convert_x_kernel(const float* __restrict__ x, int64_t M, int64_t K, int64_t ldx,
+                                 int64_t Kp, uint4* __restrict__ xh, int* __restrict__ counters,
+                                 int ncounters, int vec4) {
+  if (blockIdx.x == 0)
+    for (int i = threadIdx.x; i < ncounters; i += blockDim.x) counters[i] = 0;
+  const int64_t per_row = Kp / 8;
+  const int64_t total = M * per_row;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t m = i / per_row;
+    const int64_t k = (i - m * per_row) * 8;
+    float v[8];
+    const float* src = x + m * ldx + k;
+    if (k + 8 <= K && vec4) {
+      const float4 a = __ldg(reinterpret_cast<const float4*>(src));
+      const float4 b = __ldg(reinterpret_cast<const float4*>(src) + 1);
+      v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+      v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+    } else {
+#pragma unroll
+      for (int t = 0; t < 8; ++t) v[t] = (k + t < K) ? __ldg(src + t) : 0.0f;
+    }
+    uint4 o;
+    __half2 h0 = __floats2half2_rn(v[0], v[1]);
+    __half2 h1 = __floats2half2_rn(v[2], v[3]);
+    __half2 h2 = __floats2half2_rn(v[4], v[5]);
+    __half2 h3 = __floats2half2_rn(v[6], v[7]);
+    o.x = *reinterpret_cast<uint32_t*>(&h0);
+    o.y = *reinterpret_cast<uint32_t*>(&h1);
+    o.z = *reinterpret_cast<uint32_t*>(&h2);
+    o.w = *reinterpret_cast<uint32_t*>(&h3);
+    xh[i] = o;
+  }
+}
+
+int grid_for(int64_t total, int threads, int device) {
+  const int sms = device_sm_count(device);
+  int64_t blocks = (total + threads - 1) / threads;
+  const int64_t cap = static_cast<int64_t>(sms) * 16;
+  if (blocks > cap) blocks = cap;
+  if (blocks < 1) blocks = 1;
+  return static_cast<int>(blocks);
+}
+
+int current_device() {
+  int d = 0;
+  cudaGetDevice(&d);
+  return d;
+}
+
+}  // namespace
+
+cudaError_t launch_prepare(const uint32_t* words, const float* scales, int64_t K, int64_t N,
+                           int32_t block, int32_t layout, int64_t n0, int64_t k0, int64_t src_N,
+                           int64_t src_K, const bq4_weight* w, cudaStream_t s) {
+  const int dev = current_device();
+  const int64_t qtotal = w->ntiles * w->nkc * 1024;
+  prepare_q_kernel<<<grid_for(qtotal, 256, dev), 256, 0, s>>>(words, layout, N, K, n0, k0, src_N,
+                                                               src_K, w->nkc, qtotal, w->q);
+  note_launch();
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  const int64_t stotal = w->ntiles * w->nkb * 128;
+  prepare_s_kernel<<<grid_for(stotal, 256, dev), 256, 0, s>>>(scales, layout, N, K, block, n0, k0,
+                                                               src_N, src_K, w->nkb, stotal, w->s);
+  note_launch();
+  return cudaGetLastError();
+}
+
+cudaError_t launch_dequant_prepared(const bq4_weight* w, float* out, int32_t out_layout,
+                                    cudaStream_t s) {
+  const int64_t total = w->K * w->N;
+  dequant_prepared_kernel<<<grid_for(total, 256, w->device), 256, 0, s>>>(
+      w->q, w->s, w->K, w->N, w->nkc, w->nkb, w->block, out_layout, out);
+  note_launch();
+  return cudaGetLastError();
+}
+
+cudaError_t launch_dequant_raw(const uint32_t* words, const float* scales, int64_t K, int64_t N,
+                               int32_t block, int32_t layout, float* out, int32_t out_layout,
+                               cudaStream_t s) {
+  const int64_t total = K * N;
+  dequant_raw_kernel<<<grid_for(total, 256, current_device()), 256, 0, s>>>(
+      words, scales, K, N, block, layout, out_layout, out);
+  note_launch();
+  return cudaGetLastError();
+}
+
+cudaError_t launch_convert_x(const float* x, int64_t M, int64_t K, int64_t ldx, int64_t Kp,
+                             void* xh, int* counters, int ncounters, cudaStream_t s) {
+  const int vec4 = ((reinterpret_cast<uintptr_t>(x) & 15) == 0) && (ldx % 4 == 0);
+  const int64_t total = M * (Kp / 8);
+  convert_x_kernel<<<grid_for(total, 256, current_device()), 256, 0, s>>>(
+      x, M, K, ldx, Kp, reinterpret_cast<uint4*>(xh), counters, ncounters, vec4);
+  note_launch();
+  return cudaGetLastError();
+}
+
+}  // namespace bq4

@@ -1,0 +1,377 @@
+"""Host-side mirror of burn_image's packed-Q4 linear interface over libbq4.
+
+Names and argument meanings follow the reference so that parity tests read
+like the reference's own tests:
+
+* ``quantize_q4s_block128_f32`` -- Qwen column-layout packer
+  (crates/burn_qwen3_vl/src/artifacts.rs:1301-1366)
+* ``quantize_row_layout_q4s_block_up_to128_f32`` -- Boogu row-layout packer
+  (crates/burn_boogu/src/artifacts.rs:7296-7385)
+* ``QuantizedTensor`` / ``QuantScheme`` -- a QFloat tensor (packed u32 values
+  plus F32 scales, patches/burn-cubecl-0.21.0/src/ops/qtensor.rs:64-158)
+* ``q_matmul`` -- ``QTensorOps::q_matmul`` (qtensor.rs:303-368)
+* ``Q4Linear`` + ``linear_forward`` / ``qwen_linear_forward`` -- the linear
+  adapters (crates/burn_boogu/src/model/linear.rs:14-37,
+  crates/burn_qwen3_vl/src/linear.rs:107-140), with the bias and activation
+  fused into the kernel epilogue.
+
+Device memory and streams come from PyTorch; all arithmetic is done by the
+CUDA kernels in libbq4.so.  Tensors must live on an sm_100 CUDA device.
+"""
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass, field
+from typing import Optional, Sequence
+
+import numpy as np
+import torch
+
+from . import _lib as L
+from ._lib import Bq4Error, check
+
+VALUES_PER_WORD = 8
+SUPPORTED_BLOCKS = (8, 16, 32, 64, 128)
+
+
+def _ptr(t: Optional[torch.Tensor]):
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def _stream_ptr(device: torch.device):
+    return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+
+
+# --------------------------------------------------------------------- packers
+
+@dataclass
+class PackedQ4:
+    """Reference byte stream split into its two parts: ``words`` (u32, the
+    first N*K/2 bytes) and ``scales`` (f32, the rest), plus the scheme."""
+    words: np.ndarray
+    scales: np.ndarray
+    shape: tuple
+    scheme: "QuantScheme"
+
+    def to_bytes(self) -> bytes:
+        return self.words.astype("<u4").tobytes() + self.scales.astype("<f4").tobytes()
+
+
+def quantize_q4s_block128_f32(values, shape: Sequence[int]) -> PackedQ4:
+    """Column layout (Qwen, ``PackedU32(0)``, ``Block([128])``): the last axis
+    is packed, one F32 scale per contiguous 128-block."""
+    v = np.ascontiguousarray(np.asarray(values, dtype=np.float32)).reshape(-1)
+    shape = tuple(int(s) for s in shape)
+    if len(shape) == 0:
+        raise Bq4Error(L.EINVAL_SHAPE, "Q4S block tensor must have at least one dimension")
+    if int(np.prod(shape)) != v.size:
+        raise Bq4Error(L.EINVAL_SHAPE, f"Q4S shape {shape} describes {int(np.prod(shape))} elements, received {v.size}")
+    inner = shape[-1]
+    rows = v.size // inner if inner else 0
+    words = np.zeros(max(v.size // 8, 1), dtype=np.uint32)
+    scales = np.zeros(max(v.size // 128, 1), dtype=np.float32)
+    check(L.lib().bq4_quantize_col_block128(v.ctypes.data_as(ctypes.c_void_p), rows, inner,
+                                            words.ctypes.data_as(ctypes.c_void_p),
+                                            scales.ctypes.data_as(ctypes.c_void_p)))
+    return PackedQ4(words, scales, shape, QuantScheme(store_packed_dim=0, level=(128,)))
+
+
+def quantize_row_layout_q4s_block_up_to128_f32(values, shape: Sequence[int]) -> PackedQ4:
+    """Row layout (Boogu, ``PackedU32(1)``, ``Block([b,1])``) of a [input,
+    output] matrix; b = largest of 128/64/32/16/8 dividing input."""
+    v = np.ascontiguousarray(np.asarray(values, dtype=np.float32)).reshape(-1)
+    shape = tuple(int(s) for s in shape)
+    if len(shape) != 2:
+        raise Bq4Error(L.EINVAL_SHAPE, f"runtime Q4S denoiser quantization requires a rank-two matrix, found {shape}")
+    K, N = shape
+    b = int(L.lib().bq4_row_block_for(K)) or 8
+    words = np.zeros(max(K // 8 * N, 1), dtype=np.uint32)
+    scales = np.zeros(max(K // b * N, 1), dtype=np.float32)
+    blk = ctypes.c_int32(0)
+    check(L.lib().bq4_quantize_row_up_to128(v.ctypes.data_as(ctypes.c_void_p), K, N,
+                                            words.ctypes.data_as(ctypes.c_void_p),
+                                            scales.ctypes.data_as(ctypes.c_void_p), ctypes.byref(blk)))
+    return PackedQ4(words, scales, shape, QuantScheme(store_packed_dim=1, level=(int(blk.value), 1)))
+
+
+# --------------------------------------------------------------------- scheme
+
+@dataclass(frozen=True)
+class QuantScheme:
+    """The QuantScheme fields on this path (burn-std 0.21): Q4S values,
+    Symmetric mode, F32 params, PackedU32(store_packed_dim), Block(level)."""
+    value: str = "Q4S"
+    mode: str = "Symmetric"
+    param: str = "F32"
+    store_packed_dim: int = 0
+    level: tuple = (128,)
+
+    @property
+    def block(self) -> int:
+        return int(self.level[0])
+
+    def eligible(self) -> bool:
+        """qtensor.rs:304-323 -- the packed-Q4 kernel's eligibility test."""
+        lvl_ok = (len(self.level) == 1 or (len(self.level) == 2 and self.level[1] == 1)) and \
+            self.level[0] in SUPPORTED_BLOCKS
+        return (self.mode == "Symmetric" and self.value == "Q4S" and self.param == "F32"
+                and self.store_packed_dim in (0, 1) and lvl_ok)
+
+    def to_c(self) -> L.QuantScheme:
+        return L.QuantScheme(value=0 if self.value == "Q4S" else 99,
+                             mode=0 if self.mode == "Symmetric" else 99,
+                             param=0 if self.param == "F32" else 99,
+                             store_packed_dim=self.store_packed_dim,
+                             block_rank=len(self.level) if (len(self.level) == 1 or self.level[-1] == 1) else 99,
+                             block=self.block)
+
+
+# --------------------------------------------------------------------- workspace
+
+class Workspace:
+    """Grow-only device scratch per (device, stream).  The C ABI never
+    allocates on compute calls; this host helper owns the memory it passes."""
+    _cache: dict = {}
+
+    @classmethod
+    def get(cls, device: torch.device, nbytes: int) -> torch.Tensor:
+        key = (device.index, torch.cuda.current_stream(device).cuda_stream)
+        buf = cls._cache.get(key)
+        if buf is None or buf.numel() < nbytes:
+            buf = torch.empty(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
+            cls._cache[key] = buf
+        return buf
+
+    @classmethod
+    def clear(cls):
+        cls._cache.clear()
+
+
+# --------------------------------------------------------------------- weights
+
+class PreparedQ4Weight:
+    """A weight re-laid-out once into the kernels' device layout (the loader
+    hook of the north star).  ``K`` input width, ``N`` output width."""
+
+    def __init__(self, words, scales, K: int, N: int, block: int, layout: int,
+                 device: Optional[torch.device] = None, shard: Optional[tuple] = None):
+        dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+        if dev.type != "cuda":
+            raise Bq4Error(L.EINVAL_ARG, "prepared Q4 weights live on a CUDA device")
+        w = torch.as_tensor(np.ascontiguousarray(words).view(np.int32)) if isinstance(words, np.ndarray) else words
+        s = torch.as_tensor(np.ascontiguousarray(scales, dtype=np.float32)) if isinstance(scales, np.ndarray) else scales
+        w = w.contiguous()
+        s = s.contiguous()
+        handle = ctypes.c_void_p()
+        lib = L.lib()
+        if shard is None:
+            check(lib.bq4_weight_prepare(_ptr(w), _ptr(s), K, N, block, layout, dev.index, ctypes.byref(handle)))
+        else:
+            kind, rank, size = shard
+            check(lib.bq4_weight_prepare_shard(_ptr(w), _ptr(s), K, N, block, layout, kind, rank, size,
+                                               dev.index, ctypes.byref(handle)))
+        self._h = handle
+        k, n, b, lay, nb = ctypes.c_int64(), ctypes.c_int64(), ctypes.c_int32(), ctypes.c_int32(), ctypes.c_size_t()
+        check(lib.bq4_weight_info(handle, ctypes.byref(k), ctypes.byref(n), ctypes.byref(b), ctypes.byref(lay),
+                                  ctypes.byref(nb)))
+        self.K, self.N, self.block, self.layout, self.device_bytes = k.value, n.value, b.value, lay.value, nb.value
+        self.device = dev
+
+    @classmethod
+    def from_packed(cls, packed: PackedQ4, device=None) -> "PreparedQ4Weight":
+        layout = L.LAYOUT_COL if packed.scheme.store_packed_dim == 0 else L.LAYOUT_ROW
+        if layout == L.LAYOUT_COL:
+            N, K = packed.shape[-2], packed.shape[-1]
+        else:
+            K, N = packed.shape
+        return cls(packed.words, packed.scales, K, N, packed.scheme.block, layout, device)
+
+    @property
+    def handle(self):
+        return self._h
+
+    def free(self):
+        if getattr(self, "_h", None) is not None and self._h.value:
+            L.lib().bq4_weight_free(self._h)
+            self._h = ctypes.c_void_p()
+
+    def __del__(self):
+        try:
+            self.free()
+        except Exception:
+            pass
+
+    def dequantize(self, out_layout: int = L.LAYOUT_ROW) -> torch.Tensor:
+        shape = (self.K, self.N) if out_layout == L.LAYOUT_ROW else (self.N, self.K)
+        out = torch.empty(shape, dtype=torch.float32, device=self.device)
+        check(L.lib().bq4_dequant(self._h, _ptr(out), out_layout, _stream_ptr(self.device)))
+        return out
+
+    def workspace_bytes(self, M: int) -> int:
+        n = ctypes.c_size_t()
+        check(L.lib().bq4_linear_workspace_size(self._h, M, ctypes.byref(n)))
+        return n.value
+
+    def linear(self, x: torch.Tensor, bias: Optional[torch.Tensor] = None, act: int = L.ACT_NONE,
+               aux: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """y = act(x . W + bias) (* aux) over the last axis of x (leading dims flattened)."""
+        x2, lead = _as_rows(x, self.K, self.device)
+        M = x2.shape[0]
+        y = out if out is not None else torch.empty((M, self.N), dtype=torch.float32, device=self.device)
+        _check_out(y, M, self.N, self.device)
+        if bias is not None:
+            bias = _vec(bias, self.N, self.device)
+        if aux is not None:
+            aux = aux.reshape(M, self.N)
+            _check_out(aux, M, self.N, self.device)
+        nbytes = self.workspace_bytes(M)
+        ws = Workspace.get(self.device, nbytes)
+        check(L.lib().bq4_linear(self._h, _ptr(x2), M, x2.stride(0), _ptr(bias), act, _ptr(aux), _ptr(y),
+                                 _ptr(ws), ws.numel(), _stream_ptr(self.device)))
+        return y.reshape(*lead, self.N)
+
+
+def linear_gated(gate: PreparedQ4Weight, up: PreparedQ4Weight, x: torch.Tensor,
+                 gate_bias: Optional[torch.Tensor] = None, up_bias: Optional[torch.Tensor] = None,
+                 out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """silu(x . Wg + bg) * (x . Wu + bu) in one kernel (SwiGLU front half)."""
+    x2, lead = _as_rows(x, gate.K, gate.device)
+    M = x2.shape[0]
+    y = out if out is not None else torch.empty((M, gate.N), dtype=torch.float32, device=gate.device)
+    _check_out(y, M, gate.N, gate.device)
+    n = ctypes.c_size_t()
+    check(L.lib().bq4_linear_gated_workspace_size(gate.handle, up.handle, M, ctypes.byref(n)))
+    ws = Workspace.get(gate.device, n.value)
+    gb = _vec(gate_bias, gate.N, gate.device) if gate_bias is not None else None
+    ub = _vec(up_bias, gate.N, gate.device) if up_bias is not None else None
+    check(L.lib().bq4_linear_gated(gate.handle, up.handle, _ptr(x2), M, x2.stride(0), _ptr(gb), _ptr(ub),
+                                   _ptr(y), _ptr(ws), ws.numel(), _stream_ptr(gate.device)))
+    return y.reshape(*lead, gate.N)
+
+
+def _as_rows(x: torch.Tensor, K: int, device: torch.device):
+    if x.device != device or x.dtype != torch.float32:
+        raise Bq4Error(L.EINVAL_ARG, f"x must be float32 on {device}, got {x.dtype} on {x.device}")
+    if x.dim() < 1 or x.shape[-1] != K:
+        raise Bq4Error(L.EINVAL_SHAPE, f"x last dim {tuple(x.shape)} != K={K}")
+    lead = tuple(x.shape[:-1])
+    x2 = x.reshape(-1, K)
+    if x2.stride(1) != 1 or x2.stride(0) < K:
+        x2 = x2.contiguous()
+    return x2, lead
+
+
+def _check_out(t: torch.Tensor, M: int, N: int, device: torch.device):
+    if t.device != device or t.dtype != torch.float32 or not t.is_contiguous() or t.numel() != M * N:
+        raise Bq4Error(L.EINVAL_ARG, f"output/aux must be contiguous float32 [{M},{N}] on {device}")
+
+
+def _vec(v: torch.Tensor, n: int, device: torch.device) -> torch.Tensor:
+    if v.device != device or v.dtype != torch.float32 or v.numel() != n:
+        raise Bq4Error(L.EINVAL_ARG, f"bias must be float32 [{n}] on {device}")
+    return v.contiguous()
+
+
+# --------------------------------------------------------------------- QFloat tensor + q_matmul
+
+@dataclass
+class QuantizedTensor:
+    """A QFloat tensor as burn-cubecl stores it: u32 ``values`` and F32
+    ``scales`` on the device, a logical ``shape`` and its ``scheme``.
+    ``shape`` is the logical [K, N] the matmul sees (the Qwen weight is the
+    transposed view of its stored [N, K] tensor)."""
+    values: torch.Tensor
+    scales: torch.Tensor
+    shape: tuple
+    scheme: QuantScheme
+    _prepared: Optional[PreparedQ4Weight] = field(default=None, repr=False)
+
+    @classmethod
+    def from_packed(cls, packed: PackedQ4, device) -> "QuantizedTensor":
+        dev = torch.device(device)
+        values = torch.as_tensor(packed.words.view(np.int32)).to(dev)
+        scales = torch.as_tensor(packed.scales).to(dev)
+        if packed.scheme.store_packed_dim == 0:
+            N, K = packed.shape[-2], packed.shape[-1]
+        else:
+            K, N = packed.shape
+        return cls(values, scales, (K, N), packed.scheme)
+
+    def prepared(self) -> PreparedQ4Weight:
+        if self._prepared is None:
+            K, N = self.shape
+            layout = L.LAYOUT_COL if self.scheme.store_packed_dim == 0 else L.LAYOUT_ROW
+            self._prepared = PreparedQ4Weight(self.values, self.scales, K, N, self.scheme.block, layout,
+                                              self.values.device)
+        return self._prepared
+
+
+def q_matmul(lhs: torch.Tensor, rhs: QuantizedTensor) -> torch.Tensor:
+    """QTensorOps::q_matmul for an f32 lhs [..., M, K] and a packed-Q4 rhs
+    [K, N] (batch-broadcast over the leading dims, like the weight reshaped
+    to rank D in linear_forward).  Ineligible schemes raise (the reference
+    would select its generic quantized path, which has no B200 counterpart).
+    Goes through the C ABI entry ``bq4_q_matmul`` (prepare + GEMM per call)."""
+    if lhs.dtype != torch.float32:
+        raise Bq4Error(L.EINVAL_ARG, f"lhs dtype {lhs.dtype} is not F32")
+    if not rhs.scheme.eligible():
+        raise Bq4Error(L.EINVAL_ARG, f"scheme {rhs.scheme} is not eligible for the packed-Q4 kernel")
+    K, N = rhs.shape
+    if lhs.dim() < 2 or lhs.shape[-1] != K:
+        raise Bq4Error(L.EINVAL_SHAPE, f"lhs {tuple(lhs.shape)} does not match rhs [{K},{N}]")
+    lead = tuple(lhs.shape[:-1])
+    x = lhs.reshape(-1, K).contiguous()  # qtensor.rs:345-349 makes lhs contiguous
+    M = x.shape[0]
+    out = torch.empty((M, N), dtype=torch.float32, device=lhs.device)
+    nbytes = ctypes.c_size_t()
+    with torch.cuda.device(lhs.device):
+        check(L.lib().bq4_q_matmul_workspace_size(M, K, N, rhs.scheme.block, ctypes.byref(nbytes)))
+        ws = Workspace.get(lhs.device, nbytes.value)
+        sch = rhs.scheme.to_c()
+        check(L.lib().bq4_q_matmul(_ptr(x), M, K, _ptr(rhs.values), _ptr(rhs.scales), N, ctypes.byref(sch),
+                                   _ptr(out), _ptr(ws), ws.numel(), _stream_ptr(lhs.device)))
+    return out.reshape(*lead, N)
+
+
+# --------------------------------------------------------------------- linear adapters
+
+class Q4Linear:
+    """A linear layer whose weight is a packed-Q4 QFloat tensor ([input,
+    output] logical) with an optional F32 bias -- the nn::Linear / QwenLinear
+    the adapters receive."""
+
+    def __init__(self, weight: QuantizedTensor, bias: Optional[torch.Tensor] = None):
+        self.weight = weight
+        self.bias = bias
+
+    @property
+    def dims(self):
+        return self.weight.shape
+
+
+def linear_forward(linear: Q4Linear, input: torch.Tensor, act: int = L.ACT_NONE) -> torch.Tensor:
+    """crates/burn_boogu/src/model/linear.rs:14-37 -- rank >= 2 input, matmul
+    against the prepared Q4 weight, bias added (fused into the epilogue)."""
+    if input.dim() < 2:
+        raise Bq4Error(L.EINVAL_SHAPE, "Boogu linear projections require rank >= 2")
+    return linear.weight.prepared().linear(input, linear.bias, act)
+
+
+def qwen_linear_forward(linear: Q4Linear, input: torch.Tensor, act: int = L.ACT_NONE) -> torch.Tensor:
+    """crates/burn_qwen3_vl/src/linear.rs:107-140 -- same contract for the
+    Qwen column layout (transposed view of the stored [N, K] weight)."""
+    if input.dim() < 2:
+        raise Bq4Error(L.EINVAL_SHAPE, "Qwen linear projections require rank >= 2")
+    return linear.weight.prepared().linear(input, linear.bias, act)
+
+
+def feed_forward_swiglu(l1: Q4Linear, l3: Q4Linear, l2: Q4Linear, x: torch.Tensor) -> torch.Tensor:
+    """crates/burn_boogu/src/model/feed_forward.rs:32-36:
+    linear_2(silu(linear_1(x)) * linear_3(x)), with the gate fused."""
+    gated = linear_gated(l1.weight.prepared(), l3.weight.prepared(), x, l1.bias, l3.bias)
+    return linear_forward(l2, gated)
+
+
+def poll_device_error() -> None:
+    """Raise if a kernel's bounded device-side wait expired since the last poll."""
+    check(L.lib().bq4_poll_device_error())

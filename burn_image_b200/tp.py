@@ -1,0 +1,187 @@
+"""Tensor-parallel packed-Q4 linears over torch.distributed (NCCL on NVLink).
+
+Column-parallel (qkv, up): each rank holds N/P output features of the
+weight, with their scale columns; the output stays sharded.  Row-parallel
+(o, down): each rank holds K/P input features, cut on quant-block
+boundaries (K/P % block == 0); partial f32 outputs are summed with one
+all-reduce, the bias is added once (by rank 0's epilogue).
+
+The reference runs single-device (it has no distributed code); this module
+is the B200 multi-GPU layer around the same op.  Shards are prepared
+straight from the full reference-packed buffers by the C ABI
+(bq4_weight_prepare_shard), so no host round trip is needed.
+"""
+from __future__ import annotations
+
+import ctypes
+from typing import Optional
+
+import numpy as np
+import torch
+import torch.distributed as dist
+
+from . import _lib as L
+from .q4 import PreparedQ4Weight, Workspace, _ptr, _stream_ptr
+
+COLUMN, ROW = 0, 1
+
+
+def column_shard_bounds(N: int, rank: int, size: int):
+    """Output-feature range [n0, n1) of `rank` in a column-parallel split."""
+    if N % size:
+        raise ValueError(f"column shard: N={N} not divisible by {size}")
+    n = N // size
+    return rank * n, (rank + 1) * n
+
+
+def row_shard_bounds(K: int, block: int, rank: int, size: int):
+    """Input-feature range [k0, k1) of `rank` in a row-parallel split; the
+    cut must fall on quant-block (and 8-value word) boundaries."""
+    if K % size or (K // size) % block or (K // size) % 8:
+        raise ValueError(f"row shard: K={K} over {size} ranks does not fall on block-{block} boundaries")
+    k = K // size
+    return rank * k, (rank + 1) * k
+
+
+def slice_raw(words: np.ndarray, scales: np.ndarray, K: int, N: int, block: int, layout: int,
+              n0: int, n1: int, k0: int, k1: int):
+    """Host slice of reference-packed buffers to the window [k0,k1) x [n0,n1),
+    in the same physical layout (used for host-side sharding and tests)."""
+    if layout == L.LAYOUT_ROW:
+        w = words.reshape(K // 8, N)[k0 // 8:k1 // 8, n0:n1]
+        s = scales.reshape(K // block, N)[k0 // block:k1 // block, n0:n1]
+    else:
+        w = words.reshape(N, K // 8)[n0:n1, k0 // 8:k1 // 8]
+        s = scales.reshape(N, K // block)[n0:n1, k0 // block:k1 // block]
+    return np.ascontiguousarray(w), np.ascontiguousarray(s)
+
+
+def _world(group):
+    if dist.is_available() and dist.is_initialized():
+        return dist.get_rank(group), dist.get_world_size(group)
+    return 0, 1
+
+
+class ColumnParallelQ4Linear:
+    def __init__(self, words: torch.Tensor, scales: torch.Tensor, K: int, N: int, block: int, layout: int,
+                 device: torch.device, bias: Optional[torch.Tensor] = None, act: int = L.ACT_NONE, group=None):
+        self.rank, self.size = _world(group)
+        self.group = group
+        self.n0, self.n1 = column_shard_bounds(N, self.rank, self.size)
+        self.weight = PreparedQ4Weight(words, scales, K, N, block, layout, device,
+                                       shard=(COLUMN, self.rank, self.size))
+        self.bias = None if bias is None else bias[self.n0:self.n1].contiguous()
+        self.act = act
+
+    def forward(self, x: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """x [M, K] (replicated) -> local output columns [M, N/P]."""
+        return self.weight.linear(x, self.bias, self.act, out=out)
+
+
+class RowParallelQ4Linear:
+    def __init__(self, words: torch.Tensor, scales: torch.Tensor, K: int, N: int, block: int, layout: int,
+                 device: torch.device, bias: Optional[torch.Tensor] = None, group=None):
+        self.rank, self.size = _world(group)
+        self.group = group
+        self.k0, self.k1 = row_shard_bounds(K, block, self.rank, self.size)
+        self.weight = PreparedQ4Weight(words, scales, K, N, block, layout, device,
+                                       shard=(ROW, self.rank, self.size))
+        self.bias = bias if self.rank == 0 else None  # added once, before the sum
+
+    def forward(self, x_local: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """x_local [M, K/P] (this rank's input columns, may be a strided view)
+        -> full output [M, N] summed over ranks."""
+        w = self.weight
+        M = x_local.shape[0]
+        y = out if out is not None else torch.empty((M, w.N), dtype=torch.float32, device=w.device)
+        if x_local.stride(-1) != 1:
+            x_local = x_local.contiguous()
+        ws = Workspace.get(w.device, w.workspace_bytes(M))
+        L.check(L.lib().bq4_linear(w.handle, _ptr(x_local), M, x_local.stride(0), _ptr(self.bias), L.ACT_NONE,
+                                   None, _ptr(y), _ptr(ws), ws.numel(), _stream_ptr(w.device)))
+        if self.size > 1:
+            dist.all_reduce(y, op=dist.ReduceOp.SUM, group=self.group)
+        return y
+
+
+class DiTQ4Stack:
+    """The DiT-shaped layer stack of the benchmark: per block a fused qkv
+    (column-parallel, hidden -> 3*hidden), o (row-parallel over the v slice,
+    hidden -> hidden, bias), up (column-parallel, hidden -> mlp, bias +
+    GELU-tanh) and down (row-parallel, mlp -> hidden, bias), then the
+    activations are renormalised (RMS over the hidden axis).  Attention
+    itself is outside the Q4 path; the o-projection reads the rank's value
+    columns of the qkv output as its input shard."""
+
+    def __init__(self, blocks: int, hidden: int, qkv: int, mlp: int, device: torch.device, seed: int = 0,
+                 block: int = 128, group=None):
+        self.device = device
+        self.hidden, self.qkv, self.mlp = hidden, qkv, mlp
+        self.rank, self.size = _world(group)
+        self.layers = []
+        g = torch.Generator(device=device)
+        for b in range(blocks):
+            g.manual_seed(seed * 1000003 + b)
+            mk = lambda K, N: _random_packed(K, N, block, g, device)  # noqa: E731
+            bias = lambda N: torch.randn(N, generator=g, device=device) * 0.02  # noqa: E731
+            wq, sq = mk(hidden, qkv)
+            wo, so = mk(hidden, hidden)
+            wu, su = mk(hidden, mlp)
+            wd, sd = mk(mlp, hidden)
+            bo, bu, bd = bias(hidden), bias(mlp), bias(hidden)
+            layer = dict(
+                qkv=ColumnParallelQ4Linear(wq, sq, hidden, qkv, block, L.LAYOUT_ROW, device, group=group),
+                o=RowParallelQ4Linear(wo, so, hidden, hidden, block, L.LAYOUT_ROW, device, bo, group=group),
+                up=ColumnParallelQ4Linear(wu, su, hidden, mlp, block, L.LAYOUT_ROW, device, bu, L.ACT_GELU_TANH,
+                                          group=group),
+                down=RowParallelQ4Linear(wd, sd, mlp, hidden, block, L.LAYOUT_ROW, device, bd, group=group))
+            self.layers.append(layer)
+            del wq, sq, wo, so, wu, su, wd, sd
+        self.bufs = {}
+
+    def flops_per_token(self) -> int:
+        h, q, m = self.hidden, self.qkv, self.mlp
+        return 2 * len(self.layers) * (h * q + h * h + h * m + m * h)
+
+    def _buf(self, name, shape):
+        t = self.bufs.get(name)
+        if t is None or tuple(t.shape) != tuple(shape):
+            t = torch.empty(shape, dtype=torch.float32, device=self.device)
+            self.bufs[name] = t
+        return t
+
+    def forward(self, x: torch.Tensor, on_linear=None) -> torch.Tensor:
+        M = x.shape[0]
+        P = self.size
+        qkv_local = self.qkv // P
+        hid_local = self.hidden // P
+        for layer in self.layers:
+            t = self._buf("qkv", (M, qkv_local))
+            _timed(on_linear, "qkv", lambda: layer["qkv"].forward(x, out=t))
+            v = t[:, qkv_local - hid_local:]
+            o = self._buf("o", (M, self.hidden))
+            _timed(on_linear, "o", lambda: layer["o"].forward(v, out=o))
+            u = self._buf("up", (M, self.mlp // P))
+            _timed(on_linear, "up", lambda: layer["up"].forward(o, out=u))
+            d = self._buf("down", (M, self.hidden))
+            _timed(on_linear, "down", lambda: layer["down"].forward(u, out=d))
+            x = d * torch.rsqrt(d.pow(2).mean(-1, keepdim=True) + 1e-6)
+        return x
+
+
+def _timed(cb, name, fn):
+    if cb is None:
+        return fn()
+    cb(name, True)
+    r = fn()
+    cb(name, False)
+    return r
+
+
+def _random_packed(K: int, N: int, block: int, g: torch.Generator, device: torch.device):
+    """Row-layout raw buffers: uniform nibbles in [-8, 7] (random u32 words)
+    and scales |U(0.001, 0.02)|."""
+    words = torch.randint(-2 ** 31, 2 ** 31 - 1, (K // 8, N), generator=g, device=device,
+                          dtype=torch.int64).to(torch.int32)
+    scales = torch.rand((K // block, N), generator=g, device=device) * 0.019 + 0.001
+    return words.contiguous(), scales.contiguous()

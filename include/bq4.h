@@ -1,0 +1,206 @@
+/*
+ * bq4.h -- C ABI of the B200-native packed signed-Q4 linear (libbq4.so).
+ *
+ * Drop-in boundary for burn_image's packed-Q4 dequant-matmul.  In the
+ * reference the op is Burn's `QTensorOps::q_matmul` on the CubeCL backend
+ * (patches/burn-cubecl-0.21.0/src/ops/qtensor.rs:303-368), reached from
+ * `linear_forward` (crates/burn_boogu/src/model/linear.rs:14-37) and
+ * `qwen_linear_forward` (crates/burn_qwen3_vl/src/linear.rs:107-140).
+ *
+ * Format (Q4S): signed 4-bit, symmetric, one f32 scale per block of `block`
+ * consecutive K values (block in {8,16,32,64,128}); 8 values per
+ * little-endian u32 word, value i at bits [4i, 4i+3], two's complement.
+ * Two physical layouts exist in the reference:
+ *   BQ4_LAYOUT_COL (QuantStore::PackedU32(0) of a [N,K] tensor, Qwen):
+ *       words [N][K/8], scales [N][K/block]
+ *   BQ4_LAYOUT_ROW (QuantStore::PackedU32(1) of a [K,N] tensor, Boogu):
+ *       words [K/8][N], scales [K/block][N]
+ *
+ * Conventions: all tensor pointers passed to compute calls are DEVICE
+ * pointers on the weight's device; work is enqueued on `stream` (0 = the
+ * legacy default stream) and is stream-ordered.  Calls never abort: they
+ * return a status and `bq4_last_error_string()` (thread-local) says why.
+ * A prepared weight is immutable and may be shared by concurrent streams.
+ */
+#ifndef BQ4_H
+#define BQ4_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define BQ4_API __attribute__((visibility("default")))
+#else
+#define BQ4_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st* bq4_stream_t; /* == cudaStream_t */
+
+typedef enum {
+  BQ4_OK = 0,
+  BQ4_EINVAL_SHAPE = 1,   /* a dimension is zero/negative or not a multiple it must be */
+  BQ4_EINVAL_BLOCK = 2,   /* block not in {8,16,32,64,128} or does not divide K */
+  BQ4_EALIGN = 3,         /* pointer or stride misaligned */
+  BQ4_ECUDA = 4,          /* a CUDA runtime/driver call failed */
+  BQ4_ENCCL = 5,          /* reserved for collective helpers */
+  BQ4_ETIMEOUT = 6,       /* a bounded device-side wait expired (kernel unwound) */
+  BQ4_EINVAL_ARG = 7,     /* null pointer, bad enum, unsupported scheme */
+  BQ4_EWORKSPACE = 8,     /* workspace missing or smaller than bq4_*_workspace_size */
+  BQ4_ENONFINITE = 9,     /* packer: non-finite input value */
+  BQ4_EUNSUPPORTED = 10   /* no kernel for this device (not sm_100) */
+} bq4_status;
+
+typedef enum { BQ4_LAYOUT_COL = 0, BQ4_LAYOUT_ROW = 1 } bq4_layout;
+
+typedef enum {
+  BQ4_ACT_NONE = 0,
+  BQ4_ACT_GELU_TANH = 1, /* Burn Gelu::new_approximate (crates/burn_qwen3_vl/src/vision.rs:279) */
+  BQ4_ACT_SILU = 2
+} bq4_act;
+
+typedef struct bq4_weight bq4_weight; /* opaque prepared weight (device resident) */
+
+/* Library version string and the message of the last failed call on this thread. */
+BQ4_API const char* bq4_version(void);
+BQ4_API const char* bq4_last_error_string(void);
+
+/* ---------------------------------------------------------------- weights
+ * One-time re-layout of a reference-packed weight into the device layout the
+ * kernels stream (replaces the upload in `new_quantized`,
+ * patches/burn-cubecl-0.21.0/src/ops/qtensor.rs:64-158, called from the loader
+ * hook `q_from_data`, :167-195).  `packed_words`/`scales` may be host or
+ * device pointers (detected); the result lives on `device`.  K is the
+ * reduction (input) width, N the output width; K % 8 == 0, K % block == 0.
+ * Allocates device memory (load time only).
+ */
+BQ4_API bq4_status bq4_weight_prepare(const uint32_t* packed_words, const float* scales, int64_t K,
+                              int64_t N, int32_t block, bq4_layout layout, int32_t device,
+                              bq4_weight** out);
+
+/* Tensor-parallel shard of a reference-packed weight, prepared directly:
+ * kind 0 = column-parallel (split N into `size` equal parts, part `rank`),
+ * kind 1 = row-parallel (split K on quant-block boundaries; K/size % block == 0).
+ * Same pointer rules as bq4_weight_prepare. */
+BQ4_API bq4_status bq4_weight_prepare_shard(const uint32_t* packed_words, const float* scales, int64_t K,
+                                    int64_t N, int32_t block, bq4_layout layout, int32_t kind,
+                                    int32_t rank, int32_t size, int32_t device, bq4_weight** out);
+
+BQ4_API bq4_status bq4_weight_free(bq4_weight* w);
+
+/* K, N, block, source layout and device bytes held by a prepared weight. */
+BQ4_API bq4_status bq4_weight_info(const bq4_weight* w, int64_t* K, int64_t* N, int32_t* block,
+                           int32_t* layout, size_t* device_bytes);
+
+/* ---------------------------------------------------------------- compute
+ * Workspace: every compute call that takes `workspace` needs at least the
+ * bytes reported by the matching *_workspace_size query for the same M (and
+ * weights); the library never allocates on these calls.  The workspace must
+ * be 256-byte aligned device memory, not shared with concurrent calls.
+ */
+BQ4_API bq4_status bq4_linear_workspace_size(const bq4_weight* w, int64_t M, size_t* bytes);
+
+/*
+ * y[M,N] = act(x[M,K] . W + bias) (* aux)   -- the fused q_matmul + epilogue.
+ * x: f32, row pitch `ldx` elements (>= K); bias: f32 [N] or NULL;
+ * aux: f32 [M,N] multiplied after the activation, or NULL; y: f32 [M,N]
+ * contiguous.  Operands are staged as f16 with f32 accumulation, like the
+ * reference GPU kernel (patches/burn-cubecl-0.21.0/src/kernel/matmul/quantized.rs:172-178).
+ */
+BQ4_API bq4_status bq4_linear(const bq4_weight* w, const float* x, int64_t M, int64_t ldx,
+                      const float* bias, bq4_act act, const float* aux, float* y,
+                      void* workspace, size_t workspace_bytes, bq4_stream_t stream);
+
+BQ4_API bq4_status bq4_linear_gated_workspace_size(const bq4_weight* gate, const bq4_weight* up, int64_t M,
+                                           size_t* bytes);
+
+/*
+ * y[M,N] = silu(x . Wg + bg) * (x . Wu + bu): the SwiGLU front half
+ * (crates/burn_boogu/src/model/feed_forward.rs:32-36,
+ * crates/burn_qwen3_vl/src/text.rs:46-52) in one kernel.  gate and up must
+ * have identical K, N and block.
+ */
+BQ4_API bq4_status bq4_linear_gated(const bq4_weight* gate, const bq4_weight* up, const float* x,
+                            int64_t M, int64_t ldx, const float* gate_bias, const float* up_bias,
+                            float* y, void* workspace, size_t workspace_bytes,
+                            bq4_stream_t stream);
+
+/*
+ * Bit-exact dequantization of a prepared weight: out = q * scale in f32,
+ * written as the logical tensor of `out_layout` (BQ4_LAYOUT_ROW: [K][N],
+ * BQ4_LAYOUT_COL: [N][K]).  Mirrors the reference `dequantize`
+ * (patches/burn-cubecl-0.21.0/src/kernel/quantization/dequantize.rs:6-33).
+ */
+BQ4_API bq4_status bq4_dequant(const bq4_weight* w, float* out, bq4_layout out_layout, bq4_stream_t stream);
+
+/* Same, straight from reference-packed device buffers (no preparation). */
+BQ4_API bq4_status bq4_dequant_raw(const uint32_t* packed_words, const float* scales, int64_t K, int64_t N,
+                           int32_t block, bq4_layout layout, float* out, bq4_layout out_layout,
+                           bq4_stream_t stream);
+
+/* ------------------------------------------------------- q_matmul mirror
+ * The reference op's scheme fields (burn-std 0.21 QuantScheme) on this path.
+ * q_matmul accepts exactly what the reference's packed-Q4 eligibility test
+ * accepts (patches/burn-cubecl-0.21.0/src/ops/qtensor.rs:304-323): f32 lhs,
+ * Symmetric, Q4S, F32 params, PackedU32(0|1), Block([b]) or Block([b,1]) with
+ * b in {8,16,32,64,128}.  Everything else returns BQ4_EINVAL_ARG (the
+ * reference would fall to its generic quantized matmul, which has no B200
+ * counterpart here).
+ */
+typedef struct {
+  int32_t value;       /* 0 = Q4S (only accepted value) */
+  int32_t mode;        /* 0 = Symmetric */
+  int32_t param;       /* 0 = F32 scales */
+  int32_t store_packed_dim; /* 0 = PackedU32(0), 1 = PackedU32(1) */
+  int32_t block_rank;  /* 1 = Block([b]), 2 = Block([b,1]) */
+  int32_t block;       /* b */
+} bq4_quant_scheme;
+
+/* Workspace for bq4_q_matmul: covers an internal prepared copy of rhs. */
+BQ4_API bq4_status bq4_q_matmul_workspace_size(int64_t M, int64_t K, int64_t N, int32_t block,
+                                       size_t* bytes);
+
+/*
+ * lhs f32 [M,K] (contiguous, M = product of leading dims) times the
+ * quantized rhs of logical shape [K,N] (values/scales device buffers as the
+ * reference stores them) -> out f32 [M,N].  Prepares rhs into the workspace
+ * on every call; production callers prepare once with bq4_weight_prepare.
+ */
+BQ4_API bq4_status bq4_q_matmul(const float* lhs, int64_t M, int64_t K, const uint32_t* rhs_values,
+                        const float* rhs_scales, int64_t N, const bq4_quant_scheme* scheme,
+                        float* out, void* workspace, size_t workspace_bytes, bq4_stream_t stream);
+
+/* ------------------------------------------------------- host packers
+ * The reference's load-time quantizers, host code.  Outputs are the
+ * reference byte streams split into words and scales.
+ *   column layout: crates/burn_qwen3_vl/src/artifacts.rs:1301-1366
+ *     values [rows][inner], inner % 128 == 0 -> words rows*inner/8, scales rows*inner/128
+ *   row layout: crates/burn_boogu/src/artifacts.rs:7296-7385
+ *     values [input][output], output % 8 == 0 -> words [input/8][output],
+ *     scales [input/b][output], b = largest of {128,64,32,16,8} dividing input
+ */
+BQ4_API bq4_status bq4_quantize_col_block128(const float* values, int64_t rows, int64_t inner,
+                                     uint32_t* words, float* scales);
+BQ4_API bq4_status bq4_quantize_row_up_to128(const float* values, int64_t input, int64_t output,
+                                     uint32_t* words, float* scales, int32_t* block);
+
+/* Row-layout block policy (crates/burn_boogu/src/artifacts.rs:513-525); 0 if none. */
+BQ4_API int32_t bq4_row_block_for(int64_t input);
+
+/* Reads and clears the device-side error word of the current device: BQ4_OK, or
+ * BQ4_ETIMEOUT when a kernel's bounded wait expired since the last poll (the
+ * kernel unwound without trapping; its output is invalid).  Synchronizes. */
+BQ4_API bq4_status bq4_poll_device_error(void);
+
+/* Kernel launches issued by this thread since the last reset (bench accounting). */
+BQ4_API uint64_t bq4_launch_count(void);
+BQ4_API void bq4_launch_count_reset(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* BQ4_H */

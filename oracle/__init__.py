@@ -1,0 +1,166 @@
+"""ctypes front end of the CPU oracle (``oracle/bq4_oracle.c``).
+
+TEST INFRASTRUCTURE ONLY: the parity checker for the CUDA product and the
+timed CPU baseline.  Only ``tests/``, ``__graft_entry__.smoke()`` and
+``bench.py`` (its cpu_baseline leg and ``--impl reference`` arm) import this
+package; the product path in ``burn_image_b200`` never does.
+
+Every function restates the reference algorithm; the C file cites the
+reference file:line of each step.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "liborc.so")
+
+LAYOUT_COL = 0  # PackedU32(0): tensor [N,K], words [N][K/8], scales [N][K/b]
+LAYOUT_ROW = 1  # PackedU32(1): tensor [K,N], words [K/8][N], scales [K/b][N]
+ACT_NONE, ACT_GELU_TANH, ACT_SILU = 0, 1, 2
+
+OK, ENONFINITE, ESHAPE, EBLOCK = 0, 1, 2, 3
+
+_lib = None
+
+
+def build() -> str:
+    """Compile liborc.so with the committed Makefile (gcc + OpenMP)."""
+    subprocess.run(["make", "-s", "-C", HERE], check=True)
+    return LIB_PATH
+
+
+def lib() -> ctypes.CDLL:
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            build()
+        _lib = ctypes.CDLL(LIB_PATH)
+        i64, i32, p = ctypes.c_int64, ctypes.c_int32, ctypes.c_void_p
+        _lib.orc_quantize_col_block128.argtypes = [p, i64, i64, p, p]
+        _lib.orc_quantize_row_up_to128.argtypes = [p, i64, i64, p, p, p]
+        _lib.orc_row_block_for.argtypes = [i64]
+        _lib.orc_unpack.argtypes = [p, p, i64, i64, i32, i32, p]
+        _lib.orc_linear_f64.argtypes = [p, i64, i64, i64, p, i64, p, i32, p, p]
+        _lib.orc_linear_f64.restype = None
+        _lib.orc_linear_gated_f64.argtypes = [p, i64, i64, i64, p, p, i64, p, p, p]
+        _lib.orc_linear_gated_f64.restype = None
+        _lib.orc_cpu_linear.argtypes = [p, p, i64, i64, i32, i32, p, i64, i64, p, i32, p, p, i32]
+        _lib.orc_cpu_threads.argtypes = []
+    return _lib
+
+
+def _ptr(a):
+    return None if a is None else a.ctypes.data_as(ctypes.c_void_p)
+
+
+def _f32(a):
+    return None if a is None else np.ascontiguousarray(a, dtype=np.float32)
+
+
+class OracleError(ValueError):
+    def __init__(self, code: int, what: str):
+        super().__init__(f"{what}: oracle status {code}")
+        self.code = code
+
+
+def quantize_col_block128(values: np.ndarray):
+    """Qwen column-layout packer (crates/burn_qwen3_vl/src/artifacts.rs:1301-1366).
+
+    values: [rows, inner] float.  Returns (words u32 [rows, inner/8],
+    scales f32 [rows, inner/128]) -- the reference's byte stream is
+    ``words.tobytes() + scales.tobytes()``.
+    """
+    v = _f32(values)
+    if v.ndim < 1 or v.size == 0:
+        raise OracleError(ESHAPE, "quantize_col_block128")
+    rows = int(np.prod(v.shape[:-1])) if v.ndim > 1 else 1
+    inner = int(v.shape[-1])
+    words = np.zeros((rows, max(inner // 8, 1)), dtype=np.uint32)
+    scales = np.zeros((rows, max(inner // 128, 1)), dtype=np.float32)
+    rc = lib().orc_quantize_col_block128(_ptr(v), rows, inner, _ptr(words), _ptr(scales))
+    if rc:
+        raise OracleError(rc, "quantize_col_block128")
+    return words, scales
+
+
+def quantize_row_up_to128(values: np.ndarray):
+    """Boogu row-layout packer (crates/burn_boogu/src/artifacts.rs:7296-7385).
+
+    values: [input K, output N] float.  Returns (words u32 [K/8, N],
+    scales f32 [K/b, N], block b).
+    """
+    v = _f32(values)
+    if v.ndim != 2:
+        raise OracleError(ESHAPE, "quantize_row_up_to128")
+    K, N = v.shape
+    b = int(lib().orc_row_block_for(K)) or 8
+    words = np.zeros((max(K // 8, 1), N), dtype=np.uint32)
+    scales = np.zeros((max(K // b, 1), N), dtype=np.float32)
+    blk = ctypes.c_int32(0)
+    rc = lib().orc_quantize_row_up_to128(_ptr(v), K, N, _ptr(words), _ptr(scales), ctypes.byref(blk))
+    if rc:
+        raise OracleError(rc, "quantize_row_up_to128")
+    return words, scales, int(blk.value)
+
+
+def unpack(words: np.ndarray, scales: np.ndarray, K: int, N: int, block: int, layout: int) -> np.ndarray:
+    """Dequantized logical weight W [K, N] (y = x . W), f32, q * scale."""
+    w = np.ascontiguousarray(words, dtype=np.uint32)
+    s = _f32(scales)
+    out = np.empty((K, N), dtype=np.float32)
+    rc = lib().orc_unpack(_ptr(w), _ptr(s), K, N, block, layout, _ptr(out))
+    if rc:
+        raise OracleError(rc, "unpack")
+    return out
+
+
+def linear_f64(x: np.ndarray, w_kn: np.ndarray, bias=None, act: int = ACT_NONE, aux=None) -> np.ndarray:
+    """f64-accumulated reference linear: act(x . W + bias) (* aux)."""
+    x = _f32(x)
+    w = _f32(w_kn)
+    M, K = x.shape
+    N = w.shape[1]
+    y = np.empty((M, N), dtype=np.float32)
+    lib().orc_linear_f64(_ptr(x), M, K, K, _ptr(w), N, _ptr(_f32(bias)), act, _ptr(_f32(aux)), _ptr(y))
+    return y
+
+
+def linear_gated_f64(x, wg_kn, wu_kn, bg=None, bu=None) -> np.ndarray:
+    """f64-accumulated silu(x . Wg + bg) * (x . Wu + bu)."""
+    x = _f32(x)
+    M, K = x.shape
+    N = wg_kn.shape[1]
+    y = np.empty((M, N), dtype=np.float32)
+    lib().orc_linear_gated_f64(_ptr(x), M, K, K, _ptr(_f32(wg_kn)), _ptr(_f32(wu_kn)), N,
+                               _ptr(_f32(bg)), _ptr(_f32(bu)), _ptr(y))
+    return y
+
+
+def cpu_linear(words, scales, K, N, block, layout, x, bias=None, act=ACT_NONE, aux=None,
+               threads: int = 0, out=None) -> np.ndarray:
+    """Timed CPU baseline (dequantize + blocked SGEMM + epilogue, OpenMP)."""
+    x = _f32(x)
+    M = x.shape[0]
+    y = out if out is not None else np.empty((M, N), dtype=np.float32)
+    rc = lib().orc_cpu_linear(_ptr(np.ascontiguousarray(words, dtype=np.uint32)), _ptr(_f32(scales)),
+                              K, N, block, layout, _ptr(x), M, x.shape[1], _ptr(_f32(bias)), act,
+                              _ptr(_f32(aux)), _ptr(y), threads)
+    if rc:
+        raise OracleError(rc, "cpu_linear")
+    return y
+
+
+def cpu_threads() -> int:
+    return int(lib().orc_cpu_threads())
+
+
+def rel_frobenius(actual: np.ndarray, expected: np.ndarray) -> float:
+    a = np.asarray(actual, dtype=np.float64)
+    e = np.asarray(expected, dtype=np.float64)
+    den = np.sqrt((e * e).sum())
+    return float(np.sqrt(((a - e) ** 2).sum()) / (den if den > 0 else 1.0))
