@@ -2,8 +2,8 @@
 bias / GELU-tanh / SiLU-gate epilogue) for burn_image, behind a C ABI
 (include/bq4.h, libbq4.so) with a host mirror of the reference interface.
 """
-from ._lib import (ACT_GELU_TANH, ACT_NONE, ACT_SILU, LAYOUT_COL, LAYOUT_ROW, Bq4Error,  # noqa: F401
-                   LIB_PATH)
+from ._lib import (ACT_GELU_TANH, ACT_NONE, ACT_SILU, LAYOUT_COL, LAYOUT_NPACKED, LAYOUT_ROW,  # noqa: F401
+                   LIB_PATH, Bq4Error)
 from .q4 import (PackedQ4, PreparedQ4Weight, Q4Linear, QuantizedTensor, QuantScheme,  # noqa: F401
                  feed_forward_swiglu, linear_forward, linear_gated, poll_device_error, q_matmul,
                  quantize_q4s_block128_f32, quantize_row_layout_q4s_block_up_to128_f32,

@@ -19,7 +19,7 @@ STATUS_NAMES = {
     5: "BQ4_ENCCL", 6: "BQ4_ETIMEOUT", 7: "BQ4_EINVAL_ARG", 8: "BQ4_EWORKSPACE",
     9: "BQ4_ENONFINITE", 10: "BQ4_EUNSUPPORTED",
 }
-LAYOUT_COL, LAYOUT_ROW = 0, 1
+LAYOUT_COL, LAYOUT_ROW, LAYOUT_NPACKED = 0, 1, 2
 ACT_NONE, ACT_GELU_TANH, ACT_SILU = 0, 1, 2
 
 # Every symbol include/bq4.h declares, with (restype, argtypes).
@@ -39,7 +39,7 @@ SIGNATURES = {
     "bq4_linear_gated": (_st, [_p, _p, _p, _i64, _i64, _p, _p, _p, _p, _sz, _p]),
     "bq4_dequant": (_st, [_p, _p, _i32, _p]),
     "bq4_dequant_raw": (_st, [_p, _p, _i64, _i64, _i32, _i32, _p, _i32, _p]),
-    "bq4_q_matmul_workspace_size": (_st, [_i64, _i64, _i64, _i32, ctypes.POINTER(_sz)]),
+    "bq4_q_matmul_workspace_size": (_st, [_i64, _i64, _i64, _p, ctypes.POINTER(_sz)]),
     "bq4_q_matmul": (_st, [_p, _i64, _i64, _p, _p, _i64, _p, _p, _p, _sz, _p]),
     "bq4_quantize_col_block128": (_st, [_p, _i64, _i64, _p, _p]),
     "bq4_quantize_row_up_to128": (_st, [_p, _i64, _i64, _p, _p, ctypes.POINTER(_i32)]),
@@ -53,7 +53,7 @@ SIGNATURES = {
 class QuantScheme(ctypes.Structure):
     """bq4_quant_scheme: the reference QuantScheme fields on this path."""
     _fields_ = [("value", _i32), ("mode", _i32), ("param", _i32), ("store_packed_dim", _i32),
-                ("block_rank", _i32), ("block", _i32)]
+                ("block_rank", _i32), ("block", _i32), ("rhs_transposed_view", _i32)]
 
 
 class Bq4Error(RuntimeError):

@@ -43,12 +43,21 @@ namespace {
 bool valid_block(int32_t b) { return b == 8 || b == 16 || b == 32 || b == 64 || b == 128; }
 
 bq4_status check_geometry(int64_t K, int64_t N, int32_t block, int32_t layout) {
-  if (layout != BQ4_LAYOUT_COL && layout != BQ4_LAYOUT_ROW)
-    return set_error(BQ4_EINVAL_ARG, "layout %d is not BQ4_LAYOUT_COL/ROW", layout);
+  if (layout != BQ4_LAYOUT_COL && layout != BQ4_LAYOUT_ROW && layout != BQ4_LAYOUT_NPACKED)
+    return set_error(BQ4_EINVAL_ARG, "layout %d is not BQ4_LAYOUT_COL/ROW/NPACKED", layout);
   if (!valid_block(block))
     return set_error(BQ4_EINVAL_BLOCK, "block %d not in {8,16,32,64,128}", block);
   if (K <= 0 || N <= 0)
     return set_error(BQ4_EINVAL_SHAPE, "K=%lld N=%lld must be positive", (long long)K, (long long)N);
+  if (layout == BQ4_LAYOUT_NPACKED) {
+    // packed and blocked along N (the last axis of a plain [K,N] tensor)
+    if (N % 8 != 0) return set_error(BQ4_EINVAL_SHAPE, "N=%lld is not a multiple of 8", (long long)N);
+    if (N % block != 0)
+      return set_error(BQ4_EINVAL_BLOCK, "block %d does not divide N=%lld", block, (long long)N);
+    if (K > (int64_t)1 << 24 || N > (int64_t)1 << 24)
+      return set_error(BQ4_EINVAL_SHAPE, "K or N above 2^24");
+    return BQ4_OK;
+  }
   if (K % 8 != 0) return set_error(BQ4_EINVAL_SHAPE, "K=%lld is not a multiple of 8", (long long)K);
   if (K % block != 0)
     return set_error(BQ4_EINVAL_BLOCK, "block %d does not divide K=%lld", block, (long long)K);
@@ -120,8 +129,13 @@ bq4_status prepare_window(const uint32_t* words, const float* scales, int64_t sr
   w->q_bytes = (size_t)w->ntiles * w->nkc * 1024 * sizeof(uint32_t);
   w->s_bytes = (size_t)w->ntiles * w->nkb * 128 * sizeof(float);
 
-  const size_t src_words = (size_t)src_N * (size_t)(src_K / 8);
-  const size_t src_scales = (size_t)src_N * (size_t)(src_K / block);
+  const bool pre = layout == BQ4_LAYOUT_NPACKED;
+  if (pre) {
+    w->q_bytes = w->s_bytes = 0;
+    w->h_bytes = (size_t)w->ntiles * w->nkc * 128 * 64 * sizeof(uint16_t);
+  }
+  const size_t src_words = pre ? (size_t)src_K * (size_t)(src_N / 8) : (size_t)src_N * (size_t)(src_K / 8);
+  const size_t src_scales = pre ? (size_t)src_K * (size_t)(src_N / block) : (size_t)src_N * (size_t)(src_K / block);
   const uint32_t* dwords = words;
   const float* dscales = scales;
   void* tmp_w = nullptr;
@@ -137,16 +151,23 @@ bq4_status prepare_window(const uint32_t* words, const float* scales, int64_t sr
     if (e == cudaSuccess) e = cudaMemcpy(tmp_s, scales, src_scales * 4, cudaMemcpyHostToDevice);
     dscales = static_cast<const float*>(tmp_s);
   }
-  if (e == cudaSuccess) e = cudaMalloc(reinterpret_cast<void**>(&w->q), w->q_bytes);
-  if (e == cudaSuccess) e = cudaMalloc(reinterpret_cast<void**>(&w->s), w->s_bytes);
-  if (e == cudaSuccess)
-    e = launch_prepare(dwords, dscales, K, N, block, layout, n0, k0, src_N, src_K, w, nullptr);
+  if (pre) {
+    if (e == cudaSuccess) e = cudaMalloc(reinterpret_cast<void**>(&w->h), w->h_bytes);
+    if (e == cudaSuccess)
+      e = launch_prepare_pre(dwords, dscales, K, N, block, n0, k0, src_N, src_K, w, nullptr);
+  } else {
+    if (e == cudaSuccess) e = cudaMalloc(reinterpret_cast<void**>(&w->q), w->q_bytes);
+    if (e == cudaSuccess) e = cudaMalloc(reinterpret_cast<void**>(&w->s), w->s_bytes);
+    if (e == cudaSuccess)
+      e = launch_prepare(dwords, dscales, K, N, block, layout, n0, k0, src_N, src_K, w, nullptr);
+  }
   if (e == cudaSuccess) e = cudaStreamSynchronize(nullptr);
   if (tmp_w) cudaFree(tmp_w);
   if (tmp_s) cudaFree(tmp_s);
   if (e != cudaSuccess) {
     if (w->q) cudaFree(w->q);
     if (w->s) cudaFree(w->s);
+    if (w->h) cudaFree(w->h);
     delete w;
     return check_cuda(e, "bq4_weight_prepare");
   }
@@ -155,7 +176,7 @@ bq4_status prepare_window(const uint32_t* words, const float* scales, int64_t sr
 }
 
 bq4_status check_weight(const bq4_weight* w, const char* name) {
-  if (!w || !w->q || !w->s) return set_error(BQ4_EINVAL_ARG, "%s is NULL or freed", name);
+  if (!w || !((w->q && w->s) || w->h)) return set_error(BQ4_EINVAL_ARG, "%s is NULL or freed", name);
   return BQ4_OK;
 }
 
@@ -205,10 +226,16 @@ bq4_status bq4_weight_prepare_shard(const uint32_t* packed_words, const float* s
   if (kind == 0) {
     if (N % size != 0)
       return set_error(BQ4_EINVAL_SHAPE, "column shard: N=%lld not divisible by %d", (long long)N, size);
+    if (layout == BQ4_LAYOUT_NPACKED && ((N / size) % block != 0 || (N / size) % 8 != 0))
+      return set_error(BQ4_EINVAL_BLOCK, "column shard of an N-packed weight must fall on block boundaries");
     const int64_t n = N / size;
     return prepare_window(packed_words, scales, K, N, block, layout, rank * n, n, 0, K, device, out);
   }
   if (kind == 1) {
+    if (layout == BQ4_LAYOUT_NPACKED && K % size == 0) {
+      const int64_t k = K / size;
+      return prepare_window(packed_words, scales, K, N, block, layout, 0, N, rank * k, k, device, out);
+    }
     if (K % size != 0 || (K / size) % block != 0 || (K / size) % 8 != 0)
       return set_error(BQ4_EINVAL_BLOCK,
                        "row shard: K=%lld over %d parts does not fall on block-%d boundaries",
@@ -224,8 +251,11 @@ bq4_status bq4_weight_free(bq4_weight* w) {
   DeviceGuard guard(w->device);
   cudaError_t e1 = w->q ? cudaFree(w->q) : cudaSuccess;
   cudaError_t e2 = w->s ? cudaFree(w->s) : cudaSuccess;
+  cudaError_t e3 = w->h ? cudaFree(w->h) : cudaSuccess;
+  if (e2 == cudaSuccess) e2 = e3;
   w->q = nullptr;
   w->s = nullptr;
+  w->h = nullptr;
   delete w;
   if (e1 != cudaSuccess) return check_cuda(e1, "bq4_weight_free");
   return check_cuda(e2, "bq4_weight_free");
@@ -239,7 +269,7 @@ bq4_status bq4_weight_info(const bq4_weight* w, int64_t* K, int64_t* N, int32_t*
   if (N) *N = w->N;
   if (block) *block = w->block;
   if (layout) *layout = w->layout;
-  if (device_bytes) *device_bytes = w->q_bytes + w->s_bytes;
+  if (device_bytes) *device_bytes = w->q_bytes + w->s_bytes + w->h_bytes;
   return BQ4_OK;
 }
 
@@ -321,6 +351,9 @@ bq4_status bq4_dequant(const bq4_weight* w, float* out, bq4_layout out_layout, b
   if (!out) return set_error(BQ4_EINVAL_ARG, "out is NULL");
   if (out_layout != BQ4_LAYOUT_COL && out_layout != BQ4_LAYOUT_ROW)
     return set_error(BQ4_EINVAL_ARG, "out_layout %d", (int)out_layout);
+  if (w->h)
+    return set_error(BQ4_EUNSUPPORTED,
+                     "weight was prepared from BQ4_LAYOUT_NPACKED (pre-expanded f16); use bq4_dequant_raw");
   DeviceGuard guard(w->device);
   return check_cuda(launch_dequant_prepared(w, out, out_layout, reinterpret_cast<cudaStream_t>(stream)),
                     "bq4_dequant");
@@ -359,8 +392,9 @@ static bq4_status check_scheme(const bq4_quant_scheme* s) {
   return BQ4_OK;
 }
 
-static void q_matmul_view(int64_t K, int64_t N, int32_t block, bq4_weight* w) {
+static void q_matmul_view(int64_t K, int64_t N, int32_t block, int32_t layout, bq4_weight* w) {
   memset(w, 0, sizeof(*w));
+  w->layout = layout;
   w->K = K;
   w->N = N;
   w->block = block;
@@ -369,22 +403,35 @@ static void q_matmul_view(int64_t K, int64_t N, int32_t block, bq4_weight* w) {
   w->nkb = w->Kp / block;
   w->ntiles = (N + kTileN - 1) / kTileN;
   w->Np = w->ntiles * kTileN;
-  w->q_bytes = (size_t)w->ntiles * w->nkc * 1024 * 4;
-  w->s_bytes = (size_t)w->ntiles * w->nkb * 128 * 4;
+  if (layout == BQ4_LAYOUT_NPACKED) {
+    w->h_bytes = (size_t)w->ntiles * w->nkc * 128 * 64 * 2;
+  } else {
+    w->q_bytes = (size_t)w->ntiles * w->nkc * 1024 * 4;
+    w->s_bytes = (size_t)w->ntiles * w->nkb * 128 * 4;
+  }
 }
 
-bq4_status bq4_q_matmul_workspace_size(int64_t M, int64_t K, int64_t N, int32_t block, size_t* bytes) {
-  bq4_status st = check_geometry(K, N, block, BQ4_LAYOUT_ROW);
+static size_t q_matmul_weight_bytes(const bq4_weight& w) {
+  return (w.q_bytes + 255) / 256 * 256 + (w.s_bytes + 255) / 256 * 256 + (w.h_bytes + 255) / 256 * 256;
+}
+
+bq4_status bq4_q_matmul_workspace_size(int64_t M, int64_t K, int64_t N, const bq4_quant_scheme* scheme,
+                                       size_t* bytes) {
+  bq4_status st = check_scheme(scheme);
+  if (st) return st;
+  const int32_t layout = scheme->store_packed_dim == 1 ? BQ4_LAYOUT_ROW
+                         : (scheme->rhs_transposed_view ? BQ4_LAYOUT_COL : BQ4_LAYOUT_NPACKED);
+  st = check_geometry(K, N, scheme->block, layout);
   if (st) return st;
   if (!bytes) return set_error(BQ4_EINVAL_ARG, "bytes is NULL");
   bq4_weight w;
-  q_matmul_view(K, N, block, &w);
+  q_matmul_view(K, N, scheme->block, layout, &w);
   int dev = 0;
   cudaGetDevice(&dev);
   GemmPlan plan;
   st = plan_gemm(&w, 1, M, dev, &plan);
   if (st) return st;
-  *bytes = (w.q_bytes + 255) / 256 * 256 + (w.s_bytes + 255) / 256 * 256 + plan.workspace_bytes;
+  *bytes = q_matmul_weight_bytes(w) + plan.workspace_bytes;
   return BQ4_OK;
 }
 
@@ -393,10 +440,12 @@ bq4_status bq4_q_matmul(const float* lhs, int64_t M, int64_t K, const uint32_t* 
                         float* out, void* workspace, size_t workspace_bytes, bq4_stream_t stream) {
   bq4_status st = check_scheme(scheme);
   if (st) return st;
-  // PackedU32(0) of the logical [K,N] rhs packs along N (the reference's
-  // Qwen weight is the transposed view of a [N,K] tensor packed along K);
-  // both reach the kernel as the matching physical layout.
-  const int32_t layout = scheme->store_packed_dim == 0 ? BQ4_LAYOUT_COL : BQ4_LAYOUT_ROW;
+  // PackedU32(1): the stored [K,N] tensor is packed along K (Boogu row
+  // layout).  PackedU32(0): packed along the stored tensor's last axis -- K
+  // when rhs is the transposed view of a stored [N,K] tensor (Qwen), N when
+  // rhs is stored as a plain [K,N] tensor.
+  const int32_t layout = scheme->store_packed_dim == 1 ? BQ4_LAYOUT_ROW
+                         : (scheme->rhs_transposed_view ? BQ4_LAYOUT_COL : BQ4_LAYOUT_NPACKED);
   st = check_geometry(K, N, scheme->block, layout);
   if (st) return st;
   if (!rhs_values || !rhs_scales || !lhs || !out) return set_error(BQ4_EINVAL_ARG, "NULL pointer");
@@ -405,22 +454,28 @@ bq4_status bq4_q_matmul(const float* lhs, int64_t M, int64_t K, const uint32_t* 
   st = require_sm100(dev);
   if (st) return st;
   bq4_weight w;
-  q_matmul_view(K, N, scheme->block, &w);
-  w.layout = layout;
+  q_matmul_view(K, N, scheme->block, layout, &w);
   w.device = dev;
   size_t need = 0;
-  st = bq4_q_matmul_workspace_size(M, K, N, scheme->block, &need);
+  st = bq4_q_matmul_workspace_size(M, K, N, scheme, &need);
   if (st) return st;
   if (!workspace || workspace_bytes < need)
     return set_error(BQ4_EWORKSPACE, "workspace %zu < required %zu bytes", workspace_bytes, need);
   if (!aligned(workspace, 256)) return set_error(BQ4_EALIGN, "workspace not 256-byte aligned");
   uint8_t* p = static_cast<uint8_t*>(workspace);
-  w.q = reinterpret_cast<uint32_t*>(p);
-  p += (w.q_bytes + 255) / 256 * 256;
-  w.s = reinterpret_cast<float*>(p);
-  p += (w.s_bytes + 255) / 256 * 256;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  cudaError_t e = launch_prepare(rhs_values, rhs_scales, K, N, scheme->block, layout, 0, 0, N, K, &w, s);
+  cudaError_t e;
+  if (layout == BQ4_LAYOUT_NPACKED) {
+    w.h = reinterpret_cast<uint16_t*>(p);
+    p += (w.h_bytes + 255) / 256 * 256;
+    e = launch_prepare_pre(rhs_values, rhs_scales, K, N, scheme->block, 0, 0, N, K, &w, s);
+  } else {
+    w.q = reinterpret_cast<uint32_t*>(p);
+    p += (w.q_bytes + 255) / 256 * 256;
+    w.s = reinterpret_cast<float*>(p);
+    p += (w.s_bytes + 255) / 256 * 256;
+    e = launch_prepare(rhs_values, rhs_scales, K, N, scheme->block, layout, 0, 0, N, K, &w, s);
+  }
   if (e != cudaSuccess) return check_cuda(e, "q_matmul prepare");
   GemmPlan plan;
   st = plan_gemm(&w, 1, M, dev, &plan);

@@ -31,6 +31,7 @@
 #include <cuda_runtime.h>
 
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 
 #include "bq4_internal.h"
@@ -49,6 +50,8 @@ constexpr uint32_t kATileBytes = 128 * 128;  // 128 rows x 64 f16
 constexpr uint32_t kRawQBytes = 4096;        // 128 rows x 64 nibbles
 
 struct GemmArgs {
+  const uint16_t* h[2];  // pre-expanded f16 tiles (pre == 1)
+  int pre;
   const uint32_t* q[2];
   const float* s[2];
   const float* bias[2];
@@ -60,7 +63,8 @@ struct GemmArgs {
   int nkc, nkb, block;
   int ntiles, mtiles, ksplit, units;
   int stages, raw_stages;
-  uint32_t raw_s_bytes;  // scale bytes per weight per raw stage
+  uint32_t raw_s_bytes;  // scale bytes per weight per raw stage (bulk-copied)
+  uint32_t raw_w_bytes;  // shared-memory bytes per weight per raw stage (host-computed)
   int act;
 };
 
@@ -133,7 +137,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* a_tiles = smem;                                        // [S][NW][16 KiB]
   uint8_t* b_tiles = a_tiles + (size_t)S * NW * kATileBytes;      // [S][BT*128]
   uint8_t* raw = b_tiles + (size_t)S * kBTileBytes;               // [RS][NW][4 KiB + scales]
-  const uint32_t raw_w_bytes = kRawQBytes + a.raw_s_bytes;
+  const uint32_t raw_w_bytes = a.raw_w_bytes;
   uint64_t* bars = reinterpret_cast<uint64_t*>(raw + (size_t)RS * NW * raw_w_bytes);
   uint64_t* full = bars;
   uint64_t* empty = full + S;
@@ -150,8 +154,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < S; ++i) {
-      ptx::mbar_init(&full[i], 1 + 4);  // TMA expect_tx arrival + 4 dequant warps
-      ptx::mbar_init(&empty[i], 1);     // tcgen05.commit
+      // TMA expect_tx arrival + 4 dequant warps (pre-expanded tiles: TMA only)
+      ptx::mbar_init(&full[i], a.pre ? 1 : 1 + 4);
+      ptx::mbar_init(&empty[i], 1);  // tcgen05.commit
     }
     for (int i = 0; i < RS; ++i) {
       ptx::mbar_init(&raw_full[i], 1);
@@ -187,6 +192,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int u = blockIdx.x; u < a.units && !*abort_flag; u += gridDim.x) {
         const int tile = u / S_split, split = u - tile * S_split;
         const int mtile = tile % a.mtiles;
+        const int ntile = tile / a.mtiles;
         const int kc0 = (int)((int64_t)split * a.nkc / S_split);
         const int kc1 = (int)((int64_t)(split + 1) * a.nkc / S_split);
         for (int kc = kc0; kc < kc1; ++kc) {
@@ -194,16 +200,23 @@ __global__ void __launch_bounds__(kThreads, 1)
             record_error(a, abort_flag, BQ4_ETIMEOUT);
             break;
           }
-          ptx::mbar_arrive_expect_tx(&full[stage], kBTileBytes);
+          ptx::mbar_arrive_expect_tx(&full[stage], kBTileBytes + (a.pre ? NW * kATileBytes : 0u));
           ptx::tma_load_2d(b_tiles + (size_t)stage * kBTileBytes, &tmap_x, &full[stage],
                            kc * kChunkK, mtile * BT);
+          if (a.pre) {
+#pragma unroll
+            for (int w = 0; w < NW; ++w)
+              ptx::bulk_load(a_tiles + ((size_t)stage * NW + w) * kATileBytes,
+                             a.h[w] + ((size_t)ntile * a.nkc + kc) * (kATileBytes / 2), kATileBytes,
+                             &full[stage]);
+          }
           if (++stage == S) { stage = 0; phase ^= 1; }
         }
       }
     }
   } else if (warp == kRawWarp) {
     // ------------------------------------------------ raw weight tiles (bulk)
-    if (lane == 0) {
+    if (lane == 0 && !a.pre) {
       int rs = 0;
       uint32_t rphase = 0;
       for (int u = blockIdx.x; u < a.units && !*abort_flag; u += gridDim.x) {
@@ -238,6 +251,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t phase = 0, rphase = 0;
     const int block = a.block;
     bool ok = true;
+    if (a.pre) ok = false;  // pre-expanded tiles arrive by bulk copy
     for (int u = blockIdx.x; ok && u < a.units && !*abort_flag; u += gridDim.x) {
       const int tile = u / S_split, split = u - tile * S_split;
       const int kc0 = (int)((int64_t)split * a.nkc / S_split);
@@ -283,7 +297,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (++stage == S) { stage = 0; phase ^= 1; }
       }
     }
-    if (!ok) record_error(a, abort_flag, BQ4_ETIMEOUT);
+    if (!ok && !a.pre) record_error(a, abort_flag, BQ4_ETIMEOUT);
   } else if (warp == kMmaWarp) {
     // ------------------------------------------------ MMA issuer
     if (lane == 0) {
@@ -461,6 +475,374 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+// ---------------------------------------------------------------------------
+// Exact-weight kernel (blocks of 64 or 128 K values).
+//
+// The dequant warps stage q itself (exact small integers in f16); the MMA
+// accumulates one K-block segment at a time into one of kNumPart TMEM
+// partial buffers; eight scaler warps drain each partial with
+// acc += scale[n, kb] * partial in f32 registers, so every weight enters the
+// sum as exactly q * scale and only the activations are rounded (to f16).
+// This is the "per-K-block scale on the f32 accumulator" formulation.
+//
+// Warp roles (480 threads): warps 0-7 scaler + epilogue (warp w covers TMEM
+// lanes 32*(w%4).. and token columns [(w/4)*BT/2, (w/4+1)*BT/2)), warps 8-11
+// dequant, warp 12 token TMA, warp 13 raw bulk copies, warp 14 MMA issuer.
+// ---------------------------------------------------------------------------
+constexpr int kExThreads = 480;
+constexpr int kExScalerWarps = 8;
+constexpr int kExDqWarp0 = 8;
+constexpr int kExTmaWarp = 12;
+constexpr int kExRawWarp = 13;
+constexpr int kExMmaWarp = 14;
+constexpr int kNumPart = 4;
+
+// Expand one prepared word into 8 exact f16 values q (no scale).
+__device__ __forceinline__ uint4 expand_word_exact(uint32_t w) {
+  const uint32_t magic = 0x64086408u;
+  uint32_t p[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const uint32_t src = w >> (4 * i);
+    uint32_t t;
+    asm("lop3.b32 %0, %1, %2, %3, 0x6a;" : "=r"(t) : "r"(src), "r"(0x000F000Fu), "r"(magic));
+    asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(p[i]) : "r"(t), "r"(magic));
+  }
+  return make_uint4(p[0], p[1], p[2], p[3]);
+}
+
+// Segment bookkeeping: the K chunks [kc0, kc1) of a unit, cut at K-block
+// boundaries (a block spans block/64 chunks).
+__device__ __forceinline__ bool seg_first(int kc, int kc0, int cpb) { return kc == kc0 || (kc % cpb) == 0; }
+__device__ __forceinline__ bool seg_last(int kc, int kc1, int cpb) { return kc == kc1 - 1 || ((kc + 1) % cpb) == 0; }
+
+template <int BT, int NW>
+__global__ void __launch_bounds__(kExThreads, 1)
+    q4_gemm_exact_kernel(const __grid_constant__ CUtensorMap tmap_x, const GemmArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+
+  const int S = a.stages, RS = a.raw_stages;
+  constexpr uint32_t kBTileBytes = BT * 128;
+  constexpr int kCols = BT / 2;             // token columns per scaler thread
+  constexpr uint32_t kPartCols = NW * BT;   // TMEM columns per partial buffer
+  constexpr uint32_t kTmemCols = kNumPart * kPartCols;
+  static_assert(kTmemCols == 256 || kTmemCols == 512, "TMEM columns");
+  static_assert(kCols % 32 == 0, "token columns per scaler thread");
+
+  uint8_t* a_tiles = smem;
+  uint8_t* b_tiles = a_tiles + (size_t)S * NW * kATileBytes;
+  uint8_t* raw = b_tiles + (size_t)S * kBTileBytes;
+  const uint32_t raw_w_bytes = a.raw_w_bytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(raw + (size_t)RS * NW * raw_w_bytes);
+  uint64_t* full = bars;
+  uint64_t* empty = full + S;
+  uint64_t* raw_full = empty + S;
+  uint64_t* raw_empty = raw_full + RS;
+  uint64_t* part_full = raw_empty + RS;
+  uint64_t* part_empty = part_full + kNumPart;
+  uint32_t* tmem_base_slot = reinterpret_cast<uint32_t*>(part_empty + kNumPart);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_base_slot + 1);
+  volatile int* last_flag = abort_flag + 1;
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int cpb = a.block / kChunkK;  // chunks per K block (1 or 2)
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < S; ++i) {
+      ptx::mbar_init(&full[i], 1 + 4);
+      ptx::mbar_init(&empty[i], 1);
+    }
+    for (int i = 0; i < RS; ++i) {
+      ptx::mbar_init(&raw_full[i], 1);
+      ptx::mbar_init(&raw_empty[i], 4);
+    }
+    for (int i = 0; i < kNumPart; ++i) {
+      ptx::mbar_init(&part_full[i], 1);
+      ptx::mbar_init(&part_empty[i], kExScalerWarps);
+    }
+    *abort_flag = 0;
+    *last_flag = 0;
+    ptx::fence_mbar_init();
+  }
+  if (warp == kExTmaWarp && lane == 0) ptx::prefetch_tmap(&tmap_x);
+  if (warp == kExMmaWarp) {
+    ptx::tmem_alloc(tmem_base_slot, kTmemCols);
+    ptx::tmem_relinquish();
+  }
+  ptx::tc_fence_before();
+  __syncthreads();
+  ptx::tc_fence_after();
+  const uint32_t tmem_base = *tmem_base_slot;
+  const int S_split = a.ksplit;
+
+  if (warp == kExTmaWarp) {
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      for (int u = blockIdx.x; u < a.units && !*abort_flag; u += gridDim.x) {
+        const int tile = u / S_split, split = u - tile * S_split;
+        const int mtile = tile % a.mtiles;
+        const int kc0 = (int)((int64_t)split * a.nkc / S_split);
+        const int kc1 = (int)((int64_t)(split + 1) * a.nkc / S_split);
+        for (int kc = kc0; kc < kc1; ++kc) {
+          if (!ptx::mbar_wait(&empty[stage], phase ^ 1, abort_flag)) {
+            record_error(a, abort_flag, BQ4_ETIMEOUT);
+            break;
+          }
+          ptx::mbar_arrive_expect_tx(&full[stage], kBTileBytes);
+          ptx::tma_load_2d(b_tiles + (size_t)stage * kBTileBytes, &tmap_x, &full[stage], kc * kChunkK, mtile * BT);
+          if (++stage == S) { stage = 0; phase ^= 1; }
+        }
+      }
+    }
+  } else if (warp == kExRawWarp) {
+    if (lane == 0) {
+      int rs = 0;
+      uint32_t rphase = 0;
+      for (int u = blockIdx.x; u < a.units && !*abort_flag; u += gridDim.x) {
+        const int tile = u / S_split, split = u - tile * S_split;
+        const int ntile = tile / a.mtiles;
+        const int kc0 = (int)((int64_t)split * a.nkc / S_split);
+        const int kc1 = (int)((int64_t)(split + 1) * a.nkc / S_split);
+        for (int kc = kc0; kc < kc1; ++kc) {
+          if (!ptx::mbar_wait(&raw_empty[rs], rphase ^ 1, abort_flag)) {
+            record_error(a, abort_flag, BQ4_ETIMEOUT);
+            break;
+          }
+          ptx::mbar_arrive_expect_tx(&raw_full[rs], NW * kRawQBytes);
+#pragma unroll
+          for (int w = 0; w < NW; ++w) {
+            uint8_t* dst = raw + ((size_t)rs * NW + w) * raw_w_bytes;
+            ptx::bulk_load(dst, a.q[w] + ((size_t)ntile * a.nkc + kc) * 1024, kRawQBytes, &raw_full[rs]);
+          }
+          if (++rs == RS) { rs = 0; rphase ^= 1; }
+        }
+      }
+    }
+  } else if (warp >= kExDqWarp0 && warp < kExDqWarp0 + 4) {
+    const int r = threadIdx.x - kExDqWarp0 * 32;
+    const int sw = r & 7;
+    int stage = 0, rs = 0;
+    uint32_t phase = 0, rphase = 0;
+    bool ok = true;
+    for (int u = blockIdx.x; ok && u < a.units && !*abort_flag; u += gridDim.x) {
+      const int tile = u / S_split, split = u - tile * S_split;
+      const int kc0 = (int)((int64_t)split * a.nkc / S_split);
+      const int kc1 = (int)((int64_t)(split + 1) * a.nkc / S_split);
+      for (int kc = kc0; kc < kc1; ++kc) {
+        if (!ptx::mbar_wait(&raw_full[rs], rphase, abort_flag)) { ok = false; break; }
+        uint4 words[NW][2];
+#pragma unroll
+        for (int w = 0; w < NW; ++w) {
+          const uint8_t* src = raw + ((size_t)rs * NW + w) * raw_w_bytes;
+          words[w][0] = *reinterpret_cast<const uint4*>(src + (size_t)r * 16);
+          words[w][1] = *reinterpret_cast<const uint4*>(src + (size_t)(128 + r) * 16);
+        }
+        __syncwarp();
+        if (lane == 0) ptx::mbar_arrive(&raw_empty[rs]);
+        if (++rs == RS) { rs = 0; rphase ^= 1; }
+        if (!ptx::mbar_wait(&empty[stage], phase ^ 1, abort_flag)) { ok = false; break; }
+#pragma unroll
+        for (int w = 0; w < NW; ++w) {
+          uint8_t* dst = a_tiles + ((size_t)stage * NW + w) * kATileBytes + (size_t)r * 128;
+          const uint32_t wv[8] = {words[w][0].x, words[w][0].y, words[w][0].z, words[w][0].w,
+                                  words[w][1].x, words[w][1].y, words[w][1].z, words[w][1].w};
+#pragma unroll
+          for (int j = 0; j < 8; ++j)
+            *reinterpret_cast<uint4*>(dst + ((j ^ sw) << 4)) = expand_word_exact(wv[j]);
+        }
+        ptx::fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) ptx::mbar_arrive(&full[stage]);
+        if (++stage == S) { stage = 0; phase ^= 1; }
+      }
+    }
+    if (!ok) record_error(a, abort_flag, BQ4_ETIMEOUT);
+  } else if (warp == kExMmaWarp) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = ptx::umma_idesc_f16(128, BT);
+      int stage = 0, pb = 0;
+      uint32_t phase = 0, pphase = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; ok && u < a.units && !*abort_flag; u += gridDim.x) {
+        const int split = u % S_split;
+        const int kc0 = (int)((int64_t)split * a.nkc / S_split);
+        const int kc1 = (int)((int64_t)(split + 1) * a.nkc / S_split);
+        uint32_t d_base = 0;
+        for (int kc = kc0; kc < kc1; ++kc) {
+          const bool first = seg_first(kc, kc0, cpb);
+          if (first) {
+            if (!ptx::mbar_wait(&part_empty[pb], pphase ^ 1, abort_flag)) { ok = false; break; }
+            ptx::tc_fence_after();
+            d_base = tmem_base + (uint32_t)pb * kPartCols;
+          }
+          if (!ptx::mbar_wait(&full[stage], phase, abort_flag)) { ok = false; break; }
+          ptx::tc_fence_after();
+          const uint32_t b_addr = ptx::smem_u32(b_tiles + (size_t)stage * kBTileBytes);
+#pragma unroll
+          for (int kk = 0; kk < kChunkK / 16; ++kk) {
+            const uint64_t b_desc = ptx::umma_desc_sw128(b_addr + kk * 32);
+#pragma unroll
+            for (int w = 0; w < NW; ++w) {
+              const uint32_t a_addr = ptx::smem_u32(a_tiles + ((size_t)stage * NW + w) * kATileBytes) + kk * 32;
+              ptx::mma_f16_ss(d_base + w * BT, ptx::umma_desc_sw128(a_addr), b_desc, idesc,
+                              (first && kk == 0) ? 0u : 1u);
+            }
+          }
+          ptx::mma_commit(&empty[stage]);
+          if (++stage == S) { stage = 0; phase ^= 1; }
+          if (seg_last(kc, kc1, cpb)) {
+            ptx::mma_commit(&part_full[pb]);
+            if (++pb == kNumPart) { pb = 0; pphase ^= 1; }
+          }
+        }
+      }
+      if (!ok) record_error(a, abort_flag, BQ4_ETIMEOUT);
+    }
+  } else if (warp < kExScalerWarps) {
+    // ------------------------------------------------ scaler + epilogue
+    const int quad = warp & 3;
+    const int row = quad * 32 + lane;          // output feature within the tile
+    const int col0 = (warp >> 2) * kCols;      // first token column of this thread
+    int pb = 0;
+    uint32_t pphase = 0;
+    bool ok = true;
+    for (int u = blockIdx.x; ok && u < a.units && !*abort_flag; u += gridDim.x) {
+      const int tile = u / S_split, split = u - tile * S_split;
+      const int ntile = tile / a.mtiles, mtile = tile - ntile * a.mtiles;
+      const int n = ntile * 128 + row;
+      const int m0 = mtile * BT + col0;
+      const int kc0 = (int)((int64_t)split * a.nkc / S_split);
+      const int kc1 = (int)((int64_t)(split + 1) * a.nkc / S_split);
+      float acc[NW][kCols];
+#pragma unroll
+      for (int w = 0; w < NW; ++w)
+#pragma unroll
+        for (int j = 0; j < kCols; ++j) acc[w][j] = 0.0f;
+      const float* srow[NW];
+#pragma unroll
+      for (int w = 0; w < NW; ++w) srow[w] = a.s[w] + (size_t)ntile * a.nkb * 128 + row;
+      for (int kc = kc0; kc < kc1; ++kc) {
+        if (!seg_last(kc, kc1, cpb)) continue;
+        const int kb = (kc * kChunkK) / a.block;
+        float sc[NW];
+#pragma unroll
+        for (int w = 0; w < NW; ++w) sc[w] = __ldg(srow[w] + (size_t)kb * 128);
+        if (!ptx::mbar_wait(&part_full[pb], pphase, abort_flag)) { ok = false; break; }
+        ptx::tc_fence_after();
+        const uint32_t t_row = tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)pb * kPartCols + col0;
+#pragma unroll
+        for (int w = 0; w < NW; ++w) {
+#pragma unroll
+          for (int c = 0; c < kCols / 16; ++c) {
+            uint32_t r0[16];
+            ptx::tmem_ld_32x32b_x16(t_row + w * BT + c * 16, r0);
+            ptx::tmem_ld_wait();
+#pragma unroll
+            for (int j = 0; j < 16; ++j) acc[w][c * 16 + j] = fmaf(sc[w], __uint_as_float(r0[j]), acc[w][c * 16 + j]);
+          }
+        }
+        ptx::tc_fence_before();
+        __syncwarp();
+        if (lane == 0) ptx::mbar_arrive(&part_empty[pb]);
+        if (++pb == kNumPart) { pb = 0; pphase ^= 1; }
+      }
+      if (!ok) break;
+
+      if (S_split == 1) {
+        float b0 = 0.0f, b1 = 0.0f;
+        if (n < a.N) {
+          if (a.bias[0]) b0 = __ldg(a.bias[0] + n);
+          if (NW == 2 && a.bias[1]) b1 = __ldg(a.bias[1] + n);
+          const int act = a.act;
+#pragma unroll
+          for (int j = 0; j < kCols; ++j) {
+            const int m = m0 + j;
+            if (m < a.M) {
+              float v;
+              if (NW == 2) {
+                v = silu(acc[0][j] + b0) * (acc[NW - 1][j] + b1);
+              } else {
+                v = apply_act(acc[0][j] + b0, act);
+                if (a.aux) v *= __ldg(a.aux + (size_t)m * a.N + n);
+              }
+              a.y[(size_t)m * a.N + n] = v;
+            }
+          }
+        }
+      } else {
+        float* part = a.partials + ((size_t)tile * S_split + split) * NW * 128 * BT;
+#pragma unroll
+        for (int w = 0; w < NW; ++w) {
+          float4* dst = reinterpret_cast<float4*>(part + ((size_t)w * 128 + row) * BT + col0);
+#pragma unroll
+          for (int j = 0; j < kCols / 4; ++j)
+            dst[j] = make_float4(acc[w][4 * j], acc[w][4 * j + 1], acc[w][4 * j + 2], acc[w][4 * j + 3]);
+        }
+        __threadfence();
+        asm volatile("bar.sync 1, 256;" ::: "memory");
+        if (threadIdx.x == 0) {
+          const int prev = atomicAdd(a.counters + tile, 1);
+          *last_flag = (prev == S_split - 1) ? 1 : 0;
+          if (prev == S_split - 1) a.counters[tile] = 0;
+        }
+        asm volatile("bar.sync 1, 256;" ::: "memory");
+        if (*last_flag) {
+          __threadfence();
+          const float* base = a.partials + (size_t)tile * S_split * NW * 128 * BT;
+#pragma unroll
+          for (int w = 0; w < NW; ++w)
+#pragma unroll
+            for (int j = 0; j < kCols; ++j) acc[w][j] = 0.0f;
+          for (int sp = 0; sp < S_split; ++sp) {
+#pragma unroll
+            for (int w = 0; w < NW; ++w) {
+              const float4* src =
+                  reinterpret_cast<const float4*>(base + ((size_t)sp * NW * 128 + w * 128 + row) * BT + col0);
+#pragma unroll
+              for (int j = 0; j < kCols / 4; ++j) {
+                const float4 v = __ldcg(src + j);
+                acc[w][4 * j] += v.x; acc[w][4 * j + 1] += v.y; acc[w][4 * j + 2] += v.z; acc[w][4 * j + 3] += v.w;
+              }
+            }
+          }
+          if (n < a.N) {
+            float b0 = 0.0f, b1 = 0.0f;
+            if (a.bias[0]) b0 = __ldg(a.bias[0] + n);
+            if (NW == 2 && a.bias[1]) b1 = __ldg(a.bias[1] + n);
+#pragma unroll
+            for (int j = 0; j < kCols; ++j) {
+              const int m = m0 + j;
+              if (m < a.M) {
+                float v;
+                if (NW == 2) {
+                  v = silu(acc[0][j] + b0) * (acc[NW - 1][j] + b1);
+                } else {
+                  v = apply_act(acc[0][j] + b0, a.act);
+                  if (a.aux) v *= __ldg(a.aux + (size_t)m * a.N + n);
+                }
+                a.y[(size_t)m * a.N + n] = v;
+              }
+            }
+          }
+        }
+        asm volatile("bar.sync 1, 256;" ::: "memory");
+      }
+    }
+    if (!ok) record_error(a, abort_flag, BQ4_ETIMEOUT);
+  }
+
+  ptx::tc_fence_before();
+  __syncthreads();
+  if (warp == kExMmaWarp) {
+    ptx::tc_fence_after();
+    ptx::tmem_dealloc(tmem_base, kTmemCols);
+  }
+}
+
 // ------------------------------------------------------------------ host side
 
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
@@ -484,14 +866,21 @@ EncodeTiledFn encode_fn() {
 
 size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
-template <int BT, int NW>
+template <int BT, int NW, bool EXACT>
 cudaError_t launch_kernel(const GemmPlan& plan, const CUtensorMap& tmap, const GemmArgs& args,
                           cudaStream_t stream) {
-  auto kern = q4_gemm_kernel<BT, NW>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       (int)plan.smem_bytes);
-  if (e != cudaSuccess) return e;
-  kern<<<plan.grid, kThreads, plan.smem_bytes, stream>>>(tmap, args);
+  cudaError_t e;
+  if constexpr (EXACT) {
+    auto kern = q4_gemm_exact_kernel<BT, NW>;
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)plan.smem_bytes);
+    if (e != cudaSuccess) return e;
+    kern<<<plan.grid, kExThreads, plan.smem_bytes, stream>>>(tmap, args);
+  } else {
+    auto kern = q4_gemm_kernel<BT, NW>;
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)plan.smem_bytes);
+    if (e != cudaSuccess) return e;
+    kern<<<plan.grid, kThreads, plan.smem_bytes, stream>>>(tmap, args);
+  }
   note_launch();
   return cudaGetLastError();
 }
@@ -523,7 +912,18 @@ bq4_status plan_gemm(const bq4_weight* w, int nw, int64_t M, int device, GemmPla
   if (M > (int64_t)1 << 30) return set_error(BQ4_EINVAL_SHAPE, "M too large");
   memset(p, 0, sizeof(*p));
   p->nw = nw;
-  if (nw == 1)
+  // Blocks of 64/128 K values keep q exact and scale the f32 accumulator
+  // (exact-weight kernel, token tile <= 128); smaller blocks fold the scale
+  // into the f16 weight (folded kernel, token tile <= 256).
+  p->pre = w->h != nullptr ? 1 : 0;
+  p->exact = (!p->pre && w->block >= 64) ? 1 : 0;
+  // BQ4_FORCE_FOLDED=1 selects the folded kernel for any block (tests and
+  // tuning compare both formulations on the same shapes).
+  if (const char* f = getenv("BQ4_FORCE_FOLDED"))
+    if (f[0] == '1') p->exact = 0;
+  if (p->exact)
+    p->bt = (nw == 1 && M > 64) ? 128 : 64;
+  else if (nw == 1)
     p->bt = M > 128 ? 256 : (M > 64 ? 128 : 64);
   else
     p->bt = M > 64 ? 128 : 64;
@@ -534,12 +934,16 @@ bq4_status plan_gemm(const bq4_weight* w, int nw, int64_t M, int device, GemmPla
   const int nkc = (int)w->nkc;
 
   // Split-K factor: minimise an estimated makespan.  One unit of work costs
-  // (chunks per split + fixed pipeline fill of ~3 chunks); waves quantise.
+  // (chunks per split + fixed pipeline fill of ~3 chunks).  Split-K is only
+  // used when every unit fits in a single wave (units <= SMs): a CTA that
+  // runs a second split unit was measured to produce wrong partial tiles,
+  // so multi-wave work uses whole-K units (S = 1).
   int best_s = 1;
   double best_t = 1e30;
   const int max_s = nkc < 16 ? nkc : 16;
   for (int s = 1; s <= max_s; ++s) {
     const int units = tiles * s;
+    if (s > 1 && units > sms) break;
     const int waves = (units + sms - 1) / sms;
     const double per_unit = (double)nkc / s + 3.0;
     const double fixup = s > 1 ? 1.0 + 0.25 * s : 0.0;
@@ -549,20 +953,34 @@ bq4_status plan_gemm(const bq4_weight* w, int nw, int64_t M, int device, GemmPla
       best_s = s;
     }
   }
+  // BQ4_FORCE_KSPLIT=s pins the split-K factor (clamped to [1, chunks] and
+  // to a single wave of units).
+  if (const char* f = getenv("BQ4_FORCE_KSPLIT")) {
+    int v = atoi(f);
+    if (v >= 1) best_s = v < nkc ? v : nkc;
+    while (best_s > 1 && tiles * best_s > sms) --best_s;
+  }
   p->ksplit = best_s;
   p->units = tiles * best_s;
   p->grid = p->units < sms ? p->units : sms;
 
   // Shared memory: operand ring (S stages) + raw ring (RS stages).
+  // The exact kernel's scaler warps read scales straight from global memory,
+  // so its raw stages carry nibbles only.
   const uint32_t raw_s_bytes = 512u * (uint32_t)(w->block >= 64 ? 1 : 64 / w->block);
   const size_t stage_bytes = (size_t)nw * kATileBytes + (size_t)p->bt * 128;
-  const size_t raw_stage_bytes = (size_t)nw * (kRawQBytes + raw_s_bytes);
+  // Per-weight raw stage: nibbles (+ scales for the folded kernel); the
+  // pre-expanded path leaves the ring unused.  The kernels carve shared
+  // memory with this same value (GemmArgs::raw_w_bytes).
+  p->raw_w_bytes = p->pre ? 16u : kRawQBytes + (p->exact ? 0u : raw_s_bytes);
+  const size_t raw_stage_bytes = (size_t)nw * p->raw_w_bytes;
   const size_t budget = 227 * 1024 - 1024 /*align*/ - 512 /*barriers*/;
   int S = 0, RS = 0;
   for (int s = 4; s >= 2; --s) {
     if ((size_t)s * stage_bytes >= budget) continue;
     int rs = (int)((budget - (size_t)s * stage_bytes) / raw_stage_bytes);
     if (rs > 8) rs = 8;
+    if (p->pre) rs = 4;  // unused ring
     if (rs >= 4 || s == 2) {
       S = s;
       RS = rs;
@@ -573,7 +991,7 @@ bq4_status plan_gemm(const bq4_weight* w, int nw, int64_t M, int device, GemmPla
   p->stages = S;
   p->raw_stages = RS;
   p->smem_bytes = 1024 + (size_t)S * stage_bytes + (size_t)RS * raw_stage_bytes +
-                  (size_t)(2 * S + 2 * RS + 4) * 8 + 16;
+                  (size_t)(2 * S + 2 * RS + 2 * kNumPart + 4) * 8 + 16;
 
   p->xh_bytes = align_up((size_t)M * (size_t)w->Kp * 2, 256);
   p->counter_bytes = align_up((size_t)tiles * sizeof(int) + sizeof(int) * 4, 256);
@@ -613,7 +1031,9 @@ bq4_status run_gemm(const GemmPlan& plan, const bq4_weight* const* ws, const flo
 
   GemmArgs args;
   memset(&args, 0, sizeof(args));
+  args.pre = plan.pre;
   for (int i = 0; i < plan.nw; ++i) {
+    args.h[i] = ws[i]->h;
     args.q[i] = ws[i]->q;
     args.s[i] = ws[i]->s;
     args.bias[i] = bias ? bias[i] : nullptr;
@@ -633,16 +1053,26 @@ bq4_status run_gemm(const GemmPlan& plan, const bq4_weight* const* ws, const flo
   args.units = plan.units;
   args.stages = plan.stages;
   args.raw_stages = plan.raw_stages;
-  args.raw_s_bytes = 512u * (uint32_t)(w0->block >= 64 ? 1 : 64 / w0->block);
+  args.raw_s_bytes = plan.exact ? 0u : 512u * (uint32_t)(w0->block >= 64 ? 1 : 64 / w0->block);
+  args.raw_w_bytes = plan.raw_w_bytes;
+  if (!plan.pre && !plan.exact && args.raw_w_bytes != kRawQBytes + args.raw_s_bytes)
+    return set_error(BQ4_EINVAL_ARG, "internal: raw stage size mismatch");
   args.act = act;
 
-  if (plan.nw == 1) {
-    if (plan.bt == 256) e = launch_kernel<256, 1>(plan, tmap, args, stream);
-    else if (plan.bt == 128) e = launch_kernel<128, 1>(plan, tmap, args, stream);
-    else e = launch_kernel<64, 1>(plan, tmap, args, stream);
+  if (plan.exact) {
+    if (plan.nw == 1) {
+      if (plan.bt == 128) e = launch_kernel<128, 1, true>(plan, tmap, args, stream);
+      else e = launch_kernel<64, 1, true>(plan, tmap, args, stream);
+    } else {
+      e = launch_kernel<64, 2, true>(plan, tmap, args, stream);
+    }
+  } else if (plan.nw == 1) {
+    if (plan.bt == 256) e = launch_kernel<256, 1, false>(plan, tmap, args, stream);
+    else if (plan.bt == 128) e = launch_kernel<128, 1, false>(plan, tmap, args, stream);
+    else e = launch_kernel<64, 1, false>(plan, tmap, args, stream);
   } else {
-    if (plan.bt == 128) e = launch_kernel<128, 2>(plan, tmap, args, stream);
-    else e = launch_kernel<64, 2>(plan, tmap, args, stream);
+    if (plan.bt == 128) e = launch_kernel<128, 2, false>(plan, tmap, args, stream);
+    else e = launch_kernel<64, 2, false>(plan, tmap, args, stream);
   }
   if (e != cudaSuccess) return check_cuda(e, "q4 gemm launch");
   return BQ4_OK;

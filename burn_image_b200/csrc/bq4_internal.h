@@ -31,6 +31,12 @@ struct bq4_weight {
   uint32_t* q;
   float* s;
   size_t q_bytes, s_bytes;
+  // Pre-expanded form (BQ4_LAYOUT_NPACKED sources): f16(q * scale) tiles,
+  // [ntiles][nkc][128 rows][64 K] f16 with the 128-byte swizzle already
+  // applied (16-byte chunk j of row r stored at chunk j ^ (r & 7)), so one
+  // 16 KiB bulk copy lands as an MMA-ready operand tile.  q/s unused.
+  uint16_t* h;
+  size_t h_bytes;
 };
 
 namespace bq4 {
@@ -47,6 +53,9 @@ void note_launch(uint64_t n = 1);
 cudaError_t launch_prepare(const uint32_t* words, const float* scales, int64_t K, int64_t N,
                            int32_t block, int32_t layout, int64_t n0, int64_t k0,
                            int64_t src_N, int64_t src_K, const bq4_weight* w, cudaStream_t s);
+cudaError_t launch_prepare_pre(const uint32_t* words, const float* scales, int64_t K, int64_t N,
+                               int32_t block, int64_t n0, int64_t k0, int64_t src_N, int64_t src_K,
+                               const bq4_weight* w, cudaStream_t s);
 cudaError_t launch_dequant_prepared(const bq4_weight* w, float* out, int32_t out_layout,
                                     cudaStream_t s);
 cudaError_t launch_dequant_raw(const uint32_t* words, const float* scales, int64_t K, int64_t N,
@@ -59,9 +68,12 @@ cudaError_t launch_convert_x(const float* x, int64_t M, int64_t K, int64_t ldx, 
 // ------------------------------------------------------------ GEMM (bq4_gemm_sm100.cu)
 struct GemmPlan {
   int nw;          // 1 = plain, 2 = gated (gate, up)
+  int exact;       // 1 = exact-weight kernel (scale on the f32 accumulator)
+  int pre;         // 1 = pre-expanded f16 weight tiles (bulk-copied, no dequant)
   int bt;          // tokens per tile (MMA N): 64, 128 or 256
   int mtiles, ntiles, ksplit, units, grid;
   int stages, raw_stages;
+  uint32_t raw_w_bytes;  // shared-memory bytes per weight per raw stage
   size_t smem_bytes;
   size_t xh_bytes, counter_bytes, partial_bytes;  // workspace pieces
   size_t workspace_bytes;

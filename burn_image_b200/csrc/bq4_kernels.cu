@@ -96,6 +96,37 @@ __global__ void dequant_prepared_kernel(const uint32_t* __restrict__ q, const fl
   }
 }
 
+// Pre-expanded tiles from an N-packed source (words [K][N/8], scales
+// [K][N/block], blocks along N).  One thread per 16-byte chunk = 8 K values
+// of one row n; stored at its 128-byte-swizzled position.
+__global__ void prepare_pre_kernel(const uint32_t* __restrict__ words, const float* __restrict__ scales,
+                                   int64_t N, int64_t K, int32_t block, int64_t n0, int64_t k0,
+                                   int64_t src_N, int64_t nkc, int64_t total, uint16_t* __restrict__ out) {
+  const int64_t NW8 = src_N / 8, NB = src_N / block;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t j = i & 7;
+    const int64_t r = (i >> 3) & 127;
+    const int64_t kc = (i >> 10) % nkc;
+    const int64_t tile = (i >> 10) / nkc;
+    const int64_t n = tile * 128 + r;
+    __align__(16) __half v[8];
+#pragma unroll
+    for (int t = 0; t < 8; ++t) {
+      const int64_t k = kc * 64 + j * 8 + t;
+      float val = 0.0f;
+      if (n < N && k < K) {
+        const int64_t sn = n0 + n, sk = k0 + k;
+        const uint32_t word = words[sk * NW8 + sn / 8];
+        val = static_cast<float>(nibble_s4(word, static_cast<int>(sn & 7))) * scales[sk * NB + sn / block];
+      }
+      v[t] = __float2half_rn(val);
+    }
+    uint16_t* dst = out + ((tile * nkc + kc) * 128 + r) * 64 + ((j ^ (r & 7)) * 8);
+    *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(v);
+  }
+}
+
 __global__ void dequant_raw_kernel(const uint32_t* __restrict__ words, const float* __restrict__ scales,
                                    int64_t K, int64_t N, int32_t block, int32_t layout,
                                    int32_t out_layout, float* __restrict__ out) {
@@ -111,9 +142,15 @@ __global__ void dequant_raw_kernel(const uint32_t* __restrict__ words, const flo
       n = i / K;
       k = i - n * K;
     }
-    const uint32_t word = raw_word(words, layout, n, k >> 3, N, KW);
-    const float sc = raw_scale(scales, layout, n, k / block, N, KB);
-    out[i] = static_cast<float>(nibble_s4(word, static_cast<int>(k & 7))) * sc;
+    if (layout == BQ4_LAYOUT_NPACKED) {
+      const uint32_t word = words[k * (N / 8) + (n >> 3)];
+      const float sc = scales[k * (N / block) + n / block];
+      out[i] = static_cast<float>(nibble_s4(word, static_cast<int>(n & 7))) * sc;
+    } else {
+      const uint32_t word = raw_word(words, layout, n, k >> 3, N, KW);
+      const float sc = raw_scale(scales, layout, n, k / block, N, KB);
+      out[i] = static_cast<float>(nibble_s4(word, static_cast<int>(k & 7))) * sc;
+    }
   }
 }
 
@@ -185,6 +222,17 @@ cudaError_t launch_prepare(const uint32_t* words, const float* scales, int64_t K
   const int64_t stotal = w->ntiles * w->nkb * 128;
   prepare_s_kernel<<<grid_for(stotal, 256, dev), 256, 0, s>>>(scales, layout, N, K, block, n0, k0,
                                                                src_N, src_K, w->nkb, stotal, w->s);
+  note_launch();
+  return cudaGetLastError();
+}
+
+cudaError_t launch_prepare_pre(const uint32_t* words, const float* scales, int64_t K, int64_t N,
+                               int32_t block, int64_t n0, int64_t k0, int64_t src_N, int64_t src_K,
+                               const bq4_weight* w, cudaStream_t s) {
+  (void)src_K;
+  const int64_t total = w->ntiles * w->nkc * 1024;
+  prepare_pre_kernel<<<grid_for(total, 256, current_device()), 256, 0, s>>>(
+      words, scales, N, K, block, n0, k0, src_N, w->nkc, total, w->h);
   note_launch();
   return cudaGetLastError();
 }

@@ -117,13 +117,13 @@ class QuantScheme:
         return (self.mode == "Symmetric" and self.value == "Q4S" and self.param == "F32"
                 and self.store_packed_dim in (0, 1) and lvl_ok)
 
-    def to_c(self) -> L.QuantScheme:
+    def to_c(self, transposed_view: bool = True) -> L.QuantScheme:
         return L.QuantScheme(value=0 if self.value == "Q4S" else 99,
                              mode=0 if self.mode == "Symmetric" else 99,
                              param=0 if self.param == "F32" else 99,
                              store_packed_dim=self.store_packed_dim,
                              block_rank=len(self.level) if (len(self.level) == 1 or self.level[-1] == 1) else 99,
-                             block=self.block)
+                             block=self.block, rhs_transposed_view=1 if transposed_view else 0)
 
 
 # --------------------------------------------------------------------- workspace
@@ -178,12 +178,11 @@ class PreparedQ4Weight:
         self.device = dev
 
     @classmethod
-    def from_packed(cls, packed: PackedQ4, device=None) -> "PreparedQ4Weight":
-        layout = L.LAYOUT_COL if packed.scheme.store_packed_dim == 0 else L.LAYOUT_ROW
-        if layout == L.LAYOUT_COL:
-            N, K = packed.shape[-2], packed.shape[-1]
-        else:
-            K, N = packed.shape
+    def from_packed(cls, packed: PackedQ4, device=None, stored: str = "nk") -> "PreparedQ4Weight":
+        """stored: for a PackedU32(0) tensor, "nk" = stored [N,K] and used
+        through its transposed view (Qwen); "kn" = a plain [K,N] tensor
+        (packed and blocked along N)."""
+        K, N, layout = physical_layout(packed.scheme, packed.shape, stored)
         return cls(packed.words, packed.scales, K, N, packed.scheme.block, layout, device)
 
     @property
@@ -229,6 +228,18 @@ class PreparedQ4Weight:
         check(L.lib().bq4_linear(self._h, _ptr(x2), M, x2.stride(0), _ptr(bias), act, _ptr(aux), _ptr(y),
                                  _ptr(ws), ws.numel(), _stream_ptr(self.device)))
         return y.reshape(*lead, self.N)
+
+
+def physical_layout(scheme: QuantScheme, shape: tuple, stored: str = "nk"):
+    """(K, N, bq4 layout) of a packed tensor of stored `shape`."""
+    if scheme.store_packed_dim == 1:
+        K, N = shape
+        return K, N, L.LAYOUT_ROW
+    if stored == "nk":
+        N, K = shape[-2], shape[-1]
+        return K, N, L.LAYOUT_COL
+    K, N = shape[-2], shape[-1]
+    return K, N, L.LAYOUT_NPACKED
 
 
 def linear_gated(gate: PreparedQ4Weight, up: PreparedQ4Weight, x: torch.Tensor,
@@ -284,24 +295,27 @@ class QuantizedTensor:
     scales: torch.Tensor
     shape: tuple
     scheme: QuantScheme
+    transposed_view: bool = True  # PackedU32(0) only: stored [N,K] seen as [K,N] (Qwen)
     _prepared: Optional[PreparedQ4Weight] = field(default=None, repr=False)
 
     @classmethod
-    def from_packed(cls, packed: PackedQ4, device) -> "QuantizedTensor":
+    def from_packed(cls, packed: PackedQ4, device, stored: str = "nk") -> "QuantizedTensor":
         dev = torch.device(device)
         values = torch.as_tensor(packed.words.view(np.int32)).to(dev)
         scales = torch.as_tensor(packed.scales).to(dev)
-        if packed.scheme.store_packed_dim == 0:
-            N, K = packed.shape[-2], packed.shape[-1]
-        else:
-            K, N = packed.shape
-        return cls(values, scales, (K, N), packed.scheme)
+        K, N, layout = physical_layout(packed.scheme, packed.shape, stored)
+        return cls(values, scales, (K, N), packed.scheme, layout == L.LAYOUT_COL)
+
+    @property
+    def layout(self) -> int:
+        if self.scheme.store_packed_dim == 1:
+            return L.LAYOUT_ROW
+        return L.LAYOUT_COL if self.transposed_view else L.LAYOUT_NPACKED
 
     def prepared(self) -> PreparedQ4Weight:
         if self._prepared is None:
             K, N = self.shape
-            layout = L.LAYOUT_COL if self.scheme.store_packed_dim == 0 else L.LAYOUT_ROW
-            self._prepared = PreparedQ4Weight(self.values, self.scales, K, N, self.scheme.block, layout,
+            self._prepared = PreparedQ4Weight(self.values, self.scales, K, N, self.scheme.block, self.layout,
                                               self.values.device)
         return self._prepared
 
@@ -325,9 +339,9 @@ def q_matmul(lhs: torch.Tensor, rhs: QuantizedTensor) -> torch.Tensor:
     out = torch.empty((M, N), dtype=torch.float32, device=lhs.device)
     nbytes = ctypes.c_size_t()
     with torch.cuda.device(lhs.device):
-        check(L.lib().bq4_q_matmul_workspace_size(M, K, N, rhs.scheme.block, ctypes.byref(nbytes)))
+        sch = rhs.scheme.to_c(rhs.transposed_view)
+        check(L.lib().bq4_q_matmul_workspace_size(M, K, N, ctypes.byref(sch), ctypes.byref(nbytes)))
         ws = Workspace.get(lhs.device, nbytes.value)
-        sch = rhs.scheme.to_c()
         check(L.lib().bq4_q_matmul(_ptr(x), M, K, _ptr(rhs.values), _ptr(rhs.scales), N, ctypes.byref(sch),
                                    _ptr(out), _ptr(ws), ws.numel(), _stream_ptr(lhs.device)))
     return out.reshape(*lead, N)

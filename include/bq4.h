@@ -10,11 +10,15 @@
  * Format (Q4S): signed 4-bit, symmetric, one f32 scale per block of `block`
  * consecutive K values (block in {8,16,32,64,128}); 8 values per
  * little-endian u32 word, value i at bits [4i, 4i+3], two's complement.
- * Two physical layouts exist in the reference:
- *   BQ4_LAYOUT_COL (QuantStore::PackedU32(0) of a [N,K] tensor, Qwen):
- *       words [N][K/8], scales [N][K/block]
+ * Three physical layouts reach the reference op:
+ *   BQ4_LAYOUT_COL (QuantStore::PackedU32(0) of a [N,K] tensor seen through a
+ *       transposed view, Qwen): words [N][K/8], scales [N][K/block]
  *   BQ4_LAYOUT_ROW (QuantStore::PackedU32(1) of a [K,N] tensor, Boogu):
  *       words [K/8][N], scales [K/block][N]
+ *   BQ4_LAYOUT_NPACKED (QuantStore::PackedU32(0) of a plain [K,N] tensor,
+ *       blocks along N, as in crates/burn_boogu/src/artifacts.rs:10501-10584):
+ *       words [K][N/8], scales [K][N/block]; needs N % 8 == 0, N % block == 0.
+ *       Its scale changes along K, so it is prepared as pre-expanded f16 tiles.
  *
  * Conventions: all tensor pointers passed to compute calls are DEVICE
  * pointers on the weight's device; work is enqueued on `stream` (0 = the
@@ -54,7 +58,7 @@ typedef enum {
   BQ4_EUNSUPPORTED = 10   /* no kernel for this device (not sm_100) */
 } bq4_status;
 
-typedef enum { BQ4_LAYOUT_COL = 0, BQ4_LAYOUT_ROW = 1 } bq4_layout;
+typedef enum { BQ4_LAYOUT_COL = 0, BQ4_LAYOUT_ROW = 1, BQ4_LAYOUT_NPACKED = 2 } bq4_layout;
 
 typedef enum {
   BQ4_ACT_NONE = 0,
@@ -74,8 +78,8 @@ BQ4_API const char* bq4_last_error_string(void);
  * patches/burn-cubecl-0.21.0/src/ops/qtensor.rs:64-158, called from the loader
  * hook `q_from_data`, :167-195).  `packed_words`/`scales` may be host or
  * device pointers (detected); the result lives on `device`.  K is the
- * reduction (input) width, N the output width; K % 8 == 0, K % block == 0.
- * Allocates device memory (load time only).
+ * reduction (input) width, N the output width; K % 8 == 0, K % block == 0
+ * (COL/ROW).  Allocates device memory (load time only).
  */
 BQ4_API bq4_status bq4_weight_prepare(const uint32_t* packed_words, const float* scales, int64_t K,
                               int64_t N, int32_t block, bq4_layout layout, int32_t device,
@@ -131,7 +135,8 @@ BQ4_API bq4_status bq4_linear_gated(const bq4_weight* gate, const bq4_weight* up
 /*
  * Bit-exact dequantization of a prepared weight: out = q * scale in f32,
  * written as the logical tensor of `out_layout` (BQ4_LAYOUT_ROW: [K][N],
- * BQ4_LAYOUT_COL: [N][K]).  Mirrors the reference `dequantize`
+ * BQ4_LAYOUT_COL: [N][K]).  Not available for weights prepared from
+ * BQ4_LAYOUT_NPACKED (use bq4_dequant_raw).  Mirrors the reference `dequantize`
  * (patches/burn-cubecl-0.21.0/src/kernel/quantization/dequantize.rs:6-33).
  */
 BQ4_API bq4_status bq4_dequant(const bq4_weight* w, float* out, bq4_layout out_layout, bq4_stream_t stream);
@@ -157,11 +162,14 @@ typedef struct {
   int32_t store_packed_dim; /* 0 = PackedU32(0), 1 = PackedU32(1) */
   int32_t block_rank;  /* 1 = Block([b]), 2 = Block([b,1]) */
   int32_t block;       /* b */
+  int32_t rhs_transposed_view; /* PackedU32(0) only: 1 = rhs is the swapped-dims view of a
+                                  stored [N,K] tensor (Qwen; packed along K), 0 = stored as a
+                                  plain [K,N] tensor (packed and blocked along N) */
 } bq4_quant_scheme;
 
 /* Workspace for bq4_q_matmul: covers an internal prepared copy of rhs. */
-BQ4_API bq4_status bq4_q_matmul_workspace_size(int64_t M, int64_t K, int64_t N, int32_t block,
-                                       size_t* bytes);
+BQ4_API bq4_status bq4_q_matmul_workspace_size(int64_t M, int64_t K, int64_t N,
+                                               const bq4_quant_scheme* scheme, size_t* bytes);
 
 /*
  * lhs f32 [M,K] (contiguous, M = product of leading dims) times the

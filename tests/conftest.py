@@ -32,11 +32,17 @@ def pytest_collection_modifyitems(config, items):
 # in [-8, 7] drawn directly as nibbles; f32 scales |U(0.001, 0.02)|; bias ~N(0, 0.02).
 
 def gen_q4(K: int, N: int, block: int, layout: int, rng: np.random.Generator):
-    """Raw reference-packed words and scales for a K x N weight."""
+    """Raw reference-packed words and scales for a K x N weight (layout 0 COL,
+    1 ROW, 2 NPACKED)."""
     q = rng.integers(-8, 8, size=(K, N), dtype=np.int64)  # logical [K][N]
     nib = (q & 0xF).astype(np.uint32)
     scales_kn = np.abs(rng.uniform(0.001, 0.02, size=(K // block, N))).astype(np.float32)
-    if layout == 1:  # ROW: words [K/8][N]
+    if layout == 2:  # NPACKED: words [K][N/8] (8 consecutive N per word), scales [K][N/b]
+        w = np.zeros((K, N // 8), dtype=np.uint32)
+        for lane in range(8):
+            w |= nib[:, lane::8] << np.uint32(4 * lane)
+        s = np.abs(rng.uniform(0.001, 0.02, size=(K, N // block))).astype(np.float32)
+    elif layout == 1:  # ROW: words [K/8][N]
         w = np.zeros((K // 8, N), dtype=np.uint32)
         for lane in range(8):
             w |= nib[lane::8, :] << np.uint32(4 * lane)

@@ -57,7 +57,11 @@ def scales_kn(scales, K, N, block, layout):
 
 
 def staged_weight(words, scales, K, N, block, layout):
-    """Emulation of the kernel's weight staging: f16(q * f16(scale))."""
+    """Emulation of the kernel's weight staging: blocks of 64/128 keep
+    q * scale exact (the scale multiplies the f32 accumulator); smaller
+    blocks stage f16(q * f16(scale))."""
+    if block >= 64:
+        return O.unpack(words, scales, K, N, block, layout)
     q = decode_q(words, K, N, layout).astype(np.float16)
     s = scales_kn(scales, K, N, block, layout).astype(np.float16)
     return (q * s).astype(np.float16).astype(np.float32)
@@ -72,18 +76,27 @@ def report(name, got, ref):
 
 # ---------------------------------------------------------------- dequant
 
-@pytest.mark.parametrize("layout", [O.LAYOUT_ROW, O.LAYOUT_COL])
+def unpack_any(w, s, K, N, block, layout):
+    """Oracle unpack; the N-packed layout is the transpose of a column-layout
+    tensor of shape [K rows][N inner]."""
+    if layout == L.LAYOUT_NPACKED:
+        return O.unpack(w, s, N, K, block, O.LAYOUT_COL).T.copy()
+    return O.unpack(w, s, K, N, block, layout)
+
+
+@pytest.mark.parametrize("layout", [O.LAYOUT_ROW, O.LAYOUT_COL, L.LAYOUT_NPACKED])
 @pytest.mark.parametrize("block", [8, 16, 32, 64, 128])
 def test_dequant_raw_bit_exact(layout, block, rng):
-    K, N = 256, 136
+    K, N = 256, 384 if layout == L.LAYOUT_NPACKED else 136
     w, s = gen_q4(K, N, block, layout, rng)
-    ref = O.unpack(w, s, K, N, block, layout)
+    ref = unpack_any(w, s, K, N, block, layout)
+    wd, sd = dev(w), dev(s)
     out = torch.empty((K, N), dtype=torch.float32, device=DEV)
-    L.check(L.lib().bq4_dequant_raw(p(dev(w)), p(dev(s)), K, N, block, layout, p(out), L.LAYOUT_ROW, stream()))
+    L.check(L.lib().bq4_dequant_raw(p(wd), p(sd), K, N, block, layout, p(out), L.LAYOUT_ROW, stream()))
     torch.cuda.synchronize()
     assert np.array_equal(out.cpu().numpy(), ref)
     out_t = torch.empty((N, K), dtype=torch.float32, device=DEV)
-    L.check(L.lib().bq4_dequant_raw(p(dev(w)), p(dev(s)), K, N, block, layout, p(out_t), L.LAYOUT_COL, stream()))
+    L.check(L.lib().bq4_dequant_raw(p(wd), p(sd), K, N, block, layout, p(out_t), L.LAYOUT_COL, stream()))
     torch.cuda.synchronize()
     assert np.array_equal(out_t.cpu().numpy(), ref.T)
 
@@ -137,15 +150,16 @@ def test_exact_representable_fixture_gpu():
 
 
 def test_wave_fixture_gpu():
-    """crates/burn_boogu/src/artifacts.rs:10501-10584 thresholds on the GPU path."""
+    """crates/burn_boogu/src/artifacts.rs:10501-10584 thresholds on the GPU path:
+    the plain [input=128, output=128] tensor packed (and blocked) along its
+    last axis is used directly as the matmul rhs (BQ4_LAYOUT_NPACKED)."""
     import os
     g = dict(np.load(os.path.join(os.path.dirname(__file__), "golden", "wave_block128.npz")))
-    # the [128,128] tensor packed along its last axis is a column-layout weight
-    pw = q4.PreparedQ4Weight(dev(g["words"]), dev(g["scales"]), 128, 128, 128, O.LAYOUT_COL, DEV)
+    pw = q4.PreparedQ4Weight(dev(g["words"]), dev(g["scales"]), 128, 128, 128, L.LAYOUT_NPACKED, DEV)
     x = g["input"].reshape(1, 128)
     y = pw.linear(dev(x)).cpu().numpy()[0]
-    v = g["values"].reshape(128, 128)  # [n][k]
-    ref = v.astype(np.float64) @ x[0].astype(np.float64)
+    v = g["values"].reshape(128, 128)  # [input k][output n]
+    ref = x[0].astype(np.float64) @ v.astype(np.float64)
     err = np.sqrt(((y - ref) ** 2).sum() / (ref ** 2).sum())
     cos = (y * ref).sum() / np.linalg.norm(y) / np.linalg.norm(ref)
     assert err < 0.08 and cos > 0.996
@@ -190,6 +204,44 @@ def test_linear_parity(M, K, N, block, layout, act, with_bias, with_aux, rng):
     ref_s = O.linear_f64(xs, Ws, bias, act, aux)
     tight = 2e-3 if act != O.ACT_NONE else 1e-5  # GELU/SiLU use approximate tanh/exp
     assert report("  staged", y, ref_s) <= tight
+
+
+def test_column_layout_kernel_rel_rmse():
+    """crates/burn_qwen3_vl/src/artifacts.rs:1877-2049: Qwen column layout
+    through qwen_linear_forward; kernel rel-RMSE vs the dequantized f32
+    matmul < 1e-4 (the exact-weight kernel keeps q * scale exact), quantized
+    vs raw rel-RMSE < 0.12, cosine > 0.993, rank-3 equals rank-2 (< 1e-5)."""
+    import os
+    g = dict(np.load(os.path.join(os.path.dirname(__file__), "golden", "col_layout_256x128.npz")))
+    packed = q4.PackedQ4(g["words"].reshape(-1), g["scales"].reshape(-1), (256, 128), q4.QuantScheme())
+    lin = q4.Q4Linear(q4.QuantizedTensor.from_packed(packed, DEV, stored="nk"))
+    x = g["input"].reshape(1, 128)
+    y = q4.qwen_linear_forward(lin, dev(x)).cpu().numpy()[0]
+    y3 = q4.qwen_linear_forward(lin, dev(x.reshape(1, 1, 128))).cpu().numpy().reshape(-1)
+    assert np.abs(y3 - y).max() < 1e-5
+    W = O.unpack(g["words"], g["scales"], 128, 256, 128, O.LAYOUT_COL)
+    quant_ref = O.linear_f64(x, W)[0].astype(np.float64)
+    raw_ref = g["raw"].reshape(256, 128).astype(np.float64) @ x[0].astype(np.float64)
+    kernel_rmse = np.sqrt(((y - quant_ref) ** 2).sum() / (quant_ref ** 2).sum())
+    rmse = np.sqrt(((y - raw_ref) ** 2).sum() / (raw_ref ** 2).sum())
+    cos = (y * raw_ref).sum() / np.linalg.norm(y) / np.linalg.norm(raw_ref)
+    print(f"column layout: kernel rel-RMSE={kernel_rmse:.3e} rel-RMSE={rmse:.3e} cos={cos:.5f}")
+    assert kernel_rmse < 1e-4 and rmse < 0.12 and cos > 0.993
+
+
+@pytest.mark.parametrize("M,K,N,block", [(33, 200, 256, 8), (130, 512, 384, 128)])
+def test_npacked_linear_parity(M, K, N, block, rng):
+    """Plain [K,N] PackedU32(0) rhs (blocks along N) via q_matmul."""
+    w, s = gen_q4(K, N, block, L.LAYOUT_NPACKED, rng)
+    x = gen_x(M, K, rng)
+    W = unpack_any(w, s, K, N, block, L.LAYOUT_NPACKED)
+    ref = O.linear_f64(x, W)
+    qt = q4.QuantizedTensor(dev(w), dev(s), (K, N), q4.QuantScheme(store_packed_dim=0, level=(block,)),
+                            transposed_view=False)
+    y = q4.q_matmul(dev(x), qt).cpu().numpy()
+    assert report(f"npacked M{M}", y, ref) <= TOL
+    y2 = qt.prepared().linear(dev(x)).cpu().numpy()
+    assert np.array_equal(y, y2)
 
 
 def test_linear_strided_input(rng):
@@ -292,7 +344,7 @@ def test_baseline_shapes_vs_torch_fp32(M, K, N, act):
     bias = torch.randn(N, generator=g, device=DEV) * 0.02
     pw = q4.PreparedQ4Weight(words.contiguous(), scales, K, N, 128, L.LAYOUT_ROW, DEV)
     W = pw.dequantize()
-    ref = torch.addmm(bias, x.double(), W.double())
+    ref = torch.addmm(bias.double(), x.double(), W.double())
     if act == 1:
         ref = torch.nn.functional.gelu(ref, approximate="tanh")
     y = pw.linear(x, bias, act)
