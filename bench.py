@@ -45,6 +45,10 @@ def parse():
     ap.add_argument("--blocks", type=int, default=BLOCKS)
     ap.add_argument("--tokens", type=int, default=TOKENS)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--linear", default=None,
+                    help="M,K,N[,act[,block]]: time one fused Q4 linear instead of the stack "
+                         "(profiling / per-config rows; act 0 none, 1 gelu-tanh)")
+    ap.add_argument("--gated", default=None, help="M,K,N: time one fused SiLU-gate linear pair")
     return ap.parse_args()
 
 
@@ -321,10 +325,62 @@ def run_ours(args):
         dist.destroy_process_group()
 
 
+def run_linear(args):
+    """One fused linear (or gated pair) on cuda:0, events around each call."""
+    import torch
+
+    from burn_image_b200 import _lib as L
+    from burn_image_b200 import q4, tp
+    dev = torch.device("cuda", 0)
+    gated = args.gated is not None
+    f = [int(v) for v in (args.gated or args.linear).split(",")]
+    M, K, N = f[:3]
+    act = f[3] if len(f) > 3 and not gated else 0
+    block = f[4] if len(f) > 4 else QBLOCK
+    g = torch.Generator(device=dev).manual_seed(7)
+    w, s = tp._random_packed(K, N, block, g, dev)
+    pw = q4.PreparedQ4Weight(w, s, K, N, block, L.LAYOUT_ROW, dev)
+    if gated:
+        w2, s2 = tp._random_packed(K, N, block, g, dev)
+        pu = q4.PreparedQ4Weight(w2, s2, K, N, block, L.LAYOUT_ROW, dev)
+    # inputs larger than L2 are rotated between iterations (several copies)
+    copies = max(1, min(8, int(2 * 126e6 // (M * K * 4)) + 1))
+    xs = [torch.randn((M, K), generator=g, device=dev) for _ in range(copies)]
+    y = torch.empty((M, N), dtype=torch.float32, device=dev)
+    bias = torch.randn(N, generator=g, device=dev) * 0.02
+
+    def call(i):
+        if gated:
+            q4.linear_gated(pw, pu, xs[i % copies], out=y)
+        else:
+            pw.linear(xs[i % copies], bias, act, out=y)
+
+    for i in range(args.warmup):
+        call(i)
+    torch.cuda.synchronize()
+    st = torch.cuda.current_stream(dev)
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    for i in range(args.steps):
+        ev[i][0].record(st)
+        call(i)
+        ev[i][1].record(st)
+    torch.cuda.synchronize()
+    q4.poll_device_error()
+    ms = sorted(a.elapsed_time(b) for a, b in ev)
+    med = ms[len(ms) // 2]
+    flops = 2 * M * K * N * (2 if gated else 1)
+    nbytes = (N * K // 2 + N * K // block * 4) * (2 if gated else 1) + M * K * 4 + M * N * 4
+    print(json.dumps({"metric": "Q4 linear TFLOP/s", "value": flops / med / 1e9, "unit": "TFLOP/s",
+                      "ms": med, "gbs": nbytes / med / 1e6, "shape": [M, K, N], "act": act, "block": block,
+                      "gated": gated, "steps": args.steps}))
+
+
 def main():
     args = parse()
     if args.impl == "reference":
         run_reference(args)
+    elif args.linear or args.gated:
+        run_linear(args)
     else:
         run_ours(args)
 

@@ -121,7 +121,7 @@ bq4_status prepare_window(const uint32_t* words, const float* scales, int64_t sr
   w->block = block;
   w->layout = layout;
   w->device = device;
-  w->Kp = (K + kChunkK - 1) / kChunkK * kChunkK;
+  w->Kp = (K + kStageK - 1) / kStageK * kStageK;
   w->nkc = w->Kp / kChunkK;
   w->nkb = w->Kp / block;
   w->ntiles = (N + kTileN - 1) / kTileN;
@@ -398,7 +398,7 @@ static void q_matmul_view(int64_t K, int64_t N, int32_t block, int32_t layout, b
   w->K = K;
   w->N = N;
   w->block = block;
-  w->Kp = (K + kChunkK - 1) / kChunkK * kChunkK;
+  w->Kp = (K + kStageK - 1) / kStageK * kStageK;
   w->nkc = w->Kp / kChunkK;
   w->nkb = w->Kp / block;
   w->ntiles = (N + kTileN - 1) / kTileN;

@@ -40,33 +40,8 @@
 namespace bq4 {
 namespace {
 
-constexpr int kThreads = 352;
-constexpr int kEpiWarps = 4;
-constexpr int kDqWarp0 = 4;
-constexpr int kTmaWarp = 8;
-constexpr int kRawWarp = 9;
-constexpr int kMmaWarp = 10;
 constexpr uint32_t kATileBytes = 128 * 128;  // 128 rows x 64 f16
 constexpr uint32_t kRawQBytes = 4096;        // 128 rows x 64 nibbles
-
-struct GemmArgs {
-  const uint16_t* h[2];  // pre-expanded f16 tiles (pre == 1)
-  int pre;
-  const uint32_t* q[2];
-  const float* s[2];
-  const float* bias[2];
-  const float* aux;
-  float* y;
-  float* partials;
-  int* counters;
-  int M, N;
-  int nkc, nkb, block;
-  int ntiles, mtiles, ksplit, units;
-  int stages, raw_stages;
-  uint32_t raw_s_bytes;  // scale bytes per weight per raw stage (bulk-copied)
-  uint32_t raw_w_bytes;  // shared-memory bytes per weight per raw stage (host-computed)
-  int act;
-};
 
 __device__ __forceinline__ float gelu_tanh(float v) {
   // Burn Gelu::new_approximate: 0.5 v (1 + tanh(sqrt(2/pi) (v + 0.044715 v^3)))
@@ -102,6 +77,22 @@ __device__ __forceinline__ uint4 expand_word(uint32_t w, uint32_t scale2) {
   return make_uint4(p[0], p[1], p[2], p[3]);
 }
 
+// Expand one prepared word into 8 exact f16 values q (no scale): the
+// exact-weight formulation multiplies the f32 partial of each K block by
+// the scale instead.
+__device__ __forceinline__ uint4 expand_word_exact(uint32_t w) {
+  const uint32_t magic = 0x64086408u;
+  uint32_t p[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const uint32_t src = w >> (4 * i);
+    uint32_t t;
+    asm("lop3.b32 %0, %1, %2, %3, 0x6a;" : "=r"(t) : "r"(src), "r"(0x000F000Fu), "r"(magic));
+    asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(p[i]) : "r"(t), "r"(magic));
+  }
+  return make_uint4(p[0], p[1], p[2], p[3]);
+}
+
 __device__ __forceinline__ uint32_t scale_to_f16x2(float s) {
   uint16_t h;
   asm("cvt.rn.satfinite.f16.f32 %0, %1;" : "=h"(h) : "f"(s));
@@ -116,622 +107,325 @@ __device__ int g_bq4_device_error = 0;
 
 namespace {
 
-__device__ __forceinline__ void record_error(const GemmArgs& a, volatile int* abort_flag, int code) {
-  (void)a;
+__device__ __forceinline__ void record_error_flag(volatile int* abort_flag, int code) {
   if (!*abort_flag) {
     *abort_flag = 1;
     atomicCAS(&g_bq4_device_error, 0, code);
   }
 }
 
-template <int BT, int NW>
-__global__ void __launch_bounds__(kThreads, 1)
-    q4_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const GemmArgs a) {
-  extern __shared__ uint8_t smem_raw[];
-  // 1024-byte alignment for the swizzled operand tiles.
-  uint8_t* smem = reinterpret_cast<uint8_t*>(
-      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+// ---------------------------------------------------------------------------
+// Unified warp-specialized kernel (both numerics modes).
+//
+// The MMA issuer is a single thread, and every mbarrier wait and
+// tcgen05.commit on its path costs hundreds of cycles; the pipeline is
+// therefore organised so that it waits and commits once per 128-K stage
+// (8 MMAs of 128 x BT x 16 per weight):
+//   operand ring (S stages): per stage, A = NW x two 64-K sub-tiles of the
+//     MMA-ready weight tile [128 rows][64] f16 (written by the dequant warps,
+//     or bulk-copied pre-expanded tiles) and B = two 64-K token sub-tiles
+//     [BT][64] f16 (TMA), all with the 128-byte swizzle; one full and one
+//     empty mbarrier per stage.
+//   raw ring (RS stages): the prepared nibbles of a stage (2 x 4 KiB per
+//     weight, + scales in folded mode), by 1-D bulk copy.
+// TMEM: NP partial accumulators of NW*BT columns.  A unit's K range is cut
+// into segments (one K block of 64/128 in exact mode; the whole unit in
+// folded mode); the MMA accumulates a segment into one partial buffer and
+// the scaler warps fold it into f32 registers: acc += scale * partial
+// (scale = 1 in folded mode).  The epilogue runs from those registers.
+//
+// Warps (896 threads, 7 warpgroups, registers rebalanced with setmaxnreg):
+//   WG0-3 (warps 0-15)  scaler + epilogue, 96 regs: warp w reads TMEM lanes
+//                       32*(w%4).. and the token-column quarter w/4.
+//   WG4-5 (warps 16-23) dequant, 48 regs: thread t handles row t%128 of
+//                       64-K sub-tile t/128 (8 words) of each stage.
+//   WG6   (warps 24-27) 24 token TMA, 25 weight producer, 26 MMA issuer /
+//                       TMEM owner, 27 idle; 24 regs.
+// ---------------------------------------------------------------------------
+constexpr int kWsThreads = 896;
+constexpr int kWsRegsLaunch = 72;       // 65536 / 896, rounded down to 8
+constexpr int kWsRegsScaler = 96;       // 4*96 + 2*48 + 24 = 504 = 7*72
+constexpr int kWsRegsDequant = 48;
+constexpr int kWsRegsProducer = 24;
+constexpr int kWsTmaWarp = 24, kWsWeightWarp = 25, kWsMmaWarp = 26;
+constexpr int kWsDqWarp0 = 16, kWsDqWarps = 8, kWsScalerWarps = 16;
+constexpr uint32_t kRawStageQBytes = 2 * kRawQBytes;  // nibbles of one 128-K stage
 
-  const int S = a.stages, RS = a.raw_stages;
-  constexpr uint32_t kBTileBytes = BT * 128;
-  uint8_t* a_tiles = smem;                                        // [S][NW][16 KiB]
-  uint8_t* b_tiles = a_tiles + (size_t)S * NW * kATileBytes;      // [S][BT*128]
-  uint8_t* raw = b_tiles + (size_t)S * kBTileBytes;               // [RS][NW][4 KiB + scales]
-  const uint32_t raw_w_bytes = a.raw_w_bytes;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(raw + (size_t)RS * NW * raw_w_bytes);
-  uint64_t* full = bars;
-  uint64_t* empty = full + S;
-  uint64_t* raw_full = empty + S;
-  uint64_t* raw_empty = raw_full + RS;
-  uint64_t* tmem_full = raw_empty + RS;
-  uint64_t* tmem_empty = tmem_full + 2;
-  uint32_t* tmem_base_slot = reinterpret_cast<uint32_t*>(tmem_empty + 2);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_base_slot + 1);
-  volatile int* last_flag = abort_flag + 1;
+struct WsArgs {
+  const uint32_t* q[2];
+  const float* s[2];
+  const uint16_t* h[2];
+  const float* bias[2];
+  const float* aux;
+  float* y;
+  float* partials;
+  int* counters;
+  int M, N;
+  int nkc, nkb, block;
+  int ntiles, mtiles, ksplit, units;
+  int stages, rs;          // operand ring and raw ring depths
+  int exact, pre, act;
+  uint32_t raw_s_bytes;    // folded: scale bytes per weight per raw stage
+  uint32_t raw_w_bytes;    // raw stage bytes per weight
+};
 
-  const int warp = threadIdx.x >> 5;
-  const int lane = threadIdx.x & 31;
-
-  if (threadIdx.x == 0) {
-    for (int i = 0; i < S; ++i) {
-      // TMA expect_tx arrival + 4 dequant warps (pre-expanded tiles: TMA only)
-      ptx::mbar_init(&full[i], a.pre ? 1 : 1 + 4);
-      ptx::mbar_init(&empty[i], 1);  // tcgen05.commit
-    }
-    for (int i = 0; i < RS; ++i) {
-      ptx::mbar_init(&raw_full[i], 1);
-      ptx::mbar_init(&raw_empty[i], 4);
-    }
-    for (int i = 0; i < 2; ++i) {
-      ptx::mbar_init(&tmem_full[i], 1);
-      ptx::mbar_init(&tmem_empty[i], kEpiWarps);
-    }
-    *abort_flag = 0;
-    *last_flag = 0;
-    ptx::fence_mbar_init();
-  }
-  if (warp == kTmaWarp && lane == 0) ptx::prefetch_tmap(&tmap_x);
-  constexpr uint32_t kTmemCols = 2 * NW * BT;  // double-buffered accumulators
-  static_assert(kTmemCols == 128 || kTmemCols == 256 || kTmemCols == 512, "TMEM columns");
-  if (warp == kMmaWarp) {
-    ptx::tmem_alloc(tmem_base_slot, kTmemCols);
-    ptx::tmem_relinquish();
-  }
-  ptx::tc_fence_before();
-  __syncthreads();
-  ptx::tc_fence_after();
-  const uint32_t tmem_base = *tmem_base_slot;
-
-  const int S_split = a.ksplit;
-
-  if (warp == kTmaWarp) {
-    // ------------------------------------------------ token tiles (TMA)
-    if (lane == 0) {
-      int stage = 0;
-      uint32_t phase = 0;
-      for (int u = blockIdx.x; u < a.units && !*abort_flag; u += gridDim.x) {
-        const int tile = u / S_split, split = u - tile * S_split;
-        const int mtile = tile % a.mtiles;
-        const int ntile = tile / a.mtiles;
-        const int kc0 = (int)((int64_t)split * a.nkc / S_split);
-        const int kc1 = (int)((int64_t)(split + 1) * a.nkc / S_split);
-        for (int kc = kc0; kc < kc1; ++kc) {
-          if (!ptx::mbar_wait(&empty[stage], phase ^ 1, abort_flag)) {
-            record_error(a, abort_flag, BQ4_ETIMEOUT);
-            break;
-          }
-          ptx::mbar_arrive_expect_tx(&full[stage], kBTileBytes + (a.pre ? NW * kATileBytes : 0u));
-          ptx::tma_load_2d(b_tiles + (size_t)stage * kBTileBytes, &tmap_x, &full[stage],
-                           kc * kChunkK, mtile * BT);
-          if (a.pre) {
-#pragma unroll
-            for (int w = 0; w < NW; ++w)
-              ptx::bulk_load(a_tiles + ((size_t)stage * NW + w) * kATileBytes,
-                             a.h[w] + ((size_t)ntile * a.nkc + kc) * (kATileBytes / 2), kATileBytes,
-                             &full[stage]);
-          }
-          if (++stage == S) { stage = 0; phase ^= 1; }
-        }
-      }
-    }
-  } else if (warp == kRawWarp) {
-    // ------------------------------------------------ raw weight tiles (bulk)
-    if (lane == 0 && !a.pre) {
-      int rs = 0;
-      uint32_t rphase = 0;
-      for (int u = blockIdx.x; u < a.units && !*abort_flag; u += gridDim.x) {
-        const int tile = u / S_split, split = u - tile * S_split;
-        const int ntile = tile / a.mtiles;
-        const int kc0 = (int)((int64_t)split * a.nkc / S_split);
-        const int kc1 = (int)((int64_t)(split + 1) * a.nkc / S_split);
-        for (int kc = kc0; kc < kc1; ++kc) {
-          if (!ptx::mbar_wait(&raw_empty[rs], rphase ^ 1, abort_flag)) {
-            record_error(a, abort_flag, BQ4_ETIMEOUT);
-            break;
-          }
-          ptx::mbar_arrive_expect_tx(&raw_full[rs], NW * raw_w_bytes);
-          const int kb0 = (kc * kChunkK) / a.block;
-#pragma unroll
-          for (int w = 0; w < NW; ++w) {
-            uint8_t* dst = raw + ((size_t)rs * NW + w) * raw_w_bytes;
-            ptx::bulk_load(dst, a.q[w] + ((size_t)ntile * a.nkc + kc) * 1024, kRawQBytes,
-                           &raw_full[rs]);
-            ptx::bulk_load(dst + kRawQBytes, a.s[w] + ((size_t)ntile * a.nkb + kb0) * 128,
-                           a.raw_s_bytes, &raw_full[rs]);
-          }
-          if (++rs == RS) { rs = 0; rphase ^= 1; }
-        }
-      }
-    }
-  } else if (warp >= kDqWarp0 && warp < kDqWarp0 + 4) {
-    // ------------------------------------------------ dequant producers
-    const int r = threadIdx.x - kDqWarp0 * 32;  // A-tile row = output feature in tile
-    const int sw = r & 7;
-    int stage = 0, rs = 0;
-    uint32_t phase = 0, rphase = 0;
-    const int block = a.block;
-    bool ok = true;
-    if (a.pre) ok = false;  // pre-expanded tiles arrive by bulk copy
-    for (int u = blockIdx.x; ok && u < a.units && !*abort_flag; u += gridDim.x) {
-      const int tile = u / S_split, split = u - tile * S_split;
-      const int kc0 = (int)((int64_t)split * a.nkc / S_split);
-      const int kc1 = (int)((int64_t)(split + 1) * a.nkc / S_split);
-      for (int kc = kc0; kc < kc1; ++kc) {
-        if (!ptx::mbar_wait(&raw_full[rs], rphase, abort_flag)) { ok = false; break; }
-        uint4 words[NW][2];
-        uint32_t sc[NW][8];
-#pragma unroll
-        for (int w = 0; w < NW; ++w) {
-          const uint8_t* src = raw + ((size_t)rs * NW + w) * raw_w_bytes;
-          words[w][0] = *reinterpret_cast<const uint4*>(src + (size_t)r * 16);
-          words[w][1] = *reinterpret_cast<const uint4*>(src + (size_t)(128 + r) * 16);
-          const float* ss = reinterpret_cast<const float*>(src + kRawQBytes);
-          if (block >= 64) {
-            const uint32_t s2 = scale_to_f16x2(ss[r]);
-#pragma unroll
-            for (int j = 0; j < 8; ++j) sc[w][j] = s2;
-          } else {
-#pragma unroll
-            for (int j = 0; j < 8; ++j) sc[w][j] = scale_to_f16x2(ss[((j * 8) / block) * 128 + r]);
-          }
-        }
-        __syncwarp();
-        if (lane == 0) ptx::mbar_arrive(&raw_empty[rs]);
-        if (++rs == RS) { rs = 0; rphase ^= 1; }
-
-        if (!ptx::mbar_wait(&empty[stage], phase ^ 1, abort_flag)) { ok = false; break; }
-#pragma unroll
-        for (int w = 0; w < NW; ++w) {
-          uint8_t* dst = a_tiles + ((size_t)stage * NW + w) * kATileBytes + (size_t)r * 128;
-          const uint32_t wv[8] = {words[w][0].x, words[w][0].y, words[w][0].z, words[w][0].w,
-                                  words[w][1].x, words[w][1].y, words[w][1].z, words[w][1].w};
-#pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            const uint4 v = expand_word(wv[j], sc[w][j]);
-            *reinterpret_cast<uint4*>(dst + ((j ^ sw) << 4)) = v;
-          }
-        }
-        ptx::fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0) ptx::mbar_arrive(&full[stage]);
-        if (++stage == S) { stage = 0; phase ^= 1; }
-      }
-    }
-    if (!ok && !a.pre) record_error(a, abort_flag, BQ4_ETIMEOUT);
-  } else if (warp == kMmaWarp) {
-    // ------------------------------------------------ MMA issuer
-    if (lane == 0) {
-      constexpr uint32_t idesc = ptx::umma_idesc_f16(128, BT);
-      int stage = 0, acc = 0;
-      uint32_t phase = 0, acc_phase = 0;
-      bool ok = true;
-      for (int u = blockIdx.x; ok && u < a.units && !*abort_flag; u += gridDim.x) {
-        const int split = u % S_split;
-        const int kc0 = (int)((int64_t)split * a.nkc / S_split);
-        const int kc1 = (int)((int64_t)(split + 1) * a.nkc / S_split);
-        if (!ptx::mbar_wait(&tmem_empty[acc], acc_phase ^ 1, abort_flag)) { ok = false; break; }
-        ptx::tc_fence_after();
-        const uint32_t d_base = tmem_base + (uint32_t)(acc * NW * BT);
-        for (int kc = kc0; kc < kc1; ++kc) {
-          if (!ptx::mbar_wait(&full[stage], phase, abort_flag)) { ok = false; break; }
-          ptx::tc_fence_after();
-          const uint32_t b_addr = ptx::smem_u32(b_tiles + (size_t)stage * kBTileBytes);
-#pragma unroll
-          for (int kk = 0; kk < kChunkK / 16; ++kk) {
-            const uint64_t b_desc = ptx::umma_desc_sw128(b_addr + kk * 32);
-#pragma unroll
-            for (int w = 0; w < NW; ++w) {
-              const uint32_t a_addr =
-                  ptx::smem_u32(a_tiles + ((size_t)stage * NW + w) * kATileBytes) + kk * 32;
-              ptx::mma_f16_ss(d_base + w * BT, ptx::umma_desc_sw128(a_addr), b_desc, idesc,
-                              (kc > kc0 || kk > 0) ? 1u : 0u);
-            }
-          }
-          ptx::mma_commit(&empty[stage]);
-          if (++stage == S) { stage = 0; phase ^= 1; }
-        }
-        if (!ok) break;
-        ptx::mma_commit(&tmem_full[acc]);
-        if (++acc == 2) { acc = 0; acc_phase ^= 1; }
-      }
-      if (!ok) record_error(a, abort_flag, BQ4_ETIMEOUT);
-    }
-  } else if (warp < kEpiWarps) {
-    // ------------------------------------------------ epilogue
-    const int row = warp * 32 + lane;  // TMEM lane = output feature within tile
-    int acc = 0;
-    uint32_t acc_phase = 0;
-    bool ok = true;
-    for (int u = blockIdx.x; u < a.units && !*abort_flag; u += gridDim.x) {
-      const int tile = u / S_split, split = u - tile * S_split;
-      const int ntile = tile / a.mtiles, mtile = tile - ntile * a.mtiles;
-      const int n = ntile * 128 + row;
-      const int m0 = mtile * BT;
-      if (!ptx::mbar_wait(&tmem_full[acc], acc_phase, abort_flag)) { ok = false; break; }
-      ptx::tc_fence_after();
-      const uint32_t t_row = tmem_base + ((uint32_t)(warp * 32) << 16) + (uint32_t)(acc * NW * BT);
-
-      if (S_split == 1) {
-        float b0 = 0.0f, b1 = 0.0f;
-        if (n < a.N) {
-          if (a.bias[0]) b0 = __ldg(a.bias[0] + n);
-          if (NW == 2 && a.bias[1]) b1 = __ldg(a.bias[1] + n);
-        }
-#pragma unroll 1
-        for (int c = 0; c < BT / 32; ++c) {
-          uint32_t r0[32];
-          uint32_t r1[32];
-          ptx::tmem_ld_32x32b_x32(t_row + c * 32, r0);
-          if (NW == 2) ptx::tmem_ld_32x32b_x32(t_row + BT + c * 32, r1);
-          ptx::tmem_ld_wait();
-          if (n < a.N) {
-#pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              const int m = m0 + c * 32 + j;
-              if (m < a.M) {
-                float v;
-                if (NW == 2) {
-                  v = silu(__uint_as_float(r0[j]) + b0) * (__uint_as_float(r1[j]) + b1);
-                } else {
-                  v = apply_act(__uint_as_float(r0[j]) + b0, a.act);
-                  if (a.aux) v *= __ldg(a.aux + (size_t)m * a.N + n);
-                }
-                a.y[(size_t)m * a.N + n] = v;
-              }
-            }
-          }
-        }
-      } else {
-        // Split-K: write this split's partial tile ([NW][128 rows][BT] f32),
-        // then the last of the S splits to arrive sums all partials in split
-        // order (deterministic) and applies the epilogue.
-        float* part = a.partials + ((size_t)tile * S_split + split) * NW * 128 * BT;
-#pragma unroll 1
-        for (int c = 0; c < BT / 32; ++c) {
-#pragma unroll
-          for (int w = 0; w < NW; ++w) {
-            uint32_t r0[32];
-            ptx::tmem_ld_32x32b_x32(t_row + w * BT + c * 32, r0);
-            ptx::tmem_ld_wait();
-            float4* dst = reinterpret_cast<float4*>(part + ((size_t)w * 128 + row) * BT + c * 32);
-#pragma unroll
-            for (int j = 0; j < 8; ++j)
-              dst[j] = make_float4(__uint_as_float(r0[4 * j]), __uint_as_float(r0[4 * j + 1]),
-                                   __uint_as_float(r0[4 * j + 2]), __uint_as_float(r0[4 * j + 3]));
-          }
-        }
-        __threadfence();
-        asm volatile("bar.sync 1, 128;" ::: "memory");
-        if (threadIdx.x == 0) {
-          const int prev = atomicAdd(a.counters + tile, 1);
-          *last_flag = (prev == S_split - 1) ? 1 : 0;
-          if (prev == S_split - 1) a.counters[tile] = 0;
-        }
-        asm volatile("bar.sync 1, 128;" ::: "memory");
-        if (*last_flag) {
-          __threadfence();
-          float b0 = 0.0f, b1 = 0.0f;
-          if (n < a.N) {
-            if (a.bias[0]) b0 = __ldg(a.bias[0] + n);
-            if (NW == 2 && a.bias[1]) b1 = __ldg(a.bias[1] + n);
-          }
-          const float* base = a.partials + (size_t)tile * S_split * NW * 128 * BT;
-#pragma unroll 1
-          for (int c = 0; c < BT / 32; ++c) {
-            float g[32], up[32];
-#pragma unroll
-            for (int j = 0; j < 32; ++j) g[j] = up[j] = 0.0f;
-            for (int sp = 0; sp < S_split; ++sp) {
-              const float* p = base + (size_t)sp * NW * 128 * BT;
-              const float4* s0 = reinterpret_cast<const float4*>(p + (size_t)row * BT + c * 32);
-#pragma unroll
-              for (int j = 0; j < 8; ++j) {
-                const float4 v = __ldcg(s0 + j);
-                g[4 * j] += v.x; g[4 * j + 1] += v.y; g[4 * j + 2] += v.z; g[4 * j + 3] += v.w;
-              }
-              if (NW == 2) {
-                const float4* s1 =
-                    reinterpret_cast<const float4*>(p + (size_t)(128 + row) * BT + c * 32);
-#pragma unroll
-                for (int j = 0; j < 8; ++j) {
-                  const float4 v = __ldcg(s1 + j);
-                  up[4 * j] += v.x; up[4 * j + 1] += v.y; up[4 * j + 2] += v.z; up[4 * j + 3] += v.w;
-                }
-              }
-            }
-            if (n < a.N) {
-#pragma unroll
-              for (int j = 0; j < 32; ++j) {
-                const int m = m0 + c * 32 + j;
-                if (m < a.M) {
-                  float v;
-                  if (NW == 2) {
-                    v = silu(g[j] + b0) * (up[j] + b1);
-                  } else {
-                    v = apply_act(g[j] + b0, a.act);
-                    if (a.aux) v *= __ldg(a.aux + (size_t)m * a.N + n);
-                  }
-                  a.y[(size_t)m * a.N + n] = v;
-                }
-              }
-            }
-          }
-        }
-        asm volatile("bar.sync 1, 128;" ::: "memory");  // last_flag reuse guard
-      }
-      ptx::tc_fence_before();
-      __syncwarp();
-      if (lane == 0) ptx::mbar_arrive(&tmem_empty[acc]);
-      if (++acc == 2) { acc = 0; acc_phase ^= 1; }
-    }
-    if (!ok) record_error(a, abort_flag, BQ4_ETIMEOUT);
-  }
-
-  ptx::tc_fence_before();
-  __syncthreads();
-  if (warp == kMmaWarp) {
-    ptx::tc_fence_after();
-    ptx::tmem_dealloc(tmem_base, kTmemCols);
-  }
+// Unit u -> (tile, split) and its chunk range [kc0, kc1); splits cut at
+// stage (2-chunk) boundaries.
+__device__ __forceinline__ void ws_unit(const WsArgs& a, int u, int& tile, int& split, int& kc0, int& kc1) {
+  tile = u / a.ksplit;
+  split = u - tile * a.ksplit;
+  const int nks = a.nkc >> 1;
+  kc0 = 2 * (int)((int64_t)split * nks / a.ksplit);
+  kc1 = 2 * (int)((int64_t)(split + 1) * nks / a.ksplit);
 }
 
-// ---------------------------------------------------------------------------
-// Exact-weight kernel (blocks of 64 or 128 K values).
-//
-// The dequant warps stage q itself (exact small integers in f16); the MMA
-// accumulates one K-block segment at a time into one of kNumPart TMEM
-// partial buffers; eight scaler warps drain each partial with
-// acc += scale[n, kb] * partial in f32 registers, so every weight enters the
-// sum as exactly q * scale and only the activations are rounded (to f16).
-// This is the "per-K-block scale on the f32 accumulator" formulation.
-//
-// Warp roles (480 threads): warps 0-7 scaler + epilogue (warp w covers TMEM
-// lanes 32*(w%4).. and token columns [(w/4)*BT/2, (w/4+1)*BT/2)), warps 8-11
-// dequant, warp 12 token TMA, warp 13 raw bulk copies, warp 14 MMA issuer.
-// ---------------------------------------------------------------------------
-constexpr int kExThreads = 480;
-constexpr int kExScalerWarps = 8;
-constexpr int kExDqWarp0 = 8;
-constexpr int kExTmaWarp = 12;
-constexpr int kExRawWarp = 13;
-constexpr int kExMmaWarp = 14;
-constexpr int kNumPart = 4;
-
-// Expand one prepared word into 8 exact f16 values q (no scale).
-__device__ __forceinline__ uint4 expand_word_exact(uint32_t w) {
-  const uint32_t magic = 0x64086408u;
-  uint32_t p[4];
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const uint32_t src = w >> (4 * i);
-    uint32_t t;
-    asm("lop3.b32 %0, %1, %2, %3, 0x6a;" : "=r"(t) : "r"(src), "r"(0x000F000Fu), "r"(magic));
-    asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(p[i]) : "r"(t), "r"(magic));
-  }
-  return make_uint4(p[0], p[1], p[2], p[3]);
+// Segment boundaries inside [kc0, kc1): exact mode cuts at K-block edges
+// (cpb chunks per block); folded mode keeps the unit whole (cpb = 0).
+__device__ __forceinline__ bool ws_seg_first(int kc, int kc0, int cpb) {
+  return kc == kc0 || (cpb > 0 && (kc % cpb) == 0);
+}
+__device__ __forceinline__ bool ws_seg_last(int kc, int kc1, int cpb) {
+  return kc == kc1 - 1 || (cpb > 0 && ((kc + 1) % cpb) == 0);
 }
 
-// Segment bookkeeping: the K chunks [kc0, kc1) of a unit, cut at K-block
-// boundaries (a block spans block/64 chunks).
-__device__ __forceinline__ bool seg_first(int kc, int kc0, int cpb) { return kc == kc0 || (kc % cpb) == 0; }
-__device__ __forceinline__ bool seg_last(int kc, int kc1, int cpb) { return kc == kc1 - 1 || ((kc + 1) % cpb) == 0; }
-
 template <int BT, int NW>
-__global__ void __launch_bounds__(kExThreads, 1)
-    q4_gemm_exact_kernel(const __grid_constant__ CUtensorMap tmap_x, const GemmArgs a) {
+__global__ void __launch_bounds__(kWsThreads, 1)
+    q4_gemm_ws_kernel(const __grid_constant__ CUtensorMap tmap_x, const WsArgs a) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  constexpr uint32_t kBSub = BT * 128;              // one 64-K token sub-tile
+  constexpr uint32_t kAStage = NW * 2 * kATileBytes;
+  constexpr uint32_t kStage = kAStage + 2 * kBSub;
+  constexpr uint32_t kPartCols = NW * BT;
+  constexpr int kNP = 512 / kPartCols;   // partial buffers in TMEM
+  constexpr int kCols = BT / 4;          // token columns per scaler thread
+  static_assert(kNP >= 2, "at least double buffering");
+  static_assert(kCols % 16 == 0, "scaler column split");
 
-  const int S = a.stages, RS = a.raw_stages;
-  constexpr uint32_t kBTileBytes = BT * 128;
-  constexpr int kCols = BT / 2;             // token columns per scaler thread
-  constexpr uint32_t kPartCols = NW * BT;   // TMEM columns per partial buffer
-  constexpr uint32_t kTmemCols = kNumPart * kPartCols;
-  static_assert(kTmemCols == 256 || kTmemCols == 512, "TMEM columns");
-  static_assert(kCols % 32 == 0, "token columns per scaler thread");
-
-  uint8_t* a_tiles = smem;
-  uint8_t* b_tiles = a_tiles + (size_t)S * NW * kATileBytes;
-  uint8_t* raw = b_tiles + (size_t)S * kBTileBytes;
-  const uint32_t raw_w_bytes = a.raw_w_bytes;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(raw + (size_t)RS * NW * raw_w_bytes);
+  const int S = a.stages, RS = a.rs;
+  uint8_t* ring = smem;                                     // [S][A | B]
+  uint8_t* raw_ring = ring + (size_t)S * kStage;            // [RS][NW][raw_w_bytes]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(raw_ring + (size_t)RS * NW * a.raw_w_bytes);
   uint64_t* full = bars;
   uint64_t* empty = full + S;
   uint64_t* raw_full = empty + S;
   uint64_t* raw_empty = raw_full + RS;
   uint64_t* part_full = raw_empty + RS;
-  uint64_t* part_empty = part_full + kNumPart;
-  uint32_t* tmem_base_slot = reinterpret_cast<uint32_t*>(part_empty + kNumPart);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_base_slot + 1);
+  uint64_t* part_empty = part_full + kNP;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(part_empty + kNP);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   volatile int* last_flag = abort_flag + 1;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int cpb = a.block / kChunkK;  // chunks per K block (1 or 2)
+  const int cpb = a.exact ? a.block / kChunkK : 0;
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < S; ++i) {
-      ptx::mbar_init(&full[i], 1 + 4);
-      ptx::mbar_init(&empty[i], 1);
+      ptx::mbar_init(&full[i], a.pre ? 1 : 1 + kWsDqWarps);  // TMA expect_tx (+ dequant warps)
+      ptx::mbar_init(&empty[i], 1);                          // tcgen05.commit
     }
-    for (int i = 0; i < RS; ++i) {
-      ptx::mbar_init(&raw_full[i], 1);
-      ptx::mbar_init(&raw_empty[i], 4);
-    }
-    for (int i = 0; i < kNumPart; ++i) {
-      ptx::mbar_init(&part_full[i], 1);
-      ptx::mbar_init(&part_empty[i], kExScalerWarps);
-    }
+    for (int i = 0; i < RS; ++i) { ptx::mbar_init(&raw_full[i], 1); ptx::mbar_init(&raw_empty[i], kWsDqWarps); }
+    for (int i = 0; i < kNP; ++i) { ptx::mbar_init(&part_full[i], 1); ptx::mbar_init(&part_empty[i], kWsScalerWarps); }
     *abort_flag = 0;
     *last_flag = 0;
     ptx::fence_mbar_init();
   }
-  if (warp == kExTmaWarp && lane == 0) ptx::prefetch_tmap(&tmap_x);
-  if (warp == kExMmaWarp) {
-    ptx::tmem_alloc(tmem_base_slot, kTmemCols);
+  if (warp == kWsTmaWarp && lane == 0) ptx::prefetch_tmap(&tmap_x);
+  if (warp == kWsMmaWarp) {
+    ptx::tmem_alloc(tmem_slot, 512);
     ptx::tmem_relinquish();
   }
   ptx::tc_fence_before();
   __syncthreads();
   ptx::tc_fence_after();
-  const uint32_t tmem_base = *tmem_base_slot;
-  const int S_split = a.ksplit;
+  const uint32_t tmem_base = *tmem_slot;
 
-  if (warp == kExTmaWarp) {
-    if (lane == 0) {
-      int stage = 0;
-      uint32_t phase = 0;
+  if (warp >= kWsTmaWarp) {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kWsRegsProducer));
+    if (warp == kWsTmaWarp && lane == 0) {
+      // ------------------------------------------------ token tiles (+ pre-expanded A)
+      int s = 0;
+      uint32_t ph = 0;
       for (int u = blockIdx.x; u < a.units && !*abort_flag; u += gridDim.x) {
-        const int tile = u / S_split, split = u - tile * S_split;
-        const int mtile = tile % a.mtiles;
-        const int kc0 = (int)((int64_t)split * a.nkc / S_split);
-        const int kc1 = (int)((int64_t)(split + 1) * a.nkc / S_split);
-        for (int kc = kc0; kc < kc1; ++kc) {
-          if (!ptx::mbar_wait(&empty[stage], phase ^ 1, abort_flag)) {
-            record_error(a, abort_flag, BQ4_ETIMEOUT);
+        int tile, split, kc0, kc1;
+        ws_unit(a, u, tile, split, kc0, kc1);
+        const int mtile = tile % a.mtiles, ntile = tile / a.mtiles;
+        for (int kc = kc0; kc < kc1; kc += 2) {
+          if (!ptx::mbar_wait(&empty[s], ph ^ 1, abort_flag)) {
+            record_error_flag(abort_flag, BQ4_ETIMEOUT);
             break;
           }
-          ptx::mbar_arrive_expect_tx(&full[stage], kBTileBytes);
-          ptx::tma_load_2d(b_tiles + (size_t)stage * kBTileBytes, &tmap_x, &full[stage], kc * kChunkK, mtile * BT);
-          if (++stage == S) { stage = 0; phase ^= 1; }
+          uint8_t* st = ring + (size_t)s * kStage;
+          ptx::mbar_arrive_expect_tx(&full[s], 2 * kBSub + (a.pre ? kAStage : 0u));
+          ptx::tma_load_2d(st + kAStage, &tmap_x, &full[s], kc * kChunkK, mtile * BT);
+          ptx::tma_load_2d(st + kAStage + kBSub, &tmap_x, &full[s], (kc + 1) * kChunkK, mtile * BT);
+          if (a.pre) {
+#pragma unroll
+            for (int w = 0; w < NW; ++w)
+              ptx::bulk_load(st + (size_t)w * 2 * kATileBytes,
+                             a.h[w] + ((size_t)ntile * a.nkc + kc) * (kATileBytes / 2), 2 * kATileBytes, &full[s]);
+          }
+          if (++s == S) { s = 0; ph ^= 1; }
         }
       }
-    }
-  } else if (warp == kExRawWarp) {
-    if (lane == 0) {
+    } else if (warp == kWsWeightWarp && lane == 0 && !a.pre) {
+      // ------------------------------------------------ raw weight tiles (bulk copies)
       int rs = 0;
-      uint32_t rphase = 0;
+      uint32_t rph = 0;
       for (int u = blockIdx.x; u < a.units && !*abort_flag; u += gridDim.x) {
-        const int tile = u / S_split, split = u - tile * S_split;
+        int tile, split, kc0, kc1;
+        ws_unit(a, u, tile, split, kc0, kc1);
         const int ntile = tile / a.mtiles;
-        const int kc0 = (int)((int64_t)split * a.nkc / S_split);
-        const int kc1 = (int)((int64_t)(split + 1) * a.nkc / S_split);
-        for (int kc = kc0; kc < kc1; ++kc) {
-          if (!ptx::mbar_wait(&raw_empty[rs], rphase ^ 1, abort_flag)) {
-            record_error(a, abort_flag, BQ4_ETIMEOUT);
+        for (int kc = kc0; kc < kc1; kc += 2) {
+          if (!ptx::mbar_wait(&raw_empty[rs], rph ^ 1, abort_flag)) {
+            record_error_flag(abort_flag, BQ4_ETIMEOUT);
             break;
           }
-          ptx::mbar_arrive_expect_tx(&raw_full[rs], NW * kRawQBytes);
+          ptx::mbar_arrive_expect_tx(&raw_full[rs], NW * (kRawStageQBytes + a.raw_s_bytes));
+          const int kb0 = (kc * kChunkK) / a.block;
 #pragma unroll
           for (int w = 0; w < NW; ++w) {
-            uint8_t* dst = raw + ((size_t)rs * NW + w) * raw_w_bytes;
-            ptx::bulk_load(dst, a.q[w] + ((size_t)ntile * a.nkc + kc) * 1024, kRawQBytes, &raw_full[rs]);
+            uint8_t* dst = raw_ring + ((size_t)rs * NW + w) * a.raw_w_bytes;
+            ptx::bulk_load(dst, a.q[w] + ((size_t)ntile * a.nkc + kc) * 1024, kRawStageQBytes, &raw_full[rs]);
+            if (a.raw_s_bytes)
+              ptx::bulk_load(dst + kRawStageQBytes, a.s[w] + ((size_t)ntile * a.nkb + kb0) * 128, a.raw_s_bytes,
+                             &raw_full[rs]);
           }
-          if (++rs == RS) { rs = 0; rphase ^= 1; }
+          if (++rs == RS) { rs = 0; rph ^= 1; }
         }
       }
-    }
-  } else if (warp >= kExDqWarp0 && warp < kExDqWarp0 + 4) {
-    const int r = threadIdx.x - kExDqWarp0 * 32;
-    const int sw = r & 7;
-    int stage = 0, rs = 0;
-    uint32_t phase = 0, rphase = 0;
-    bool ok = true;
-    for (int u = blockIdx.x; ok && u < a.units && !*abort_flag; u += gridDim.x) {
-      const int tile = u / S_split, split = u - tile * S_split;
-      const int kc0 = (int)((int64_t)split * a.nkc / S_split);
-      const int kc1 = (int)((int64_t)(split + 1) * a.nkc / S_split);
-      for (int kc = kc0; kc < kc1; ++kc) {
-        if (!ptx::mbar_wait(&raw_full[rs], rphase, abort_flag)) { ok = false; break; }
-        uint4 words[NW][2];
-#pragma unroll
-        for (int w = 0; w < NW; ++w) {
-          const uint8_t* src = raw + ((size_t)rs * NW + w) * raw_w_bytes;
-          words[w][0] = *reinterpret_cast<const uint4*>(src + (size_t)r * 16);
-          words[w][1] = *reinterpret_cast<const uint4*>(src + (size_t)(128 + r) * 16);
-        }
-        __syncwarp();
-        if (lane == 0) ptx::mbar_arrive(&raw_empty[rs]);
-        if (++rs == RS) { rs = 0; rphase ^= 1; }
-        if (!ptx::mbar_wait(&empty[stage], phase ^ 1, abort_flag)) { ok = false; break; }
-#pragma unroll
-        for (int w = 0; w < NW; ++w) {
-          uint8_t* dst = a_tiles + ((size_t)stage * NW + w) * kATileBytes + (size_t)r * 128;
-          const uint32_t wv[8] = {words[w][0].x, words[w][0].y, words[w][0].z, words[w][0].w,
-                                  words[w][1].x, words[w][1].y, words[w][1].z, words[w][1].w};
-#pragma unroll
-          for (int j = 0; j < 8; ++j)
-            *reinterpret_cast<uint4*>(dst + ((j ^ sw) << 4)) = expand_word_exact(wv[j]);
-        }
-        ptx::fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0) ptx::mbar_arrive(&full[stage]);
-        if (++stage == S) { stage = 0; phase ^= 1; }
-      }
-    }
-    if (!ok) record_error(a, abort_flag, BQ4_ETIMEOUT);
-  } else if (warp == kExMmaWarp) {
-    if (lane == 0) {
+    } else if (warp == kWsMmaWarp && lane == 0) {
+      // ------------------------------------------------ MMA issuer
       constexpr uint32_t idesc = ptx::umma_idesc_f16(128, BT);
-      int stage = 0, pb = 0;
-      uint32_t phase = 0, pphase = 0;
+      int s = 0, pb = 0;
+      uint32_t ph = 0, pph = 0;
       bool ok = true;
       for (int u = blockIdx.x; ok && u < a.units && !*abort_flag; u += gridDim.x) {
-        const int split = u % S_split;
-        const int kc0 = (int)((int64_t)split * a.nkc / S_split);
-        const int kc1 = (int)((int64_t)(split + 1) * a.nkc / S_split);
+        int tile, split, kc0, kc1;
+        ws_unit(a, u, tile, split, kc0, kc1);
         uint32_t d_base = 0;
-        for (int kc = kc0; kc < kc1; ++kc) {
-          const bool first = seg_first(kc, kc0, cpb);
-          if (first) {
-            if (!ptx::mbar_wait(&part_empty[pb], pphase ^ 1, abort_flag)) { ok = false; break; }
-            ptx::tc_fence_after();
-            d_base = tmem_base + (uint32_t)pb * kPartCols;
-          }
-          if (!ptx::mbar_wait(&full[stage], phase, abort_flag)) { ok = false; break; }
+        for (int kc = kc0; ok && kc < kc1; kc += 2) {
+          if (!ptx::mbar_wait(&full[s], ph, abort_flag)) { ok = false; break; }
           ptx::tc_fence_after();
-          const uint32_t b_addr = ptx::smem_u32(b_tiles + (size_t)stage * kBTileBytes);
+          const uint32_t st = ptx::smem_u32(ring + (size_t)s * kStage);
 #pragma unroll
-          for (int kk = 0; kk < kChunkK / 16; ++kk) {
-            const uint64_t b_desc = ptx::umma_desc_sw128(b_addr + kk * 32);
+          for (int sub = 0; sub < 2; ++sub) {
+            const int c = kc + sub;
+            const bool first = ws_seg_first(c, kc0, cpb);
+            if (first) {
+              if (!ptx::mbar_wait(&part_empty[pb], pph ^ 1, abort_flag)) { ok = false; break; }
+              ptx::tc_fence_after();
+              d_base = tmem_base + (uint32_t)pb * kPartCols;
+            }
+            const uint32_t b_addr = st + kAStage + sub * kBSub;
 #pragma unroll
-            for (int w = 0; w < NW; ++w) {
-              const uint32_t a_addr = ptx::smem_u32(a_tiles + ((size_t)stage * NW + w) * kATileBytes) + kk * 32;
-              ptx::mma_f16_ss(d_base + w * BT, ptx::umma_desc_sw128(a_addr), b_desc, idesc,
-                              (first && kk == 0) ? 0u : 1u);
+            for (int kk = 0; kk < kChunkK / 16; ++kk) {
+              const uint64_t b_desc = ptx::umma_desc_sw128(b_addr + kk * 32);
+#pragma unroll
+              for (int w = 0; w < NW; ++w)
+                ptx::mma_f16_ss(d_base + w * BT,
+                                ptx::umma_desc_sw128(st + (uint32_t)((w * 2 + sub) * kATileBytes) + kk * 32), b_desc,
+                                idesc, (first && kk == 0) ? 0u : 1u);
+            }
+            if (sub == 1) ptx::mma_commit(&empty[s]);  // stage free once its MMAs retire
+            if (ws_seg_last(c, kc1, cpb)) {
+              ptx::mma_commit(&part_full[pb]);
+              if (++pb == kNP) { pb = 0; pph ^= 1; }
             }
           }
-          ptx::mma_commit(&empty[stage]);
-          if (++stage == S) { stage = 0; phase ^= 1; }
-          if (seg_last(kc, kc1, cpb)) {
-            ptx::mma_commit(&part_full[pb]);
-            if (++pb == kNumPart) { pb = 0; pphase ^= 1; }
-          }
+          if (++s == S) { s = 0; ph ^= 1; }
         }
       }
-      if (!ok) record_error(a, abort_flag, BQ4_ETIMEOUT);
+      if (!ok) record_error_flag(abort_flag, BQ4_ETIMEOUT);
     }
-  } else if (warp < kExScalerWarps) {
+  } else if (warp >= kWsDqWarp0) {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kWsRegsDequant));
+    if (!a.pre) {
+      // ------------------------------------------------ dequant
+      const int t = threadIdx.x - kWsDqWarp0 * 32;
+      const int r = t & 127;
+      const int sub = t >> 7;  // which 64-K sub-tile of the stage
+      const int sw = r & 7;
+      const int block = a.block;
+      int rs = 0, s = 0;
+      uint32_t rph = 0, ph = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; ok && u < a.units && !*abort_flag; u += gridDim.x) {
+        int tile, split, kc0, kc1;
+        ws_unit(a, u, tile, split, kc0, kc1);
+        for (int kc = kc0; kc < kc1; kc += 2) {
+          if (!ptx::mbar_wait(&raw_full[rs], rph, abort_flag)) { ok = false; break; }
+          uint4 wlo[NW], whi[NW];
+          uint32_t sc[NW][8];
+#pragma unroll
+          for (int w = 0; w < NW; ++w) {
+            const uint8_t* src = raw_ring + ((size_t)rs * NW + w) * a.raw_w_bytes + (size_t)sub * kRawQBytes;
+            wlo[w] = *reinterpret_cast<const uint4*>(src + (size_t)r * 16);
+            whi[w] = *reinterpret_cast<const uint4*>(src + (size_t)(128 + r) * 16);
+            if (!a.exact) {
+              const float* ss = reinterpret_cast<const float*>(raw_ring + ((size_t)rs * NW + w) * a.raw_w_bytes +
+                                                               kRawStageQBytes);
+              if (block >= 128) {
+                const uint32_t s2 = scale_to_f16x2(ss[r]);
+#pragma unroll
+                for (int j = 0; j < 8; ++j) sc[w][j] = s2;
+              } else {
+#pragma unroll
+                for (int j = 0; j < 8; ++j) sc[w][j] = scale_to_f16x2(ss[((sub * 64 + j * 8) / block) * 128 + r]);
+              }
+            }
+          }
+          __syncwarp();
+          if (lane == 0) ptx::mbar_arrive(&raw_empty[rs]);
+          if (++rs == RS) { rs = 0; rph ^= 1; }
+          if (!ptx::mbar_wait(&empty[s], ph ^ 1, abort_flag)) { ok = false; break; }
+#pragma unroll
+          for (int w = 0; w < NW; ++w) {
+            uint8_t* dst = ring + (size_t)s * kStage + (size_t)(w * 2 + sub) * kATileBytes + (size_t)r * 128;
+            const uint32_t wv[8] = {wlo[w].x, wlo[w].y, wlo[w].z, wlo[w].w, whi[w].x, whi[w].y, whi[w].z, whi[w].w};
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              const uint4 v = a.exact ? expand_word_exact(wv[j]) : expand_word(wv[j], sc[w][j]);
+              *reinterpret_cast<uint4*>(dst + ((j ^ sw) << 4)) = v;
+            }
+          }
+          ptx::fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) ptx::mbar_arrive(&full[s]);
+          if (++s == S) { s = 0; ph ^= 1; }
+        }
+      }
+      if (!ok) record_error_flag(abort_flag, BQ4_ETIMEOUT);
+    }
+  } else {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kWsRegsScaler));
     // ------------------------------------------------ scaler + epilogue
     const int quad = warp & 3;
-    const int row = quad * 32 + lane;          // output feature within the tile
-    const int col0 = (warp >> 2) * kCols;      // first token column of this thread
+    const int row = quad * 32 + lane;
+    const int col0 = (warp >> 2) * kCols;
     int pb = 0;
-    uint32_t pphase = 0;
+    uint32_t pph = 0;
     bool ok = true;
     for (int u = blockIdx.x; ok && u < a.units && !*abort_flag; u += gridDim.x) {
-      const int tile = u / S_split, split = u - tile * S_split;
+      int tile, split, kc0, kc1;
+      ws_unit(a, u, tile, split, kc0, kc1);
       const int ntile = tile / a.mtiles, mtile = tile - ntile * a.mtiles;
       const int n = ntile * 128 + row;
       const int m0 = mtile * BT + col0;
-      const int kc0 = (int)((int64_t)split * a.nkc / S_split);
-      const int kc1 = (int)((int64_t)(split + 1) * a.nkc / S_split);
       float acc[NW][kCols];
 #pragma unroll
       for (int w = 0; w < NW; ++w)
 #pragma unroll
         for (int j = 0; j < kCols; ++j) acc[w][j] = 0.0f;
-      const float* srow[NW];
-#pragma unroll
-      for (int w = 0; w < NW; ++w) srow[w] = a.s[w] + (size_t)ntile * a.nkb * 128 + row;
       for (int kc = kc0; kc < kc1; ++kc) {
-        if (!seg_last(kc, kc1, cpb)) continue;
-        const int kb = (kc * kChunkK) / a.block;
+        if (!ws_seg_last(kc, kc1, cpb)) continue;
         float sc[NW];
 #pragma unroll
-        for (int w = 0; w < NW; ++w) sc[w] = __ldg(srow[w] + (size_t)kb * 128);
-        if (!ptx::mbar_wait(&part_full[pb], pphase, abort_flag)) { ok = false; break; }
+        for (int w = 0; w < NW; ++w)
+          sc[w] = a.exact ? __ldg(a.s[w] + ((size_t)ntile * a.nkb + (kc * kChunkK) / a.block) * 128 + row) : 1.0f;
+        if (!ptx::mbar_wait(&part_full[pb], pph, abort_flag)) { ok = false; break; }
         ptx::tc_fence_after();
         const uint32_t t_row = tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)pb * kPartCols + col0;
 #pragma unroll
@@ -748,98 +442,80 @@ __global__ void __launch_bounds__(kExThreads, 1)
         ptx::tc_fence_before();
         __syncwarp();
         if (lane == 0) ptx::mbar_arrive(&part_empty[pb]);
-        if (++pb == kNumPart) { pb = 0; pphase ^= 1; }
+        if (++pb == kNP) { pb = 0; pph ^= 1; }
       }
       if (!ok) break;
 
-      if (S_split == 1) {
-        float b0 = 0.0f, b1 = 0.0f;
-        if (n < a.N) {
-          if (a.bias[0]) b0 = __ldg(a.bias[0] + n);
-          if (NW == 2 && a.bias[1]) b1 = __ldg(a.bias[1] + n);
-          const int act = a.act;
-#pragma unroll
-          for (int j = 0; j < kCols; ++j) {
-            const int m = m0 + j;
-            if (m < a.M) {
-              float v;
-              if (NW == 2) {
-                v = silu(acc[0][j] + b0) * (acc[NW - 1][j] + b1);
-              } else {
-                v = apply_act(acc[0][j] + b0, act);
-                if (a.aux) v *= __ldg(a.aux + (size_t)m * a.N + n);
-              }
-              a.y[(size_t)m * a.N + n] = v;
-            }
-          }
-        }
-      } else {
-        float* part = a.partials + ((size_t)tile * S_split + split) * NW * 128 * BT;
+      const int SPL = a.ksplit;
+      if (SPL > 1) {
+        // Split-K: publish this split's partial, the last split sums all of
+        // them in split order (deterministic) and runs the epilogue.
+        float* part = a.partials + ((size_t)tile * SPL + split) * NW * 128 * BT;
 #pragma unroll
         for (int w = 0; w < NW; ++w) {
           float4* dst = reinterpret_cast<float4*>(part + ((size_t)w * 128 + row) * BT + col0);
 #pragma unroll
           for (int j = 0; j < kCols / 4; ++j)
-            dst[j] = make_float4(acc[w][4 * j], acc[w][4 * j + 1], acc[w][4 * j + 2], acc[w][4 * j + 3]);
+            __stcg(dst + j, make_float4(acc[w][4 * j], acc[w][4 * j + 1], acc[w][4 * j + 2], acc[w][4 * j + 3]));
         }
         __threadfence();
-        asm volatile("bar.sync 1, 256;" ::: "memory");
+        asm volatile("bar.sync 1, 512;" ::: "memory");
         if (threadIdx.x == 0) {
-          const int prev = atomicAdd(a.counters + tile, 1);
-          *last_flag = (prev == S_split - 1) ? 1 : 0;
-          if (prev == S_split - 1) a.counters[tile] = 0;
-        }
-        asm volatile("bar.sync 1, 256;" ::: "memory");
-        if (*last_flag) {
           __threadfence();
-          const float* base = a.partials + (size_t)tile * S_split * NW * 128 * BT;
+          const int prev = atomicAdd(a.counters + tile, 1);
+          *last_flag = (prev == SPL - 1) ? 1 : 0;
+          if (prev == SPL - 1) a.counters[tile] = 0;
+        }
+        asm volatile("bar.sync 1, 512;" ::: "memory");
+        const bool last = *last_flag != 0;
+        asm volatile("bar.sync 1, 512;" ::: "memory");
+        if (!last) continue;
+        __threadfence();
+        const float* base = a.partials + (size_t)tile * SPL * NW * 128 * BT;
 #pragma unroll
-          for (int w = 0; w < NW; ++w)
+        for (int w = 0; w < NW; ++w)
 #pragma unroll
-            for (int j = 0; j < kCols; ++j) acc[w][j] = 0.0f;
-          for (int sp = 0; sp < S_split; ++sp) {
+          for (int j = 0; j < kCols; ++j) acc[w][j] = 0.0f;
+        for (int sp = 0; sp < SPL; ++sp) {
 #pragma unroll
-            for (int w = 0; w < NW; ++w) {
-              const float4* src =
-                  reinterpret_cast<const float4*>(base + ((size_t)sp * NW * 128 + w * 128 + row) * BT + col0);
+          for (int w = 0; w < NW; ++w) {
+            const float4* src = reinterpret_cast<const float4*>(base + ((size_t)(sp * NW + w) * 128 + row) * BT + col0);
 #pragma unroll
-              for (int j = 0; j < kCols / 4; ++j) {
-                const float4 v = __ldcg(src + j);
-                acc[w][4 * j] += v.x; acc[w][4 * j + 1] += v.y; acc[w][4 * j + 2] += v.z; acc[w][4 * j + 3] += v.w;
-              }
-            }
-          }
-          if (n < a.N) {
-            float b0 = 0.0f, b1 = 0.0f;
-            if (a.bias[0]) b0 = __ldg(a.bias[0] + n);
-            if (NW == 2 && a.bias[1]) b1 = __ldg(a.bias[1] + n);
-#pragma unroll
-            for (int j = 0; j < kCols; ++j) {
-              const int m = m0 + j;
-              if (m < a.M) {
-                float v;
-                if (NW == 2) {
-                  v = silu(acc[0][j] + b0) * (acc[NW - 1][j] + b1);
-                } else {
-                  v = apply_act(acc[0][j] + b0, a.act);
-                  if (a.aux) v *= __ldg(a.aux + (size_t)m * a.N + n);
-                }
-                a.y[(size_t)m * a.N + n] = v;
-              }
+            for (int j = 0; j < kCols / 4; ++j) {
+              const float4 v = __ldcg(src + j);
+              acc[w][4 * j] += v.x; acc[w][4 * j + 1] += v.y; acc[w][4 * j + 2] += v.z; acc[w][4 * j + 3] += v.w;
             }
           }
         }
-        asm volatile("bar.sync 1, 256;" ::: "memory");
+      }
+      if (n < a.N) {
+        const float b0 = a.bias[0] ? __ldg(a.bias[0] + n) : 0.0f;
+        const float b1 = (NW == 2 && a.bias[1]) ? __ldg(a.bias[1] + n) : 0.0f;
+        const int act = a.act;
+#pragma unroll
+        for (int j = 0; j < kCols; ++j) {
+          const int m = m0 + j;
+          if (m < a.M) {
+            float v;
+            if (NW == 2) {
+              v = silu(acc[0][j] + b0) * (acc[NW - 1][j] + b1);
+            } else {
+              v = apply_act(acc[0][j] + b0, act);
+              if (a.aux) v *= __ldg(a.aux + (size_t)m * a.N + n);
+            }
+            a.y[(size_t)m * a.N + n] = v;
+          }
+        }
       }
     }
-    if (!ok) record_error(a, abort_flag, BQ4_ETIMEOUT);
+    if (!ok) record_error_flag(abort_flag, BQ4_ETIMEOUT);
   }
 
   ptx::tc_fence_before();
   __syncthreads();
-  if (warp == kExMmaWarp) {
+  if (warp == kWsMmaWarp) {
     ptx::tc_fence_after();
-    ptx::tmem_dealloc(tmem_base, kTmemCols);
+    ptx::tmem_dealloc(tmem_base, 512);
   }
 }
 
@@ -866,21 +542,36 @@ EncodeTiledFn encode_fn() {
 
 size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
-template <int BT, int NW, bool EXACT>
-cudaError_t launch_kernel(const GemmPlan& plan, const CUtensorMap& tmap, const GemmArgs& args,
-                          cudaStream_t stream) {
-  cudaError_t e;
-  if constexpr (EXACT) {
-    auto kern = q4_gemm_exact_kernel<BT, NW>;
-    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)plan.smem_bytes);
+// The kernel rebalances registers with setmaxnreg; the split only fits the
+// pool the block was launched with when ptxas gave every thread exactly
+// kWsRegsLaunch registers.  Checked once per instantiation before any launch
+// (a mismatch would make setmaxnreg.inc wait forever).
+template <int BT, int NW>
+cudaError_t prepare_ws_kernel(size_t smem_bytes, bool* ok_regs) {
+  auto kern = q4_gemm_ws_kernel<BT, NW>;
+  static int checked = 0;  // 0 unknown, 1 ok, -1 bad
+  if (checked == 0) {
+    cudaFuncAttributes attr;
+    cudaError_t e = cudaFuncGetAttributes(&attr, kern);
     if (e != cudaSuccess) return e;
-    kern<<<plan.grid, kExThreads, plan.smem_bytes, stream>>>(tmap, args);
-  } else {
-    auto kern = q4_gemm_kernel<BT, NW>;
-    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)plan.smem_bytes);
-    if (e != cudaSuccess) return e;
-    kern<<<plan.grid, kThreads, plan.smem_bytes, stream>>>(tmap, args);
+    checked = (attr.numRegs == kWsRegsLaunch) ? 1 : -1;
   }
+  *ok_regs = checked == 1;
+  static size_t smem_set = 0;
+  if (smem_set < smem_bytes) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_bytes);
+    if (e != cudaSuccess) return e;
+    smem_set = smem_bytes;
+  }
+  return cudaSuccess;
+}
+
+template <int BT, int NW>
+cudaError_t launch_ws(const GemmPlan& plan, const CUtensorMap& tmap, const WsArgs& args, cudaStream_t stream,
+                      bool* ok_regs) {
+  cudaError_t e = prepare_ws_kernel<BT, NW>(plan.smem_bytes, ok_regs);
+  if (e != cudaSuccess || !*ok_regs) return e;
+  q4_gemm_ws_kernel<BT, NW><<<plan.grid, kWsThreads, plan.smem_bytes, stream>>>(tmap, args);
   note_launch();
   return cudaGetLastError();
 }
@@ -912,40 +603,44 @@ bq4_status plan_gemm(const bq4_weight* w, int nw, int64_t M, int device, GemmPla
   if (M > (int64_t)1 << 30) return set_error(BQ4_EINVAL_SHAPE, "M too large");
   memset(p, 0, sizeof(*p));
   p->nw = nw;
-  // Blocks of 64/128 K values keep q exact and scale the f32 accumulator
-  // (exact-weight kernel, token tile <= 128); smaller blocks fold the scale
-  // into the f16 weight (folded kernel, token tile <= 256).
+  // Numerics: blocks of 64/128 keep q exact in f16 and multiply the f32
+  // partial of each K block by its scale (exact weights); smaller blocks
+  // stage f16(q * f16(scale)) (folded); N-packed sources are pre-expanded.
   p->pre = w->h != nullptr ? 1 : 0;
   p->exact = (!p->pre && w->block >= 64) ? 1 : 0;
-  // BQ4_FORCE_FOLDED=1 selects the folded kernel for any block (tests and
-  // tuning compare both formulations on the same shapes).
+  // BQ4_FORCE_FOLDED=1 selects folded staging for any block (tests compare
+  // both formulations on the same shapes).
   if (const char* f = getenv("BQ4_FORCE_FOLDED"))
     if (f[0] == '1') p->exact = 0;
-  if (p->exact)
-    p->bt = (nw == 1 && M > 64) ? 128 : 64;
-  else if (nw == 1)
+  if (nw == 1)
     p->bt = M > 128 ? 256 : (M > 64 ? 128 : 64);
   else
     p->bt = M > 64 ? 128 : 64;
+  // BQ4_FORCE_BT=64|128|256 pins the token tile (tuning).
+  if (const char* f = getenv("BQ4_FORCE_BT")) {
+    const int v = atoi(f);
+    if (v == 64 || v == 128 || (v == 256 && nw == 1)) p->bt = v;
+  }
   p->mtiles = (int)((M + p->bt - 1) / p->bt);
   p->ntiles = (int)w->ntiles;
   const int sms = device_sm_count(device);
   const int tiles = p->mtiles * p->ntiles;
   const int nkc = (int)w->nkc;
+  const int nks = nkc / 2;  // 128-K stages
 
-  // Split-K factor: minimise an estimated makespan.  One unit of work costs
-  // (chunks per split + fixed pipeline fill of ~3 chunks).  Split-K is only
-  // used when every unit fits in a single wave (units <= SMs): a CTA that
-  // runs a second split unit was measured to produce wrong partial tiles,
-  // so multi-wave work uses whole-K units (S = 1).
+  // Split-K factor: minimise an estimated makespan (chunks per split plus a
+  // pipeline fill of ~3 chunks per unit, plus the partial-tile fix-up).
+  // Split-K is only used when all units fit in one wave (units <= SMs);
+  // multi-wave work uses whole-K units (S = 1).
   int best_s = 1;
   double best_t = 1e30;
-  const int max_s = nkc < 16 ? nkc : 16;
+  const int max_s = nks < 16 ? nks : 16;
+  const bool multiwave_split = getenv("BQ4_ALLOW_MULTIWAVE_SPLIT") != nullptr;
   for (int s = 1; s <= max_s; ++s) {
     const int units = tiles * s;
-    if (s > 1 && units > sms) break;
+    if (s > 1 && units > sms && !multiwave_split) break;
     const int waves = (units + sms - 1) / sms;
-    const double per_unit = (double)nkc / s + 3.0;
+    const double per_unit = (double)nkc / s + 3.0;  // chunks
     const double fixup = s > 1 ? 1.0 + 0.25 * s : 0.0;
     const double t = waves * (per_unit + fixup);
     if (t < best_t - 1e-9) {
@@ -957,41 +652,47 @@ bq4_status plan_gemm(const bq4_weight* w, int nw, int64_t M, int device, GemmPla
   // to a single wave of units).
   if (const char* f = getenv("BQ4_FORCE_KSPLIT")) {
     int v = atoi(f);
-    if (v >= 1) best_s = v < nkc ? v : nkc;
-    while (best_s > 1 && tiles * best_s > sms) --best_s;
+    if (v >= 1) best_s = v < nks ? v : nks;
+    while (best_s > 1 && tiles * best_s > sms && !multiwave_split) --best_s;
   }
   p->ksplit = best_s;
   p->units = tiles * best_s;
   p->grid = p->units < sms ? p->units : sms;
 
-  // Shared memory: operand ring (S stages) + raw ring (RS stages).
-  // The exact kernel's scaler warps read scales straight from global memory,
-  // so its raw stages carry nibbles only.
-  const uint32_t raw_s_bytes = 512u * (uint32_t)(w->block >= 64 ? 1 : 64 / w->block);
-  const size_t stage_bytes = (size_t)nw * kATileBytes + (size_t)p->bt * 128;
-  // Per-weight raw stage: nibbles (+ scales for the folded kernel); the
-  // pre-expanded path leaves the ring unused.  The kernels carve shared
-  // memory with this same value (GemmArgs::raw_w_bytes).
-  p->raw_w_bytes = p->pre ? 16u : kRawQBytes + (p->exact ? 0u : raw_s_bytes);
-  const size_t raw_stage_bytes = (size_t)nw * p->raw_w_bytes;
+  // Shared memory: operand ring of 128-K stages (A + B) as deep as fits
+  // (2..4 stages) next to a raw ring of 2..4 stages.
+  const uint32_t raw_s_bytes = 512u * (uint32_t)(w->block >= 128 ? 1 : 128 / w->block);
+  p->raw_s_bytes = p->exact || p->pre ? 0u : raw_s_bytes;
+  p->raw_w_bytes = p->pre ? 16u : 2 * kRawQBytes + p->raw_s_bytes;
+  const size_t stage_bytes = (size_t)nw * 2 * kATileBytes + 2 * (size_t)p->bt * 128;
+  const size_t raw_stage = (size_t)nw * p->raw_w_bytes;
   const size_t budget = 227 * 1024 - 1024 /*align*/ - 512 /*barriers*/;
   int S = 0, RS = 0;
-  for (int s = 4; s >= 2; --s) {
-    if ((size_t)s * stage_bytes >= budget) continue;
-    int rs = (int)((budget - (size_t)s * stage_bytes) / raw_stage_bytes);
-    if (rs > 8) rs = 8;
-    if (p->pre) rs = 4;  // unused ring
-    if (rs >= 4 || s == 2) {
-      S = s;
-      RS = rs;
-      break;
+  for (int s = 4; s >= 2 && !S; --s) {
+    if ((size_t)s * stage_bytes + raw_stage > budget) continue;
+    int rs = (int)((budget - (size_t)s * stage_bytes) / raw_stage);
+    if (rs > 4) rs = 4;
+    if (p->pre) rs = 1;
+    S = s;
+    RS = rs;
+  }
+  // BQ4_FORCE_RINGS=S,RS pins the ring depths (tuning); ignored when it
+  // does not fit the shared-memory budget.
+  if (const char* f = getenv("BQ4_FORCE_RINGS")) {
+    int fs = 0, fr = 0;
+    if (sscanf(f, "%d,%d", &fs, &fr) == 2 && fs >= 2 && fr >= 1 &&
+        (size_t)fs * stage_bytes + (size_t)fr * raw_stage <= budget) {
+      S = fs;
+      RS = p->pre ? 1 : fr;
     }
   }
-  if (S < 2 || RS < 2) return set_error(BQ4_EUNSUPPORTED, "no shared-memory plan for this shape");
+  if (S < 2 || RS < 1) return set_error(BQ4_EUNSUPPORTED, "no shared-memory plan for this shape");
   p->stages = S;
+  p->a_stages = S;
   p->raw_stages = RS;
-  p->smem_bytes = 1024 + (size_t)S * stage_bytes + (size_t)RS * raw_stage_bytes +
-                  (size_t)(2 * S + 2 * RS + 2 * kNumPart + 4) * 8 + 16;
+  const int np = 512 / (nw * p->bt);
+  p->smem_bytes = 1024 + (size_t)S * stage_bytes + (size_t)RS * raw_stage +
+                  (size_t)(2 * S + 2 * RS + 2 * np) * 8 + 16;
 
   p->xh_bytes = align_up((size_t)M * (size_t)w->Kp * 2, 256);
   p->counter_bytes = align_up((size_t)tiles * sizeof(int) + sizeof(int) * 4, 256);
@@ -1011,7 +712,7 @@ bq4_status run_gemm(const GemmPlan& plan, const bq4_weight* const* ws, const flo
   float* partials =
       plan.partial_bytes ? reinterpret_cast<float*>(wsp + plan.xh_bytes + plan.counter_bytes) : nullptr;
 
-  // 1) stage activations as f16 (also zeroes split-K counters and the error word)
+  // 1) stage activations as f16 (also zeroes the split-K tile counters)
   cudaError_t e = launch_convert_x(x, M, w0->K, ldx, w0->Kp, xh, counters,
                                    plan.mtiles * plan.ntiles + 4, stream);
   if (e != cudaSuccess) return check_cuda(e, "convert_x launch");
@@ -1029,13 +730,12 @@ bq4_status run_gemm(const GemmPlan& plan, const bq4_weight* const* ws, const flo
                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (cr != CUDA_SUCCESS) return set_error(BQ4_ECUDA, "cuTensorMapEncodeTiled failed (%d)", (int)cr);
 
-  GemmArgs args;
+  WsArgs args;
   memset(&args, 0, sizeof(args));
-  args.pre = plan.pre;
   for (int i = 0; i < plan.nw; ++i) {
-    args.h[i] = ws[i]->h;
     args.q[i] = ws[i]->q;
     args.s[i] = ws[i]->s;
+    args.h[i] = ws[i]->h;
     args.bias[i] = bias ? bias[i] : nullptr;
   }
   args.aux = aux;
@@ -1052,29 +752,26 @@ bq4_status run_gemm(const GemmPlan& plan, const bq4_weight* const* ws, const flo
   args.ksplit = plan.ksplit;
   args.units = plan.units;
   args.stages = plan.stages;
-  args.raw_stages = plan.raw_stages;
-  args.raw_s_bytes = plan.exact ? 0u : 512u * (uint32_t)(w0->block >= 64 ? 1 : 64 / w0->block);
-  args.raw_w_bytes = plan.raw_w_bytes;
-  if (!plan.pre && !plan.exact && args.raw_w_bytes != kRawQBytes + args.raw_s_bytes)
-    return set_error(BQ4_EINVAL_ARG, "internal: raw stage size mismatch");
+  args.rs = plan.raw_stages;
+  args.exact = plan.exact;
+  args.pre = plan.pre;
   args.act = act;
+  args.raw_s_bytes = plan.raw_s_bytes;
+  args.raw_w_bytes = plan.raw_w_bytes;
 
-  if (plan.exact) {
-    if (plan.nw == 1) {
-      if (plan.bt == 128) e = launch_kernel<128, 1, true>(plan, tmap, args, stream);
-      else e = launch_kernel<64, 1, true>(plan, tmap, args, stream);
-    } else {
-      e = launch_kernel<64, 2, true>(plan, tmap, args, stream);
-    }
-  } else if (plan.nw == 1) {
-    if (plan.bt == 256) e = launch_kernel<256, 1, false>(plan, tmap, args, stream);
-    else if (plan.bt == 128) e = launch_kernel<128, 1, false>(plan, tmap, args, stream);
-    else e = launch_kernel<64, 1, false>(plan, tmap, args, stream);
+  bool ok_regs = true;
+  if (plan.nw == 1) {
+    if (plan.bt == 256) e = launch_ws<256, 1>(plan, tmap, args, stream, &ok_regs);
+    else if (plan.bt == 128) e = launch_ws<128, 1>(plan, tmap, args, stream, &ok_regs);
+    else e = launch_ws<64, 1>(plan, tmap, args, stream, &ok_regs);
   } else {
-    if (plan.bt == 128) e = launch_kernel<128, 2, false>(plan, tmap, args, stream);
-    else e = launch_kernel<64, 2, false>(plan, tmap, args, stream);
+    if (plan.bt == 128) e = launch_ws<128, 2>(plan, tmap, args, stream, &ok_regs);
+    else e = launch_ws<64, 2>(plan, tmap, args, stream, &ok_regs);
   }
   if (e != cudaSuccess) return check_cuda(e, "q4 gemm launch");
+  if (!ok_regs)
+    return set_error(BQ4_EUNSUPPORTED, "q4 gemm kernel was not built with %d registers per thread",
+                     kWsRegsLaunch);
   return BQ4_OK;
 }
 

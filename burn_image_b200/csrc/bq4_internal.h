@@ -19,8 +19,8 @@
 //        consecutive K values land in the low/high halves of an f16x2.
 //   s: f32 [ntiles][nkb][128]          scale of (row, K block), 0 in padding
 //
-// N is padded to Np = 128*ntiles and K to Kp = 64*nkc with zero nibbles and
-// zero scales; nkb = Kp / block.
+// N is padded to Np = 128*ntiles and K to Kp = 128*(nkc/2) with zero nibbles
+// and zero scales (nkc is even); nkb = Kp / block.
 struct bq4_weight {
   int64_t K, N;
   int64_t Kp, Np;
@@ -42,7 +42,8 @@ struct bq4_weight {
 namespace bq4 {
 
 constexpr int kTileN = 128;   // output features per tile (MMA M)
-constexpr int kChunkK = 64;   // K per pipeline stage (128 B of f16)
+constexpr int kChunkK = 64;   // K per MMA operand sub-tile (128 B of f16)
+constexpr int kStageK = 128;  // K per pipeline stage (two sub-tiles); K is padded to it
 
 // Error plumbing (thread-local message, see bq4_api.cu).
 bq4_status set_error(bq4_status code, const char* fmt, ...);
@@ -72,7 +73,8 @@ struct GemmPlan {
   int pre;         // 1 = pre-expanded f16 weight tiles (bulk-copied, no dequant)
   int bt;          // tokens per tile (MMA N): 64, 128 or 256
   int mtiles, ntiles, ksplit, units, grid;
-  int stages, raw_stages;
+  int stages, a_stages, raw_stages;  // B ring, A ring, raw ring depths
+  uint32_t raw_s_bytes;  // scale bytes per weight per raw stage (folded)
   uint32_t raw_w_bytes;  // shared-memory bytes per weight per raw stage
   size_t smem_bytes;
   size_t xh_bytes, counter_bytes, partial_bytes;  // workspace pieces

@@ -56,14 +56,32 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// try_wait with a suspend-time hint: the hardware parks the thread until the
+// phase completes (immediate wake-up) or the hint (ns) elapses.
+__device__ __forceinline__ bool mbar_try_wait_suspend(uint64_t* bar, uint32_t parity,
+                                                      uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
+
 // Bounded wait on the phase with parity `parity`.  Returns false on timeout
 // or when `abort_flag` (shared, set by any role that gave up) is raised.
+// The abort flag and the clock are only consulted between suspended
+// try_waits, so a completing phase wakes the waiter without extra latency.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
                                           volatile int* abort_flag) {
-  if (mbar_try_wait(bar, parity)) return true;
+  constexpr uint32_t kSuspendNs = 200000;  // 0.2 ms per suspended try
+  if (mbar_try_wait_suspend(bar, parity, kSuspendNs)) return true;
   const uint64_t t0 = globaltimer();
   while (true) {
-    if (mbar_try_wait(bar, parity)) return true;
+    if (mbar_try_wait_suspend(bar, parity, kSuspendNs)) return true;
     if (*abort_flag) return false;
     if (globaltimer() - t0 > kWaitTimeoutNs) return false;
   }
