@@ -133,6 +133,12 @@ __device__ __forceinline__ void record_error_flag(volatile int* abort_flag, int 
 // folded mode); the MMA accumulates a segment into one partial buffer and
 // the scaler warps fold it into f32 registers: acc += scale * partial
 // (scale = 1 in folded mode).  The epilogue runs from those registers.
+// Lockstep variant (exact mode, 128-blocks, 2 stages and 2 partials): a
+// segment is exactly one stage and uses the partial buffer of the same
+// index, so the scaler waits on the stage's `empty` barrier (its MMAs have
+// retired) and announces "partial free" by arriving on the `full` barrier
+// of that stage's next use; the issuer then needs no separate partial
+// handshakes -- one wait and one commit per stage, as in folded mode.
 //
 // Warps (896 threads, 7 warpgroups, registers rebalanced with setmaxnreg):
 //   WG0-3 (warps 0-15)  scaler + epilogue, 96 regs: warp w reads TMEM lanes
@@ -165,6 +171,7 @@ struct WsArgs {
   int ntiles, mtiles, ksplit, units;
   int stages, rs;          // operand ring and raw ring depths
   int exact, pre, act;
+  int lockstep;            // exact, 128-blocks, 2 stages == 2 TMEM partials (see below)
   uint32_t raw_s_bytes;    // folded: scale bytes per weight per raw stage
   uint32_t raw_w_bytes;    // raw stage bytes per weight
 };
@@ -223,8 +230,9 @@ __global__ void __launch_bounds__(kWsThreads, 1)
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < S; ++i) {
-      ptx::mbar_init(&full[i], a.pre ? 1 : 1 + kWsDqWarps);  // TMA expect_tx (+ dequant warps)
-      ptx::mbar_init(&empty[i], 1);                          // tcgen05.commit
+      // TMA expect_tx (+ dequant warps) (+ scaler warps in lockstep mode)
+      ptx::mbar_init(&full[i], (a.pre ? 1 : 1 + kWsDqWarps) + (a.lockstep ? kWsScalerWarps : 0));
+      ptx::mbar_init(&empty[i], 1);  // tcgen05.commit
     }
     for (int i = 0; i < RS; ++i) { ptx::mbar_init(&raw_full[i], 1); ptx::mbar_init(&raw_empty[i], kWsDqWarps); }
     for (int i = 0; i < kNP; ++i) { ptx::mbar_init(&part_full[i], 1); ptx::mbar_init(&part_empty[i], kWsScalerWarps); }
@@ -315,9 +323,13 @@ __global__ void __launch_bounds__(kWsThreads, 1)
             const int c = kc + sub;
             const bool first = ws_seg_first(c, kc0, cpb);
             if (first) {
-              if (!ptx::mbar_wait(&part_empty[pb], pph ^ 1, abort_flag)) { ok = false; break; }
-              ptx::tc_fence_after();
-              d_base = tmem_base + (uint32_t)pb * kPartCols;
+              if (a.lockstep) {
+                d_base = tmem_base + (uint32_t)s * kPartCols;  // freed via full[s]
+              } else {
+                if (!ptx::mbar_wait(&part_empty[pb], pph ^ 1, abort_flag)) { ok = false; break; }
+                ptx::tc_fence_after();
+                d_base = tmem_base + (uint32_t)pb * kPartCols;
+              }
             }
             const uint32_t b_addr = st + kAStage + sub * kBSub;
 #pragma unroll
@@ -330,7 +342,7 @@ __global__ void __launch_bounds__(kWsThreads, 1)
                                 idesc, (first && kk == 0) ? 0u : 1u);
             }
             if (sub == 1) ptx::mma_commit(&empty[s]);  // stage free once its MMAs retire
-            if (ws_seg_last(c, kc1, cpb)) {
+            if (!a.lockstep && ws_seg_last(c, kc1, cpb)) {
               ptx::mma_commit(&part_full[pb]);
               if (++pb == kNP) { pb = 0; pph ^= 1; }
             }
@@ -408,6 +420,10 @@ __global__ void __launch_bounds__(kWsThreads, 1)
     int pb = 0;
     uint32_t pph = 0;
     bool ok = true;
+    if (a.lockstep && lane == 0) {
+      // both partial buffers start free: the first use of each stage
+      for (int i = 0; i < S; ++i) ptx::mbar_arrive(&full[i]);
+    }
     for (int u = blockIdx.x; ok && u < a.units && !*abort_flag; u += gridDim.x) {
       int tile, split, kc0, kc1;
       ws_unit(a, u, tile, split, kc0, kc1);
@@ -425,7 +441,8 @@ __global__ void __launch_bounds__(kWsThreads, 1)
 #pragma unroll
         for (int w = 0; w < NW; ++w)
           sc[w] = a.exact ? __ldg(a.s[w] + ((size_t)ntile * a.nkb + (kc * kChunkK) / a.block) * 128 + row) : 1.0f;
-        if (!ptx::mbar_wait(&part_full[pb], pph, abort_flag)) { ok = false; break; }
+        // lockstep: segment == stage pb (S == NP), retired when empty[pb] completes
+        if (!ptx::mbar_wait(a.lockstep ? &empty[pb] : &part_full[pb], pph, abort_flag)) { ok = false; break; }
         ptx::tc_fence_after();
         const uint32_t t_row = tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)pb * kPartCols + col0;
 #pragma unroll
@@ -441,7 +458,7 @@ __global__ void __launch_bounds__(kWsThreads, 1)
         }
         ptx::tc_fence_before();
         __syncwarp();
-        if (lane == 0) ptx::mbar_arrive(&part_empty[pb]);
+        if (lane == 0) ptx::mbar_arrive(a.lockstep ? &full[pb] : &part_empty[pb]);
         if (++pb == kNP) { pb = 0; pph ^= 1; }
       }
       if (!ok) break;
@@ -690,6 +707,10 @@ bq4_status plan_gemm(const bq4_weight* w, int nw, int64_t M, int device, GemmPla
   p->stages = S;
   p->a_stages = S;
   p->raw_stages = RS;
+  // Lockstep partial handoff: exact 128-blocks, one segment per stage, as
+  // many stages as TMEM partial buffers (2).
+  p->lockstep = (p->exact && w->block == 128 && S == 2 && 512 / (nw * p->bt) == 2) ? 1 : 0;
+  if (getenv("BQ4_NO_LOCKSTEP")) p->lockstep = 0;
   const int np = 512 / (nw * p->bt);
   p->smem_bytes = 1024 + (size_t)S * stage_bytes + (size_t)RS * raw_stage +
                   (size_t)(2 * S + 2 * RS + 2 * np) * 8 + 16;
@@ -755,6 +776,7 @@ bq4_status run_gemm(const GemmPlan& plan, const bq4_weight* const* ws, const flo
   args.rs = plan.raw_stages;
   args.exact = plan.exact;
   args.pre = plan.pre;
+  args.lockstep = plan.lockstep;
   args.act = act;
   args.raw_s_bytes = plan.raw_s_bytes;
   args.raw_w_bytes = plan.raw_w_bytes;

@@ -71,6 +71,7 @@ struct GemmPlan {
   int nw;          // 1 = plain, 2 = gated (gate, up)
   int exact;       // 1 = exact-weight kernel (scale on the f32 accumulator)
   int pre;         // 1 = pre-expanded f16 weight tiles (bulk-copied, no dequant)
+  int lockstep;    // 1 = exact mode with stage == segment partial handoff
   int bt;          // tokens per tile (MMA N): 64, 128 or 256
   int mtiles, ntiles, ksplit, units, grid;
   int stages, a_stages, raw_stages;  // B ring, A ring, raw ring depths
