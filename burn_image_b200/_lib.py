@@ -21,6 +21,7 @@ STATUS_NAMES = {
 }
 LAYOUT_COL, LAYOUT_ROW, LAYOUT_NPACKED = 0, 1, 2
 ACT_NONE, ACT_GELU_TANH, ACT_SILU = 0, 1, 2
+NOALLOC_SCRATCH_BYTES = 32 << 20  # BQ4_NOALLOC_SCRATCH_BYTES
 
 # Every symbol include/bq4.h declares, with (restype, argtypes).
 _p, _i32, _i64, _sz, _u64 = ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64, ctypes.c_size_t, ctypes.c_uint64
@@ -35,6 +36,7 @@ SIGNATURES = {
                               ctypes.POINTER(_i32), ctypes.POINTER(_sz)]),
     "bq4_linear_workspace_size": (_st, [_p, _i64, ctypes.POINTER(_sz)]),
     "bq4_linear": (_st, [_p, _p, _i64, _i64, _p, _i32, _p, _p, _p, _sz, _p]),
+    "bq4_linear_noalloc": (_st, [_p, _p, _i64, _i64, _p, _i32, _p, _p, _p]),
     "bq4_linear_gated_workspace_size": (_st, [_p, _p, _i64, ctypes.POINTER(_sz)]),
     "bq4_linear_gated": (_st, [_p, _p, _p, _i64, _i64, _p, _p, _p, _p, _sz, _p]),
     "bq4_dequant": (_st, [_p, _p, _i32, _p]),

@@ -146,6 +146,26 @@ BQ4_API bq4_status bq4_dequant_raw(const uint32_t* packed_words, const float* sc
                            int32_t block, bq4_layout layout, float* out, bq4_layout out_layout,
                            bq4_stream_t stream);
 
+/*
+ * bq4_linear for callers that cannot allocate device memory.  No
+ * counterpart in the reference: its op allocates through Burn's own
+ * allocator.  Some callers of this library have no way to hand it a
+ * workspace -- a runtime whose allocator owns all device memory, code that
+ * must not call the (device-synchronizing) cudaMalloc, or a process that may
+ * not grow its device footprint after start-up.  This entry point computes
+ * exactly what bq4_linear computes, with its scratch in a static device
+ * array of BQ4_NOALLOC_SCRATCH_BYTES that every GPU loading the library
+ * holds until exit; it allocates nothing.  Calls whose scratch need
+ * (bq4_linear_workspace_size for the same weight and M) exceeds that size
+ * return BQ4_EWORKSPACE.  The first call on a device looks up the array's
+ * device address, so make it before any stream capture.  All calls on a
+ * device share the array: calls that overlap on the GPU race.
+ */
+#define BQ4_NOALLOC_SCRATCH_BYTES (32u << 20)
+BQ4_API bq4_status bq4_linear_noalloc(const bq4_weight* w, const float* x, int64_t M, int64_t ldx,
+                                      const float* bias, bq4_act act, const float* aux, float* y,
+                                      bq4_stream_t stream);
+
 /* ------------------------------------------------------- q_matmul mirror
  * The reference op's scheme fields (burn-std 0.21 QuantScheme) on this path.
  * q_matmul accepts exactly what the reference's packed-Q4 eligibility test
