@@ -39,7 +39,7 @@ WORKLOAD = "dit_layer_stack_24x(qkv3072x9216,o3072x3072,up3072x12288+gelu,down12
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--blocks", type=int, default=BLOCKS)
@@ -60,7 +60,7 @@ def dist_env():
 
 class ClockSampler:
     """nvidia-smi sampling of SM clocks and throttle reasons during the timed region."""
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+    FIELDS = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
@@ -74,15 +74,22 @@ class ClockSampler:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+                 "-lms", "50"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.thread = threading.Thread(target=self._read, daemon=True)
             self.thread.start()
+            time.sleep(1.0)  # let nvidia-smi start sampling before the timed region
         except Exception:
             self.proc = None
 
     def _read(self):
         for line in self.proc.stdout:
-            self.lines.append(line.strip())
+            self.lines.append((time.time(), line.strip()))
+
+    def mark(self, start: bool):
+        if start:
+            self.t_start = time.time()
+        else:
+            self.t_end = time.time()
 
     def stop(self):
         if self.proc is None:
@@ -96,16 +103,20 @@ class ClockSampler:
             self.thread.join(timeout=2)
         sm, smax, reasons = [], [], set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
+        t0 = getattr(self, "t_start", 0.0)
+        t1 = getattr(self, "t_end", 1e30)
+        for ts, ln in self.lines:
+            if not (t0 <= ts <= t1 + 0.05):  # samples read during the timed region
+                continue
             parts = [p.strip() for p in ln.split(",")]
-            if len(parts) < 9:
+            if len(parts) < 10:
                 continue
             try:
-                sm.append(float(parts[1]))
-                smax.append(float(parts[2]))
+                sm.append(float(parts[2]))
+                smax.append(float(parts[3]))
             except ValueError:
                 continue
-            for nm, v in zip(names, parts[5:9]):
+            for nm, v in zip(names, parts[6:10]):
                 if v.lower() == "active":
                     reasons.add(nm)
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(smax) if smax else None,
@@ -227,6 +238,7 @@ def run_ours(args):
     lib.bq4_launch_count_reset()
     t_start = torch.cuda.Event(enable_timing=True)
     t_end = torch.cuda.Event(enable_timing=True)
+    clocks.mark(True)
     torch.cuda.nvtx.range_push("timed")
     t_start.record(stream)
     for _ in range(args.steps):
@@ -234,6 +246,7 @@ def run_ours(args):
     t_end.record(stream)
     torch.cuda.nvtx.range_pop()
     barrier()
+    clocks.mark(False)
     launches = int(lib.bq4_launch_count())
     clk = clocks.stop()
     elapsed_ms = t_start.elapsed_time(t_end)
@@ -251,6 +264,25 @@ def run_ours(args):
     lin_ms = sum(sum(v) for v in per.values())
     lin_flops = flops_step * args.steps / world  # this rank's share
     achieved_tflops = lin_flops / (lin_ms * 1e-3) / 1e12
+
+    # ---- the same stack with exact-weight numerics (scale on the f32 accumulator)
+    from burn_image_b200 import q4 as _q4
+    _q4.set_numerics(L.NUMERICS_EXACT)
+    for _ in range(2):
+        stack.forward(x0)
+    barrier()
+    x_start = torch.cuda.Event(enable_timing=True)
+    x_end = torch.cuda.Event(enable_timing=True)
+    x_start.record(stream)
+    for _ in range(args.steps):
+        stack.forward(x0)
+    x_end.record(stream)
+    barrier()
+    _q4.set_numerics(L.NUMERICS_AUTO)
+    t = torch.tensor([x_start.elapsed_time(x_end)], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    value_exact = flops_step / (t.item() / args.steps * 1e-3) / 1e12
 
     # ---- e2e: through the public API with host buffers
     x_host = x0.cpu().pin_memory()
@@ -312,6 +344,9 @@ def run_ours(args):
                          "frac": achieved_tflops / peak, "traffic": traffic,
                          "peak_source": peak_src,
                          "kernel": "bq4_linear (convert_x + q4_gemm_kernel), CUDA events per call, rank 0"},
+            "numerics": "auto: f16(q*scale) staging (the reference kernel's) at this M; "
+                        "value_exact = the same stack with q exact and the scale on the f32 accumulator",
+            "value_exact": value_exact,
             "per_linear_ms": {k: sum(v) / len(v) for k, v in per.items()},
             "e2e": {"value": e2e_value, "unit": "TFLOP/s", "h2d_bytes_per_step": M * HIDDEN * 4,
                     "d2h_bytes_per_step": M * HIDDEN * 4},

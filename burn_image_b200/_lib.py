@@ -22,6 +22,7 @@ STATUS_NAMES = {
 LAYOUT_COL, LAYOUT_ROW, LAYOUT_NPACKED = 0, 1, 2
 ACT_NONE, ACT_GELU_TANH, ACT_SILU = 0, 1, 2
 NOALLOC_SCRATCH_BYTES = 32 << 20  # BQ4_NOALLOC_SCRATCH_BYTES
+NUMERICS_AUTO, NUMERICS_EXACT, NUMERICS_FOLDED = 0, 1, 2
 
 # Every symbol include/bq4.h declares, with (restype, argtypes).
 _p, _i32, _i64, _sz, _u64 = ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64, ctypes.c_size_t, ctypes.c_uint64
@@ -47,6 +48,7 @@ SIGNATURES = {
     "bq4_quantize_row_up_to128": (_st, [_p, _i64, _i64, _p, _p, ctypes.POINTER(_i32)]),
     "bq4_row_block_for": (_i32, [_i64]),
     "bq4_poll_device_error": (_st, []),
+    "bq4_set_numerics": (_st, [_i32]),
     "bq4_launch_count": (_u64, []),
     "bq4_launch_count_reset": (None, []),
 }

@@ -208,6 +208,13 @@ void bq4_launch_count_reset(void) { g_launches = 0; }
 
 bq4_status bq4_poll_device_error(void) { return poll_device_error(); }
 
+bq4_status bq4_set_numerics(bq4_numerics mode) {
+  if (mode != BQ4_NUMERICS_AUTO && mode != BQ4_NUMERICS_EXACT && mode != BQ4_NUMERICS_FOLDED)
+    return set_error(BQ4_EINVAL_ARG, "numerics mode %d unknown", (int)mode);
+  set_numerics_mode((int)mode);
+  return BQ4_OK;
+}
+
 bq4_status bq4_weight_prepare(const uint32_t* packed_words, const float* scales, int64_t K,
                               int64_t N, int32_t block, bq4_layout layout, int32_t device,
                               bq4_weight** out) {

@@ -30,6 +30,7 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
@@ -595,6 +596,27 @@ cudaError_t launch_ws(const GemmPlan& plan, const CUtensorMap& tmap, const WsArg
 
 }  // namespace
 
+namespace {
+std::atomic<int> g_numerics{-1};
+}
+
+int numerics_mode() {
+  int v = g_numerics.load(std::memory_order_relaxed);
+  if (v < 0) {
+    v = BQ4_NUMERICS_AUTO;
+    if (const char* e = getenv("BQ4_NUMERICS")) {
+      if (!strcmp(e, "exact")) v = BQ4_NUMERICS_EXACT;
+      else if (!strcmp(e, "folded")) v = BQ4_NUMERICS_FOLDED;
+    }
+    int expected = -1;
+    g_numerics.compare_exchange_strong(expected, v);
+    v = g_numerics.load(std::memory_order_relaxed);
+  }
+  return v;
+}
+
+void set_numerics_mode(int mode) { g_numerics.store(mode, std::memory_order_relaxed); }
+
 int device_sm_count(int device) {
   static int cache[64] = {0};
   if (device < 0 || device >= 64) return 148;
@@ -624,7 +646,10 @@ bq4_status plan_gemm(const bq4_weight* w, int nw, int64_t M, int device, GemmPla
   // partial of each K block by its scale (exact weights); smaller blocks
   // stage f16(q * f16(scale)) (folded); N-packed sources are pre-expanded.
   p->pre = w->h != nullptr ? 1 : 0;
-  p->exact = (!p->pre && w->block >= 64) ? 1 : 0;
+  const int mode = numerics_mode();
+  p->exact = (!p->pre && w->block >= 64 &&
+              (mode == BQ4_NUMERICS_EXACT || (mode == BQ4_NUMERICS_AUTO && M <= kAutoExactMaxM)))
+                 ? 1 : 0;
   // BQ4_FORCE_FOLDED=1 selects folded staging for any block (tests compare
   // both formulations on the same shapes).
   if (const char* f = getenv("BQ4_FORCE_FOLDED"))

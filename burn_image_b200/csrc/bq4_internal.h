@@ -88,6 +88,12 @@ bq4_status run_gemm(const GemmPlan& plan, const bq4_weight* const* ws, const flo
                     int64_t ldx, const float* const* bias, int act, const float* aux, float* y,
                     void* workspace, cudaStream_t stream);
 
+// Operand staging policy (bq4_numerics); AUTO keeps exact weights up to
+// this many rows.
+constexpr int64_t kAutoExactMaxM = 1024;
+int numerics_mode();
+void set_numerics_mode(int mode);
+
 int device_sm_count(int device);
 int device_is_sm100(int device);
 

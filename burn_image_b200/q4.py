@@ -386,6 +386,13 @@ def feed_forward_swiglu(l1: Q4Linear, l3: Q4Linear, l2: Q4Linear, x: torch.Tenso
     return linear_forward(l2, gated)
 
 
+def set_numerics(mode: int) -> None:
+    """Operand staging for subsequent calls: NUMERICS_AUTO (exact weights up
+    to M = 1024 rows, the reference's f16 staging above), NUMERICS_EXACT or
+    NUMERICS_FOLDED (see include/bq4.h)."""
+    check(L.lib().bq4_set_numerics(mode))
+
+
 def poll_device_error() -> None:
     """Raise if a kernel's bounded device-side wait expired since the last poll."""
     check(L.lib().bq4_poll_device_error())

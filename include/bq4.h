@@ -68,6 +68,22 @@ typedef enum {
 
 typedef struct bq4_weight bq4_weight; /* opaque prepared weight (device resident) */
 
+/*
+ * Operand staging of the GEMM (weights with blocks of 64/128; smaller blocks
+ * and N-packed weights always use FOLDED):
+ *   EXACT  -- q stays exact in f16 and each K block's f32 partial is
+ *             multiplied by its scale: weights enter the sum as exactly
+ *             q * scale; only activations are rounded (to f16).
+ *   FOLDED -- weights staged as f16(q * f16(scale)), the staging of the
+ *             reference GPU kernel (patches/burn-cubecl-0.21.0/src/kernel/
+ *             matmul/quantized.rs:172-178); faster at large M.
+ *   AUTO   -- EXACT for M <= 1024 rows, FOLDED above (default).
+ * Both are f32-accumulated; both meet the 5e-3 relative-Frobenius bound.
+ * The initial value comes from the environment variable BQ4_NUMERICS
+ * (auto|exact|folded), else AUTO.
+ */
+typedef enum { BQ4_NUMERICS_AUTO = 0, BQ4_NUMERICS_EXACT = 1, BQ4_NUMERICS_FOLDED = 2 } bq4_numerics;
+
 /* Library version string and the message of the last failed call on this thread. */
 BQ4_API const char* bq4_version(void);
 BQ4_API const char* bq4_last_error_string(void);
@@ -222,6 +238,9 @@ BQ4_API int32_t bq4_row_block_for(int64_t input);
  * BQ4_ETIMEOUT when a kernel's bounded wait expired since the last poll (the
  * kernel unwound without trapping; its output is invalid).  Synchronizes. */
 BQ4_API bq4_status bq4_poll_device_error(void);
+
+/* Process-wide operand staging for subsequent compute calls (see bq4_numerics). */
+BQ4_API bq4_status bq4_set_numerics(bq4_numerics mode);
 
 /* Kernel launches issued by this thread since the last reset (bench accounting). */
 BQ4_API uint64_t bq4_launch_count(void);

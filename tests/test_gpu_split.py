@@ -26,8 +26,14 @@ def problem(M, K, N, block):
 @pytest.mark.parametrize("M,K,N", [(256, 9728, 2560), (512, 4096, 4096), (4352, 12288, 3072)])
 def test_partitioning_does_not_change_results(M, K, N, S, folded, monkeypatch):
     monkeypatch.setenv("BQ4_FORCE_KSPLIT", str(S))
-    if folded:
-        monkeypatch.setenv("BQ4_FORCE_FOLDED", "1")
+    q4.set_numerics(L.NUMERICS_FOLDED if folded else L.NUMERICS_EXACT)
+    try:
+        _check_partitioning(M, K, N, folded)
+    finally:
+        q4.set_numerics(L.NUMERICS_AUTO)
+
+
+def _check_partitioning(M, K, N, folded):
     block = 128
     words, scales, x = problem(M, K, N, block)
     pw = q4.PreparedQ4Weight(words, scales, K, N, block, L.LAYOUT_ROW, DEV)
@@ -47,3 +53,24 @@ def test_partitioning_does_not_change_results(M, K, N, S, folded, monkeypatch):
             first = y.clone()
         else:
             assert torch.equal(first, y)
+
+
+@pytest.mark.parametrize("M,K,N", [(256, 2560, 512), (4352, 3072, 1024)])
+def test_numerics_modes_both_within_tolerance(M, K, N):
+    """EXACT and FOLDED staging (and AUTO) all meet the 5e-3 relative
+    Frobenius bound against a float64 reference of the exact weights."""
+    words, scales, x = problem(M, K, N, 128)
+    pw = q4.PreparedQ4Weight(words, scales, K, N, 128, L.LAYOUT_ROW, DEV)
+    ref = x.double() @ pw.dequantize().double()
+    errs = {}
+    for mode in (L.NUMERICS_EXACT, L.NUMERICS_FOLDED, L.NUMERICS_AUTO):
+        q4.set_numerics(mode)
+        try:
+            y = pw.linear(x)
+            torch.cuda.synchronize()
+        finally:
+            q4.set_numerics(L.NUMERICS_AUTO)
+        errs[mode] = (torch.linalg.norm(y.double() - ref) / torch.linalg.norm(ref)).item()
+        assert errs[mode] <= 5e-3
+    assert errs[L.NUMERICS_EXACT] < errs[L.NUMERICS_FOLDED]
+    print(f"numerics M{M}: exact {errs[1]:.3e} folded {errs[2]:.3e} auto {errs[0]:.3e}")
