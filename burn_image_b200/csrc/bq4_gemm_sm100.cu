@@ -7,21 +7,16 @@
 // of tokens (f16 activations, K-major), so D[n, m] accumulates in TMEM with
 // TMEM lane = output feature and TMEM column = token.
 //
-// Warp roles (352 threads, one CTA per SM, persistent over work units):
-//   warps 0-3  epilogue: tcgen05.ld of the accumulator, bias / GELU-tanh /
-//              SiLU-gate / aux-multiply, coalesced f32 stores (or split-K
-//              partials plus a last-arriver fix-up)
-//   warps 4-7  dequant: read a raw 4 KiB nibble tile + its scales from shared
-//              memory, expand to f16(q * scale) and write the A tile in the
-//              128-byte-swizzled K-major layout the MMA reads
-//   warp 8     TMA producer for token tiles (2-D tensor map, no multicast)
-//   warp 9     bulk-copy producer for raw nibble/scale tiles (1-D bulk copies)
-//   warp 10    TMEM allocator and single-thread MMA issuer
+// One CTA of 896 threads per SM, persistent over (M tile, N tile) units; the
+// warp roles are described above q4_gemm_ws_kernel.  Split-K units of one
+// tile run as one thread-block cluster and reduce their partial tiles
+// through distributed shared memory.
 //
-// Numerics: operands staged as f16 (activations rounded to nearest even,
-// weights f16(q * f16(scale))), f32 accumulation.  This is the staging of the
-// reference GPU kernel (patches/burn-cubecl-0.21.0/src/kernel/matmul/
-// quantized.rs:172-178: lhs and rhs stage/register dtypes f16, f32 acc).
+// Numerics: activations staged as f16 (round to nearest even), f32
+// accumulation; weights either exact (q in f16, the f32 partial of each K
+// block multiplied by its scale) or folded (f16(q * f16(scale)), the staging
+// of the reference GPU kernel, patches/burn-cubecl-0.21.0/src/kernel/matmul/
+// quantized.rs:172-178: lhs and rhs stage dtypes f16, f32 accumulation).
 //
 // Every mbarrier wait is time-bounded; on expiry the kernel records
 // BQ4_ETIMEOUT in the device error word, raises a shared abort flag so every
@@ -134,8 +129,8 @@ __device__ __forceinline__ void record_error_flag(volatile int* abort_flag, int 
 // folded mode); the MMA accumulates a segment into one partial buffer and
 // the scaler warps fold it into f32 registers: acc += scale * partial
 // (scale = 1 in folded mode).  The epilogue runs from those registers.
-// Lockstep variant (exact mode, 128-blocks, 2 stages and 2 partials): a
-// segment is exactly one stage and uses the partial buffer of the same
+// Lockstep variant (exact mode, 128-blocks, no more stages than partials):
+// a segment is exactly one stage and uses the partial buffer of the same
 // index, so the scaler waits on the stage's `empty` barrier (its MMAs have
 // retired) and announces "partial free" by arriving on the `full` barrier
 // of that stage's next use; the issuer then needs no separate partial
@@ -157,6 +152,7 @@ constexpr int kWsRegsProducer = 24;
 constexpr int kWsTmaWarp = 24, kWsWeightWarp = 25, kWsMmaWarp = 26;
 constexpr int kWsDqWarp0 = 16, kWsDqWarps = 8, kWsScalerWarps = 16;
 constexpr uint32_t kRawStageQBytes = 2 * kRawQBytes;  // nibbles of one 128-K stage
+constexpr int kMaxSplit = 8;  // split-K factor limit: the portable cluster size
 
 struct WsArgs {
   const uint32_t* q[2];
@@ -165,26 +161,40 @@ struct WsArgs {
   const float* bias[2];
   const float* aux;
   float* y;
-  float* partials;
-  int* counters;
   int M, N;
   int nkc, nkb, block;
   int ntiles, mtiles, ksplit, units;
+  int nfast;               // 1: N tile varies fastest along the unit order
+  int yvec;                // 1: y rows 16-byte aligned (float4 stores in the split epilogue)
   int stages, rs;          // operand ring and raw ring depths
   int exact, pre, act;
-  int lockstep;            // exact, 128-blocks, 2 stages == 2 TMEM partials (see below)
+  int lockstep;            // exact, 128-blocks, stage s accumulates into TMEM partial s (see below)
   uint32_t raw_s_bytes;    // folded: scale bytes per weight per raw stage
   uint32_t raw_w_bytes;    // raw stage bytes per weight
 };
 
 // Unit u -> (tile, split) and its chunk range [kc0, kc1); splits cut at
-// stage (2-chunk) boundaries.
+// stage (2-chunk) boundaries.  With ksplit > 1 the grid has one CTA per unit
+// and the ksplit units of a tile form one cluster (split == cluster rank).
 __device__ __forceinline__ void ws_unit(const WsArgs& a, int u, int& tile, int& split, int& kc0, int& kc1) {
   tile = u / a.ksplit;
   split = u - tile * a.ksplit;
   const int nks = a.nkc >> 1;
   kc0 = 2 * (int)((int64_t)split * nks / a.ksplit);
   kc1 = 2 * (int)((int64_t)(split + 1) * nks / a.ksplit);
+}
+
+// Tile -> (M tile, N tile).  Consecutive tiles run in the same wave; the
+// planner makes the operand that is larger in HBM (f16 tokens vs Q4 weights)
+// the one a wave shares, so it is read from DRAM about once.
+__device__ __forceinline__ void ws_tile(const WsArgs& a, int tile, int& mtile, int& ntile) {
+  if (a.nfast) {
+    mtile = tile / a.ntiles;
+    ntile = tile - mtile * a.ntiles;
+  } else {
+    ntile = tile / a.mtiles;
+    mtile = tile - ntile * a.mtiles;
+  }
 }
 
 // Segment boundaries inside [kc0, kc1): exact mode cuts at K-block edges
@@ -194,6 +204,74 @@ __device__ __forceinline__ bool ws_seg_first(int kc, int kc0, int cpb) {
 }
 __device__ __forceinline__ bool ws_seg_last(int kc, int kc1, int cpb) {
   return kc == kc1 - 1 || (cpb > 0 && ((kc + 1) % cpb) == 0);
+}
+
+// Split-K reduction across the cluster (one CTA per split, cluster rank =
+// split).  Every CTA holds its split's partial tile red[NW][BT][128] f32 in
+// shared memory; CTA `rank` sums a 1/ksplit slice of the tile over all
+// splits in rank order (deterministic), through distributed shared memory,
+// and runs the epilogue on it.  Called by the 512 scaler threads between two
+// cluster barriers.
+template <int BT, int NW>
+__device__ __forceinline__ void split_reduce_epilogue(const WsArgs& a, const uint8_t* red_smem) {
+  const int SPL = a.ksplit;
+  const uint32_t rank = ptx::cluster_ctarank();
+  int mtile, ntile;
+  ws_tile(a, (int)blockIdx.x / SPL, mtile, ntile);
+  constexpr int kGroups = BT * 32;            // 4-feature groups of one weight's partial tile
+  constexpr int kBatch = NW == 1 ? 8 : 4;     // peer loads in flight per thread
+  const int g0 = (int)((int64_t)kGroups * rank / SPL);
+  const int g1 = (int)((int64_t)kGroups * (rank + 1) / SPL);
+  const uint32_t red = ptx::smem_u32(red_smem);
+  const int act = a.act;
+  for (int g = g0 + (int)threadIdx.x; g < g1; g += kWsScalerWarps * 32) {
+    const int col = g >> 5;
+    const int r4 = (g & 31) << 2;
+    const int m = mtile * BT + col;
+    const int n = ntile * 128 + r4;
+    if (m >= a.M || n >= a.N) continue;
+    float v[NW][4];
+#pragma unroll
+    for (int w = 0; w < NW; ++w) v[w][0] = v[w][1] = v[w][2] = v[w][3] = 0.0f;
+    for (int p0 = 0; p0 < SPL; p0 += kBatch) {
+      float4 t[kBatch][NW];
+#pragma unroll
+      for (int i = 0; i < kBatch; ++i)
+        if (p0 + i < SPL)
+#pragma unroll
+          for (int w = 0; w < NW; ++w)
+            t[i][w] = ptx::ld_shared_cluster_f4(
+                ptx::mapa_shared(red + (uint32_t)(((w * BT + col) * 128 + r4) * 4), (uint32_t)(p0 + i)));
+#pragma unroll
+      for (int i = 0; i < kBatch; ++i)
+        if (p0 + i < SPL)
+#pragma unroll
+          for (int w = 0; w < NW; ++w) {
+            v[w][0] += t[i][w].x; v[w][1] += t[i][w].y; v[w][2] += t[i][w].z; v[w][3] += t[i][w].w;
+          }
+    }
+    float o[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int nn = n + i < a.N ? n + i : a.N - 1;
+      const float b0 = a.bias[0] ? __ldg(a.bias[0] + nn) : 0.0f;
+      if (NW == 2) {
+        const float b1 = a.bias[1] ? __ldg(a.bias[1] + nn) : 0.0f;
+        o[i] = silu(v[0][i] + b0) * (v[NW - 1][i] + b1);
+      } else {
+        o[i] = apply_act(v[0][i] + b0, act);
+        if (a.aux) o[i] *= __ldg(a.aux + (size_t)m * a.N + nn);
+      }
+    }
+    float* dst = a.y + (size_t)m * a.N + n;
+    if (a.yvec && n + 3 < a.N) {
+      *reinterpret_cast<float4*>(dst) = make_float4(o[0], o[1], o[2], o[3]);
+    } else {
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+        if (n + i < a.N) dst[i] = o[i];
+    }
+  }
 }
 
 template <int BT, int NW>
@@ -223,7 +301,6 @@ __global__ void __launch_bounds__(kWsThreads, 1)
   uint64_t* part_empty = part_full + kNP;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(part_empty + kNP);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  volatile int* last_flag = abort_flag + 1;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -238,7 +315,6 @@ __global__ void __launch_bounds__(kWsThreads, 1)
     for (int i = 0; i < RS; ++i) { ptx::mbar_init(&raw_full[i], 1); ptx::mbar_init(&raw_empty[i], kWsDqWarps); }
     for (int i = 0; i < kNP; ++i) { ptx::mbar_init(&part_full[i], 1); ptx::mbar_init(&part_empty[i], kWsScalerWarps); }
     *abort_flag = 0;
-    *last_flag = 0;
     ptx::fence_mbar_init();
   }
   if (warp == kWsTmaWarp && lane == 0) ptx::prefetch_tmap(&tmap_x);
@@ -255,12 +331,16 @@ __global__ void __launch_bounds__(kWsThreads, 1)
     asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kWsRegsProducer));
     if (warp == kWsTmaWarp && lane == 0) {
       // ------------------------------------------------ token tiles (+ pre-expanded A)
+      // xh is written by the activation-staging grid launched just before
+      // this one; every other operand was complete before that grid started.
+      ptx::griddep_wait();
       int s = 0;
       uint32_t ph = 0;
       for (int u = blockIdx.x; u < a.units && !*abort_flag; u += gridDim.x) {
         int tile, split, kc0, kc1;
         ws_unit(a, u, tile, split, kc0, kc1);
-        const int mtile = tile % a.mtiles, ntile = tile / a.mtiles;
+        int mtile, ntile;
+        ws_tile(a, tile, mtile, ntile);
         for (int kc = kc0; kc < kc1; kc += 2) {
           if (!ptx::mbar_wait(&empty[s], ph ^ 1, abort_flag)) {
             record_error_flag(abort_flag, BQ4_ETIMEOUT);
@@ -286,7 +366,8 @@ __global__ void __launch_bounds__(kWsThreads, 1)
       for (int u = blockIdx.x; u < a.units && !*abort_flag; u += gridDim.x) {
         int tile, split, kc0, kc1;
         ws_unit(a, u, tile, split, kc0, kc1);
-        const int ntile = tile / a.mtiles;
+        int mtile, ntile;
+        ws_tile(a, tile, mtile, ntile);
         for (int kc = kc0; kc < kc1; kc += 2) {
           if (!ptx::mbar_wait(&raw_empty[rs], rph ^ 1, abort_flag)) {
             record_error_flag(abort_flag, BQ4_ETIMEOUT);
@@ -353,6 +434,11 @@ __global__ void __launch_bounds__(kWsThreads, 1)
       }
       if (!ok) record_error_flag(abort_flag, BQ4_ETIMEOUT);
     }
+    if (a.ksplit > 1) {  // the two cluster barriers of the split reduction
+      __syncwarp();
+      ptx::cluster_sync();
+      ptx::cluster_sync();
+    }
   } else if (warp >= kWsDqWarp0) {
     asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kWsRegsDequant));
     if (!a.pre) {
@@ -412,6 +498,11 @@ __global__ void __launch_bounds__(kWsThreads, 1)
       }
       if (!ok) record_error_flag(abort_flag, BQ4_ETIMEOUT);
     }
+    if (a.ksplit > 1) {  // the two cluster barriers of the split reduction
+      __syncwarp();
+      ptx::cluster_sync();
+      ptx::cluster_sync();
+    }
   } else {
     asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kWsRegsScaler));
     // ------------------------------------------------ scaler + epilogue
@@ -428,7 +519,8 @@ __global__ void __launch_bounds__(kWsThreads, 1)
     for (int u = blockIdx.x; ok && u < a.units && !*abort_flag; u += gridDim.x) {
       int tile, split, kc0, kc1;
       ws_unit(a, u, tile, split, kc0, kc1);
-      const int ntile = tile / a.mtiles, mtile = tile - ntile * a.mtiles;
+      int mtile, ntile;
+      ws_tile(a, tile, mtile, ntile);
       const int n = ntile * 128 + row;
       const int m0 = mtile * BT + col0;
       float acc[NW][kCols];
@@ -442,7 +534,7 @@ __global__ void __launch_bounds__(kWsThreads, 1)
 #pragma unroll
         for (int w = 0; w < NW; ++w)
           sc[w] = a.exact ? __ldg(a.s[w] + ((size_t)ntile * a.nkb + (kc * kChunkK) / a.block) * 128 + row) : 1.0f;
-        // lockstep: segment == stage pb (S == NP), retired when empty[pb] completes
+        // lockstep: segment == stage pb (partial pb), retired when empty[pb] completes
         if (!ptx::mbar_wait(a.lockstep ? &empty[pb] : &part_full[pb], pph, abort_flag)) { ok = false; break; }
         ptx::tc_fence_after();
         const uint32_t t_row = tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)pb * kPartCols + col0;
@@ -460,51 +552,21 @@ __global__ void __launch_bounds__(kWsThreads, 1)
         ptx::tc_fence_before();
         __syncwarp();
         if (lane == 0) ptx::mbar_arrive(a.lockstep ? &full[pb] : &part_empty[pb]);
-        if (++pb == kNP) { pb = 0; pph ^= 1; }
+        if (++pb == (a.lockstep ? S : kNP)) { pb = 0; pph ^= 1; }
       }
       if (!ok) break;
 
-      const int SPL = a.ksplit;
-      if (SPL > 1) {
-        // Split-K: publish this split's partial, the last split sums all of
-        // them in split order (deterministic) and runs the epilogue.
-        float* part = a.partials + ((size_t)tile * SPL + split) * NW * 128 * BT;
-#pragma unroll
-        for (int w = 0; w < NW; ++w) {
-          float4* dst = reinterpret_cast<float4*>(part + ((size_t)w * 128 + row) * BT + col0);
-#pragma unroll
-          for (int j = 0; j < kCols / 4; ++j)
-            __stcg(dst + j, make_float4(acc[w][4 * j], acc[w][4 * j + 1], acc[w][4 * j + 2], acc[w][4 * j + 3]));
-        }
-        __threadfence();
-        asm volatile("bar.sync 1, 512;" ::: "memory");
-        if (threadIdx.x == 0) {
-          __threadfence();
-          const int prev = atomicAdd(a.counters + tile, 1);
-          *last_flag = (prev == SPL - 1) ? 1 : 0;
-          if (prev == SPL - 1) a.counters[tile] = 0;
-        }
-        asm volatile("bar.sync 1, 512;" ::: "memory");
-        const bool last = *last_flag != 0;
-        asm volatile("bar.sync 1, 512;" ::: "memory");
-        if (!last) continue;
-        __threadfence();
-        const float* base = a.partials + (size_t)tile * SPL * NW * 128 * BT;
+      if (a.ksplit > 1) {
+        // Split-K: this split's partial tile goes to this CTA's own shared
+        // memory -- the operand ring, idle now that every MMA of the unit
+        // (the CTA's only one) has retired -- as red[w][token][feature];
+        // the cluster sums the splits after the role loops.
+        float* red = reinterpret_cast<float*>(ring);
 #pragma unroll
         for (int w = 0; w < NW; ++w)
 #pragma unroll
-          for (int j = 0; j < kCols; ++j) acc[w][j] = 0.0f;
-        for (int sp = 0; sp < SPL; ++sp) {
-#pragma unroll
-          for (int w = 0; w < NW; ++w) {
-            const float4* src = reinterpret_cast<const float4*>(base + ((size_t)(sp * NW + w) * 128 + row) * BT + col0);
-#pragma unroll
-            for (int j = 0; j < kCols / 4; ++j) {
-              const float4 v = __ldcg(src + j);
-              acc[w][4 * j] += v.x; acc[w][4 * j + 1] += v.y; acc[w][4 * j + 2] += v.z; acc[w][4 * j + 3] += v.w;
-            }
-          }
-        }
+          for (int j = 0; j < kCols; ++j) red[((size_t)w * BT + col0 + j) * 128 + row] = acc[w][j];
+        continue;
       }
       if (n < a.N) {
         const float b0 = a.bias[0] ? __ldg(a.bias[0] + n) : 0.0f;
@@ -527,6 +589,18 @@ __global__ void __launch_bounds__(kWsThreads, 1)
       }
     }
     if (!ok) record_error_flag(abort_flag, BQ4_ETIMEOUT);
+    if (a.ksplit > 1) {
+      // Split reduction.  Every role of every CTA of the cluster passes two
+      // cluster barriers (each role branch has its own pair, so each runs
+      // under its warps' register budget): after the first, every split's
+      // partial tile is in its CTA's shared memory; the second keeps that
+      // memory alive until all peers have read it.
+      __syncwarp();
+      ptx::cluster_sync();
+      split_reduce_epilogue<BT, NW>(a, ring);
+      __syncwarp();
+      ptx::cluster_sync();
+    }
   }
 
   ptx::tc_fence_before();
@@ -575,11 +649,15 @@ cudaError_t prepare_ws_kernel(size_t smem_bytes, bool* ok_regs) {
     checked = (attr.numRegs == kWsRegsLaunch) ? 1 : -1;
   }
   *ok_regs = checked == 1;
-  static size_t smem_set = 0;
-  if (smem_set < smem_bytes) {
+  // the shared-memory opt-in is a per-device function attribute
+  static std::atomic<size_t> smem_set[64];
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) dev = 0;
+  if (smem_set[dev].load(std::memory_order_relaxed) < smem_bytes) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_bytes);
     if (e != cudaSuccess) return e;
-    smem_set = smem_bytes;
+    smem_set[dev].store(smem_bytes, std::memory_order_relaxed);
   }
   return cudaSuccess;
 }
@@ -589,9 +667,94 @@ cudaError_t launch_ws(const GemmPlan& plan, const CUtensorMap& tmap, const WsArg
                       bool* ok_regs) {
   cudaError_t e = prepare_ws_kernel<BT, NW>(plan.smem_bytes, ok_regs);
   if (e != cudaSuccess || !*ok_regs) return e;
-  q4_gemm_ws_kernel<BT, NW><<<plan.grid, kWsThreads, plan.smem_bytes, stream>>>(tmap, args);
+  // Launched as a programmatic dependent of the activation-staging grid
+  // before it (only the token loads wait for that grid, see the kernel), and
+  // with split-K as clusters of the splits of one tile (grid = units).
+  cudaLaunchConfig_t cfg;
+  memset(&cfg, 0, sizeof(cfg));
+  cfg.gridDim = dim3((unsigned)plan.grid, 1, 1);
+  cfg.blockDim = dim3(kWsThreads, 1, 1);
+  cfg.dynamicSmemBytes = plan.smem_bytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  unsigned n = 0;
+  if (plan.pdl) {
+    attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[n].val.programmaticStreamSerializationAllowed = 1;
+    ++n;
+  }
+  if (plan.cluster > 1) {
+    attr[n].id = cudaLaunchAttributeClusterDimension;
+    attr[n].val.clusterDim.x = (unsigned)plan.cluster;
+    attr[n].val.clusterDim.y = 1;
+    attr[n].val.clusterDim.z = 1;
+    ++n;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = n;
+  e = cudaLaunchKernelEx(&cfg, q4_gemm_ws_kernel<BT, NW>, tmap, args);
   note_launch();
-  return cudaGetLastError();
+  return e;
+}
+
+// How many clusters of `cs` CTAs of this kernel can be resident at once on
+// the current device (0 if none).  One CTA fills an SM's shared memory, so
+// this depends only on the cluster size; cached per size (every GPU a
+// process drives here is the same part).
+template <int BT, int NW>
+int cluster_capacity_t(int cs, size_t smem_bytes) {
+  static std::atomic<int> cache[kMaxSplit + 1];
+  if (cs < 2 || cs > kMaxSplit) return 0;
+  int v = cache[cs].load(std::memory_order_relaxed);
+  if (v > 0) return v - 1;
+  bool ok_regs = true;
+  int n = 0;
+  bool known = false;
+  if (prepare_ws_kernel<BT, NW>(smem_bytes, &ok_regs) == cudaSuccess) {
+    cudaLaunchConfig_t cfg;
+    memset(&cfg, 0, sizeof(cfg));
+    cfg.gridDim = dim3((unsigned)cs, 1, 1);
+    cfg.blockDim = dim3(kWsThreads, 1, 1);
+    cfg.dynamicSmemBytes = smem_bytes;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = (unsigned)cs;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (cudaOccupancyMaxActiveClusters(&n, q4_gemm_ws_kernel<BT, NW>, &cfg) == cudaSuccess) {
+      known = true;
+    } else {
+      cudaGetLastError();
+      n = 0;
+    }
+  } else {
+    cudaGetLastError();
+  }
+  if (known) cache[cs].store(n + 1, std::memory_order_relaxed);  // failures are not cached
+  return n;
+}
+
+int cluster_capacity_any(int bt, int nw, int cs, size_t smem_bytes);
+
+int cluster_capacity(int bt, int nw, int cs, size_t smem_bytes, int device) {
+  int prev = -1;
+  cudaGetDevice(&prev);
+  if (prev != device) cudaSetDevice(device);
+  const int n = cluster_capacity_any(bt, nw, cs, smem_bytes);
+  if (prev >= 0 && prev != device) cudaSetDevice(prev);
+  return n;
+}
+
+int cluster_capacity_any(int bt, int nw, int cs, size_t smem_bytes) {
+  if (nw == 1) {
+    if (bt == 256) return cluster_capacity_t<256, 1>(cs, smem_bytes);
+    if (bt == 128) return cluster_capacity_t<128, 1>(cs, smem_bytes);
+    return cluster_capacity_t<64, 1>(cs, smem_bytes);
+  }
+  if (bt == 128) return cluster_capacity_t<128, 2>(cs, smem_bytes);
+  return cluster_capacity_t<64, 2>(cs, smem_bytes);
 }
 
 }  // namespace
@@ -670,39 +833,8 @@ bq4_status plan_gemm(const bq4_weight* w, int nw, int64_t M, int device, GemmPla
   const int nkc = (int)w->nkc;
   const int nks = nkc / 2;  // 128-K stages
 
-  // Split-K factor: minimise an estimated makespan (chunks per split plus a
-  // pipeline fill of ~3 chunks per unit, plus the partial-tile fix-up).
-  // Split-K is only used when all units fit in one wave (units <= SMs);
-  // multi-wave work uses whole-K units (S = 1).
-  int best_s = 1;
-  double best_t = 1e30;
-  const int max_s = nks < 16 ? nks : 16;
-  const bool multiwave_split = getenv("BQ4_ALLOW_MULTIWAVE_SPLIT") != nullptr;
-  for (int s = 1; s <= max_s; ++s) {
-    const int units = tiles * s;
-    if (s > 1 && units > sms && !multiwave_split) break;
-    const int waves = (units + sms - 1) / sms;
-    const double per_unit = (double)nkc / s + 3.0;  // chunks
-    const double fixup = s > 1 ? 1.0 + 0.25 * s : 0.0;
-    const double t = waves * (per_unit + fixup);
-    if (t < best_t - 1e-9) {
-      best_t = t;
-      best_s = s;
-    }
-  }
-  // BQ4_FORCE_KSPLIT=s pins the split-K factor (clamped to [1, chunks] and
-  // to a single wave of units).
-  if (const char* f = getenv("BQ4_FORCE_KSPLIT")) {
-    int v = atoi(f);
-    if (v >= 1) best_s = v < nks ? v : nks;
-    while (best_s > 1 && tiles * best_s > sms && !multiwave_split) --best_s;
-  }
-  p->ksplit = best_s;
-  p->units = tiles * best_s;
-  p->grid = p->units < sms ? p->units : sms;
-
   // Shared memory: operand ring of 128-K stages (A + B) as deep as fits
-  // (2..4 stages) next to a raw ring of 2..4 stages.
+  // (2..4 stages) next to a raw ring of 1..4 stages.
   const uint32_t raw_s_bytes = 512u * (uint32_t)(w->block >= 128 ? 1 : 128 / w->block);
   p->raw_s_bytes = p->exact || p->pre ? 0u : raw_s_bytes;
   p->raw_w_bytes = p->pre ? 16u : 2 * kRawQBytes + p->raw_s_bytes;
@@ -732,19 +864,57 @@ bq4_status plan_gemm(const bq4_weight* w, int nw, int64_t M, int device, GemmPla
   p->stages = S;
   p->a_stages = S;
   p->raw_stages = RS;
-  // Lockstep partial handoff: exact 128-blocks, one segment per stage, as
-  // many stages as TMEM partial buffers (2).
-  p->lockstep = (p->exact && w->block == 128 && S == 2 && 512 / (nw * p->bt) == 2) ? 1 : 0;
+  // Lockstep partial handoff: exact 128-blocks (one segment per stage) and
+  // at most as many stages as TMEM partial buffers, so stage s always
+  // accumulates into partial s.
+  p->lockstep = (p->exact && w->block == 128 && S <= 512 / (nw * p->bt)) ? 1 : 0;
   if (getenv("BQ4_NO_LOCKSTEP")) p->lockstep = 0;
   const int np = 512 / (nw * p->bt);
   p->smem_bytes = 1024 + (size_t)S * stage_bytes + (size_t)RS * raw_stage +
                   (size_t)(2 * S + 2 * RS + 2 * np) * 8 + 16;
 
+  // Split-K factor: minimise an estimated makespan (chunks per split plus a
+  // pipeline fill of ~3 chunks per unit, plus the cluster reduction).  The
+  // splits of a tile form one thread-block cluster (at most 8 CTAs, the
+  // portable limit), and split-K is only used when every cluster is
+  // co-resident (one wave); multi-wave work uses whole-K units.
+  int best_s = 1;
+  double best_t = 1e30;
+  const int max_s = nks < kMaxSplit ? nks : kMaxSplit;
+  for (int s = 1; s <= max_s; ++s) {
+    const int units = tiles * s;
+    if (s > 1 && units > s * cluster_capacity(p->bt, nw, s, p->smem_bytes, device)) continue;
+    const int waves = (units + sms - 1) / sms;
+    const double per_unit = (double)nkc / s + 3.0;  // chunks
+    const double fixup = s > 1 ? 1.0 + 0.25 * s : 0.0;
+    const double t = waves * (per_unit + fixup);
+    if (t < best_t - 1e-9) {
+      best_t = t;
+      best_s = s;
+    }
+  }
+  // BQ4_FORCE_KSPLIT=s pins the split-K factor (clamped to [1, min(stages,
+  // 8)] and to what one wave of clusters holds).
+  if (const char* f = getenv("BQ4_FORCE_KSPLIT")) {
+    int v = atoi(f);
+    if (v >= 1) best_s = v < max_s ? v : max_s;
+    while (best_s > 1 && tiles * best_s > best_s * cluster_capacity(p->bt, nw, best_s, p->smem_bytes, device)) --best_s;
+  }
+  p->ksplit = best_s;
+  p->units = tiles * best_s;
+  p->cluster = best_s;
+  p->grid = best_s > 1 ? p->units : (p->units < sms ? p->units : sms);
+  // Unit order: the wave shares the operand that is larger in HBM -- the
+  // f16 token rows (M*K*2 bytes) or the Q4 weights (nw*N*K/2 bytes).
+  p->nfast = ((int64_t)M * 4 > (int64_t)nw * w->Np) ? 1 : 0;
+  if (const char* f = getenv("BQ4_FORCE_NFAST")) p->nfast = f[0] == '1' ? 1 : 0;
+
+  // Programmatic dependent launch of the GEMM after the activation staging
+  // (BQ4_NO_PDL=1 launches it in plain stream order).
+  p->pdl = getenv("BQ4_NO_PDL") ? 0 : 1;
+
   p->xh_bytes = align_up((size_t)M * (size_t)w->Kp * 2, 256);
-  p->counter_bytes = align_up((size_t)tiles * sizeof(int) + sizeof(int) * 4, 256);
-  p->partial_bytes =
-      best_s > 1 ? align_up((size_t)tiles * best_s * nw * 128 * p->bt * sizeof(float), 256) : 0;
-  p->workspace_bytes = p->xh_bytes + p->counter_bytes + p->partial_bytes;
+  p->workspace_bytes = p->xh_bytes;
   return BQ4_OK;
 }
 
@@ -754,13 +924,9 @@ bq4_status run_gemm(const GemmPlan& plan, const bq4_weight* const* ws, const flo
   const bq4_weight* w0 = ws[0];
   uint8_t* wsp = static_cast<uint8_t*>(workspace);
   void* xh = wsp;
-  int* counters = reinterpret_cast<int*>(wsp + plan.xh_bytes);
-  float* partials =
-      plan.partial_bytes ? reinterpret_cast<float*>(wsp + plan.xh_bytes + plan.counter_bytes) : nullptr;
 
-  // 1) stage activations as f16 (also zeroes the split-K tile counters)
-  cudaError_t e = launch_convert_x(x, M, w0->K, ldx, w0->Kp, xh, counters,
-                                   plan.mtiles * plan.ntiles + 4, stream);
+  // 1) stage activations as f16
+  cudaError_t e = launch_convert_x(x, M, w0->K, ldx, w0->Kp, xh, stream);
   if (e != cudaSuccess) return check_cuda(e, "convert_x launch");
 
   // 2) tensor map over xh [M][Kp] f16, box {64, BT}, 128-byte swizzle
@@ -786,8 +952,6 @@ bq4_status run_gemm(const GemmPlan& plan, const bq4_weight* const* ws, const flo
   }
   args.aux = aux;
   args.y = y;
-  args.partials = partials;
-  args.counters = counters;
   args.M = (int)M;
   args.N = (int)w0->N;
   args.nkc = (int)w0->nkc;
@@ -797,6 +961,8 @@ bq4_status run_gemm(const GemmPlan& plan, const bq4_weight* const* ws, const flo
   args.mtiles = plan.mtiles;
   args.ksplit = plan.ksplit;
   args.units = plan.units;
+  args.nfast = plan.nfast;
+  args.yvec = ((reinterpret_cast<uintptr_t>(y) & 15) == 0 && w0->N % 4 == 0) ? 1 : 0;
   args.stages = plan.stages;
   args.rs = plan.raw_stages;
   args.exact = plan.exact;

@@ -62,9 +62,9 @@ cudaError_t launch_dequant_prepared(const bq4_weight* w, float* out, int32_t out
 cudaError_t launch_dequant_raw(const uint32_t* words, const float* scales, int64_t K, int64_t N,
                                int32_t block, int32_t layout, float* out, int32_t out_layout,
                                cudaStream_t s);
-// x f32 [M][ldx] -> xh f16 [M][Kp] (zero padded); also zeroes `counters`.
+// x f32 [M][ldx] -> xh f16 [M][Kp] (zero padded).
 cudaError_t launch_convert_x(const float* x, int64_t M, int64_t K, int64_t ldx, int64_t Kp,
-                             void* xh, int* counters, int ncounters, cudaStream_t s);
+                             void* xh, cudaStream_t s);
 
 // ------------------------------------------------------------ GEMM (bq4_gemm_sm100.cu)
 struct GemmPlan {
@@ -74,11 +74,14 @@ struct GemmPlan {
   int lockstep;    // 1 = exact mode with stage == segment partial handoff
   int bt;          // tokens per tile (MMA N): 64, 128 or 256
   int mtiles, ntiles, ksplit, units, grid;
+  int cluster;     // CTAs per cluster (= ksplit when the K range is split, else 1)
+  int nfast;       // 1: N tile varies fastest along the unit order
+  int pdl;         // 1: GEMM launched as a programmatic dependent of the staging grid
   int stages, a_stages, raw_stages;  // B ring, A ring, raw ring depths
   uint32_t raw_s_bytes;  // scale bytes per weight per raw stage (folded)
   uint32_t raw_w_bytes;  // shared-memory bytes per weight per raw stage
   size_t smem_bytes;
-  size_t xh_bytes, counter_bytes, partial_bytes;  // workspace pieces
+  size_t xh_bytes;         // the f16 copy of x, the only workspace piece
   size_t workspace_bytes;
 };
 

@@ -158,10 +158,11 @@ __global__ void dequant_raw_kernel(const uint32_t* __restrict__ words, const flo
 // K..Kp-1.  Each thread converts 8 consecutive K values into one 16-byte
 // store.  Block 0 also zeroes the split-K tile counters.
 __global__ void convert_x_kernel(const float* __restrict__ x, int64_t M, int64_t K, int64_t ldx,
-                                 int64_t Kp, uint4* __restrict__ xh, int* __restrict__ counters,
-                                 int ncounters, int vec4) {
-  if (blockIdx.x == 0)
-    for (int i = threadIdx.x; i < ncounters; i += blockDim.x) counters[i] = 0;
+                                 int64_t Kp, uint4* __restrict__ xh, int vec4) {
+  // The GEMM that consumes xh is launched as a programmatic dependent: it may
+  // start its weight-side prologue now and waits for this grid's completion
+  // before it reads xh.
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   const int64_t per_row = Kp / 8;
   const int64_t total = M * per_row;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
@@ -257,11 +258,11 @@ cudaError_t launch_dequant_raw(const uint32_t* words, const float* scales, int64
 }
 
 cudaError_t launch_convert_x(const float* x, int64_t M, int64_t K, int64_t ldx, int64_t Kp,
-                             void* xh, int* counters, int ncounters, cudaStream_t s) {
+                             void* xh, cudaStream_t s) {
   const int vec4 = ((reinterpret_cast<uintptr_t>(x) & 15) == 0) && (ldx % 4 == 0);
   const int64_t total = M * (Kp / 8);
   convert_x_kernel<<<grid_for(total, 256, current_device()), 256, 0, s>>>(
-      x, M, K, ldx, Kp, reinterpret_cast<uint4*>(xh), counters, ncounters, vec4);
+      x, M, K, ldx, Kp, reinterpret_cast<uint4*>(xh), vec4);
   note_launch();
   return cudaGetLastError();
 }

@@ -74,3 +74,18 @@ def test_numerics_modes_both_within_tolerance(M, K, N):
         assert errs[mode] <= 5e-3
     assert errs[L.NUMERICS_EXACT] < errs[L.NUMERICS_FOLDED]
     print(f"numerics M{M}: exact {errs[1]:.3e} folded {errs[2]:.3e} auto {errs[0]:.3e}")
+
+
+@pytest.mark.parametrize("M,K,N", [(4352, 12288, 3072), (1024, 3072, 9216), (300, 1024, 640)])
+def test_unit_order_does_not_change_results(M, K, N, monkeypatch):
+    """N-tile-fastest and M-tile-fastest unit orders only reschedule whole
+    tiles, so the outputs are bit-identical."""
+    words, scales, x = problem(M, K, N, 128)
+    pw = q4.PreparedQ4Weight(words, scales, K, N, 128, L.LAYOUT_ROW, DEV)
+    outs = []
+    for order in ("0", "1"):
+        monkeypatch.setenv("BQ4_FORCE_NFAST", order)
+        outs.append(pw.linear(x))
+        torch.cuda.synchronize()
+        q4.poll_device_error()
+    assert torch.equal(outs[0], outs[1])
