@@ -49,6 +49,8 @@ def parse():
                     help="M,K,N[,act[,block]]: time one fused Q4 linear instead of the stack "
                          "(profiling / per-config rows; act 0 none, 1 gelu-tanh)")
     ap.add_argument("--gated", default=None, help="M,K,N: time one fused SiLU-gate linear pair")
+    ap.add_argument("--no-rows", action="store_true", help="skip the per-config rows")
+    ap.add_argument("--rows-only", action="store_true", help="print only the per-config rows (1 GPU)")
     return ap.parse_args()
 
 
@@ -186,6 +188,97 @@ def run_reference(args):
     }))
 
 
+# ------------------------------------------------------------------ per-config rows
+
+# BASELINE configs as single-GPU rows: (name, M, K, N, kind, act); kind
+# "linear" = one fused linear (+bias), "gated" = silu(x.Wg+bg)*(x.Wu+bu).
+ROWS = [
+    ("c1_cpu_linear_512x2560x9728", 512, 2560, 9728, "linear", 0),
+    ("c2_text_qo_256x2560x2560", 256, 2560, 2560, "linear", 0),
+    ("c2_text_kv_256x2560x512", 256, 2560, 512, "linear", 0),
+    ("c2_text_gate_up_silu_256x2560x2x9728", 256, 2560, 9728, "gated", 0),
+    ("c2_text_down_256x9728x2560", 256, 9728, 2560, "linear", 0),
+    ("c3_dit_up_gelu_4352x3072x12288", 4352, 3072, 12288, "linear", 1),
+    ("c3_dit_down_4352x12288x3072", 4352, 12288, 3072, "linear", 0),
+    ("c4_edit_qkv_18432x3072x9216", 18432, 3072, 9216, "linear", 0),
+    ("c4_edit_o_18432x3072x3072", 18432, 3072, 3072, "linear", 0),
+]
+
+
+def config_rows(dev, peaks, names=None):
+    """Device time of each BASELINE config shape, one GPU.
+
+    Each call reads its own weight/activation/output set; the sets rotate so
+    that together they exceed twice the 126 MB L2 (every call starts cold).
+    The calls are captured in a CUDA graph and replayed, so the time is the
+    device time of the two kernels of a call (activation staging + GEMM),
+    without host submission overhead.  Roofline: t* = max(algorithmic bytes /
+    measured copy bandwidth, FLOPs / measured bf16 burst peak)."""
+    import torch
+
+    from burn_image_b200 import _lib as L
+    from burn_image_b200 import q4, tp
+    hbm = peaks.get("hbm_gbs", 6650.0)
+    tfl = peaks.get("bf16_tflops", 1590.0)
+    out = {}
+    for name, M, K, N, kind, act in ROWS:
+        if names and name not in names:
+            continue
+        nw = 2 if kind == "gated" else 1
+        wbytes = nw * (N * K // 2 + N * K // QBLOCK * 4)
+        set_bytes = wbytes + M * K * 4 + M * N * 4
+        sets = max(2, min(64, int(2 * 126e6 // set_bytes) + 1))
+        g = torch.Generator(device=dev).manual_seed(11)
+        items = []
+        for _ in range(sets):
+            ws = [q4.PreparedQ4Weight(*tp._random_packed(K, N, QBLOCK, g, dev), K, N, QBLOCK, L.LAYOUT_ROW, dev)
+                  for _ in range(nw)]
+            bias = [torch.randn(N, generator=g, device=dev) * 0.02 for _ in range(nw)]
+            x = torch.randn((M, K), generator=g, device=dev)
+            y = torch.empty((M, N), device=dev)
+            items.append((ws, bias, x, y))
+
+        def call(it):
+            ws, bias, x, y = it
+            if nw == 2:
+                q4.linear_gated(ws[0], ws[1], x, bias[0], bias[1], out=y)
+            else:
+                ws[0].linear(x, bias[0], act, out=y)
+
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):
+            for it in items:
+                call(it)  # warm-up on the capture stream (workspace, attributes)
+        torch.cuda.current_stream(dev).wait_stream(side)
+        torch.cuda.synchronize(dev)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=side):
+            for it in items:
+                call(it)
+        graph.replay()
+        torch.cuda.synchronize(dev)
+        reps = max(3, int(40 // sets))
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            graph.replay()
+        e1.record()
+        torch.cuda.synchronize(dev)
+        q4.poll_device_error()
+        t = e0.elapsed_time(e1) * 1e-3 / (reps * sets)
+        flops = 2 * M * K * N * nw
+        nbytes = wbytes + M * K * 4 + M * N * 4 + nw * N * 4
+        t_star = max(nbytes / (hbm * 1e9), flops / (tfl * 1e12))
+        bound = "hbm" if nbytes / (hbm * 1e9) > flops / (tfl * 1e12) else "tensor"
+        out[name] = {"us": t * 1e6, "tflops": flops / t / 1e12, "gbs": nbytes / t / 1e9, "bound": bound,
+                     "t_star_us": t_star * 1e6, "frac": t_star / t, "sets": sets}
+        del graph, items
+        torch.cuda.empty_cache()
+    return out
+
+
 # ------------------------------------------------------------------ GPU arm
 
 def run_ours(args):
@@ -320,6 +413,10 @@ def run_ours(args):
     except Exception:
         pass
 
+    rows = None
+    if rank == 0 and world == 1 and not args.no_rows:
+        rows = config_rows(dev, peaks)
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         try:
@@ -353,6 +450,7 @@ def run_ours(args):
             "gpu_launches": launches,
             "clocks": clk,
             "cpu_baseline": cpu,
+            "rows": rows,
         }
         print(json.dumps(out))
     if world > 1:
@@ -414,6 +512,14 @@ def main():
     args = parse()
     if args.impl == "reference":
         run_reference(args)
+    elif args.rows_only:
+        import torch
+        peaks = {}
+        try:
+            peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
+        except Exception:
+            pass
+        print(json.dumps({"rows": config_rows(torch.device("cuda", 0), peaks)}))
     elif args.linear or args.gated:
         run_linear(args)
     else:

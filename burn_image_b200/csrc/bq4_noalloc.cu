@@ -14,9 +14,9 @@
 // looked up with cudaGetSymbolAddress once per device (with that device
 // current) on the first call there, and cached.  Calls on one device share
 // the array: two calls that overlap on the GPU (different streams, or
-// different host threads without ordering) race on it.  Nothing in it needs
-// to start at zero except the split-K tile counters, which the activation
-// staging kernel of every call clears before the GEMM reads them.
+// different host threads without ordering) race on it.  It holds only the
+// f16 copy of the activations, which every call writes in full before the
+// GEMM reads it, so nothing in it needs to start at zero.
 #include <cuda_runtime.h>
 
 #include <mutex>
