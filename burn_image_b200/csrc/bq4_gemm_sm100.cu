@@ -274,19 +274,28 @@ __device__ __forceinline__ void split_reduce_epilogue(const WsArgs& a, const uin
   }
 }
 
-template <int BT, int NW>
+// TA = true: the dequantized weight tile (MMA operand A) is written to TMEM
+// by the dequant warps (tcgen05.st) and read from there by the MMA, instead
+// of going through shared memory.  Shared memory then holds only token
+// tiles, so the ring is deeper (3 stages of BT=256 instead of 2) and more
+// token bytes are in flight; TMEM holds one accumulator (columns
+// [0, NW*BT)) and one 64-column A slot per stage after it.  Folded numerics,
+// one weight.
+template <int BT, int NW, bool TA>
 __global__ void __launch_bounds__(kWsThreads, 1)
     q4_gemm_ws_kernel(const __grid_constant__ CUtensorMap tmap_x, const WsArgs a) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   constexpr uint32_t kBSub = BT * 128;              // one 64-K token sub-tile
-  constexpr uint32_t kAStage = NW * 2 * kATileBytes;
+  constexpr uint32_t kAStage = TA ? 0u : NW * 2 * kATileBytes;
   constexpr uint32_t kStage = kAStage + 2 * kBSub;
   constexpr uint32_t kPartCols = NW * BT;
-  constexpr int kNP = 512 / kPartCols;   // partial buffers in TMEM
+  constexpr int kNP = TA ? 1 : 512 / kPartCols;   // partial buffers in TMEM
+  constexpr uint32_t kACol0 = kNP * kPartCols;    // TA: first A-slot column
   constexpr int kCols = BT / 4;          // token columns per scaler thread
-  static_assert(kNP >= 2, "at least double buffering");
+  static_assert(TA || kNP >= 2, "at least double buffering");
+  static_assert(!TA || (NW == 1 && kACol0 + 64 <= 512), "TMEM operand A: one weight, room for a slot");
   static_assert(kCols % 16 == 0, "scaler column split");
 
   const int S = a.stages, RS = a.rs;
@@ -417,11 +426,16 @@ __global__ void __launch_bounds__(kWsThreads, 1)
 #pragma unroll
             for (int kk = 0; kk < kChunkK / 16; ++kk) {
               const uint64_t b_desc = ptx::umma_desc_sw128(b_addr + kk * 32);
-#pragma unroll
-              for (int w = 0; w < NW; ++w)
-                ptx::mma_f16_ss(d_base + w * BT,
-                                ptx::umma_desc_sw128(st + (uint32_t)((w * 2 + sub) * kATileBytes) + kk * 32), b_desc,
+              if constexpr (TA) {
+                ptx::mma_f16_ts(d_base, tmem_base + kACol0 + (uint32_t)s * 64 + (uint32_t)sub * 32 + kk * 8, b_desc,
                                 idesc, (first && kk == 0) ? 0u : 1u);
+              } else {
+#pragma unroll
+                for (int w = 0; w < NW; ++w)
+                  ptx::mma_f16_ss(d_base + w * BT,
+                                  ptx::umma_desc_sw128(st + (uint32_t)((w * 2 + sub) * kATileBytes) + kk * 32),
+                                  b_desc, idesc, (first && kk == 0) ? 0u : 1u);
+              }
             }
             if (sub == 1) ptx::mma_commit(&empty[s]);  // stage free once its MMAs retire
             if (!a.lockstep && ws_seg_last(c, kc1, cpb)) {
@@ -480,17 +494,38 @@ __global__ void __launch_bounds__(kWsThreads, 1)
           if (lane == 0) ptx::mbar_arrive(&raw_empty[rs]);
           if (++rs == RS) { rs = 0; rph ^= 1; }
           if (!ptx::mbar_wait(&empty[s], ph ^ 1, abort_flag)) { ok = false; break; }
+          if constexpr (TA) {
+            // row r = TMEM lane r (this warp's lane quarter is r / 32), the
+            // sub-tile's 64 K values = 32 columns of A slot s
+            ptx::tc_fence_after();
+            const uint32_t wv[8] = {wlo[0].x, wlo[0].y, wlo[0].z, wlo[0].w, whi[0].x, whi[0].y, whi[0].z, whi[0].w};
+            const uint32_t t_a = tmem_base + ((uint32_t)((warp & 3) * 32) << 16) + kACol0 + (uint32_t)s * 64 +
+                                 (uint32_t)sub * 32;
 #pragma unroll
-          for (int w = 0; w < NW; ++w) {
-            uint8_t* dst = ring + (size_t)s * kStage + (size_t)(w * 2 + sub) * kATileBytes + (size_t)r * 128;
-            const uint32_t wv[8] = {wlo[w].x, wlo[w].y, wlo[w].z, wlo[w].w, whi[w].x, whi[w].y, whi[w].z, whi[w].w};
+            for (int h = 0; h < 2; ++h) {
+              uint32_t v[16];
 #pragma unroll
-            for (int j = 0; j < 8; ++j) {
-              const uint4 v = a.exact ? expand_word_exact(wv[j]) : expand_word(wv[j], sc[w][j]);
-              *reinterpret_cast<uint4*>(dst + ((j ^ sw) << 4)) = v;
+              for (int j = 0; j < 4; ++j) {
+                const uint4 e = expand_word(wv[h * 4 + j], sc[0][h * 4 + j]);
+                v[4 * j] = e.x; v[4 * j + 1] = e.y; v[4 * j + 2] = e.z; v[4 * j + 3] = e.w;
+              }
+              ptx::tmem_st_32x32b_x16(t_a + (uint32_t)h * 16, v);
             }
+            ptx::tmem_st_wait();
+            ptx::tc_fence_before();
+          } else {
+#pragma unroll
+            for (int w = 0; w < NW; ++w) {
+              uint8_t* dst = ring + (size_t)s * kStage + (size_t)(w * 2 + sub) * kATileBytes + (size_t)r * 128;
+              const uint32_t wv[8] = {wlo[w].x, wlo[w].y, wlo[w].z, wlo[w].w, whi[w].x, whi[w].y, whi[w].z, whi[w].w};
+#pragma unroll
+              for (int j = 0; j < 8; ++j) {
+                const uint4 v = a.exact ? expand_word_exact(wv[j]) : expand_word(wv[j], sc[w][j]);
+                *reinterpret_cast<uint4*>(dst + ((j ^ sw) << 4)) = v;
+              }
+            }
+            ptx::fence_proxy_async_smem();
           }
-          ptx::fence_proxy_async_smem();
           __syncwarp();
           if (lane == 0) ptx::mbar_arrive(&full[s]);
           if (++s == S) { s = 0; ph ^= 1; }
@@ -638,9 +673,9 @@ size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 // pool the block was launched with when ptxas gave every thread exactly
 // kWsRegsLaunch registers.  Checked once per instantiation before any launch
 // (a mismatch would make setmaxnreg.inc wait forever).
-template <int BT, int NW>
+template <int BT, int NW, bool TA>
 cudaError_t prepare_ws_kernel(size_t smem_bytes, bool* ok_regs) {
-  auto kern = q4_gemm_ws_kernel<BT, NW>;
+  auto kern = q4_gemm_ws_kernel<BT, NW, TA>;
   static int checked = 0;  // 0 unknown, 1 ok, -1 bad
   if (checked == 0) {
     cudaFuncAttributes attr;
@@ -662,10 +697,10 @@ cudaError_t prepare_ws_kernel(size_t smem_bytes, bool* ok_regs) {
   return cudaSuccess;
 }
 
-template <int BT, int NW>
+template <int BT, int NW, bool TA = false>
 cudaError_t launch_ws(const GemmPlan& plan, const CUtensorMap& tmap, const WsArgs& args, cudaStream_t stream,
                       bool* ok_regs) {
-  cudaError_t e = prepare_ws_kernel<BT, NW>(plan.smem_bytes, ok_regs);
+  cudaError_t e = prepare_ws_kernel<BT, NW, TA>(plan.smem_bytes, ok_regs);
   if (e != cudaSuccess || !*ok_regs) return e;
   // Launched as a programmatic dependent of the activation-staging grid
   // before it (only the token loads wait for that grid, see the kernel), and
@@ -692,7 +727,7 @@ cudaError_t launch_ws(const GemmPlan& plan, const CUtensorMap& tmap, const WsArg
   }
   cfg.attrs = attr;
   cfg.numAttrs = n;
-  e = cudaLaunchKernelEx(&cfg, q4_gemm_ws_kernel<BT, NW>, tmap, args);
+  e = cudaLaunchKernelEx(&cfg, q4_gemm_ws_kernel<BT, NW, TA>, tmap, args);
   note_launch();
   return e;
 }
@@ -710,7 +745,7 @@ int cluster_capacity_t(int cs, size_t smem_bytes) {
   bool ok_regs = true;
   int n = 0;
   bool known = false;
-  if (prepare_ws_kernel<BT, NW>(smem_bytes, &ok_regs) == cudaSuccess) {
+  if (prepare_ws_kernel<BT, NW, false>(smem_bytes, &ok_regs) == cudaSuccess) {
     cudaLaunchConfig_t cfg;
     memset(&cfg, 0, sizeof(cfg));
     cfg.gridDim = dim3((unsigned)cs, 1, 1);
@@ -723,7 +758,7 @@ int cluster_capacity_t(int cs, size_t smem_bytes) {
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    if (cudaOccupancyMaxActiveClusters(&n, q4_gemm_ws_kernel<BT, NW>, &cfg) == cudaSuccess) {
+    if (cudaOccupancyMaxActiveClusters(&n, q4_gemm_ws_kernel<BT, NW, false>, &cfg) == cudaSuccess) {
       known = true;
     } else {
       cudaGetLastError();
@@ -838,11 +873,15 @@ bq4_status plan_gemm(const bq4_weight* w, int nw, int64_t M, int device, GemmPla
   const uint32_t raw_s_bytes = 512u * (uint32_t)(w->block >= 128 ? 1 : 128 / w->block);
   p->raw_s_bytes = p->exact || p->pre ? 0u : raw_s_bytes;
   p->raw_w_bytes = p->pre ? 16u : 2 * kRawQBytes + p->raw_s_bytes;
-  const size_t stage_bytes = (size_t)nw * 2 * kATileBytes + 2 * (size_t)p->bt * 128;
+  // Operand A in TMEM (folded numerics, one weight, 256-token tiles): shared
+  // memory then holds only token tiles.  BQ4_NO_TA=1 keeps A in shared memory.
+  p->ta = (!p->exact && !p->pre && nw == 1 && p->bt == 256 && !getenv("BQ4_NO_TA")) ? 1 : 0;
+  const size_t stage_bytes = (p->ta ? 0 : (size_t)nw * 2 * kATileBytes) + 2 * (size_t)p->bt * 128;
+  const int max_stages = p->ta ? (512 - 256) / 64 : 4;  // TA: one 64-column TMEM A slot per stage
   const size_t raw_stage = (size_t)nw * p->raw_w_bytes;
   const size_t budget = 227 * 1024 - 1024 /*align*/ - 512 /*barriers*/;
   int S = 0, RS = 0;
-  for (int s = 4; s >= 2 && !S; --s) {
+  for (int s = max_stages; s >= 2 && !S; --s) {
     if ((size_t)s * stage_bytes + raw_stage > budget) continue;
     int rs = (int)((budget - (size_t)s * stage_bytes) / raw_stage);
     if (rs > 4) rs = 4;
@@ -854,7 +893,7 @@ bq4_status plan_gemm(const bq4_weight* w, int nw, int64_t M, int device, GemmPla
   // does not fit the shared-memory budget.
   if (const char* f = getenv("BQ4_FORCE_RINGS")) {
     int fs = 0, fr = 0;
-    if (sscanf(f, "%d,%d", &fs, &fr) == 2 && fs >= 2 && fr >= 1 &&
+    if (sscanf(f, "%d,%d", &fs, &fr) == 2 && fs >= 2 && fs <= max_stages && fr >= 1 &&
         (size_t)fs * stage_bytes + (size_t)fr * raw_stage <= budget) {
       S = fs;
       RS = p->pre ? 1 : fr;
@@ -974,7 +1013,8 @@ bq4_status run_gemm(const GemmPlan& plan, const bq4_weight* const* ws, const flo
 
   bool ok_regs = true;
   if (plan.nw == 1) {
-    if (plan.bt == 256) e = launch_ws<256, 1>(plan, tmap, args, stream, &ok_regs);
+    if (plan.ta) e = launch_ws<256, 1, true>(plan, tmap, args, stream, &ok_regs);
+    else if (plan.bt == 256) e = launch_ws<256, 1>(plan, tmap, args, stream, &ok_regs);
     else if (plan.bt == 128) e = launch_ws<128, 1>(plan, tmap, args, stream, &ok_regs);
     else e = launch_ws<64, 1>(plan, tmap, args, stream, &ok_regs);
   } else {

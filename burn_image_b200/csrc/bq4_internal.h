@@ -77,6 +77,7 @@ struct GemmPlan {
   int cluster;     // CTAs per cluster (= ksplit when the K range is split, else 1)
   int nfast;       // 1: N tile varies fastest along the unit order
   int pdl;         // 1: GEMM launched as a programmatic dependent of the staging grid
+  int ta;          // 1: operand A (dequantized weights) staged in TMEM, not shared memory
   int stages, a_stages, raw_stages;  // B ring, A ring, raw ring depths
   uint32_t raw_s_bytes;  // scale bytes per weight per raw stage (folded)
   uint32_t raw_w_bytes;  // shared-memory bytes per weight per raw stage
