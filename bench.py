@@ -127,13 +127,25 @@ class ClockSampler:
 
 # ------------------------------------------------------------------ CPU baseline (oracle)
 
+def host_cores() -> int:
+    """Host threads this process may run on (torchrun sets OMP_NUM_THREADS=1,
+    so the CPU arms pass this count explicitly)."""
+    try:
+        return len(os.sched_getaffinity(0))
+    except Exception:
+        return os.cpu_count() or 1
+
+
 def cpu_sample(tokens_sample: int, repeats: int, threads: int = 0):
     """Time the CPU restatement of the reference q_matmul (dequantize + f32
     SGEMM + epilogue, OpenMP) on one block's four linears at `tokens_sample`
-    rows.  Returns (TFLOP/s, seconds, threads)."""
+    rows, on `threads` host threads (all usable cores when 0).  Returns
+    (TFLOP/s, seconds, threads)."""
     import numpy as np
 
     import oracle as O
+    if threads <= 0:
+        threads = host_cores()
     rng = np.random.default_rng(0)
     shapes = [(HIDDEN, QKV, 0, False), (HIDDEN, HIDDEN, 0, True), (HIDDEN, MLP, O.ACT_GELU_TANH, True),
               (MLP, HIDDEN, 0, True)]
@@ -154,7 +166,7 @@ def cpu_sample(tokens_sample: int, repeats: int, threads: int = 0):
             h = O.cpu_linear(words, scales, K, N, QBLOCK, O.LAYOUT_ROW, inp, bias, act, threads=threads)
             flops += 2 * tokens_sample * K * N
     dt = time.perf_counter() - t0
-    return flops / dt / 1e12, dt, O.cpu_threads() if threads <= 0 else threads
+    return flops / dt / 1e12, dt, threads
 
 
 def run_reference(args):

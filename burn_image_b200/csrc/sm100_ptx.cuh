@@ -1,6 +1,7 @@
 // sm100_ptx.cuh -- thin inline-PTX wrappers for the Blackwell (sm_100a)
-// features the Q4 GEMM uses: mbarriers, TMA (tensor + 1-D bulk, never with
-// cluster multicast), and the tcgen05 tensor-core / TMEM instructions.
+// features the Q4 GEMM uses: mbarriers, TMA (tensor + 1-D bulk, each copy
+// landing only in the issuing CTA's shared memory), and the tcgen05
+// tensor-core / TMEM instructions.
 //
 // Every wait is bounded: a wait that exceeds `kWaitTimeoutNs` of
 // %globaltimer returns false, the caller records an error status and the
@@ -142,7 +143,7 @@ __device__ __forceinline__ void prefetch_tmap(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
 
-// 2-D tiled load, global -> shared, completion counted on `bar` (no multicast).
+// 2-D tiled load, global -> this CTA's shared memory, completion counted on `bar`.
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar,
                                             int32_t x, int32_t y) {
   asm volatile(
