@@ -50,6 +50,12 @@ def parse():
                          "(profiling / per-config rows; act 0 none, 1 gelu-tanh)")
     ap.add_argument("--gated", default=None, help="M,K,N: time one fused SiLU-gate linear pair")
     ap.add_argument("--no-rows", action="store_true", help="skip the per-config rows")
+    ap.add_argument("--act-dtype", choices=["f16", "f32"], default="f16",
+                    help="activations between the stack's linears: f16 (the GEMM operand format, written by "
+                         "each epilogue) or f32 (staged by every call)")
+    ap.add_argument("--chunks", type=int, default=1, help="token chunks of the stack pipeline (each chunk's "
+                                                          "all-reduces overlap the other chunks' GEMMs)")
+    ap.add_argument("--sm-budget", type=int, default=0, help="cap the SMs a GEMM occupies (0: all)")
     ap.add_argument("--rows-only", action="store_true", help="print only the per-config rows (1 GPU)")
     return ap.parse_args()
 
@@ -309,7 +315,14 @@ def run_ours(args):
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
     lib = L.lib()
 
-    stack = tp.DiTQ4Stack(args.blocks, HIDDEN, QKV, MLP, dev, seed=1, block=QBLOCK, group=group)
+    import torch as _t
+    act_dtype = _t.float16 if args.act_dtype == "f16" else _t.float32
+    chunks = max(1, args.chunks)
+    if args.sm_budget > 0:
+        from burn_image_b200 import q4 as _q
+        _q.set_sm_budget(args.sm_budget)
+    stack = tp.DiTQ4Stack(args.blocks, HIDDEN, QKV, MLP, dev, seed=1, block=QBLOCK, group=group,
+                          act_dtype=act_dtype, chunks=chunks)
     M = args.tokens
     g = torch.Generator(device=dev).manual_seed(42)
     x0 = torch.randn((M, HIDDEN), generator=g, device=dev)
@@ -389,6 +402,29 @@ def run_ours(args):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     value_exact = flops_step / (t.item() / args.steps * 1e-3) / 1e12
 
+    # ---- token-parallel alternative (N > 1): every rank runs the unsharded
+    # stack on its M/N tokens, no collective; same metric, max over ranks
+    value_tokens = None
+    if world > 1:
+        local = tp.DiTQ4Stack(args.blocks, HIDDEN, QKV, MLP, dev, seed=1, block=QBLOCK, group=tp.LOCAL,
+                              act_dtype=act_dtype, chunks=1)
+        a0, a1 = M * rank // world, M * (rank + 1) // world
+        xl = x0[a0:a1]
+        for _ in range(args.warmup):
+            local.forward(xl)
+        barrier()
+        l_start = torch.cuda.Event(enable_timing=True)
+        l_end = torch.cuda.Event(enable_timing=True)
+        l_start.record(stream)
+        for _ in range(args.steps):
+            local.forward(xl)
+        l_end.record(stream)
+        barrier()
+        t = torch.tensor([l_start.elapsed_time(l_end)], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        value_tokens = flops_step / (t.item() / args.steps * 1e-3) / 1e12
+        del local
+
     # ---- e2e: through the public API with host buffers
     x_host = x0.cpu().pin_memory()
     y_host = torch.empty((M, HIDDEN), dtype=torch.float32).pin_memory()
@@ -448,6 +484,9 @@ def run_ours(args):
             "vs_baseline": None, "dtype": "f16 operands, f32 accumulate (Q4 weights)", "data": "synthetic",
             "config": {"workload": WORKLOAD, "tokens": M, "blocks": args.blocks, "block": QBLOCK,
                        "parallelism": f"tp{world}" if world > 1 else "single",
+                       "activations": ("f16 between linears (written by each epilogue, read in place)"
+                                       if args.act_dtype == "f16" else "f32 between linears"),
+                       "token_chunks": chunks, "sm_budget": args.sm_budget or None,
                        "l2": "inputs larger than L2 (1.44 GB of Q4 weights streamed per step)"},
             "roofline": {"bound": "tensor", "achieved": achieved_tflops, "peak": peak, "unit": "TFLOP/s",
                          "frac": achieved_tflops / peak, "traffic": traffic,
@@ -463,6 +502,10 @@ def run_ours(args):
             "clocks": clk,
             "cpu_baseline": cpu,
             "rows": rows,
+            "value_token_parallel": value_tokens,
+            "token_parallel": None if value_tokens is None else (
+                "the alternative to tensor parallelism: each GPU runs the unsharded stack on M/N tokens, no "
+                "collective; same metric and FLOPs, max over ranks"),
         }
         print(json.dumps(out))
     if world > 1:

@@ -23,6 +23,7 @@ LAYOUT_COL, LAYOUT_ROW, LAYOUT_NPACKED = 0, 1, 2
 ACT_NONE, ACT_GELU_TANH, ACT_SILU = 0, 1, 2
 NOALLOC_SCRATCH_BYTES = 32 << 20  # BQ4_NOALLOC_SCRATCH_BYTES
 NUMERICS_AUTO, NUMERICS_EXACT, NUMERICS_FOLDED = 0, 1, 2
+DTYPE_F32, DTYPE_F16 = 0, 1
 
 # Every symbol include/bq4.h declares, with (restype, argtypes).
 _p, _i32, _i64, _sz, _u64 = ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64, ctypes.c_size_t, ctypes.c_uint64
@@ -38,6 +39,8 @@ SIGNATURES = {
     "bq4_linear_workspace_size": (_st, [_p, _i64, ctypes.POINTER(_sz)]),
     "bq4_linear": (_st, [_p, _p, _i64, _i64, _p, _i32, _p, _p, _p, _sz, _p]),
     "bq4_linear_noalloc": (_st, [_p, _p, _i64, _i64, _p, _i32, _p, _p, _p]),
+    "bq4_linear_ex_workspace_size": (_st, [_p, _i64, _i32, ctypes.POINTER(_sz)]),
+    "bq4_linear_ex": (_st, [_p, _p, _i32, _i64, _i64, _p, _i32, _p, _p, _i32, _i64, _p, _sz, _p]),
     "bq4_linear_gated_workspace_size": (_st, [_p, _p, _i64, ctypes.POINTER(_sz)]),
     "bq4_linear_gated": (_st, [_p, _p, _p, _i64, _i64, _p, _p, _p, _p, _sz, _p]),
     "bq4_dequant": (_st, [_p, _p, _i32, _p]),
@@ -49,6 +52,8 @@ SIGNATURES = {
     "bq4_row_block_for": (_i32, [_i64]),
     "bq4_poll_device_error": (_st, []),
     "bq4_set_numerics": (_st, [_i32]),
+    "bq4_set_sm_budget": (_st, [_i32]),
+    "bq4_rms_renorm": (_st, [_p, _i32, _i64, _i64, _i64, _p, _i32, _i64, ctypes.c_float, _p]),
     "bq4_launch_count": (_u64, []),
     "bq4_launch_count_reset": (None, []),
 }

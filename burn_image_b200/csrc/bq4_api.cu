@@ -313,6 +313,83 @@ bq4_status bq4_linear(const bq4_weight* w, const float* x, int64_t M, int64_t ld
                   reinterpret_cast<cudaStream_t>(stream));
 }
 
+bq4_status bq4_set_sm_budget(int32_t sms) {
+  if (sms < 0) return set_error(BQ4_EINVAL_ARG, "sm budget %d is negative", (int)sms);
+  set_sm_budget(sms);
+  return BQ4_OK;
+}
+
+bq4_status bq4_rms_renorm(const void* x, bq4_dtype x_dtype, int64_t M, int64_t H, int64_t ldx, void* out,
+                          bq4_dtype out_dtype, int64_t ldo, float eps, bq4_stream_t stream) {
+  if ((x_dtype != BQ4_DTYPE_F32 && x_dtype != BQ4_DTYPE_F16) ||
+      (out_dtype != BQ4_DTYPE_F32 && out_dtype != BQ4_DTYPE_F16))
+    return set_error(BQ4_EINVAL_ARG, "dtype unknown");
+  if (!x || !out) return set_error(BQ4_EINVAL_ARG, "x/out is NULL");
+  if (M <= 0 || H <= 0 || M > 0x7fffffff || ldx < H || ldo < H)
+    return set_error(BQ4_EINVAL_SHAPE, "M=%lld H=%lld ldx=%lld ldo=%lld", (long long)M, (long long)H,
+                     (long long)ldx, (long long)ldo);
+  if (!(eps > 0.0f)) return set_error(BQ4_EINVAL_ARG, "eps must be positive");
+  const size_t ax = x_dtype == BQ4_DTYPE_F16 ? 2 : 4, ao = out_dtype == BQ4_DTYPE_F16 ? 2 : 4;
+  if (!aligned(x, ax) || !aligned(out, ao)) return set_error(BQ4_EALIGN, "x/out misaligned");
+  cudaError_t e = launch_rms_renorm(x, x_dtype == BQ4_DTYPE_F16, M, H, ldx, out, out_dtype == BQ4_DTYPE_F16, ldo,
+                                    eps, reinterpret_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? BQ4_OK : check_cuda(e, "rms_renorm launch");
+}
+
+bq4_status bq4_linear_ex_workspace_size(const bq4_weight* w, int64_t M, bq4_dtype x_dtype, size_t* bytes) {
+  if (x_dtype != BQ4_DTYPE_F32 && x_dtype != BQ4_DTYPE_F16)
+    return set_error(BQ4_EINVAL_ARG, "x_dtype %d unknown", (int)x_dtype);
+  bq4_status st = bq4_linear_workspace_size(w, M, bytes);
+  if (st == BQ4_OK && x_dtype == BQ4_DTYPE_F16) *bytes = 0;
+  return st;
+}
+
+bq4_status bq4_linear_ex(const bq4_weight* w, const void* x, bq4_dtype x_dtype, int64_t M, int64_t ldx,
+                         const float* bias, bq4_act act, const float* aux, void* y, bq4_dtype y_dtype,
+                         int64_t ldy, void* workspace, size_t workspace_bytes, bq4_stream_t stream) {
+  bq4_status st = check_weight(w, "w");
+  if (st) return st;
+  if (act != BQ4_ACT_NONE && act != BQ4_ACT_GELU_TANH && act != BQ4_ACT_SILU)
+    return set_error(BQ4_EINVAL_ARG, "act %d unknown", (int)act);
+  if ((x_dtype != BQ4_DTYPE_F32 && x_dtype != BQ4_DTYPE_F16) ||
+      (y_dtype != BQ4_DTYPE_F32 && y_dtype != BQ4_DTYPE_F16))
+    return set_error(BQ4_EINVAL_ARG, "x_dtype %d / y_dtype %d unknown", (int)x_dtype, (int)y_dtype);
+  if (!x || !y) return set_error(BQ4_EINVAL_ARG, "x/y is NULL");
+  if (M <= 0) return set_error(BQ4_EINVAL_SHAPE, "M=%lld must be positive", (long long)M);
+  if (ldx < w->K) return set_error(BQ4_EINVAL_SHAPE, "ldx=%lld < K=%lld", (long long)ldx, (long long)w->K);
+  if (ldy == 0) ldy = w->N;
+  if (ldy < w->N) return set_error(BQ4_EINVAL_SHAPE, "ldy=%lld < N=%lld", (long long)ldy, (long long)w->N);
+  const int x16 = x_dtype == BQ4_DTYPE_F16, y16 = y_dtype == BQ4_DTYPE_F16;
+  if (x16) {
+    if (w->K != w->Kp)
+      return set_error(BQ4_EINVAL_SHAPE, "f16 x needs K %% 128 == 0 (K=%lld)", (long long)w->K);
+    if (!aligned(x, 16) || ldx % 8)
+      return set_error(BQ4_EALIGN, "f16 x needs a 16-byte aligned base and ldx %% 8 == 0");
+  } else if (!aligned(x, 4)) {
+    return set_error(BQ4_EALIGN, "x not 4-byte aligned");
+  }
+  if (!aligned(y, y16 ? 2 : 4)) return set_error(BQ4_EALIGN, "y misaligned");
+  GemmPlan plan;
+  st = plan_gemm(w, 1, M, w->device, &plan);
+  if (st) return st;
+  const size_t need = x16 ? 0 : plan.workspace_bytes;
+  if (need) {
+    if (!workspace) return set_error(BQ4_EWORKSPACE, "workspace is NULL");
+    if (!aligned(workspace, 256)) return set_error(BQ4_EALIGN, "workspace not 256-byte aligned");
+    if (workspace_bytes < need)
+      return set_error(BQ4_EWORKSPACE, "workspace %zu < required %zu bytes", workspace_bytes, need);
+  }
+  DeviceGuard guard(w->device);
+  const bq4_weight* ws[1] = {w};
+  const float* b[1] = {bias};
+  GemmIo io;
+  io.x_f16 = x16;
+  io.y_f16 = y16;
+  io.ldy = ldy;
+  return run_gemm(plan, ws, x, M, ldx, b, (int)act, aux, y, workspace, reinterpret_cast<cudaStream_t>(stream),
+                  io);
+}
+
 bq4_status bq4_linear_gated_workspace_size(const bq4_weight* gate, const bq4_weight* up, int64_t M,
                                            size_t* bytes) {
   bq4_status st = check_weight(gate, "gate");

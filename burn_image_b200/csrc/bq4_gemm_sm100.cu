@@ -160,7 +160,8 @@ struct WsArgs {
   const uint16_t* h[2];
   const float* bias[2];
   const float* aux;
-  float* y;
+  void* y;                 // f32 or f16 (y_f16), row pitch ldy elements
+  int y_f16, ldy;
   int M, N;
   int nkc, nkb, block;
   int ntiles, mtiles, ksplit, units;
@@ -172,6 +173,13 @@ struct WsArgs {
   uint32_t raw_s_bytes;    // folded: scale bytes per weight per raw stage
   uint32_t raw_w_bytes;    // raw stage bytes per weight
 };
+
+__device__ __forceinline__ void store_y(const WsArgs& a, int m, int n, float v) {
+  if (a.y_f16)
+    reinterpret_cast<__half*>(a.y)[(size_t)m * a.ldy + n] = __float2half_rn(v);
+  else
+    reinterpret_cast<float*>(a.y)[(size_t)m * a.ldy + n] = v;
+}
 
 // Unit u -> (tile, split) and its chunk range [kc0, kc1); splits cut at
 // stage (2-chunk) boundaries.  With ksplit > 1 the grid has one CTA per unit
@@ -208,68 +216,87 @@ __device__ __forceinline__ bool ws_seg_last(int kc, int kc1, int cpb) {
 
 // Split-K reduction across the cluster (one CTA per split, cluster rank =
 // split).  Every CTA holds its split's partial tile red[NW][BT][128] f32 in
-// shared memory; CTA `rank` sums a 1/ksplit slice of the tile over all
-// splits in rank order (deterministic), through distributed shared memory,
-// and runs the epilogue on it.  Called by the 512 scaler threads between two
-// cluster barriers.
+// shared memory; CTA `rank` owns the token columns [c0, c1) of the tile,
+// sums them over all splits in rank order (deterministic) through
+// distributed shared memory, and runs the epilogue on them.  Called by the
+// 512 scaler threads between two cluster barriers: warp w takes every 16th
+// column from c0 + w, lane l the four features 4l..4l+3 (its bias is loaded
+// once); two columns' peer loads are in flight at a time (one with NW = 2).
 template <int BT, int NW>
 __device__ __forceinline__ void split_reduce_epilogue(const WsArgs& a, const uint8_t* red_smem) {
   const int SPL = a.ksplit;
-  const uint32_t rank = ptx::cluster_ctarank();
+  const int rank = (int)ptx::cluster_ctarank();
   int mtile, ntile;
   ws_tile(a, (int)blockIdx.x / SPL, mtile, ntile);
-  constexpr int kGroups = BT * 32;            // 4-feature groups of one weight's partial tile
-  constexpr int kBatch = NW == 1 ? 8 : 4;     // peer loads in flight per thread
-  const int g0 = (int)((int64_t)kGroups * rank / SPL);
-  const int g1 = (int)((int64_t)kGroups * (rank + 1) / SPL);
-  const uint32_t red = ptx::smem_u32(red_smem);
-  const int act = a.act;
-  for (int g = g0 + (int)threadIdx.x; g < g1; g += kWsScalerWarps * 32) {
-    const int col = g >> 5;
-    const int r4 = (g & 31) << 2;
-    const int m = mtile * BT + col;
-    const int n = ntile * 128 + r4;
-    if (m >= a.M || n >= a.N) continue;
-    float v[NW][4];
+  const int c0 = BT * rank / SPL, c1 = BT * (rank + 1) / SPL;
+  const int r4 = (int)(threadIdx.x & 31) * 4;
+  const int n = ntile * 128 + r4;
+  if (n >= a.N) return;
+  constexpr int kColsPer = NW == 1 ? 2 : 1;
+  float b[NW][4];
 #pragma unroll
-    for (int w = 0; w < NW; ++w) v[w][0] = v[w][1] = v[w][2] = v[w][3] = 0.0f;
-    for (int p0 = 0; p0 < SPL; p0 += kBatch) {
-      float4 t[kBatch][NW];
-#pragma unroll
-      for (int i = 0; i < kBatch; ++i)
-        if (p0 + i < SPL)
-#pragma unroll
-          for (int w = 0; w < NW; ++w)
-            t[i][w] = ptx::ld_shared_cluster_f4(
-                ptx::mapa_shared(red + (uint32_t)(((w * BT + col) * 128 + r4) * 4), (uint32_t)(p0 + i)));
-#pragma unroll
-      for (int i = 0; i < kBatch; ++i)
-        if (p0 + i < SPL)
-#pragma unroll
-          for (int w = 0; w < NW; ++w) {
-            v[w][0] += t[i][w].x; v[w][1] += t[i][w].y; v[w][2] += t[i][w].z; v[w][3] += t[i][w].w;
-          }
-    }
-    float o[4];
+  for (int w = 0; w < NW; ++w)
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
       const int nn = n + i < a.N ? n + i : a.N - 1;
-      const float b0 = a.bias[0] ? __ldg(a.bias[0] + nn) : 0.0f;
-      if (NW == 2) {
-        const float b1 = a.bias[1] ? __ldg(a.bias[1] + nn) : 0.0f;
-        o[i] = silu(v[0][i] + b0) * (v[NW - 1][i] + b1);
-      } else {
-        o[i] = apply_act(v[0][i] + b0, act);
-        if (a.aux) o[i] *= __ldg(a.aux + (size_t)m * a.N + nn);
-      }
+      b[w][i] = a.bias[w] ? __ldg(a.bias[w] + nn) : 0.0f;
     }
-    float* dst = a.y + (size_t)m * a.N + n;
-    if (a.yvec && n + 3 < a.N) {
-      *reinterpret_cast<float4*>(dst) = make_float4(o[0], o[1], o[2], o[3]);
-    } else {
+  uint32_t peer[kMaxSplit];
+  const uint32_t red = ptx::smem_u32(red_smem);
 #pragma unroll
-      for (int i = 0; i < 4; ++i)
-        if (n + i < a.N) dst[i] = o[i];
+  for (int p = 0; p < kMaxSplit; ++p) peer[p] = p < SPL ? ptx::mapa_shared(red, (uint32_t)p) : 0u;
+  const int act = a.act;
+  for (int col0 = c0 + (int)(threadIdx.x >> 5); col0 < c1; col0 += 16 * kColsPer) {
+    float4 t[kColsPer][kMaxSplit][NW];
+#pragma unroll
+    for (int c = 0; c < kColsPer; ++c) {
+      const int col = col0 + 16 * c;
+#pragma unroll
+      for (int p = 0; p < kMaxSplit; ++p)
+        if (p < SPL && col < c1)
+#pragma unroll
+          for (int w = 0; w < NW; ++w)
+            t[c][p][w] = ptx::ld_shared_cluster_f4(peer[p] + (uint32_t)(((w * BT + col) * 128 + r4) * 4));
+    }
+#pragma unroll
+    for (int c = 0; c < kColsPer; ++c) {
+      const int col = col0 + 16 * c;
+      const int m = mtile * BT + col;
+      if (col >= c1 || m >= a.M) continue;
+      float v[NW][4];
+#pragma unroll
+      for (int w = 0; w < NW; ++w) {
+        v[w][0] = v[w][1] = v[w][2] = v[w][3] = 0.0f;
+#pragma unroll
+        for (int p = 0; p < kMaxSplit; ++p)
+          if (p < SPL) {
+            v[w][0] += t[c][p][w].x; v[w][1] += t[c][p][w].y; v[w][2] += t[c][p][w].z; v[w][3] += t[c][p][w].w;
+          }
+      }
+      float o[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        if (NW == 2) {
+          o[i] = silu(v[0][i] + b[0][i]) * (v[NW - 1][i] + b[NW - 1][i]);
+        } else {
+          o[i] = apply_act(v[0][i] + b[0][i], act);
+          if (a.aux) o[i] *= __ldg(a.aux + (size_t)m * a.N + (n + i < a.N ? n + i : a.N - 1));
+        }
+      }
+      if (a.yvec && n + 3 < a.N) {
+        if (a.y_f16) {
+          const __half2 h01 = __floats2half2_rn(o[0], o[1]), h23 = __floats2half2_rn(o[2], o[3]);
+          *reinterpret_cast<uint2*>(reinterpret_cast<__half*>(a.y) + (size_t)m * a.ldy + n) =
+              make_uint2(*reinterpret_cast<const uint32_t*>(&h01), *reinterpret_cast<const uint32_t*>(&h23));
+        } else {
+          *reinterpret_cast<float4*>(reinterpret_cast<float*>(a.y) + (size_t)m * a.ldy + n) =
+              make_float4(o[0], o[1], o[2], o[3]);
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+          if (n + i < a.N) store_y(a, m, n + i, o[i]);
+      }
     }
   }
 }
@@ -618,7 +645,7 @@ __global__ void __launch_bounds__(kWsThreads, 1)
               v = apply_act(acc[0][j] + b0, act);
               if (a.aux) v *= __ldg(a.aux + (size_t)m * a.N + n);
             }
-            a.y[(size_t)m * a.N + n] = v;
+            store_y(a, m, n, v);
           }
         }
       }
@@ -815,6 +842,24 @@ int numerics_mode() {
 
 void set_numerics_mode(int mode) { g_numerics.store(mode, std::memory_order_relaxed); }
 
+namespace {
+std::atomic<int> g_sm_budget{-1};
+}
+
+int sm_budget() {
+  int v = g_sm_budget.load(std::memory_order_relaxed);
+  if (v < 0) {
+    v = 0;
+    if (const char* e = getenv("BQ4_SM_BUDGET")) v = atoi(e) > 0 ? atoi(e) : 0;
+    int expected = -1;
+    g_sm_budget.compare_exchange_strong(expected, v);
+    v = g_sm_budget.load(std::memory_order_relaxed);
+  }
+  return v;
+}
+
+void set_sm_budget(int sms) { g_sm_budget.store(sms > 0 ? sms : 0, std::memory_order_relaxed); }
+
 int device_sm_count(int device) {
   static int cache[64] = {0};
   if (device < 0 || device >= 64) return 148;
@@ -863,7 +908,8 @@ bq4_status plan_gemm(const bq4_weight* w, int nw, int64_t M, int device, GemmPla
   }
   p->mtiles = (int)((M + p->bt - 1) / p->bt);
   p->ntiles = (int)w->ntiles;
-  const int sms = device_sm_count(device);
+  int sms = device_sm_count(device);
+  if (sm_budget() > 0 && sm_budget() < sms) sms = sm_budget();  // leave SMs to other streams
   const int tiles = p->mtiles * p->ntiles;
   const int nkc = (int)w->nkc;
   const int nks = nkc / 2;  // 128-K stages
@@ -922,7 +968,7 @@ bq4_status plan_gemm(const bq4_weight* w, int nw, int64_t M, int device, GemmPla
   const int max_s = nks < kMaxSplit ? nks : kMaxSplit;
   for (int s = 1; s <= max_s; ++s) {
     const int units = tiles * s;
-    if (s > 1 && units > s * cluster_capacity(p->bt, nw, s, p->smem_bytes, device)) continue;
+    if (s > 1 && (units > s * cluster_capacity(p->bt, nw, s, p->smem_bytes, device) || units > sms)) continue;
     const int waves = (units + sms - 1) / sms;
     const double per_unit = (double)nkc / s + 3.0;  // chunks
     const double fixup = s > 1 ? 1.0 + 0.25 * s : 0.0;
@@ -937,7 +983,9 @@ bq4_status plan_gemm(const bq4_weight* w, int nw, int64_t M, int device, GemmPla
   if (const char* f = getenv("BQ4_FORCE_KSPLIT")) {
     int v = atoi(f);
     if (v >= 1) best_s = v < max_s ? v : max_s;
-    while (best_s > 1 && tiles * best_s > best_s * cluster_capacity(p->bt, nw, best_s, p->smem_bytes, device)) --best_s;
+    while (best_s > 1 && (tiles * best_s > best_s * cluster_capacity(p->bt, nw, best_s, p->smem_bytes, device) ||
+                          tiles * best_s > sms))
+      --best_s;
   }
   p->ksplit = best_s;
   p->units = tiles * best_s;
@@ -957,26 +1005,32 @@ bq4_status plan_gemm(const bq4_weight* w, int nw, int64_t M, int device, GemmPla
   return BQ4_OK;
 }
 
-bq4_status run_gemm(const GemmPlan& plan, const bq4_weight* const* ws, const float* x, int64_t M,
-                    int64_t ldx, const float* const* bias, int act, const float* aux, float* y,
-                    void* workspace, cudaStream_t stream) {
+bq4_status run_gemm(const GemmPlan& plan, const bq4_weight* const* ws, const void* x, int64_t M,
+                    int64_t ldx, const float* const* bias, int act, const float* aux, void* y,
+                    void* workspace, cudaStream_t stream, const GemmIo& io) {
   const bq4_weight* w0 = ws[0];
-  uint8_t* wsp = static_cast<uint8_t*>(workspace);
-  void* xh = wsp;
+  cudaError_t e = cudaSuccess;
+  const void* xh = x;
+  int64_t x_pitch = ldx;
+  if (!io.x_f16) {
+    // 1) stage activations as f16 [M][Kp] in the workspace
+    void* dst = workspace;
+    e = launch_convert_x(static_cast<const float*>(x), M, w0->K, ldx, w0->Kp, dst, stream);
+    if (e != cudaSuccess) return check_cuda(e, "convert_x launch");
+    xh = dst;
+    x_pitch = w0->Kp;
+  }
 
-  // 1) stage activations as f16
-  cudaError_t e = launch_convert_x(x, M, w0->K, ldx, w0->Kp, xh, stream);
-  if (e != cudaSuccess) return check_cuda(e, "convert_x launch");
-
-  // 2) tensor map over xh [M][Kp] f16, box {64, BT}, 128-byte swizzle
+  // 2) tensor map over the f16 tokens [M][Kp] (caller's buffer when x is
+  //    already f16 with K == Kp), box {64, BT}, 128-byte swizzle
   EncodeTiledFn enc = encode_fn();
   if (!enc) return set_error(BQ4_ECUDA, "cuTensorMapEncodeTiled unavailable");
   CUtensorMap tmap;
   cuuint64_t gdim[2] = {(cuuint64_t)w0->Kp, (cuuint64_t)M};
-  cuuint64_t gstride[1] = {(cuuint64_t)w0->Kp * 2};
+  cuuint64_t gstride[1] = {(cuuint64_t)x_pitch * 2};
   cuuint32_t box[2] = {(cuuint32_t)kChunkK, (cuuint32_t)plan.bt};
   cuuint32_t estride[2] = {1, 1};
-  CUresult cr = enc(&tmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, xh, gdim, gstride, box, estride,
+  CUresult cr = enc(&tmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(xh), gdim, gstride, box, estride,
                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (cr != CUDA_SUCCESS) return set_error(BQ4_ECUDA, "cuTensorMapEncodeTiled failed (%d)", (int)cr);
@@ -991,6 +1045,8 @@ bq4_status run_gemm(const GemmPlan& plan, const bq4_weight* const* ws, const flo
   }
   args.aux = aux;
   args.y = y;
+  args.y_f16 = io.y_f16;
+  args.ldy = (int)(io.ldy > 0 ? io.ldy : w0->N);
   args.M = (int)M;
   args.N = (int)w0->N;
   args.nkc = (int)w0->nkc;
@@ -1001,7 +1057,7 @@ bq4_status run_gemm(const GemmPlan& plan, const bq4_weight* const* ws, const flo
   args.ksplit = plan.ksplit;
   args.units = plan.units;
   args.nfast = plan.nfast;
-  args.yvec = ((reinterpret_cast<uintptr_t>(y) & 15) == 0 && w0->N % 4 == 0) ? 1 : 0;
+  args.yvec = ((reinterpret_cast<uintptr_t>(y) & (io.y_f16 ? 7 : 15)) == 0 && args.ldy % 4 == 0) ? 1 : 0;
   args.stages = plan.stages;
   args.rs = plan.raw_stages;
   args.exact = plan.exact;

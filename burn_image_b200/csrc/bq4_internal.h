@@ -66,6 +66,10 @@ cudaError_t launch_dequant_raw(const uint32_t* words, const float* scales, int64
 cudaError_t launch_convert_x(const float* x, int64_t M, int64_t K, int64_t ldx, int64_t Kp,
                              void* xh, cudaStream_t s);
 
+// Per-row RMS renormalisation (the layer-stack workload's between-block step).
+cudaError_t launch_rms_renorm(const void* x, int x_f16, int64_t M, int64_t H, int64_t ldx, void* out,
+                              int out_f16, int64_t ldo, float eps, cudaStream_t s);
+
 // ------------------------------------------------------------ GEMM (bq4_gemm_sm100.cu)
 struct GemmPlan {
   int nw;          // 1 = plain, 2 = gated (gate, up)
@@ -88,15 +92,27 @@ struct GemmPlan {
 
 bq4_status plan_gemm(const bq4_weight* w, int nw, int64_t M, int device, GemmPlan* plan);
 
-bq4_status run_gemm(const GemmPlan& plan, const bq4_weight* const* ws, const float* x, int64_t M,
-                    int64_t ldx, const float* const* bias, int act, const float* aux, float* y,
-                    void* workspace, cudaStream_t stream);
+// Activation / output formats of one GEMM call: x f32 (staged to f16 in the
+// workspace) or f16 (read in place; needs K == Kp), y f32 or f16 with row
+// pitch ldy elements (0 = N).
+struct GemmIo {
+  int x_f16 = 0;
+  int y_f16 = 0;
+  int64_t ldy = 0;
+};
+
+bq4_status run_gemm(const GemmPlan& plan, const bq4_weight* const* ws, const void* x, int64_t M,
+                    int64_t ldx, const float* const* bias, int act, const float* aux, void* y,
+                    void* workspace, cudaStream_t stream, const GemmIo& io = GemmIo());
 
 // Operand staging policy (bq4_numerics); AUTO keeps exact weights up to
 // this many rows.
 constexpr int64_t kAutoExactMaxM = 1024;
 int numerics_mode();
 void set_numerics_mode(int mode);
+// Resident-CTA cap for GEMM launches (0 = every SM).
+int sm_budget();
+void set_sm_budget(int sms);
 
 int device_sm_count(int device);
 int device_is_sm100(int device);

@@ -257,6 +257,49 @@ cudaError_t launch_dequant_raw(const uint32_t* words, const float* scales, int64
   return cudaGetLastError();
 }
 
+// One block of 256 threads per row: out[m,:] = x[m,:] * rsqrt(mean(x[m,:]^2)
+// + eps), f32 arithmetic, f32 or f16 in and out.
+__global__ void rms_renorm_kernel(const void* __restrict__ x, int x_f16, int64_t H, int64_t ldx,
+                                  void* __restrict__ out, int out_f16, int64_t ldo, float eps) {
+  const int64_t m = blockIdx.x;
+  const __half* xh = reinterpret_cast<const __half*>(x) + m * ldx;
+  const float* xf = reinterpret_cast<const float*>(x) + m * ldx;
+  float ss = 0.0f;
+  for (int64_t h = threadIdx.x; h < H; h += blockDim.x) {
+    const float v = x_f16 ? __half2float(xh[h]) : xf[h];
+    ss = fmaf(v, v, ss);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  __shared__ float part[32];
+  if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float t = threadIdx.x < (blockDim.x >> 5) ? part[threadIdx.x] : 0.0f;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+    if (threadIdx.x == 0) part[0] = t;
+  }
+  __syncthreads();
+  const float r = rsqrtf(part[0] / (float)H + eps);
+  __half* oh = reinterpret_cast<__half*>(out) + m * ldo;
+  float* of = reinterpret_cast<float*>(out) + m * ldo;
+  for (int64_t h = threadIdx.x; h < H; h += blockDim.x) {
+    const float v = (x_f16 ? __half2float(xh[h]) : xf[h]) * r;
+    if (out_f16)
+      oh[h] = __float2half_rn(v);
+    else
+      of[h] = v;
+  }
+}
+
+cudaError_t launch_rms_renorm(const void* x, int x_f16, int64_t M, int64_t H, int64_t ldx, void* out,
+                              int out_f16, int64_t ldo, float eps, cudaStream_t s) {
+  rms_renorm_kernel<<<(unsigned)M, 256, 0, s>>>(x, x_f16, H, ldx, out, out_f16, ldo, eps);
+  note_launch();
+  return cudaGetLastError();
+}
+
 cudaError_t launch_convert_x(const float* x, int64_t M, int64_t K, int64_t ldx, int64_t Kp,
                              void* xh, cudaStream_t s) {
   const int vec4 = ((reinterpret_cast<uintptr_t>(x) & 15) == 0) && (ldx % 4 == 0);

@@ -129,12 +129,14 @@ __device__ __forceinline__ uint32_t mapa_shared(uint32_t smem_addr, uint32_t ran
   return r;
 }
 
+// Load from a cluster peer's shared memory.  No memory clobber: callers read
+// data published before a cluster barrier (whose own clobber orders them),
+// so the compiler may keep other loads in flight around these.
 __device__ __forceinline__ float4 ld_shared_cluster_f4(uint32_t cluster_addr) {
   float4 v;
   asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
                : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
-               : "r"(cluster_addr)
-               : "memory");
+               : "r"(cluster_addr));
   return v;
 }
 

@@ -230,6 +230,56 @@ class PreparedQ4Weight:
         return y.reshape(*lead, self.N)
 
 
+    def linear_ex(self, x: torch.Tensor, bias: Optional[torch.Tensor] = None, act: int = L.ACT_NONE,
+                  aux: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None,
+                  out_dtype: torch.dtype = torch.float32) -> torch.Tensor:
+        """bq4_linear_ex: the same linear for chained activations.  x is a
+        float32 or float16 [M, K] view with unit column stride (its row pitch
+        is passed on, so a column slice of a wider buffer works; float16 x
+        needs K % 128 == 0 and 16-byte aligned rows and is read in place).
+        The output is float32 or float16 (``out``'s dtype, else
+        ``out_dtype``), written to ``out`` -- an [M, N] view with unit column
+        stride, possibly a column slice of a wider buffer."""
+        dt = {torch.float32: L.DTYPE_F32, torch.float16: L.DTYPE_F16}
+        if x.device != self.device or x.dtype not in dt or x.dim() != 2 or x.shape[1] != self.K or x.stride(1) != 1:
+            raise Bq4Error(L.EINVAL_ARG, f"x must be a float32/float16 [M, {self.K}] row view on {self.device}")
+        M = x.shape[0]
+        y = out if out is not None else torch.empty((M, self.N), dtype=out_dtype, device=self.device)
+        if y.device != self.device or y.dtype not in dt or tuple(y.shape) != (M, self.N) or y.stride(1) != 1:
+            raise Bq4Error(L.EINVAL_ARG, f"out must be a float32/float16 [{M}, {self.N}] row view on {self.device}")
+        if bias is not None:
+            bias = _vec(bias, self.N, self.device)
+        if aux is not None:
+            aux = aux.reshape(M, self.N)
+            _check_out(aux, M, self.N, self.device)
+        n = ctypes.c_size_t()
+        check(L.lib().bq4_linear_ex_workspace_size(self._h, M, dt[x.dtype], ctypes.byref(n)))
+        ws = Workspace.get(self.device, n.value) if n.value else None
+        check(L.lib().bq4_linear_ex(self._h, _ptr(x), dt[x.dtype], M, x.stride(0), _ptr(bias), act, _ptr(aux),
+                                    _ptr(y), dt[y.dtype], y.stride(0), _ptr(ws), ws.numel() if ws is not None else 0,
+                                    _stream_ptr(self.device)))
+        return y
+
+
+def rms_renorm(x: torch.Tensor, out: torch.Tensor, eps: float = 1e-6) -> torch.Tensor:
+    """out[m,:] = x[m,:] / sqrt(mean(x[m,:]^2) + eps) in one kernel (the
+    between-block step of the layer-stack workload); x and out are float32 or
+    float16 [M, H] row views with unit column stride."""
+    dt = {torch.float32: L.DTYPE_F32, torch.float16: L.DTYPE_F16}
+    if x.dim() != 2 or out.shape != x.shape or x.stride(1) != 1 or out.stride(1) != 1 \
+            or x.dtype not in dt or out.dtype not in dt:
+        raise Bq4Error(L.EINVAL_ARG, "rms_renorm needs float32/float16 [M, H] row views of one shape")
+    check(L.lib().bq4_rms_renorm(_ptr(x), dt[x.dtype], x.shape[0], x.shape[1], x.stride(0), _ptr(out),
+                                 dt[out.dtype], out.stride(0), ctypes.c_float(eps), _stream_ptr(x.device)))
+    return out
+
+
+def set_sm_budget(sms: int) -> None:
+    """Cap the SMs a GEMM launch occupies (0 = all), leaving room for
+    kernels on other streams such as overlapping NCCL collectives."""
+    check(L.lib().bq4_set_sm_budget(int(sms)))
+
+
 def physical_layout(scheme: QuantScheme, shape: tuple, stored: str = "nk"):
     """(K, N, bq4 layout) of a packed tensor of stored `shape`."""
     if scheme.store_packed_dim == 1:

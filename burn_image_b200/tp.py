@@ -56,7 +56,14 @@ def slice_raw(words: np.ndarray, scales: np.ndarray, K: int, N: int, block: int,
     return np.ascontiguousarray(w), np.ascontiguousarray(s)
 
 
+# Pass as `group` to build an unsharded linear or stack on every rank (token
+# parallelism: each rank runs the whole weight on its own tokens).
+LOCAL = "local"
+
+
 def _world(group):
+    if group == LOCAL:
+        return 0, 1
     if dist.is_available() and dist.is_initialized():
         return dist.get_rank(group), dist.get_world_size(group)
     return 0, 1
@@ -76,6 +83,10 @@ class ColumnParallelQ4Linear:
     def forward(self, x: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
         """x [M, K] (replicated) -> local output columns [M, N/P]."""
         return self.weight.linear(x, self.bias, self.act, out=out)
+
+    def forward_ex(self, x: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
+        """Same, with float16 or float32 activations in and out."""
+        return self.weight.linear_ex(x, self.bias, self.act, out=out)
 
 
 class RowParallelQ4Linear:
@@ -103,6 +114,18 @@ class RowParallelQ4Linear:
             dist.all_reduce(y, op=dist.ReduceOp.SUM, group=self.group)
         return y
 
+    def forward_ex(self, x_local: torch.Tensor, out: torch.Tensor, async_op: bool = False):
+        """Same, with float16 or float32 activations; the partial sums are
+        reduced in ``out``'s dtype.  With ``async_op`` the all-reduce is only
+        enqueued and its work handle returned (``wait()`` makes the current
+        stream wait for it); otherwise returns ``out``."""
+        self.weight.linear_ex(x_local, self.bias, L.ACT_NONE, out=out)
+        if self.size > 1:
+            work = dist.all_reduce(out, op=dist.ReduceOp.SUM, group=self.group, async_op=async_op)
+            if async_op:
+                return work
+        return None if async_op else out
+
 
 class DiTQ4Stack:
     """The DiT-shaped layer stack of the benchmark: per block a fused qkv
@@ -114,8 +137,17 @@ class DiTQ4Stack:
     columns of the qkv output as its input shard."""
 
     def __init__(self, blocks: int, hidden: int, qkv: int, mlp: int, device: torch.device, seed: int = 0,
-                 block: int = 128, group=None):
+                 block: int = 128, group=None, act_dtype: torch.dtype = torch.float32, chunks: int = 1):
         self.device = device
+        # act_dtype float16: activations stay in the GEMM's operand format
+        # between linears (bq4_linear_ex), the renorm is one kernel.  The
+        # row-parallel partials (P > 1) are still summed in float32: float16
+        # partial sums overflow on this workload (its random weights have a
+        # nonzero mean, so activations grow to ~1e5 between renorms).
+        # chunks > 1 pipelines token chunks so that each chunk's all-reduces
+        # overlap the other chunks' GEMMs.
+        self.act_dtype = act_dtype
+        self.chunks = max(1, int(chunks))
         self.hidden, self.qkv, self.mlp = hidden, qkv, mlp
         self.rank, self.size = _world(group)
         self.layers = []
@@ -143,14 +175,16 @@ class DiTQ4Stack:
         h, q, m = self.hidden, self.qkv, self.mlp
         return 2 * len(self.layers) * (h * q + h * h + h * m + m * h)
 
-    def _buf(self, name, shape):
+    def _buf(self, name, shape, dtype=torch.float32):
         t = self.bufs.get(name)
-        if t is None or tuple(t.shape) != tuple(shape):
-            t = torch.empty(shape, dtype=torch.float32, device=self.device)
+        if t is None or tuple(t.shape) != tuple(shape) or t.dtype != dtype:
+            t = torch.empty(shape, dtype=dtype, device=self.device)
             self.bufs[name] = t
         return t
 
     def forward(self, x: torch.Tensor, on_linear=None) -> torch.Tensor:
+        if self.act_dtype == torch.float16:
+            return self._forward_chained(x, on_linear)
         M = x.shape[0]
         P = self.size
         qkv_local = self.qkv // P
@@ -167,6 +201,55 @@ class DiTQ4Stack:
             _timed(on_linear, "down", lambda: layer["down"].forward(u, out=d))
             x = d * torch.rsqrt(d.pow(2).mean(-1, keepdim=True) + 1e-6)
         return x
+
+
+    def _forward_chained(self, x: torch.Tensor, on_linear=None) -> torch.Tensor:
+        """The stack with float16 activations between linears (float32 where
+        a row-parallel partial sum is reduced), in token chunks.  Per block and chunk: [renorm of the previous block's output,
+        qkv, o (row-parallel partial, all-reduce enqueued)] then [wait, up,
+        down (partial, all-reduce enqueued)]; each phase runs over all chunks
+        before the next, so a chunk's all-reduce overlaps the other chunks'
+        GEMMs.  Returns the renormalised float32 output of the last block."""
+        from .q4 import rms_renorm
+        M = x.shape[0]
+        P, C = self.size, self.chunks
+        qkv_local, hid_local, mlp_local = self.qkv // P, self.hidden // P, self.mlp // P
+        bounds = [(M * c // C, M * (c + 1) // C) for c in range(C)]
+        f16 = torch.float16
+        o_dtype = f16 if P == 1 else torch.float32   # row-parallel outputs are reduced in float32
+        d_dtype = torch.float32                       # down output: the renorm's input
+        xin = self._buf("x16", (M, self.hidden), f16)
+        t = self._buf("qkv16", (M, qkv_local), f16)
+        o = self._buf("o_c", (M, self.hidden), o_dtype)
+        u = self._buf("up16", (M, mlp_local), f16)
+        d = self._buf("down_c", (M, self.hidden), d_dtype)
+        pending = [None] * C
+        first = True
+        for layer in self.layers:
+            works = []
+            for c, (a, b) in enumerate(bounds):
+                if first:
+                    xc = x[a:b]
+                else:
+                    if pending[c] is not None:
+                        pending[c].wait()
+                    xc = rms_renorm(d[a:b], xin[a:b])
+                _timed(on_linear, "qkv", lambda: layer["qkv"].forward_ex(xc, out=t[a:b]))
+                v = t[a:b, qkv_local - hid_local:]
+                works.append(_timed(on_linear, "o", lambda: layer["o"].forward_ex(v, out=o[a:b], async_op=True)))
+            first = False
+            for c, (a, b) in enumerate(bounds):
+                if works[c] is not None:
+                    works[c].wait()
+                _timed(on_linear, "up", lambda: layer["up"].forward_ex(o[a:b], out=u[a:b]))
+                pending[c] = _timed(on_linear, "down",
+                                    lambda: layer["down"].forward_ex(u[a:b], out=d[a:b], async_op=True))
+        out = self._buf("out32", (M, self.hidden), torch.float32)
+        for c, (a, b) in enumerate(bounds):
+            if pending[c] is not None:
+                pending[c].wait()
+            rms_renorm(d[a:b], out[a:b])
+        return out
 
 
 def _timed(cb, name, fn):

@@ -134,6 +134,30 @@ BQ4_API bq4_status bq4_linear(const bq4_weight* w, const float* x, int64_t M, in
                       const float* bias, bq4_act act, const float* aux, float* y,
                       void* workspace, size_t workspace_bytes, bq4_stream_t stream);
 
+typedef enum { BQ4_DTYPE_F32 = 0, BQ4_DTYPE_F16 = 1 } bq4_dtype;
+
+/* Workspace for bq4_linear_ex: the bq4_linear size for f32 x, 0 for f16 x. */
+BQ4_API bq4_status bq4_linear_ex_workspace_size(const bq4_weight* w, int64_t M, bq4_dtype x_dtype,
+                                                size_t* bytes);
+
+/*
+ * bq4_linear for chains of linears whose activations stay on the device in
+ * the GEMM's operand format.  The reference keeps activations f32 between
+ * ops and its matmul casts them to f16 on entry (quantized.rs:172-178); here
+ * a linear may instead write its output already rounded to f16 (round to
+ * nearest even, the same rounding the next call's staging would apply) and a
+ * linear may read f16 activations in place, skipping the staging copy.  The
+ * arithmetic is unchanged, so a chain computes the same bits either way.
+ *   x: f32 or f16, row pitch ldx elements.  f16 x needs K % 128 == 0, a
+ *      16-byte aligned base and ldx % 8 == 0.
+ *   y: f32 or f16, row pitch ldy elements (>= N; 0 means N).
+ *   workspace: bq4_linear_ex_workspace_size bytes (NULL allowed when 0).
+ */
+BQ4_API bq4_status bq4_linear_ex(const bq4_weight* w, const void* x, bq4_dtype x_dtype, int64_t M,
+                                 int64_t ldx, const float* bias, bq4_act act, const float* aux, void* y,
+                                 bq4_dtype y_dtype, int64_t ldy, void* workspace, size_t workspace_bytes,
+                                 bq4_stream_t stream);
+
 BQ4_API bq4_status bq4_linear_gated_workspace_size(const bq4_weight* gate, const bq4_weight* up, int64_t M,
                                            size_t* bytes);
 
@@ -241,6 +265,21 @@ BQ4_API bq4_status bq4_poll_device_error(void);
 
 /* Process-wide operand staging for subsequent compute calls (see bq4_numerics). */
 BQ4_API bq4_status bq4_set_numerics(bq4_numerics mode);
+
+/* Caps the CTAs (one per SM) that a GEMM launch keeps resident, process-wide;
+ * 0 (the default, or the environment variable BQ4_SM_BUDGET) means every SM.
+ * A GEMM otherwise occupies the whole GPU until it ends; a cap leaves SMs for
+ * kernels on other streams, e.g. NCCL collectives meant to overlap it.  The
+ * reference has no counterpart (it runs on one device). */
+BQ4_API bq4_status bq4_set_sm_budget(int32_t sms);
+
+/* Per-token RMS renormalisation, out[m,:] = x[m,:] / sqrt(mean(x[m,:]^2) +
+ * eps), f32 arithmetic, f32 or f16 in and out, rows of H values at pitches
+ * ldx / ldo.  Not a step of the reference's Q4 path: it is the between-block
+ * step of the DiT-shaped layer-stack workload (activations renormalised per
+ * block), provided so that workload runs in one kernel per block. */
+BQ4_API bq4_status bq4_rms_renorm(const void* x, bq4_dtype x_dtype, int64_t M, int64_t H, int64_t ldx, void* out,
+                                  bq4_dtype out_dtype, int64_t ldo, float eps, bq4_stream_t stream);
 
 /* Kernel launches issued by this thread since the last reset (bench accounting). */
 BQ4_API uint64_t bq4_launch_count(void);
