@@ -215,24 +215,52 @@ __device__ __forceinline__ bool ws_seg_last(int kc, int kc1, int cpb) {
 }
 
 // Split-K reduction across the cluster (one CTA per split, cluster rank =
-// split).  Every CTA holds its split's partial tile red[NW][BT][128] f32 in
-// shared memory; CTA `rank` owns the token columns [c0, c1) of the tile,
-// sums them over all splits in rank order (deterministic) through
-// distributed shared memory, and runs the epilogue on them.  Called by the
-// 512 scaler threads between two cluster barriers: warp w takes every 16th
-// column from c0 + w, lane l the four features 4l..4l+3 (its bias is loaded
-// once); two columns' peer loads are in flight at a time (one with NW = 2).
+// split).  CTA r owns the token columns [c0_r, c1_r), c0_r = BT*r/splits.
+// After the main loop each split pushes its f32 partial tile, column by
+// column, into the owner's receive buffer recv[src][w][col - c0_r][128]
+// (in the owner's idle operand ring) with posted distributed-shared-memory
+// stores; after a cluster barrier each owner sums its columns over the
+// splits in rank order (deterministic) from its own shared memory and runs
+// the epilogue.
+__host__ __device__ constexpr int split_cols_max(int bt, int spl) { return (bt + spl - 1) / spl; }
+
+__device__ __forceinline__ int split_owner(int col, int bt, int spl) { return ((col + 1) * spl - 1) / bt; }
+
+// Push this thread's partial columns (row `row`, token columns col0..) to
+// their owners.
+template <int BT, int NW, int kCols>
+__device__ __forceinline__ void split_push(const WsArgs& a, const uint8_t* ring, const float (&acc)[NW][kCols],
+                                           int row, int col0) {
+  const int SPL = a.ksplit;
+  const int src = (int)ptx::cluster_ctarank();
+  const int ncm = split_cols_max(BT, SPL);
+  const uint32_t base = ptx::smem_u32(ring);
+#pragma unroll
+  for (int j = 0; j < kCols; ++j) {
+    const int col = col0 + j;
+    const int r = split_owner(col, BT, SPL);
+    const int cc = col - BT * r / SPL;
+#pragma unroll
+    for (int w = 0; w < NW; ++w) {
+      const uint32_t off = (uint32_t)((((src * NW + w) * ncm + cc) * 128 + row) * 4);
+      ptx::st_shared_cluster_f32(ptx::mapa_shared(base + off, (uint32_t)r), acc[w][j]);
+    }
+  }
+}
+
+// Owner side: warp w takes every 16th owned column from c0 + w, lane l the
+// features 4l..4l+3 (bias loaded once).
 template <int BT, int NW>
-__device__ __forceinline__ void split_reduce_epilogue(const WsArgs& a, const uint8_t* red_smem) {
+__device__ __forceinline__ void split_reduce_epilogue(const WsArgs& a, const uint8_t* ring) {
   const int SPL = a.ksplit;
   const int rank = (int)ptx::cluster_ctarank();
   int mtile, ntile;
   ws_tile(a, (int)blockIdx.x / SPL, mtile, ntile);
   const int c0 = BT * rank / SPL, c1 = BT * (rank + 1) / SPL;
+  const int ncm = split_cols_max(BT, SPL);
   const int r4 = (int)(threadIdx.x & 31) * 4;
   const int n = ntile * 128 + r4;
   if (n >= a.N) return;
-  constexpr int kColsPer = NW == 1 ? 2 : 1;
   float b[NW][4];
 #pragma unroll
   for (int w = 0; w < NW; ++w)
@@ -241,62 +269,44 @@ __device__ __forceinline__ void split_reduce_epilogue(const WsArgs& a, const uin
       const int nn = n + i < a.N ? n + i : a.N - 1;
       b[w][i] = a.bias[w] ? __ldg(a.bias[w] + nn) : 0.0f;
     }
-  uint32_t peer[kMaxSplit];
-  const uint32_t red = ptx::smem_u32(red_smem);
-#pragma unroll
-  for (int p = 0; p < kMaxSplit; ++p) peer[p] = p < SPL ? ptx::mapa_shared(red, (uint32_t)p) : 0u;
+  const float* recv = reinterpret_cast<const float*>(ring);
   const int act = a.act;
-  for (int col0 = c0 + (int)(threadIdx.x >> 5); col0 < c1; col0 += 16 * kColsPer) {
-    float4 t[kColsPer][kMaxSplit][NW];
+  for (int col = c0 + (int)(threadIdx.x >> 5); col < c1; col += 16) {
+    const int m = mtile * BT + col;
+    if (m >= a.M) break;
+    float v[NW][4];
 #pragma unroll
-    for (int c = 0; c < kColsPer; ++c) {
-      const int col = col0 + 16 * c;
-#pragma unroll
-      for (int p = 0; p < kMaxSplit; ++p)
-        if (p < SPL && col < c1)
-#pragma unroll
-          for (int w = 0; w < NW; ++w)
-            t[c][p][w] = ptx::ld_shared_cluster_f4(peer[p] + (uint32_t)(((w * BT + col) * 128 + r4) * 4));
+    for (int w = 0; w < NW; ++w) {
+      v[w][0] = v[w][1] = v[w][2] = v[w][3] = 0.0f;
+      for (int p = 0; p < SPL; ++p) {
+        const float4 t =
+            *reinterpret_cast<const float4*>(recv + (((size_t)(p * NW + w) * ncm + (col - c0)) * 128 + r4));
+        v[w][0] += t.x; v[w][1] += t.y; v[w][2] += t.z; v[w][3] += t.w;
+      }
     }
+    float o[4];
 #pragma unroll
-    for (int c = 0; c < kColsPer; ++c) {
-      const int col = col0 + 16 * c;
-      const int m = mtile * BT + col;
-      if (col >= c1 || m >= a.M) continue;
-      float v[NW][4];
-#pragma unroll
-      for (int w = 0; w < NW; ++w) {
-        v[w][0] = v[w][1] = v[w][2] = v[w][3] = 0.0f;
-#pragma unroll
-        for (int p = 0; p < kMaxSplit; ++p)
-          if (p < SPL) {
-            v[w][0] += t[c][p][w].x; v[w][1] += t[c][p][w].y; v[w][2] += t[c][p][w].z; v[w][3] += t[c][p][w].w;
-          }
-      }
-      float o[4];
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        if (NW == 2) {
-          o[i] = silu(v[0][i] + b[0][i]) * (v[NW - 1][i] + b[NW - 1][i]);
-        } else {
-          o[i] = apply_act(v[0][i] + b[0][i], act);
-          if (a.aux) o[i] *= __ldg(a.aux + (size_t)m * a.N + (n + i < a.N ? n + i : a.N - 1));
-        }
-      }
-      if (a.yvec && n + 3 < a.N) {
-        if (a.y_f16) {
-          const __half2 h01 = __floats2half2_rn(o[0], o[1]), h23 = __floats2half2_rn(o[2], o[3]);
-          *reinterpret_cast<uint2*>(reinterpret_cast<__half*>(a.y) + (size_t)m * a.ldy + n) =
-              make_uint2(*reinterpret_cast<const uint32_t*>(&h01), *reinterpret_cast<const uint32_t*>(&h23));
-        } else {
-          *reinterpret_cast<float4*>(reinterpret_cast<float*>(a.y) + (size_t)m * a.ldy + n) =
-              make_float4(o[0], o[1], o[2], o[3]);
-        }
+    for (int i = 0; i < 4; ++i) {
+      if (NW == 2) {
+        o[i] = silu(v[0][i] + b[0][i]) * (v[NW - 1][i] + b[NW - 1][i]);
       } else {
-#pragma unroll
-        for (int i = 0; i < 4; ++i)
-          if (n + i < a.N) store_y(a, m, n + i, o[i]);
+        o[i] = apply_act(v[0][i] + b[0][i], act);
+        if (a.aux) o[i] *= __ldg(a.aux + (size_t)m * a.N + (n + i < a.N ? n + i : a.N - 1));
       }
+    }
+    if (a.yvec && n + 3 < a.N) {
+      if (a.y_f16) {
+        const __half2 h01 = __floats2half2_rn(o[0], o[1]), h23 = __floats2half2_rn(o[2], o[3]);
+        *reinterpret_cast<uint2*>(reinterpret_cast<__half*>(a.y) + (size_t)m * a.ldy + n) =
+            make_uint2(*reinterpret_cast<const uint32_t*>(&h01), *reinterpret_cast<const uint32_t*>(&h23));
+      } else {
+        *reinterpret_cast<float4*>(reinterpret_cast<float*>(a.y) + (size_t)m * a.ldy + n) =
+            make_float4(o[0], o[1], o[2], o[3]);
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+        if (n + i < a.N) store_y(a, m, n + i, o[i]);
     }
   }
 }
@@ -574,6 +584,7 @@ __global__ void __launch_bounds__(kWsThreads, 1)
     int pb = 0;
     uint32_t pph = 0;
     bool ok = true;
+    bool split_synced = false;  // this warp has passed the split's two cluster barriers
     if (a.lockstep && lane == 0) {
       // both partial buffers start free: the first use of each stage
       for (int i = 0; i < S; ++i) ptx::mbar_arrive(&full[i]);
@@ -619,16 +630,17 @@ __global__ void __launch_bounds__(kWsThreads, 1)
       if (!ok) break;
 
       if (a.ksplit > 1) {
-        // Split-K: this split's partial tile goes to this CTA's own shared
-        // memory -- the operand ring, idle now that every MMA of the unit
-        // (the CTA's only one) has retired -- as red[w][token][feature];
-        // the cluster sums the splits after the role loops.
-        float* red = reinterpret_cast<float*>(ring);
-#pragma unroll
-        for (int w = 0; w < NW; ++w)
-#pragma unroll
-          for (int j = 0; j < kCols; ++j) red[((size_t)w * BT + col0 + j) * 128 + row] = acc[w][j];
-        continue;
+        // Split-K (the CTA's only unit): barrier 1 -- every CTA of the
+        // cluster has retired its MMAs, so every operand ring is free to
+        // receive; push this split's partial columns to their owners;
+        // barrier 2 -- all pushes landed; reduce the owned columns.
+        __syncwarp();
+        ptx::cluster_sync();
+        split_push<BT, NW, kCols>(a, ring, acc, row, col0);
+        __syncwarp();
+        ptx::cluster_sync();
+        split_synced = true;
+        break;
       }
       if (n < a.N) {
         const float b0 = a.bias[0] ? __ldg(a.bias[0] + n) : 0.0f;
@@ -651,16 +663,13 @@ __global__ void __launch_bounds__(kWsThreads, 1)
       }
     }
     if (!ok) record_error_flag(abort_flag, BQ4_ETIMEOUT);
-    if (a.ksplit > 1) {
-      // Split reduction.  Every role of every CTA of the cluster passes two
-      // cluster barriers (each role branch has its own pair, so each runs
-      // under its warps' register budget): after the first, every split's
-      // partial tile is in its CTA's shared memory; the second keeps that
-      // memory alive until all peers have read it.
+    if (split_synced) split_reduce_epilogue<BT, NW>(a, ring);
+    if (a.ksplit > 1 && !split_synced) {
+      // Every role of every CTA of the cluster passes the split's two
+      // cluster barriers exactly once (each role branch has its own pair);
+      // a scaler warp that left its loop early passes them here.
       __syncwarp();
       ptx::cluster_sync();
-      split_reduce_epilogue<BT, NW>(a, ring);
-      __syncwarp();
       ptx::cluster_sync();
     }
   }
@@ -987,6 +996,9 @@ bq4_status plan_gemm(const bq4_weight* w, int nw, int64_t M, int device, GemmPla
                           tiles * best_s > sms))
       --best_s;
   }
+  // the split's receive buffers must fit the operand ring
+  while (best_s > 1 && (size_t)best_s * nw * split_cols_max(p->bt, best_s) * 128 * 4 > (size_t)S * stage_bytes)
+    --best_s;
   p->ksplit = best_s;
   p->units = tiles * best_s;
   p->cluster = best_s;

@@ -129,6 +129,12 @@ __device__ __forceinline__ uint32_t mapa_shared(uint32_t smem_addr, uint32_t ran
   return r;
 }
 
+// Posted store to a cluster peer's shared memory (visible to the peer after
+// a release/acquire cluster barrier).
+__device__ __forceinline__ void st_shared_cluster_f32(uint32_t cluster_addr, float v) {
+  asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(cluster_addr), "f"(v) : "memory");
+}
+
 // Load from a cluster peer's shared memory.  No memory clobber: callers read
 // data published before a cluster barrier (whose own clobber orders them),
 // so the compiler may keep other loads in flight around these.
