@@ -220,6 +220,9 @@ ROWS = [
     ("c3_dit_down_4352x12288x3072", 4352, 12288, 3072, "linear", 0),
     ("c4_edit_qkv_18432x3072x9216", 18432, 3072, 9216, "linear", 0),
     ("c4_edit_o_18432x3072x3072", 18432, 3072, 3072, "linear", 0),
+    # next row of the path: the packed-Q4 embedding lookup (q_select + dequantize), 256
+    # prompt tokens from a 151936 x 2560 table (rows = table rows, K = row width)
+    ("f1_q4_embedding_256_of_151936x2560", 256, 2560, 151936, "select", 0),
 ]
 
 
@@ -241,6 +244,9 @@ def config_rows(dev, peaks, names=None):
     out = {}
     for name, M, K, N, kind, act in ROWS:
         if names and name not in names:
+            continue
+        if kind == "select":
+            out[name] = _select_row(dev, M, K, N, hbm)
             continue
         nw = 2 if kind == "gated" else 1
         wbytes = nw * (N * K // 2 + N * K // QBLOCK * 4)
@@ -295,6 +301,56 @@ def config_rows(dev, peaks, names=None):
         del graph, items
         torch.cuda.empty_cache()
     return out
+
+
+def _select_row(dev, n, cols, rows, hbm):
+    """Embedding lookup row: n random ids into a packed table of `rows` x
+    `cols` (block 128, PackedU32(0)); graph-replayed over 64 id sets and
+    outputs, whose footprint exceeds L2, so the selected rows come from HBM."""
+    import torch
+
+    from burn_image_b200 import q4
+    g = torch.Generator(device=dev).manual_seed(13)
+    values = torch.randint(-2 ** 31, 2 ** 31 - 1, (rows, cols // 8), generator=g, device=dev,
+                           dtype=torch.int64).to(torch.int32)
+    scales = torch.rand((rows, cols // QBLOCK), generator=g, device=dev) * 0.019 + 0.001
+    qt = q4.QuantizedTensor(values, scales, (rows, cols), q4.QuantScheme(store_packed_dim=0, level=(QBLOCK,)),
+                            transposed_view=False)
+    sets = 64  # selected rows + outputs of one replay cycle: ~190 MB, more than the 126 MB L2
+    ids = [torch.randint(0, rows, (n,), generator=g, device=dev, dtype=torch.int64) for _ in range(sets)]
+    outs = [torch.empty((n, cols), device=dev) for _ in range(sets)]
+    lib = q4.L.lib()
+
+    def call(i, stream):
+        q4.check(lib.bq4_q_select_rows_dequant(values.data_ptr(), scales.data_ptr(), rows, cols, QBLOCK,
+                                               ids[i].data_ptr(), 1, n, outs[i].data_ptr(), stream))
+
+    side = torch.cuda.Stream(dev)
+    side.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(side):
+        for i in range(sets):
+            call(i, side.cuda_stream)
+    torch.cuda.synchronize(dev)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=side):
+        for i in range(sets):
+            call(i, side.cuda_stream)
+    graph.replay()
+    torch.cuda.synchronize(dev)
+    reps = 5
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        graph.replay()
+    e1.record()
+    torch.cuda.synchronize(dev)
+    q4.poll_device_error()
+    t = e0.elapsed_time(e1) * 1e-3 / (reps * sets)
+    nbytes = n * (cols // 2 + cols // QBLOCK * 4) + n * cols * 4 + n * 8
+    t_star = nbytes / (hbm * 1e9)
+    del graph
+    return {"us": t * 1e6, "tflops": 0.0, "gbs": nbytes / t / 1e9, "bound": "hbm", "t_star_us": t_star * 1e6,
+            "frac": t_star / t, "sets": sets}
 
 
 # ------------------------------------------------------------------ GPU arm

@@ -313,6 +313,45 @@ bq4_status bq4_linear(const bq4_weight* w, const float* x, int64_t M, int64_t ld
                   reinterpret_cast<cudaStream_t>(stream));
 }
 
+static bq4_status select_rows(const uint32_t* values, const float* scales, int64_t rows, int64_t cols, int32_t block,
+                              const void* ids, int32_t ids_i64, int64_t n, uint32_t* out_values, float* out_scales,
+                              float* out_f32, bq4_stream_t stream) {
+  if (!values || !scales || !ids) return set_error(BQ4_EINVAL_ARG, "values/scales/ids is NULL");
+  if (block != 8 && block != 16 && block != 32 && block != 64 && block != 128)
+    return set_error(BQ4_EINVAL_BLOCK, "block %d not in {8,16,32,64,128}", (int)block);
+  if (rows <= 0 || cols <= 0 || n < 0 || cols % block)
+    return set_error(BQ4_EINVAL_SHAPE, "rows=%lld cols=%lld n=%lld block=%d", (long long)rows, (long long)cols,
+                     (long long)n, (int)block);
+  if (!aligned(values, 4) || !aligned(scales, 4) || !aligned(ids, ids_i64 ? 8 : 4))
+    return set_error(BQ4_EALIGN, "values/scales/ids misaligned");
+  if (out_f32 && !aligned(out_f32, 16)) return set_error(BQ4_EALIGN, "out not 16-byte aligned");
+  if (n == 0) return BQ4_OK;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  bq4_status st = require_sm100(dev);
+  if (st) return st;
+  int* err = device_error_word();
+  if (!err) return set_error(BQ4_ECUDA, "device error word unavailable");
+  cudaError_t e = launch_select_rows(values, scales, rows, cols, block, ids, ids_i64 ? 1 : 0, n, out_values,
+                                     out_scales, out_f32, err, reinterpret_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? BQ4_OK : check_cuda(e, "select_rows launch");
+}
+
+bq4_status bq4_q_select_rows(const uint32_t* values, const float* scales, int64_t rows, int64_t cols, int32_t block,
+                             const void* ids, int32_t ids_i64, int64_t n, uint32_t* out_values, float* out_scales,
+                             bq4_stream_t stream) {
+  if (!out_values || !out_scales) return set_error(BQ4_EINVAL_ARG, "out_values/out_scales is NULL");
+  if (!aligned(out_values, 4) || !aligned(out_scales, 4)) return set_error(BQ4_EALIGN, "outputs misaligned");
+  return select_rows(values, scales, rows, cols, block, ids, ids_i64, n, out_values, out_scales, nullptr, stream);
+}
+
+bq4_status bq4_q_select_rows_dequant(const uint32_t* values, const float* scales, int64_t rows, int64_t cols,
+                                     int32_t block, const void* ids, int32_t ids_i64, int64_t n, float* out,
+                                     bq4_stream_t stream) {
+  if (!out) return set_error(BQ4_EINVAL_ARG, "out is NULL");
+  return select_rows(values, scales, rows, cols, block, ids, ids_i64, n, nullptr, nullptr, out, stream);
+}
+
 bq4_status bq4_set_sm_budget(int32_t sms) {
   if (sms < 0) return set_error(BQ4_EINVAL_ARG, "sm budget %d is negative", (int)sms);
   set_sm_budget(sms);

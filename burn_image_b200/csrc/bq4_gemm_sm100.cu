@@ -1096,6 +1096,21 @@ bq4_status run_gemm(const GemmPlan& plan, const bq4_weight* const* ws, const voi
   return BQ4_OK;
 }
 
+int* device_error_word() {
+  static std::atomic<int*> cache[64];
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) dev = 0;
+  int* p = cache[dev].load(std::memory_order_relaxed);
+  if (!p) {
+    void* q = nullptr;
+    if (cudaGetSymbolAddress(&q, g_bq4_device_error) != cudaSuccess) return nullptr;
+    p = static_cast<int*>(q);
+    cache[dev].store(p, std::memory_order_relaxed);
+  }
+  return p;
+}
+
 bq4_status poll_device_error() {
   int v = 0;
   cudaError_t e = cudaMemcpyFromSymbol(&v, g_bq4_device_error, sizeof(int));

@@ -66,6 +66,14 @@ cudaError_t launch_dequant_raw(const uint32_t* words, const float* scales, int64
 cudaError_t launch_convert_x(const float* x, int64_t M, int64_t K, int64_t ldx, int64_t Kp,
                              void* xh, cudaStream_t s);
 
+// Packed-Q4 row selection (q_select on dim 0), optionally dequantized.
+cudaError_t launch_select_rows(const uint32_t* values, const float* scales, int64_t rows, int64_t cols, int block,
+                               const void* ids, int ids64, int64_t n, uint32_t* out_values, float* out_scales,
+                               float* out_f32, int* err, cudaStream_t s);
+// Device address of the error word bq4_poll_device_error reads, on the
+// current device (for kernels compiled outside the GEMM's unit).
+int* device_error_word();
+
 // Per-row RMS renormalisation (the layer-stack workload's between-block step).
 cudaError_t launch_rms_renorm(const void* x, int x_f16, int64_t M, int64_t H, int64_t ldx, void* out,
                               int out_f16, int64_t ldo, float eps, cudaStream_t s);

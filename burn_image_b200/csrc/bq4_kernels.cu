@@ -257,6 +257,57 @@ cudaError_t launch_dequant_raw(const uint32_t* words, const float* scales, int64
   return cudaGetLastError();
 }
 
+// Row selection from a packed Q4S matrix [rows][cols] (PackedU32(0): words
+// [rows][wpr], scales [rows][spr], blocks along the row).  One thread per
+// output word: copies it (out_values) and/or writes its 8 dequantized values
+// (out_f32); one thread per output scale copies it (out_scales).  An index
+// outside [0, rows) gives a zero row and records BQ4_EINVAL_ARG in *err.
+__global__ void select_rows_kernel(const uint32_t* __restrict__ values, const float* __restrict__ scales,
+                                   int64_t rows, int64_t wpr, int64_t spr, int block, const void* __restrict__ ids,
+                                   int ids64, int64_t n, uint32_t* __restrict__ out_values,
+                                   float* __restrict__ out_scales, float* __restrict__ out_f32, int* err) {
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  const int64_t t0 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  for (int64_t i = t0; i < n * wpr; i += stride) {
+    const int64_t r = i / wpr, w = i - r * wpr;
+    const int64_t id = ids64 ? reinterpret_cast<const int64_t*>(ids)[r] : reinterpret_cast<const int32_t*>(ids)[r];
+    const bool ok = id >= 0 && id < rows;
+    if (!ok && w == 0) atomicCAS(err, 0, (int)BQ4_EINVAL_ARG);
+    const uint32_t word = ok ? __ldg(values + id * wpr + w) : 0u;
+    if (out_values) out_values[i] = word;
+    if (out_f32) {
+      const float sc = ok ? __ldg(scales + id * spr + (w * 8) / block) : 0.0f;
+      float v[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int q = (int)((word >> (4 * j)) & 0xFu);
+        v[j] = (float)(q >= 8 ? q - 16 : q) * sc;
+      }
+      float4* dst = reinterpret_cast<float4*>(out_f32 + r * wpr * 8 + w * 8);
+      dst[0] = make_float4(v[0], v[1], v[2], v[3]);
+      dst[1] = make_float4(v[4], v[5], v[6], v[7]);
+    }
+  }
+  if (out_scales) {
+    for (int64_t i = t0; i < n * spr; i += stride) {
+      const int64_t r = i / spr, c = i - r * spr;
+      const int64_t id = ids64 ? reinterpret_cast<const int64_t*>(ids)[r] : reinterpret_cast<const int32_t*>(ids)[r];
+      out_scales[i] = (id >= 0 && id < rows) ? __ldg(scales + id * spr + c) : 0.0f;
+    }
+  }
+}
+
+cudaError_t launch_select_rows(const uint32_t* values, const float* scales, int64_t rows, int64_t cols, int block,
+                               const void* ids, int ids64, int64_t n, uint32_t* out_values, float* out_scales,
+                               float* out_f32, int* err, cudaStream_t s) {
+  const int64_t wpr = cols / 8, spr = cols / block;
+  const int64_t work = n * wpr > n * spr ? n * wpr : n * spr;
+  select_rows_kernel<<<grid_for(work, 256, current_device()), 256, 0, s>>>(
+      values, scales, rows, wpr, spr, block, ids, ids64, n, out_values, out_scales, out_f32, err);
+  note_launch();
+  return cudaGetLastError();
+}
+
 // One block of 256 threads per row: out[m,:] = x[m,:] * rsqrt(mean(x[m,:]^2)
 // + eps), f32 arithmetic, f32 or f16 in and out.
 __global__ void rms_renorm_kernel(const void* __restrict__ x, int x_f16, int64_t H, int64_t ldx,

@@ -397,6 +397,62 @@ def q_matmul(lhs: torch.Tensor, rhs: QuantizedTensor) -> torch.Tensor:
     return out.reshape(*lead, N)
 
 
+# --------------------------------------------------------------------- quantized row selection
+
+def _stored_rows(qt: QuantizedTensor):
+    """(rows, cols) of the stored rank-2 PackedU32(0) tensor behind qt."""
+    if qt.scheme.store_packed_dim != 0:
+        raise Bq4Error(L.EINVAL_ARG, "quantized row selection requires PackedU32(0) (blocks along the row)")
+    K, N = qt.shape
+    return (N, K) if qt.transposed_view else (K, N)
+
+
+def _ids(indices: torch.Tensor, device: torch.device):
+    if indices.dim() != 1:
+        raise Bq4Error(L.EINVAL_SHAPE, "quantized select indices must be rank one")
+    if indices.dtype not in (torch.int32, torch.int64):
+        raise Bq4Error(L.EINVAL_ARG, f"indices must be int32 or int64, got {indices.dtype}")
+    return indices.to(device).contiguous()
+
+
+def q_select(qt: QuantizedTensor, dim: int, indices: torch.Tensor) -> QuantizedTensor:
+    """QTensorOps::q_select (patches/burn-cubecl-0.21.0/src/ops/qtensor.rs:267-293):
+    rows of the stored rank-2 packed-Q4 tensor, kept packed (values and scales
+    of each selected row copied, nothing widened).  Same restrictions as the
+    reference: dim 0, Q4S, Block level, F32 scales, PackedU32(0).  The result
+    is a plain stored [n, cols] tensor.  An out-of-range index gives a zero row
+    and is reported by poll_device_error()."""
+    if dim != 0:
+        raise Bq4Error(L.EINVAL_ARG, "quantized select only supports rows (dim 0)")
+    if not (qt.scheme.value == "Q4S" and qt.scheme.param == "F32"):
+        raise Bq4Error(L.EINVAL_ARG, "quantized row selection requires packed Q4S with F32 scales")
+    rows, cols = _stored_rows(qt)
+    block = qt.scheme.block
+    dev = qt.values.device
+    ids = _ids(indices, dev)
+    n = ids.shape[0]
+    out_v = torch.empty((n, cols // 8), dtype=torch.int32, device=dev)
+    out_s = torch.empty((n, cols // block), dtype=torch.float32, device=dev)
+    check(L.lib().bq4_q_select_rows(_ptr(qt.values), _ptr(qt.scales), rows, cols, block, _ptr(ids),
+                                    1 if ids.dtype == torch.int64 else 0, n, _ptr(out_v), _ptr(out_s),
+                                    _stream_ptr(dev)))
+    return QuantizedTensor(out_v, out_s, (n, cols), qt.scheme, transposed_view=False)
+
+
+def embedding(qt: QuantizedTensor, indices: torch.Tensor) -> torch.Tensor:
+    """Embedding lookup on a packed-Q4 table: q_select of the rows, then their
+    dequantization (dequantize.rs:6-33), fused in one pass; f32 [n, cols],
+    bit-exact."""
+    rows, cols = _stored_rows(qt)
+    dev = qt.values.device
+    ids = _ids(indices, dev)
+    out = torch.empty((ids.shape[0], cols), dtype=torch.float32, device=dev)
+    check(L.lib().bq4_q_select_rows_dequant(_ptr(qt.values), _ptr(qt.scales), rows, cols, qt.scheme.block,
+                                            _ptr(ids), 1 if ids.dtype == torch.int64 else 0, ids.shape[0],
+                                            _ptr(out), _stream_ptr(dev)))
+    return out
+
+
 # --------------------------------------------------------------------- linear adapters
 
 class Q4Linear:

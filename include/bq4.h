@@ -227,6 +227,28 @@ typedef struct {
                                   plain [K,N] tensor (packed and blocked along N) */
 } bq4_quant_scheme;
 
+/*
+ * Row selection from a packed Q4S matrix without widening it: QTensorOps::q_select on dim 0
+ * (patches/burn-cubecl-0.21.0/src/ops/qtensor.rs:267-293; kernel
+ * patches/burn-cubecl-0.21.0/src/kernel/index/select.rs:83-175), the op behind the Qwen token
+ * and vision-position embedding tables.  The matrix is rows x cols logical values stored as
+ * PackedU32(0) with blocks along the row: values u32 [rows][cols/8], scales f32
+ * [rows][cols/block].  ids: n row indices on the device, int32 (ids_i64 = 0) or int64.
+ * Output: out_values [n][cols/8], out_scales [n][cols/block] (device).  The reference does not
+ * check indices; here an index outside [0, rows) selects a zero row and records BQ4_EINVAL_ARG,
+ * reported by bq4_poll_device_error.
+ */
+BQ4_API bq4_status bq4_q_select_rows(const uint32_t* values, const float* scales, int64_t rows, int64_t cols,
+                                     int32_t block, const void* ids, int32_t ids_i64, int64_t n,
+                                     uint32_t* out_values, float* out_scales, bq4_stream_t stream);
+
+/* The same selection dequantized in the same pass (what an embedding lookup does next with
+ * the selected rows, dequantize.rs:6-33): out f32 [n][cols] = q * scale, bit-exact; out must be
+ * 16-byte aligned. */
+BQ4_API bq4_status bq4_q_select_rows_dequant(const uint32_t* values, const float* scales, int64_t rows, int64_t cols,
+                                             int32_t block, const void* ids, int32_t ids_i64, int64_t n, float* out,
+                                             bq4_stream_t stream);
+
 /* Workspace for bq4_q_matmul: covers an internal prepared copy of rhs. */
 BQ4_API bq4_status bq4_q_matmul_workspace_size(int64_t M, int64_t K, int64_t N,
                                                const bq4_quant_scheme* scheme, size_t* bytes);

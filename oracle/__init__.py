@@ -45,6 +45,7 @@ def lib() -> ctypes.CDLL:
         _lib.orc_quantize_row_up_to128.argtypes = [p, i64, i64, p, p, p]
         _lib.orc_row_block_for.argtypes = [i64]
         _lib.orc_unpack.argtypes = [p, p, i64, i64, i32, i32, p]
+        _lib.orc_select_rows.argtypes = [p, p, i64, i64, i32, p, i64, p, p, p]
         _lib.orc_linear_f64.argtypes = [p, i64, i64, i64, p, i64, p, i32, p, p]
         _lib.orc_linear_f64.restype = None
         _lib.orc_linear_gated_f64.argtypes = [p, i64, i64, i64, p, p, i64, p, p, p]
@@ -117,6 +118,24 @@ def unpack(words: np.ndarray, scales: np.ndarray, K: int, N: int, block: int, la
     if rc:
         raise OracleError(rc, "unpack")
     return out
+
+
+def select_rows(words: np.ndarray, scales: np.ndarray, rows: int, cols: int, block: int, ids) -> tuple:
+    """q_select on dim 0 of a packed [rows, cols] table (PackedU32(0), blocks
+    along the row): (selected words [n, cols/8], scales [n, cols/block],
+    dequantized rows [n, cols] f32, ok).  ok is False when an index was out
+    of range (its row is zero)."""
+    w = np.ascontiguousarray(words, dtype=np.uint32)
+    s = _f32(scales)
+    idx = np.ascontiguousarray(ids, dtype=np.int64)
+    n = idx.shape[0]
+    ow = np.empty((n, cols // 8), dtype=np.uint32)
+    osc = np.empty((n, cols // block), dtype=np.float32)
+    of = np.empty((n, cols), dtype=np.float32)
+    rc = lib().orc_select_rows(_ptr(w), _ptr(s), rows, cols, block, _ptr(idx), n, _ptr(ow), _ptr(osc), _ptr(of))
+    if rc not in (0, 2):
+        raise OracleError(rc, "select_rows")
+    return ow, osc, of, rc == 0
 
 
 def linear_f64(x: np.ndarray, w_kn: np.ndarray, bias=None, act: int = ACT_NONE, aux=None) -> np.ndarray:

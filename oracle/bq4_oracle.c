@@ -196,6 +196,39 @@ int orc_unpack(const uint32_t* words, const float* scales, int64_t K, int64_t N,
     return ORC_OK;
 }
 
+/* Row selection of a packed Q4S matrix [rows][cols], PackedU32(0) with
+ * blocks along the row: words [rows][cols/8], scales [rows][cols/block].
+ * Restates the reference's q_select kernel
+ * (patches/burn-cubecl-0.21.0/src/kernel/index/select.rs:83-108: output word
+ * and scale (r, c) are the source's (indices[r], c)).  out_f32 (optional)
+ * receives the selected rows dequantized as in orc_unpack.  An index outside
+ * [0, rows) yields a zero row and ORC_ESHAPE (the reference reads out of
+ * bounds). */
+int orc_select_rows(const uint32_t* words, const float* scales, int64_t rows, int64_t cols, int32_t block,
+                    const int64_t* ids, int64_t n, uint32_t* out_words, float* out_scales, float* out_f32) {
+    if (!(block == 8 || block == 16 || block == 32 || block == 64 || block == 128)) return ORC_EBLOCK;
+    if (rows <= 0 || cols <= 0 || n < 0 || cols % block != 0) return ORC_ESHAPE;
+    const int64_t wpr = cols / 8, spr = cols / block;
+    int rc = ORC_OK;
+    for (int64_t r = 0; r < n; ++r) {
+        const int64_t id = ids[r];
+        const int ok = id >= 0 && id < rows;
+        if (!ok) rc = ORC_ESHAPE;
+        for (int64_t w = 0; w < wpr; ++w) {
+            const uint32_t word = ok ? words[id * wpr + w] : 0u;
+            if (out_words) out_words[r * wpr + w] = word;
+            if (out_f32) {
+                const float sc = ok ? scales[id * spr + (w * 8) / block] : 0.0f;
+                for (int lane = 0; lane < 8; ++lane)
+                    out_f32[r * cols + w * 8 + lane] = (float)q4_nibble(word, lane) * sc;
+            }
+        }
+        if (out_scales)
+            for (int64_t c = 0; c < spr; ++c) out_scales[r * spr + c] = ok ? scales[id * spr + c] : 0.0f;
+    }
+    return rc;
+}
+
 static inline double act_f64(double v, int32_t act) {
     if (act == ORC_ACT_GELU_TANH) {
         /* Burn Gelu::new_approximate: 0.5 x (1 + tanh(sqrt(2/pi) (x + 0.044715 x^3))) */
