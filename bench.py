@@ -57,6 +57,7 @@ def parse():
                                                           "all-reduces overlap the other chunks' GEMMs)")
     ap.add_argument("--sm-budget", type=int, default=0, help="cap the SMs a GEMM occupies (0: all)")
     ap.add_argument("--rows-only", action="store_true", help="print only the per-config rows (1 GPU)")
+    ap.add_argument("--rows", default=None, help="comma-separated row names to run (with --rows-only)")
     return ap.parse_args()
 
 
@@ -630,7 +631,8 @@ def main():
             peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
         except Exception:
             pass
-        print(json.dumps({"rows": config_rows(torch.device("cuda", 0), peaks)}))
+        names = set(args.rows.split(",")) if args.rows else None
+        print(json.dumps({"rows": config_rows(torch.device("cuda", 0), peaks, names)}))
     elif args.linear or args.gated:
         run_linear(args)
     else:

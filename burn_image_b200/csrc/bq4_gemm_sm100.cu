@@ -328,11 +328,13 @@ __global__ void __launch_bounds__(kWsThreads, 1)
   constexpr uint32_t kAStage = TA ? 0u : NW * 2 * kATileBytes;
   constexpr uint32_t kStage = kAStage + 2 * kBSub;
   constexpr uint32_t kPartCols = NW * BT;
-  constexpr int kNP = TA ? 1 : 512 / kPartCols;   // partial buffers in TMEM
+  // partial buffers in TMEM: TA keeps 256 columns for them (one 256-token
+  // accumulator, or two 128-token partials for exact numerics)
+  constexpr int kNP = TA ? 256 / kPartCols : 512 / kPartCols;
   constexpr uint32_t kACol0 = kNP * kPartCols;    // TA: first A-slot column
   constexpr int kCols = BT / 4;          // token columns per scaler thread
   static_assert(TA || kNP >= 2, "at least double buffering");
-  static_assert(!TA || (NW == 1 && kACol0 + 64 <= 512), "TMEM operand A: one weight, room for a slot");
+  static_assert(!TA || (NW == 1 && kACol0 == 256 && BT >= 128), "TMEM operand A: one weight, slots from column 256");
   static_assert(kCols % 16 == 0, "scaler column split");
 
   const int S = a.stages, RS = a.rs;
@@ -543,7 +545,7 @@ __global__ void __launch_bounds__(kWsThreads, 1)
               uint32_t v[16];
 #pragma unroll
               for (int j = 0; j < 4; ++j) {
-                const uint4 e = expand_word(wv[h * 4 + j], sc[0][h * 4 + j]);
+                const uint4 e = a.exact ? expand_word_exact(wv[h * 4 + j]) : expand_word(wv[h * 4 + j], sc[0][h * 4 + j]);
                 v[4 * j] = e.x; v[4 * j + 1] = e.y; v[4 * j + 2] = e.z; v[4 * j + 3] = e.w;
               }
               ptx::tmem_st_32x32b_x16(t_a + (uint32_t)h * 16, v);
@@ -889,39 +891,16 @@ int device_is_sm100(int device) {
   return major == 10 && minor == 0;
 }
 
-bq4_status plan_gemm(const bq4_weight* w, int nw, int64_t M, int device, GemmPlan* p) {
-  if (M <= 0) return set_error(BQ4_EINVAL_SHAPE, "M must be positive (got %lld)", (long long)M);
-  if (M > (int64_t)1 << 30) return set_error(BQ4_EINVAL_SHAPE, "M too large");
-  memset(p, 0, sizeof(*p));
-  p->nw = nw;
-  // Numerics: blocks of 64/128 keep q exact in f16 and multiply the f32
-  // partial of each K block by its scale (exact weights); smaller blocks
-  // stage f16(q * f16(scale)) (folded); N-packed sources are pre-expanded.
-  p->pre = w->h != nullptr ? 1 : 0;
-  const int mode = numerics_mode();
-  p->exact = (!p->pre && w->block >= 64 &&
-              (mode == BQ4_NUMERICS_EXACT || (mode == BQ4_NUMERICS_AUTO && M <= kAutoExactMaxM)))
-                 ? 1 : 0;
-  // BQ4_FORCE_FOLDED=1 selects folded staging for any block (tests compare
-  // both formulations on the same shapes).
-  if (const char* f = getenv("BQ4_FORCE_FOLDED"))
-    if (f[0] == '1') p->exact = 0;
-  if (nw == 1)
-    p->bt = M > 128 ? 256 : (M > 64 ? 128 : 64);
-  else
-    p->bt = M > 64 ? 128 : 64;
-  // BQ4_FORCE_BT=64|128|256 pins the token tile (tuning).
-  if (const char* f = getenv("BQ4_FORCE_BT")) {
-    const int v = atoi(f);
-    if (v == 64 || v == 128 || (v == 256 && nw == 1)) p->bt = v;
-  }
+// Plan for one token-tile size; *cost is the estimated makespan in µs.
+static bq4_status plan_for_bt(const bq4_weight* w, int nw, int64_t M, int device, int bt, GemmPlan* p,
+                              double* cost) {
+  p->bt = bt;
   p->mtiles = (int)((M + p->bt - 1) / p->bt);
   p->ntiles = (int)w->ntiles;
   int sms = device_sm_count(device);
   if (sm_budget() > 0 && sm_budget() < sms) sms = sm_budget();  // leave SMs to other streams
   const int tiles = p->mtiles * p->ntiles;
-  const int nkc = (int)w->nkc;
-  const int nks = nkc / 2;  // 128-K stages
+  const int nks = (int)w->nkc / 2;  // 128-K stages
 
   // Shared memory: operand ring of 128-K stages (A + B) as deep as fits
   // (2..4 stages) next to a raw ring of 1..4 stages.
@@ -930,9 +909,14 @@ bq4_status plan_gemm(const bq4_weight* w, int nw, int64_t M, int device, GemmPla
   p->raw_w_bytes = p->pre ? 16u : 2 * kRawQBytes + p->raw_s_bytes;
   // Operand A in TMEM (folded numerics, one weight, 256-token tiles): shared
   // memory then holds only token tiles.  BQ4_NO_TA=1 keeps A in shared memory.
-  p->ta = (!p->exact && !p->pre && nw == 1 && p->bt == 256 && !getenv("BQ4_NO_TA")) ? 1 : 0;
+  // Exact numerics need two TMEM partials, which leave room for A slots only
+  // at 128-token tiles (BQ4_EXACT_TA=1 enables that combination).
+  p->ta = (!p->pre && nw == 1 && !getenv("BQ4_NO_TA") &&
+           ((!p->exact && p->bt == 256) || (p->exact && p->bt == 128 && getenv("BQ4_EXACT_TA"))))
+              ? 1 : 0;
   const size_t stage_bytes = (p->ta ? 0 : (size_t)nw * 2 * kATileBytes) + 2 * (size_t)p->bt * 128;
   const int max_stages = p->ta ? (512 - 256) / 64 : 4;  // TA: one 64-column TMEM A slot per stage
+  const int np = p->ta ? 256 / p->bt : 512 / (nw * p->bt);  // TMEM partial buffers of the kernel
   const size_t raw_stage = (size_t)nw * p->raw_w_bytes;
   const size_t budget = 227 * 1024 - 1024 /*align*/ - 512 /*barriers*/;
   int S = 0, RS = 0;
@@ -961,32 +945,34 @@ bq4_status plan_gemm(const bq4_weight* w, int nw, int64_t M, int device, GemmPla
   // Lockstep partial handoff: exact 128-blocks (one segment per stage) and
   // at most as many stages as TMEM partial buffers, so stage s always
   // accumulates into partial s.
-  p->lockstep = (p->exact && w->block == 128 && S <= 512 / (nw * p->bt)) ? 1 : 0;
+  p->lockstep = (p->exact && w->block == 128 && S <= np) ? 1 : 0;
   if (getenv("BQ4_NO_LOCKSTEP")) p->lockstep = 0;
-  const int np = 512 / (nw * p->bt);
   p->smem_bytes = 1024 + (size_t)S * stage_bytes + (size_t)RS * raw_stage +
                   (size_t)(2 * S + 2 * RS + 2 * np) * 8 + 16;
 
-  // Split-K factor: minimise an estimated makespan (chunks per split plus a
-  // pipeline fill of ~3 chunks per unit, plus the cluster reduction).  The
+  // Split-K factor: minimise the estimated makespan (µs, measured on B200):
+  // waves x (128-K stages per unit x stage time + unit fill + the cluster
+  // reduction, whose distributed-shared-memory traffic grows with BT).  The
   // splits of a tile form one thread-block cluster (at most 8 CTAs, the
   // portable limit), and split-K is only used when every cluster is
   // co-resident (one wave); multi-wave work uses whole-K units.
+  const double t_stage = (p->bt == 256 ? 1.1 : (p->bt == 128 ? 0.8 : 0.7)) * (nw == 2 ? 1.6 : 1.0);
+  const double t_red = 0.018 * p->bt * nw + 1.0;
   int best_s = 1;
   double best_t = 1e30;
   const int max_s = nks < kMaxSplit ? nks : kMaxSplit;
   for (int s = 1; s <= max_s; ++s) {
     const int units = tiles * s;
     if (s > 1 && (units > s * cluster_capacity(p->bt, nw, s, p->smem_bytes, device) || units > sms)) continue;
+    if (s > 1 && (size_t)s * nw * split_cols_max(p->bt, s) * 128 * 4 > (size_t)S * stage_bytes) continue;
     const int waves = (units + sms - 1) / sms;
-    const double per_unit = (double)nkc / s + 3.0;  // chunks
-    const double fixup = s > 1 ? 1.0 + 0.25 * s : 0.0;
-    const double t = waves * (per_unit + fixup);
+    const double t = waves * ((nks + s - 1) / s * t_stage + 1.0 + (s > 1 ? t_red : 0.0));
     if (t < best_t - 1e-9) {
       best_t = t;
       best_s = s;
     }
   }
+  *cost = best_t + 2.0;
   // BQ4_FORCE_KSPLIT=s pins the split-K factor (clamped to [1, min(stages,
   // 8)] and to what one wave of clusters holds).
   if (const char* f = getenv("BQ4_FORCE_KSPLIT")) {
@@ -1015,6 +1001,51 @@ bq4_status plan_gemm(const bq4_weight* w, int nw, int64_t M, int device, GemmPla
   p->xh_bytes = align_up((size_t)M * (size_t)w->Kp * 2, 256);
   p->workspace_bytes = p->xh_bytes;
   return BQ4_OK;
+}
+
+
+bq4_status plan_gemm(const bq4_weight* w, int nw, int64_t M, int device, GemmPlan* p) {
+  if (M <= 0) return set_error(BQ4_EINVAL_SHAPE, "M must be positive (got %lld)", (long long)M);
+  if (M > (int64_t)1 << 30) return set_error(BQ4_EINVAL_SHAPE, "M too large");
+  memset(p, 0, sizeof(*p));
+  p->nw = nw;
+  // Numerics: blocks of 64/128 keep q exact in f16 and multiply the f32
+  // partial of each K block by its scale (exact weights); smaller blocks
+  // stage f16(q * f16(scale)) (folded); N-packed sources are pre-expanded.
+  p->pre = w->h != nullptr ? 1 : 0;
+  const int mode = numerics_mode();
+  p->exact = (!p->pre && w->block >= 64 &&
+              (mode == BQ4_NUMERICS_EXACT || (mode == BQ4_NUMERICS_AUTO && M <= kAutoExactMaxM)))
+                 ? 1 : 0;
+  // BQ4_FORCE_FOLDED=1 selects folded staging for any block (tests compare
+  // both formulations on the same shapes).
+  if (const char* f = getenv("BQ4_FORCE_FOLDED"))
+    if (f[0] == '1') p->exact = 0;
+  // Token tile: every candidate up to 2M (64 always) is planned and costed;
+  // BQ4_FORCE_BT=64|128|256 pins it (tuning).
+  int forced = 0;
+  if (const char* f = getenv("BQ4_FORCE_BT")) {
+    const int v = atoi(f);
+    if (v == 64 || v == 128 || (v == 256 && nw == 1)) forced = v;
+  }
+  const GemmPlan base = *p;
+  double best = 1e300;
+  bool have = false;
+  bq4_status last = BQ4_OK;
+  for (int bt : {256, 128, 64}) {
+    if (nw == 2 && bt == 256) continue;
+    if (forced ? bt != forced : (bt != 64 && bt > 2 * M)) continue;
+    GemmPlan cand = base;
+    double cost = 0.0;
+    last = plan_for_bt(w, nw, M, device, bt, &cand, &cost);
+    if (last != BQ4_OK) continue;
+    if (!have || cost < best - 1e-9) {
+      *p = cand;
+      best = cost;
+      have = true;
+    }
+  }
+  return have ? BQ4_OK : (last != BQ4_OK ? last : set_error(BQ4_EUNSUPPORTED, "no plan for this shape"));
 }
 
 bq4_status run_gemm(const GemmPlan& plan, const bq4_weight* const* ws, const void* x, int64_t M,
@@ -1081,7 +1112,8 @@ bq4_status run_gemm(const GemmPlan& plan, const bq4_weight* const* ws, const voi
 
   bool ok_regs = true;
   if (plan.nw == 1) {
-    if (plan.ta) e = launch_ws<256, 1, true>(plan, tmap, args, stream, &ok_regs);
+    if (plan.ta && plan.bt == 256) e = launch_ws<256, 1, true>(plan, tmap, args, stream, &ok_regs);
+    else if (plan.ta) e = launch_ws<128, 1, true>(plan, tmap, args, stream, &ok_regs);
     else if (plan.bt == 256) e = launch_ws<256, 1>(plan, tmap, args, stream, &ok_regs);
     else if (plan.bt == 128) e = launch_ws<128, 1>(plan, tmap, args, stream, &ok_regs);
     else e = launch_ws<64, 1>(plan, tmap, args, stream, &ok_regs);
