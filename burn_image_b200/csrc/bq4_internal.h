@@ -115,7 +115,7 @@ bq4_status run_gemm(const GemmPlan& plan, const bq4_weight* const* ws, const voi
 
 // Operand staging policy (bq4_numerics); AUTO keeps exact weights up to
 // this many rows.
-constexpr int64_t kAutoExactMaxM = 1024;
+constexpr int64_t kAutoExactMaxM = 256;
 int numerics_mode();
 void set_numerics_mode(int mode);
 // Resident-CTA cap for GEMM launches (0 = every SM).

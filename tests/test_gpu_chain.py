@@ -71,6 +71,12 @@ def test_rms_renorm_matches_torch():
     assert (out16.double() - ref).abs().max().item() < 2e-3  # one f16 rounding of |v| < 8
     ref16 = d.half().double() * torch.rsqrt(d.half().double().pow(2).mean(-1, keepdim=True) + 1e-6)
     assert (in16.double() - ref16).abs().max().item() < 1e-5
+    # an unaligned column slice (width 3071) takes the scalar kernel
+    ds = d[:, 1:]
+    refs = ds.double() * torch.rsqrt(ds.double().pow(2).mean(-1, keepdim=True) + 1e-6)
+    outs = q4.rms_renorm(ds, torch.empty((517, 3071), device=DEV))
+    torch.cuda.synchronize()
+    assert (outs.double() - refs).abs().max().item() < 1e-5
 
 
 def test_chained_stack_matches_float32_stack():
