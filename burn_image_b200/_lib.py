@@ -53,6 +53,8 @@ SIGNATURES = {
     "bq4_poll_device_error": (_st, []),
     "bq4_set_numerics": (_st, [_i32]),
     "bq4_set_sm_budget": (_st, [_i32]),
+    "bq4_parse_stored_dtype": (_st, [ctypes.c_char_p, ctypes.POINTER(_i32), ctypes.POINTER(_i32)]),
+    "bq4_weight_prepare_payload": (_st, [_p, _sz, _i64, _i64, ctypes.c_char_p, _i32, _i32, ctypes.POINTER(_p)]),
     "bq4_q_select_rows": (_st, [_p, _p, _i64, _i64, _i32, _p, _i32, _i64, _p, _p, _p]),
     "bq4_q_select_rows_dequant": (_st, [_p, _p, _i64, _i64, _i32, _p, _i32, _i64, _p, _p]),
     "bq4_rms_renorm": (_st, [_p, _i32, _i64, _i64, _i64, _p, _i32, _i64, ctypes.c_float, _p]),

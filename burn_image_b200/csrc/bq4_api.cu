@@ -352,6 +352,68 @@ bq4_status bq4_q_select_rows_dequant(const uint32_t* values, const float* scales
   return select_rows(values, scales, rows, cols, block, ids, ids_i64, n, nullptr, nullptr, out, stream);
 }
 
+bq4_status bq4_parse_stored_dtype(const char* stored_dtype, int32_t* block, int32_t* axis) {
+  if (!stored_dtype || !block || !axis) return set_error(BQ4_EINVAL_ARG, "NULL argument");
+  int b = 0, n = 0;
+  int ax = -1;
+  if (sscanf(stored_dtype, "q4s-block%dx1-f32-packed-axis1%n", &b, &n) == 1 && stored_dtype[n] == '\0') {
+    ax = 1;
+  } else if (sscanf(stored_dtype, "q4s-block%d-f32-packed-axis0%n", &b, &n) == 1 && stored_dtype[n] == '\0') {
+    ax = 0;
+  }
+  if (ax < 0 || !(b == 8 || b == 16 || b == 32 || b == 64 || b == 128))
+    return set_error(BQ4_EINVAL_ARG, "stored dtype '%s' is not a packed-Q4 (Q4S, F32 scales) spelling",
+                     stored_dtype);
+  // the parse must round-trip to the exact spelling (no leading zeros or signs)
+  char canon[64];
+  snprintf(canon, sizeof(canon), ax ? "q4s-block%dx1-f32-packed-axis1" : "q4s-block%d-f32-packed-axis0", b);
+  if (strcmp(canon, stored_dtype) != 0)
+    return set_error(BQ4_EINVAL_ARG, "stored dtype '%s' is not in canonical form", stored_dtype);
+  *block = b;
+  *axis = ax;
+  return BQ4_OK;
+}
+
+bq4_status bq4_weight_prepare_payload(const void* payload, size_t nbytes, int64_t rows, int64_t cols,
+                                      const char* stored_dtype, int32_t transposed_view, int32_t device,
+                                      bq4_weight** out) {
+  int32_t block = 0, axis = 0;
+  bq4_status st = bq4_parse_stored_dtype(stored_dtype, &block, &axis);
+  if (st) return st;
+  if (!payload || !out) return set_error(BQ4_EINVAL_ARG, "payload/out is NULL");
+  if (rows <= 0 || cols <= 0) return set_error(BQ4_EINVAL_SHAPE, "shape [%lld, %lld]", (long long)rows, (long long)cols);
+  const int64_t elems = rows * cols;
+  if (elems % block || elems % 8 || elems / rows != cols)
+    return set_error(BQ4_EINVAL_SHAPE, "shape [%lld, %lld] does not hold whole blocks of %d", (long long)rows,
+                     (long long)cols, (int)block);
+  const size_t words_bytes = (size_t)(elems / 2), want = words_bytes + (size_t)(elems / block) * 4;
+  if (nbytes != want)
+    return set_error(BQ4_EINVAL_SHAPE, "payload of %zu bytes; shape [%lld, %lld] block %d needs %zu", nbytes,
+                     (long long)rows, (long long)cols, (int)block, want);
+  int64_t K, N;
+  bq4_layout layout;
+  if (axis == 1) {
+    K = rows; N = cols; layout = BQ4_LAYOUT_ROW;          // stored [K, N], packed along K
+  } else if (transposed_view) {
+    K = cols; N = rows; layout = BQ4_LAYOUT_COL;          // stored [N, K] seen as [K, N]
+  } else {
+    K = rows; N = cols; layout = BQ4_LAYOUT_NPACKED;      // plain stored [K, N], packed along N
+  }
+  const uint8_t* p8 = static_cast<const uint8_t*>(payload);
+  // a host payload may sit at any byte offset of a file buffer: copy it to
+  // 4-byte alignment first (device payloads must already be aligned)
+  std::vector<uint32_t> aligned_copy;
+  if (!is_device_ptr(payload) && !aligned(payload, 4)) {
+    aligned_copy.resize((nbytes + 3) / 4);
+    memcpy(aligned_copy.data(), payload, nbytes);
+    p8 = reinterpret_cast<const uint8_t*>(aligned_copy.data());
+  } else if (!aligned(payload, 4)) {
+    return set_error(BQ4_EALIGN, "device payload not 4-byte aligned");
+  }
+  return bq4_weight_prepare(reinterpret_cast<const uint32_t*>(p8), reinterpret_cast<const float*>(p8 + words_bytes),
+                            K, N, block, layout, device, out);
+}
+
 bq4_status bq4_set_sm_budget(int32_t sms) {
   if (sms < 0) return set_error(BQ4_EINVAL_ARG, "sm budget %d is negative", (int)sms);
   set_sm_budget(sms);

@@ -56,6 +56,25 @@ class PackedQ4:
     def to_bytes(self) -> bytes:
         return self.words.astype("<u4").tobytes() + self.scales.astype("<f4").tobytes()
 
+    @property
+    def stored_dtype(self) -> str:
+        """The sealed-inventory spelling of this tensor's storage contract."""
+        return q4s_stored_dtype(self.scheme.block, self.scheme.store_packed_dim)
+
+
+def q4s_stored_dtype(block: int, axis: int) -> str:
+    """crates/burn_boogu/src/artifacts.rs:527-537 -- the stable inventory
+    spelling of one Q4S / F32-scale storage contract."""
+    return f"q4s-block{block}-f32-packed-axis0" if axis == 0 else f"q4s-block{block}x1-f32-packed-axis1"
+
+
+def parse_stored_dtype(stored_dtype: str) -> tuple:
+    """(block, packed axis) of a packed-Q4 inventory spelling (through the C
+    ABI's parser); raises for any other dtype."""
+    block, axis = ctypes.c_int32(), ctypes.c_int32()
+    check(L.lib().bq4_parse_stored_dtype(stored_dtype.encode(), ctypes.byref(block), ctypes.byref(axis)))
+    return block.value, axis.value
+
 
 def quantize_q4s_block128_f32(values, shape: Sequence[int]) -> PackedQ4:
     """Column layout (Qwen, ``PackedU32(0)``, ``Block([128])``): the last axis
@@ -176,6 +195,36 @@ class PreparedQ4Weight:
                                   ctypes.byref(nb)))
         self.K, self.N, self.block, self.layout, self.device_bytes = k.value, n.value, b.value, lay.value, nb.value
         self.device = dev
+
+    @classmethod
+    def from_payload(cls, payload, shape: tuple, stored_dtype: str, transposed_view: bool = True,
+                     device=None) -> "PreparedQ4Weight":
+        """Loader hook: prepare straight from a stored tensor's QFloat payload
+        (the reference's byte stream: packed words, then F32 scales), its
+        stored [rows, cols] shape and inventory dtype (bq4_weight_prepare_payload).
+        ``transposed_view`` (axis-0 spellings only): the stored tensor is the
+        [N, K] weight the matmul sees transposed (Qwen), else a plain [K, N]."""
+        dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+        if isinstance(payload, torch.Tensor):
+            buf, nbytes = payload, payload.numel() * payload.element_size()
+            ptr = ctypes.c_void_p(payload.data_ptr())
+        else:
+            buf = np.frombuffer(bytes(payload), dtype=np.uint8)
+            nbytes = buf.size
+            ptr = ctypes.c_void_p(buf.ctypes.data)
+        rows, cols = int(shape[0]), int(shape[1])
+        handle = ctypes.c_void_p()
+        check(L.lib().bq4_weight_prepare_payload(ptr, nbytes, rows, cols, stored_dtype.encode(),
+                                                 1 if transposed_view else 0, dev.index, ctypes.byref(handle)))
+        del buf
+        self = cls.__new__(cls)
+        self._h = handle
+        k, n, b, lay, nb = ctypes.c_int64(), ctypes.c_int64(), ctypes.c_int32(), ctypes.c_int32(), ctypes.c_size_t()
+        check(L.lib().bq4_weight_info(handle, ctypes.byref(k), ctypes.byref(n), ctypes.byref(b), ctypes.byref(lay),
+                                      ctypes.byref(nb)))
+        self.K, self.N, self.block, self.layout, self.device_bytes = k.value, n.value, b.value, lay.value, nb.value
+        self.device = dev
+        return self
 
     @classmethod
     def from_packed(cls, packed: PackedQ4, device=None, stored: str = "nk") -> "PreparedQ4Weight":

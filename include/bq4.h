@@ -249,6 +249,29 @@ BQ4_API bq4_status bq4_q_select_rows_dequant(const uint32_t* values, const float
                                              int32_t block, const void* ids, int32_t ids_i64, int64_t n, float* out,
                                              bq4_stream_t stream);
 
+/*
+ * Stored-dtype spelling of a packed-Q4 tensor in the reference's sealed artifact inventory
+ * (q4s_stored_dtype, crates/burn_boogu/src/artifacts.rs:527-537): "q4s-block{b}-f32-packed-axis0"
+ * (PackedU32(0), Block([b])) or "q4s-block{b}x1-f32-packed-axis1" (PackedU32(1), Block([b,1])).
+ * Returns the block and packed axis; BQ4_EINVAL_ARG for any other spelling.
+ */
+BQ4_API bq4_status bq4_parse_stored_dtype(const char* stored_dtype, int32_t* block, int32_t* axis);
+
+/*
+ * Loader hook: prepare a weight straight from a stored tensor's QFloat payload, the byte
+ * stream the reference writes (crates/burn_qwen3_vl/src/artifacts.rs:1356-1363: every packed
+ * u32 word little-endian, then every f32 scale) and whose size it checks
+ * (crates/burn_qwen3_vl/src/artifacts.rs:1204-1240).  rows x cols is the stored tensor's
+ * shape and stored_dtype its inventory spelling.  axis 1: the stored tensor is the [K, N]
+ * weight (Boogu row layout).  axis 0: packed along cols; transposed_view = 1 when the matmul
+ * uses it as the transposed view of a stored [N, K] weight (Qwen), 0 when it is a plain
+ * [K, N] weight.  The payload is host or device memory; nbytes must equal
+ * rows*cols/2 + rows*cols/block*4 (BQ4_EINVAL_SHAPE otherwise).
+ */
+BQ4_API bq4_status bq4_weight_prepare_payload(const void* payload, size_t nbytes, int64_t rows, int64_t cols,
+                                              const char* stored_dtype, int32_t transposed_view, int32_t device,
+                                              bq4_weight** out);
+
 /* Workspace for bq4_q_matmul: covers an internal prepared copy of rhs. */
 BQ4_API bq4_status bq4_q_matmul_workspace_size(int64_t M, int64_t K, int64_t N,
                                                const bq4_quant_scheme* scheme, size_t* bytes);
