@@ -182,9 +182,11 @@ class DiTQ4Stack:
             self.bufs[name] = t
         return t
 
-    def forward(self, x: torch.Tensor, on_linear=None) -> torch.Tensor:
+    def forward(self, x: torch.Tensor, on_linear=None, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """The stack on x [M, hidden]; the renormalised float32 output goes to
+        ``out`` when given (else an internal buffer reused by the next call)."""
         if self.act_dtype == torch.float16:
-            return self._forward_chained(x, on_linear)
+            return self._forward_chained(x, on_linear, out)
         M = x.shape[0]
         P = self.size
         qkv_local = self.qkv // P
@@ -200,10 +202,13 @@ class DiTQ4Stack:
             d = self._buf("down", (M, self.hidden))
             _timed(on_linear, "down", lambda: layer["down"].forward(u, out=d))
             x = d * torch.rsqrt(d.pow(2).mean(-1, keepdim=True) + 1e-6)
+        if out is not None:
+            out.copy_(x)
+            return out
         return x
 
 
-    def _forward_chained(self, x: torch.Tensor, on_linear=None) -> torch.Tensor:
+    def _forward_chained(self, x: torch.Tensor, on_linear=None, out: Optional[torch.Tensor] = None) -> torch.Tensor:
         """The stack with float16 activations between linears (float32 where
         a row-parallel partial sum is reduced), in token chunks.  Per block and chunk: [renorm of the previous block's output,
         qkv, o (row-parallel partial, all-reduce enqueued)] then [wait, up,
@@ -244,7 +249,8 @@ class DiTQ4Stack:
                 _timed(on_linear, "up", lambda: layer["up"].forward_ex(o[a:b], out=u[a:b]))
                 pending[c] = _timed(on_linear, "down",
                                     lambda: layer["down"].forward_ex(u[a:b], out=d[a:b], async_op=True))
-        out = self._buf("out32", (M, self.hidden), torch.float32)
+        if out is None:
+            out = self._buf("out32", (M, self.hidden), torch.float32)
         for c, (a, b) in enumerate(bounds):
             if pending[c] is not None:
                 pending[c].wait()
