@@ -440,9 +440,14 @@ bq4_status bq4_rms_renorm(const void* x, bq4_dtype x_dtype, int64_t M, int64_t H
 bq4_status bq4_linear_ex_workspace_size(const bq4_weight* w, int64_t M, bq4_dtype x_dtype, size_t* bytes) {
   if (x_dtype != BQ4_DTYPE_F32 && x_dtype != BQ4_DTYPE_F16)
     return set_error(BQ4_EINVAL_ARG, "x_dtype %d unknown", (int)x_dtype);
-  bq4_status st = bq4_linear_workspace_size(w, M, bytes);
-  if (st == BQ4_OK && x_dtype == BQ4_DTYPE_F16) *bytes = 0;
-  return st;
+  bq4_status st = check_weight(w, "w");
+  if (st) return st;
+  if (!bytes) return set_error(BQ4_EINVAL_ARG, "bytes is NULL");
+  GemmPlan plan;
+  st = plan_gemm(w, 1, M, w->device, &plan);
+  if (st) return st;
+  *bytes = x_dtype == BQ4_DTYPE_F16 ? plan.partial_bytes : plan.workspace_bytes;
+  return BQ4_OK;
 }
 
 bq4_status bq4_linear_ex(const bq4_weight* w, const void* x, bq4_dtype x_dtype, int64_t M, int64_t ldx,
@@ -473,7 +478,7 @@ bq4_status bq4_linear_ex(const bq4_weight* w, const void* x, bq4_dtype x_dtype, 
   GemmPlan plan;
   st = plan_gemm(w, 1, M, w->device, &plan);
   if (st) return st;
-  const size_t need = x16 ? 0 : plan.workspace_bytes;
+  const size_t need = x16 ? plan.partial_bytes : plan.workspace_bytes;
   if (need) {
     if (!workspace) return set_error(BQ4_EWORKSPACE, "workspace is NULL");
     if (!aligned(workspace, 256)) return set_error(BQ4_EALIGN, "workspace not 256-byte aligned");

@@ -160,6 +160,7 @@ struct WsArgs {
   const uint16_t* h[2];
   const float* bias[2];
   const float* aux;
+  float* partials;         // split-K: f32 partial tiles [tiles][ksplit][NW][BT][128] (workspace)
   void* y;                 // f32 or f16 (y_f16), row pitch ldy elements
   int y_f16, ldy;
   int M, N;
@@ -215,49 +216,34 @@ __device__ __forceinline__ bool ws_seg_last(int kc, int kc1, int cpb) {
 }
 
 // Split-K reduction across the cluster (one CTA per split, cluster rank =
-// split).  CTA r owns the token columns [c0_r, c1_r), c0_r = BT*r/splits.
-// After the main loop each split pushes its f32 partial tile, column by
-// column, into the owner's receive buffer recv[src][w][col - c0_r][128]
-// (in the owner's idle operand ring) with posted distributed-shared-memory
-// stores; after a cluster barrier each owner sums its columns over the
-// splits in rank order (deterministic) from its own shared memory and runs
-// the epilogue.
-__host__ __device__ constexpr int split_cols_max(int bt, int spl) { return (bt + spl - 1) / spl; }
-
-__device__ __forceinline__ int split_owner(int col, int bt, int spl) { return ((col + 1) * spl - 1) / bt; }
-
-// Push this thread's partial columns (row `row`, token columns col0..) to
-// their owners.
+// split).  After the main loop each split writes its f32 partial tile to its
+// own slot of the workspace, partials[tile][split][w][col][row] (coalesced
+// along the features); after one cluster barrier CTA r owns the token columns
+// [c0_r, c1_r), c0_r = BT*r/splits, sums them over the splits in rank order
+// (deterministic) reading through L2, and runs the epilogue.  (An exchange
+// through distributed shared memory moved only ~28 GB/s per SM.)
 template <int BT, int NW, int kCols>
-__device__ __forceinline__ void split_push(const WsArgs& a, const uint8_t* ring, const float (&acc)[NW][kCols],
-                                           int row, int col0) {
-  const int SPL = a.ksplit;
-  const int src = (int)ptx::cluster_ctarank();
-  const int ncm = split_cols_max(BT, SPL);
-  const uint32_t base = ptx::smem_u32(ring);
+__device__ __forceinline__ void split_publish(const WsArgs& a, int tile, int split, const float (&acc)[NW][kCols],
+                                              int row, int col0) {
+  float* part = a.partials + ((size_t)tile * a.ksplit + split) * NW * BT * 128;
 #pragma unroll
-  for (int j = 0; j < kCols; ++j) {
-    const int col = col0 + j;
-    const int r = split_owner(col, BT, SPL);
-    const int cc = col - BT * r / SPL;
+  for (int w = 0; w < NW; ++w)
 #pragma unroll
-    for (int w = 0; w < NW; ++w) {
-      const uint32_t off = (uint32_t)((((src * NW + w) * ncm + cc) * 128 + row) * 4);
-      ptx::st_shared_cluster_f32(ptx::mapa_shared(base + off, (uint32_t)r), acc[w][j]);
-    }
-  }
+    for (int j = 0; j < kCols; ++j) __stcg(part + ((size_t)w * BT + col0 + j) * 128 + row, acc[w][j]);
+  __threadfence();
 }
 
 // Owner side: warp w takes every 16th owned column from c0 + w, lane l the
-// features 4l..4l+3 (bias loaded once).
+// features 4l..4l+3 (bias loaded once); all splits' loads of a column are in
+// flight before they are summed.
 template <int BT, int NW>
-__device__ __forceinline__ void split_reduce_epilogue(const WsArgs& a, const uint8_t* ring) {
+__device__ __forceinline__ void split_reduce_epilogue(const WsArgs& a) {
   const int SPL = a.ksplit;
   const int rank = (int)ptx::cluster_ctarank();
+  const int tile = (int)blockIdx.x / SPL;
   int mtile, ntile;
-  ws_tile(a, (int)blockIdx.x / SPL, mtile, ntile);
+  ws_tile(a, tile, mtile, ntile);
   const int c0 = BT * rank / SPL, c1 = BT * (rank + 1) / SPL;
-  const int ncm = split_cols_max(BT, SPL);
   const int r4 = (int)(threadIdx.x & 31) * 4;
   const int n = ntile * 128 + r4;
   if (n >= a.N) return;
@@ -269,7 +255,7 @@ __device__ __forceinline__ void split_reduce_epilogue(const WsArgs& a, const uin
       const int nn = n + i < a.N ? n + i : a.N - 1;
       b[w][i] = a.bias[w] ? __ldg(a.bias[w] + nn) : 0.0f;
     }
-  const float* recv = reinterpret_cast<const float*>(ring);
+  const float* part = a.partials + (size_t)tile * SPL * NW * BT * 128;
   const int act = a.act;
   for (int col = c0 + (int)(threadIdx.x >> 5); col < c1; col += 16) {
     const int m = mtile * BT + col;
@@ -277,12 +263,17 @@ __device__ __forceinline__ void split_reduce_epilogue(const WsArgs& a, const uin
     float v[NW][4];
 #pragma unroll
     for (int w = 0; w < NW; ++w) {
+      float4 t[kMaxSplit];
+#pragma unroll
+      for (int p = 0; p < kMaxSplit; ++p)
+        if (p < SPL)
+          t[p] = __ldcg(reinterpret_cast<const float4*>(part + (((size_t)p * NW + w) * BT + col) * 128 + r4));
       v[w][0] = v[w][1] = v[w][2] = v[w][3] = 0.0f;
-      for (int p = 0; p < SPL; ++p) {
-        const float4 t =
-            *reinterpret_cast<const float4*>(recv + (((size_t)(p * NW + w) * ncm + (col - c0)) * 128 + r4));
-        v[w][0] += t.x; v[w][1] += t.y; v[w][2] += t.z; v[w][3] += t.w;
-      }
+#pragma unroll
+      for (int p = 0; p < kMaxSplit; ++p)
+        if (p < SPL) {
+          v[w][0] += t[p].x; v[w][1] += t[p].y; v[w][2] += t[p].z; v[w][3] += t[p].w;
+        }
     }
     float o[4];
 #pragma unroll
@@ -487,9 +478,8 @@ __global__ void __launch_bounds__(kWsThreads, 1)
       }
       if (!ok) record_error_flag(abort_flag, BQ4_ETIMEOUT);
     }
-    if (a.ksplit > 1) {  // the two cluster barriers of the split reduction
+    if (a.ksplit > 1) {  // the cluster barrier of the split reduction
       __syncwarp();
-      ptx::cluster_sync();
       ptx::cluster_sync();
     }
   } else if (warp >= kWsDqWarp0) {
@@ -572,9 +562,8 @@ __global__ void __launch_bounds__(kWsThreads, 1)
       }
       if (!ok) record_error_flag(abort_flag, BQ4_ETIMEOUT);
     }
-    if (a.ksplit > 1) {  // the two cluster barriers of the split reduction
+    if (a.ksplit > 1) {  // the cluster barrier of the split reduction
       __syncwarp();
-      ptx::cluster_sync();
       ptx::cluster_sync();
     }
   } else {
@@ -586,7 +575,7 @@ __global__ void __launch_bounds__(kWsThreads, 1)
     int pb = 0;
     uint32_t pph = 0;
     bool ok = true;
-    bool split_synced = false;  // this warp has passed the split's two cluster barriers
+    bool split_synced = false;  // this warp has passed the split's cluster barrier
     if (a.lockstep && lane == 0) {
       // both partial buffers start free: the first use of each stage
       for (int i = 0; i < S; ++i) ptx::mbar_arrive(&full[i]);
@@ -632,13 +621,9 @@ __global__ void __launch_bounds__(kWsThreads, 1)
       if (!ok) break;
 
       if (a.ksplit > 1) {
-        // Split-K (the CTA's only unit): barrier 1 -- every CTA of the
-        // cluster has retired its MMAs, so every operand ring is free to
-        // receive; push this split's partial columns to their owners;
-        // barrier 2 -- all pushes landed; reduce the owned columns.
-        __syncwarp();
-        ptx::cluster_sync();
-        split_push<BT, NW, kCols>(a, ring, acc, row, col0);
+        // Split-K (the CTA's only unit): publish this split's partial tile,
+        // then the cluster barrier -- every split's tile is in the workspace.
+        split_publish<BT, NW, kCols>(a, tile, split, acc, row, col0);
         __syncwarp();
         ptx::cluster_sync();
         split_synced = true;
@@ -665,13 +650,12 @@ __global__ void __launch_bounds__(kWsThreads, 1)
       }
     }
     if (!ok) record_error_flag(abort_flag, BQ4_ETIMEOUT);
-    if (split_synced) split_reduce_epilogue<BT, NW>(a, ring);
+    if (split_synced) split_reduce_epilogue<BT, NW>(a);
     if (a.ksplit > 1 && !split_synced) {
-      // Every role of every CTA of the cluster passes the split's two
-      // cluster barriers exactly once (each role branch has its own pair);
-      // a scaler warp that left its loop early passes them here.
+      // Every role of every CTA of the cluster passes the split's cluster
+      // barrier exactly once (each role branch has its own); a scaler warp
+      // that left its loop early passes it here.
       __syncwarp();
-      ptx::cluster_sync();
       ptx::cluster_sync();
     }
   }
@@ -957,14 +941,13 @@ static bq4_status plan_for_bt(const bq4_weight* w, int nw, int64_t M, int device
   // portable limit), and split-K is only used when every cluster is
   // co-resident (one wave); multi-wave work uses whole-K units.
   const double t_stage = (p->bt == 256 ? 1.1 : (p->bt == 128 ? 0.8 : 0.7)) * (nw == 2 ? 1.6 : 1.0);
-  const double t_red = 0.018 * p->bt * nw + 1.0;
+  const double t_red = 0.008 * p->bt * nw + 1.0;
   int best_s = 1;
   double best_t = 1e30;
   const int max_s = nks < kMaxSplit ? nks : kMaxSplit;
   for (int s = 1; s <= max_s; ++s) {
     const int units = tiles * s;
     if (s > 1 && (units > s * cluster_capacity(p->bt, nw, s, p->smem_bytes, device) || units > sms)) continue;
-    if (s > 1 && (size_t)s * nw * split_cols_max(p->bt, s) * 128 * 4 > (size_t)S * stage_bytes) continue;
     const int waves = (units + sms - 1) / sms;
     const double t = waves * ((nks + s - 1) / s * t_stage + 1.0 + (s > 1 ? t_red : 0.0));
     if (t < best_t - 1e-9) {
@@ -982,9 +965,6 @@ static bq4_status plan_for_bt(const bq4_weight* w, int nw, int64_t M, int device
                           tiles * best_s > sms))
       --best_s;
   }
-  // the split's receive buffers must fit the operand ring
-  while (best_s > 1 && (size_t)best_s * nw * split_cols_max(p->bt, best_s) * 128 * 4 > (size_t)S * stage_bytes)
-    --best_s;
   p->ksplit = best_s;
   p->units = tiles * best_s;
   p->cluster = best_s;
@@ -998,8 +978,12 @@ static bq4_status plan_for_bt(const bq4_weight* w, int nw, int64_t M, int device
   // (BQ4_NO_PDL=1 launches it in plain stream order).
   p->pdl = getenv("BQ4_NO_PDL") ? 0 : 1;
 
+  // Workspace: the split-K partial tiles, then the f16 copy of x (callers
+  // passing f16 activations need only the first part).
+  p->partial_bytes =
+      best_s > 1 ? align_up((size_t)tiles * best_s * nw * p->bt * 128 * sizeof(float), 256) : 0;
   p->xh_bytes = align_up((size_t)M * (size_t)w->Kp * 2, 256);
-  p->workspace_bytes = p->xh_bytes;
+  p->workspace_bytes = p->partial_bytes + p->xh_bytes;
   return BQ4_OK;
 }
 
@@ -1055,9 +1039,10 @@ bq4_status run_gemm(const GemmPlan& plan, const bq4_weight* const* ws, const voi
   cudaError_t e = cudaSuccess;
   const void* xh = x;
   int64_t x_pitch = ldx;
+  float* partials = plan.partial_bytes ? static_cast<float*>(workspace) : nullptr;
   if (!io.x_f16) {
     // 1) stage activations as f16 [M][Kp] in the workspace
-    void* dst = workspace;
+    void* dst = static_cast<uint8_t*>(workspace) + plan.partial_bytes;
     e = launch_convert_x(static_cast<const float*>(x), M, w0->K, ldx, w0->Kp, dst, stream);
     if (e != cudaSuccess) return check_cuda(e, "convert_x launch");
     xh = dst;
@@ -1087,6 +1072,7 @@ bq4_status run_gemm(const GemmPlan& plan, const bq4_weight* const* ws, const voi
     args.bias[i] = bias ? bias[i] : nullptr;
   }
   args.aux = aux;
+  args.partials = partials;
   args.y = y;
   args.y_f16 = io.y_f16;
   args.ldy = (int)(io.ldy > 0 ? io.ldy : w0->N);

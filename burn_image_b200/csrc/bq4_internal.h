@@ -94,7 +94,8 @@ struct GemmPlan {
   uint32_t raw_s_bytes;  // scale bytes per weight per raw stage (folded)
   uint32_t raw_w_bytes;  // shared-memory bytes per weight per raw stage
   size_t smem_bytes;
-  size_t xh_bytes;         // the f16 copy of x, the only workspace piece
+  size_t partial_bytes;    // workspace part 1: split-K partial tiles (0 without split)
+  size_t xh_bytes;         // workspace part 2: the f16 copy of x (unused with f16 x)
   size_t workspace_bytes;
 };
 

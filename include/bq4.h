@@ -136,7 +136,8 @@ BQ4_API bq4_status bq4_linear(const bq4_weight* w, const float* x, int64_t M, in
 
 typedef enum { BQ4_DTYPE_F32 = 0, BQ4_DTYPE_F16 = 1 } bq4_dtype;
 
-/* Workspace for bq4_linear_ex: the bq4_linear size for f32 x, 0 for f16 x. */
+/* Workspace for bq4_linear_ex: the bq4_linear size for f32 x; for f16 x only the split-K
+ * partial tiles (0 when the plan does not split K). */
 BQ4_API bq4_status bq4_linear_ex_workspace_size(const bq4_weight* w, int64_t M, bq4_dtype x_dtype,
                                                 size_t* bytes);
 
