@@ -9,8 +9,9 @@
 //
 // One CTA of 896 threads per SM, persistent over (M tile, N tile) units; the
 // warp roles are described above q4_gemm_ws_kernel.  Split-K units of one
-// tile run as one thread-block cluster and reduce their partial tiles
-// through distributed shared memory.
+// tile run as one thread-block cluster: each split writes its partial tile
+// to the workspace, and after one cluster barrier every CTA sums its share
+// of the token columns over the splits, reading through L2.
 //
 // Numerics: activations staged as f16 (round to nearest even), f32
 // accumulation; weights either exact (q in f16, the f32 partial of each K

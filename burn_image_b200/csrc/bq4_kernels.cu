@@ -156,7 +156,7 @@ __global__ void dequant_raw_kernel(const uint32_t* __restrict__ words, const flo
 
 // x f32 [M][ldx] -> xh f16 [M][Kp] with round-to-nearest-even, zero padding
 // K..Kp-1.  Each thread converts 8 consecutive K values into one 16-byte
-// store.  Block 0 also zeroes the split-K tile counters.
+// store.
 __global__ void convert_x_kernel(const float* __restrict__ x, int64_t M, int64_t K, int64_t ldx,
                                  int64_t Kp, uint4* __restrict__ xh, int vec4) {
   // The GEMM that consumes xh is launched as a programmatic dependent: it may

@@ -1,7 +1,7 @@
 // bq4_noalloc.cu -- bq4_linear for callers that cannot allocate device memory.
 //
 // bq4_linear needs a caller-provided workspace (the f16 copy of the
-// activations, split-K counters and partial tiles).  Some callers have no
+// activations and the split-K partial tiles).  Some callers have no
 // way to provide one: a host runtime whose allocator owns all device memory
 // and offers no hook to hand a foreign op a scratch buffer, code that must
 // not call cudaMalloc because it synchronizes the device, or a process that
@@ -14,9 +14,10 @@
 // looked up with cudaGetSymbolAddress once per device (with that device
 // current) on the first call there, and cached.  Calls on one device share
 // the array: two calls that overlap on the GPU (different streams, or
-// different host threads without ordering) race on it.  It holds only the
-// f16 copy of the activations, which every call writes in full before the
-// GEMM reads it, so nothing in it needs to start at zero.
+// different host threads without ordering) race on it.  It holds the f16
+// copy of the activations and the split-K partial tiles; every call writes
+// each of them in full before anything reads it, so nothing in it needs to
+// start at zero.
 #include <cuda_runtime.h>
 
 #include <mutex>
