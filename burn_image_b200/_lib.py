@@ -37,6 +37,7 @@ SIGNATURES = {
     "bq4_weight_info": (_st, [_p, ctypes.POINTER(_i64), ctypes.POINTER(_i64), ctypes.POINTER(_i32),
                               ctypes.POINTER(_i32), ctypes.POINTER(_sz)]),
     "bq4_linear_workspace_size": (_st, [_p, _i64, ctypes.POINTER(_sz)]),
+    "bq4_linear_plan_info": (_st, [_p, _i64, _i32, ctypes.POINTER(_i32), _i32]),
     "bq4_linear": (_st, [_p, _p, _i64, _i64, _p, _i32, _p, _p, _p, _sz, _p]),
     "bq4_linear_noalloc": (_st, [_p, _p, _i64, _i64, _p, _i32, _p, _p, _p]),
     "bq4_linear_ex_workspace_size": (_st, [_p, _i64, _i32, ctypes.POINTER(_sz)]),

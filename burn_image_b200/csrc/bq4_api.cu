@@ -291,6 +291,20 @@ bq4_status bq4_linear_workspace_size(const bq4_weight* w, int64_t M, size_t* byt
   return BQ4_OK;
 }
 
+bq4_status bq4_linear_plan_info(const bq4_weight* w, int64_t M, int32_t gated, int32_t* info, int32_t n) {
+  bq4_status st = check_weight(w, "w");
+  if (st) return st;
+  if (!info || n < 0) return set_error(BQ4_EINVAL_ARG, "info is NULL or n < 0");
+  DeviceGuard guard(w->device);
+  GemmPlan plan;
+  st = plan_gemm(w, gated ? 2 : 1, M, w->device, &plan);
+  if (st) return st;
+  const int32_t v[9] = {plan.bt, plan.ksplit, plan.grid, plan.exact, plan.ta, plan.stages, plan.sk_tiles,
+                        plan.dp_tiles, (int32_t)(plan.workspace_bytes / 256)};
+  for (int32_t i = 0; i < n && i < 9; ++i) info[i] = v[i];
+  return BQ4_OK;
+}
+
 bq4_status bq4_linear(const bq4_weight* w, const float* x, int64_t M, int64_t ldx,
                       const float* bias, bq4_act act, const float* aux, float* y, void* workspace,
                       size_t workspace_bytes, bq4_stream_t stream) {
@@ -446,7 +460,7 @@ bq4_status bq4_linear_ex_workspace_size(const bq4_weight* w, int64_t M, bq4_dtyp
   GemmPlan plan;
   st = plan_gemm(w, 1, M, w->device, &plan);
   if (st) return st;
-  *bytes = x_dtype == BQ4_DTYPE_F16 ? plan.partial_bytes : plan.workspace_bytes;
+  *bytes = x_dtype == BQ4_DTYPE_F16 ? plan.sk_bytes + plan.partial_bytes : plan.workspace_bytes;
   return BQ4_OK;
 }
 
@@ -478,7 +492,7 @@ bq4_status bq4_linear_ex(const bq4_weight* w, const void* x, bq4_dtype x_dtype, 
   GemmPlan plan;
   st = plan_gemm(w, 1, M, w->device, &plan);
   if (st) return st;
-  const size_t need = x16 ? plan.partial_bytes : plan.workspace_bytes;
+  const size_t need = x16 ? plan.sk_bytes + plan.partial_bytes : plan.workspace_bytes;
   if (need) {
     if (!workspace) return set_error(BQ4_EWORKSPACE, "workspace is NULL");
     if (!aligned(workspace, 256)) return set_error(BQ4_EALIGN, "workspace not 256-byte aligned");

@@ -172,6 +172,13 @@ struct WsArgs {
   int stages, rs;          // operand ring and raw ring depths
   int exact, pre, act;
   int lockstep;            // exact, 128-blocks, stage s accumulates into TMEM partial s (see below)
+  // Stream-K tail (whole-K units only): tiles [dp_tiles, dp_tiles + sk_tiles)
+  // are dealt to the CTAs as equal ranges of sk_w 128-K stages; a tile cut
+  // between CTAs c-1 and c is finished by c from the partial c-1 published.
+  int dp_tiles, sk_tiles;
+  int sk_w;                // grid * sk_w < 2^31 (checked by the planner)
+  float* sk_part;          // [grid][NW][BT][128] f32: slot c = partial for CTA c
+  unsigned* sk_flag;       // [grid]: slot c = 1 once sk_part[c] is complete (zeroed per call)
   uint32_t raw_s_bytes;    // folded: scale bytes per weight per raw stage
   uint32_t raw_w_bytes;    // raw stage bytes per weight
 };
@@ -214,6 +221,144 @@ __device__ __forceinline__ bool ws_seg_first(int kc, int kc0, int cpb) {
 }
 __device__ __forceinline__ bool ws_seg_last(int kc, int kc1, int cpb) {
   return kc == kc1 - 1 || (cpb > 0 && ((kc + 1) % cpb) == 0);
+}
+
+// One unit of a CTA's work: tile, 64-K chunk range, and what the scaler
+// does with the result.
+constexpr int kUnitFull = 0;  // whole K range (or a split-K unit): epilogue
+constexpr int kUnitHead = 1;  // stream-K: first part of a tile's K range, published for CTA c+1
+constexpr int kUnitTail = 2;  // stream-K: rest of the K range, finished with CTA c-1's partial
+struct Unit {
+  int tile, split, kc0, kc1, kind;
+};
+
+// The i-th unit of this CTA; false past the last.  Every role walks the same
+// list.  Stream-K order: the head piece of the CTA's last tile first (its
+// partial is then ready long before CTA c+1 needs it), whole tiles next,
+// the tail piece of its first tile last (CTA c-1 published that tile's head
+// partial as its own first unit).  Ranges are at least one tile long, so a
+// tile is cut at most once.
+__device__ __forceinline__ bool cta_unit(const WsArgs& a, int i, Unit& un) {
+  const int c = (int)blockIdx.x, P = (int)gridDim.x;
+  un.split = 0;
+  un.kind = kUnitFull;
+  if (a.ksplit > 1) {  // one split-K unit per CTA
+    if (i) return false;
+    ws_unit(a, c, un.tile, un.split, un.kc0, un.kc1);
+    return true;
+  }
+  un.kc0 = 0;
+  un.kc1 = a.nkc;
+  if (a.sk_tiles == 0) {
+    un.tile = c + i * P;
+    return un.tile < a.units;
+  }
+  const int nks = a.nkc >> 1;
+  const int s0 = c * a.sk_w / P, s1 = (c + 1) * a.sk_w / P;
+  const int t0 = s0 / nks, t1 = (s1 - 1) / nks;
+  const bool tail = (s0 % nks) != 0, head = (s1 % nks) != 0;
+  const int ndp = c < a.dp_tiles ? (a.dp_tiles - 1 - c) / P + 1 : 0;
+  const int f0 = tail ? t0 + 1 : t0, f1 = head ? t1 - 1 : t1;
+  const int nfull = f1 >= f0 ? f1 - f0 + 1 : 0;
+  int k = i;
+  if (head) {
+    if (k == 0) {
+      un.tile = a.dp_tiles + t1;
+      un.kc1 = 2 * (s1 - t1 * nks);
+      un.kind = kUnitHead;
+      return true;
+    }
+    --k;
+  }
+  if (k < ndp) {
+    un.tile = c + k * P;
+    return true;
+  }
+  k -= ndp;
+  if (k < nfull) {
+    un.tile = a.dp_tiles + f0 + k;
+    return true;
+  }
+  k -= nfull;
+  if (tail && k == 0) {
+    un.tile = a.dp_tiles + t0;
+    un.kc0 = 2 * (s0 - t0 * nks);
+    un.kind = kUnitTail;
+    return true;
+  }
+  return false;
+}
+
+// Stream-K head piece: publish this CTA's partial tile for CTA c+1.  Each
+// scaler warp arrives on `pub_bar` after its stores; thread 0 then raises
+// the flag (release at GPU scope).  Used at most once per launch (parity 0).
+template <int BT, int NW, int kCols>
+__device__ __forceinline__ void sk_publish(const WsArgs& a, const float (&acc)[NW][kCols], int row, int col0,
+                                           uint64_t* pub_bar, volatile int* abort_flag) {
+  float* part = a.sk_part + (size_t)(blockIdx.x + 1) * NW * BT * 128;
+#pragma unroll
+  for (int w = 0; w < NW; ++w)
+#pragma unroll
+    for (int j = 0; j < kCols; ++j) __stcg(part + ((size_t)w * BT + col0 + j) * 128 + row, acc[w][j]);
+  __threadfence();
+  __syncwarp();
+  if ((threadIdx.x & 31) == 0) ptx::mbar_arrive(pub_bar);
+  if (threadIdx.x == 0) {
+    if (ptx::mbar_wait(pub_bar, 0, abort_flag)) {
+      __threadfence();
+      asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(a.sk_flag + blockIdx.x + 1), "r"(1u) : "memory");
+    } else {
+      record_error_flag(abort_flag, BQ4_ETIMEOUT);
+    }
+  }
+}
+
+// Stream-K tail piece (always the CTA's last unit, so its operand ring is
+// idle): thread 0 waits (bounded) for CTA c-1's flag, then bulk-copies the
+// head partial into the ring, counted on `tail_bar`; every scaler thread
+// then folds it in from shared memory first: acc = head + tail, a fixed
+// order.  On a timeout thread 0 still arrives, so nobody waits twice.
+template <int BT, int NW, int kCols>
+__device__ __forceinline__ bool sk_absorb(const WsArgs& a, float (&acc)[NW][kCols], int row, int col0,
+                                          uint8_t* ring, uint64_t* tail_bar, volatile int* abort_flag) {
+  constexpr uint32_t kBytes = NW * BT * 128 * sizeof(float);
+  constexpr uint32_t kChunk = kBytes < 32768u ? kBytes : 32768u;
+  if (threadIdx.x == 0) {
+    const unsigned* f = a.sk_flag + blockIdx.x;
+    const uint64_t t0 = ptx::globaltimer();
+    bool ready = false;
+    while (true) {
+      unsigned v;
+      asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(f) : "memory");
+      if (v) {
+        ready = true;
+        break;
+      }
+      if (*abort_flag || ptx::globaltimer() - t0 > ptx::kWaitTimeoutNs) {
+        record_error_flag(abort_flag, BQ4_ETIMEOUT);
+        break;
+      }
+      __nanosleep(64);
+    }
+    if (ready) {
+      // the partial was written through the generic proxy; the copy reads it
+      // through the async proxy
+      asm volatile("fence.proxy.async.global;" ::: "memory");
+      ptx::mbar_arrive_expect_tx(tail_bar, kBytes);
+      const uint8_t* src = reinterpret_cast<const uint8_t*>(a.sk_part + (size_t)blockIdx.x * NW * BT * 128);
+#pragma unroll 1
+      for (uint32_t o = 0; o < kBytes; o += kChunk) ptx::bulk_load(ring + o, src + o, kChunk, tail_bar);
+    } else {
+      ptx::mbar_arrive(tail_bar);
+    }
+  }
+  if (!ptx::mbar_wait(tail_bar, 0, abort_flag) || *abort_flag) return false;
+  const float* part = reinterpret_cast<const float*>(ring);
+#pragma unroll
+  for (int w = 0; w < NW; ++w)
+#pragma unroll
+    for (int j = 0; j < kCols; ++j) acc[w][j] = part[(w * BT + col0 + j) * 128 + row] + acc[w][j];
+  return true;
 }
 
 // Split-K reduction across the cluster (one CTA per split, cluster rank =
@@ -339,7 +484,8 @@ __global__ void __launch_bounds__(kWsThreads, 1)
   uint64_t* raw_empty = raw_full + RS;
   uint64_t* part_full = raw_empty + RS;
   uint64_t* part_empty = part_full + kNP;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(part_empty + kNP);
+  uint64_t* sk_bars = part_empty + kNP;  // stream-K: [0] head published, [1] head partial ready
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sk_bars + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -354,6 +500,8 @@ __global__ void __launch_bounds__(kWsThreads, 1)
     }
     for (int i = 0; i < RS; ++i) { ptx::mbar_init(&raw_full[i], 1); ptx::mbar_init(&raw_empty[i], kWsDqWarps); }
     for (int i = 0; i < kNP; ++i) { ptx::mbar_init(&part_full[i], 1); ptx::mbar_init(&part_empty[i], kWsScalerWarps); }
+    ptx::mbar_init(&sk_bars[0], kWsScalerWarps);
+    ptx::mbar_init(&sk_bars[1], 1);
     *abort_flag = 0;
     ptx::fence_mbar_init();
   }
@@ -376,9 +524,9 @@ __global__ void __launch_bounds__(kWsThreads, 1)
       ptx::griddep_wait();
       int s = 0;
       uint32_t ph = 0;
-      for (int u = blockIdx.x; u < a.units && !*abort_flag; u += gridDim.x) {
-        int tile, split, kc0, kc1;
-        ws_unit(a, u, tile, split, kc0, kc1);
+      Unit un;
+      for (int i = 0; !*abort_flag && cta_unit(a, i, un); ++i) {
+        const int tile = un.tile, kc0 = un.kc0, kc1 = un.kc1;
         int mtile, ntile;
         ws_tile(a, tile, mtile, ntile);
         for (int kc = kc0; kc < kc1; kc += 2) {
@@ -403,9 +551,9 @@ __global__ void __launch_bounds__(kWsThreads, 1)
       // ------------------------------------------------ raw weight tiles (bulk copies)
       int rs = 0;
       uint32_t rph = 0;
-      for (int u = blockIdx.x; u < a.units && !*abort_flag; u += gridDim.x) {
-        int tile, split, kc0, kc1;
-        ws_unit(a, u, tile, split, kc0, kc1);
+      Unit un;
+      for (int i = 0; !*abort_flag && cta_unit(a, i, un); ++i) {
+        const int tile = un.tile, kc0 = un.kc0, kc1 = un.kc1;
         int mtile, ntile;
         ws_tile(a, tile, mtile, ntile);
         for (int kc = kc0; kc < kc1; kc += 2) {
@@ -432,9 +580,9 @@ __global__ void __launch_bounds__(kWsThreads, 1)
       int s = 0, pb = 0;
       uint32_t ph = 0, pph = 0;
       bool ok = true;
-      for (int u = blockIdx.x; ok && u < a.units && !*abort_flag; u += gridDim.x) {
-        int tile, split, kc0, kc1;
-        ws_unit(a, u, tile, split, kc0, kc1);
+      Unit un;
+      for (int i = 0; ok && !*abort_flag && cta_unit(a, i, un); ++i) {
+        const int kc0 = un.kc0, kc1 = un.kc1;
         uint32_t d_base = 0;
         for (int kc = kc0; ok && kc < kc1; kc += 2) {
           if (!ptx::mbar_wait(&full[s], ph, abort_flag)) { ok = false; break; }
@@ -495,9 +643,9 @@ __global__ void __launch_bounds__(kWsThreads, 1)
       int rs = 0, s = 0;
       uint32_t rph = 0, ph = 0;
       bool ok = true;
-      for (int u = blockIdx.x; ok && u < a.units && !*abort_flag; u += gridDim.x) {
-        int tile, split, kc0, kc1;
-        ws_unit(a, u, tile, split, kc0, kc1);
+      Unit un;
+      for (int i = 0; ok && !*abort_flag && cta_unit(a, i, un); ++i) {
+        const int kc0 = un.kc0, kc1 = un.kc1;
         for (int kc = kc0; kc < kc1; kc += 2) {
           if (!ptx::mbar_wait(&raw_full[rs], rph, abort_flag)) { ok = false; break; }
           uint4 wlo[NW], whi[NW];
@@ -581,9 +729,9 @@ __global__ void __launch_bounds__(kWsThreads, 1)
       // both partial buffers start free: the first use of each stage
       for (int i = 0; i < S; ++i) ptx::mbar_arrive(&full[i]);
     }
-    for (int u = blockIdx.x; ok && u < a.units && !*abort_flag; u += gridDim.x) {
-      int tile, split, kc0, kc1;
-      ws_unit(a, u, tile, split, kc0, kc1);
+    Unit un;
+    for (int i = 0; ok && !*abort_flag && cta_unit(a, i, un); ++i) {
+      const int tile = un.tile, split = un.split, kc0 = un.kc0, kc1 = un.kc1;
       int mtile, ntile;
       ws_tile(a, tile, mtile, ntile);
       const int n = ntile * 128 + row;
@@ -628,6 +776,14 @@ __global__ void __launch_bounds__(kWsThreads, 1)
         __syncwarp();
         ptx::cluster_sync();
         split_synced = true;
+        break;
+      }
+      if (un.kind == kUnitHead) {
+        sk_publish<BT, NW, kCols>(a, acc, row, col0, &sk_bars[0], abort_flag);
+        continue;
+      }
+      if (un.kind == kUnitTail && !sk_absorb<BT, NW, kCols>(a, acc, row, col0, ring, &sk_bars[1], abort_flag)) {
+        ok = false;
         break;
       }
       if (n < a.N) {
@@ -877,8 +1033,13 @@ int device_is_sm100(int device) {
 }
 
 // Plan for one token-tile size; *cost is the estimated makespan in µs.
+// Stream-K partial slots ([grid][NW][BT][128] f32) and flags ([grid]).
+static size_t sk_part_bytes(int grid, int nw, int bt) {
+  return align_up((size_t)grid * nw * bt * 128 * sizeof(float), 256);
+}
+
 static bq4_status plan_for_bt(const bq4_weight* w, int nw, int64_t M, int device, int bt, GemmPlan* p,
-                              double* cost) {
+                              double* cost, bool allow_sk) {
   p->bt = bt;
   p->mtiles = (int)((M + p->bt - 1) / p->bt);
   p->ntiles = (int)w->ntiles;
@@ -933,7 +1094,7 @@ static bq4_status plan_for_bt(const bq4_weight* w, int nw, int64_t M, int device
   p->lockstep = (p->exact && w->block == 128 && S <= np) ? 1 : 0;
   if (getenv("BQ4_NO_LOCKSTEP")) p->lockstep = 0;
   p->smem_bytes = 1024 + (size_t)S * stage_bytes + (size_t)RS * raw_stage +
-                  (size_t)(2 * S + 2 * RS + 2 * np) * 8 + 16;
+                  (size_t)(2 * S + 2 * RS + 2 * np + 2) * 8 + 16;
 
   // Split-K factor: minimise the estimated makespan (µs, measured on B200):
   // waves x (128-K stages per unit x stage time + unit fill + the cluster
@@ -970,6 +1131,39 @@ static bq4_status plan_for_bt(const bq4_weight* w, int nw, int64_t M, int device
   p->units = tiles * best_s;
   p->cluster = best_s;
   p->grid = best_s > 1 ? p->units : (p->units < sms ? p->units : sms);
+
+  // Stream-K tail for whole-K plans whose last wave is partial: the last
+  // full wave plus the remainder (sms + rem tiles) are dealt to the CTAs as
+  // equal ranges of 128-K stages, so no SM idles through the final wave.
+  // Each range is at least one tile long, so a tile is cut at most once;
+  // its two pieces meet through a partial slot in the workspace (about
+  // t_fix µs to read back).  Measured on B200 against whole tiles it pays
+  // for exact numerics and the gated pair (0.92x for 150 exact tiles, 0.82x
+  // for the gated pair's 152); folded plans lose: with the weight tile in
+  // TMEM the single accumulator serialises the pieces' epilogues (1.05-1.2x),
+  // and 128-token folded tiles with the tail lose to 256-token whole tiles
+  // (c1: 63.6 vs 55.1 µs).  Those keep whole tiles.  BQ4_NO_STREAMK=1 keeps
+  // whole tiles everywhere.
+  p->dp_tiles = p->sk_tiles = 0;
+  p->sk_bytes = 0;
+  if (best_s == 1 && allow_sk && (p->exact || nw == 2) && !p->ta && !getenv("BQ4_NO_STREAMK") && tiles > sms &&
+      tiles % sms != 0 &&
+      (int64_t)(2 * sms) * sms * nks < ((int64_t)1 << 31)) {
+    const int full = tiles / sms, rem = tiles % sms;
+    const double t_tile = nks * t_stage + 1.0;
+    const double t_fix = 0.01 * p->bt * nw + 0.5;
+    const double t_dp = (double)(full + 1) * t_tile;
+    const double t_sk = (double)(full - 1) * t_tile + ((double)(sms + rem) * nks / sms + 1.0) * t_stage + 1.0 + t_fix;
+    // the tail piece pulls its head partial into the (then idle) operand ring
+    const bool fits = (size_t)nw * p->bt * 128 * sizeof(float) <= (size_t)S * stage_bytes;
+    if (t_sk < t_dp && fits) {
+      p->sk_tiles = sms + rem;
+      p->dp_tiles = tiles - p->sk_tiles;
+      p->sk_bytes = sk_part_bytes(p->grid, nw, p->bt) + align_up((size_t)p->grid * sizeof(unsigned), 256);
+      best_t = t_sk;
+      *cost = best_t + 2.0;
+    }
+  }
   // Unit order: the wave shares the operand that is larger in HBM -- the
   // f16 token rows (M*K*2 bytes) or the Q4 weights (nw*N*K/2 bytes).
   p->nfast = ((int64_t)M * 4 > (int64_t)nw * w->Np) ? 1 : 0;
@@ -979,17 +1173,18 @@ static bq4_status plan_for_bt(const bq4_weight* w, int nw, int64_t M, int device
   // (BQ4_NO_PDL=1 launches it in plain stream order).
   p->pdl = getenv("BQ4_NO_PDL") ? 0 : 1;
 
-  // Workspace: the split-K partial tiles, then the f16 copy of x (callers
-  // passing f16 activations need only the first part).
+  // Workspace: the stream-K slots and flags, the split-K partial tiles, then
+  // the f16 copy of x (callers passing f16 activations need only the first
+  // two parts).
   p->partial_bytes =
       best_s > 1 ? align_up((size_t)tiles * best_s * nw * p->bt * 128 * sizeof(float), 256) : 0;
   p->xh_bytes = align_up((size_t)M * (size_t)w->Kp * 2, 256);
-  p->workspace_bytes = p->partial_bytes + p->xh_bytes;
+  p->workspace_bytes = p->sk_bytes + p->partial_bytes + p->xh_bytes;
   return BQ4_OK;
 }
 
 
-bq4_status plan_gemm(const bq4_weight* w, int nw, int64_t M, int device, GemmPlan* p) {
+bq4_status plan_gemm(const bq4_weight* w, int nw, int64_t M, int device, GemmPlan* p, bool allow_sk) {
   if (M <= 0) return set_error(BQ4_EINVAL_SHAPE, "M must be positive (got %lld)", (long long)M);
   if (M > (int64_t)1 << 30) return set_error(BQ4_EINVAL_SHAPE, "M too large");
   memset(p, 0, sizeof(*p));
@@ -1022,7 +1217,7 @@ bq4_status plan_gemm(const bq4_weight* w, int nw, int64_t M, int device, GemmPla
     if (forced ? bt != forced : (bt != 64 && bt > 2 * M)) continue;
     GemmPlan cand = base;
     double cost = 0.0;
-    last = plan_for_bt(w, nw, M, device, bt, &cand, &cost);
+    last = plan_for_bt(w, nw, M, device, bt, &cand, &cost, allow_sk);
     if (last != BQ4_OK) continue;
     if (!have || cost < best - 1e-9) {
       *p = cand;
@@ -1040,14 +1235,23 @@ bq4_status run_gemm(const GemmPlan& plan, const bq4_weight* const* ws, const voi
   cudaError_t e = cudaSuccess;
   const void* xh = x;
   int64_t x_pitch = ldx;
-  float* partials = plan.partial_bytes ? static_cast<float*>(workspace) : nullptr;
+  uint8_t* wsb = static_cast<uint8_t*>(workspace);
+  float* sk_part = plan.sk_tiles ? reinterpret_cast<float*>(wsb) : nullptr;
+  unsigned* sk_flag =
+      plan.sk_tiles ? reinterpret_cast<unsigned*>(wsb + sk_part_bytes(plan.grid, plan.nw, plan.bt)) : nullptr;
+  const int nflags = plan.sk_tiles ? plan.grid : 0;
+  float* partials = plan.partial_bytes ? reinterpret_cast<float*>(wsb + plan.sk_bytes) : nullptr;
   if (!io.x_f16) {
-    // 1) stage activations as f16 [M][Kp] in the workspace
-    void* dst = static_cast<uint8_t*>(workspace) + plan.partial_bytes;
-    e = launch_convert_x(static_cast<const float*>(x), M, w0->K, ldx, w0->Kp, dst, stream);
+    // 1) stage activations as f16 [M][Kp] in the workspace (and zero the
+    //    stream-K flags)
+    void* dst = wsb + plan.sk_bytes + plan.partial_bytes;
+    e = launch_convert_x(static_cast<const float*>(x), M, w0->K, ldx, w0->Kp, dst, sk_flag, nflags, stream);
     if (e != cudaSuccess) return check_cuda(e, "convert_x launch");
     xh = dst;
     x_pitch = w0->Kp;
+  } else if (nflags) {
+    e = launch_zero_flags(sk_flag, nflags, stream);
+    if (e != cudaSuccess) return check_cuda(e, "zero_flags launch");
   }
 
   // 2) tensor map over the f16 tokens [M][Kp] (caller's buffer when x is
@@ -1093,6 +1297,11 @@ bq4_status run_gemm(const GemmPlan& plan, const bq4_weight* const* ws, const voi
   args.exact = plan.exact;
   args.pre = plan.pre;
   args.lockstep = plan.lockstep;
+  args.dp_tiles = plan.dp_tiles;
+  args.sk_tiles = plan.sk_tiles;
+  args.sk_w = plan.sk_tiles * (int)(w0->nkc / 2);
+  args.sk_part = sk_part;
+  args.sk_flag = sk_flag;
   args.act = act;
   args.raw_s_bytes = plan.raw_s_bytes;
   args.raw_w_bytes = plan.raw_w_bytes;

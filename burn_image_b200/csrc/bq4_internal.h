@@ -62,9 +62,11 @@ cudaError_t launch_dequant_prepared(const bq4_weight* w, float* out, int32_t out
 cudaError_t launch_dequant_raw(const uint32_t* words, const float* scales, int64_t K, int64_t N,
                                int32_t block, int32_t layout, float* out, int32_t out_layout,
                                cudaStream_t s);
-// x f32 [M][ldx] -> xh f16 [M][Kp] (zero padded).
+// x f32 [M][ldx] -> xh f16 [M][Kp] (zero padded); also zeroes nflags
+// stream-K flags (flags may be null when nflags is 0).
 cudaError_t launch_convert_x(const float* x, int64_t M, int64_t K, int64_t ldx, int64_t Kp,
-                             void* xh, cudaStream_t s);
+                             void* xh, unsigned* flags, int nflags, cudaStream_t s);
+cudaError_t launch_zero_flags(unsigned* flags, int nflags, cudaStream_t s);
 
 // Packed-Q4 row selection (q_select on dim 0), optionally dequantized.
 cudaError_t launch_select_rows(const uint32_t* values, const float* scales, int64_t rows, int64_t cols, int block,
@@ -94,12 +96,15 @@ struct GemmPlan {
   uint32_t raw_s_bytes;  // scale bytes per weight per raw stage (folded)
   uint32_t raw_w_bytes;  // shared-memory bytes per weight per raw stage
   size_t smem_bytes;
+  int dp_tiles, sk_tiles;  // stream-K tail: tiles dealt as equal stage ranges (0 = none)
+  size_t sk_bytes;         // workspace part 0: stream-K partial slots + flags (0 without)
   size_t partial_bytes;    // workspace part 1: split-K partial tiles (0 without split)
   size_t xh_bytes;         // workspace part 2: the f16 copy of x (unused with f16 x)
   size_t workspace_bytes;
 };
 
-bq4_status plan_gemm(const bq4_weight* w, int nw, int64_t M, int device, GemmPlan* plan);
+// allow_sk = false plans without the stream-K tail (smaller workspace).
+bq4_status plan_gemm(const bq4_weight* w, int nw, int64_t M, int device, GemmPlan* plan, bool allow_sk = true);
 
 // Activation / output formats of one GEMM call: x f32 (staged to f16 in the
 // workspace) or f16 (read in place; needs K == Kp), y f32 or f16 with row

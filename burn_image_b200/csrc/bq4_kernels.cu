@@ -156,13 +156,16 @@ __global__ void dequant_raw_kernel(const uint32_t* __restrict__ words, const flo
 
 // x f32 [M][ldx] -> xh f16 [M][Kp] with round-to-nearest-even, zero padding
 // K..Kp-1.  Each thread converts 8 consecutive K values into one 16-byte
-// store.
+// store.  Block 0 also zeroes the GEMM's stream-K flags (nflags words).
 __global__ void convert_x_kernel(const float* __restrict__ x, int64_t M, int64_t K, int64_t ldx,
-                                 int64_t Kp, uint4* __restrict__ xh, int vec4) {
+                                 int64_t Kp, uint4* __restrict__ xh, int vec4, unsigned* __restrict__ flags,
+                                 int nflags) {
   // The GEMM that consumes xh is launched as a programmatic dependent: it may
   // start its weight-side prologue now and waits for this grid's completion
-  // before it reads xh.
+  // before it reads xh or touches the flags.
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  if (blockIdx.x == 0)
+    for (int i = threadIdx.x; i < nflags; i += blockDim.x) flags[i] = 0u;
   const int64_t per_row = Kp / 8;
   const int64_t total = M * per_row;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
@@ -417,11 +420,24 @@ cudaError_t launch_rms_renorm(const void* x, int x_f16, int64_t M, int64_t H, in
 }
 
 cudaError_t launch_convert_x(const float* x, int64_t M, int64_t K, int64_t ldx, int64_t Kp,
-                             void* xh, cudaStream_t s) {
+                             void* xh, unsigned* flags, int nflags, cudaStream_t s) {
   const int vec4 = ((reinterpret_cast<uintptr_t>(x) & 15) == 0) && (ldx % 4 == 0);
   const int64_t total = M * (Kp / 8);
   convert_x_kernel<<<grid_for(total, 256, current_device()), 256, 0, s>>>(
-      x, M, K, ldx, Kp, reinterpret_cast<uint4*>(xh), vec4);
+      x, M, K, ldx, Kp, reinterpret_cast<uint4*>(xh), vec4, flags, nflags);
+  note_launch();
+  return cudaGetLastError();
+}
+
+// Zeroes the GEMM's stream-K flags when there is no staging grid to do it
+// (f16 activations); the GEMM follows as a programmatic dependent.
+__global__ void zero_flags_kernel(unsigned* __restrict__ flags, int nflags) {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  for (int i = threadIdx.x; i < nflags; i += blockDim.x) flags[i] = 0u;
+}
+
+cudaError_t launch_zero_flags(unsigned* flags, int nflags, cudaStream_t s) {
+  zero_flags_kernel<<<1, 256, 0, s>>>(flags, nflags);
   note_launch();
   return cudaGetLastError();
 }

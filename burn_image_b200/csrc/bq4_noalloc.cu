@@ -1,11 +1,12 @@
 // bq4_noalloc.cu -- bq4_linear for callers that cannot allocate device memory.
 //
 // bq4_linear needs a caller-provided workspace (the f16 copy of the
-// activations and the split-K partial tiles).  Some callers have no
-// way to provide one: a host runtime whose allocator owns all device memory
-// and offers no hook to hand a foreign op a scratch buffer, code that must
-// not call cudaMalloc because it synchronizes the device, or a process that
-// is not permitted to grow its device footprint after start-up.  For them
+// activations, the split-K partial tiles and the stream-K slots).  Some
+// callers have no way to provide one: a host runtime whose allocator owns
+// all device memory and offers no hook to hand a foreign op a scratch
+// buffer, code that must not call cudaMalloc because it synchronizes the
+// device, or a process that is not permitted to grow its device footprint
+// after start-up.  For them
 // bq4_linear_noalloc runs the same GEMM with its scratch in a fixed-size
 // static device array that every GPU loading this library holds until the
 // process exits (BQ4_NOALLOC_SCRATCH_BYTES per device).
@@ -15,9 +16,10 @@
 // current) on the first call there, and cached.  Calls on one device share
 // the array: two calls that overlap on the GPU (different streams, or
 // different host threads without ordering) race on it.  It holds the f16
-// copy of the activations and the split-K partial tiles; every call writes
-// each of them in full before anything reads it, so nothing in it needs to
-// start at zero.
+// copy of the activations, the split-K partial tiles and the stream-K
+// partial slots, which every call writes in full before anything reads
+// them, and the stream-K flags, which the call zeroes first -- so nothing in
+// it needs to start at zero.
 #include <cuda_runtime.h>
 
 #include <mutex>
@@ -66,6 +68,8 @@ extern "C" bq4_status bq4_linear_noalloc(const bq4_weight* w, const float* x, in
     return set_error(BQ4_EALIGN, "x/y not 4-byte aligned");
   GemmPlan plan;
   bq4_status st = plan_gemm(w, 1, M, w->device, &plan);
+  if (st == BQ4_OK && plan.sk_tiles && plan.workspace_bytes > (size_t)BQ4_NOALLOC_SCRATCH_BYTES)
+    st = plan_gemm(w, 1, M, w->device, &plan, false);  // whole tiles need no stream-K slots
   if (st) return st;
   if (plan.workspace_bytes > (size_t)BQ4_NOALLOC_SCRATCH_BYTES)
     return set_error(BQ4_EWORKSPACE,

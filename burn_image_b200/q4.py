@@ -260,6 +260,14 @@ class PreparedQ4Weight:
         check(L.lib().bq4_linear_workspace_size(self._h, M, ctypes.byref(n)))
         return n.value
 
+    PLAN_FIELDS = ("bt", "ksplit", "grid", "exact", "ta", "stages", "sk_tiles", "dp_tiles", "workspace_256")
+
+    def plan_info(self, M: int, gated: bool = False) -> dict:
+        """The launch plan of bq4_linear (or of the gated pair) for M rows."""
+        info = (ctypes.c_int32 * len(self.PLAN_FIELDS))()
+        check(L.lib().bq4_linear_plan_info(self._h, M, 1 if gated else 0, info, len(self.PLAN_FIELDS)))
+        return dict(zip(self.PLAN_FIELDS, list(info)))
+
     def linear(self, x: torch.Tensor, bias: Optional[torch.Tensor] = None, act: int = L.ACT_NONE,
                aux: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None) -> torch.Tensor:
         """y = act(x . W + bias) (* aux) over the last axis of x (leading dims flattened)."""

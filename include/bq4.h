@@ -124,6 +124,17 @@ BQ4_API bq4_status bq4_weight_info(const bq4_weight* w, int64_t* K, int64_t* N, 
 BQ4_API bq4_status bq4_linear_workspace_size(const bq4_weight* w, int64_t M, size_t* bytes);
 
 /*
+ * The launch plan bq4_linear uses for this weight and M (diagnostics and
+ * tests).  Writes min(n, 9) values to info: token tile (64/128/256),
+ * split-K factor (1 = none), grid size, exact numerics (0/1), weight tile in
+ * TMEM (0/1), operand-ring stages, stream-K tiles (0 = whole tiles only),
+ * whole tiles before them, workspace bytes / 256.  gated = 1 plans the
+ * SiLU-gated pair (bq4_linear_gated) with `w` as both weights.
+ */
+BQ4_API bq4_status bq4_linear_plan_info(const bq4_weight* w, int64_t M, int32_t gated, int32_t* info,
+                                        int32_t n);
+
+/*
  * y[M,N] = act(x[M,K] . W + bias) (* aux)   -- the fused q_matmul + epilogue.
  * x: f32, row pitch `ldx` elements (>= K); bias: f32 [N] or NULL;
  * aux: f32 [M,N] multiplied after the activation, or NULL; y: f32 [M,N]
@@ -137,7 +148,7 @@ BQ4_API bq4_status bq4_linear(const bq4_weight* w, const float* x, int64_t M, in
 typedef enum { BQ4_DTYPE_F32 = 0, BQ4_DTYPE_F16 = 1 } bq4_dtype;
 
 /* Workspace for bq4_linear_ex: the bq4_linear size for f32 x; for f16 x only the split-K
- * partial tiles (0 when the plan does not split K). */
+ * partial tiles and the stream-K slots (0 when the plan uses neither). */
 BQ4_API bq4_status bq4_linear_ex_workspace_size(const bq4_weight* w, int64_t M, bq4_dtype x_dtype,
                                                 size_t* bytes);
 
@@ -196,9 +207,10 @@ BQ4_API bq4_status bq4_dequant_raw(const uint32_t* packed_words, const float* sc
  * not grow its device footprint after start-up.  This entry point computes
  * exactly what bq4_linear computes, with its scratch in a static device
  * array of BQ4_NOALLOC_SCRATCH_BYTES that every GPU loading the library
- * holds until exit; it allocates nothing.  Calls whose scratch need
- * (bq4_linear_workspace_size for the same weight and M) exceeds that size
- * return BQ4_EWORKSPACE.  The first call on a device looks up the array's
+ * holds until exit; it allocates nothing.  When bq4_linear's workspace for
+ * the same weight and M exceeds that size it plans without the stream-K
+ * tail (whose partial slots need workspace); calls whose scratch need still
+ * exceeds it return BQ4_EWORKSPACE.  The first call on a device looks up the array's
  * device address, so make it before any stream capture.  All calls on a
  * device share the array: calls that overlap on the GPU race.
  */

@@ -79,7 +79,10 @@ def test_numerics_modes_both_within_tolerance(M, K, N):
 @pytest.mark.parametrize("M,K,N", [(4352, 12288, 3072), (1024, 3072, 9216), (300, 1024, 640)])
 def test_unit_order_does_not_change_results(M, K, N, monkeypatch):
     """N-tile-fastest and M-tile-fastest unit orders only reschedule whole
-    tiles, so the outputs are bit-identical."""
+    tiles, so the outputs are bit-identical.  (With a stream-K tail the order
+    also decides which tiles are cut in two, which moves rounding; that plan
+    is compared with whole tiles in test_gpu_streamk.py.)"""
+    monkeypatch.setenv("BQ4_NO_STREAMK", "1")
     words, scales, x = problem(M, K, N, 128)
     pw = q4.PreparedQ4Weight(words, scales, K, N, 128, L.LAYOUT_ROW, DEV)
     outs = []
