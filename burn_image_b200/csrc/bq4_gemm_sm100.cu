@@ -233,11 +233,34 @@ struct Unit {
 };
 
 // The i-th unit of this CTA; false past the last.  Every role walks the same
-// list.  Stream-K order: the head piece of the CTA's last tile first (its
+// list.  kSK = false compiles only whole-tile and split-K units (kernels the
+// planner never gives a stream-K tail), keeping the roles' loops lean.
+// Stream-K order: the head piece of the CTA's last tile first (its
 // partial is then ready long before CTA c+1 needs it), whole tiles next,
 // the tail piece of its first tile last (CTA c-1 published that tile's head
 // partial as its own first unit).  Ranges are at least one tile long, so a
 // tile is cut at most once.
+// The loop every role runs over its units.  Without stream-K it is the
+// plain persistent loop u = blockIdx.x, blockIdx.x + gridDim.x, ...; with
+// it, the i-th unit of cta_unit.  COND is the role's extra loop condition.
+#define BQ4_FOR_UNITS(COND)                                                          \
+  Unit un;                                                                           \
+  for (int i = 0, u_ = (int)blockIdx.x;                                              \
+       (COND) && (kSK ? cta_unit<kSK>(a, i, un) : unit_at(a, u_, un));               \
+       ++i, u_ += (int)gridDim.x)
+
+template <bool kSK>
+__device__ __forceinline__ bool cta_unit(const WsArgs& a, int i, Unit& un);
+
+// Whole-tile (or split-K) unit number u of the persistent loop.
+__device__ __forceinline__ bool unit_at(const WsArgs& a, int u, Unit& un) {
+  if (u >= a.units) return false;
+  un.kind = kUnitFull;
+  ws_unit(a, u, un.tile, un.split, un.kc0, un.kc1);
+  return true;
+}
+
+template <bool kSK>
 __device__ __forceinline__ bool cta_unit(const WsArgs& a, int i, Unit& un) {
   const int c = (int)blockIdx.x, P = (int)gridDim.x;
   un.split = 0;
@@ -249,7 +272,7 @@ __device__ __forceinline__ bool cta_unit(const WsArgs& a, int i, Unit& un) {
   }
   un.kc0 = 0;
   un.kc1 = a.nkc;
-  if (a.sk_tiles == 0) {
+  if (!kSK || a.sk_tiles == 0) {
     un.tile = c + i * P;
     return un.tile < a.units;
   }
@@ -470,6 +493,7 @@ __global__ void __launch_bounds__(kWsThreads, 1)
   constexpr int kNP = TA ? 256 / kPartCols : 512 / kPartCols;
   constexpr uint32_t kACol0 = kNP * kPartCols;    // TA: first A-slot column
   constexpr int kCols = BT / 4;          // token columns per scaler thread
+  constexpr bool kSK = !TA;              // stream-K tails are planned only for A in shared memory
   static_assert(TA || kNP >= 2, "at least double buffering");
   static_assert(!TA || (NW == 1 && kACol0 == 256 && BT >= 128), "TMEM operand A: one weight, slots from column 256");
   static_assert(kCols % 16 == 0, "scaler column split");
@@ -524,8 +548,7 @@ __global__ void __launch_bounds__(kWsThreads, 1)
       ptx::griddep_wait();
       int s = 0;
       uint32_t ph = 0;
-      Unit un;
-      for (int i = 0; !*abort_flag && cta_unit(a, i, un); ++i) {
+      BQ4_FOR_UNITS(!*abort_flag) {
         const int tile = un.tile, kc0 = un.kc0, kc1 = un.kc1;
         int mtile, ntile;
         ws_tile(a, tile, mtile, ntile);
@@ -551,8 +574,7 @@ __global__ void __launch_bounds__(kWsThreads, 1)
       // ------------------------------------------------ raw weight tiles (bulk copies)
       int rs = 0;
       uint32_t rph = 0;
-      Unit un;
-      for (int i = 0; !*abort_flag && cta_unit(a, i, un); ++i) {
+      BQ4_FOR_UNITS(!*abort_flag) {
         const int tile = un.tile, kc0 = un.kc0, kc1 = un.kc1;
         int mtile, ntile;
         ws_tile(a, tile, mtile, ntile);
@@ -580,8 +602,7 @@ __global__ void __launch_bounds__(kWsThreads, 1)
       int s = 0, pb = 0;
       uint32_t ph = 0, pph = 0;
       bool ok = true;
-      Unit un;
-      for (int i = 0; ok && !*abort_flag && cta_unit(a, i, un); ++i) {
+      BQ4_FOR_UNITS(ok && !*abort_flag) {
         const int kc0 = un.kc0, kc1 = un.kc1;
         uint32_t d_base = 0;
         for (int kc = kc0; ok && kc < kc1; kc += 2) {
@@ -643,8 +664,7 @@ __global__ void __launch_bounds__(kWsThreads, 1)
       int rs = 0, s = 0;
       uint32_t rph = 0, ph = 0;
       bool ok = true;
-      Unit un;
-      for (int i = 0; ok && !*abort_flag && cta_unit(a, i, un); ++i) {
+      BQ4_FOR_UNITS(ok && !*abort_flag) {
         const int kc0 = un.kc0, kc1 = un.kc1;
         for (int kc = kc0; kc < kc1; kc += 2) {
           if (!ptx::mbar_wait(&raw_full[rs], rph, abort_flag)) { ok = false; break; }
@@ -729,8 +749,7 @@ __global__ void __launch_bounds__(kWsThreads, 1)
       // both partial buffers start free: the first use of each stage
       for (int i = 0; i < S; ++i) ptx::mbar_arrive(&full[i]);
     }
-    Unit un;
-    for (int i = 0; ok && !*abort_flag && cta_unit(a, i, un); ++i) {
+    BQ4_FOR_UNITS(ok && !*abort_flag) {
       const int tile = un.tile, split = un.split, kc0 = un.kc0, kc1 = un.kc1;
       int mtile, ntile;
       ws_tile(a, tile, mtile, ntile);
@@ -778,13 +797,15 @@ __global__ void __launch_bounds__(kWsThreads, 1)
         split_synced = true;
         break;
       }
-      if (un.kind == kUnitHead) {
-        sk_publish<BT, NW, kCols>(a, acc, row, col0, &sk_bars[0], abort_flag);
-        continue;
-      }
-      if (un.kind == kUnitTail && !sk_absorb<BT, NW, kCols>(a, acc, row, col0, ring, &sk_bars[1], abort_flag)) {
-        ok = false;
-        break;
+      if constexpr (kSK) {
+        if (un.kind == kUnitHead) {
+          sk_publish<BT, NW, kCols>(a, acc, row, col0, &sk_bars[0], abort_flag);
+          continue;
+        }
+        if (un.kind == kUnitTail && !sk_absorb<BT, NW, kCols>(a, acc, row, col0, ring, &sk_bars[1], abort_flag)) {
+          ok = false;
+          break;
+        }
       }
       if (n < a.N) {
         const float b0 = a.bias[0] ? __ldg(a.bias[0] + n) : 0.0f;
