@@ -59,6 +59,11 @@ SIGNATURES = {
     "bq4_q_select_rows": (_st, [_p, _p, _i64, _i64, _i32, _p, _i32, _i64, _p, _p, _p]),
     "bq4_q_select_rows_dequant": (_st, [_p, _p, _i64, _i64, _i32, _p, _i32, _i64, _p, _p]),
     "bq4_rms_renorm": (_st, [_p, _i32, _i64, _i64, _i64, _p, _i32, _i64, ctypes.c_float, _p]),
+    "bq4_qk_norm_rope": (_st, [_p, _i32, _i64, _i64, _i64, _i64, _p, ctypes.c_float, _p, _p, _i64, _p, _i32, _i64,
+                               _p]),
+    "bq4_linear_qk_norm_rope_workspace_size": (_st, [_p, _i64, _i32, _i64, ctypes.POINTER(_sz)]),
+    "bq4_linear_qk_norm_rope": (_st, [_p, _p, _i32, _i64, _i64, _p, _i64, _i64, _i64, _p, _p, ctypes.c_float, _p, _p,
+                                      _i64, _p, _i32, _i64, _p, _sz, _p]),
     "bq4_launch_count": (_u64, []),
     "bq4_launch_count_reset": (None, []),
 }

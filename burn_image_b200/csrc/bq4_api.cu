@@ -451,6 +451,129 @@ bq4_status bq4_rms_renorm(const void* x, bq4_dtype x_dtype, int64_t M, int64_t H
   return e == cudaSuccess ? BQ4_OK : check_cuda(e, "rms_renorm launch");
 }
 
+bq4_status bq4_qk_norm_rope(const void* x, bq4_dtype x_dtype, int64_t M, int64_t heads, int64_t head_dim,
+                            int64_t ldx, const float* gamma, float eps, const float* cos_t, const float* sin_t,
+                            int64_t ld_rope, void* y, bq4_dtype y_dtype, int64_t ldy, bq4_stream_t stream) {
+  if ((x_dtype != BQ4_DTYPE_F32 && x_dtype != BQ4_DTYPE_F16) || (y_dtype != BQ4_DTYPE_F32 && y_dtype != BQ4_DTYPE_F16))
+    return set_error(BQ4_EINVAL_ARG, "dtype unknown");
+  if (!x || !y) return set_error(BQ4_EINVAL_ARG, "x/y is NULL");
+  if ((cos_t == nullptr) != (sin_t == nullptr)) return set_error(BQ4_EINVAL_ARG, "cos and sin must both be given");
+  if (M <= 0 || heads <= 0 || head_dim <= 0 || head_dim % 2 || head_dim > 256 || M * heads > 0x7fffffffLL ||
+      ldx < heads * head_dim || ldy < heads * head_dim || (cos_t && ld_rope < head_dim))
+    return set_error(BQ4_EINVAL_SHAPE, "M=%lld heads=%lld head_dim=%lld (even, <= 256) ldx=%lld ldy=%lld ld_rope=%lld",
+                     (long long)M, (long long)heads, (long long)head_dim, (long long)ldx, (long long)ldy,
+                     (long long)ld_rope);
+  if (!(eps > 0.0f)) return set_error(BQ4_EINVAL_ARG, "eps must be positive");
+  if (x == y && (x_dtype != y_dtype || ldx != ldy))
+    return set_error(BQ4_EINVAL_ARG, "in place needs the same dtype and pitch");
+  const size_t ax = x_dtype == BQ4_DTYPE_F16 ? 2 : 4, ay = y_dtype == BQ4_DTYPE_F16 ? 2 : 4;
+  if (!aligned(x, ax) || !aligned(y, ay) || (gamma && !aligned(gamma, 4)) || (cos_t && (!aligned(cos_t, 4) ||
+                                                                                      !aligned(sin_t, 4))))
+    return set_error(BQ4_EALIGN, "x/y/gamma/cos/sin misaligned");
+  cudaError_t e = launch_qk_norm_rope(x, x_dtype == BQ4_DTYPE_F16, M, (int)heads, (int)head_dim, ldx, gamma, eps,
+                                      cos_t, sin_t, ld_rope, y, y_dtype == BQ4_DTYPE_F16, ldy,
+                                      reinterpret_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? BQ4_OK : check_cuda(e, "qk_norm_rope launch");
+}
+
+static bool qk_fused(const bq4_weight* w, int64_t head_dim) { return head_dim == 128 && w->N % 128 == 0; }
+
+bq4_status bq4_linear_qk_norm_rope_workspace_size(const bq4_weight* w, int64_t M, bq4_dtype x_dtype,
+                                                  int64_t head_dim, size_t* bytes) {
+  if (x_dtype != BQ4_DTYPE_F32 && x_dtype != BQ4_DTYPE_F16)
+    return set_error(BQ4_EINVAL_ARG, "x_dtype %d unknown", (int)x_dtype);
+  bq4_status st = check_weight(w, "w");
+  if (st) return st;
+  if (!bytes) return set_error(BQ4_EINVAL_ARG, "bytes is NULL");
+  GemmPlan plan;
+  st = plan_gemm(w, 1, M, w->device, &plan, true, qk_fused(w, head_dim));
+  if (st) return st;
+  *bytes = x_dtype == BQ4_DTYPE_F16 ? plan.sk_bytes + plan.partial_bytes : plan.workspace_bytes;
+  return BQ4_OK;
+}
+
+bq4_status bq4_linear_qk_norm_rope(const bq4_weight* w, const void* x, bq4_dtype x_dtype, int64_t M, int64_t ldx,
+                                   const float* bias, int64_t q_heads, int64_t k_heads, int64_t head_dim,
+                                   const float* gamma_q, const float* gamma_k, float eps, const float* cos_t,
+                                   const float* sin_t, int64_t ld_rope, void* y, bq4_dtype y_dtype, int64_t ldy,
+                                   void* workspace, size_t workspace_bytes, bq4_stream_t stream) {
+  bq4_status st = check_weight(w, "w");
+  if (st) return st;
+  if (head_dim <= 0 || head_dim % 2 || head_dim > 256 || q_heads < 0 || k_heads < 0 || w->N % head_dim ||
+      (q_heads + k_heads) * head_dim > w->N)
+    return set_error(BQ4_EINVAL_SHAPE, "heads %lld + %lld of %lld (even, <= 256) do not fit N=%lld",
+                     (long long)q_heads, (long long)k_heads, (long long)head_dim, (long long)w->N);
+  if ((cos_t == nullptr) != (sin_t == nullptr)) return set_error(BQ4_EINVAL_ARG, "cos and sin must both be given");
+  if (cos_t && ld_rope < head_dim) return set_error(BQ4_EINVAL_SHAPE, "ld_rope < head_dim");
+  if (!(eps > 0.0f)) return set_error(BQ4_EINVAL_ARG, "eps must be positive");
+  if (ldy == 0) ldy = w->N;
+  if (!qk_fused(w, head_dim)) {
+    // the linear, then the norm and rotation in place on its q and k sections
+    st = bq4_linear_ex(w, x, x_dtype, M, ldx, bias, BQ4_ACT_NONE, nullptr, y, y_dtype, ldy, workspace,
+                       workspace_bytes, stream);
+    if (st) return st;
+    DeviceGuard guard(w->device);
+    const size_t es = y_dtype == BQ4_DTYPE_F16 ? 2 : 4;
+    if (q_heads > 0) {
+      st = bq4_qk_norm_rope(y, y_dtype, M, q_heads, head_dim, ldy, gamma_q, eps, cos_t, sin_t, ld_rope, y, y_dtype,
+                            ldy, stream);
+      if (st) return st;
+    }
+    if (k_heads > 0) {
+      void* yk = static_cast<uint8_t*>(y) + (size_t)q_heads * head_dim * es;
+      st = bq4_qk_norm_rope(yk, y_dtype, M, k_heads, head_dim, ldy, gamma_k, eps, cos_t, sin_t, ld_rope, yk,
+                            y_dtype, ldy, stream);
+    }
+    return st;
+  }
+  // fused: every 128-feature tile is one head
+  if ((x_dtype != BQ4_DTYPE_F32 && x_dtype != BQ4_DTYPE_F16) || (y_dtype != BQ4_DTYPE_F32 && y_dtype != BQ4_DTYPE_F16))
+    return set_error(BQ4_EINVAL_ARG, "x_dtype %d / y_dtype %d unknown", (int)x_dtype, (int)y_dtype);
+  if (!x || !y) return set_error(BQ4_EINVAL_ARG, "x/y is NULL");
+  if (M <= 0 || M > 0x7fffffff) return set_error(BQ4_EINVAL_SHAPE, "M=%lld", (long long)M);
+  if (ldx < w->K) return set_error(BQ4_EINVAL_SHAPE, "ldx=%lld < K=%lld", (long long)ldx, (long long)w->K);
+  if (ldy < w->N) return set_error(BQ4_EINVAL_SHAPE, "ldy=%lld < N=%lld", (long long)ldy, (long long)w->N);
+  const int x16 = x_dtype == BQ4_DTYPE_F16, y16 = y_dtype == BQ4_DTYPE_F16;
+  if (x16) {
+    if (w->K != w->Kp)
+      return set_error(BQ4_EINVAL_SHAPE, "f16 x needs K %% 128 == 0 (K=%lld)", (long long)w->K);
+    if (!aligned(x, 16) || ldx % 8)
+      return set_error(BQ4_EALIGN, "f16 x needs a 16-byte aligned base and ldx %% 8 == 0");
+  } else if (!aligned(x, 4)) {
+    return set_error(BQ4_EALIGN, "x not 4-byte aligned");
+  }
+  if (!aligned(y, y16 ? 2 : 4)) return set_error(BQ4_EALIGN, "y misaligned");
+  GemmPlan plan;
+  st = plan_gemm(w, 1, M, w->device, &plan, true, true);
+  if (st) return st;
+  const size_t need = x16 ? plan.sk_bytes + plan.partial_bytes : plan.workspace_bytes;
+  if (need) {
+    if (!workspace) return set_error(BQ4_EWORKSPACE, "workspace is NULL");
+    if (!aligned(workspace, 256)) return set_error(BQ4_EALIGN, "workspace not 256-byte aligned");
+    if (workspace_bytes < need)
+      return set_error(BQ4_EWORKSPACE, "workspace %zu < required %zu bytes", workspace_bytes, need);
+  }
+  DeviceGuard guard(w->device);
+  QkParams qk;
+  qk.q_heads = (int)q_heads;
+  qk.k_heads = (int)k_heads;
+  qk.eps = eps;
+  qk.gamma_q = gamma_q;
+  qk.gamma_k = gamma_k;
+  qk.cos_t = cos_t;
+  qk.sin_t = sin_t;
+  qk.ld_rope = cos_t ? ld_rope : 128;
+  const bq4_weight* ws[1] = {w};
+  const float* b[1] = {bias};
+  GemmIo io;
+  io.x_f16 = x16;
+  io.y_f16 = y16;
+  io.ldy = ldy;
+  io.qk = &qk;
+  return run_gemm(plan, ws, x, M, ldx, b, (int)BQ4_ACT_NONE, nullptr, y, workspace,
+                  reinterpret_cast<cudaStream_t>(stream), io);
+}
+
 bq4_status bq4_linear_ex_workspace_size(const bq4_weight* w, int64_t M, bq4_dtype x_dtype, size_t* bytes) {
   if (x_dtype != BQ4_DTYPE_F32 && x_dtype != BQ4_DTYPE_F16)
     return set_error(BQ4_EINVAL_ARG, "x_dtype %d unknown", (int)x_dtype);

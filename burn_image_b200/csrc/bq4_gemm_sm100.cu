@@ -179,6 +179,16 @@ struct WsArgs {
   int sk_w;                // grid * sk_w < 2^31 (checked by the planner)
   float* sk_part;          // [grid][NW][BT][128] f32: slot c = partial for CTA c
   unsigned* sk_flag;       // [grid]: slot c = 1 once sk_part[c] is complete (zeroed per call)
+  // QK-norm + RoPE epilogue (kernels built with QK): every 128-feature N
+  // tile is one head; tiles [0, qk_q) are q heads, [qk_q, qk_q + qk_k) k
+  // heads, the rest pass through.  cos_t / sin_t [M][128] at row pitch
+  // ld_rope (NULL: no rotation); gamma_q / gamma_k [128] (NULL: ones).
+  int qk_q, qk_k, ld_rope;
+  float qk_eps;
+  const float* gamma_q;
+  const float* gamma_k;
+  const float* cos_t;
+  const float* sin_t;
   uint32_t raw_s_bytes;    // folded: scale bytes per weight per raw stage
   uint32_t raw_w_bytes;    // raw stage bytes per weight
 };
@@ -384,6 +394,74 @@ __device__ __forceinline__ bool sk_absorb(const WsArgs& a, float (&acc)[NW][kCol
   return true;
 }
 
+// QK-norm + RoPE on one q or k head tile, in place on the register
+// epilogue's values (the reference applies it between the projections and
+// attention: crates/burn_boogu/src/model/attention.rs:114-133, 916-928).
+// Thread (quad q, lane l) of column quarter c holds feature row 32q + l of
+// the head for kCols tokens.  Per token the squares are summed over the 128
+// rows: for each chunk of 16 columns a reduce-scatter butterfly (masks
+// 16..2, then an xor-1 add) leaves lanes 2i and 2i+1 the warp's sum of the
+// chunk's column i; the four quad warps of the quarter add theirs through
+// `scratch` (double-buffered by use parity, one bounded mbarrier wait per
+// use); the inverse RMS goes back to every lane by shuffle.  Then
+// v = v * inv * gamma[row] and the interleaved-pair rotation with the
+// partner row (lane ^ 1).
+template <int BT, int kCols>
+__device__ __forceinline__ bool qk_epilogue(const WsArgs& a, float (&v)[kCols], int row, int mtile, int col0,
+                                            bool is_q, float* scratch, uint64_t* qk_bars, uint32_t& uses,
+                                            volatile int* abort_flag) {
+  constexpr int kChunks = kCols / 16;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, quad = warp & 3, quarter = warp >> 2;
+  float* sc = scratch + (size_t)(((uses & 1) * 4 + quarter) * 4) * kCols;  // [quad][kCols]
+#pragma unroll
+  for (int c = 0; c < kChunks; ++c) {
+    float r[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) r[i] = v[16 * c + i] * v[16 * c + i];
+#pragma unroll
+    for (int half = 8, mask = 16; half >= 1; half >>= 1, mask >>= 1) {
+      const bool up = (lane & mask) != 0;
+#pragma unroll
+      for (int i = 0; i < half; ++i) {
+        const float send = up ? r[i] : r[half + i];
+        const float keep = up ? r[half + i] : r[i];
+        r[i] = keep + __shfl_xor_sync(0xffffffffu, send, mask);
+      }
+    }
+    r[0] += __shfl_xor_sync(0xffffffffu, r[0], 1);
+    if ((lane & 1) == 0) sc[quad * kCols + 16 * c + (lane >> 1)] = r[0];
+  }
+  __syncwarp();
+  if (lane == 0) ptx::mbar_arrive(&qk_bars[quarter]);
+  if (!ptx::mbar_wait(&qk_bars[quarter], uses & 1, abort_flag)) return false;
+  ++uses;
+  float inv[kChunks];
+#pragma unroll
+  for (int c = 0; c < kChunks; ++c) {
+    const int col = 16 * c + (lane >> 1);
+    const float tot = ((sc[col] + sc[kCols + col]) + sc[2 * kCols + col]) + sc[3 * kCols + col];
+    inv[c] = 1.0f / sqrtf(tot * (1.0f / 128.0f) + a.qk_eps);
+  }
+  const float* gp = is_q ? a.gamma_q : a.gamma_k;
+  const float g = gp ? __ldg(gp + row) : 1.0f;
+#pragma unroll
+  for (int j = 0; j < kCols; ++j) v[j] = v[j] * __shfl_sync(0xffffffffu, inv[j / 16], 2 * (j % 16)) * g;
+  if (a.cos_t) {
+    const bool odd = (row & 1) != 0;
+#pragma unroll
+    for (int j = 0; j < kCols; ++j) {
+      const float partner = __shfl_xor_sync(0xffffffffu, v[j], 1);
+      const int m = mtile * BT + col0 + j;
+      if (m < a.M) {
+        const float cs = __ldg(a.cos_t + (size_t)m * a.ld_rope + row);
+        const float sn = __ldg(a.sin_t + (size_t)m * a.ld_rope + row);
+        v[j] = odd ? v[j] * cs + partner * sn : v[j] * cs - partner * sn;
+      }
+    }
+  }
+  return true;
+}
+
 // Split-K reduction across the cluster (one CTA per split, cluster rank =
 // split).  After the main loop each split writes its f32 partial tile to its
 // own slot of the workspace, partials[tile][split][w][col][row] (coalesced
@@ -478,7 +556,7 @@ __device__ __forceinline__ void split_reduce_epilogue(const WsArgs& a) {
 // token bytes are in flight; TMEM holds one accumulator (columns
 // [0, NW*BT)) and one 64-column A slot per stage after it.  Folded numerics,
 // one weight.
-template <int BT, int NW, bool TA>
+template <int BT, int NW, bool TA, bool QK = false>
 __global__ void __launch_bounds__(kWsThreads, 1)
     q4_gemm_ws_kernel(const __grid_constant__ CUtensorMap tmap_x, const WsArgs a) {
   extern __shared__ uint8_t smem_raw[];
@@ -497,11 +575,15 @@ __global__ void __launch_bounds__(kWsThreads, 1)
   static_assert(TA || kNP >= 2, "at least double buffering");
   static_assert(!TA || (NW == 1 && kACol0 == 256 && BT >= 128), "TMEM operand A: one weight, slots from column 256");
   static_assert(kCols % 16 == 0, "scaler column split");
+  static_assert(!QK || (NW == 1 && BT >= 128), "QK-norm epilogue: one weight, 128- or 256-token tiles");
 
   const int S = a.stages, RS = a.rs;
   uint8_t* ring = smem;                                     // [S][A | B]
   uint8_t* raw_ring = ring + (size_t)S * kStage;            // [RS][NW][raw_w_bytes]
-  uint64_t* bars = reinterpret_cast<uint64_t*>(raw_ring + (size_t)RS * NW * a.raw_w_bytes);
+  // QK: the epilogue's per-quarter partial sums, [2][4 quarters][4 quads][kCols] f32
+  float* qk_scratch = reinterpret_cast<float*>(raw_ring + (size_t)RS * NW * a.raw_w_bytes);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(qk_scratch) +
+                                               (QK ? (size_t)32 * kCols * sizeof(float) : 0));
   uint64_t* full = bars;
   uint64_t* empty = full + S;
   uint64_t* raw_full = empty + S;
@@ -509,7 +591,8 @@ __global__ void __launch_bounds__(kWsThreads, 1)
   uint64_t* part_full = raw_empty + RS;
   uint64_t* part_empty = part_full + kNP;
   uint64_t* sk_bars = part_empty + kNP;  // stream-K: [0] head published, [1] head partial ready
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sk_bars + 2);
+  uint64_t* qk_bars = sk_bars + 2;       // QK: one per column quarter
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(qk_bars + (QK ? 4 : 0));
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -526,6 +609,8 @@ __global__ void __launch_bounds__(kWsThreads, 1)
     for (int i = 0; i < kNP; ++i) { ptx::mbar_init(&part_full[i], 1); ptx::mbar_init(&part_empty[i], kWsScalerWarps); }
     ptx::mbar_init(&sk_bars[0], kWsScalerWarps);
     ptx::mbar_init(&sk_bars[1], 1);
+    if (QK)
+      for (int i = 0; i < 4; ++i) ptx::mbar_init(&qk_bars[i], 4);
     *abort_flag = 0;
     ptx::fence_mbar_init();
   }
@@ -745,6 +830,7 @@ __global__ void __launch_bounds__(kWsThreads, 1)
     uint32_t pph = 0;
     bool ok = true;
     bool split_synced = false;  // this warp has passed the split's cluster barrier
+    uint32_t qk_uses = 0;       // QK: scratch buffer / barrier phase of this warp
     if (a.lockstep && lane == 0) {
       // both partial buffers start free: the first use of each stage
       for (int i = 0; i < S; ++i) ptx::mbar_arrive(&full[i]);
@@ -805,6 +891,26 @@ __global__ void __launch_bounds__(kWsThreads, 1)
         if (un.kind == kUnitTail && !sk_absorb<BT, NW, kCols>(a, acc, row, col0, ring, &sk_bars[1], abort_flag)) {
           ok = false;
           break;
+        }
+      }
+      if constexpr (QK) {
+        const bool is_q = ntile < a.qk_q;
+        if (is_q || ntile < a.qk_q + a.qk_k) {
+          // a q or k head: bias, QK-norm + RoPE (every lane takes part), store
+          const float b0 = (a.bias[0] && n < a.N) ? __ldg(a.bias[0] + n) : 0.0f;
+#pragma unroll
+          for (int j = 0; j < kCols; ++j) acc[0][j] += b0;
+          if (!qk_epilogue<BT, kCols>(a, acc[0], row, mtile, col0, is_q, qk_scratch, qk_bars, qk_uses,
+                                      abort_flag)) {
+            ok = false;
+            break;
+          }
+          if (n < a.N) {
+#pragma unroll
+            for (int j = 0; j < kCols; ++j)
+              if (m0 + j < a.M) store_y(a, m0 + j, n, acc[0][j]);
+          }
+          continue;
         }
       }
       if (n < a.N) {
@@ -873,9 +979,9 @@ size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 // pool the block was launched with when ptxas gave every thread exactly
 // kWsRegsLaunch registers.  Checked once per instantiation before any launch
 // (a mismatch would make setmaxnreg.inc wait forever).
-template <int BT, int NW, bool TA>
+template <int BT, int NW, bool TA, bool QK = false>
 cudaError_t prepare_ws_kernel(size_t smem_bytes, bool* ok_regs) {
-  auto kern = q4_gemm_ws_kernel<BT, NW, TA>;
+  auto kern = q4_gemm_ws_kernel<BT, NW, TA, QK>;
   static int checked = 0;  // 0 unknown, 1 ok, -1 bad
   if (checked == 0) {
     cudaFuncAttributes attr;
@@ -897,10 +1003,10 @@ cudaError_t prepare_ws_kernel(size_t smem_bytes, bool* ok_regs) {
   return cudaSuccess;
 }
 
-template <int BT, int NW, bool TA = false>
+template <int BT, int NW, bool TA = false, bool QK = false>
 cudaError_t launch_ws(const GemmPlan& plan, const CUtensorMap& tmap, const WsArgs& args, cudaStream_t stream,
                       bool* ok_regs) {
-  cudaError_t e = prepare_ws_kernel<BT, NW, TA>(plan.smem_bytes, ok_regs);
+  cudaError_t e = prepare_ws_kernel<BT, NW, TA, QK>(plan.smem_bytes, ok_regs);
   if (e != cudaSuccess || !*ok_regs) return e;
   // Launched as a programmatic dependent of the activation-staging grid
   // before it (only the token loads wait for that grid, see the kernel), and
@@ -927,7 +1033,7 @@ cudaError_t launch_ws(const GemmPlan& plan, const CUtensorMap& tmap, const WsArg
   }
   cfg.attrs = attr;
   cfg.numAttrs = n;
-  e = cudaLaunchKernelEx(&cfg, q4_gemm_ws_kernel<BT, NW, TA>, tmap, args);
+  e = cudaLaunchKernelEx(&cfg, q4_gemm_ws_kernel<BT, NW, TA, QK>, tmap, args);
   note_launch();
   return e;
 }
@@ -1060,7 +1166,7 @@ static size_t sk_part_bytes(int grid, int nw, int bt) {
 }
 
 static bq4_status plan_for_bt(const bq4_weight* w, int nw, int64_t M, int device, int bt, GemmPlan* p,
-                              double* cost, bool allow_sk) {
+                              double* cost, bool allow_sk, bool qk) {
   p->bt = bt;
   p->mtiles = (int)((M + p->bt - 1) / p->bt);
   p->ntiles = (int)w->ntiles;
@@ -1085,7 +1191,9 @@ static bq4_status plan_for_bt(const bq4_weight* w, int nw, int64_t M, int device
   const int max_stages = p->ta ? (512 - 256) / 64 : 4;  // TA: one 64-column TMEM A slot per stage
   const int np = p->ta ? 256 / p->bt : 512 / (nw * p->bt);  // TMEM partial buffers of the kernel
   const size_t raw_stage = (size_t)nw * p->raw_w_bytes;
-  const size_t budget = 227 * 1024 - 1024 /*align*/ - 512 /*barriers*/;
+  // QK: the epilogue's partial sums, 2 x 16 warps x BT/4 columns of f32
+  const size_t qk_bytes = qk ? (size_t)32 * (p->bt / 4) * sizeof(float) : 0;
+  const size_t budget = 227 * 1024 - 1024 /*align*/ - 512 /*barriers*/ - qk_bytes;
   int S = 0, RS = 0;
   for (int s = max_stages; s >= 2 && !S; --s) {
     if ((size_t)s * stage_bytes + raw_stage > budget) continue;
@@ -1114,8 +1222,9 @@ static bq4_status plan_for_bt(const bq4_weight* w, int nw, int64_t M, int device
   // accumulates into partial s.
   p->lockstep = (p->exact && w->block == 128 && S <= np) ? 1 : 0;
   if (getenv("BQ4_NO_LOCKSTEP")) p->lockstep = 0;
-  p->smem_bytes = 1024 + (size_t)S * stage_bytes + (size_t)RS * raw_stage +
-                  (size_t)(2 * S + 2 * RS + 2 * np + 2) * 8 + 16;
+  p->qk = qk ? 1 : 0;
+  p->smem_bytes = 1024 + (size_t)S * stage_bytes + (size_t)RS * raw_stage + qk_bytes +
+                  (size_t)(2 * S + 2 * RS + 2 * np + 2 + (qk ? 4 : 0)) * 8 + 16;
 
   // Split-K factor: minimise the estimated makespan (µs, measured on B200):
   // waves x (128-K stages per unit x stage time + unit fill + the cluster
@@ -1128,7 +1237,7 @@ static bq4_status plan_for_bt(const bq4_weight* w, int nw, int64_t M, int device
   int best_s = 1;
   double best_t = 1e30;
   const int max_s = nks < kMaxSplit ? nks : kMaxSplit;
-  for (int s = 1; s <= max_s; ++s) {
+  for (int s = 1; s <= (qk ? 1 : max_s); ++s) {  // the QK epilogue needs whole-K tiles
     const int units = tiles * s;
     if (s > 1 && (units > s * cluster_capacity(p->bt, nw, s, p->smem_bytes, device) || units > sms)) continue;
     const int waves = (units + sms - 1) / sms;
@@ -1144,6 +1253,7 @@ static bq4_status plan_for_bt(const bq4_weight* w, int nw, int64_t M, int device
   if (const char* f = getenv("BQ4_FORCE_KSPLIT")) {
     int v = atoi(f);
     if (v >= 1) best_s = v < max_s ? v : max_s;
+    if (qk) best_s = 1;
     while (best_s > 1 && (tiles * best_s > best_s * cluster_capacity(p->bt, nw, best_s, p->smem_bytes, device) ||
                           tiles * best_s > sms))
       --best_s;
@@ -1205,7 +1315,7 @@ static bq4_status plan_for_bt(const bq4_weight* w, int nw, int64_t M, int device
 }
 
 
-bq4_status plan_gemm(const bq4_weight* w, int nw, int64_t M, int device, GemmPlan* p, bool allow_sk) {
+bq4_status plan_gemm(const bq4_weight* w, int nw, int64_t M, int device, GemmPlan* p, bool allow_sk, bool qk) {
   if (M <= 0) return set_error(BQ4_EINVAL_SHAPE, "M must be positive (got %lld)", (long long)M);
   if (M > (int64_t)1 << 30) return set_error(BQ4_EINVAL_SHAPE, "M too large");
   memset(p, 0, sizeof(*p));
@@ -1222,7 +1332,7 @@ bq4_status plan_gemm(const bq4_weight* w, int nw, int64_t M, int device, GemmPla
   // both formulations on the same shapes).
   if (const char* f = getenv("BQ4_FORCE_FOLDED"))
     if (f[0] == '1') p->exact = 0;
-  // Token tile: every candidate up to 2M (64 always) is planned and costed;
+  // Token tile: every candidate up to 2M (the smallest always) is planned and costed;
   // BQ4_FORCE_BT=64|128|256 pins it (tuning).
   int forced = 0;
   if (const char* f = getenv("BQ4_FORCE_BT")) {
@@ -1235,10 +1345,12 @@ bq4_status plan_gemm(const bq4_weight* w, int nw, int64_t M, int device, GemmPla
   bq4_status last = BQ4_OK;
   for (int bt : {256, 128, 64}) {
     if (nw == 2 && bt == 256) continue;
-    if (forced ? bt != forced : (bt != 64 && bt > 2 * M)) continue;
+    if (qk && bt == 64) continue;  // the QK epilogue reduces over 32+ token columns per thread
+    const int smallest = qk ? 128 : 64;  // always a candidate, however small M is
+    if (forced ? bt != forced : (bt != smallest && bt > 2 * M)) continue;
     GemmPlan cand = base;
     double cost = 0.0;
-    last = plan_for_bt(w, nw, M, device, bt, &cand, &cost, allow_sk);
+    last = plan_for_bt(w, nw, M, device, bt, &cand, &cost, allow_sk, qk);
     if (last != BQ4_OK) continue;
     if (!have || cost < best - 1e-9) {
       *p = cand;
@@ -1323,12 +1435,28 @@ bq4_status run_gemm(const GemmPlan& plan, const bq4_weight* const* ws, const voi
   args.sk_w = plan.sk_tiles * (int)(w0->nkc / 2);
   args.sk_part = sk_part;
   args.sk_flag = sk_flag;
+  if (plan.qk) {
+    if (!io.qk) return set_error(BQ4_EINVAL_ARG, "a QK-norm plan needs its parameters");
+    args.qk_q = io.qk->q_heads;
+    args.qk_k = io.qk->k_heads;
+    args.qk_eps = io.qk->eps;
+    args.gamma_q = io.qk->gamma_q;
+    args.gamma_k = io.qk->gamma_k;
+    args.cos_t = io.qk->cos_t;
+    args.sin_t = io.qk->sin_t;
+    args.ld_rope = (int)io.qk->ld_rope;
+  }
   args.act = act;
   args.raw_s_bytes = plan.raw_s_bytes;
   args.raw_w_bytes = plan.raw_w_bytes;
 
   bool ok_regs = true;
-  if (plan.nw == 1) {
+  if (plan.qk) {
+    if (plan.nw != 1 || plan.ksplit != 1 || plan.bt < 128) return set_error(BQ4_EUNSUPPORTED, "QK-norm plan shape");
+    if (plan.ta) e = launch_ws<256, 1, true, true>(plan, tmap, args, stream, &ok_regs);
+    else if (plan.bt == 256) e = launch_ws<256, 1, false, true>(plan, tmap, args, stream, &ok_regs);
+    else e = launch_ws<128, 1, false, true>(plan, tmap, args, stream, &ok_regs);
+  } else if (plan.nw == 1) {
     if (plan.ta && plan.bt == 256) e = launch_ws<256, 1, true>(plan, tmap, args, stream, &ok_regs);
     else if (plan.ta) e = launch_ws<128, 1, true>(plan, tmap, args, stream, &ok_regs);
     else if (plan.bt == 256) e = launch_ws<256, 1>(plan, tmap, args, stream, &ok_regs);

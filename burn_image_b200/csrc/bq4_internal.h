@@ -67,6 +67,11 @@ cudaError_t launch_dequant_raw(const uint32_t* words, const float* scales, int64
 cudaError_t launch_convert_x(const float* x, int64_t M, int64_t K, int64_t ldx, int64_t Kp,
                              void* xh, unsigned* flags, int nflags, cudaStream_t s);
 cudaError_t launch_zero_flags(unsigned* flags, int nflags, cudaStream_t s);
+// QK-norm + RoPE over `heads` heads of hd (even, <= 256) per token; cos/sin
+// NULL skips the rotation, gamma NULL means ones.
+cudaError_t launch_qk_norm_rope(const void* x, int x_f16, int64_t M, int heads, int hd, int64_t ldx,
+                                const float* gamma, float eps, const float* cos_t, const float* sin_t, int64_t ldr,
+                                void* y, int y_f16, int64_t ldy, cudaStream_t s);
 
 // Packed-Q4 row selection (q_select on dim 0), optionally dequantized.
 cudaError_t launch_select_rows(const uint32_t* values, const float* scales, int64_t rows, int64_t cols, int block,
@@ -92,6 +97,7 @@ struct GemmPlan {
   int nfast;       // 1: N tile varies fastest along the unit order
   int pdl;         // 1: GEMM launched as a programmatic dependent of the staging grid
   int ta;          // 1: operand A (dequantized weights) staged in TMEM, not shared memory
+  int qk;          // 1: QK-norm + RoPE epilogue (every 128-feature tile one head)
   int stages, a_stages, raw_stages;  // B ring, A ring, raw ring depths
   uint32_t raw_s_bytes;  // scale bytes per weight per raw stage (folded)
   uint32_t raw_w_bytes;  // shared-memory bytes per weight per raw stage
@@ -103,16 +109,31 @@ struct GemmPlan {
   size_t workspace_bytes;
 };
 
-// allow_sk = false plans without the stream-K tail (smaller workspace).
-bq4_status plan_gemm(const bq4_weight* w, int nw, int64_t M, int device, GemmPlan* plan, bool allow_sk = true);
+// allow_sk = false plans without the stream-K tail (smaller workspace);
+// qk = true plans the QK-norm + RoPE epilogue (whole-K tiles of 128 or 256
+// tokens, shared memory for its reduction).
+bq4_status plan_gemm(const bq4_weight* w, int nw, int64_t M, int device, GemmPlan* plan, bool allow_sk = true,
+                     bool qk = false);
 
 // Activation / output formats of one GEMM call: x f32 (staged to f16 in the
 // workspace) or f16 (read in place; needs K == Kp), y f32 or f16 with row
 // pitch ldy elements (0 = N).
+// Parameters of the QK-norm + RoPE epilogue (head_dim 128).
+struct QkParams {
+  int q_heads = 0, k_heads = 0;
+  float eps = 1e-5f;
+  const float* gamma_q = nullptr;
+  const float* gamma_k = nullptr;
+  const float* cos_t = nullptr;
+  const float* sin_t = nullptr;
+  int64_t ld_rope = 128;
+};
+
 struct GemmIo {
   int x_f16 = 0;
   int y_f16 = 0;
   int64_t ldy = 0;
+  const QkParams* qk = nullptr;  // with a plan from plan_gemm(..., qk = true)
 };
 
 bq4_status run_gemm(const GemmPlan& plan, const bq4_weight* const* ws, const void* x, int64_t M,

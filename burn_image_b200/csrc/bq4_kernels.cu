@@ -419,6 +419,91 @@ cudaError_t launch_rms_renorm(const void* x, int x_f16, int64_t M, int64_t H, in
   return cudaGetLastError();
 }
 
+// QK-norm + RoPE on the q or k section of a projection output
+// (crates/burn_boogu/src/model/attention.rs:114-133, 916-928): one warp per
+// (token, head); lane l holds the pairs l, l+32, ... of the head, so the
+// interleaved rotation needs no exchange.  Every pair is loaded before any
+// is stored (in place is allowed).  The divide and sqrt are IEEE
+// (x / sqrt(mean(x^2) + eps) * gamma, the reference's order).
+template <typename TI, typename TO>
+__global__ void qk_norm_rope_kernel(const TI* __restrict__ x, int64_t M, int heads, int hd, int64_t ldx,
+                                    const float* __restrict__ gamma, float eps, const float* __restrict__ cos_t,
+                                    const float* __restrict__ sin_t, int64_t ldr, TO* __restrict__ y, int64_t ldy) {
+  constexpr int kMaxPairs = 4;  // head_dim <= 256
+  const int lane = threadIdx.x & 31;
+  const int64_t rows = M * heads;
+  const int npairs = hd >> 1;
+  for (int64_t r = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); r < rows;
+       r += (int64_t)gridDim.x * (blockDim.x >> 5)) {
+    const int64_t m = r / heads;
+    const int h = (int)(r - m * heads);
+    const TI* xr = x + m * ldx + (int64_t)h * hd;
+    float a[kMaxPairs], b[kMaxPairs];
+    float ss = 0.0f;
+#pragma unroll
+    for (int i = 0; i < kMaxPairs; ++i) {
+      const int p = lane + 32 * i;
+      a[i] = b[i] = 0.0f;
+      if (p < npairs) {
+        a[i] = static_cast<float>(xr[2 * p]);
+        b[i] = static_cast<float>(xr[2 * p + 1]);
+        ss += a[i] * a[i] + b[i] * b[i];
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    const float rms = sqrtf(ss / (float)hd + eps);
+    TO* yr = y + m * ldy + (int64_t)h * hd;
+#pragma unroll
+    for (int i = 0; i < kMaxPairs; ++i) {
+      const int p = lane + 32 * i;
+      if (p < npairs) {
+        float v0 = a[i] / rms, v1 = b[i] / rms;
+        if (gamma) {
+          v0 *= __ldg(gamma + 2 * p);
+          v1 *= __ldg(gamma + 2 * p + 1);
+        }
+        float o0 = v0, o1 = v1;
+        if (cos_t) {
+          const float* cr = cos_t + m * ldr + 2 * p;
+          const float* sr = sin_t + m * ldr + 2 * p;
+          o0 = v0 * __ldg(cr) - v1 * __ldg(sr);
+          o1 = v1 * __ldg(cr + 1) + v0 * __ldg(sr + 1);
+        }
+        yr[2 * p] = static_cast<TO>(o0);
+        yr[2 * p + 1] = static_cast<TO>(o1);
+      }
+    }
+  }
+}
+
+cudaError_t launch_qk_norm_rope(const void* x, int x_f16, int64_t M, int heads, int hd, int64_t ldx,
+                                const float* gamma, float eps, const float* cos_t, const float* sin_t, int64_t ldr,
+                                void* y, int y_f16, int64_t ldy, cudaStream_t s) {
+  const int64_t rows = M * heads;
+  const int grid = grid_for(rows * 32, 256, current_device());
+  if (x_f16) {
+    if (y_f16)
+      qk_norm_rope_kernel<__half, __half><<<grid, 256, 0, s>>>(static_cast<const __half*>(x), M, heads, hd, ldx,
+                                                              gamma, eps, cos_t, sin_t, ldr,
+                                                              static_cast<__half*>(y), ldy);
+    else
+      qk_norm_rope_kernel<__half, float><<<grid, 256, 0, s>>>(static_cast<const __half*>(x), M, heads, hd, ldx,
+                                                             gamma, eps, cos_t, sin_t, ldr, static_cast<float*>(y),
+                                                             ldy);
+  } else {
+    if (y_f16)
+      qk_norm_rope_kernel<float, __half><<<grid, 256, 0, s>>>(static_cast<const float*>(x), M, heads, hd, ldx,
+                                                             gamma, eps, cos_t, sin_t, ldr,
+                                                             static_cast<__half*>(y), ldy);
+    else
+      qk_norm_rope_kernel<float, float><<<grid, 256, 0, s>>>(static_cast<const float*>(x), M, heads, hd, ldx, gamma,
+                                                            eps, cos_t, sin_t, ldr, static_cast<float*>(y), ldy);
+  }
+  note_launch();
+  return cudaGetLastError();
+}
+
 cudaError_t launch_convert_x(const float* x, int64_t M, int64_t K, int64_t ldx, int64_t Kp,
                              void* xh, unsigned* flags, int nflags, cudaStream_t s) {
   const int vec4 = ((reinterpret_cast<uintptr_t>(x) & 15) == 0) && (ldx % 4 == 0);

@@ -317,6 +317,38 @@ class PreparedQ4Weight:
                                     _stream_ptr(self.device)))
         return y
 
+    def linear_qk_norm_rope(self, x: torch.Tensor, q_heads: int, k_heads: int, head_dim: int,
+                            bias: Optional[torch.Tensor] = None, gamma_q: Optional[torch.Tensor] = None,
+                            gamma_k: Optional[torch.Tensor] = None, eps: float = 1e-5,
+                            cos: Optional[torch.Tensor] = None, sin: Optional[torch.Tensor] = None,
+                            out: Optional[torch.Tensor] = None, out_dtype: torch.dtype = torch.float32) -> torch.Tensor:
+        """bq4_linear_qk_norm_rope: the q/k/v projection (features = q heads,
+        k heads, v heads of head_dim) with QK-norm + RoPE on the q and k heads;
+        fused into the GEMM epilogue when head_dim == 128.  x as linear_ex;
+        gamma_q/gamma_k [head_dim], cos/sin [M, head_dim] float32."""
+        dt = {torch.float32: L.DTYPE_F32, torch.float16: L.DTYPE_F16}
+        if x.device != self.device or x.dtype not in dt or x.dim() != 2 or x.shape[1] != self.K or x.stride(1) != 1:
+            raise Bq4Error(L.EINVAL_ARG, f"x must be a float32/float16 [M, {self.K}] row view on {self.device}")
+        M = x.shape[0]
+        y = out if out is not None else torch.empty((M, self.N), dtype=out_dtype, device=self.device)
+        if y.device != self.device or y.dtype not in dt or tuple(y.shape) != (M, self.N) or y.stride(1) != 1:
+            raise Bq4Error(L.EINVAL_ARG, f"out must be a float32/float16 [{M}, {self.N}] row view on {self.device}")
+        if bias is not None:
+            bias = _vec(bias, self.N, self.device)
+        for t in (gamma_q, gamma_k, cos, sin):
+            if t is not None and (t.dtype != torch.float32 or t.device != self.device or t.stride(-1) != 1):
+                raise Bq4Error(L.EINVAL_ARG, "gamma/cos/sin must be float32 on the weight's device")
+        ld_rope = cos.stride(0) if cos is not None else 0
+        n = ctypes.c_size_t()
+        check(L.lib().bq4_linear_qk_norm_rope_workspace_size(self._h, M, dt[x.dtype], head_dim, ctypes.byref(n)))
+        ws = Workspace.get(self.device, n.value) if n.value else None
+        check(L.lib().bq4_linear_qk_norm_rope(self._h, _ptr(x), dt[x.dtype], M, x.stride(0), _ptr(bias), q_heads,
+                                              k_heads, head_dim, _ptr(gamma_q), _ptr(gamma_k), ctypes.c_float(eps),
+                                              _ptr(cos), _ptr(sin), ld_rope, _ptr(y), dt[y.dtype], y.stride(0),
+                                              _ptr(ws), ws.numel() if ws is not None else 0,
+                                              _stream_ptr(self.device)))
+        return y
+
 
 def rms_renorm(x: torch.Tensor, out: torch.Tensor, eps: float = 1e-6) -> torch.Tensor:
     """out[m,:] = x[m,:] / sqrt(mean(x[m,:]^2) + eps) in one kernel (the
@@ -328,6 +360,33 @@ def rms_renorm(x: torch.Tensor, out: torch.Tensor, eps: float = 1e-6) -> torch.T
         raise Bq4Error(L.EINVAL_ARG, "rms_renorm needs float32/float16 [M, H] row views of one shape")
     check(L.lib().bq4_rms_renorm(_ptr(x), dt[x.dtype], x.shape[0], x.shape[1], x.stride(0), _ptr(out),
                                  dt[out.dtype], out.stride(0), ctypes.c_float(eps), _stream_ptr(x.device)))
+    return out
+
+
+def qk_norm_rope(x: torch.Tensor, heads: int, head_dim: int, gamma: Optional[torch.Tensor] = None,
+                 eps: float = 1e-5, cos: Optional[torch.Tensor] = None, sin: Optional[torch.Tensor] = None,
+                 out: Optional[torch.Tensor] = None, out_dtype: Optional[torch.dtype] = None) -> torch.Tensor:
+    """QK-norm + RoPE (attention.rs:114-133, 916-928) on x [M, >= heads*head_dim]
+    (float32/float16 row view): per head x / sqrt(mean(x^2) + eps) * gamma,
+    then the interleaved-pair rotation by cos/sin [M, head_dim] (float32).
+    Writes `out` (may be x itself) or a new [M, heads*head_dim] tensor."""
+    dt = {torch.float32: L.DTYPE_F32, torch.float16: L.DTYPE_F16}
+    if x.dim() != 2 or x.stride(1) != 1 or x.dtype not in dt:
+        raise Bq4Error(L.EINVAL_ARG, "qk_norm_rope needs a float32/float16 [M, W] row view")
+    M = x.shape[0]
+    if out is None:
+        out = torch.empty((M, heads * head_dim), dtype=out_dtype or x.dtype, device=x.device)
+    if out.dim() != 2 or out.stride(1) != 1 or out.dtype not in dt or out.shape[0] != M:
+        raise Bq4Error(L.EINVAL_ARG, "out must be a float32/float16 [M, W] row view")
+    for t in (gamma, cos, sin):
+        if t is not None and (t.dtype != torch.float32 or t.device != x.device or t.stride(-1) != 1):
+            raise Bq4Error(L.EINVAL_ARG, "gamma/cos/sin must be float32 on the device of x")
+    ld_rope = cos.stride(0) if cos is not None else 0
+    if cos is not None and (sin is None or sin.stride(0) != ld_rope):
+        raise Bq4Error(L.EINVAL_ARG, "cos and sin must be given together with the same row pitch")
+    check(L.lib().bq4_qk_norm_rope(_ptr(x), dt[x.dtype], M, heads, head_dim, x.stride(0), _ptr(gamma),
+                                   ctypes.c_float(eps), _ptr(cos), _ptr(sin), ld_rope, _ptr(out), dt[out.dtype],
+                                   out.stride(0), _stream_ptr(x.device)))
     return out
 
 

@@ -339,6 +339,44 @@ BQ4_API bq4_status bq4_set_sm_budget(int32_t sms);
 BQ4_API bq4_status bq4_rms_renorm(const void* x, bq4_dtype x_dtype, int64_t M, int64_t H, int64_t ldx, void* out,
                                   bq4_dtype out_dtype, int64_t ldo, float eps, bq4_stream_t stream);
 
+/*
+ * QK-norm + RoPE, the step between the q/k projections and attention
+ * (crates/burn_boogu/src/model/attention.rs:114-133): for each of M tokens
+ * and `heads` heads of head_dim values of x (row pitch ldx elements),
+ *   v = x / sqrt(mean(x^2) + eps) * gamma          (Burn nn::RmsNorm, StrictF32)
+ *   y[2p]   = v[2p] cos[2p] - v[2p+1] sin[2p]       (apply_rope, :916-928)
+ *   y[2p+1] = v[2p+1] cos[2p+1] + v[2p] sin[2p+1]
+ * with cos/sin f32 [M][head_dim] at row pitch ld_rope (both NULL: no
+ * rotation) and gamma f32 [head_dim] (NULL: ones).  x and y are f32 or f16
+ * at pitches ldx / ldy and may be the same buffer (same dtype and pitch).
+ * head_dim is even and at most 256.  Call it once for the q section and once
+ * for the k section of a projection output (their gammas differ).
+ */
+BQ4_API bq4_status bq4_qk_norm_rope(const void* x, bq4_dtype x_dtype, int64_t M, int64_t heads, int64_t head_dim,
+                                    int64_t ldx, const float* gamma, float eps, const float* cos_t,
+                                    const float* sin_t, int64_t ld_rope, void* y, bq4_dtype y_dtype, int64_t ldy,
+                                    bq4_stream_t stream);
+
+/*
+ * A q/k/v projection with QK-norm + RoPE: y = x . W + bias, whose N features
+ * are q_heads heads, then k_heads heads, then the remaining (v) heads, all of
+ * head_dim values; the q and k heads then get bq4_qk_norm_rope with gamma_q
+ * and gamma_k (the reference's separate q/k/v linears followed by
+ * attention.rs:114-133).  With head_dim == 128 every 128-feature tile of the
+ * GEMM is one head and the norm and rotation run in the GEMM's epilogue (no
+ * second pass over y); otherwise the linear is followed by bq4_qk_norm_rope
+ * in place on y.  x: f32 or f16 (as bq4_linear_ex), y: f32 or f16 at pitch
+ * ldy (0 = N).  Workspace from bq4_linear_qk_norm_rope_workspace_size.
+ */
+BQ4_API bq4_status bq4_linear_qk_norm_rope_workspace_size(const bq4_weight* w, int64_t M, bq4_dtype x_dtype,
+                                                          int64_t head_dim, size_t* bytes);
+BQ4_API bq4_status bq4_linear_qk_norm_rope(const bq4_weight* w, const void* x, bq4_dtype x_dtype, int64_t M,
+                                           int64_t ldx, const float* bias, int64_t q_heads, int64_t k_heads,
+                                           int64_t head_dim, const float* gamma_q, const float* gamma_k, float eps,
+                                           const float* cos_t, const float* sin_t, int64_t ld_rope, void* y,
+                                           bq4_dtype y_dtype, int64_t ldy, void* workspace, size_t workspace_bytes,
+                                           bq4_stream_t stream);
+
 /* Kernel launches issued by this thread since the last reset (bench accounting). */
 BQ4_API uint64_t bq4_launch_count(void);
 BQ4_API void bq4_launch_count_reset(void);

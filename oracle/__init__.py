@@ -52,6 +52,8 @@ def lib() -> ctypes.CDLL:
         _lib.orc_linear_gated_f64.restype = None
         _lib.orc_cpu_linear.argtypes = [p, p, i64, i64, i32, i32, p, i64, i64, p, i32, p, p, i32]
         _lib.orc_cpu_threads.argtypes = []
+        _lib.orc_qk_norm_rope_f64.argtypes = [p, i64, i64, i64, i64, p, ctypes.c_double, p, p, i64, p, i64]
+        _lib.orc_qk_norm_rope_f64.restype = None
     return _lib
 
 
@@ -176,6 +178,37 @@ def cpu_linear(words, scales, K, N, block, layout, x, bias=None, act=ACT_NONE, a
 
 def cpu_threads() -> int:
     return int(lib().orc_cpu_threads())
+
+
+def qk_norm_rope_f64(x: np.ndarray, heads: int, head_dim: int, gamma=None, eps: float = 1e-5,
+                     cos=None, sin=None) -> np.ndarray:
+    """RMS-normalise each head of x [M, heads*head_dim] (times gamma), then
+    rotate interleaved pairs by the per-(token, dim) cos/sin [M, head_dim];
+    f64 inside, f32 out (bq4_oracle.c orc_qk_norm_rope_f64)."""
+    x = _f32(x)
+    M = x.shape[0]
+    assert x.shape[1] >= heads * head_dim and head_dim % 2 == 0
+    g = None if gamma is None else _f32(gamma)
+    c = None if cos is None else _f32(cos)
+    s = None if sin is None else _f32(sin)
+    y = np.zeros((M, heads * head_dim), dtype=np.float32)
+    lib().orc_qk_norm_rope_f64(_ptr(x), M, heads, head_dim, x.shape[1], _ptr(g), float(eps), _ptr(c), _ptr(s),
+                               head_dim if c is None else c.shape[1], _ptr(y), heads * head_dim)
+    return y
+
+
+def rope_tables(ids: np.ndarray, axis_dims, theta: float = 10000.0):
+    """cos/sin [S, sum(axis_dims)] for position ids [S, 3]: per axis, pair p of
+    that axis' dims rotates by id * theta^(-2p/dim), each value repeated for
+    the two dims of the pair (crates/burn_boogu/src/model/denoiser.rs:992-1032)."""
+    ids = np.asarray(ids)
+    cos_parts, sin_parts = [], []
+    for axis, dim in enumerate(axis_dims):
+        inv = theta ** (-(2.0 * np.arange(dim // 2)) / dim)
+        phase = ids[:, axis:axis + 1].astype(np.float64) * inv[None, :]
+        cos_parts.append(np.repeat(np.cos(phase).astype(np.float32), 2, axis=1))
+        sin_parts.append(np.repeat(np.sin(phase).astype(np.float32), 2, axis=1))
+    return np.concatenate(cos_parts, 1), np.concatenate(sin_parts, 1)
 
 
 def rel_frobenius(actual: np.ndarray, expected: np.ndarray) -> float:

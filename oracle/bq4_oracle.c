@@ -29,6 +29,15 @@
  *       GELU-tanh (crates/burn_qwen3_vl/src/vision.rs:279,283-289) and
  *       silu(gate) * up (crates/burn_boogu/src/model/feed_forward.rs:32-36,
  *       crates/burn_qwen3_vl/src/text.rs:46-52).
+ *   - QK-norm + RoPE on the q/k projections (the consumer of the qkv linear):
+ *       crates/burn_boogu/src/model/attention.rs:114-133 (RMS-normalise q and
+ *       k per head with norm_q / norm_k, then rotate), the StrictF32 policy
+ *       crates/burn_boogu/src/model/norm.rs:86-96 (Burn nn::RmsNorm, burn-nn
+ *       0.21.0: x / sqrt(mean(x^2) + eps) * gamma over the head dimension),
+ *       apply_rope crates/burn_boogu/src/model/attention.rs:916-928
+ *       (interleaved pairs: out[2p] = x[2p] cos - x[2p+1] sin,
+ *       out[2p+1] = x[2p+1] cos + x[2p] sin), and the per-(token, dim) cos/sin
+ *       tables of crates/burn_boogu/src/model/denoiser.rs:992-1032.
  *
  * Reference arithmetic lives in third-party crates that are not vendored:
  * cubek-matmul 0.2.0 / cubek-quant 0.2.0 (GPU) and burn-ndarray 0.21.0 /
@@ -286,6 +295,40 @@ void orc_linear_gated_f64(const float* x, int64_t M, int64_t K, int64_t ldx, con
     }
     free(g);
     free(u);
+}
+
+/*
+ * QK-norm + RoPE checker, f64: for every token m and head h of
+ * x[m][h*hd + d] (row pitch ldx), v = x / sqrt(mean_d(x^2) + eps) * gamma[d]
+ * (gamma NULL: 1), then, when cos_t/sin_t are given ([m][d], row pitch ldr),
+ * the interleaved-pair rotation.  y has row pitch ldy.  hd must be even.
+ */
+void orc_qk_norm_rope_f64(const float* x, int64_t M, int64_t heads, int64_t hd, int64_t ldx,
+                          const float* gamma, double eps, const float* cos_t, const float* sin_t,
+                          int64_t ldr, float* y, int64_t ldy) {
+    double* v = (double*)malloc(sizeof(double) * (size_t)hd);
+    for (int64_t m = 0; m < M; ++m) {
+        for (int64_t h = 0; h < heads; ++h) {
+            const float* xr = x + m * ldx + h * hd;
+            double ss = 0.0;
+            for (int64_t d = 0; d < hd; ++d) ss += (double)xr[d] * (double)xr[d];
+            const double rms = sqrt(ss / (double)hd + eps);
+            for (int64_t d = 0; d < hd; ++d) v[d] = (double)xr[d] / rms * (gamma ? (double)gamma[d] : 1.0);
+            float* yr = y + m * ldy + h * hd;
+            for (int64_t d = 0; d < hd; d += 2) {
+                if (cos_t && sin_t) {
+                    const double c0 = cos_t[m * ldr + d], s0 = sin_t[m * ldr + d];
+                    const double c1 = cos_t[m * ldr + d + 1], s1 = sin_t[m * ldr + d + 1];
+                    yr[d] = (float)(v[d] * c0 - v[d + 1] * s0);
+                    yr[d + 1] = (float)(v[d + 1] * c1 + v[d] * s1);
+                } else {
+                    yr[d] = (float)v[d];
+                    yr[d + 1] = (float)v[d + 1];
+                }
+            }
+        }
+    }
+    free(v);
 }
 
 /* ------------------------------------------------------------------------
