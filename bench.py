@@ -224,7 +224,39 @@ ROWS = [
     # next row of the path: the packed-Q4 embedding lookup (q_select + dequantize), 256
     # prompt tokens from a 151936 x 2560 table (rows = table rows, K = row width)
     ("f1_q4_embedding_256_of_151936x2560", 256, 2560, 151936, "select", 0),
+    # next row: the DiT qkv projection with QK-norm + RoPE on its q and k heads (24 + 24 + 24
+    # heads of 128), fused into the GEMM epilogue; "us_unfused" = linear + two norm passes
+    ("f3_qkv_qknorm_rope_4352x3072x9216", 4352, 3072, 9216, "qknorm", 0),
 ]
+
+
+def _graph_time(dev, items, call):
+    """Device time of one call: every item's call captured once in a CUDA
+    graph, the graph replayed, total / (replays x items)."""
+    import torch
+    side = torch.cuda.Stream(dev)
+    side.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(side):
+        for it in items:
+            call(it)  # warm-up on the capture stream (workspace, attributes)
+    torch.cuda.current_stream(dev).wait_stream(side)
+    torch.cuda.synchronize(dev)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=side):
+        for it in items:
+            call(it)
+    graph.replay()
+    torch.cuda.synchronize(dev)
+    reps = max(3, int(40 // len(items)))
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        graph.replay()
+    e1.record()
+    torch.cuda.synchronize(dev)
+    del graph
+    return e0.elapsed_time(e1) * 1e-3 / (reps * len(items))
 
 
 def config_rows(dev, peaks, names=None):
@@ -255,51 +287,50 @@ def config_rows(dev, peaks, names=None):
         sets = max(2, min(64, int(2 * 126e6 // set_bytes) + 1))
         g = torch.Generator(device=dev).manual_seed(11)
         items = []
+        hd = 128
+        heads = N // hd // 3  # q, k and v heads (qknorm rows)
         for _ in range(sets):
             ws = [q4.PreparedQ4Weight(*tp._random_packed(K, N, QBLOCK, g, dev), K, N, QBLOCK, L.LAYOUT_ROW, dev)
                   for _ in range(nw)]
             bias = [torch.randn(N, generator=g, device=dev) * 0.02 for _ in range(nw)]
             x = torch.randn((M, K), generator=g, device=dev)
             y = torch.empty((M, N), device=dev)
-            items.append((ws, bias, x, y))
+            extra = None
+            if kind == "qknorm":
+                phase = torch.rand((M, hd), generator=g, device=dev) * 6.0
+                extra = (torch.rand(hd, generator=g, device=dev) + 0.5, torch.rand(hd, generator=g, device=dev) + 0.5,
+                         torch.cos(phase), torch.sin(phase))
+            items.append((ws, bias, x, y, extra))
 
         def call(it):
-            ws, bias, x, y = it
+            ws, bias, x, y, extra = it
             if nw == 2:
                 q4.linear_gated(ws[0], ws[1], x, bias[0], bias[1], out=y)
+            elif kind == "qknorm":
+                gq, gk, cs, sn = extra
+                ws[0].linear_qk_norm_rope(x, heads, heads, hd, bias[0], gq, gk, 1e-5, cs, sn, out=y)
             else:
                 ws[0].linear(x, bias[0], act, out=y)
 
-        side = torch.cuda.Stream(dev)
-        side.wait_stream(torch.cuda.current_stream(dev))
-        with torch.cuda.stream(side):
-            for it in items:
-                call(it)  # warm-up on the capture stream (workspace, attributes)
-        torch.cuda.current_stream(dev).wait_stream(side)
-        torch.cuda.synchronize(dev)
-        graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(graph, stream=side):
-            for it in items:
-                call(it)
-        graph.replay()
-        torch.cuda.synchronize(dev)
-        reps = max(3, int(40 // sets))
-        e0 = torch.cuda.Event(enable_timing=True)
-        e1 = torch.cuda.Event(enable_timing=True)
-        e0.record()
-        for _ in range(reps):
-            graph.replay()
-        e1.record()
-        torch.cuda.synchronize(dev)
+        def call_unfused(it):
+            ws, bias, x, y, (gq, gk, cs, sn) = it
+            ws[0].linear(x, bias[0], out=y)
+            q4.qk_norm_rope(y[:, :heads * hd], heads, hd, gq, 1e-5, cs, sn, out=y[:, :heads * hd])
+            q4.qk_norm_rope(y[:, heads * hd:2 * heads * hd], heads, hd, gk, 1e-5, cs, sn,
+                            out=y[:, heads * hd:2 * heads * hd])
+
+        t = _graph_time(dev, items, call)
+        t_unfused = _graph_time(dev, items, call_unfused) if kind == "qknorm" else None
         q4.poll_device_error()
-        t = e0.elapsed_time(e1) * 1e-3 / (reps * sets)
         flops = 2 * M * K * N * nw
-        nbytes = wbytes + M * K * 4 + M * N * 4 + nw * N * 4
+        nbytes = wbytes + M * K * 4 + M * N * 4 + nw * N * 4 + (2 * M * hd * 4 if kind == "qknorm" else 0)
         t_star = max(nbytes / (hbm * 1e9), flops / (tfl * 1e12))
         bound = "hbm" if nbytes / (hbm * 1e9) > flops / (tfl * 1e12) else "tensor"
         out[name] = {"us": t * 1e6, "tflops": flops / t / 1e12, "gbs": nbytes / t / 1e9, "bound": bound,
                      "t_star_us": t_star * 1e6, "frac": t_star / t, "sets": sets}
-        del graph, items
+        if t_unfused is not None:
+            out[name]["us_unfused"] = t_unfused * 1e6
+        del items
         torch.cuda.empty_cache()
     return out
 

@@ -447,15 +447,23 @@ __device__ __forceinline__ bool qk_epilogue(const WsArgs& a, float (&v)[kCols], 
 #pragma unroll
   for (int j = 0; j < kCols; ++j) v[j] = v[j] * __shfl_sync(0xffffffffu, inv[j / 16], 2 * (j % 16)) * g;
   if (a.cos_t) {
+    // 8 tokens at a time, every table load issued before any is used (one
+    // L2 round trip per 8 tokens instead of per token)
     const bool odd = (row & 1) != 0;
+    const int m0 = mtile * BT + col0;
 #pragma unroll
-    for (int j = 0; j < kCols; ++j) {
-      const float partner = __shfl_xor_sync(0xffffffffu, v[j], 1);
-      const int m = mtile * BT + col0 + j;
-      if (m < a.M) {
-        const float cs = __ldg(a.cos_t + (size_t)m * a.ld_rope + row);
-        const float sn = __ldg(a.sin_t + (size_t)m * a.ld_rope + row);
-        v[j] = odd ? v[j] * cs + partner * sn : v[j] * cs - partner * sn;
+    for (int c = 0; c < kCols; c += 8) {
+      float cs[8], sn[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int m = m0 + c + i < a.M ? m0 + c + i : a.M - 1;
+        cs[i] = __ldg(a.cos_t + (size_t)m * a.ld_rope + row);
+        sn[i] = __ldg(a.sin_t + (size_t)m * a.ld_rope + row);
+      }
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float partner = __shfl_xor_sync(0xffffffffu, v[c + i], 1);
+        v[c + i] = odd ? v[c + i] * cs[i] + partner * sn[i] : v[c + i] * cs[i] - partner * sn[i];
       }
     }
   }
