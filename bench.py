@@ -319,8 +319,13 @@ def config_rows(dev, peaks, names=None):
             q4.qk_norm_rope(y[:, heads * hd:2 * heads * hd], heads, hd, gk, 1e-5, cs, sn,
                             out=y[:, heads * hd:2 * heads * hd])
 
+        def call_norm(it):  # one standalone pass over the q heads, in place (HBM-bound)
+            ws, bias, x, y, (gq, gk, cs, sn) = it
+            q4.qk_norm_rope(y[:, :heads * hd], heads, hd, gq, 1e-5, cs, sn, out=y[:, :heads * hd])
+
         t = _graph_time(dev, items, call)
         t_unfused = _graph_time(dev, items, call_unfused) if kind == "qknorm" else None
+        t_norm = _graph_time(dev, items, call_norm) if kind == "qknorm" else None
         q4.poll_device_error()
         flops = 2 * M * K * N * nw
         nbytes = wbytes + M * K * 4 + M * N * 4 + nw * N * 4 + (2 * M * hd * 4 if kind == "qknorm" else 0)
@@ -329,7 +334,11 @@ def config_rows(dev, peaks, names=None):
         out[name] = {"us": t * 1e6, "tflops": flops / t / 1e12, "gbs": nbytes / t / 1e9, "bound": bound,
                      "t_star_us": t_star * 1e6, "frac": t_star / t, "sets": sets}
         if t_unfused is not None:
+            # the standalone pass: reads and writes M x heads x 128 f32 and reads the two tables
+            norm_bytes = 2 * M * heads * hd * 4 + 2 * M * hd * 4
             out[name]["us_unfused"] = t_unfused * 1e6
+            out[name]["norm_pass"] = {"us": t_norm * 1e6, "gbs": norm_bytes / t_norm / 1e9,
+                                      "frac_hbm": norm_bytes / t_norm / 1e9 / hbm}
         del items
         torch.cuda.empty_cache()
     return out
