@@ -56,6 +56,10 @@ def parse():
     ap.add_argument("--chunks", type=int, default=1, help="token chunks of the stack pipeline (each chunk's "
                                                           "all-reduces overlap the other chunks' GEMMs)")
     ap.add_argument("--sm-budget", type=int, default=0, help="cap the SMs a GEMM occupies (0: all)")
+    ap.add_argument("--tp-exchange", choices=["p2p", "nccl"], default="nccl",
+                    help="row-parallel exchange at N > 1: p2p (GEMM epilogue writes each row's partial to its "
+                         "owner over NVLink peer memory, owner sums + renormalises, f16 all-gather) or nccl "
+                         "(f32 all-reduce of the partials)")
     ap.add_argument("--rows-only", action="store_true", help="print only the per-config rows (1 GPU)")
     ap.add_argument("--rows", default=None, help="comma-separated row names to run (with --rows-only)")
     return ap.parse_args()
@@ -418,8 +422,9 @@ def run_ours(args):
     if args.sm_budget > 0:
         from burn_image_b200 import q4 as _q
         _q.set_sm_budget(args.sm_budget)
+    exchange = args.tp_exchange if (world > 1 and args.act_dtype == "f16" and chunks == 1) else "nccl"
     stack = tp.DiTQ4Stack(args.blocks, HIDDEN, QKV, MLP, dev, seed=1, block=QBLOCK, group=group,
-                          act_dtype=act_dtype, chunks=chunks)
+                          act_dtype=act_dtype, chunks=chunks, exchange=exchange)
     M = args.tokens
     g = torch.Generator(device=dev).manual_seed(42)
     x0 = torch.randn((M, HIDDEN), generator=g, device=dev)
@@ -619,6 +624,7 @@ def run_ours(args):
                        "activations": ("f16 between linears (written by each epilogue, read in place)"
                                        if args.act_dtype == "f16" else "f32 between linears"),
                        "token_chunks": chunks, "sm_budget": args.sm_budget or None,
+                       "tp_exchange": exchange if world > 1 else None,
                        "l2": "inputs larger than L2 (1.44 GB of Q4 weights streamed per step)"},
             "roofline": {"bound": "tensor", "achieved": achieved_tflops, "peak": peak, "unit": "TFLOP/s",
                          "frac": achieved_tflops / peak, "traffic": traffic,
@@ -642,6 +648,7 @@ def run_ours(args):
         }
         print(json.dumps(out))
     if world > 1:
+        stack.close()
         dist.barrier()
         dist.destroy_process_group()
 

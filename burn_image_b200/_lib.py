@@ -24,6 +24,8 @@ ACT_NONE, ACT_GELU_TANH, ACT_SILU = 0, 1, 2
 NOALLOC_SCRATCH_BYTES = 32 << 20  # BQ4_NOALLOC_SCRATCH_BYTES
 NUMERICS_AUTO, NUMERICS_EXACT, NUMERICS_FOLDED = 0, 1, 2
 DTYPE_F32, DTYPE_F16 = 0, 1
+MAX_PEERS = 8            # BQ4_MAX_PEERS
+IPC_HANDLE_BYTES = 64    # BQ4_IPC_HANDLE_BYTES
 
 # Every symbol include/bq4.h declares, with (restype, argtypes).
 _p, _i32, _i64, _sz, _u64 = ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64, ctypes.c_size_t, ctypes.c_uint64
@@ -62,6 +64,13 @@ SIGNATURES = {
     "bq4_qk_norm_rope": (_st, [_p, _i32, _i64, _i64, _i64, _i64, _p, ctypes.c_float, _p, _p, _i64, _p, _i32, _i64,
                                _p]),
     "bq4_linear_qk_norm_rope_workspace_size": (_st, [_p, _i64, _i32, _i64, ctypes.POINTER(_sz)]),
+    "bq4_peer_buffer_alloc": (_st, [_sz, _i32, ctypes.POINTER(_p), _p]),
+    "bq4_peer_buffer_open": (_st, [_p, _i32, ctypes.POINTER(_p)]),
+    "bq4_peer_buffer_close": (_st, [_p]),
+    "bq4_peer_buffer_free": (_st, [_p, _i32]),
+    "bq4_peer_signal_wait": (_st, [_p, _p, _i32, _i32, ctypes.c_uint32, _p]),
+    "bq4_reduce_slices": (_st, [_p, _i32, _i64, _i64, _i64, _i32, ctypes.c_float, _p, _i32, _i64, _p]),
+    "bq4_linear_rowscatter": (_st, [_p, _p, _i32, _i64, _i64, _p, _i32, _p, _i32, _i32, _i64, _p, _sz, _p]),
     "bq4_linear_qk_norm_rope": (_st, [_p, _p, _i32, _i64, _i64, _p, _i64, _i64, _i64, _p, _p, ctypes.c_float, _p, _p,
                                       _i64, _p, _i32, _i64, _p, _sz, _p]),
     "bq4_launch_count": (_u64, []),

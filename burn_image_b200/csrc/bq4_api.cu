@@ -574,6 +574,128 @@ bq4_status bq4_linear_qk_norm_rope(const bq4_weight* w, const void* x, bq4_dtype
                   reinterpret_cast<cudaStream_t>(stream), io);
 }
 
+// ---------------------------------------------------------------- peer exchange
+
+bq4_status bq4_peer_buffer_alloc(size_t bytes, int32_t device, void** ptr, void* handle) {
+  if (!ptr || !handle || bytes == 0) return set_error(BQ4_EINVAL_ARG, "ptr/handle is NULL or bytes is 0");
+  DeviceGuard guard(device);
+  void* p = nullptr;
+  cudaError_t e = cudaMalloc(&p, bytes);
+  if (e != cudaSuccess) return check_cuda(e, "cudaMalloc (peer buffer)");
+  e = cudaMemset(p, 0, bytes);
+  cudaIpcMemHandle_t h;
+  if (e == cudaSuccess) e = cudaIpcGetMemHandle(&h, p);
+  if (e != cudaSuccess) {
+    cudaFree(p);
+    return check_cuda(e, "peer buffer set-up");
+  }
+  static_assert(sizeof(cudaIpcMemHandle_t) == BQ4_IPC_HANDLE_BYTES, "IPC handle size");
+  memcpy(handle, &h, sizeof(h));
+  *ptr = p;
+  return BQ4_OK;
+}
+
+bq4_status bq4_peer_buffer_open(const void* handle, int32_t device, void** ptr) {
+  if (!ptr || !handle) return set_error(BQ4_EINVAL_ARG, "ptr/handle is NULL");
+  DeviceGuard guard(device);
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof(h));
+  cudaError_t e = cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess);
+  return e == cudaSuccess ? BQ4_OK : check_cuda(e, "cudaIpcOpenMemHandle");
+}
+
+bq4_status bq4_peer_buffer_close(void* ptr) {
+  if (!ptr) return BQ4_OK;
+  cudaError_t e = cudaIpcCloseMemHandle(ptr);
+  return e == cudaSuccess ? BQ4_OK : check_cuda(e, "cudaIpcCloseMemHandle");
+}
+
+bq4_status bq4_peer_buffer_free(void* ptr, int32_t device) {
+  if (!ptr) return BQ4_OK;
+  DeviceGuard guard(device);
+  cudaError_t e = cudaFree(ptr);
+  return e == cudaSuccess ? BQ4_OK : check_cuda(e, "cudaFree (peer buffer)");
+}
+
+bq4_status bq4_peer_signal_wait(uint32_t* flags, uint32_t* const* peer_flags, int32_t nranks, int32_t rank,
+                                uint32_t epoch, bq4_stream_t stream) {
+  if (!flags || !peer_flags) return set_error(BQ4_EINVAL_ARG, "flags is NULL");
+  if (nranks < 1 || nranks > BQ4_MAX_PEERS || rank < 0 || rank >= nranks)
+    return set_error(BQ4_EINVAL_ARG, "rank %d of %d ranks (at most %d)", (int)rank, (int)nranks, BQ4_MAX_PEERS);
+  for (int r = 0; r < nranks; ++r)
+    if (r != rank && !peer_flags[r]) return set_error(BQ4_EINVAL_ARG, "peer_flags[%d] is NULL", r);
+  if (nranks == 1) return BQ4_OK;
+  cudaError_t e = launch_peer_signal_wait(flags, peer_flags, nranks, rank, epoch, device_error_word(),
+                                          reinterpret_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? BQ4_OK : check_cuda(e, "peer signal/wait launch");
+}
+
+bq4_status bq4_reduce_slices(const float* recv, int32_t nranks, int64_t rows, int64_t H, int64_t ld, int32_t renorm,
+                             float eps, void* out, bq4_dtype out_dtype, int64_t ldo, bq4_stream_t stream) {
+  if (!recv || !out) return set_error(BQ4_EINVAL_ARG, "recv/out is NULL");
+  if (out_dtype != BQ4_DTYPE_F32 && out_dtype != BQ4_DTYPE_F16) return set_error(BQ4_EINVAL_ARG, "dtype unknown");
+  if (nranks < 1 || nranks > BQ4_MAX_PEERS || rows <= 0 || H <= 0 || H % 4 || H > 8192 || ld < H || ld % 4 ||
+      ldo < H || ldo % 4)
+    return set_error(BQ4_EINVAL_SHAPE, "nranks=%d rows=%lld H=%lld (H %% 4 == 0, <= 8192) ld=%lld ldo=%lld",
+                     (int)nranks, (long long)rows, (long long)H, (long long)ld, (long long)ldo);
+  if (renorm && !(eps > 0.0f)) return set_error(BQ4_EINVAL_ARG, "eps must be positive");
+  if (!aligned(recv, 16) || !aligned(out, out_dtype == BQ4_DTYPE_F16 ? 8 : 16))
+    return set_error(BQ4_EALIGN, "recv/out misaligned");
+  cudaError_t e = launch_reduce_slices(recv, nranks, rows, H, ld, renorm, eps, out, out_dtype == BQ4_DTYPE_F16, ldo,
+                                       reinterpret_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? BQ4_OK : check_cuda(e, "reduce_slices launch");
+}
+
+bq4_status bq4_linear_rowscatter(const bq4_weight* w, const void* x, bq4_dtype x_dtype, int64_t M, int64_t ldx,
+                                 const float* bias, bq4_act act, float* const* y_ranks, int32_t nranks, int32_t rank,
+                                 int64_t ldy, void* workspace, size_t workspace_bytes, bq4_stream_t stream) {
+  bq4_status st = check_weight(w, "w");
+  if (st) return st;
+  if (act != BQ4_ACT_NONE && act != BQ4_ACT_GELU_TANH && act != BQ4_ACT_SILU)
+    return set_error(BQ4_EINVAL_ARG, "act %d unknown", (int)act);
+  if (x_dtype != BQ4_DTYPE_F32 && x_dtype != BQ4_DTYPE_F16) return set_error(BQ4_EINVAL_ARG, "x_dtype unknown");
+  if (!x || !y_ranks) return set_error(BQ4_EINVAL_ARG, "x/y_ranks is NULL");
+  if (nranks < 1 || nranks > BQ4_MAX_PEERS || rank < 0 || rank >= nranks)
+    return set_error(BQ4_EINVAL_ARG, "rank %d of %d ranks (at most %d)", (int)rank, (int)nranks, BQ4_MAX_PEERS);
+  for (int r = 0; r < nranks; ++r)
+    if (!y_ranks[r] || !aligned(y_ranks[r], 4)) return set_error(BQ4_EINVAL_ARG, "y_ranks[%d] is NULL or misaligned", r);
+  if (M <= 0 || M % nranks || M > 0x7fffffff)
+    return set_error(BQ4_EINVAL_SHAPE, "M=%lld must be a positive multiple of nranks=%d", (long long)M, (int)nranks);
+  if (ldx < w->K) return set_error(BQ4_EINVAL_SHAPE, "ldx=%lld < K=%lld", (long long)ldx, (long long)w->K);
+  if (ldy == 0) ldy = w->N;
+  if (ldy < w->N) return set_error(BQ4_EINVAL_SHAPE, "ldy=%lld < N=%lld", (long long)ldy, (long long)w->N);
+  const int x16 = x_dtype == BQ4_DTYPE_F16;
+  if (x16) {
+    if (w->K != w->Kp) return set_error(BQ4_EINVAL_SHAPE, "f16 x needs K %% 128 == 0 (K=%lld)", (long long)w->K);
+    if (!aligned(x, 16) || ldx % 8) return set_error(BQ4_EALIGN, "f16 x needs a 16-byte aligned base and ldx %% 8 == 0");
+  } else if (!aligned(x, 4)) {
+    return set_error(BQ4_EALIGN, "x not 4-byte aligned");
+  }
+  GemmPlan plan;
+  st = plan_gemm(w, 1, M, w->device, &plan);
+  if (st) return st;
+  const size_t need = x16 ? plan.sk_bytes + plan.partial_bytes : plan.workspace_bytes;
+  if (need) {
+    if (!workspace) return set_error(BQ4_EWORKSPACE, "workspace is NULL");
+    if (!aligned(workspace, 256)) return set_error(BQ4_EALIGN, "workspace not 256-byte aligned");
+    if (workspace_bytes < need)
+      return set_error(BQ4_EWORKSPACE, "workspace %zu < required %zu bytes", workspace_bytes, need);
+  }
+  DeviceGuard guard(w->device);
+  const bq4_weight* ws[1] = {w};
+  const float* b[1] = {bias};
+  GemmIo io;
+  io.x_f16 = x16;
+  io.y_f16 = 0;
+  io.ldy = ldy;
+  io.sc_rows = (int)(M / nranks);
+  io.sc_rank = rank;
+  io.sc_nranks = nranks;
+  io.sc_y = y_ranks;
+  return run_gemm(plan, ws, x, M, ldx, b, (int)act, nullptr, y_ranks[rank], workspace,
+                  reinterpret_cast<cudaStream_t>(stream), io);
+}
+
 bq4_status bq4_linear_ex_workspace_size(const bq4_weight* w, int64_t M, bq4_dtype x_dtype, size_t* bytes) {
   if (x_dtype != BQ4_DTYPE_F32 && x_dtype != BQ4_DTYPE_F16)
     return set_error(BQ4_EINVAL_ARG, "x_dtype %d unknown", (int)x_dtype);

@@ -184,6 +184,10 @@ struct WsArgs {
   // heads, the rest pass through.  cos_t / sin_t [M][128] at row pitch
   // ld_rope (NULL: no rotation); gamma_q / gamma_k [128] (NULL: ones).
   int qk_q, qk_k, ld_rope;
+  // Row scatter (kernels built with SC): row m goes to sc_y[m / sc_rows] at
+  // row sc_rank * sc_rows + m % sc_rows (the owner's receive buffer, f32, pitch ldy).
+  float* sc_y[BQ4_MAX_PEERS];
+  int sc_rows, sc_rank;
   float qk_eps;
   const float* gamma_q;
   const float* gamma_k;
@@ -198,6 +202,19 @@ __device__ __forceinline__ void store_y(const WsArgs& a, int m, int n, float v) 
     reinterpret_cast<__half*>(a.y)[(size_t)m * a.ldy + n] = __float2half_rn(v);
   else
     reinterpret_cast<float*>(a.y)[(size_t)m * a.ldy + n] = v;
+}
+
+// Output element (m, n); kernels built with SC (row scatter) write row m to
+// its owner rank's receive buffer sc_y[m / sc_rows] at row
+// sc_rank * sc_rows + m % sc_rows (f32, pitch ldy).  Without SC, store_y.
+template <bool SC>
+__device__ __forceinline__ void store_out(const WsArgs& a, int m, int n, float v) {
+  if constexpr (SC) {
+    const int owner = m / a.sc_rows;
+    a.sc_y[owner][(size_t)(a.sc_rank * a.sc_rows + (m - owner * a.sc_rows)) * a.ldy + n] = v;
+  } else {
+    store_y(a, m, n, v);
+  }
 }
 
 // Unit u -> (tile, split) and its chunk range [kc0, kc1); splits cut at
@@ -491,7 +508,7 @@ __device__ __forceinline__ void split_publish(const WsArgs& a, int tile, int spl
 // Owner side: warp w takes every 16th owned column from c0 + w, lane l the
 // features 4l..4l+3 (bias loaded once); all splits' loads of a column are in
 // flight before they are summed.
-template <int BT, int NW>
+template <int BT, int NW, bool SC>
 __device__ __forceinline__ void split_reduce_epilogue(const WsArgs& a) {
   const int SPL = a.ksplit;
   const int rank = (int)ptx::cluster_ctarank();
@@ -540,7 +557,7 @@ __device__ __forceinline__ void split_reduce_epilogue(const WsArgs& a) {
         if (a.aux) o[i] *= __ldg(a.aux + (size_t)m * a.N + (n + i < a.N ? n + i : a.N - 1));
       }
     }
-    if (a.yvec && n + 3 < a.N) {
+    if (!SC && a.yvec && n + 3 < a.N) {
       if (a.y_f16) {
         const __half2 h01 = __floats2half2_rn(o[0], o[1]), h23 = __floats2half2_rn(o[2], o[3]);
         *reinterpret_cast<uint2*>(reinterpret_cast<__half*>(a.y) + (size_t)m * a.ldy + n) =
@@ -552,7 +569,7 @@ __device__ __forceinline__ void split_reduce_epilogue(const WsArgs& a) {
     } else {
 #pragma unroll
       for (int i = 0; i < 4; ++i)
-        if (n + i < a.N) store_y(a, m, n + i, o[i]);
+        if (n + i < a.N) store_out<SC>(a, m, n + i, o[i]);
     }
   }
 }
@@ -564,7 +581,7 @@ __device__ __forceinline__ void split_reduce_epilogue(const WsArgs& a) {
 // token bytes are in flight; TMEM holds one accumulator (columns
 // [0, NW*BT)) and one 64-column A slot per stage after it.  Folded numerics,
 // one weight.
-template <int BT, int NW, bool TA, bool QK = false>
+template <int BT, int NW, bool TA, bool QK = false, bool SC = false>
 __global__ void __launch_bounds__(kWsThreads, 1)
     q4_gemm_ws_kernel(const __grid_constant__ CUtensorMap tmap_x, const WsArgs a) {
   extern __shared__ uint8_t smem_raw[];
@@ -584,6 +601,7 @@ __global__ void __launch_bounds__(kWsThreads, 1)
   static_assert(!TA || (NW == 1 && kACol0 == 256 && BT >= 128), "TMEM operand A: one weight, slots from column 256");
   static_assert(kCols % 16 == 0, "scaler column split");
   static_assert(!QK || (NW == 1 && BT >= 128), "QK-norm epilogue: one weight, 128- or 256-token tiles");
+  static_assert(!SC || (NW == 1 && !QK), "row scatter: one weight, plain epilogue");
 
   const int S = a.stages, RS = a.rs;
   uint8_t* ring = smem;                                     // [S][A | B]
@@ -936,13 +954,13 @@ __global__ void __launch_bounds__(kWsThreads, 1)
               v = apply_act(acc[0][j] + b0, act);
               if (a.aux) v *= __ldg(a.aux + (size_t)m * a.N + n);
             }
-            store_y(a, m, n, v);
+            store_out<SC>(a, m, n, v);
           }
         }
       }
     }
     if (!ok) record_error_flag(abort_flag, BQ4_ETIMEOUT);
-    if (split_synced) split_reduce_epilogue<BT, NW>(a);
+    if (split_synced) split_reduce_epilogue<BT, NW, SC>(a);
     if (a.ksplit > 1 && !split_synced) {
       // Every role of every CTA of the cluster passes the split's cluster
       // barrier exactly once (each role branch has its own); a scaler warp
@@ -987,9 +1005,9 @@ size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 // pool the block was launched with when ptxas gave every thread exactly
 // kWsRegsLaunch registers.  Checked once per instantiation before any launch
 // (a mismatch would make setmaxnreg.inc wait forever).
-template <int BT, int NW, bool TA, bool QK = false>
+template <int BT, int NW, bool TA, bool QK = false, bool SC = false>
 cudaError_t prepare_ws_kernel(size_t smem_bytes, bool* ok_regs) {
-  auto kern = q4_gemm_ws_kernel<BT, NW, TA, QK>;
+  auto kern = q4_gemm_ws_kernel<BT, NW, TA, QK, SC>;
   static int checked = 0;  // 0 unknown, 1 ok, -1 bad
   if (checked == 0) {
     cudaFuncAttributes attr;
@@ -1011,10 +1029,10 @@ cudaError_t prepare_ws_kernel(size_t smem_bytes, bool* ok_regs) {
   return cudaSuccess;
 }
 
-template <int BT, int NW, bool TA = false, bool QK = false>
+template <int BT, int NW, bool TA = false, bool QK = false, bool SC = false>
 cudaError_t launch_ws(const GemmPlan& plan, const CUtensorMap& tmap, const WsArgs& args, cudaStream_t stream,
                       bool* ok_regs) {
-  cudaError_t e = prepare_ws_kernel<BT, NW, TA, QK>(plan.smem_bytes, ok_regs);
+  cudaError_t e = prepare_ws_kernel<BT, NW, TA, QK, SC>(plan.smem_bytes, ok_regs);
   if (e != cudaSuccess || !*ok_regs) return e;
   // Launched as a programmatic dependent of the activation-staging grid
   // before it (only the token loads wait for that grid, see the kernel), and
@@ -1041,7 +1059,7 @@ cudaError_t launch_ws(const GemmPlan& plan, const CUtensorMap& tmap, const WsArg
   }
   cfg.attrs = attr;
   cfg.numAttrs = n;
-  e = cudaLaunchKernelEx(&cfg, q4_gemm_ws_kernel<BT, NW, TA, QK>, tmap, args);
+  e = cudaLaunchKernelEx(&cfg, q4_gemm_ws_kernel<BT, NW, TA, QK, SC>, tmap, args);
   note_launch();
   return e;
 }
@@ -1443,6 +1461,13 @@ bq4_status run_gemm(const GemmPlan& plan, const bq4_weight* const* ws, const voi
   args.sk_w = plan.sk_tiles * (int)(w0->nkc / 2);
   args.sk_part = sk_part;
   args.sk_flag = sk_flag;
+  if (io.sc_rows) {
+    if (io.y_f16 || io.sc_nranks < 1 || io.sc_nranks > BQ4_MAX_PEERS || !io.sc_y)
+      return set_error(BQ4_EINVAL_ARG, "row scatter needs f32 output and 1..%d ranks", BQ4_MAX_PEERS);
+    args.sc_rows = io.sc_rows;
+    args.sc_rank = io.sc_rank;
+    for (int r = 0; r < io.sc_nranks; ++r) args.sc_y[r] = io.sc_y[r];
+  }
   if (plan.qk) {
     if (!io.qk) return set_error(BQ4_EINVAL_ARG, "a QK-norm plan needs its parameters");
     args.qk_q = io.qk->q_heads;
@@ -1459,7 +1484,14 @@ bq4_status run_gemm(const GemmPlan& plan, const bq4_weight* const* ws, const voi
   args.raw_w_bytes = plan.raw_w_bytes;
 
   bool ok_regs = true;
-  if (plan.qk) {
+  if (args.sc_rows) {
+    if (plan.nw != 1 || plan.qk) return set_error(BQ4_EUNSUPPORTED, "row scatter: one weight, plain epilogue");
+    if (plan.ta && plan.bt != 256) return set_error(BQ4_EUNSUPPORTED, "row scatter with 128-token TMEM operands");
+    if (plan.ta) e = launch_ws<256, 1, true, false, true>(plan, tmap, args, stream, &ok_regs);
+    else if (plan.bt == 256) e = launch_ws<256, 1, false, false, true>(plan, tmap, args, stream, &ok_regs);
+    else if (plan.bt == 128) e = launch_ws<128, 1, false, false, true>(plan, tmap, args, stream, &ok_regs);
+    else e = launch_ws<64, 1, false, false, true>(plan, tmap, args, stream, &ok_regs);
+  } else if (plan.qk) {
     if (plan.nw != 1 || plan.ksplit != 1 || plan.bt < 128) return set_error(BQ4_EUNSUPPORTED, "QK-norm plan shape");
     if (plan.ta) e = launch_ws<256, 1, true, true>(plan, tmap, args, stream, &ok_regs);
     else if (plan.bt == 256) e = launch_ws<256, 1, false, true>(plan, tmap, args, stream, &ok_regs);

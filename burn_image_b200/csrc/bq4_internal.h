@@ -67,6 +67,11 @@ cudaError_t launch_dequant_raw(const uint32_t* words, const float* scales, int64
 cudaError_t launch_convert_x(const float* x, int64_t M, int64_t K, int64_t ldx, int64_t Kp,
                              void* xh, unsigned* flags, int nflags, cudaStream_t s);
 cudaError_t launch_zero_flags(unsigned* flags, int nflags, cudaStream_t s);
+// Tensor-parallel exchange over peer memory (bq4_peer.cu).
+cudaError_t launch_peer_signal_wait(unsigned* local, unsigned* const* peers, int nranks, int rank, unsigned epoch,
+                                    int* err, cudaStream_t s);
+cudaError_t launch_reduce_slices(const float* recv, int P, int64_t R, int64_t H, int64_t ld, int renorm, float eps,
+                                 void* out, int out_f16, int64_t ldo, cudaStream_t s);
 // QK-norm + RoPE over `heads` heads of hd (even, <= 256) per token; cos/sin
 // NULL skips the rotation, gamma NULL means ones.
 cudaError_t launch_qk_norm_rope(const void* x, int x_f16, int64_t M, int heads, int hd, int64_t ldx,
@@ -133,6 +138,10 @@ struct GemmIo {
   int x_f16 = 0;
   int y_f16 = 0;
   int64_t ldy = 0;
+  // Row scatter (f32 y): output row m goes to sc_y[m / sc_rows] at row
+  // sc_rank * sc_rows + m % sc_rows (each owner's [nranks][rows][ldy] receive buffer).
+  int sc_rows = 0, sc_rank = 0, sc_nranks = 0;
+  float* const* sc_y = nullptr;
   const QkParams* qk = nullptr;  // with a plan from plan_gemm(..., qk = true)
 };
 

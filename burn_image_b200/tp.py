@@ -114,6 +114,22 @@ class RowParallelQ4Linear:
             dist.all_reduce(y, op=dist.ReduceOp.SUM, group=self.group)
         return y
 
+    def forward_scatter(self, x_local: torch.Tensor, ex: "PeerExchange", b: int) -> None:
+        """This rank's partial product, written by the GEMM epilogue straight
+        into the receive buffer b of each output row's owner rank
+        (bq4_linear_rowscatter), then the cross-rank signal/wait: afterwards
+        every rank holds all partials of its own rows."""
+        w = self.weight
+        M = x_local.shape[0]
+        dt = {torch.float32: L.DTYPE_F32, torch.float16: L.DTYPE_F16}
+        n = ctypes.c_size_t()
+        L.check(L.lib().bq4_linear_ex_workspace_size(w.handle, M, dt[x_local.dtype], ctypes.byref(n)))
+        ws = Workspace.get(w.device, n.value) if n.value else None
+        L.check(L.lib().bq4_linear_rowscatter(w.handle, _ptr(x_local), dt[x_local.dtype], M, x_local.stride(0),
+                                              _ptr(self.bias), L.ACT_NONE, ex.targets(b), ex.size, ex.rank, ex.H,
+                                              _ptr(ws), ws.numel() if ws is not None else 0, _stream_ptr(w.device)))
+        ex.signal_wait()
+
     def forward_ex(self, x_local: torch.Tensor, out: torch.Tensor, async_op: bool = False):
         """Same, with float16 or float32 activations; the partial sums are
         reduced in ``out``'s dtype.  With ``async_op`` the all-reduce is only
@@ -127,6 +143,73 @@ class RowParallelQ4Linear:
         return None if async_op else out
 
 
+class PeerExchange:
+    """Receive buffers and flags shared between the ranks of `group` through
+    CUDA IPC (bq4_peer_buffer_*), for the row-parallel exchange over NVLink
+    peer memory: two [P][rows][H] f32 receive buffers used alternately (the
+    barrier of one exchange proves every rank has finished reading the buffer
+    before it), and one [P] u32 flag array per rank for bq4_peer_signal_wait.
+    """
+
+    def __init__(self, device: torch.device, group, rows: int, H: int):
+        self.device, self.group = device, group
+        self.rank, self.size = _world(group)
+        self.rows, self.H = rows, H
+        lib = L.lib()
+        sizes = [self.size * rows * H * 4] * 2 + [4 * L.MAX_PEERS]
+        self.local, handles = [], []
+        for n in sizes:
+            ptr, h = ctypes.c_void_p(), (ctypes.c_uint8 * L.IPC_HANDLE_BYTES)()
+            L.check(lib.bq4_peer_buffer_alloc(n, device.index, ctypes.byref(ptr), h))
+            self.local.append(ptr.value)
+            handles.append(bytes(h))
+        everyone = [None] * self.size
+        dist.all_gather_object(everyone, handles, group=group)
+        self.peer = [[None] * self.size for _ in sizes]  # [buffer][rank] -> device pointer mapped here
+        self.opened = []
+        for r in range(self.size):
+            for b in range(len(sizes)):
+                if r == self.rank:
+                    self.peer[b][r] = self.local[b]
+                    continue
+                ptr = ctypes.c_void_p()
+                h = (ctypes.c_uint8 * L.IPC_HANDLE_BYTES).from_buffer_copy(everyone[r][b])
+                L.check(lib.bq4_peer_buffer_open(h, device.index, ctypes.byref(ptr)))
+                self.peer[b][r] = ptr.value
+                self.opened.append(ptr.value)
+        self.epoch = 0
+
+    def targets(self, b: int):
+        """y_ranks argument of bq4_linear_rowscatter for receive buffer b."""
+        return (ctypes.c_void_p * self.size)(*self.peer[b])
+
+    def signal_wait(self):
+        self.epoch += 1
+        flags = (ctypes.c_void_p * self.size)(*self.peer[2])
+        L.check(L.lib().bq4_peer_signal_wait(ctypes.c_void_p(self.local[2]), flags, self.size, self.rank,
+                                             ctypes.c_uint32(self.epoch), _stream_ptr(self.device)))
+
+    def reduce(self, b: int, out: torch.Tensor, renorm: bool, eps: float = 1e-6):
+        """Sum this rank's rows of receive buffer b over the ranks (rank
+        order), optionally RMS-renormalised, into `out` [rows, H] (f16/f32)."""
+        dt = {torch.float32: L.DTYPE_F32, torch.float16: L.DTYPE_F16}
+        L.check(L.lib().bq4_reduce_slices(ctypes.c_void_p(self.local[b]), self.size, self.rows, self.H, self.H,
+                                          1 if renorm else 0, ctypes.c_float(eps), _ptr(out), dt[out.dtype],
+                                          out.stride(0), _stream_ptr(self.device)))
+
+    def close(self):
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)
+        lib = L.lib()
+        for p in self.opened:
+            lib.bq4_peer_buffer_close(ctypes.c_void_p(p))
+        self.opened = []
+        dist.barrier(group=self.group)
+        for p in self.local:
+            lib.bq4_peer_buffer_free(ctypes.c_void_p(p), self.device.index)
+        self.local = []
+
+
 class DiTQ4Stack:
     """The DiT-shaped layer stack of the benchmark: per block a fused qkv
     (column-parallel, hidden -> 3*hidden), o (row-parallel over the v slice,
@@ -137,8 +220,17 @@ class DiTQ4Stack:
     columns of the qkv output as its input shard."""
 
     def __init__(self, blocks: int, hidden: int, qkv: int, mlp: int, device: torch.device, seed: int = 0,
-                 block: int = 128, group=None, act_dtype: torch.dtype = torch.float32, chunks: int = 1):
+                 block: int = 128, group=None, act_dtype: torch.dtype = torch.float32, chunks: int = 1,
+                 exchange: str = "nccl"):
         self.device = device
+        # exchange "p2p" (P > 1, float16 activations): the row-parallel
+        # partials go to each row's owner through the GEMM epilogue over NVLink
+        # peer memory, the owner sums (and renormalises) its rows, and an NCCL
+        # all-gather of float16 rows rebuilds the replicated activations
+        # (_forward_p2p); "nccl": a float32 all-reduce of the partials.
+        self.exchange = exchange
+        self.group = group
+        self._peer = None
         # act_dtype float16: activations stay in the GEMM's operand format
         # between linears (bq4_linear_ex), the renorm is one kernel.  The
         # row-parallel partials (P > 1) are still summed in float32: float16
@@ -186,6 +278,8 @@ class DiTQ4Stack:
         """The stack on x [M, hidden]; the renormalised float32 output goes to
         ``out`` when given (else an internal buffer reused by the next call)."""
         if self.act_dtype == torch.float16:
+            if self.exchange == "p2p" and self.size > 1:
+                return self._forward_p2p(x, on_linear, out)
             return self._forward_chained(x, on_linear, out)
         M = x.shape[0]
         P = self.size
@@ -256,6 +350,57 @@ class DiTQ4Stack:
                 pending[c].wait()
             rms_renorm(d[a:b], out[a:b])
         return out
+
+
+    def _forward_p2p(self, x: torch.Tensor, on_linear=None, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """The float16-chained stack with the row-parallel exchange over peer
+        memory.  Rank r owns token rows [r*M/P, (r+1)*M/P).  Per block: qkv
+        (column-parallel) -> o partials scattered to the row owners -> owners
+        sum them into float16 rows -> all-gather -> up (column-parallel) ->
+        down partials scattered -> owners sum and renormalise -> all-gather.
+        Same arithmetic as _forward_chained with a float32 all-reduce (the
+        owner adds the partials in rank order; the renorm and float16
+        rounding are the same kernels' math).  Returns the renormalised
+        float32 output of the last block."""
+        M = x.shape[0]
+        P, r = self.size, self.rank
+        if M % P:
+            raise ValueError(f"p2p exchange: M={M} not divisible by {P} ranks")
+        R = M // P
+        if self._peer is None or self._peer.rows != R:
+            if self._peer is not None:
+                self._peer.close()
+            self._peer = PeerExchange(self.device, self.group, R, self.hidden)
+        ex = self._peer
+        qkv_local, hid_local, mlp_local = self.qkv // P, self.hidden // P, self.mlp // P
+        f16 = torch.float16
+        xin = self._buf("x16", (M, self.hidden), f16)
+        t = self._buf("qkv16", (M, qkv_local), f16)
+        o16 = self._buf("o16", (M, self.hidden), f16)
+        u = self._buf("up16", (M, mlp_local), f16)
+        if out is None:
+            out = self._buf("out32", (M, self.hidden), torch.float32)
+        mine = slice(r * R, (r + 1) * R)
+        n = len(self.layers)
+        for i, layer in enumerate(self.layers):
+            xc = x if i == 0 else xin
+            _timed(on_linear, "qkv", lambda: layer["qkv"].forward_ex(xc, out=t))
+            v = t[:, qkv_local - hid_local:]
+            _timed(on_linear, "o", lambda: layer["o"].forward_scatter(v, ex, 0))
+            ex.reduce(0, o16[mine], renorm=False)
+            dist.all_gather_into_tensor(o16, o16[mine], group=self.group)
+            _timed(on_linear, "up", lambda: layer["up"].forward_ex(o16, out=u))
+            _timed(on_linear, "down", lambda: layer["down"].forward_scatter(u, ex, 1))
+            dst = out if i == n - 1 else xin
+            ex.reduce(1, dst[mine], renorm=True)
+            dist.all_gather_into_tensor(dst, dst[mine], group=self.group)
+        return out
+
+    def close(self):
+        """Release the peer-exchange buffers (collective over the group)."""
+        if self._peer is not None:
+            self._peer.close()
+            self._peer = None
 
 
 def _timed(cb, name, fn):

@@ -377,6 +377,49 @@ BQ4_API bq4_status bq4_linear_qk_norm_rope(const bq4_weight* w, const void* x, b
                                            bq4_dtype y_dtype, int64_t ldy, void* workspace, size_t workspace_bytes,
                                            bq4_stream_t stream);
 
+/*
+ * Tensor-parallel exchange over NVLink peer memory (one process per GPU of
+ * one node).  It replaces the all-reduce after a row-parallel linear
+ * (o, down):
+ *   1. bq4_linear_rowscatter: every rank computes its K-partial and the GEMM
+ *      epilogue writes output row m straight into the receive buffer of its
+ *      owner rank m / (M / nranks), at row (rank * M/nranks + m % (M/nranks)),
+ *      so the exchange overlaps the GEMM;
+ *   2. bq4_peer_signal_wait: a one-thread kernel publishes `epoch` to every
+ *      peer's flag array and waits (bounded, 10 s) until all peers did;
+ *   3. bq4_reduce_slices: each owner sums the nranks partials of its rows in
+ *      rank order, optionally RMS-renormalising them, into f16/f32 rows.
+ * Buffers are cudaMalloc allocations shared with CUDA IPC handles
+ * (BQ4_IPC_HANDLE_BYTES bytes, exchanged by the caller, e.g. with an
+ * all-gather); plain peer loads and stores between GPUs.  The reference runs
+ * on one device and has no counterpart.
+ */
+#define BQ4_MAX_PEERS 8
+#define BQ4_IPC_HANDLE_BYTES 64
+/* Allocates `bytes` of zeroed device memory on `device` and writes its IPC handle. */
+BQ4_API bq4_status bq4_peer_buffer_alloc(size_t bytes, int32_t device, void** ptr, void* handle);
+/* Maps a peer's buffer (handle from bq4_peer_buffer_alloc in another process) on `device`. */
+BQ4_API bq4_status bq4_peer_buffer_open(const void* handle, int32_t device, void** ptr);
+BQ4_API bq4_status bq4_peer_buffer_close(void* ptr);
+BQ4_API bq4_status bq4_peer_buffer_free(void* ptr, int32_t device);
+/* flags: this rank's [nranks] u32 array; peer_flags[r]: rank r's array as
+ * mapped here (peer_flags[rank] may be `flags`).  epoch grows by one per use. */
+BQ4_API bq4_status bq4_peer_signal_wait(uint32_t* flags, uint32_t* const* peer_flags, int32_t nranks, int32_t rank,
+                                        uint32_t epoch, bq4_stream_t stream);
+/* out[r] = sum_s recv[s][r] (s = 0..nranks-1 in order) for rows r < rows of
+ * H floats (recv pitch ld, H % 4 == 0, H <= 8192, 16-byte aligned), then
+ * x / sqrt(mean(x^2) + eps) per row when renorm; out f32 or f16 at pitch ldo. */
+BQ4_API bq4_status bq4_reduce_slices(const float* recv, int32_t nranks, int64_t rows, int64_t H, int64_t ld,
+                                     int32_t renorm, float eps, void* out, bq4_dtype out_dtype, int64_t ldo,
+                                     bq4_stream_t stream);
+/* bq4_linear_ex with f32 output scattered by row owner (see above):
+ * y_ranks[r] = rank r's receive buffer [nranks][M/nranks][ldy] f32 as mapped
+ * here; M % nranks == 0.  Workspace as bq4_linear_ex. */
+BQ4_API bq4_status bq4_linear_rowscatter(const bq4_weight* w, const void* x, bq4_dtype x_dtype, int64_t M,
+                                         int64_t ldx, const float* bias, bq4_act act, float* const* y_ranks,
+                                         int32_t nranks, int32_t rank, int64_t ldy, void* workspace,
+                                         size_t workspace_bytes, bq4_stream_t stream);
+
 /* Kernel launches issued by this thread since the last reset (bench accounting). */
 BQ4_API uint64_t bq4_launch_count(void);
 BQ4_API void bq4_launch_count_reset(void);

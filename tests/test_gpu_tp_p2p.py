@@ -1,0 +1,81 @@
+"""GPU, 2 devices: the tensor-parallel DiT stack with the row-parallel exchange
+over NVLink peer memory (GEMM epilogue scatters each output row's partial to
+its owner, the owner sums and renormalises its rows, f16 all-gather) against
+the same stack with an NCCL float32 all-reduce, and against the unsharded
+stack.  With two ranks both exchanges add the same two partials, so the
+outputs must be bit-identical; repeated calls (advancing barrier epochs)
+must give the same bits.  Skipped on hosts with fewer than 2 GPUs.
+"""
+import os
+import socket
+from datetime import timedelta
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+WORLD = 2
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, world, port, results):
+    import torch.distributed as dist
+
+    from burn_image_b200 import q4, tp
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
+                      LOCAL_RANK=str(rank))
+    dev = torch.device("cuda", rank)
+    torch.cuda.set_device(dev)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60), device_id=dev)
+    try:
+        M, H, QKV, MLP = 300, 512, 1536, 2048
+        g = torch.Generator(device=dev).manual_seed(7)
+        x = torch.randn((M, H), generator=g, device=dev)
+        p2p = tp.DiTQ4Stack(2, H, QKV, MLP, dev, seed=3, act_dtype=torch.float16, exchange="p2p")
+        ar = tp.DiTQ4Stack(2, H, QKV, MLP, dev, seed=3, act_dtype=torch.float16, exchange="nccl")
+        a = p2p.forward(x).clone()
+        a2 = p2p.forward(x).clone()
+        b = ar.forward(x).clone()
+        local = tp.DiTQ4Stack(2, H, QKV, MLP, dev, seed=3, act_dtype=torch.float16, group=tp.LOCAL)
+        c = local.forward(x).clone()
+        torch.cuda.synchronize(dev)
+        q4.poll_device_error()
+        rel = (torch.linalg.norm(a.double() - c.double()) / torch.linalg.norm(c.double())).item()
+        results[rank] = (bool(torch.equal(a, b)), bool(torch.equal(a, a2)), rel, None)
+        p2p.close()
+    except Exception as e:  # reported to the parent
+        results[rank] = (False, False, float("nan"), repr(e))
+    finally:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def test_p2p_exchange_matches_allreduce():
+    if torch.cuda.device_count() < WORLD:
+        pytest.skip(f"needs {WORLD} GPUs")
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    results = ctx.Manager().dict()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, WORLD, port, results)) for r in range(WORLD)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=300)
+    alive = [p for p in procs if p.is_alive()]
+    for p in alive:  # only our own children, by handle
+        p.kill()
+        p.join(timeout=30)
+    assert not alive, "a rank did not finish"
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+    for r in range(WORLD):
+        same, repeat, rel, err = results[r]
+        assert err is None, f"rank {r}: {err}"
+        assert same, f"rank {r}: p2p exchange differs from the all-reduce"
+        assert repeat, f"rank {r}: repeated calls differ"
+        assert rel <= 5e-3, f"rank {r}: rel to unsharded {rel}"
