@@ -231,6 +231,13 @@ ROWS = [
     # next row: the DiT qkv projection with QK-norm + RoPE on its q and k heads (24 + 24 + 24
     # heads of 128), fused into the GEMM epilogue; "us_unfused" = linear + two norm passes
     ("f3_qkv_qknorm_rope_4352x3072x9216", 4352, 3072, 9216, "qknorm", 0),
+    # next row: packed-F16 storage (the VAE's weights), kind::tf32.  The reference's own
+    # throughput smokes (a 4096^3 matmul; a 512 -> 512 3x3 conv at 64 x 64) and the
+    # largest FLUX-VAE decoder conv (128 -> 128 channels, 3x3, 1024 x 1024).
+    # (name, M, K, N, kind, act); conv rows: M = output positions, K = in * 9, N = out.
+    ("f4_f16_matmul_4096x4096x4096", 4096, 4096, 4096, "f16mm", 0),
+    ("f4_f16_conv3x3_512to512_64x64", 64 * 64, 512 * 9, 512, "f16conv", 0),
+    ("f4_vae_conv3x3_128to128_1024x1024", 1024 * 1024, 128 * 9, 128, "f16conv", 0),
 ]
 
 
@@ -284,6 +291,9 @@ def config_rows(dev, peaks, names=None):
             continue
         if kind == "select":
             out[name] = _select_row(dev, M, K, N, hbm)
+            continue
+        if kind in ("f16mm", "f16conv"):
+            out[name] = _f16_row(dev, kind, M, K, N, hbm, tfl)
             continue
         nw = 2 if kind == "gated" else 1
         wbytes = nw * (N * K // 2 + N * K // QBLOCK * 4)
@@ -396,6 +406,93 @@ def _select_row(dev, n, cols, rows, hbm):
     del graph
     return {"us": t * 1e6, "tflops": 0.0, "gbs": nbytes / t / 1e9, "bound": "hbm", "t_star_us": t_star * 1e6,
             "frac": t_star / t, "sets": sets}
+
+
+def _f16_row(dev, kind, M, K, N, hbm, tfl):
+    """Packed-F16 rows (kind::tf32): the prepared-weight matmul, or the whole
+    bq4_conv2d call (NCHW staging + implicit GEMM) on a square image of
+    sqrt(M) x sqrt(M) with padding 1.  Graph-replayed over enough sets that
+    each call starts cold.  Roofline: tf32 at half the measured bf16 burst
+    peak (the nominal dense tf32 : bf16 ratio) against the algorithmic HBM
+    bytes: f32 input read, f16 weights read once, f32 output written (conv:
+    plus the staged copy written and read).  cpu: the oracle's f32 arm on all
+    host threads (rhs widened once, blocked SGEMM; the conv as im2col blocks),
+    over a sample of the rows."""
+    import math
+    import time
+
+    import numpy as np
+    import torch
+
+    import oracle as O
+    from burn_image_b200 import f16 as F
+    from burn_image_b200 import q4
+    g = torch.Generator(device=dev).manual_seed(17)
+    if kind == "f16mm":
+        set_bytes = M * K * 4 + K * N * 4 + M * N * 4
+    else:
+        S = int(math.isqrt(M))
+        cin, cout = K // 9, N
+        set_bytes = M * cin * 4 * 2 + M * cout * 4 + K * N * 4
+    sets = max(2, min(16, int(2 * 126e6 // set_bytes) + 1))
+    items = []
+    for _ in range(sets):
+        if kind == "f16mm":
+            w = (torch.randn((N, K), generator=g, device=dev) * K ** -0.5).half()
+            items.append((F.PreparedF16Weight(w.t()), torch.randn((M, K), generator=g, device=dev),
+                          torch.empty((M, N), device=dev)))
+        else:
+            w = (torch.randn((cout, cin, 3, 3), generator=g, device=dev) * K ** -0.5).half()
+            items.append((F.PreparedF16ConvWeight(w), torch.randn((1, cin, S, S), generator=g, device=dev),
+                          torch.empty((1, cout, S, S), device=dev), torch.randn(cout, generator=g, device=dev)))
+    opt = F.ConvOptions((1, 1), (1, 1), (1, 1), 1)
+
+    def call(it):
+        if kind == "f16mm":
+            it[0].linear(it[1], out=it[2])
+        else:
+            it[0].conv2d(it[1], it[3], opt, out=it[2])
+
+    t = _graph_time(dev, items, call)
+    q4.poll_device_error()
+    flops = 2.0 * M * K * N
+    if kind == "f16mm":
+        nbytes = M * K * 4 + K * N * 2 + M * N * 4
+    else:
+        hp = (S + 2) ** 2
+        cp = (cin + 31) // 32 * 32
+        nbytes = M * cin * 4 + 2 * hp * cp * 4 + K * N * 2 + M * cout * 4 + cout * 4
+    tf32 = tfl / 2.0
+    t_star = max(nbytes / (hbm * 1e9), flops / (tf32 * 1e12))
+    row = {"us": t * 1e6, "tflops": flops / t / 1e12, "gbs": nbytes / t / 1e9,
+           "bound": "tensor" if flops / (tf32 * 1e12) >= nbytes / (hbm * 1e9) else "hbm",
+           "t_star_us": t_star * 1e6, "frac": t_star / t, "peak_tf32_tflops": tf32, "sets": sets}
+    del items
+    torch.cuda.empty_cache()
+    # CPU arm on a row sample (about a second of work)
+    try:
+        rng = np.random.default_rng(3)
+        if kind == "f16mm":
+            rows = min(M, 512)
+            x = rng.standard_normal((rows, K)).astype(np.float32)
+            wb = (rng.standard_normal((N, K)) * K ** -0.5).astype(np.float16).view(np.uint16)
+            O.cpu_f16_matmul(x[:16], wb, K, N, 1, K)
+            t0 = time.perf_counter()
+            O.cpu_f16_matmul(x, wb, K, N, 1, K)
+            dt = time.perf_counter() - t0
+            cflops, sample = 2.0 * rows * K * N, f"{rows} of {M} rows"
+        else:
+            hs = min(S, max(8, int(4096 // S)))
+            x = rng.standard_normal((1, cin, hs, S)).astype(np.float32)
+            wb = (rng.standard_normal((cout, cin, 3, 3)) * K ** -0.5).astype(np.float16).view(np.uint16)
+            t0 = time.perf_counter()
+            O.cpu_f16_conv2d(x, wb, None, (1, 1), (1, 1))
+            dt = time.perf_counter() - t0
+            cflops, sample = 2.0 * hs * S * K * N, f"{hs} of {S} image rows"
+        row["cpu"] = {"tflops": cflops / dt / 1e12, "cores": O.cpu_threads(), "kind": "port", "sample": sample}
+    except Exception as e:  # noqa: BLE001 -- the CPU arm is informational
+        row["cpu"] = {"tflops": None, "sample": f"failed: {e}"}
+    return row
 
 
 # ------------------------------------------------------------------ GPU arm

@@ -19,7 +19,7 @@ STATUS_NAMES = {
     5: "BQ4_ENCCL", 6: "BQ4_ETIMEOUT", 7: "BQ4_EINVAL_ARG", 8: "BQ4_EWORKSPACE",
     9: "BQ4_ENONFINITE", 10: "BQ4_EUNSUPPORTED",
 }
-LAYOUT_COL, LAYOUT_ROW, LAYOUT_NPACKED = 0, 1, 2
+LAYOUT_COL, LAYOUT_ROW, LAYOUT_NPACKED, LAYOUT_F16 = 0, 1, 2, 3
 ACT_NONE, ACT_GELU_TANH, ACT_SILU = 0, 1, 2
 NOALLOC_SCRATCH_BYTES = 32 << 20  # BQ4_NOALLOC_SCRATCH_BYTES
 NUMERICS_AUTO, NUMERICS_EXACT, NUMERICS_FOLDED = 0, 1, 2
@@ -73,6 +73,17 @@ SIGNATURES = {
     "bq4_linear_rowscatter": (_st, [_p, _p, _i32, _i64, _i64, _p, _i32, _p, _i32, _i32, _i64, _p, _sz, _p]),
     "bq4_linear_qk_norm_rope": (_st, [_p, _p, _i32, _i64, _i64, _p, _i64, _i64, _i64, _p, _p, ctypes.c_float, _p, _p,
                                       _i64, _p, _i32, _i64, _p, _sz, _p]),
+    "bq4_packed_f16_to_f32": (_st, [_p, _i32, ctypes.POINTER(_i64), ctypes.POINTER(_i64), _p, _p]),
+    "bq4_packed_f16_select_rows": (_st, [_p, _i64, _i64, _p, _i64, _p, _p]),
+    "bq4_f16_weight_prepare": (_st, [_p, _i64, _i64, _i64, _i64, _i32, ctypes.POINTER(_p)]),
+    "bq4_packed_f16_rhs_matmul_workspace_size": (_st, [_i64, _i64, _i64, ctypes.POINTER(_sz)]),
+    "bq4_packed_f16_rhs_matmul": (_st, [_p, _i64, _i64, _p, _i64, _i64, _i64, _p, _p, _sz, _p]),
+    "bq4_f16_conv_weight_prepare": (_st, [_p, _i64, _i64, _i32, _i32, _i32, ctypes.POINTER(_p)]),
+    "bq4_conv2d_workspace_size": (_st, [_p, _i64, _i64, _i64, _p, ctypes.POINTER(_sz)]),
+    "bq4_conv2d": (_st, [_p, _i64, _i64, _i64, _p, _p, _p, _p, _p, _sz, _p]),
+    "bq4_packed_f16_conv2d_workspace_size": (_st, [_i64, _i64, _i64, _i64, _i64, _i32, _i32, _p,
+                                                   ctypes.POINTER(_sz)]),
+    "bq4_packed_f16_conv2d": (_st, [_p, _i64, _i64, _i64, _i64, _p, _i64, _i32, _i32, _p, _p, _p, _p, _sz, _p]),
     "bq4_launch_count": (_u64, []),
     "bq4_launch_count_reset": (None, []),
 }
@@ -82,6 +93,11 @@ class QuantScheme(ctypes.Structure):
     """bq4_quant_scheme: the reference QuantScheme fields on this path."""
     _fields_ = [("value", _i32), ("mode", _i32), ("param", _i32), ("store_packed_dim", _i32),
                 ("block_rank", _i32), ("block", _i32), ("rhs_transposed_view", _i32)]
+
+
+class Conv2dOptions(ctypes.Structure):
+    """bq4_conv2d_options: Burn ConvOptions<2> ([height, width] pairs, groups)."""
+    _fields_ = [("stride", _i32 * 2), ("padding", _i32 * 2), ("dilation", _i32 * 2), ("groups", _i32)]
 
 
 class Bq4Error(RuntimeError):

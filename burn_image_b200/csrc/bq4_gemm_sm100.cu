@@ -188,6 +188,15 @@ struct WsArgs {
   // row sc_rank * sc_rows + m % sc_rows (the owner's receive buffer, f32, pitch ldy).
   float* sc_y[BQ4_MAX_PEERS];
   int sc_rows, sc_rank;
+  // Convolution (kernels built with CV): token m is position m of the
+  // zero-padded NHWC image stack, [batch][cv_hp][cv_wp] positions of
+  // cv_cchunks * 32 channels.  Chunk kc reads tap kc / cv_cchunks
+  // (ky = tap / cv_kw, kx = tap % cv_kw) from the token rows shifted by
+  // ky * cv_dy + kx * cv_dx, channels (kc % cv_cchunks) * 32..; chunks past
+  // cv_taps taps read zeros.  Output NCHW f32 [batch][N][cv_oh][cv_ow];
+  // positions with py >= cv_oh or px >= cv_ow are not stored.
+  int cv_cchunks, cv_taps, cv_kw, cv_dy, cv_dx;
+  int cv_hp, cv_wp, cv_oh, cv_ow;
   float qk_eps;
   const float* gamma_q;
   const float* gamma_k;
@@ -215,6 +224,22 @@ __device__ __forceinline__ void store_out(const WsArgs& a, int m, int n, float v
   } else {
     store_y(a, m, n, v);
   }
+}
+
+// Convolution: the TMA coordinates (channel column x, token row y) of chunk
+// kc for the token tile starting at row m0 (see WsArgs::cv_*).  A chunk past
+// the last tap (K padding) starts at row M: the whole box is out of bounds
+// and reads zeros.
+__device__ __forceinline__ void cv_coord(const WsArgs& a, int kc, int m0, int& x, int& y) {
+  const int tap = kc / a.cv_cchunks;
+  if (tap >= a.cv_taps) {
+    x = 0;
+    y = a.M;
+    return;
+  }
+  const int ky = tap / a.cv_kw;
+  x = (kc - tap * a.cv_cchunks) * 32;
+  y = m0 + ky * a.cv_dy + (tap - ky * a.cv_kw) * a.cv_dx;
 }
 
 // Unit u -> (tile, split) and its chunk range [kc0, kc1); splits cut at
@@ -581,7 +606,16 @@ __device__ __forceinline__ void split_reduce_epilogue(const WsArgs& a) {
 // token bytes are in flight; TMEM holds one accumulator (columns
 // [0, NW*BT)) and one 64-column A slot per stage after it.  Folded numerics,
 // one weight.
-template <int BT, int NW, bool TA, bool QK = false, bool SC = false>
+// TF = true: packed-F16 weights, kind::tf32.  Both operands are f32 rows
+// (pre-expanded weight tiles [128][32] f32 and f32 token tiles read by TMA
+// straight from the caller's rows), so a 128-byte operand row holds 32 K
+// values and a stage 64; the MMA walks the same bytes as kind::f16.
+// CV = true (implies TF): implicit-GEMM convolution.  The token rows of chunk kc
+// are shifted by its kernel tap (cv_coord), and the operands are swapped:
+// A = the token tile (128 tokens per MMA, BT/128 MMAs), B = the 128-channel
+// weight tile, so a TMEM lane is a token and the epilogue's warps store 32
+// consecutive output positions of one channel plane per instruction (NCHW).
+template <int BT, int NW, bool TA, bool QK = false, bool SC = false, bool CV = false, bool TF = false>
 __global__ void __launch_bounds__(kWsThreads, 1)
     q4_gemm_ws_kernel(const __grid_constant__ CUtensorMap tmap_x, const WsArgs a) {
   extern __shared__ uint8_t smem_raw[];
@@ -602,6 +636,9 @@ __global__ void __launch_bounds__(kWsThreads, 1)
   static_assert(kCols % 16 == 0, "scaler column split");
   static_assert(!QK || (NW == 1 && BT >= 128), "QK-norm epilogue: one weight, 128- or 256-token tiles");
   static_assert(!SC || (NW == 1 && !QK), "row scatter: one weight, plain epilogue");
+  static_assert(!TF || (NW == 1 && !TA && !QK && !SC), "tf32: one pre-expanded weight, plain epilogue");
+  static_assert(!CV || (TF && BT >= 128), "convolution: tf32, 128-token MMAs");
+  constexpr int kCK = TF ? 32 : kChunkK;  // K values per 128-byte operand row
 
   const int S = a.stages, RS = a.rs;
   uint8_t* ring = smem;                                     // [S][A | B]
@@ -670,8 +707,13 @@ __global__ void __launch_bounds__(kWsThreads, 1)
           }
           uint8_t* st = ring + (size_t)s * kStage;
           ptx::mbar_arrive_expect_tx(&full[s], 2 * kBSub + (a.pre ? kAStage : 0u));
-          ptx::tma_load_2d(st + kAStage, &tmap_x, &full[s], kc * kChunkK, mtile * BT);
-          ptx::tma_load_2d(st + kAStage + kBSub, &tmap_x, &full[s], (kc + 1) * kChunkK, mtile * BT);
+          int x0 = kc * kCK, y0 = mtile * BT, x1 = (kc + 1) * kCK, y1 = mtile * BT;
+          if constexpr (CV) {
+            cv_coord(a, kc, mtile * BT, x0, y0);
+            cv_coord(a, kc + 1, mtile * BT, x1, y1);
+          }
+          ptx::tma_load_2d(st + kAStage, &tmap_x, &full[s], x0, y0);
+          ptx::tma_load_2d(st + kAStage + kBSub, &tmap_x, &full[s], x1, y1);
           if (a.pre) {
 #pragma unroll
             for (int w = 0; w < NW; ++w)
@@ -709,7 +751,7 @@ __global__ void __launch_bounds__(kWsThreads, 1)
       }
     } else if (warp == kWsMmaWarp && lane == 0) {
       // ------------------------------------------------ MMA issuer
-      constexpr uint32_t idesc = ptx::umma_idesc_f16(128, BT);
+      constexpr uint32_t idesc = TF ? ptx::umma_idesc_tf32(128, CV ? 128 : BT) : ptx::umma_idesc_f16(128, BT);
       int s = 0, pb = 0;
       uint32_t ph = 0, pph = 0;
       bool ok = true;
@@ -740,6 +782,16 @@ __global__ void __launch_bounds__(kWsThreads, 1)
               if constexpr (TA) {
                 ptx::mma_f16_ts(d_base, tmem_base + kACol0 + (uint32_t)s * 64 + (uint32_t)sub * 32 + kk * 8, b_desc,
                                 idesc, (first && kk == 0) ? 0u : 1u);
+              } else if constexpr (CV) {
+                // tokens as A (128 per MMA), the weight tile as B (128 channels)
+                const uint64_t w_desc = ptx::umma_desc_sw128(st + (uint32_t)(sub * kATileBytes) + kk * 32);
+#pragma unroll
+                for (int h = 0; h < BT / 128; ++h)
+                  ptx::mma_tf32_ss(d_base + h * 128, ptx::umma_desc_sw128(b_addr + h * 128 * 128 + kk * 32), w_desc,
+                                   idesc, (first && kk == 0) ? 0u : 1u);
+              } else if constexpr (TF) {
+                ptx::mma_tf32_ss(d_base, ptx::umma_desc_sw128(st + (uint32_t)(sub * kATileBytes) + kk * 32), b_desc,
+                                 idesc, (first && kk == 0) ? 0u : 1u);
               } else {
 #pragma unroll
                 for (int w = 0; w < NW; ++w)
@@ -919,6 +971,30 @@ __global__ void __launch_bounds__(kWsThreads, 1)
           break;
         }
       }
+      if constexpr (CV) {
+        // TMEM lane = token, columns = channels: this thread holds token
+        // (col0 / 128) * 128 + row of the tile, channels col0 % 128 .. + kCols
+        const int p = mtile * BT + (col0 / 128) * 128 + row;
+        if (p < a.M) {
+          const int img = a.cv_hp * a.cv_wp;
+          const int b = p / img, r = p - b * img;
+          const int py = r / a.cv_wp, px = r - py * a.cv_wp;
+          if (py < a.cv_oh && px < a.cv_ow) {
+            const size_t plane = (size_t)a.cv_oh * a.cv_ow;
+            const int nb = ntile * 128 + (col0 & 127);
+            float* o = reinterpret_cast<float*>(a.y) + ((size_t)b * a.N + nb) * plane + (size_t)py * a.cv_ow + px;
+            const int act = a.act;
+#pragma unroll
+            for (int j = 0; j < kCols; ++j) {
+              if (nb + j < a.N) {
+                const float bj = a.bias[0] ? __ldg(a.bias[0] + nb + j) : 0.0f;
+                o[(size_t)j * plane] = apply_act(acc[0][j] + bj, act);
+              }
+            }
+          }
+        }
+        continue;
+      }
       if constexpr (QK) {
         const bool is_q = ntile < a.qk_q;
         if (is_q || ntile < a.qk_q + a.qk_k) {
@@ -1000,14 +1076,15 @@ EncodeTiledFn encode_fn() {
 }
 
 size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
 // The kernel rebalances registers with setmaxnreg; the split only fits the
 // pool the block was launched with when ptxas gave every thread exactly
 // kWsRegsLaunch registers.  Checked once per instantiation before any launch
 // (a mismatch would make setmaxnreg.inc wait forever).
-template <int BT, int NW, bool TA, bool QK = false, bool SC = false>
+template <int BT, int NW, bool TA, bool QK = false, bool SC = false, bool CV = false, bool TF = false>
 cudaError_t prepare_ws_kernel(size_t smem_bytes, bool* ok_regs) {
-  auto kern = q4_gemm_ws_kernel<BT, NW, TA, QK, SC>;
+  auto kern = q4_gemm_ws_kernel<BT, NW, TA, QK, SC, CV, TF>;
   static int checked = 0;  // 0 unknown, 1 ok, -1 bad
   if (checked == 0) {
     cudaFuncAttributes attr;
@@ -1029,10 +1106,10 @@ cudaError_t prepare_ws_kernel(size_t smem_bytes, bool* ok_regs) {
   return cudaSuccess;
 }
 
-template <int BT, int NW, bool TA = false, bool QK = false, bool SC = false>
+template <int BT, int NW, bool TA = false, bool QK = false, bool SC = false, bool CV = false, bool TF = false>
 cudaError_t launch_ws(const GemmPlan& plan, const CUtensorMap& tmap, const WsArgs& args, cudaStream_t stream,
                       bool* ok_regs) {
-  cudaError_t e = prepare_ws_kernel<BT, NW, TA, QK, SC>(plan.smem_bytes, ok_regs);
+  cudaError_t e = prepare_ws_kernel<BT, NW, TA, QK, SC, CV, TF>(plan.smem_bytes, ok_regs);
   if (e != cudaSuccess || !*ok_regs) return e;
   // Launched as a programmatic dependent of the activation-staging grid
   // before it (only the token loads wait for that grid, see the kernel), and
@@ -1059,7 +1136,7 @@ cudaError_t launch_ws(const GemmPlan& plan, const CUtensorMap& tmap, const WsArg
   }
   cfg.attrs = attr;
   cfg.numAttrs = n;
-  e = cudaLaunchKernelEx(&cfg, q4_gemm_ws_kernel<BT, NW, TA, QK, SC>, tmap, args);
+  e = cudaLaunchKernelEx(&cfg, q4_gemm_ws_kernel<BT, NW, TA, QK, SC, CV, TF>, tmap, args);
   note_launch();
   return e;
 }
@@ -1192,7 +1269,7 @@ static size_t sk_part_bytes(int grid, int nw, int bt) {
 }
 
 static bq4_status plan_for_bt(const bq4_weight* w, int nw, int64_t M, int device, int bt, GemmPlan* p,
-                              double* cost, bool allow_sk, bool qk) {
+                              double* cost, bool allow_sk, bool qk, bool cv) {
   p->bt = bt;
   p->mtiles = (int)((M + p->bt - 1) / p->bt);
   p->ntiles = (int)w->ntiles;
@@ -1203,7 +1280,7 @@ static bq4_status plan_for_bt(const bq4_weight* w, int nw, int64_t M, int device
 
   // Shared memory: operand ring of 128-K stages (A + B) as deep as fits
   // (2..4 stages) next to a raw ring of 1..4 stages.
-  const uint32_t raw_s_bytes = 512u * (uint32_t)(w->block >= 128 ? 1 : 128 / w->block);
+  const uint32_t raw_s_bytes = p->pre ? 0u : 512u * (uint32_t)(w->block >= 128 ? 1 : 128 / w->block);
   p->raw_s_bytes = p->exact || p->pre ? 0u : raw_s_bytes;
   p->raw_w_bytes = p->pre ? 16u : 2 * kRawQBytes + p->raw_s_bytes;
   // Operand A in TMEM (folded numerics, one weight, 256-token tiles): shared
@@ -1263,7 +1340,7 @@ static bq4_status plan_for_bt(const bq4_weight* w, int nw, int64_t M, int device
   int best_s = 1;
   double best_t = 1e30;
   const int max_s = nks < kMaxSplit ? nks : kMaxSplit;
-  for (int s = 1; s <= (qk ? 1 : max_s); ++s) {  // the QK epilogue needs whole-K tiles
+  for (int s = 1; s <= (qk || cv ? 1 : max_s); ++s) {  // the QK and conv epilogues need whole-K tiles
     const int units = tiles * s;
     if (s > 1 && (units > s * cluster_capacity(p->bt, nw, s, p->smem_bytes, device) || units > sms)) continue;
     const int waves = (units + sms - 1) / sms;
@@ -1279,7 +1356,7 @@ static bq4_status plan_for_bt(const bq4_weight* w, int nw, int64_t M, int device
   if (const char* f = getenv("BQ4_FORCE_KSPLIT")) {
     int v = atoi(f);
     if (v >= 1) best_s = v < max_s ? v : max_s;
-    if (qk) best_s = 1;
+    if (qk || cv) best_s = 1;
     while (best_s > 1 && (tiles * best_s > best_s * cluster_capacity(p->bt, nw, best_s, p->smem_bytes, device) ||
                           tiles * best_s > sms))
       --best_s;
@@ -1335,17 +1412,24 @@ static bq4_status plan_for_bt(const bq4_weight* w, int nw, int64_t M, int device
   // two parts).
   p->partial_bytes =
       best_s > 1 ? align_up((size_t)tiles * best_s * nw * p->bt * 128 * sizeof(float), 256) : 0;
-  p->xh_bytes = align_up((size_t)M * (size_t)w->Kp * 2, 256);
+  // tf32 plans read the caller's f32 rows in place (their entry points stage
+  // the rows themselves when they must)
+  p->xh_bytes = p->tf ? 0 : align_up((size_t)M * (size_t)w->Kp * 2, 256);
   p->workspace_bytes = p->sk_bytes + p->partial_bytes + p->xh_bytes;
   return BQ4_OK;
 }
 
 
-bq4_status plan_gemm(const bq4_weight* w, int nw, int64_t M, int device, GemmPlan* p, bool allow_sk, bool qk) {
+bq4_status plan_gemm(const bq4_weight* w, int nw, int64_t M, int device, GemmPlan* p, bool allow_sk, bool qk,
+                     bool cv) {
   if (M <= 0) return set_error(BQ4_EINVAL_SHAPE, "M must be positive (got %lld)", (long long)M);
   if (M > (int64_t)1 << 30) return set_error(BQ4_EINVAL_SHAPE, "M too large");
   memset(p, 0, sizeof(*p));
   p->nw = nw;
+  p->tf = w->tf32 ? 1 : 0;
+  p->cv = cv ? 1 : 0;
+  if ((p->tf || cv) && (nw != 1 || qk || !w->h || (cv && !p->tf)))
+    return set_error(BQ4_EINVAL_ARG, "packed-F16 plans take one packed-F16 weight and the plain or conv epilogue");
   // Numerics: blocks of 64/128 keep q exact in f16 and multiply the f32
   // partial of each K block by its scale (exact weights); smaller blocks
   // stage f16(q * f16(scale)) (folded); N-packed sources are pre-expanded.
@@ -1371,12 +1455,12 @@ bq4_status plan_gemm(const bq4_weight* w, int nw, int64_t M, int device, GemmPla
   bq4_status last = BQ4_OK;
   for (int bt : {256, 128, 64}) {
     if (nw == 2 && bt == 256) continue;
-    if (qk && bt == 64) continue;  // the QK epilogue reduces over 32+ token columns per thread
-    const int smallest = qk ? 128 : 64;  // always a candidate, however small M is
+    if ((qk || cv) && bt == 64) continue;  // QK: 32+ token columns per thread; conv: 128-token MMAs
+    const int smallest = qk || cv ? 128 : 64;  // always a candidate, however small M is
     if (forced ? bt != forced : (bt != smallest && bt > 2 * M)) continue;
     GemmPlan cand = base;
     double cost = 0.0;
-    last = plan_for_bt(w, nw, M, device, bt, &cand, &cost, allow_sk, qk);
+    last = plan_for_bt(w, nw, M, device, bt, &cand, &cost, allow_sk && !cv, qk, cv);
     if (last != BQ4_OK) continue;
     if (!have || cost < best - 1e-9) {
       *p = cand;
@@ -1400,7 +1484,12 @@ bq4_status run_gemm(const GemmPlan& plan, const bq4_weight* const* ws, const voi
       plan.sk_tiles ? reinterpret_cast<unsigned*>(wsb + sk_part_bytes(plan.grid, plan.nw, plan.bt)) : nullptr;
   const int nflags = plan.sk_tiles ? plan.grid : 0;
   float* partials = plan.partial_bytes ? reinterpret_cast<float*>(wsb + plan.sk_bytes) : nullptr;
-  if (!io.x_f16) {
+  if (plan.tf) {
+    // tf32: the token tiles are read from the caller's f32 rows in place
+    if (io.x_f16) return set_error(BQ4_EINVAL_ARG, "packed-F16 weights take f32 activations");
+    if (!aligned16(x) || ldx % 4 != 0)
+      return set_error(BQ4_EALIGN, "packed-F16 weights read x in place: 16-byte aligned rows, ldx %% 4 == 0");
+  } else if (!io.x_f16) {
     // 1) stage activations as f16 [M][Kp] in the workspace (and zero the
     //    stream-K flags)
     void* dst = wsb + plan.sk_bytes + plan.partial_bytes;
@@ -1418,11 +1507,15 @@ bq4_status run_gemm(const GemmPlan& plan, const bq4_weight* const* ws, const voi
   EncodeTiledFn enc = encode_fn();
   if (!enc) return set_error(BQ4_ECUDA, "cuTensorMapEncodeTiled unavailable");
   CUtensorMap tmap;
-  cuuint64_t gdim[2] = {(cuuint64_t)w0->Kp, (cuuint64_t)M};
-  cuuint64_t gstride[1] = {(cuuint64_t)x_pitch * 2};
-  cuuint32_t box[2] = {(cuuint32_t)kChunkK, (cuuint32_t)plan.bt};
+  // tf32: f32 rows of K values (conv: x_cols staged channels), box {32, BT};
+  // columns past the extent read zeros
+  const int64_t x_cols = plan.tf ? (io.cv ? io.cv->x_cols : w0->K) : w0->Kp;
+  cuuint64_t gdim[2] = {(cuuint64_t)x_cols, (cuuint64_t)M};
+  cuuint64_t gstride[1] = {(cuuint64_t)x_pitch * (plan.tf ? 4 : 2)};
+  cuuint32_t box[2] = {(cuuint32_t)(plan.tf ? 32 : kChunkK), (cuuint32_t)plan.bt};
   cuuint32_t estride[2] = {1, 1};
-  CUresult cr = enc(&tmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(xh), gdim, gstride, box, estride,
+  CUresult cr = enc(&tmap, plan.tf ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
+                    const_cast<void*>(xh), gdim, gstride, box, estride,
                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (cr != CUDA_SUCCESS) return set_error(BQ4_ECUDA, "cuTensorMapEncodeTiled failed (%d)", (int)cr);
@@ -1479,12 +1572,33 @@ bq4_status run_gemm(const GemmPlan& plan, const bq4_weight* const* ws, const voi
     args.sin_t = io.qk->sin_t;
     args.ld_rope = (int)io.qk->ld_rope;
   }
+  if (plan.cv) {
+    if (!io.cv) return set_error(BQ4_EINVAL_ARG, "a convolution plan needs its geometry");
+    args.cv_cchunks = io.cv->cchunks;
+    args.cv_taps = io.cv->taps;
+    args.cv_kw = io.cv->kw;
+    args.cv_dy = io.cv->dy;
+    args.cv_dx = io.cv->dx;
+    args.cv_hp = io.cv->hp;
+    args.cv_wp = io.cv->wp;
+    args.cv_oh = io.cv->oh;
+    args.cv_ow = io.cv->ow;
+  }
   args.act = act;
   args.raw_s_bytes = plan.raw_s_bytes;
   args.raw_w_bytes = plan.raw_w_bytes;
 
   bool ok_regs = true;
-  if (args.sc_rows) {
+  if (plan.cv) {
+    if (plan.ksplit != 1 || plan.sk_tiles || plan.bt < 128) return set_error(BQ4_EUNSUPPORTED, "conv plan shape");
+    if (plan.bt == 256) e = launch_ws<256, 1, false, false, false, true, true>(plan, tmap, args, stream, &ok_regs);
+    else e = launch_ws<128, 1, false, false, false, true, true>(plan, tmap, args, stream, &ok_regs);
+  } else if (plan.tf) {
+    if (args.sc_rows || plan.sk_tiles) return set_error(BQ4_EUNSUPPORTED, "tf32 plan shape");
+    if (plan.bt == 256) e = launch_ws<256, 1, false, false, false, false, true>(plan, tmap, args, stream, &ok_regs);
+    else if (plan.bt == 128) e = launch_ws<128, 1, false, false, false, false, true>(plan, tmap, args, stream, &ok_regs);
+    else e = launch_ws<64, 1, false, false, false, false, true>(plan, tmap, args, stream, &ok_regs);
+  } else if (args.sc_rows) {
     if (plan.nw != 1 || plan.qk) return set_error(BQ4_EUNSUPPORTED, "row scatter: one weight, plain epilogue");
     if (plan.ta && plan.bt != 256) return set_error(BQ4_EUNSUPPORTED, "row scatter with 128-token TMEM operands");
     if (plan.ta) e = launch_ws<256, 1, true, false, true>(plan, tmap, args, stream, &ok_regs);

@@ -37,6 +37,13 @@ struct bq4_weight {
   // 16 KiB bulk copy lands as an MMA-ready operand tile.  q/s unused.
   uint16_t* h;
   size_t h_bytes;
+  // Packed-F16 weights (tf32 = 1): h holds f32 tiles [ntiles][nkc][128][32]
+  // (tf32-exact widened f16 values) with the same 128-byte swizzle, so a
+  // chunk is 32 K and Kp is a multiple of 64.  Convolution weights (conv_kh
+  // > 0) order K as (tap = ky * conv_kw + kx, channel): K = taps * conv_cp,
+  // channels padded to conv_cp = a multiple of 32 with zeros.
+  int32_t tf32;
+  int32_t conv_kh, conv_kw, conv_cin, conv_cp;
 };
 
 namespace bq4 {
@@ -103,6 +110,8 @@ struct GemmPlan {
   int pdl;         // 1: GEMM launched as a programmatic dependent of the staging grid
   int ta;          // 1: operand A (dequantized weights) staged in TMEM, not shared memory
   int qk;          // 1: QK-norm + RoPE epilogue (every 128-feature tile one head)
+  int tf;          // 1: packed-F16 weight, kind::tf32 on f32 token rows (no staging pass)
+  int cv;          // 1: implicit-GEMM convolution (tf32, NCHW epilogue)
   int stages, a_stages, raw_stages;  // B ring, A ring, raw ring depths
   uint32_t raw_s_bytes;  // scale bytes per weight per raw stage (folded)
   uint32_t raw_w_bytes;  // shared-memory bytes per weight per raw stage
@@ -118,7 +127,7 @@ struct GemmPlan {
 // qk = true plans the QK-norm + RoPE epilogue (whole-K tiles of 128 or 256
 // tokens, shared memory for its reduction).
 bq4_status plan_gemm(const bq4_weight* w, int nw, int64_t M, int device, GemmPlan* plan, bool allow_sk = true,
-                     bool qk = false);
+                     bool qk = false, bool cv = false);
 
 // Activation / output formats of one GEMM call: x f32 (staged to f16 in the
 // workspace) or f16 (read in place; needs K == Kp), y f32 or f16 with row
@@ -134,6 +143,15 @@ struct QkParams {
   int64_t ld_rope = 128;
 };
 
+// Geometry of an implicit-GEMM convolution (kernels built with CV): see
+// WsArgs::cv_* in bq4_gemm_sm100.cu.  x_cols = f32 values per token row of
+// the staged activations (the row pitch too).
+struct ConvGeom {
+  int cchunks = 1, taps = 1, kw = 1, dy = 0, dx = 0;
+  int hp = 1, wp = 1, oh = 1, ow = 1;
+  int64_t x_cols = 0;
+};
+
 struct GemmIo {
   int x_f16 = 0;
   int y_f16 = 0;
@@ -143,6 +161,7 @@ struct GemmIo {
   int sc_rows = 0, sc_rank = 0, sc_nranks = 0;
   float* const* sc_y = nullptr;
   const QkParams* qk = nullptr;  // with a plan from plan_gemm(..., qk = true)
+  const ConvGeom* cv = nullptr;  // with a plan from plan_gemm(..., cv = true)
 };
 
 bq4_status run_gemm(const GemmPlan& plan, const bq4_weight* const* ws, const void* x, int64_t M,

@@ -300,5 +300,28 @@ __host__ __device__ constexpr uint32_t umma_idesc_f16(uint32_t M, uint32_t N) {
          | ((M >> 4) << 24);    // M / 16
 }
 
+// Instruction descriptor, kind::tf32: A,B tf32 (f32 in memory, the tensor
+// core reads sign, exponent and the top 10 mantissa bits), D f32, both
+// K-major, MxN.  One K=8 step spans the same 32 bytes of a 128-byte operand
+// row as a K=16 step of kind::f16.
+__host__ __device__ constexpr uint32_t umma_idesc_tf32(uint32_t M, uint32_t N) {
+  return (1u << 4)              // D format f32
+         | (2u << 7)            // A tf32
+         | (2u << 10)           // B tf32
+         | ((N >> 3) << 17)     // N / 8
+         | ((M >> 4) << 24);    // M / 16
+}
+
+// D[tmem] (+)= A[smem] * B[smem]^T, kind::tf32, both operands K-major.
+__device__ __forceinline__ void mma_tf32_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                            uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
 }  // namespace ptx
 }  // namespace bq4

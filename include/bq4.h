@@ -58,7 +58,10 @@ typedef enum {
   BQ4_EUNSUPPORTED = 10   /* no kernel for this device (not sm_100) */
 } bq4_status;
 
-typedef enum { BQ4_LAYOUT_COL = 0, BQ4_LAYOUT_ROW = 1, BQ4_LAYOUT_NPACKED = 2 } bq4_layout;
+/* BQ4_LAYOUT_F16: reported by bq4_weight_info for weights prepared from
+ * packed-F16 storage (bq4_f16_weight_prepare, bq4_f16_conv_weight_prepare);
+ * not accepted by the Q4 preparation calls. */
+typedef enum { BQ4_LAYOUT_COL = 0, BQ4_LAYOUT_ROW = 1, BQ4_LAYOUT_NPACKED = 2, BQ4_LAYOUT_F16 = 3 } bq4_layout;
 
 typedef enum {
   BQ4_ACT_NONE = 0,
@@ -423,6 +426,87 @@ BQ4_API bq4_status bq4_linear_rowscatter(const bq4_weight* w, const void* x, bq4
 /* Kernel launches issued by this thread since the last reset (bench accounting). */
 BQ4_API uint64_t bq4_launch_count(void);
 BQ4_API void bq4_launch_count_reset(void);
+
+/* ---------------------------------------------------------------- packed F16
+ * IEEE binary16 storage bound as u32 words, two values per word, the
+ * even-index value in the low half: the VAE's weights and the F16 profiles'
+ * tables.  Counterparts of the four kernels of
+ * patches/burn-cubecl-0.21.0/src/kernel/packed_f16.rs, which the reference
+ * dispatches when a device lacks typed f16 (ops/tensor.rs:164-165, 222-223,
+ * 697-698; ops/module.rs:73-74).  Widening is bit-exact to the binary16
+ * value, NaN payloads kept with the quiet bit set (packed_f16.rs:48-74).
+ * The matmul and convolution run on the tensor cores as kind::tf32: every
+ * f16 weight is exact in tf32, the f32 activations enter with their top 10
+ * mantissa bits (cut for matmul rows read in place, rounded to nearest by the
+ * convolution's staging pass), and accumulation is f32; both meet the 5e-3
+ * relative-Frobenius bound and reproduce the reference's small-integer cases
+ * exactly.  Element strides and offsets below count f16 values.
+ */
+
+/* packed_f16_to_f32 (packed_f16.rs:88-131): out (contiguous, `rank` <= 8
+ * dims of `shape`) = the widened values at sum(coord * strides) of packed. */
+BQ4_API bq4_status bq4_packed_f16_to_f32(const uint32_t* packed, int32_t rank, const int64_t* shape,
+                                         const int64_t* strides, float* out, bq4_stream_t stream);
+
+/* packed_f16_select_rows (packed_f16.rs:296-358): out f32 [n][cols] = rows
+ * indices[i] of the contiguous table [rows][cols].  The reference does not
+ * check indices; here an index outside [0, rows) gives a zero row and records
+ * BQ4_EINVAL_ARG, reported by bq4_poll_device_error. */
+BQ4_API bq4_status bq4_packed_f16_select_rows(const uint32_t* table, int64_t rows, int64_t cols,
+                                              const int32_t* indices, int64_t n, float* out,
+                                              bq4_stream_t stream);
+
+/* One-time preparation of a packed-F16 matmul rhs of logical shape [K, N],
+ * element (k, n) at k * inner_stride + n * col_stride (the zero-copy
+ * transposed view of a stored [N, K] checkpoint: inner 1, col K).  Host or
+ * device source.  The result works with bq4_linear / bq4_linear_ex (f32 x
+ * with 16-byte aligned rows and ldx % 4 == 0, bias and activations fused). */
+BQ4_API bq4_status bq4_f16_weight_prepare(const uint32_t* packed, int64_t K, int64_t N, int64_t inner_stride,
+                                          int64_t col_stride, int32_t device, bq4_weight** out);
+
+/* packed_f16_rhs_matmul (packed_f16.rs:133-292): lhs f32 [M, K] contiguous
+ * (16-byte aligned when K % 4 == 0) times the packed rhs above -> out f32
+ * [M, N].  Prepares rhs into the workspace on every call. */
+BQ4_API bq4_status bq4_packed_f16_rhs_matmul_workspace_size(int64_t M, int64_t K, int64_t N, size_t* bytes);
+BQ4_API bq4_status bq4_packed_f16_rhs_matmul(const float* lhs, int64_t M, int64_t K, const uint32_t* packed_rhs,
+                                             int64_t inner_stride, int64_t col_stride, int64_t N, float* out,
+                                             void* workspace, size_t workspace_bytes, bq4_stream_t stream);
+
+/* Burn ConvOptions<2>: [height, width] pairs; groups must be 1. */
+typedef struct {
+  int32_t stride[2];
+  int32_t padding[2];
+  int32_t dilation[2];
+  int32_t groups;
+} bq4_conv2d_options;
+
+/* One-time preparation of an OIHW packed-F16 convolution weight
+ * [out_channels][in_channels][kernel_h][kernel_w] (host or device). */
+BQ4_API bq4_status bq4_f16_conv_weight_prepare(const uint32_t* packed_oihw, int64_t out_channels,
+                                               int64_t in_channels, int32_t kernel_h, int32_t kernel_w,
+                                               int32_t device, bq4_weight** out);
+
+/* Convolution with a prepared weight: input f32 NCHW [batch][in_channels]
+ * [in_h][in_w], bias f32 [out_channels] or NULL -> out f32 NCHW [batch]
+ * [out_channels][out_h][out_w], out_h = (in_h + 2 pad - dil (kh - 1) - 1) /
+ * stride + 1 (likewise out_w). */
+BQ4_API bq4_status bq4_conv2d_workspace_size(const bq4_weight* w, int64_t batch, int64_t in_h, int64_t in_w,
+                                             const bq4_conv2d_options* options, size_t* bytes);
+BQ4_API bq4_status bq4_conv2d(const float* input, int64_t batch, int64_t in_h, int64_t in_w, const bq4_weight* w,
+                              const float* bias, const bq4_conv2d_options* options, float* out, void* workspace,
+                              size_t workspace_bytes, bq4_stream_t stream);
+
+/* packed_f16_conv2d (packed_f16.rs:421-602): the same from the stored OIHW
+ * packed weight, prepared into the workspace on every call. */
+BQ4_API bq4_status bq4_packed_f16_conv2d_workspace_size(int64_t batch, int64_t in_channels, int64_t in_h,
+                                                        int64_t in_w, int64_t out_channels, int32_t kernel_h,
+                                                        int32_t kernel_w, const bq4_conv2d_options* options,
+                                                        size_t* bytes);
+BQ4_API bq4_status bq4_packed_f16_conv2d(const float* input, int64_t batch, int64_t in_channels, int64_t in_h,
+                                         int64_t in_w, const uint32_t* packed_weight, int64_t out_channels,
+                                         int32_t kernel_h, int32_t kernel_w, const float* bias,
+                                         const bq4_conv2d_options* options, float* out, void* workspace,
+                                         size_t workspace_bytes, bq4_stream_t stream);
 
 #ifdef __cplusplus
 }

@@ -54,6 +54,14 @@ def lib() -> ctypes.CDLL:
         _lib.orc_cpu_threads.argtypes = []
         _lib.orc_qk_norm_rope_f64.argtypes = [p, i64, i64, i64, i64, p, ctypes.c_double, p, p, i64, p, i64]
         _lib.orc_qk_norm_rope_f64.restype = None
+        _lib.orc_f16_widen_bits.argtypes = [p, i64, p]
+        _lib.orc_f16_widen_bits.restype = None
+        _lib.orc_f16_matmul_f64.argtypes = [p, i64, i64, p, i64, i64, i64, p, p]
+        _lib.orc_f16_matmul_f64.restype = None
+        _lib.orc_f16_conv2d_f64.argtypes = [p, i64, i64, i64, i64, p, i64, i64, i64, p] + [i64] * 6 + [p]
+        _lib.orc_f16_conv2d_f64.restype = None
+        _lib.orc_cpu_f16_matmul.argtypes = [p, i64, i64, p, i64, i64, i64, p, i32]
+        _lib.orc_cpu_f16_conv2d.argtypes = [p, i64, i64, i64, i64, p, i64, i64, i64, p] + [i64] * 6 + [p, i32]
     return _lib
 
 
@@ -216,3 +224,74 @@ def rel_frobenius(actual: np.ndarray, expected: np.ndarray) -> float:
     e = np.asarray(expected, dtype=np.float64)
     den = np.sqrt((e * e).sum())
     return float(np.sqrt(((a - e) ** 2).sum()) / (den if den > 0 else 1.0))
+
+
+# ---------------------------------------------------------------- packed F16
+
+def _bits(a) -> np.ndarray:
+    """binary16 bit patterns (uint16) of a float16 / uint16 array."""
+    a = np.asarray(a)
+    if a.dtype == np.float16:
+        a = a.view(np.uint16)
+    return np.ascontiguousarray(a, dtype=np.uint16)
+
+
+def f16_widen_bits(bits) -> np.ndarray:
+    """binary32 bit patterns of binary16 bit patterns (packed_f16.rs:48-74)."""
+    h = _bits(bits)
+    out = np.empty(h.shape, dtype=np.uint32)
+    lib().orc_f16_widen_bits(_ptr(h), h.size, _ptr(out))
+    return out
+
+
+def f16_matmul_f64(lhs, rhs_bits, K: int, N: int, inner: int, col: int, bias=None) -> np.ndarray:
+    """lhs f32 [M, K] times the packed rhs (element (k, n) at k*inner + n*col
+    of rhs_bits), f64 accumulation (packed_f16.rs:133-292)."""
+    x = _f32(lhs).reshape(-1, K)
+    h = _bits(rhs_bits).reshape(-1)
+    out = np.empty((x.shape[0], N), dtype=np.float64)
+    lib().orc_f16_matmul_f64(_ptr(x), x.shape[0], K, _ptr(h), inner, col, N, _ptr(_f32(bias)), _ptr(out))
+    return out
+
+
+def f16_conv2d_f64(inp, weight_bits, bias=None, stride=(1, 1), padding=(0, 0), dilation=(1, 1)) -> np.ndarray:
+    """NCHW f32 input, OIHW binary16 weight, groups 1, f64 accumulation
+    (packed_f16.rs:375-602)."""
+    x = _f32(inp)
+    B, C, H, W = x.shape
+    wb = _bits(weight_bits)
+    O, Cw, kh, kw = wb.shape
+    assert Cw == C
+    OH = (H + 2 * padding[0] - dilation[0] * (kh - 1) - 1) // stride[0] + 1
+    OW = (W + 2 * padding[1] - dilation[1] * (kw - 1) - 1) // stride[1] + 1
+    out = np.empty((B, O, OH, OW), dtype=np.float64)
+    lib().orc_f16_conv2d_f64(_ptr(x), B, C, H, W, _ptr(wb), O, kh, kw, _ptr(_f32(bias)), stride[0], stride[1],
+                             padding[0], padding[1], dilation[0], dilation[1], _ptr(out))
+    return out
+
+
+def cpu_f16_matmul(lhs, rhs_bits, K: int, N: int, inner: int, col: int, threads: int = 0, out=None) -> np.ndarray:
+    """Timed CPU arm: rhs widened to f32 panels, blocked SGEMM (OpenMP)."""
+    x = _f32(lhs).reshape(-1, K)
+    y = out if out is not None else np.empty((x.shape[0], N), dtype=np.float32)
+    rc = lib().orc_cpu_f16_matmul(_ptr(x), x.shape[0], K, _ptr(_bits(rhs_bits)), inner, col, N, _ptr(y), threads)
+    if rc:
+        raise OracleError(rc, "cpu_f16_matmul")
+    return y
+
+
+def cpu_f16_conv2d(inp, weight_bits, bias=None, stride=(1, 1), padding=(0, 0), dilation=(1, 1), threads: int = 0,
+                   out=None) -> np.ndarray:
+    """Timed CPU arm: im2col blocks times the widened OIHW panels (OpenMP)."""
+    x = _f32(inp)
+    B, C, H, W = x.shape
+    wb = _bits(weight_bits)
+    O, _, kh, kw = wb.shape
+    OH = (H + 2 * padding[0] - dilation[0] * (kh - 1) - 1) // stride[0] + 1
+    OW = (W + 2 * padding[1] - dilation[1] * (kw - 1) - 1) // stride[1] + 1
+    y = out if out is not None else np.empty((B, O, OH, OW), dtype=np.float32)
+    rc = lib().orc_cpu_f16_conv2d(_ptr(x), B, C, H, W, _ptr(wb), O, kh, kw, _ptr(_f32(bias)), stride[0], stride[1],
+                                  padding[0], padding[1], dilation[0], dilation[1], _ptr(y), threads)
+    if rc:
+        raise OracleError(rc, "cpu_f16_conv2d")
+    return y

@@ -486,3 +486,235 @@ int orc_cpu_linear(const uint32_t* words, const float* scales, int64_t K, int64_
     free(panels);
     return ORC_OK;
 }
+
+/* ========================================================================
+ * Packed-F16 storage (the VAE's weights; next to the Q4 path in the same
+ * patched backend): patches/burn-cubecl-0.21.0/src/kernel/packed_f16.rs.
+ * IEEE binary16 bits, two per u32 word, the even-index value in the low half
+ * (load_packed_f16, :77-86).
+ * ====================================================================== */
+
+/*
+ * Widening, restated from widen_f16_bits_to_f32 (packed_f16.rs:48-74) and its
+ * test twin reference_f16_bits_to_f32_bits (crates/burn_boogu/src/model/
+ * packed_f16.rs:554-568): sign moved to bit 31; zero exponent with zero
+ * mantissa -> signed zero; subnormal m -> normalised (exponent 113 - shift,
+ * shift = leading zeros of m within its 10 bits + 1); exponent 31 -> infinity,
+ * or NaN with the quiet bit set and the payload shifted up; otherwise the
+ * exponent rebiased by 112 and the mantissa shifted up 13 bits.
+ */
+static uint32_t f16_bits_to_f32_bits(uint32_t bits) {
+    const uint32_t sign = (bits & 0x8000u) << 16;
+    const uint32_t exponent = (bits >> 10) & 0x1fu;
+    const uint32_t mantissa = bits & 0x03ffu;
+    if (exponent == 0) {
+        if (mantissa == 0) return sign;
+        uint32_t shift = 1; /* leading zeros of the 10-bit field, plus one */
+        while (!((mantissa << shift) & 0x400u)) ++shift;
+        return sign | ((113u - shift) << 23) | (((mantissa << shift) & 0x03ffu) << 13);
+    }
+    if (exponent == 0x1fu) {
+        if (mantissa == 0) return sign | 0x7f800000u;
+        return sign | 0x7fc00000u | (mantissa << 13);
+    }
+    return sign | ((exponent + 112u) << 23) | (mantissa << 13);
+}
+
+static inline float f16_value(uint16_t bits) {
+    const uint32_t b = f16_bits_to_f32_bits(bits);
+    float f;
+    memcpy(&f, &b, sizeof(f));
+    return f;
+}
+
+void orc_f16_widen_bits(const uint16_t* h, int64_t n, uint32_t* out) {
+    for (int64_t i = 0; i < n; ++i) out[i] = f16_bits_to_f32_bits(h[i]);
+}
+
+/*
+ * packed_f16_rhs_matmul (packed_f16.rs:133-292), checker in f64:
+ * out[m][n] = sum_k lhs[m][k] * widen(rhs[k * inner + n * col]).
+ */
+void orc_f16_matmul_f64(const float* lhs, int64_t M, int64_t K, const uint16_t* rhs, int64_t inner, int64_t col,
+                        int64_t N, const float* bias, double* out) {
+    double* w = (double*)malloc(sizeof(double) * (size_t)(K * N));
+    for (int64_t k = 0; k < K; ++k)
+        for (int64_t n = 0; n < N; ++n) w[k * N + n] = (double)f16_value(rhs[k * inner + n * col]);
+#pragma omp parallel for schedule(static)
+    for (int64_t m = 0; m < M; ++m) {
+        double* o = out + m * N;
+        for (int64_t n = 0; n < N; ++n) o[n] = bias ? (double)bias[n] : 0.0;
+        for (int64_t k = 0; k < K; ++k) {
+            const double a = (double)lhs[m * K + k];
+            const double* wr = w + k * N;
+            for (int64_t n = 0; n < N; ++n) o[n] += a * wr[n];
+        }
+    }
+    free(w);
+}
+
+/*
+ * packed_f16_conv2d (packed_f16.rs:375-602), checker in f64: NCHW input
+ * [B][C][H][W], OIHW weight [O][C][kh][kw], groups 1,
+ * out[b][o][oy][ox] = bias[o] + sum_{c,ky,kx} in[b][c][iy][ix] * widen(w[o][c][ky][kx]),
+ * iy = oy*sh + ky*dh - ph, ix = ox*sw + kx*dw - pw, zero outside the input
+ * (packed_conv2d_input_value, :375-419); OH = (H + 2ph - dh(kh-1) - 1)/sh + 1.
+ */
+void orc_f16_conv2d_f64(const float* in, int64_t B, int64_t C, int64_t H, int64_t W, const uint16_t* wt, int64_t O,
+                        int64_t kh, int64_t kw, const float* bias, int64_t sh, int64_t sw, int64_t ph, int64_t pw,
+                        int64_t dh, int64_t dw, double* out) {
+    const int64_t OH = (H + 2 * ph - dh * (kh - 1) - 1) / sh + 1;
+    const int64_t OW = (W + 2 * pw - dw * (kw - 1) - 1) / sw + 1;
+    const int64_t inner = C * kh * kw;
+    double* w = (double*)malloc(sizeof(double) * (size_t)(O * inner));
+    for (int64_t i = 0; i < O * inner; ++i) w[i] = (double)f16_value(wt[i]);
+#pragma omp parallel for collapse(2) schedule(static)
+    for (int64_t b = 0; b < B; ++b)
+        for (int64_t o = 0; o < O; ++o) {
+            for (int64_t oy = 0; oy < OH; ++oy)
+                for (int64_t ox = 0; ox < OW; ++ox) {
+                    double acc = bias ? (double)bias[o] : 0.0;
+                    for (int64_t c = 0; c < C; ++c)
+                        for (int64_t ky = 0; ky < kh; ++ky) {
+                            const int64_t iy = oy * sh + ky * dh - ph;
+                            if (iy < 0 || iy >= H) continue;
+                            for (int64_t kx = 0; kx < kw; ++kx) {
+                                const int64_t ix = ox * sw + kx * dw - pw;
+                                if (ix < 0 || ix >= W) continue;
+                                acc += (double)in[((b * C + c) * H + iy) * W + ix] *
+                                       w[((o * C + c) * kh + ky) * kw + kx];
+                            }
+                        }
+                    out[((b * O + o) * OH + oy) * OW + ox] = acc;
+                }
+        }
+    free(w);
+}
+
+/*
+ * Timed CPU arms for the packed-F16 rows (f32 throughout, OpenMP): the rhs
+ * widened once into column panels, then the blocked SGEMM above; the
+ * convolution as im2col rows per output row block, then the same SGEMM.
+ */
+static void f16_panels(const uint16_t* rhs, int64_t K, int64_t N, int64_t inner, int64_t col, float* panels) {
+    const int64_t P = (N + NR - 1) / NR;
+#pragma omp parallel for schedule(static)
+    for (int64_t p = 0; p < P; ++p) {
+        float* dst = panels + p * K * NR;
+        for (int64_t k = 0; k < K; ++k)
+            for (int j = 0; j < NR; ++j) {
+                const int64_t n = p * NR + j;
+                dst[k * NR + j] = n < N ? f16_value(rhs[k * inner + n * col]) : 0.0f;
+            }
+    }
+}
+
+static void sgemm_panels(const float* x, int64_t M, int64_t K, int64_t ldx, const float* panels, int64_t N,
+                         float* y, int64_t ldy_n, int64_t ldy_m) {
+    const int64_t P = (N + NR - 1) / NR, MB = (M + MR - 1) / MR;
+#pragma omp parallel for collapse(2) schedule(dynamic, 4)
+    for (int64_t p = 0; p < P; ++p)
+        for (int64_t mb = 0; mb < MB; ++mb) {
+            const int64_t m0 = mb * MR;
+            const int rows = (int)((M - m0) < MR ? (M - m0) : MR);
+            float acc[MR][NR];
+            memset(acc, 0, sizeof(acc));
+            const float* panel = panels + p * K * NR;
+            for (int64_t k0 = 0; k0 < K; k0 += KC) {
+                const int64_t kc = (K - k0) < KC ? (K - k0) : KC;
+#if defined(__x86_64__)
+                if (g_have_avx2)
+                    micro_avx2(x + m0 * ldx, ldx, panel, k0, kc, rows, acc);
+                else
+#endif
+                    micro_scalar(x + m0 * ldx, ldx, panel, k0, kc, rows, acc);
+            }
+            for (int r = 0; r < rows; ++r)
+                for (int j = 0; j < NR; ++j) {
+                    const int64_t n = p * NR + j;
+                    if (n < N) y[(m0 + r) * ldy_m + n * ldy_n] = acc[r][j];
+                }
+        }
+}
+
+static void detect_avx2(void) {
+#if defined(__x86_64__)
+    if (g_have_avx2 < 0) {
+        __builtin_cpu_init();
+        g_have_avx2 = __builtin_cpu_supports("avx2") && __builtin_cpu_supports("fma");
+    }
+#else
+    g_have_avx2 = 0;
+#endif
+}
+
+int orc_cpu_f16_matmul(const float* lhs, int64_t M, int64_t K, const uint16_t* rhs, int64_t inner, int64_t col,
+                       int64_t N, float* out, int32_t threads) {
+    if (M <= 0 || K <= 0 || N <= 0) return ORC_ESHAPE;
+#ifdef _OPENMP
+    if (threads > 0) omp_set_num_threads(threads);
+#else
+    (void)threads;
+#endif
+    detect_avx2();
+    const int64_t P = (N + NR - 1) / NR;
+    float* panels = (float*)aligned_alloc(64, sizeof(float) * (size_t)(P * K * NR) + 64);
+    if (!panels) return ORC_ESHAPE;
+    f16_panels(rhs, K, N, inner, col, panels);
+    sgemm_panels(lhs, M, K, K, panels, N, out, 1, N);
+    free(panels);
+    return ORC_OK;
+}
+
+/* out NCHW f32; the rows of one image's output plane block are gathered
+ * (im2col, [rows][C*kh*kw]) and multiplied by the OIHW weight panels. */
+int orc_cpu_f16_conv2d(const float* in, int64_t B, int64_t C, int64_t H, int64_t W, const uint16_t* wt, int64_t O,
+                       int64_t kh, int64_t kw, const float* bias, int64_t sh, int64_t sw, int64_t ph, int64_t pw,
+                       int64_t dh, int64_t dw, float* out, int32_t threads) {
+    const int64_t OH = (H + 2 * ph - dh * (kh - 1) - 1) / sh + 1;
+    const int64_t OW = (W + 2 * pw - dw * (kw - 1) - 1) / sw + 1;
+    if (B <= 0 || C <= 0 || O <= 0 || OH <= 0 || OW <= 0) return ORC_ESHAPE;
+#ifdef _OPENMP
+    if (threads > 0) omp_set_num_threads(threads);
+#else
+    (void)threads;
+#endif
+    detect_avx2();
+    const int64_t inner = C * kh * kw, P = (O + NR - 1) / NR;
+    /* OIHW is [O][inner]: element (k, o) at o * inner + k */
+    float* panels = (float*)aligned_alloc(64, sizeof(float) * (size_t)(P * inner * NR) + 64);
+    const int64_t RB = 4096; /* output positions per im2col block */
+    float* cols = (float*)aligned_alloc(64, sizeof(float) * (size_t)(RB * inner) + 64);
+    if (!panels || !cols) {
+        free(panels);
+        free(cols);
+        return ORC_ESHAPE;
+    }
+    f16_panels(wt, inner, O, 1, inner, panels);
+    const int64_t plane = OH * OW;
+    for (int64_t b = 0; b < B; ++b)
+        for (int64_t r0 = 0; r0 < plane; r0 += RB) {
+            const int64_t rows = plane - r0 < RB ? plane - r0 : RB;
+#pragma omp parallel for schedule(static)
+            for (int64_t r = 0; r < rows; ++r) {
+                const int64_t oy = (r0 + r) / OW, ox = (r0 + r) % OW;
+                float* dst = cols + r * inner;
+                for (int64_t c = 0; c < C; ++c)
+                    for (int64_t ky = 0; ky < kh; ++ky)
+                        for (int64_t kx = 0; kx < kw; ++kx) {
+                            const int64_t iy = oy * sh + ky * dh - ph, ix = ox * sw + kx * dw - pw;
+                            *dst++ = (iy >= 0 && iy < H && ix >= 0 && ix < W) ? in[((b * C + c) * H + iy) * W + ix]
+                                                                               : 0.0f;
+                        }
+            }
+            /* y[(b, o, r0 + r)] : row r of this block, column o -> plane stride */
+            sgemm_panels(cols, rows, inner, inner, panels, O, out + b * O * plane + r0, plane, 1);
+        }
+    if (bias)
+        for (int64_t b = 0; b < B; ++b)
+            for (int64_t o = 0; o < O; ++o)
+                for (int64_t i = 0; i < plane; ++i) out[(b * O + o) * plane + i] += bias[o];
+    free(panels);
+    free(cols);
+    return ORC_OK;
+}
