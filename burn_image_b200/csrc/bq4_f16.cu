@@ -363,7 +363,7 @@ struct ConvShape {
 
 bq4_status conv_shape(const bq4_weight* w, int64_t B, int64_t H, int64_t W, const bq4_conv2d_options* o,
                       ConvShape* cs) {
-  if (!w || !w->h || !w->conv_kh) return set_error(BQ4_EINVAL_ARG, "w is not a prepared packed-F16 conv weight");
+  if (!w || !w->tf32 || !w->conv_kh) return set_error(BQ4_EINVAL_ARG, "w is not a packed-F16 conv weight");
   if (!o) return set_error(BQ4_EINVAL_ARG, "options is NULL");
   if (o->groups != 1) return set_error(BQ4_EUNSUPPORTED, "groups=%d: only groups = 1", (int)o->groups);
   for (int i = 0; i < 2; ++i)
@@ -643,7 +643,6 @@ bq4_status bq4_packed_f16_conv2d_workspace_size(int64_t batch, int64_t in_channe
   bq4_weight w;
   conv_view(out_channels, in_channels, kernel_h, kernel_w, &w);
   w.device = dev;
-  w.h = reinterpret_cast<uint16_t*>(&w);  // a view: only its geometry is read
   ConvShape cs;
   bq4_status st = conv_shape(&w, batch, in_h, in_w, options, &cs);
   if (st) return st;

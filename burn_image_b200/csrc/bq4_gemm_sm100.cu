@@ -1428,12 +1428,12 @@ bq4_status plan_gemm(const bq4_weight* w, int nw, int64_t M, int device, GemmPla
   p->nw = nw;
   p->tf = w->tf32 ? 1 : 0;
   p->cv = cv ? 1 : 0;
-  if ((p->tf || cv) && (nw != 1 || qk || !w->h || (cv && !p->tf)))
+  if ((p->tf || cv) && (nw != 1 || qk || (cv && !p->tf)))
     return set_error(BQ4_EINVAL_ARG, "packed-F16 plans take one packed-F16 weight and the plain or conv epilogue");
   // Numerics: blocks of 64/128 keep q exact in f16 and multiply the f32
   // partial of each K block by its scale (exact weights); smaller blocks
   // stage f16(q * f16(scale)) (folded); N-packed sources are pre-expanded.
-  p->pre = w->h != nullptr ? 1 : 0;
+  p->pre = (w->h != nullptr || w->tf32) ? 1 : 0;  // packed-F16 views are pre-expanded too
   const int mode = numerics_mode();
   p->exact = (!p->pre && w->block >= 64 &&
               (mode == BQ4_NUMERICS_EXACT || (mode == BQ4_NUMERICS_AUTO && M <= kAutoExactMaxM)))
