@@ -132,26 +132,30 @@ __global__ void f16_select_rows_vec8_kernel(const uint4* __restrict__ table, int
   }
 }
 
-// MMA-ready tf32 weight tiles: f32 [ntiles][nkc][128 rows][32 K], 16-byte
-// chunk j of row r stored at chunk j ^ (r & 7) (the 128-byte swizzle).  One
-// thread per chunk (4 K values of one output row n).  Source element (k, n):
+// MMA-ready tf32 weight tiles: f32 [ntiles][nkc][128 rows][RF K] with RF =
+// 16 (64-byte rows, 64-byte swizzle: 16-byte chunk j of row r stored at
+// chunk j ^ ((r >> 1) & 3)) for the linear, or RF = 32 (128-byte rows,
+// 128-byte swizzle: chunk j at j ^ (r & 7)) for the convolution.  One thread
+// per 16-byte chunk (4 K values of one output row n).  Source element (k, n):
 //   linear: packed[k * inner_stride + n * col_stride];
 //   conv (taps > 0): k = tap * cp + c, packed OIHW [n][cin][taps], zero for
 //   c >= cin (channel padding).
 // K >= K_real and n >= N are zero.
+template <int RF>
 __global__ void prepare_f16_tiles_kernel(const uint16_t* __restrict__ src, int64_t K, int64_t N,
                                          int64_t inner_stride, int64_t col_stride, int taps, int cin, int cp,
                                          int64_t nkc, int64_t total, float* __restrict__ out) {
+  constexpr int kJ = RF / 4;  // 16-byte chunks per row
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t j = i & 7;
-    const int64_t r = (i >> 3) & 127;
-    const int64_t kc = (i >> 10) % nkc;
-    const int64_t tile = (i >> 10) / nkc;
+    const int64_t j = i % kJ;
+    const int64_t r = (i / kJ) & 127;
+    const int64_t kc = (i / (kJ * 128)) % nkc;
+    const int64_t tile = (i / (kJ * 128)) / nkc;
     const int64_t n = tile * 128 + r;
     float v[4];
 #pragma unroll
     for (int t = 0; t < 4; ++t) {
-      const int64_t k = kc * 32 + j * 4 + t;
+      const int64_t k = kc * RF + j * 4 + t;
       uint32_t bits = 0;
       if (n < N && k < K) {
         if (taps > 0) {
@@ -163,7 +167,8 @@ __global__ void prepare_f16_tiles_kernel(const uint16_t* __restrict__ src, int64
       }
       v[t] = widen_f16(bits);
     }
-    *reinterpret_cast<float4*>(out + ((tile * nkc + kc) * 128 + r) * 32 + ((j ^ (r & 7)) * 4)) =
+    const int64_t js = RF == 16 ? (j ^ ((r >> 1) & 3)) : (j ^ (r & 7));
+    *reinterpret_cast<float4*>(out + ((tile * nkc + kc) * 128 + r) * RF + js * 4) =
         make_float4(v[0], v[1], v[2], v[3]);
   }
 }
@@ -273,24 +278,25 @@ bq4_status need_sm100(int dev) {
   return BQ4_OK;
 }
 
-// Weight view of a packed-F16 operand, K x N (no allocation).  Conv
-// weights: K = taps * cp, kh/kw/cin recorded.
-void f16_view(int64_t K, int64_t N, bq4_weight* w) {
+// Weight view of a packed-F16 operand, K x N (no allocation): tiles of
+// 128 rows x rf K f32 (rf = 16 for the linear, 32 for the convolution), K
+// padded to a stage (2 rf).  Conv weights: K = taps * cp, kh/kw/cin recorded.
+void f16_view(int64_t K, int64_t N, bq4_weight* w, int rf = 16) {
   memset(w, 0, sizeof(*w));
   w->K = K;
   w->N = N;
   w->layout = BQ4_LAYOUT_F16;
   w->tf32 = 1;
-  w->Kp = round_up(K, 64);  // a stage is two 32-K chunks
-  w->nkc = w->Kp / 32;
+  w->Kp = round_up(K, 2 * rf);  // a stage is two chunks
+  w->nkc = w->Kp / rf;
   w->ntiles = (N + kTileN - 1) / kTileN;
   w->Np = w->ntiles * kTileN;
-  w->h_bytes = (size_t)w->ntiles * w->nkc * 128 * 32 * sizeof(float);
+  w->h_bytes = (size_t)w->ntiles * w->nkc * 128 * rf * sizeof(float);
 }
 
 void conv_view(int64_t cout, int64_t cin, int kh, int kw, bq4_weight* w) {
   const int64_t cp = round_up(cin, 32);
-  f16_view((int64_t)kh * kw * cp, cout, w);
+  f16_view((int64_t)kh * kw * cp, cout, w, 32);
   w->conv_kh = kh;
   w->conv_kw = kw;
   w->conv_cin = (int32_t)cin;
@@ -299,10 +305,16 @@ void conv_view(int64_t cout, int64_t cin, int kh, int kw, bq4_weight* w) {
 
 cudaError_t launch_prepare_f16(const uint16_t* src, const bq4_weight* w, int64_t inner, int64_t col,
                                cudaStream_t s) {
-  const int64_t total = w->ntiles * w->nkc * 1024;
   const int taps = w->conv_kh ? w->conv_kh * w->conv_kw : 0;
-  prepare_f16_tiles_kernel<<<grid_for(total, 256, current_device()), 256, 0, s>>>(
-      src, w->K, w->N, inner, col, taps, w->conv_cin, w->conv_cp, w->nkc, total, reinterpret_cast<float*>(w->h));
+  if (taps) {  // 128-byte rows
+    const int64_t total = w->ntiles * w->nkc * 1024;
+    prepare_f16_tiles_kernel<32><<<grid_for(total, 256, current_device()), 256, 0, s>>>(
+        src, w->K, w->N, inner, col, taps, w->conv_cin, w->conv_cp, w->nkc, total, reinterpret_cast<float*>(w->h));
+  } else {     // 64-byte rows
+    const int64_t total = w->ntiles * w->nkc * 512;
+    prepare_f16_tiles_kernel<16><<<grid_for(total, 256, current_device()), 256, 0, s>>>(
+        src, w->K, w->N, inner, col, 0, 0, 0, w->nkc, total, reinterpret_cast<float*>(w->h));
+  }
   note_launch();
   return cudaGetLastError();
 }
@@ -379,7 +391,7 @@ bq4_status conv_shape(const bq4_weight* w, int64_t B, int64_t H, int64_t W, cons
   cs->OW = (cs->Wp - ew) / o->stride[1] + 1;
   cs->implicit = o->stride[0] == 1 && o->stride[1] == 1;
   cs->M = cs->implicit ? B * cs->Hp * cs->Wp : B * cs->OH * cs->OW;
-  if (cs->Hp > 65535 || B * (w->conv_cp / 32) > 65535 || cs->M > ((int64_t)1 << 30) ||
+  if (cs->Hp > 65535 || B * ((w->conv_cp + 31) / 32) > 65535 || cs->M > ((int64_t)1 << 30) ||
       (int64_t)o->dilation[0] * cs->Wp * kh > ((int64_t)1 << 30))
     return set_error(BQ4_EINVAL_SHAPE, "convolution too large");
   cs->stage_bytes = up256((size_t)(B * cs->Hp * cs->Wp) * (size_t)w->conv_cp * sizeof(float));
@@ -408,7 +420,7 @@ bq4_status run_conv(const float* input, int64_t B, int64_t H, int64_t W, const b
   if (!al(ws, 256)) return set_error(BQ4_EALIGN, "workspace not 256-byte aligned");
   const int cp = w->conv_cp, cin = w->conv_cin;
   float* staged = reinterpret_cast<float*>(ws);
-  const int cblocks = cp / 32;
+  const int cblocks = (cp + 31) / 32;
   stage_nhwc_kernel<<<dim3((unsigned)((cs.Wp + 31) / 32), (unsigned)cs.Hp, (unsigned)(B * cblocks)), dim3(32, 8), 0,
                       s>>>(input, cin, (int)H, (int)W, cp, (int)cs.Hp, (int)cs.Wp, o->padding[0], o->padding[1],
                            cblocks, staged);

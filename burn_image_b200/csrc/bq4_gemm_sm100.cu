@@ -230,7 +230,7 @@ __device__ __forceinline__ void store_out(const WsArgs& a, int m, int n, float v
 // kc for the token tile starting at row m0 (see WsArgs::cv_*).  A chunk past
 // the last tap (K padding) starts at row M: the whole box is out of bounds
 // and reads zeros.
-__device__ __forceinline__ void cv_coord(const WsArgs& a, int kc, int m0, int& x, int& y) {
+__device__ __forceinline__ void cv_coord(const WsArgs& a, int kc, int ck, int m0, int& x, int& y) {
   const int tap = kc / a.cv_cchunks;
   if (tap >= a.cv_taps) {
     x = 0;
@@ -238,7 +238,7 @@ __device__ __forceinline__ void cv_coord(const WsArgs& a, int kc, int m0, int& x
     return;
   }
   const int ky = tap / a.cv_kw;
-  x = (kc - tap * a.cv_cchunks) * 32;
+  x = (kc - tap * a.cv_cchunks) * ck;
   y = m0 + ky * a.cv_dy + (tap - ky * a.cv_kw) * a.cv_dx;
 }
 
@@ -607,9 +607,10 @@ __device__ __forceinline__ void split_reduce_epilogue(const WsArgs& a) {
 // [0, NW*BT)) and one 64-column A slot per stage after it.  Folded numerics,
 // one weight.
 // TF = true: packed-F16 weights, kind::tf32.  Both operands are f32 rows
-// (pre-expanded weight tiles [128][32] f32 and f32 token tiles read by TMA
-// straight from the caller's rows), so a 128-byte operand row holds 32 K
-// values and a stage 64; the MMA walks the same bytes as kind::f16.
+// (pre-expanded weight tiles and f32 token tiles read by TMA straight from
+// the caller's rows).  The linear uses rows of 64 bytes with the 64-byte
+// swizzle: a chunk is 16 K, a stage 32 K, and a 256-token stage 48 KB, so 4
+// stages are in flight where 128-byte rows fit 2.
 // CV = true (implies TF): implicit-GEMM convolution.  The token rows of chunk kc
 // are shifted by its kernel tap (cv_coord), and the operands are swapped:
 // A = the token tile (128 tokens per MMA, BT/128 MMAs), B = the 128-channel
@@ -621,8 +622,16 @@ __global__ void __launch_bounds__(kWsThreads, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
-  constexpr uint32_t kBSub = BT * 128;              // one 64-K token sub-tile
-  constexpr uint32_t kAStage = TA ? 0u : NW * 2 * kATileBytes;
+  // Operand rows: 128 bytes (64 f16, or 32 f32 for the convolution) with the
+  // 128-byte swizzle; the tf32 linear uses 64-byte rows (16 f32) with the
+  // 64-byte swizzle, so that a stage stays small enough for 4..8 of them to be
+  // in flight.  (The convolution's row-shifted boxes measured slower that way:
+  // twice the TMA row requests per byte.)
+  constexpr bool kNarrow = TF && !CV;
+  constexpr uint32_t kRowB = kNarrow ? 64u : 128u;
+  constexpr uint32_t kATile = 128 * kRowB;          // one weight sub-tile (128 rows)
+  constexpr uint32_t kBSub = BT * kRowB;            // one token sub-tile
+  constexpr uint32_t kAStage = TA ? 0u : NW * 2 * kATile;
   constexpr uint32_t kStage = kAStage + 2 * kBSub;
   constexpr uint32_t kPartCols = NW * BT;
   // partial buffers in TMEM: TA keeps 256 columns for them (one 256-token
@@ -638,7 +647,8 @@ __global__ void __launch_bounds__(kWsThreads, 1)
   static_assert(!SC || (NW == 1 && !QK), "row scatter: one weight, plain epilogue");
   static_assert(!TF || (NW == 1 && !TA && !QK && !SC), "tf32: one pre-expanded weight, plain epilogue");
   static_assert(!CV || (TF && BT >= 128), "convolution: tf32, 128-token MMAs");
-  constexpr int kCK = TF ? 32 : kChunkK;  // K values per 128-byte operand row
+  constexpr int kCK = TF ? (int)kRowB / 4 : kChunkK;  // K values per operand row
+  constexpr int kSteps = (int)kRowB / 32;  // MMA K steps per row (32 bytes each)
 
   const int S = a.stages, RS = a.rs;
   uint8_t* ring = smem;                                     // [S][A | B]
@@ -709,16 +719,16 @@ __global__ void __launch_bounds__(kWsThreads, 1)
           ptx::mbar_arrive_expect_tx(&full[s], 2 * kBSub + (a.pre ? kAStage : 0u));
           int x0 = kc * kCK, y0 = mtile * BT, x1 = (kc + 1) * kCK, y1 = mtile * BT;
           if constexpr (CV) {
-            cv_coord(a, kc, mtile * BT, x0, y0);
-            cv_coord(a, kc + 1, mtile * BT, x1, y1);
+            cv_coord(a, kc, kCK, mtile * BT, x0, y0);
+            cv_coord(a, kc + 1, kCK, mtile * BT, x1, y1);
           }
           ptx::tma_load_2d(st + kAStage, &tmap_x, &full[s], x0, y0);
           ptx::tma_load_2d(st + kAStage + kBSub, &tmap_x, &full[s], x1, y1);
           if (a.pre) {
 #pragma unroll
             for (int w = 0; w < NW; ++w)
-              ptx::bulk_load(st + (size_t)w * 2 * kATileBytes,
-                             a.h[w] + ((size_t)ntile * a.nkc + kc) * (kATileBytes / 2), 2 * kATileBytes, &full[s]);
+              ptx::bulk_load(st + (size_t)w * 2 * kATile, a.h[w] + ((size_t)ntile * a.nkc + kc) * (kATile / 2),
+                             2 * kATile, &full[s]);
           }
           if (++s == S) { s = 0; ph ^= 1; }
         }
@@ -777,20 +787,21 @@ __global__ void __launch_bounds__(kWsThreads, 1)
             }
             const uint32_t b_addr = st + kAStage + sub * kBSub;
 #pragma unroll
-            for (int kk = 0; kk < kChunkK / 16; ++kk) {
-              const uint64_t b_desc = ptx::umma_desc_sw128(b_addr + kk * 32);
+            for (int kk = 0; kk < kSteps; ++kk) {
+              const uint64_t b_desc =
+                  kNarrow ? ptx::umma_desc_sw64(b_addr + kk * 32) : ptx::umma_desc_sw128(b_addr + kk * 32);
               if constexpr (TA) {
                 ptx::mma_f16_ts(d_base, tmem_base + kACol0 + (uint32_t)s * 64 + (uint32_t)sub * 32 + kk * 8, b_desc,
                                 idesc, (first && kk == 0) ? 0u : 1u);
               } else if constexpr (CV) {
                 // tokens as A (128 per MMA), the weight tile as B (128 channels)
-                const uint64_t w_desc = ptx::umma_desc_sw128(st + (uint32_t)(sub * kATileBytes) + kk * 32);
+                const uint64_t w_desc = ptx::umma_desc_sw128(st + (uint32_t)(sub * kATile) + kk * 32);
 #pragma unroll
                 for (int h = 0; h < BT / 128; ++h)
-                  ptx::mma_tf32_ss(d_base + h * 128, ptx::umma_desc_sw128(b_addr + h * 128 * 128 + kk * 32), w_desc,
+                  ptx::mma_tf32_ss(d_base + h * 128, ptx::umma_desc_sw128(b_addr + h * 128 * kRowB + kk * 32), w_desc,
                                    idesc, (first && kk == 0) ? 0u : 1u);
               } else if constexpr (TF) {
-                ptx::mma_tf32_ss(d_base, ptx::umma_desc_sw128(st + (uint32_t)(sub * kATileBytes) + kk * 32), b_desc,
+                ptx::mma_tf32_ss(d_base, ptx::umma_desc_sw64(st + (uint32_t)(sub * kATile) + kk * 32), b_desc,
                                  idesc, (first && kk == 0) ? 0u : 1u);
               } else {
 #pragma unroll
@@ -1290,8 +1301,11 @@ static bq4_status plan_for_bt(const bq4_weight* w, int nw, int64_t M, int device
   p->ta = (!p->pre && nw == 1 && !getenv("BQ4_NO_TA") &&
            ((!p->exact && p->bt == 256) || (p->exact && p->bt == 128 && getenv("BQ4_EXACT_TA"))))
               ? 1 : 0;
-  const size_t stage_bytes = (p->ta ? 0 : (size_t)nw * 2 * kATileBytes) + 2 * (size_t)p->bt * 128;
-  const int max_stages = p->ta ? (512 - 256) / 64 : 4;  // TA: one 64-column TMEM A slot per stage
+  // operand rows: 128 bytes, or 64 for the tf32 linear (whose stages are then
+  // small enough for up to 8 in flight)
+  const size_t row_b = (p->tf && !cv) ? 64 : 128;
+  const size_t stage_bytes = (p->ta ? 0 : (size_t)nw * 2 * 128 * row_b) + 2 * (size_t)p->bt * row_b;
+  const int max_stages = p->ta ? (512 - 256) / 64 : (p->tf ? 8 : 4);  // TA: one 64-column TMEM A slot per stage
   const int np = p->ta ? 256 / p->bt : 512 / (nw * p->bt);  // TMEM partial buffers of the kernel
   const size_t raw_stage = (size_t)nw * p->raw_w_bytes;
   // QK: the epilogue's partial sums, 2 x 16 warps x BT/4 columns of f32
@@ -1335,7 +1349,9 @@ static bq4_status plan_for_bt(const bq4_weight* w, int nw, int64_t M, int device
   // splits of a tile form one thread-block cluster (at most 8 CTAs, the
   // portable limit), and split-K is only used when every cluster is
   // co-resident (one wave); multi-wave work uses whole-K units.
-  const double t_stage = (p->bt == 256 ? 1.1 : (p->bt == 128 ? 0.8 : 0.7)) * (nw == 2 ? 1.6 : 1.0);
+  // (a tf32 stage is 32 K at half the f16 rate: half an f16 stage's time)
+  const double t_stage =
+      (p->bt == 256 ? 1.1 : (p->bt == 128 ? 0.8 : 0.7)) * (nw == 2 ? 1.6 : 1.0) * (p->tf ? 0.5 : 1.0);
   const double t_red = 0.008 * p->bt * nw + 1.0;
   int best_s = 1;
   double best_t = 1e30;
@@ -1507,16 +1523,18 @@ bq4_status run_gemm(const GemmPlan& plan, const bq4_weight* const* ws, const voi
   EncodeTiledFn enc = encode_fn();
   if (!enc) return set_error(BQ4_ECUDA, "cuTensorMapEncodeTiled unavailable");
   CUtensorMap tmap;
-  // tf32: f32 rows of K values (conv: x_cols staged channels), box {32, BT};
-  // columns past the extent read zeros
+  // tf32: f32 rows of K values (conv: x_cols staged channels), box {16, BT}
+  // with the 64-byte swizzle (conv: {32, BT}, 128-byte swizzle); columns past
+  // the extent read zeros
+  const bool narrow = plan.tf && !plan.cv;
   const int64_t x_cols = plan.tf ? (io.cv ? io.cv->x_cols : w0->K) : w0->Kp;
   cuuint64_t gdim[2] = {(cuuint64_t)x_cols, (cuuint64_t)M};
   cuuint64_t gstride[1] = {(cuuint64_t)x_pitch * (plan.tf ? 4 : 2)};
-  cuuint32_t box[2] = {(cuuint32_t)(plan.tf ? 32 : kChunkK), (cuuint32_t)plan.bt};
+  cuuint32_t box[2] = {(cuuint32_t)(narrow ? 16 : (plan.tf ? 32 : kChunkK)), (cuuint32_t)plan.bt};
   cuuint32_t estride[2] = {1, 1};
   CUresult cr = enc(&tmap, plan.tf ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
-                    const_cast<void*>(xh), gdim, gstride, box, estride,
-                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                    const_cast<void*>(xh), gdim, gstride, box, estride, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                    narrow ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B,
                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (cr != CUDA_SUCCESS) return set_error(BQ4_ECUDA, "cuTensorMapEncodeTiled failed (%d)", (int)cr);
 

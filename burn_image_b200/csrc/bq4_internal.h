@@ -37,11 +37,13 @@ struct bq4_weight {
   // 16 KiB bulk copy lands as an MMA-ready operand tile.  q/s unused.
   uint16_t* h;
   size_t h_bytes;
-  // Packed-F16 weights (tf32 = 1): h holds f32 tiles [ntiles][nkc][128][32]
-  // (tf32-exact widened f16 values) with the same 128-byte swizzle, so a
-  // chunk is 32 K and Kp is a multiple of 64.  Convolution weights (conv_kh
-  // > 0) order K as (tap = ky * conv_kw + kx, channel): K = taps * conv_cp,
-  // channels padded to conv_cp = a multiple of 32 with zeros.
+  // Packed-F16 weights (tf32 = 1): h holds f32 tiles of tf32-exact widened
+  // f16 values, [ntiles][nkc][128][16] in 64-byte rows with the 64-byte
+  // swizzle (linear: a chunk is 16 K, Kp a multiple of 32), or
+  // [ntiles][nkc][128][32] in 128-byte rows with the 128-byte swizzle
+  // (convolution, conv_kh > 0: a chunk is 32 K, Kp a multiple of 64).
+  // Convolution weights order K as (tap = ky * conv_kw + kx, channel):
+  // K = taps * conv_cp, channels padded to conv_cp = a multiple of 32 with zeros.
   int32_t tf32;
   int32_t conv_kh, conv_kw, conv_cin, conv_cp;
 };

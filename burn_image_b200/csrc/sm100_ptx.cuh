@@ -289,6 +289,20 @@ __device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t smem_addr) {
   return d;
 }
 
+// The same for the 64-byte swizzle: rows of 64 bytes, 8-row groups 512
+// bytes apart (SBO = 512), layout type 4 (SWIZZLE_64B).  The operand base
+// must be 512-aligned; the start address advances by 32 bytes per K step
+// (two steps per row).
+__device__ __forceinline__ uint64_t umma_desc_sw64(uint32_t smem_addr) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((smem_addr >> 4) & 0x3FFF);
+  d |= static_cast<uint64_t>(1) << 16;             // LBO (unused for swizzled K-major)
+  d |= static_cast<uint64_t>(512 >> 4) << 32;      // SBO
+  d |= static_cast<uint64_t>(1) << 46;             // version
+  d |= static_cast<uint64_t>(4) << 61;             // SWIZZLE_64B
+  return d;
+}
+
 // Instruction descriptor, kind::f16: A,B f16, D f32, both K-major, MxN.
 __host__ __device__ constexpr uint32_t umma_idesc_f16(uint32_t M, uint32_t N) {
   return (1u << 4)              // D format f32
@@ -302,8 +316,8 @@ __host__ __device__ constexpr uint32_t umma_idesc_f16(uint32_t M, uint32_t N) {
 
 // Instruction descriptor, kind::tf32: A,B tf32 (f32 in memory, the tensor
 // core reads sign, exponent and the top 10 mantissa bits), D f32, both
-// K-major, MxN.  One K=8 step spans the same 32 bytes of a 128-byte operand
-// row as a K=16 step of kind::f16.
+// K-major, MxN.  One K=8 step spans 32 bytes of an operand row, as a K=16
+// step of kind::f16 does.
 __host__ __device__ constexpr uint32_t umma_idesc_tf32(uint32_t M, uint32_t N) {
   return (1u << 4)              // D format f32
          | (2u << 7)            // A tf32
