@@ -1392,8 +1392,10 @@ static bq4_status plan_for_bt(const bq4_weight* w, int nw, int64_t M, int device
   // for the gated pair's 152); folded plans lose: with the weight tile in
   // TMEM the single accumulator serialises the pieces' epilogues (1.05-1.2x),
   // and 128-token folded tiles with the tail lose to 256-token whole tiles
-  // (c1: 63.6 vs 55.1 µs).  Those keep whole tiles.  BQ4_NO_STREAMK=1 keeps
-  // whole tiles everywhere.
+  // (c1: 63.6 vs 55.1 µs).  Those keep whole tiles, and so does the tf32
+  // linear (4096^3, 512 tiles: 256.6 vs 255.9 µs -- its operand ingest, not
+  // the partial last wave, sets the time).  BQ4_NO_STREAMK=1 keeps whole
+  // tiles everywhere.
   p->dp_tiles = p->sk_tiles = 0;
   p->sk_bytes = 0;
   if (best_s == 1 && allow_sk && (p->exact || nw == 2) && !p->ta && !getenv("BQ4_NO_STREAMK") && tiles > sms &&
