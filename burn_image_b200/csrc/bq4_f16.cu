@@ -291,7 +291,8 @@ void f16_view(int64_t K, int64_t N, bq4_weight* w, int rf = 16) {
   w->nkc = w->Kp / rf;
   w->ntiles = (N + kTileN - 1) / kTileN;
   w->Np = w->ntiles * kTileN;
-  w->h_bytes = (size_t)w->ntiles * w->nkc * 128 * rf * sizeof(float);
+  // an even number of tiles: the wide kernel takes N tiles in pairs
+  w->h_bytes = (size_t)((w->ntiles + 1) / 2 * 2) * w->nkc * 128 * rf * sizeof(float);
 }
 
 void conv_view(int64_t cout, int64_t cin, int kh, int kw, bq4_weight* w) {
@@ -310,8 +311,8 @@ cudaError_t launch_prepare_f16(const uint16_t* src, const bq4_weight* w, int64_t
     const int64_t total = w->ntiles * w->nkc * 1024;
     prepare_f16_tiles_kernel<32><<<grid_for(total, 256, current_device()), 256, 0, s>>>(
         src, w->K, w->N, inner, col, taps, w->conv_cin, w->conv_cp, w->nkc, total, reinterpret_cast<float*>(w->h));
-  } else {     // 64-byte rows
-    const int64_t total = w->ntiles * w->nkc * 512;
+  } else {     // 64-byte rows; the tile after an odd last one is zeroed
+    const int64_t total = (w->ntiles + 1) / 2 * 2 * w->nkc * 512;
     prepare_f16_tiles_kernel<16><<<grid_for(total, 256, current_device()), 256, 0, s>>>(
         src, w->K, w->N, inner, col, 0, 0, 0, w->nkc, total, reinterpret_cast<float*>(w->h));
   }

@@ -640,12 +640,18 @@ __global__ void __launch_bounds__(kWsThreads, 1)
   constexpr uint32_t kACol0 = kNP * kPartCols;    // TA: first A-slot column
   constexpr int kCols = BT / 4;          // token columns per scaler thread
   constexpr bool kSK = !TA;              // stream-K tails are planned only for A in shared memory
-  static_assert(TA || kNP >= 2, "at least double buffering");
+  // TF with NW = 2 ("wide"): the two weights are consecutive 128-row N tiles
+  // of one weight on one 256-token tile, so a CTA computes 256 x 256 outputs
+  // from 2 KB of operands per K (a 128 x 256 tile needs 1.5 KB for half the
+  // FLOPs).  Its accumulator pair fills TMEM: one partial buffer.
+  constexpr bool kWide = TF && NW == 2;
+  static_assert(TA || kNP >= 2 || kWide, "at least double buffering");
   static_assert(!TA || (NW == 1 && kACol0 == 256 && BT >= 128), "TMEM operand A: one weight, slots from column 256");
   static_assert(kCols % 16 == 0, "scaler column split");
   static_assert(!QK || (NW == 1 && BT >= 128), "QK-norm epilogue: one weight, 128- or 256-token tiles");
   static_assert(!SC || (NW == 1 && !QK), "row scatter: one weight, plain epilogue");
-  static_assert(!TF || (NW == 1 && !TA && !QK && !SC), "tf32: one pre-expanded weight, plain epilogue");
+  static_assert(!TF || ((NW == 1 || (NW == 2 && BT == 256 && !CV)) && !TA && !QK && !SC),
+                "tf32: pre-expanded weight tiles, plain epilogue");
   static_assert(!CV || (TF && BT >= 128), "convolution: tf32, 128-token MMAs");
   constexpr int kCK = TF ? (int)kRowB / 4 : kChunkK;  // K values per operand row
   constexpr int kSteps = (int)kRowB / 32;  // MMA K steps per row (32 bytes each)
@@ -726,9 +732,11 @@ __global__ void __launch_bounds__(kWsThreads, 1)
           ptx::tma_load_2d(st + kAStage + kBSub, &tmap_x, &full[s], x1, y1);
           if (a.pre) {
 #pragma unroll
-            for (int w = 0; w < NW; ++w)
-              ptx::bulk_load(st + (size_t)w * 2 * kATile, a.h[w] + ((size_t)ntile * a.nkc + kc) * (kATile / 2),
+            for (int w = 0; w < NW; ++w) {
+              const int tw = kWide ? 2 * ntile + w : ntile;  // wide: N tiles 2 ntile, 2 ntile + 1
+              ptx::bulk_load(st + (size_t)w * 2 * kATile, a.h[w] + ((size_t)tw * a.nkc + kc) * (kATile / 2),
                              2 * kATile, &full[s]);
+            }
           }
           if (++s == S) { s = 0; ph ^= 1; }
         }
@@ -801,8 +809,10 @@ __global__ void __launch_bounds__(kWsThreads, 1)
                   ptx::mma_tf32_ss(d_base + h * 128, ptx::umma_desc_sw128(b_addr + h * 128 * kRowB + kk * 32), w_desc,
                                    idesc, (first && kk == 0) ? 0u : 1u);
               } else if constexpr (TF) {
-                ptx::mma_tf32_ss(d_base, ptx::umma_desc_sw64(st + (uint32_t)(sub * kATile) + kk * 32), b_desc,
-                                 idesc, (first && kk == 0) ? 0u : 1u);
+#pragma unroll
+                for (int w = 0; w < NW; ++w)
+                  ptx::mma_tf32_ss(d_base + w * BT, ptx::umma_desc_sw64(st + (uint32_t)((w * 2 + sub) * kATile) + kk * 32),
+                                   b_desc, idesc, (first && kk == 0) ? 0u : 1u);
               } else {
 #pragma unroll
                 for (int w = 0; w < NW; ++w)
@@ -928,120 +938,156 @@ __global__ void __launch_bounds__(kWsThreads, 1)
       const int tile = un.tile, split = un.split, kc0 = un.kc0, kc1 = un.kc1;
       int mtile, ntile;
       ws_tile(a, tile, mtile, ntile);
-      const int n = ntile * 128 + row;
-      const int m0 = mtile * BT + col0;
-      float acc[NW][kCols];
-#pragma unroll
-      for (int w = 0; w < NW; ++w)
-#pragma unroll
-        for (int j = 0; j < kCols; ++j) acc[w][j] = 0.0f;
-      for (int kc = kc0; kc < kc1; ++kc) {
-        if (!ws_seg_last(kc, kc1, cpb)) continue;
-        float sc[NW];
-#pragma unroll
-        for (int w = 0; w < NW; ++w)
-          sc[w] = a.exact ? __ldg(a.s[w] + ((size_t)ntile * a.nkb + (kc * kChunkK) / a.block) * 128 + row) : 1.0f;
-        // lockstep: segment == stage pb (partial pb), retired when empty[pb] completes
-        if (!ptx::mbar_wait(a.lockstep ? &empty[pb] : &part_full[pb], pph, abort_flag)) { ok = false; break; }
+      if constexpr (kWide) {
+        // stream each 16-column chunk of the two accumulators from TMEM to y
+        // (the pair does not fit the registers), then release the buffer
+        if (!ptx::mbar_wait(&part_full[pb], pph, abort_flag)) { ok = false; break; }
         ptx::tc_fence_after();
         const uint32_t t_row = tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)pb * kPartCols + col0;
+        const int m0w = mtile * BT + col0;
+        const int act = a.act;
 #pragma unroll
         for (int w = 0; w < NW; ++w) {
+          const int nw_ = (2 * ntile + w) * 128 + row;
+          const float bw = (a.bias[0] && nw_ < a.N) ? __ldg(a.bias[0] + nw_) : 0.0f;
 #pragma unroll
           for (int c = 0; c < kCols / 16; ++c) {
             uint32_t r0[16];
             ptx::tmem_ld_32x32b_x16(t_row + w * BT + c * 16, r0);
             ptx::tmem_ld_wait();
+            if (nw_ < a.N) {
 #pragma unroll
-            for (int j = 0; j < 16; ++j) acc[w][c * 16 + j] = fmaf(sc[w], __uint_as_float(r0[j]), acc[w][c * 16 + j]);
-          }
-        }
-        ptx::tc_fence_before();
-        __syncwarp();
-        if (lane == 0) ptx::mbar_arrive(a.lockstep ? &full[pb] : &part_empty[pb]);
-        if (++pb == (a.lockstep ? S : kNP)) { pb = 0; pph ^= 1; }
-      }
-      if (!ok) break;
-
-      if (a.ksplit > 1) {
-        // Split-K (the CTA's only unit): publish this split's partial tile,
-        // then the cluster barrier -- every split's tile is in the workspace.
-        split_publish<BT, NW, kCols>(a, tile, split, acc, row, col0);
-        __syncwarp();
-        ptx::cluster_sync();
-        split_synced = true;
-        break;
-      }
-      if constexpr (kSK) {
-        if (un.kind == kUnitHead) {
-          sk_publish<BT, NW, kCols>(a, acc, row, col0, &sk_bars[0], abort_flag);
-          continue;
-        }
-        if (un.kind == kUnitTail && !sk_absorb<BT, NW, kCols>(a, acc, row, col0, ring, &sk_bars[1], abort_flag)) {
-          ok = false;
-          break;
-        }
-      }
-      if constexpr (CV) {
-        // TMEM lane = token, columns = channels: this thread holds token
-        // (col0 / 128) * 128 + row of the tile, channels col0 % 128 .. + kCols
-        const int p = mtile * BT + (col0 / 128) * 128 + row;
-        if (p < a.M) {
-          const int img = a.cv_hp * a.cv_wp;
-          const int b = p / img, r = p - b * img;
-          const int py = r / a.cv_wp, px = r - py * a.cv_wp;
-          if (py < a.cv_oh && px < a.cv_ow) {
-            const size_t plane = (size_t)a.cv_oh * a.cv_ow;
-            const int nb = ntile * 128 + (col0 & 127);
-            float* o = reinterpret_cast<float*>(a.y) + ((size_t)b * a.N + nb) * plane + (size_t)py * a.cv_ow + px;
-            const int act = a.act;
-#pragma unroll
-            for (int j = 0; j < kCols; ++j) {
-              if (nb + j < a.N) {
-                const float bj = a.bias[0] ? __ldg(a.bias[0] + nb + j) : 0.0f;
-                o[(size_t)j * plane] = apply_act(acc[0][j] + bj, act);
+              for (int j = 0; j < 16; ++j) {
+                const int m = m0w + c * 16 + j;
+                if (m < a.M) {
+                  float v = apply_act(__uint_as_float(r0[j]) + bw, act);
+                  if (a.aux) v *= __ldg(a.aux + (size_t)m * a.N + nw_);
+                  store_y(a, m, nw_, v);
+                }
               }
             }
           }
         }
-        continue;
-      }
-      if constexpr (QK) {
-        const bool is_q = ntile < a.qk_q;
-        if (is_q || ntile < a.qk_q + a.qk_k) {
-          // a q or k head: bias, QK-norm + RoPE (every lane takes part), store
-          const float b0 = (a.bias[0] && n < a.N) ? __ldg(a.bias[0] + n) : 0.0f;
-#pragma unroll
-          for (int j = 0; j < kCols; ++j) acc[0][j] += b0;
-          if (!qk_epilogue<BT, kCols>(a, acc[0], row, mtile, col0, is_q, qk_scratch, qk_bars, qk_uses,
-                                      abort_flag)) {
+        ptx::tc_fence_before();
+        __syncwarp();
+        if (lane == 0) ptx::mbar_arrive(&part_empty[pb]);
+        if (++pb == kNP) { pb = 0; pph ^= 1; }
+      } else {
+        const int n = ntile * 128 + row;
+        const int m0 = mtile * BT + col0;
+        float acc[NW][kCols];
+  #pragma unroll
+        for (int w = 0; w < NW; ++w)
+  #pragma unroll
+          for (int j = 0; j < kCols; ++j) acc[w][j] = 0.0f;
+        for (int kc = kc0; kc < kc1; ++kc) {
+          if (!ws_seg_last(kc, kc1, cpb)) continue;
+          float sc[NW];
+  #pragma unroll
+          for (int w = 0; w < NW; ++w)
+            sc[w] = a.exact ? __ldg(a.s[w] + ((size_t)ntile * a.nkb + (kc * kChunkK) / a.block) * 128 + row) : 1.0f;
+          // lockstep: segment == stage pb (partial pb), retired when empty[pb] completes
+          if (!ptx::mbar_wait(a.lockstep ? &empty[pb] : &part_full[pb], pph, abort_flag)) { ok = false; break; }
+          ptx::tc_fence_after();
+          const uint32_t t_row = tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)pb * kPartCols + col0;
+  #pragma unroll
+          for (int w = 0; w < NW; ++w) {
+  #pragma unroll
+            for (int c = 0; c < kCols / 16; ++c) {
+              uint32_t r0[16];
+              ptx::tmem_ld_32x32b_x16(t_row + w * BT + c * 16, r0);
+              ptx::tmem_ld_wait();
+  #pragma unroll
+              for (int j = 0; j < 16; ++j) acc[w][c * 16 + j] = fmaf(sc[w], __uint_as_float(r0[j]), acc[w][c * 16 + j]);
+            }
+          }
+          ptx::tc_fence_before();
+          __syncwarp();
+          if (lane == 0) ptx::mbar_arrive(a.lockstep ? &full[pb] : &part_empty[pb]);
+          if (++pb == (a.lockstep ? S : kNP)) { pb = 0; pph ^= 1; }
+        }
+        if (!ok) break;
+
+        if (a.ksplit > 1) {
+          // Split-K (the CTA's only unit): publish this split's partial tile,
+          // then the cluster barrier -- every split's tile is in the workspace.
+          split_publish<BT, NW, kCols>(a, tile, split, acc, row, col0);
+          __syncwarp();
+          ptx::cluster_sync();
+          split_synced = true;
+          break;
+        }
+        if constexpr (kSK) {
+          if (un.kind == kUnitHead) {
+            sk_publish<BT, NW, kCols>(a, acc, row, col0, &sk_bars[0], abort_flag);
+            continue;
+          }
+          if (un.kind == kUnitTail && !sk_absorb<BT, NW, kCols>(a, acc, row, col0, ring, &sk_bars[1], abort_flag)) {
             ok = false;
             break;
           }
-          if (n < a.N) {
-#pragma unroll
-            for (int j = 0; j < kCols; ++j)
-              if (m0 + j < a.M) store_y(a, m0 + j, n, acc[0][j]);
+        }
+        if constexpr (CV) {
+          // TMEM lane = token, columns = channels: this thread holds token
+          // (col0 / 128) * 128 + row of the tile, channels col0 % 128 .. + kCols
+          const int p = mtile * BT + (col0 / 128) * 128 + row;
+          if (p < a.M) {
+            const int img = a.cv_hp * a.cv_wp;
+            const int b = p / img, r = p - b * img;
+            const int py = r / a.cv_wp, px = r - py * a.cv_wp;
+            if (py < a.cv_oh && px < a.cv_ow) {
+              const size_t plane = (size_t)a.cv_oh * a.cv_ow;
+              const int nb = ntile * 128 + (col0 & 127);
+              float* o = reinterpret_cast<float*>(a.y) + ((size_t)b * a.N + nb) * plane + (size_t)py * a.cv_ow + px;
+              const int act = a.act;
+  #pragma unroll
+              for (int j = 0; j < kCols; ++j) {
+                if (nb + j < a.N) {
+                  const float bj = a.bias[0] ? __ldg(a.bias[0] + nb + j) : 0.0f;
+                  o[(size_t)j * plane] = apply_act(acc[0][j] + bj, act);
+                }
+              }
+            }
           }
           continue;
         }
-      }
-      if (n < a.N) {
-        const float b0 = a.bias[0] ? __ldg(a.bias[0] + n) : 0.0f;
-        const float b1 = (NW == 2 && a.bias[1]) ? __ldg(a.bias[1] + n) : 0.0f;
-        const int act = a.act;
-#pragma unroll
-        for (int j = 0; j < kCols; ++j) {
-          const int m = m0 + j;
-          if (m < a.M) {
-            float v;
-            if (NW == 2) {
-              v = silu(acc[0][j] + b0) * (acc[NW - 1][j] + b1);
-            } else {
-              v = apply_act(acc[0][j] + b0, act);
-              if (a.aux) v *= __ldg(a.aux + (size_t)m * a.N + n);
+        if constexpr (QK) {
+          const bool is_q = ntile < a.qk_q;
+          if (is_q || ntile < a.qk_q + a.qk_k) {
+            // a q or k head: bias, QK-norm + RoPE (every lane takes part), store
+            const float b0 = (a.bias[0] && n < a.N) ? __ldg(a.bias[0] + n) : 0.0f;
+  #pragma unroll
+            for (int j = 0; j < kCols; ++j) acc[0][j] += b0;
+            if (!qk_epilogue<BT, kCols>(a, acc[0], row, mtile, col0, is_q, qk_scratch, qk_bars, qk_uses,
+                                        abort_flag)) {
+              ok = false;
+              break;
             }
-            store_out<SC>(a, m, n, v);
+            if (n < a.N) {
+  #pragma unroll
+              for (int j = 0; j < kCols; ++j)
+                if (m0 + j < a.M) store_y(a, m0 + j, n, acc[0][j]);
+            }
+            continue;
+          }
+        }
+        if (n < a.N) {
+          const float b0 = a.bias[0] ? __ldg(a.bias[0] + n) : 0.0f;
+          const float b1 = (NW == 2 && a.bias[1]) ? __ldg(a.bias[1] + n) : 0.0f;
+          const int act = a.act;
+  #pragma unroll
+          for (int j = 0; j < kCols; ++j) {
+            const int m = m0 + j;
+            if (m < a.M) {
+              float v;
+              if (NW == 2) {
+                v = silu(acc[0][j] + b0) * (acc[NW - 1][j] + b1);
+              } else {
+                v = apply_act(acc[0][j] + b0, act);
+                if (a.aux) v *= __ldg(a.aux + (size_t)m * a.N + n);
+              }
+              store_out<SC>(a, m, n, v);
+            }
           }
         }
       }
@@ -1486,6 +1532,29 @@ bq4_status plan_gemm(const bq4_weight* w, int nw, int64_t M, int device, GemmPla
       have = true;
     }
   }
+  // tf32 linear with at least a wave of 256 x 256 tiles: two N tiles per
+  // token tile (2/3 of the operand bytes per FLOP, which is what bounds the
+  // tf32 kernels).  Whole-K tiles, one TMEM buffer.  BQ4_NO_WIDE=1 keeps
+  // 128 x BT tiles.
+  if (have && p->tf && !cv && !qk && nw == 1 && w->ntiles >= 2 && !forced && !getenv("BQ4_NO_WIDE")) {
+    GemmPlan cand = base;
+    double cost = 0.0;
+    int sms = device_sm_count(device);
+    if (sm_budget() > 0 && sm_budget() < sms) sms = sm_budget();
+    const int pairs = (int)((w->ntiles + 1) / 2);
+    const int mt = (int)((M + 255) / 256);
+    if ((int64_t)mt * pairs >= sms && plan_for_bt(w, 2, M, device, 256, &cand, &cost, false, false, false) == BQ4_OK) {
+      cand.nw = 1;
+      cand.wide = 1;
+      cand.ntiles = pairs;
+      cand.ksplit = cand.cluster = 1;
+      cand.units = mt * pairs;
+      cand.grid = cand.units < sms ? cand.units : sms;
+      cand.partial_bytes = 0;
+      cand.workspace_bytes = cand.sk_bytes + cand.xh_bytes;
+      *p = cand;
+    }
+  }
   return have ? BQ4_OK : (last != BQ4_OK ? last : set_error(BQ4_EUNSUPPORTED, "no plan for this shape"));
 }
 
@@ -1615,7 +1684,11 @@ bq4_status run_gemm(const GemmPlan& plan, const bq4_weight* const* ws, const voi
     else e = launch_ws<128, 1, false, false, false, true, true>(plan, tmap, args, stream, &ok_regs);
   } else if (plan.tf) {
     if (args.sc_rows || plan.sk_tiles) return set_error(BQ4_EUNSUPPORTED, "tf32 plan shape");
-    if (plan.bt == 256) e = launch_ws<256, 1, false, false, false, false, true>(plan, tmap, args, stream, &ok_regs);
+    if (plan.wide) {
+      if (plan.bt != 256 || plan.ksplit != 1) return set_error(BQ4_EUNSUPPORTED, "wide tf32 plan shape");
+      args.h[1] = args.h[0];  // the same weight: N tiles 2t and 2t + 1
+      e = launch_ws<256, 2, false, false, false, false, true>(plan, tmap, args, stream, &ok_regs);
+    } else if (plan.bt == 256) e = launch_ws<256, 1, false, false, false, false, true>(plan, tmap, args, stream, &ok_regs);
     else if (plan.bt == 128) e = launch_ws<128, 1, false, false, false, false, true>(plan, tmap, args, stream, &ok_regs);
     else e = launch_ws<64, 1, false, false, false, false, true>(plan, tmap, args, stream, &ok_regs);
   } else if (args.sc_rows) {

@@ -42,6 +42,8 @@ struct bq4_weight {
   // swizzle (linear: a chunk is 16 K, Kp a multiple of 32), or
   // [ntiles][nkc][128][32] in 128-byte rows with the 128-byte swizzle
   // (convolution, conv_kh > 0: a chunk is 32 K, Kp a multiple of 64).
+  // The linear's tile array holds an even number of tiles (a zero tile after
+  // an odd last one), so that N tiles can be taken in pairs.
   // Convolution weights order K as (tap = ky * conv_kw + kx, channel):
   // K = taps * conv_cp, channels padded to conv_cp = a multiple of 32 with zeros.
   int32_t tf32;
@@ -114,6 +116,7 @@ struct GemmPlan {
   int qk;          // 1: QK-norm + RoPE epilogue (every 128-feature tile one head)
   int tf;          // 1: packed-F16 weight, kind::tf32 on f32 token rows (no staging pass)
   int cv;          // 1: implicit-GEMM convolution (tf32, NCHW epilogue)
+  int wide;        // 1: tf32 linear on 256 x 256 tiles (two N tiles per token tile); ntiles = pairs
   int stages, a_stages, raw_stages;  // B ring, A ring, raw ring depths
   uint32_t raw_s_bytes;  // scale bytes per weight per raw stage (folded)
   uint32_t raw_w_bytes;  // shared-memory bytes per weight per raw stage

@@ -217,7 +217,11 @@ class DiTQ4Stack:
     GELU-tanh) and down (row-parallel, mlp -> hidden, bias), then the
     activations are renormalised (RMS over the hidden axis).  Attention
     itself is outside the Q4 path; the o-projection reads the rank's value
-    columns of the qkv output as its input shard."""
+    columns of the qkv output as its input shard.  For P > 1 the fused qkv
+    weight's columns are ordered so that rank r's contiguous column shard is
+    [q_r | k_r | v_r] (each hidden / P wide, Megatron-style), hence v_r -- the
+    last hidden / P columns of the shard -- is the slice of v whose rows of
+    the o weight rank r holds: the sharded stack computes the unsharded one."""
 
     def __init__(self, blocks: int, hidden: int, qkv: int, mlp: int, device: torch.device, seed: int = 0,
                  block: int = 128, group=None, act_dtype: torch.dtype = torch.float32, chunks: int = 1,
@@ -249,6 +253,9 @@ class DiTQ4Stack:
             mk = lambda K, N: _random_packed(K, N, block, g, device)  # noqa: E731
             bias = lambda N: torch.randn(N, generator=g, device=device) * 0.02  # noqa: E731
             wq, sq = mk(hidden, qkv)
+            if self.size > 1:
+                perm = _qkv_rank_order(hidden, qkv, self.size, device)
+                wq, sq = wq[:, perm].contiguous(), sq[:, perm].contiguous()
             wo, so = mk(hidden, hidden)
             wu, su = mk(hidden, mlp)
             wd, sd = mk(mlp, hidden)
@@ -410,6 +417,18 @@ def _timed(cb, name, fn):
     r = fn()
     cb(name, False)
     return r
+
+
+def _qkv_rank_order(hidden: int, qkv: int, P: int, device: torch.device) -> torch.Tensor:
+    """Column order of a fused [q | k | v] weight (each section `hidden` wide)
+    whose r-th contiguous N shard is [q_r | k_r | v_r]."""
+    if qkv != 3 * hidden or hidden % P:
+        raise ValueError(f"qkv={qkv} must be 3 x hidden={hidden} with hidden divisible by {P} ranks")
+    part = hidden // P
+    r = torch.arange(P, device=device).view(P, 1, 1)
+    sec = torch.arange(3, device=device).view(1, 3, 1)
+    j = torch.arange(part, device=device).view(1, 1, part)
+    return (sec * hidden + r * part + j).reshape(-1)
 
 
 def _random_packed(K: int, N: int, block: int, g: torch.Generator, device: torch.device):

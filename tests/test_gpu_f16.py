@@ -141,6 +141,30 @@ def test_prepared_weight_linear_with_epilogue():
     _check_matmul(x2, w2, y2)
 
 
+def test_wide_tiles(monkeypatch):
+    # 256 x 256 tiles (two N tiles per token tile) once they fill a wave; an odd
+    # N-tile count (1100 = 8.6 tiles) pairs the last tile with a zero one
+    M, K, N = 9000, 384, 1100
+    g = torch.Generator(device=DEV).manual_seed(21)
+    x = torch.randn((M, K), generator=g, device=DEV)
+    w = (torch.randn((K, N), generator=g, device=DEV) * K ** -0.5).half()
+    bias = torch.randn(N, generator=g, device=DEV)
+    pw = F.PreparedF16Weight(w)
+    plan = pw.plan_info(M)
+    assert plan["wide"] == 1 and plan["bt"] == 256 and plan["ksplit"] == 1
+    y = pw.linear(x, bias, L.ACT_SILU)
+    torch.cuda.synchronize()
+    q4.poll_device_error()
+    W = O.f16_widen_bits(_bits(w)).view(np.float32).reshape(K, N)
+    ref = O.linear_f64(x.cpu().numpy(), W, bias.cpu().numpy(), O.ACT_SILU)
+    assert O.rel_frobenius(y.cpu().numpy(), ref) <= 5e-3
+    # the same K order per output either way: bit-identical to 128-row tiles
+    monkeypatch.setenv("BQ4_NO_WIDE", "1")
+    assert pw.plan_info(M)["wide"] == 0
+    assert torch.equal(y, pw.linear(x, bias, L.ACT_SILU))
+    _check_matmul(x[:500], w, pw.linear(x[:500]))
+
+
 def test_rhs_matmul_throughput_smoke_value():
     # packed_f16.rs :876-943 at its size: ones [4096, 4096] x f16(1/4096) -> 1 within 1e-3
     n = 4096

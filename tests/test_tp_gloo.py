@@ -86,3 +86,24 @@ def test_shard_bounds_rules():
         tp.row_shard_bounds(3360, 32, 0, 4)  # 840 is not a multiple of 32: real Boogu widths cannot split 4-way
     with pytest.raises(ValueError):
         tp.column_shard_bounds(3072, 0, 5)
+
+
+@pytest.mark.parametrize("P", [1, 2, 4, 8])
+def test_stack_qkv_order_gives_each_rank_its_value_slice(P):
+    # the DiT stack's o-projection reads the last hidden/P columns of a rank's
+    # contiguous qkv shard as its v slice; with the rank order of the fused
+    # weight's columns the sharded block equals the unsharded one
+    from burn_image_b200.tp import _qkv_rank_order
+    rng = np.random.default_rng(P)
+    H, M = 16, 5
+    x = rng.standard_normal((M, H))
+    wqkv = rng.standard_normal((H, 3 * H))
+    wo = rng.standard_normal((H, H))
+    ref = (x @ wqkv)[:, 2 * H:] @ wo  # o(v)
+    perm = _qkv_rank_order(H, 3 * H, P, torch.device("cpu")).numpy()
+    assert sorted(perm.tolist()) == list(range(3 * H))
+    wp = wqkv[:, perm]
+    shard, part = 3 * H // P, H // P
+    total = sum((x @ wp[:, r * shard:(r + 1) * shard])[:, shard - part:] @ wo[r * part:(r + 1) * part]
+                for r in range(P))
+    assert np.allclose(total, ref)
