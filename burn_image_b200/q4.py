@@ -610,7 +610,7 @@ def feed_forward_swiglu(l1: Q4Linear, l3: Q4Linear, l2: Q4Linear, x: torch.Tenso
 
 def set_numerics(mode: int) -> None:
     """Operand staging for subsequent calls: NUMERICS_AUTO (exact weights up
-    to M = 256 rows, the reference's f16 staging above), NUMERICS_EXACT or
+    to M = 64 rows, the reference's f16 staging above), NUMERICS_EXACT or
     NUMERICS_FOLDED (see include/bq4.h)."""
     check(L.lib().bq4_set_numerics(mode))
 

@@ -80,7 +80,7 @@ typedef struct bq4_weight bq4_weight; /* opaque prepared weight (device resident
  *   FOLDED -- weights staged as f16(q * f16(scale)), the staging of the
  *             reference GPU kernel (patches/burn-cubecl-0.21.0/src/kernel/
  *             matmul/quantized.rs:172-178); faster at large M.
- *   AUTO   -- EXACT for M <= 256 rows, FOLDED above (default).
+ *   AUTO   -- EXACT for M <= 64 rows, FOLDED above (default).
  * Both are f32-accumulated; both meet the 5e-3 relative-Frobenius bound.
  * The initial value comes from the environment variable BQ4_NUMERICS
  * (auto|exact|folded), else AUTO.

@@ -56,11 +56,12 @@ def scales_kn(scales, K, N, block, layout):
     return np.repeat(np.ascontiguousarray(s), block, axis=0)[:K]
 
 
-def staged_weight(words, scales, K, N, block, layout):
-    """Emulation of the kernel's weight staging: blocks of 64/128 keep
-    q * scale exact (the scale multiplies the f32 accumulator); smaller
-    blocks stage f16(q * f16(scale))."""
-    if block >= 64:
+def staged_weight(words, scales, K, N, block, layout, exact=None):
+    """Emulation of the kernel's weight staging: exact plans (blocks of
+    64/128) keep q * scale exact (the scale multiplies the f32 accumulator);
+    folded plans stage f16(q * f16(scale)).  exact=None: exact for every
+    block of 64/128 (the EXACT numerics mode)."""
+    if exact if exact is not None else block >= 64:
         return O.unpack(words, scales, K, N, block, layout)
     q = decode_q(words, K, N, layout).astype(np.float16)
     s = scales_kn(scales, K, N, block, layout).astype(np.float16)
@@ -199,7 +200,7 @@ def test_linear_parity(M, K, N, block, layout, act, with_bias, with_aux, rng):
     assert np.all(np.isfinite(y))
     assert report(f"M{M}K{K}N{N}b{block}", y, ref) <= TOL
     # tight check: the same staging emulated on the CPU (f16 x, f16 weights)
-    Ws = staged_weight(w, s, K, N, block, layout)
+    Ws = staged_weight(w, s, K, N, block, layout, exact=pw.plan_info(M)["exact"] == 1)
     xs = x.astype(np.float16).astype(np.float32)
     ref_s = O.linear_f64(xs, Ws, bias, act, aux)
     tight = 2e-3 if act != O.ACT_NONE else 1e-5  # GELU/SiLU use approximate tanh/exp
