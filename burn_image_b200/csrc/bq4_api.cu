@@ -299,9 +299,10 @@ bq4_status bq4_linear_plan_info(const bq4_weight* w, int64_t M, int32_t gated, i
   GemmPlan plan;
   st = plan_gemm(w, gated ? 2 : 1, M, w->device, &plan);
   if (st) return st;
-  const int32_t v[10] = {plan.bt, plan.ksplit, plan.grid, plan.exact, plan.ta, plan.stages, plan.sk_tiles,
-                         plan.dp_tiles, (int32_t)(plan.workspace_bytes / 256), plan.wide};
-  for (int32_t i = 0; i < n && i < 10; ++i) info[i] = v[i];
+  const int32_t v[12] = {plan.bt, plan.ksplit, plan.grid, plan.exact, plan.ta, plan.stages, plan.sk_tiles,
+                         plan.dp_tiles, (int32_t)(plan.workspace_bytes / 256), plan.wide, plan.tail_tiles,
+                         plan.tail_split};
+  for (int32_t i = 0; i < n && i < 12; ++i) info[i] = v[i];
   return BQ4_OK;
 }
 

@@ -167,6 +167,7 @@ struct WsArgs {
   int M, N;
   int nkc, nkb, block;
   int ntiles, mtiles, ksplit, units;
+  int tile0;               // first tile of this launch (the split-K tail launch starts past the whole tiles)
   int nfast;               // 1: N tile varies fastest along the unit order
   int yvec;                // 1: y rows 16-byte aligned (float4 stores in the split epilogue)
   int stages, rs;          // operand ring and raw ring depths
@@ -257,6 +258,7 @@ __device__ __forceinline__ void ws_unit(const WsArgs& a, int u, int& tile, int& 
 // planner makes the operand that is larger in HBM (f16 tokens vs Q4 weights)
 // the one a wave shares, so it is read from DRAM about once.
 __device__ __forceinline__ void ws_tile(const WsArgs& a, int tile, int& mtile, int& ntile) {
+  tile += a.tile0;
   if (a.nfast) {
     mtile = tile / a.ntiles;
     ntile = tile - mtile * a.ntiles;
@@ -1462,6 +1464,34 @@ static bq4_status plan_for_bt(const bq4_weight* w, int nw, int64_t M, int device
       *cost = best_t + 2.0;
     }
   }
+  // Split-K tail launch: when whole tiles leave the last wave partial (rem
+  // tiles), the full waves run as one launch and the rem tiles as a second
+  // one in which each tile is cut into s K ranges, a cluster of s CTAs
+  // reducing through the workspace (the split-K path).  The last wave then
+  // takes about 1/s of a tile plus the reduction and a launch instead of a
+  // whole tile.  Not with stream-K or the QK / conv epilogues (whole-K
+  // tiles), nor when the caller plans without workspace extras (allow_sk =
+  // false).  Opt-in (BQ4_SPLIT_TAIL=1): measured on B200 it does not pay --
+  // c1 (152 tiles, 4 in the tail, 8 splits) 50.9 vs 52.5 us, and the DiT
+  // stack (qkv and up with tails) 1224 vs 1242 TFLOP/s: the cluster
+  // reduction and the second launch cost about what the short wave saves.
+  p->tail_tiles = p->tail_split = 0;
+  if (best_s == 1 && allow_sk && p->sk_tiles == 0 && !qk && !cv && tiles > sms && tiles % sms != 0 &&
+      getenv("BQ4_SPLIT_TAIL") && !getenv("BQ4_NO_TAIL")) {
+    const int rem = tiles % sms;
+    int s = sms / rem;
+    if (s > kMaxSplit) s = kMaxSplit;
+    if (s > nks) s = nks;
+    const double t_tile = nks * t_stage + 1.0;
+    const double t_tail = (double)((nks + s - 1) / s) * t_stage + 1.0 + t_red + 2.0;
+    if (s >= 2 && t_tail < t_tile && rem <= cluster_capacity(p->bt, nw, s, p->smem_bytes, device)) {
+      p->tail_tiles = rem;
+      p->tail_split = s;
+      p->units = tiles - rem;
+      p->grid = sms;
+      *cost = best_t - t_tile + t_tail + 2.0;
+    }
+  }
   // Unit order: the wave shares the operand that is larger in HBM -- the
   // f16 token rows (M*K*2 bytes) or the Q4 weights (nw*N*K/2 bytes).
   p->nfast = ((int64_t)M * 4 > (int64_t)nw * w->Np) ? 1 : 0;
@@ -1476,6 +1506,8 @@ static bq4_status plan_for_bt(const bq4_weight* w, int nw, int64_t M, int device
   // two parts).
   p->partial_bytes =
       best_s > 1 ? align_up((size_t)tiles * best_s * nw * p->bt * 128 * sizeof(float), 256) : 0;
+  if (p->tail_tiles)
+    p->partial_bytes = align_up((size_t)p->tail_tiles * p->tail_split * nw * p->bt * 128 * sizeof(float), 256);
   // tf32 plans read the caller's f32 rows in place (their entry points stage
   // the rows themselves when they must)
   p->xh_bytes = p->tf ? 0 : align_up((size_t)M * (size_t)w->Kp * 2, 256);
@@ -1677,47 +1709,67 @@ bq4_status run_gemm(const GemmPlan& plan, const bq4_weight* const* ws, const voi
   args.raw_s_bytes = plan.raw_s_bytes;
   args.raw_w_bytes = plan.raw_w_bytes;
 
-  bool ok_regs = true;
-  if (plan.cv) {
-    if (plan.ksplit != 1 || plan.sk_tiles || plan.bt < 128) return set_error(BQ4_EUNSUPPORTED, "conv plan shape");
-    if (plan.bt == 256) e = launch_ws<256, 1, false, false, false, true, true>(plan, tmap, args, stream, &ok_regs);
-    else e = launch_ws<128, 1, false, false, false, true, true>(plan, tmap, args, stream, &ok_regs);
-  } else if (plan.tf) {
-    if (args.sc_rows || plan.sk_tiles) return set_error(BQ4_EUNSUPPORTED, "tf32 plan shape");
-    if (plan.wide) {
-      if (plan.bt != 256 || plan.ksplit != 1) return set_error(BQ4_EUNSUPPORTED, "wide tf32 plan shape");
-      args.h[1] = args.h[0];  // the same weight: N tiles 2t and 2t + 1
-      e = launch_ws<256, 2, false, false, false, false, true>(plan, tmap, args, stream, &ok_regs);
-    } else if (plan.bt == 256) e = launch_ws<256, 1, false, false, false, false, true>(plan, tmap, args, stream, &ok_regs);
-    else if (plan.bt == 128) e = launch_ws<128, 1, false, false, false, false, true>(plan, tmap, args, stream, &ok_regs);
-    else e = launch_ws<64, 1, false, false, false, false, true>(plan, tmap, args, stream, &ok_regs);
-  } else if (args.sc_rows) {
-    if (plan.nw != 1 || plan.qk) return set_error(BQ4_EUNSUPPORTED, "row scatter: one weight, plain epilogue");
-    if (plan.ta && plan.bt != 256) return set_error(BQ4_EUNSUPPORTED, "row scatter with 128-token TMEM operands");
-    if (plan.ta) e = launch_ws<256, 1, true, false, true>(plan, tmap, args, stream, &ok_regs);
-    else if (plan.bt == 256) e = launch_ws<256, 1, false, false, true>(plan, tmap, args, stream, &ok_regs);
-    else if (plan.bt == 128) e = launch_ws<128, 1, false, false, true>(plan, tmap, args, stream, &ok_regs);
-    else e = launch_ws<64, 1, false, false, true>(plan, tmap, args, stream, &ok_regs);
-  } else if (plan.qk) {
-    if (plan.nw != 1 || plan.ksplit != 1 || plan.bt < 128) return set_error(BQ4_EUNSUPPORTED, "QK-norm plan shape");
-    if (plan.ta) e = launch_ws<256, 1, true, true>(plan, tmap, args, stream, &ok_regs);
-    else if (plan.bt == 256) e = launch_ws<256, 1, false, true>(plan, tmap, args, stream, &ok_regs);
-    else e = launch_ws<128, 1, false, true>(plan, tmap, args, stream, &ok_regs);
-  } else if (plan.nw == 1) {
-    if (plan.ta && plan.bt == 256) e = launch_ws<256, 1, true>(plan, tmap, args, stream, &ok_regs);
-    else if (plan.ta) e = launch_ws<128, 1, true>(plan, tmap, args, stream, &ok_regs);
-    else if (plan.bt == 256) e = launch_ws<256, 1>(plan, tmap, args, stream, &ok_regs);
-    else if (plan.bt == 128) e = launch_ws<128, 1>(plan, tmap, args, stream, &ok_regs);
-    else e = launch_ws<64, 1>(plan, tmap, args, stream, &ok_regs);
-  } else {
-    if (plan.bt == 128) e = launch_ws<128, 2>(plan, tmap, args, stream, &ok_regs);
-    else e = launch_ws<64, 2>(plan, tmap, args, stream, &ok_regs);
-  }
-  if (e != cudaSuccess) return check_cuda(e, "q4 gemm launch");
-  if (!ok_regs)
-    return set_error(BQ4_EUNSUPPORTED, "q4 gemm kernel was not built with %d registers per thread",
-                     kWsRegsLaunch);
-  return BQ4_OK;
+  // One launch of the planned kernel variant, plan `pl`, arguments `ar`.
+  auto dispatch = [&](const GemmPlan& pl, WsArgs& ar) -> bq4_status {
+    bool ok_regs = true;
+    cudaError_t e = cudaSuccess;
+    if (pl.cv) {
+      if (pl.ksplit != 1 || pl.sk_tiles || pl.bt < 128) return set_error(BQ4_EUNSUPPORTED, "conv plan shape");
+      if (pl.bt == 256) e = launch_ws<256, 1, false, false, false, true, true>(pl, tmap, ar, stream, &ok_regs);
+      else e = launch_ws<128, 1, false, false, false, true, true>(pl, tmap, ar, stream, &ok_regs);
+    } else if (pl.tf) {
+      if (ar.sc_rows || pl.sk_tiles) return set_error(BQ4_EUNSUPPORTED, "tf32 plan shape");
+      if (pl.wide) {
+        if (pl.bt != 256 || pl.ksplit != 1) return set_error(BQ4_EUNSUPPORTED, "wide tf32 plan shape");
+        ar.h[1] = ar.h[0];  // the same weight: N tiles 2t and 2t + 1
+        e = launch_ws<256, 2, false, false, false, false, true>(pl, tmap, ar, stream, &ok_regs);
+      } else if (pl.bt == 256) e = launch_ws<256, 1, false, false, false, false, true>(pl, tmap, ar, stream, &ok_regs);
+      else if (pl.bt == 128) e = launch_ws<128, 1, false, false, false, false, true>(pl, tmap, ar, stream, &ok_regs);
+      else e = launch_ws<64, 1, false, false, false, false, true>(pl, tmap, ar, stream, &ok_regs);
+    } else if (ar.sc_rows) {
+      if (pl.nw != 1 || pl.qk) return set_error(BQ4_EUNSUPPORTED, "row scatter: one weight, plain epilogue");
+      if (pl.ta && pl.bt != 256) return set_error(BQ4_EUNSUPPORTED, "row scatter with 128-token TMEM operands");
+      if (pl.ta) e = launch_ws<256, 1, true, false, true>(pl, tmap, ar, stream, &ok_regs);
+      else if (pl.bt == 256) e = launch_ws<256, 1, false, false, true>(pl, tmap, ar, stream, &ok_regs);
+      else if (pl.bt == 128) e = launch_ws<128, 1, false, false, true>(pl, tmap, ar, stream, &ok_regs);
+      else e = launch_ws<64, 1, false, false, true>(pl, tmap, ar, stream, &ok_regs);
+    } else if (pl.qk) {
+      if (pl.nw != 1 || pl.ksplit != 1 || pl.bt < 128) return set_error(BQ4_EUNSUPPORTED, "QK-norm plan shape");
+      if (pl.ta) e = launch_ws<256, 1, true, true>(pl, tmap, ar, stream, &ok_regs);
+      else if (pl.bt == 256) e = launch_ws<256, 1, false, true>(pl, tmap, ar, stream, &ok_regs);
+      else e = launch_ws<128, 1, false, true>(pl, tmap, ar, stream, &ok_regs);
+    } else if (pl.nw == 1) {
+      if (pl.ta && pl.bt == 256) e = launch_ws<256, 1, true>(pl, tmap, ar, stream, &ok_regs);
+      else if (pl.ta) e = launch_ws<128, 1, true>(pl, tmap, ar, stream, &ok_regs);
+      else if (pl.bt == 256) e = launch_ws<256, 1>(pl, tmap, ar, stream, &ok_regs);
+      else if (pl.bt == 128) e = launch_ws<128, 1>(pl, tmap, ar, stream, &ok_regs);
+      else e = launch_ws<64, 1>(pl, tmap, ar, stream, &ok_regs);
+    } else {
+      if (pl.bt == 128) e = launch_ws<128, 2>(pl, tmap, ar, stream, &ok_regs);
+      else e = launch_ws<64, 2>(pl, tmap, ar, stream, &ok_regs);
+    }
+    if (e != cudaSuccess) return check_cuda(e, "q4 gemm launch");
+    if (!ok_regs)
+      return set_error(BQ4_EUNSUPPORTED, "q4 gemm kernel was not built with %d registers per thread",
+                       kWsRegsLaunch);
+    return BQ4_OK;
+  };
+  // Whole tiles, then (split-K tail plans) the tail tiles as clusters of
+  // tail_split CTAs; row-scatter calls keep whole tiles throughout.
+  const bool tail = plan.tail_tiles > 0 && !io.sc_rows;
+  GemmPlan whole = plan;
+  if (plan.tail_tiles && !tail) whole.units += plan.tail_tiles;
+  args.units = whole.units;
+  bq4_status st = dispatch(whole, args);
+  if (st != BQ4_OK || !tail) return st;
+  GemmPlan tp = plan;
+  tp.ksplit = tp.cluster = plan.tail_split;
+  tp.units = tp.grid = plan.tail_tiles * plan.tail_split;
+  WsArgs at = args;
+  at.tile0 = plan.units;
+  at.ksplit = tp.ksplit;
+  at.units = tp.units;
+  return dispatch(tp, at);
 }
 
 int* device_error_word() {

@@ -117,6 +117,10 @@ struct GemmPlan {
   int tf;          // 1: packed-F16 weight, kind::tf32 on f32 token rows (no staging pass)
   int cv;          // 1: implicit-GEMM convolution (tf32, NCHW epilogue)
   int wide;        // 1: tf32 linear on 256 x 256 tiles (two N tiles per token tile); ntiles = pairs
+  // split-K tail launch: units/grid describe the whole tiles [0, units);
+  // tiles [units, units + tail_tiles) follow in a second launch, each cut
+  // into tail_split K ranges (clusters of tail_split CTAs)
+  int tail_tiles, tail_split;
   int stages, a_stages, raw_stages;  // B ring, A ring, raw ring depths
   uint32_t raw_s_bytes;  // scale bytes per weight per raw stage (folded)
   uint32_t raw_w_bytes;  // shared-memory bytes per weight per raw stage

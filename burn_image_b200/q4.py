@@ -260,7 +260,8 @@ class PreparedQ4Weight:
         check(L.lib().bq4_linear_workspace_size(self._h, M, ctypes.byref(n)))
         return n.value
 
-    PLAN_FIELDS = ("bt", "ksplit", "grid", "exact", "ta", "stages", "sk_tiles", "dp_tiles", "workspace_256", "wide")
+    PLAN_FIELDS = ("bt", "ksplit", "grid", "exact", "ta", "stages", "sk_tiles", "dp_tiles", "workspace_256", "wide",
+                   "tail_tiles", "tail_split")
 
     def plan_info(self, M: int, gated: bool = False) -> dict:
         """The launch plan of bq4_linear (or of the gated pair) for M rows."""

@@ -128,12 +128,14 @@ BQ4_API bq4_status bq4_linear_workspace_size(const bq4_weight* w, int64_t M, siz
 
 /*
  * The launch plan bq4_linear uses for this weight and M (diagnostics and
- * tests).  Writes min(n, 10) values to info: token tile (64/128/256),
+ * tests).  Writes min(n, 12) values to info: token tile (64/128/256),
  * split-K factor (1 = none), grid size, exact numerics (0/1), weight tile in
  * TMEM (0/1), operand-ring stages, stream-K tiles (0 = whole tiles only),
- * whole tiles before them, workspace bytes / 256, and 1 when a packed-F16
- * weight runs on 256 x 256 tiles (two N tiles per token tile).  gated = 1
- * plans the SiLU-gated pair (bq4_linear_gated) with `w` as both weights.
+ * whole tiles before them, workspace bytes / 256, 1 when a packed-F16
+ * weight runs on 256 x 256 tiles (two N tiles per token tile), and the
+ * split-K tail: tiles of the partial last wave run in a second launch, each
+ * cut into the given number of K ranges (0, 0 = none).  gated = 1 plans the
+ * SiLU-gated pair (bq4_linear_gated) with `w` as both weights.
  */
 BQ4_API bq4_status bq4_linear_plan_info(const bq4_weight* w, int64_t M, int32_t gated, int32_t* info,
                                         int32_t n);
