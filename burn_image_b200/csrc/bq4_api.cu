@@ -780,6 +780,10 @@ bq4_status bq4_linear_gated(const bq4_weight* gate, const bq4_weight* up, const 
   if (st) return st;
   if (gate->K != up->K || gate->N != up->N || gate->block != up->block || gate->device != up->device)
     return set_error(BQ4_EINVAL_SHAPE, "gate and up weights differ in K/N/block/device");
+  // one kernel streams both weights: the same prepared form (pre-expanded
+  // N-packed tiles, or nibbles + scales), and packed-Q4 weights only
+  if ((gate->h != nullptr) != (up->h != nullptr) || gate->tf32 || up->tf32)
+    return set_error(BQ4_EINVAL_ARG, "gate and up must both be packed-Q4 weights of the same prepared form");
   st = check_compute_args(gate, x, M, ldx, y, workspace);
   if (st) return st;
   GemmPlan plan;
@@ -801,6 +805,9 @@ bq4_status bq4_dequant(const bq4_weight* w, float* out, bq4_layout out_layout, b
   if (!out) return set_error(BQ4_EINVAL_ARG, "out is NULL");
   if (out_layout != BQ4_LAYOUT_COL && out_layout != BQ4_LAYOUT_ROW)
     return set_error(BQ4_EINVAL_ARG, "out_layout %d", (int)out_layout);
+  if (w->tf32)
+    return set_error(BQ4_EUNSUPPORTED,
+                     "a packed-F16 weight holds no Q4 values; widen its source with bq4_packed_f16_to_f32");
   if (w->h)
     return set_error(BQ4_EUNSUPPORTED,
                      "weight was prepared from BQ4_LAYOUT_NPACKED (pre-expanded f16); use bq4_dequant_raw");

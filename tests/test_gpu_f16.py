@@ -247,3 +247,16 @@ def test_argument_checks():
     pw = F.PreparedF16Weight(_h(np.ones(64 * 128), (64, 128)))
     with pytest.raises(Bq4Error, match="EINVAL_ARG"):
         pw.linear_ex(torch.ones((4, 64), device=DEV).half())  # f16 activations: f32 only
+    with pytest.raises(Bq4Error, match="EINVAL_ARG"):
+        q4.linear_gated(pw, pw, torch.ones((4, 64), device=DEV))  # the gated pair takes packed-Q4 weights
+    # a gated pair must share one prepared form: N-packed (pre-expanded) with row layout is refused
+    K, N = 128, 128
+    words = torch.randint(-2 ** 31, 2 ** 31 - 1, (K // 8, N), device=DEV, dtype=torch.int64).to(torch.int32)
+    scales = torch.rand((K // 128, N), device=DEV) * 0.01 + 0.001
+    row = q4.PreparedQ4Weight(words, scales, K, N, 128, L.LAYOUT_ROW, DEV)
+    npk = q4.PreparedQ4Weight(torch.randint(-2 ** 31, 2 ** 31 - 1, (K, N // 8), device=DEV,
+                                            dtype=torch.int64).to(torch.int32).contiguous(),
+                              (torch.rand((K, N // 128), device=DEV) * 0.01 + 0.001).contiguous(),
+                              K, N, 128, L.LAYOUT_NPACKED, DEV)
+    with pytest.raises(Bq4Error, match="EINVAL_ARG"):
+        q4.linear_gated(row, npk, torch.ones((4, K), device=DEV))
