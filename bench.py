@@ -232,6 +232,9 @@ ROWS = [
     # next row: the DiT qkv projection with QK-norm + RoPE on its q and k heads (24 + 24 + 24
     # heads of 128), fused into the GEMM epilogue; "us_unfused" = linear + two norm passes
     ("f3_qkv_qknorm_rope_4352x3072x9216", 4352, 3072, 9216, "qknorm", 0),
+    # the attention that consumes it: 24 heads of 128 over 4352 tokens, f16 q/k/v
+    # (M = tokens, K = head_dim, N = heads)
+    ("f3_attention_24x4352x4352x128", 4352, 128, 24, "attn", 0),
     # next row: packed-F16 storage (the VAE's weights), kind::tf32.  The reference's own
     # throughput smokes (a 4096^3 matmul; a 512 -> 512 3x3 conv at 64 x 64) and the
     # largest FLUX-VAE decoder conv (128 -> 128 channels, 3x3, 1024 x 1024).
@@ -295,6 +298,9 @@ def config_rows(dev, peaks, names=None):
             continue
         if kind in ("f16mm", "f16conv"):
             out[name] = _f16_row(dev, kind, M, K, N, hbm, tfl)
+            continue
+        if kind == "attn":
+            out[name] = _attn_row(dev, M, K, N, hbm, tfl)
             continue
         nw = 2 if kind == "gated" else 1
         wbytes = nw * (N * K // 2 + N * K // QBLOCK * 4)
@@ -407,6 +413,41 @@ def _select_row(dev, n, cols, rows, hbm):
     del graph
     return {"us": t * 1e6, "tflops": 0.0, "gbs": nbytes / t / 1e9, "bound": "hbm", "t_star_us": t_star * 1e6,
             "frac": t_star / t, "sets": sets}
+
+
+def _attn_row(dev, S, D, H, hbm, tfl):
+    """Attention row: softmax(q k^T / sqrt(D)) v over H heads of S tokens,
+    f16 q/k/v, f32 out, graph-replayed on two input sets (each over 2x L2 with
+    its per-head score matrix).  Roofline: tf32 (half the measured bf16 burst)
+    for the 4 S^2 D H FLOPs, against the algorithmic bytes of a fused kernel
+    (q, k, v read once, out written once); the unfused kernels also move each
+    head's S x S f32 scores."""
+    import torch
+
+    from burn_image_b200 import f16 as F
+    from burn_image_b200 import q4
+    g = torch.Generator(device=dev).manual_seed(19)
+    items = []
+    for _ in range(2):
+        q = (torch.randn((1, H, S, D), generator=g, device=dev) * 0.5).half()
+        k = (torch.randn((1, H, S, D), generator=g, device=dev) * 0.5).half()
+        v = torch.randn((1, H, S, D), generator=g, device=dev).half()
+        items.append((q, k, v, torch.empty((1, H, S, D), device=dev)))
+
+    def call(it):
+        F.attention(it[0], it[1], it[2], out=it[3])
+
+    t = _graph_time(dev, items, call)
+    q4.poll_device_error()
+    flops = 4.0 * H * S * S * D
+    nbytes = 3 * H * S * D * 2 + H * S * D * 4
+    tf32 = tfl / 2.0
+    t_star = max(nbytes / (hbm * 1e9), flops / (tf32 * 1e12))
+    del items
+    torch.cuda.empty_cache()
+    return {"us": t * 1e6, "tflops": flops / t / 1e12, "gbs": nbytes / t / 1e9, "bound": "tensor",
+            "t_star_us": t_star * 1e6, "frac": t_star / t, "peak_tf32_tflops": tf32, "sets": 2,
+            "scores_bytes_per_head": S * S * 4}
 
 
 def _f16_row(dev, kind, M, K, N, hbm, tfl):

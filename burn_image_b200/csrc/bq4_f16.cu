@@ -17,6 +17,7 @@
 // mantissa bits, accumulated in f32.
 #include <cuda_runtime.h>
 
+#include <cmath>
 #include <cstring>
 #include <new>
 
@@ -238,6 +239,71 @@ __global__ void pad_rows_kernel(const float* __restrict__ x, int64_t M, int64_t 
     const int64_t m = i / Kp, k = i - m * Kp;
     out[i] = k < K ? x[m * ldx + k] : 0.0f;
   }
+}
+
+// ------------------------------------------------------------- attention
+// softmax(scale * q k^T) v per (batch, head), unfused: S = q k^T and O = P v
+// run as tf32 GEMMs (k and v read as packed-F16 weights through strided
+// views), with these two passes around them.
+
+// q rows of one head, f16 [S][D] at row pitch ldq -> f32 [S][D] (the GEMM's
+// in-place token rows).
+__global__ void attn_q_rows_kernel(const uint16_t* __restrict__ q, int64_t S, int D, int64_t ldq,
+                                   float* __restrict__ out) {
+  const int64_t total = S * D;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = i / D, c = i - r * D;
+    out[i] = widen_f16(q[r * ldq + c]);
+  }
+}
+
+// In place over rows of n scores (row pitch ld): e = exp(scale * s - max),
+// and inv[r] = 1 / sum(e) for the rows of P v to be scaled afterwards
+// (attn_scale_rows_kernel), so the probabilities are never normalised in
+// place.  One block of 256 threads per row: a max pass, then one expf per
+// score; f32 sums in a fixed order, deterministic.
+__global__ void attn_softmax_kernel(float* __restrict__ s, int64_t rows, int64_t n, int64_t ld, float scale,
+                                    float* __restrict__ inv) {
+  __shared__ float red[8];
+  __shared__ float bcast;
+  for (int64_t r = blockIdx.x; r < rows; r += gridDim.x) {
+    float* row = s + r * ld;
+    float m = -INFINITY;
+    for (int64_t j = threadIdx.x; j < n; j += blockDim.x) m = fmaxf(m, row[j] * scale);
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      float t = red[0];
+      for (int w = 1; w < (int)(blockDim.x >> 5); ++w) t = fmaxf(t, red[w]);
+      bcast = t;
+    }
+    __syncthreads();
+    m = bcast;
+    float sum = 0.0f;
+    for (int64_t j = threadIdx.x; j < n; j += blockDim.x) {
+      const float e = expf(row[j] * scale - m);
+      row[j] = e;
+      sum += e;
+    }
+    for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    __syncthreads();  // bcast was read by every thread
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = sum;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      float t = 0.0f;
+      for (int w = 0; w < (int)(blockDim.x >> 5); ++w) t += red[w];
+      inv[r] = 1.0f / t;
+    }
+    __syncthreads();  // red is rewritten by the next row
+  }
+}
+
+// out[r][d] *= inv[r] over rows of D values (the softmax normalisation of P v).
+__global__ void attn_scale_rows_kernel(float* __restrict__ out, int64_t rows, int D, const float* __restrict__ inv) {
+  const int64_t total = rows * D;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x)
+    out[i] *= inv[i / D];
 }
 
 }  // namespace
@@ -694,6 +760,134 @@ bq4_status bq4_packed_f16_conv2d(const float* input, int64_t batch, int64_t in_c
   if (e != cudaSuccess) return check_cuda(e, "packed-F16 conv weight preparation");
   const size_t wb = up256(w.h_bytes);
   return run_conv(input, batch, in_h, in_w, &w, bias, options, out, p + wb, workspace_bytes - wb, s);
+}
+
+}  // extern "C"
+
+// ---------------------------------------------------------------- attention
+
+namespace {
+
+struct AttnLayout {
+  size_t q32, s, kt, vt, gemm, inv, total;  // workspace parts (256-aligned offsets follow this order)
+  int64_t ldS;                          // score row pitch (multiple of 4: the PV GEMM reads rows in place)
+};
+
+bq4_status attn_layout(int64_t Sq, int64_t Skv, int64_t D, int dev, AttnLayout* L, GemmPlan* ps, GemmPlan* pv) {
+  if (Sq <= 0 || Skv <= 0 || D <= 0 || D % 4 || D > 1024 || Sq > (1 << 24) || Skv > (1 << 24))
+    return set_error(BQ4_EINVAL_SHAPE, "Sq=%lld Skv=%lld D=%lld (D %% 4 == 0, D <= 1024)", (long long)Sq,
+                     (long long)Skv, (long long)D);
+  L->ldS = round_up(Skv, 4);
+  bq4_weight wk, wv;
+  f16_view(D, Skv, &wk);
+  f16_view(Skv, D, &wv);
+  bq4_status st = plan_gemm(&wk, 1, Sq, dev, ps);
+  if (st) return st;
+  st = plan_gemm(&wv, 1, Sq, dev, pv);
+  if (st) return st;
+  L->q32 = up256((size_t)Sq * D * sizeof(float));
+  L->s = up256((size_t)Sq * L->ldS * sizeof(float));
+  L->kt = up256(wk.h_bytes);
+  L->vt = up256(wv.h_bytes);
+  L->gemm = up256(ps->workspace_bytes > pv->workspace_bytes ? ps->workspace_bytes : pv->workspace_bytes);
+  L->inv = up256((size_t)Sq * sizeof(float));
+  L->total = L->q32 + L->s + L->kt + L->vt + L->gemm + L->inv;
+  return BQ4_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+bq4_status bq4_attention_workspace_size(int64_t Sq, int64_t Skv, int64_t D, size_t* bytes) {
+  if (!bytes) return set_error(BQ4_EINVAL_ARG, "bytes is NULL");
+  int dev = 0;
+  cudaGetDevice(&dev);
+  AttnLayout L;
+  GemmPlan ps, pv;
+  bq4_status st = attn_layout(Sq, Skv, D, dev, &L, &ps, &pv);
+  if (st) return st;
+  *bytes = L.total;
+  return BQ4_OK;
+}
+
+bq4_status bq4_attention(const uint32_t* q, const uint32_t* k, const uint32_t* v, int64_t B, int64_t Hq, int64_t Hkv,
+                         int64_t Sq, int64_t Skv, int64_t D, float scale, float* out, void* workspace,
+                         size_t workspace_bytes, bq4_stream_t stream) {
+  if (!q || !k || !v || !out) return set_error(BQ4_EINVAL_ARG, "NULL pointer");
+  if (B <= 0 || Hq <= 0 || Hkv <= 0 || Hq % Hkv)
+    return set_error(BQ4_EINVAL_SHAPE, "B=%lld Hq=%lld Hkv=%lld (Hq %% Hkv == 0)", (long long)B, (long long)Hq,
+                     (long long)Hkv);
+  if (!al(out, 16)) return set_error(BQ4_EALIGN, "out must be 16-byte aligned");
+  int dev = 0;
+  cudaGetDevice(&dev);
+  bq4_status st = need_sm100(dev);
+  if (st) return st;
+  AttnLayout L;
+  GemmPlan ps, pv;
+  st = attn_layout(Sq, Skv, D, dev, &L, &ps, &pv);
+  if (st) return st;
+  if (!workspace || workspace_bytes < L.total)
+    return set_error(BQ4_EWORKSPACE, "workspace %zu < required %zu bytes", workspace_bytes, L.total);
+  if (!al(workspace, 256)) return set_error(BQ4_EALIGN, "workspace not 256-byte aligned");
+  const float sc = scale > 0.0f ? scale : 1.0f / std::sqrt((float)D);
+  const cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  uint8_t* p = static_cast<uint8_t*>(workspace);
+  float* q32 = reinterpret_cast<float*>(p);
+  float* S = reinterpret_cast<float*>(p + L.q32);
+  bq4_weight wk, wv;
+  f16_view(D, Skv, &wk);
+  f16_view(Skv, D, &wv);
+  wk.device = wv.device = dev;
+  wk.h = reinterpret_cast<uint16_t*>(p + L.q32 + L.s);
+  wv.h = reinterpret_cast<uint16_t*>(p + L.q32 + L.s + L.kt);
+  void* gws = p + L.q32 + L.s + L.kt + L.vt;
+  float* inv = reinterpret_cast<float*>(p + L.q32 + L.s + L.kt + L.vt + L.gemm);
+  const uint16_t* q16 = reinterpret_cast<const uint16_t*>(q);
+  const uint16_t* k16 = reinterpret_cast<const uint16_t*>(k);
+  const uint16_t* v16 = reinterpret_cast<const uint16_t*>(v);
+  const int64_t group = Hq / Hkv;
+  const bq4_weight* wl[1];
+  const float* nob[1] = {nullptr};
+  for (int64_t b = 0; b < B; ++b) {
+    for (int64_t hk = 0; hk < Hkv; ++hk) {
+      // k as the rhs [D][Skv] (element (d, j) at j * D + d), v as [Skv][D]
+      const uint16_t* kb = k16 + (b * Hkv + hk) * Skv * D;
+      const uint16_t* vb = v16 + (b * Hkv + hk) * Skv * D;
+      cudaError_t e = launch_prepare_f16(kb, &wk, 1, D, s);
+      if (e == cudaSuccess) e = launch_prepare_f16(vb, &wv, D, 1, s);
+      if (e != cudaSuccess) return check_cuda(e, "attention k/v preparation");
+      for (int64_t g = 0; g < group; ++g) {
+        const int64_t h = hk * group + g;
+        const uint16_t* qb = q16 + (b * Hq + h) * Sq * D;
+        attn_q_rows_kernel<<<grid_for(Sq * D, 256, dev), 256, 0, s>>>(qb, Sq, (int)D, D, q32);
+        note_launch();
+        e = cudaGetLastError();
+        if (e != cudaSuccess) return check_cuda(e, "attention q staging launch");
+        GemmIo io;
+        io.ldy = L.ldS;
+        wl[0] = &wk;
+        st = run_gemm(ps, wl, q32, Sq, D, nob, (int)BQ4_ACT_NONE, nullptr, S, gws, s, io);  // S = q k^T
+        if (st) return st;
+        const int grid = Sq < 148 * 16 ? (int)Sq : 148 * 16;
+        attn_softmax_kernel<<<grid, 256, 0, s>>>(S, Sq, Skv, L.ldS, sc, inv);
+        note_launch();
+        e = cudaGetLastError();
+        if (e != cudaSuccess) return check_cuda(e, "attention softmax launch");
+        GemmIo io2;
+        io2.ldy = D;
+        wl[0] = &wv;
+        float* ob = out + (b * Hq + h) * Sq * D;
+        st = run_gemm(pv, wl, S, Sq, L.ldS, nob, (int)BQ4_ACT_NONE, nullptr, ob, gws, s, io2);  // O = e v
+        if (st) return st;
+        attn_scale_rows_kernel<<<grid_for(Sq * D, 256, dev), 256, 0, s>>>(ob, Sq, (int)D, inv);  // / sum(e)
+        note_launch();
+        e = cudaGetLastError();
+        if (e != cudaSuccess) return check_cuda(e, "attention row scaling launch");
+      }
+    }
+  }
+  return BQ4_OK;
 }
 
 }  // extern "C"

@@ -1564,11 +1564,14 @@ bq4_status plan_gemm(const bq4_weight* w, int nw, int64_t M, int device, GemmPla
       have = true;
     }
   }
-  // tf32 linear with at least a wave of 256 x 256 tiles: two N tiles per
-  // token tile (2/3 of the operand bytes per FLOP, which is what bounds the
-  // tf32 kernels).  Whole-K tiles, one TMEM buffer.  BQ4_NO_WIDE=1 keeps
-  // 128 x BT tiles.
-  if (have && p->tf && !cv && !qk && nw == 1 && w->ntiles >= 2 && !forced && !getenv("BQ4_NO_WIDE")) {
+  // tf32 linear with at least a wave of 256 x 256 tiles and a K loop of 16+
+  // stages (512+ K): two N tiles per token tile (2/3 of the operand bytes per
+  // FLOP).  Whole-K tiles, one TMEM buffer, so the epilogue of a tile holds
+  // the next tile's MMAs: with a short K loop (attention scores, K = 128) the
+  // tile is all epilogue and 128 x 256 tiles with two buffers are faster.
+  // BQ4_NO_WIDE=1 keeps 128 x BT tiles.
+  if (have && p->tf && !cv && !qk && nw == 1 && w->ntiles >= 2 && w->nkc >= 32 && !forced &&
+      !getenv("BQ4_NO_WIDE")) {
     GemmPlan cand = base;
     double cost = 0.0;
     int sms = device_sm_count(device);

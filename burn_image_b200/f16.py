@@ -227,3 +227,28 @@ class PreparedF16ConvWeight(PreparedQ4Weight):
         check(L.lib().bq4_conv2d(_ptr(x), B, H, W, self._h, _ptr(b), ctypes.byref(opt), _ptr(y), _ptr(ws),
                                  ws.numel(), _stream_ptr(self.device)))
         return y
+
+
+def attention(query: torch.Tensor, key: torch.Tensor, value: torch.Tensor, scale: Optional[float] = None,
+              out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """softmax(scale * q k^T) v, no mask, as Burn's ``attention`` with default
+    options (the reference's consumer of the q/k/v projection).  query
+    [B, Hq, Sq, D], key / value [B, Hkv, Skv, D], float16 on one device;
+    query head h attends with kv head h // (Hq // Hkv).  Returns float32
+    [B, Hq, Sq, D].  scale None: 1 / sqrt(D)."""
+    q = _f16(query, "query").contiguous()
+    k = _f16(key, "key").contiguous()
+    v = _f16(value, "value").contiguous()
+    if q.dim() != 4 or k.dim() != 4 or v.shape != k.shape or q.shape[0] != k.shape[0] or q.shape[3] != k.shape[3]:
+        raise Bq4Error(L.EINVAL_SHAPE, "attention takes q [B,Hq,Sq,D], k and v [B,Hkv,Skv,D]")
+    if k.device != q.device or v.device != q.device:
+        raise Bq4Error(L.EINVAL_ARG, "q, k and v must be on one device")
+    B, Hq, Sq, D = q.shape
+    Hkv, Skv = k.shape[1], k.shape[2]
+    y = out if out is not None else torch.empty((B, Hq, Sq, D), dtype=torch.float32, device=q.device)
+    n = ctypes.c_size_t()
+    check(L.lib().bq4_attention_workspace_size(Sq, Skv, D, ctypes.byref(n)))
+    ws = Workspace.get(q.device, n.value)
+    check(L.lib().bq4_attention(_ptr(q), _ptr(k), _ptr(v), B, Hq, Hkv, Sq, Skv, D, float(scale or 0.0), _ptr(y),
+                                _ptr(ws), ws.numel(), _stream_ptr(q.device)))
+    return y

@@ -62,6 +62,8 @@ def lib() -> ctypes.CDLL:
         _lib.orc_f16_conv2d_f64.restype = None
         _lib.orc_cpu_f16_matmul.argtypes = [p, i64, i64, p, i64, i64, i64, p, i32]
         _lib.orc_cpu_f16_conv2d.argtypes = [p, i64, i64, i64, i64, p, i64, i64, i64, p] + [i64] * 6 + [p, i32]
+        _lib.orc_attention_f64.argtypes = [p, p, p, i64, i64, i64, i64, i64, i64, ctypes.c_double, p]
+        _lib.orc_attention_f64.restype = None
     return _lib
 
 
@@ -295,3 +297,16 @@ def cpu_f16_conv2d(inp, weight_bits, bias=None, stride=(1, 1), padding=(0, 0), d
     if rc:
         raise OracleError(rc, "cpu_f16_conv2d")
     return y
+
+
+def attention_f64(q, k, v, scale=None) -> np.ndarray:
+    """softmax(scale q k^T) v per batch and query head, query head h on kv
+    head h // (Hq // Hkv); q [B,Hq,Sq,D], k/v [B,Hkv,Skv,D]; f64 out."""
+    q, k, v = _f32(q), _f32(k), _f32(v)
+    B, Hq, Sq, D = q.shape
+    Hkv, Skv = k.shape[1], k.shape[2]
+    assert Hq % Hkv == 0 and v.shape == k.shape
+    out = np.empty((B, Hq, Sq, D), dtype=np.float64)
+    lib().orc_attention_f64(_ptr(q), _ptr(k), _ptr(v), B, Hq, Hkv, Sq, Skv, D,
+                            float(scale if scale is not None else 1.0 / np.sqrt(D)), _ptr(out))
+    return out

@@ -718,3 +718,48 @@ int orc_cpu_f16_conv2d(const float* in, int64_t B, int64_t C, int64_t H, int64_t
     free(cols);
     return ORC_OK;
 }
+
+/*
+ * Attention checker, f64: out[b][h][i] = sum_j p_j v[b][h/g][j],
+ * p = softmax_j(scale * q[b][h][i] . k[b][h/g][j]) with g = Hq / Hkv (grouped
+ * query heads share a kv head).  This is Burn's `attention` with default
+ * options (no mask, scale 1/sqrt(D)), the composition the reference's
+ * attention tests compare against (crates/burn_boogu/src/model/
+ * native_flash.rs:2784-2843, with the kv heads repeated per group).
+ * q [B][Hq][Sq][D], k and v [B][Hkv][Skv][D], out [B][Hq][Sq][D].
+ */
+void orc_attention_f64(const float* q, const float* k, const float* v, int64_t B, int64_t Hq, int64_t Hkv,
+                       int64_t Sq, int64_t Skv, int64_t D, double scale, double* out) {
+    const int64_t g = Hq / Hkv;
+#pragma omp parallel
+    {
+        double* p = (double*)malloc(sizeof(double) * (size_t)Skv);
+#pragma omp for collapse(3) schedule(static)
+        for (int64_t b = 0; b < B; ++b)
+            for (int64_t h = 0; h < Hq; ++h)
+                for (int64_t i = 0; i < Sq; ++i) {
+                    const float* qi = q + ((b * Hq + h) * Sq + i) * D;
+                    const float* kb = k + (b * Hkv + h / g) * Skv * D;
+                    const float* vb = v + (b * Hkv + h / g) * Skv * D;
+                    double m = -INFINITY;
+                    for (int64_t j = 0; j < Skv; ++j) {
+                        double t = 0.0;
+                        for (int64_t d = 0; d < D; ++d) t += (double)qi[d] * (double)kb[j * D + d];
+                        p[j] = t * scale;
+                        if (p[j] > m) m = p[j];
+                    }
+                    double sum = 0.0;
+                    for (int64_t j = 0; j < Skv; ++j) {
+                        p[j] = exp(p[j] - m);
+                        sum += p[j];
+                    }
+                    double* o = out + ((b * Hq + h) * Sq + i) * D;
+                    for (int64_t d = 0; d < D; ++d) o[d] = 0.0;
+                    for (int64_t j = 0; j < Skv; ++j) {
+                        const double w = p[j] / sum;
+                        for (int64_t d = 0; d < D; ++d) o[d] += w * (double)vb[j * D + d];
+                    }
+                }
+        free(p);
+    }
+}

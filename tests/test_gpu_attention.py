@@ -1,0 +1,84 @@
+"""GPU: attention on the q/k/v projection output (bq4_attention), against the
+oracle (pinned to the reference's attention test, native_flash.rs:2784-2843).
+
+Inputs are binary16, so the oracle runs on the same f16 values; the kernels
+add the tf32 rounding of the softmax probabilities and f32 accumulation.
+
+- the reference test's grouped-query fixture (4 query heads on 2 kv heads);
+- random shapes with grouped heads, the model's head_dim 120 and 128,
+  sequence lengths off the tile sizes, an explicit scale;
+- a DiT-size head set (24 heads, 4352 tokens) checked on a slice of query rows;
+- repeated calls give the same bits; argument errors.
+"""
+import numpy as np
+import pytest
+import torch
+
+import oracle as O
+from burn_image_b200 import f16 as F
+from burn_image_b200 import q4
+from burn_image_b200.q4 import Bq4Error
+
+pytestmark = pytest.mark.gpu
+DEV = torch.device("cuda", 0)
+TOL = 5e-3
+
+
+def _deterministic(shape, offset):
+    n = int(np.prod(shape))
+    idx = np.arange(n, dtype=np.int64)
+    return ((((idx + offset) * 19 + 7) % 53) - 26.0).astype(np.float32).reshape(shape) / np.float32(17.0)
+
+
+def _check(q, k, v, scale=None, rows=None):
+    out = F.attention(q, k, v, scale)
+    torch.cuda.synchronize()
+    q4.poll_device_error()
+    qn = q.float().cpu().numpy()
+    if rows is not None:
+        qn = qn[:, :, rows]
+    ref = O.attention_f64(qn, k.float().cpu().numpy(), v.float().cpu().numpy(), scale)
+    got = out.cpu().numpy() if rows is None else out.cpu().numpy()[:, :, rows]
+    rel = O.rel_frobenius(got, ref)
+    assert rel <= TOL, f"rel_frob {rel}, max_abs {np.abs(got - ref).max()}"
+    return out, rel
+
+
+def test_reference_gqa_fixture():
+    h = lambda a: torch.from_numpy(a).to(DEV).half()  # noqa: E731
+    q = h(_deterministic([1, 4, 3, 120], 2))
+    k = h(_deterministic([1, 2, 5, 120], 7))
+    v = h(_deterministic([1, 2, 5, 120], 11))
+    _, rel = _check(q, k, v)
+    assert rel <= 2e-3
+
+
+@pytest.mark.parametrize("B,Hq,Hkv,Sq,Skv,D,scale", [(1, 4, 2, 300, 260, 128, None), (2, 3, 3, 77, 131, 120, None),
+                                                     (1, 2, 1, 513, 1000, 64, 0.05)])
+def test_random_shapes(B, Hq, Hkv, Sq, Skv, D, scale):
+    g = torch.Generator(device=DEV).manual_seed(Sq + Skv + D)
+    q = torch.randn((B, Hq, Sq, D), generator=g, device=DEV).half()
+    k = torch.randn((B, Hkv, Skv, D), generator=g, device=DEV).half()
+    v = torch.randn((B, Hkv, Skv, D), generator=g, device=DEV).half()
+    out, _ = _check(q, k, v, scale)
+    assert torch.equal(out, F.attention(q, k, v, scale))
+
+
+def test_dit_size_slice():
+    # 24 heads of 128 over 4352 tokens (the DiT block at 1024 px); query rows sampled
+    g = torch.Generator(device=DEV).manual_seed(11)
+    q = (torch.randn((1, 24, 4352, 128), generator=g, device=DEV) * 0.5).half()
+    k = (torch.randn((1, 24, 4352, 128), generator=g, device=DEV) * 0.5).half()
+    v = torch.randn((1, 24, 4352, 128), generator=g, device=DEV).half()
+    _check(q, k, v, rows=np.array([0, 1, 255, 256, 2047, 4095, 4351]))
+
+
+def test_argument_checks():
+    q = torch.zeros((1, 3, 8, 64), device=DEV).half()
+    k = torch.zeros((1, 2, 8, 64), device=DEV).half()
+    with pytest.raises(Bq4Error, match="EINVAL_SHAPE"):
+        F.attention(q, k, k)  # 3 query heads on 2 kv heads
+    q6 = torch.zeros((1, 2, 8, 6), device=DEV).half()
+    k6 = torch.zeros((1, 2, 8, 6), device=DEV).half()
+    with pytest.raises(Bq4Error, match="EINVAL_SHAPE"):
+        F.attention(q6, k6, k6)  # head_dim not a multiple of 4

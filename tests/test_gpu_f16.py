@@ -142,9 +142,10 @@ def test_prepared_weight_linear_with_epilogue():
 
 
 def test_wide_tiles(monkeypatch):
-    # 256 x 256 tiles (two N tiles per token tile) once they fill a wave; an odd
-    # N-tile count (1100 = 8.6 tiles) pairs the last tile with a zero one
-    M, K, N = 9000, 384, 1100
+    # 256 x 256 tiles (two N tiles per token tile) once they fill a wave and the
+    # K loop is 16+ stages (K >= 512); an odd N-tile count (1100 = 8.6 tiles)
+    # pairs the last tile with a zero one
+    M, K, N = 9000, 512, 1100
     g = torch.Generator(device=DEV).manual_seed(21)
     x = torch.randn((M, K), generator=g, device=DEV)
     w = (torch.randn((K, N), generator=g, device=DEV) * K ** -0.5).half()
@@ -163,6 +164,8 @@ def test_wide_tiles(monkeypatch):
     assert pw.plan_info(M)["wide"] == 0
     assert torch.equal(y, pw.linear(x, bias, L.ACT_SILU))
     _check_matmul(x[:500], w, pw.linear(x[:500]))
+    monkeypatch.delenv("BQ4_NO_WIDE")
+    assert F.PreparedF16Weight(w[:384]).plan_info(M)["wide"] == 0  # K = 384: too short a K loop
 
 
 def test_rhs_matmul_throughput_smoke_value():
