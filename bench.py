@@ -417,11 +417,11 @@ def _select_row(dev, n, cols, rows, hbm):
 
 def _attn_row(dev, S, D, H, hbm, tfl):
     """Attention row: softmax(q k^T / sqrt(D)) v over H heads of S tokens,
-    f16 q/k/v, f32 out, graph-replayed on two input sets (each over 2x L2 with
-    its per-head score matrix).  Roofline: tf32 (half the measured bf16 burst)
-    for the 4 S^2 D H FLOPs, against the algorithmic bytes of a fused kernel
-    (q, k, v read once, out written once); the unfused kernels also move each
-    head's S x S f32 scores."""
+    f16 q/k/v, f32 out, graph-replayed on two input sets.  head_dim 128 runs
+    the fused kernel (f16 MMAs): roofline = the measured bf16 burst peak for
+    the 4 S^2 D H FLOPs against q, k, v read once and out written once.  It
+    also needs S^2 H exponentials, which bound it before the tensor core
+    does."""
     import torch
 
     from burn_image_b200 import f16 as F
@@ -441,13 +441,12 @@ def _attn_row(dev, S, D, H, hbm, tfl):
     q4.poll_device_error()
     flops = 4.0 * H * S * S * D
     nbytes = 3 * H * S * D * 2 + H * S * D * 4
-    tf32 = tfl / 2.0
-    t_star = max(nbytes / (hbm * 1e9), flops / (tf32 * 1e12))
+    t_star = max(nbytes / (hbm * 1e9), flops / (tfl * 1e12))
     del items
     torch.cuda.empty_cache()
     return {"us": t * 1e6, "tflops": flops / t / 1e12, "gbs": nbytes / t / 1e9, "bound": "tensor",
-            "t_star_us": t_star * 1e6, "frac": t_star / t, "peak_tf32_tflops": tf32, "sets": 2,
-            "scores_bytes_per_head": S * S * 4}
+            "t_star_us": t_star * 1e6, "frac": t_star / t, "peak_tflops": tfl, "kernel": "fused (f16 MMA)",
+            "exp_per_s": H * S * S / t, "sets": 2}
 
 
 def _f16_row(dev, kind, M, K, N, hbm, tfl):

@@ -84,7 +84,7 @@ SIGNATURES = {
     "bq4_packed_f16_conv2d_workspace_size": (_st, [_i64, _i64, _i64, _i64, _i64, _i32, _i32, _p,
                                                    ctypes.POINTER(_sz)]),
     "bq4_packed_f16_conv2d": (_st, [_p, _i64, _i64, _i64, _i64, _p, _i64, _i32, _i32, _p, _p, _p, _p, _sz, _p]),
-    "bq4_attention_workspace_size": (_st, [_i64, _i64, _i64, ctypes.POINTER(_sz)]),
+    "bq4_attention_workspace_size": (_st, [_i64, _i64, _i64, _i64, _i64, _i64, ctypes.POINTER(_sz)]),
     "bq4_attention": (_st, [_p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64, ctypes.c_float, _p, _p, _sz, _p]),
     "bq4_launch_count": (_u64, []),
     "bq4_launch_count_reset": (None, []),

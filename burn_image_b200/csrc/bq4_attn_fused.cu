@@ -1,0 +1,364 @@
+// bq4_attn_fused.cu -- fused attention for head_dim 128: out = softmax(scale
+// q k^T) v per (batch, query head), one CTA per 128 query rows.
+//
+// The scores never leave the SM.  Per 128-key block j:
+//   warp 0 (TMA)      k_j [128 keys][128] f16 and v_j^T [128 d][128 keys] f16
+//                     into a 2-stage ring (128-byte swizzle); q once.
+//   warp 1 (MMA)      S_j = q k_j^T into TMEM buffer j % 2 (tcgen05, f16 in,
+//                     f32 out), and after the softmax of block j, O += P_j v_j
+//                     into the TMEM accumulator; S_{j+2} is issued as soon as
+//                     buffer j % 2 is released.
+//   warps 4..7        one query row per thread: the row max of S_j (scaled, in
+//                     log2 units), P = exp2(s - m) as f16 into shared memory
+//                     in the MMA operand layout, the running sum, and -- when
+//                     the max grew -- O rescaled in TMEM before the next P v.
+// At the end O / sum is written as f32.  Every wait is bounded: a timeout
+// records BQ4_ETIMEOUT and every role unwinds.
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <cstring>
+
+#include "bq4_internal.h"
+#include "sm100_ptx.cuh"
+
+namespace bq4 {
+namespace {
+
+constexpr int kAThreads = 256;
+constexpr uint32_t kASub = 128 * 128;       // one [128 rows][64] f16 sub-tile (16 KB)
+constexpr uint32_t kATileB = 2 * kASub;     // one [128][128] f16 operand
+constexpr uint32_t kASmem = 6 * kATileB + 1024 + 256;  // q, k[2], vt[2], p; alignment; barriers
+
+struct AttnArgs {
+  float* out;     // [B*Hq][Sq][128] f32
+  int Sq, Skv, Hq, Hkv, qtiles, nblk;
+  float c;        // scale * log2(e)
+  int* err;
+};
+
+__device__ __forceinline__ bool attn_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int* err) {
+  if (ptx::mbar_wait(bar, parity, abort_flag)) return true;
+  if (!*abort_flag) {
+    *abort_flag = 1;
+    if (err) atomicCAS(err, 0, (int)BQ4_ETIMEOUT);
+  }
+  return false;
+}
+
+__global__ void __launch_bounds__(kAThreads, 1)
+    attn_fused_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
+                      const __grid_constant__ CUtensorMap tvt, const AttnArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  uint8_t* qs = smem;
+  uint8_t* ks = qs + kATileB;          // [2] stages
+  uint8_t* vs = ks + 2 * kATileB;      // [2] stages
+  uint8_t* ps = vs + 2 * kATileB;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(ps + kATileB);
+  uint64_t* q_full = bars;
+  uint64_t* k_full = bars + 1;   // [2]
+  uint64_t* k_empty = bars + 3;  // [2]
+  uint64_t* v_full = bars + 5;   // [2]
+  uint64_t* v_empty = bars + 7;  // [2]
+  uint64_t* s_full = bars + 9;   // [2]
+  uint64_t* s_free = bars + 11;  // [2]
+  uint64_t* p_full = bars + 13;
+  uint64_t* pv_done = bars + 14;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 15);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int bh = blockIdx.x / a.qtiles, qt = blockIdx.x - bh * a.qtiles;
+  const int b = bh / a.Hq, h = bh - b * a.Hq;
+  const int bkv = b * a.Hkv + h / (a.Hq / a.Hkv);
+  const int nblk = a.nblk;
+
+  if (threadIdx.x == 0) {
+    ptx::mbar_init(q_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      ptx::mbar_init(&k_full[i], 1);
+      ptx::mbar_init(&k_empty[i], 1);
+      ptx::mbar_init(&v_full[i], 1);
+      ptx::mbar_init(&v_empty[i], 1);
+      ptx::mbar_init(&s_full[i], 1);
+      ptx::mbar_init(&s_free[i], 4);
+    }
+    ptx::mbar_init(p_full, 4);
+    ptx::mbar_init(pv_done, 1);
+    *abort_flag = 0;
+    ptx::fence_mbar_init();
+  }
+  if (warp == 1) {
+    ptx::tmem_alloc(tmem_slot, 512);
+    ptx::tmem_relinquish();
+  }
+  ptx::tc_fence_before();
+  __syncthreads();
+  ptx::tc_fence_after();
+  const uint32_t tmem = *tmem_slot;  // S buffers at columns 0 and 128, O at 256
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ------------------------------------------------ TMA producer
+      ptx::prefetch_tmap(&tq);
+      ptx::prefetch_tmap(&tk);
+      ptx::prefetch_tmap(&tvt);
+      ptx::griddep_wait();
+      const int qrow = bh * a.Sq + qt * 128;
+      ptx::mbar_arrive_expect_tx(q_full, kATileB);
+      ptx::tma_load_2d(qs, &tq, q_full, 0, qrow);
+      ptx::tma_load_2d(qs + kASub, &tq, q_full, 64, qrow);
+      for (int j = 0; j < nblk; ++j) {
+        const int st = j & 1;
+        const uint32_t ph = (j >> 1) & 1;
+        if (!attn_wait(&k_empty[st], ph ^ 1, abort_flag, a.err)) break;
+        const int krow = bkv * a.Skv + j * 128;
+        ptx::mbar_arrive_expect_tx(&k_full[st], kATileB);
+        ptx::tma_load_2d(ks + st * kATileB, &tk, &k_full[st], 0, krow);
+        ptx::tma_load_2d(ks + st * kATileB + kASub, &tk, &k_full[st], 64, krow);
+        if (!attn_wait(&v_empty[st], ph ^ 1, abort_flag, a.err)) break;
+        ptx::mbar_arrive_expect_tx(&v_full[st], kATileB);
+        ptx::tma_load_2d(vs + st * kATileB, &tvt, &v_full[st], j * 128, bkv * 128);
+        ptx::tma_load_2d(vs + st * kATileB + kASub, &tvt, &v_full[st], j * 128 + 64, bkv * 128);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ------------------------------------------------ MMA issuer
+      constexpr uint32_t idesc = ptx::umma_idesc_f16(128, 128);
+      const uint32_t q_a = ptx::smem_u32(qs), p_a = ptx::smem_u32(ps);
+      bool ok = attn_wait(q_full, 0, abort_flag, a.err);
+      auto issue_s = [&](int j) -> bool {
+        const int st = j & 1;
+        if (!attn_wait(&k_full[st], (j >> 1) & 1, abort_flag, a.err)) return false;
+        if (j >= 2 && !attn_wait(&s_free[st], ((j >> 1) - 1) & 1, abort_flag, a.err)) return false;
+        ptx::tc_fence_after();
+        const uint32_t k_a = ptx::smem_u32(ks + st * kATileB);
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          const uint32_t off = (uint32_t)(kk >> 2) * kASub + (uint32_t)(kk & 3) * 32;
+          ptx::mma_f16_ss(tmem + st * 128, ptx::umma_desc_sw128(q_a + off), ptx::umma_desc_sw128(k_a + off), idesc,
+                          kk > 0 ? 1u : 0u);
+        }
+        ptx::mma_commit(&s_full[st]);
+        ptx::mma_commit(&k_empty[st]);
+        return true;
+      };
+      if (ok) ok = issue_s(0);
+      if (ok && nblk > 1) ok = issue_s(1);
+      for (int j = 0; ok && j < nblk; ++j) {
+        const int st = j & 1;
+        if (!attn_wait(p_full, j & 1, abort_flag, a.err) ||
+            !attn_wait(&v_full[st], (j >> 1) & 1, abort_flag, a.err)) break;
+        ptx::tc_fence_after();
+        const uint32_t v_a = ptx::smem_u32(vs + st * kATileB);
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          const uint32_t off = (uint32_t)(kk >> 2) * kASub + (uint32_t)(kk & 3) * 32;
+          ptx::mma_f16_ss(tmem + 256, ptx::umma_desc_sw128(p_a + off), ptx::umma_desc_sw128(v_a + off), idesc,
+                          (j > 0 || kk > 0) ? 1u : 0u);
+        }
+        ptx::mma_commit(pv_done);
+        ptx::mma_commit(&v_empty[st]);
+        if (j + 2 < nblk && !issue_s(j + 2)) break;
+      }
+    }
+  } else if (warp >= 4) {
+    // ------------------------------------------------ softmax, one query row per thread
+    const int wq = warp - 4;
+    const int row = wq * 32 + lane;
+    const uint32_t t_lane = tmem + ((uint32_t)(wq * 32) << 16);
+    const float c = a.c;
+    float m = -INFINITY, l = 0.0f;
+    bool ok = true;
+    for (int j = 0; j < nblk && ok; ++j) {
+      const int st = j & 1;
+      ok = __all_sync(0xffffffffu, attn_wait(&s_full[st], (j >> 1) & 1, abort_flag, a.err));
+      if (!ok) break;
+      ptx::tc_fence_after();
+      const int valid = a.Skv - j * 128;  // keys of this block (>= 1)
+      float mx = -INFINITY;
+#pragma unroll
+      for (int cc = 0; cc < 8; ++cc) {
+        uint32_t r[16];
+        ptx::tmem_ld_32x32b_x16(t_lane + st * 128 + cc * 16, r);
+        ptx::tmem_ld_wait();
+#pragma unroll
+        for (int i = 0; i < 16; ++i)
+          if (cc * 16 + i < valid) mx = fmaxf(mx, __uint_as_float(r[i]) * c);
+      }
+      const float m_new = fmaxf(m, mx);
+      const float alpha = exp2f(m - m_new);  // 0 on the first block (m = -inf)
+      if (j > 0) {
+        // P's buffer and O are free once P_{j-1} v_{j-1} has completed
+        ok = __all_sync(0xffffffffu, attn_wait(pv_done, (j - 1) & 1, abort_flag, a.err));
+        if (!ok) break;
+        ptx::tc_fence_after();
+      }
+      float sum = 0.0f;
+#pragma unroll
+      for (int cc = 0; cc < 8; ++cc) {
+        uint32_t r[16];
+        ptx::tmem_ld_32x32b_x16(t_lane + st * 128 + cc * 16, r);
+        ptx::tmem_ld_wait();
+        uint32_t pk[8];
+#pragma unroll
+        for (int i = 0; i < 16; i += 2) {
+          const float p0 = (cc * 16 + i < valid) ? exp2f(__uint_as_float(r[i]) * c - m_new) : 0.0f;
+          const float p1 = (cc * 16 + i + 1 < valid) ? exp2f(__uint_as_float(r[i + 1]) * c - m_new) : 0.0f;
+          sum += p0 + p1;
+          const __half2 hp = __floats2half2_rn(p0, p1);
+          pk[i >> 1] = *reinterpret_cast<const uint32_t*>(&hp);
+        }
+        // keys 16 cc .. 16 cc + 15 = 16-byte chunks 2 cc, 2 cc + 1 of row `row`
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+          const int ch = 2 * cc + hh;
+          uint8_t* dst = ps + (ch >> 3) * kASub + row * 128 + (((ch & 7) ^ (row & 7)) * 16);
+          *reinterpret_cast<uint4*>(dst) = make_uint4(pk[4 * hh], pk[4 * hh + 1], pk[4 * hh + 2], pk[4 * hh + 3]);
+        }
+      }
+      // S_j has been read: its buffer may take S_{j+2}
+      ptx::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) ptx::mbar_arrive(&s_free[st]);
+      l = l * alpha + sum;
+      if (j > 0 && __any_sync(0xffffffffu, alpha != 1.0f)) {
+#pragma unroll
+        for (int cc = 0; cc < 8; ++cc) {
+          uint32_t r[16];
+          ptx::tmem_ld_32x32b_x16(t_lane + 256 + cc * 16, r);
+          ptx::tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 16; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
+          ptx::tmem_st_32x32b_x16(t_lane + 256 + cc * 16, r);
+        }
+        ptx::tmem_st_wait();
+      }
+      m = m_new;
+      ptx::fence_proxy_async_smem();  // P's stores, for the MMA's reads
+      ptx::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) ptx::mbar_arrive(p_full);
+    }
+    if (ok) ok = __all_sync(0xffffffffu, attn_wait(pv_done, (nblk - 1) & 1, abort_flag, a.err));
+    if (ok) {
+      ptx::tc_fence_after();
+      const int qrow = qt * 128 + row;
+      const float inv = 1.0f / l;
+      float* o = a.out + ((size_t)bh * a.Sq + qrow) * 128;
+#pragma unroll
+      for (int cc = 0; cc < 8; ++cc) {
+        uint32_t r[16];
+        ptx::tmem_ld_32x32b_x16(t_lane + 256 + cc * 16, r);
+        ptx::tmem_ld_wait();
+        if (qrow < a.Sq) {
+#pragma unroll
+          for (int i = 0; i < 16; i += 4)
+            *reinterpret_cast<float4*>(o + cc * 16 + i) =
+                make_float4(__uint_as_float(r[i]) * inv, __uint_as_float(r[i + 1]) * inv,
+                            __uint_as_float(r[i + 2]) * inv, __uint_as_float(r[i + 3]) * inv);
+        }
+      }
+    }
+  }
+  ptx::tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    ptx::tc_fence_after();
+    ptx::tmem_dealloc(tmem, 512);
+  }
+}
+
+// v [B*Hkv][Skv][128] f16 -> v^T [B*Hkv][128][pitch] f16, zero for keys >= Skv;
+// 32 x 32 tiles through shared memory.
+__global__ void attn_vt_kernel(const uint16_t* __restrict__ v, int Skv, int pitch, uint16_t* __restrict__ vt) {
+  __shared__ uint16_t tile[32][33];
+  const int j0 = blockIdx.x * 32, d0 = blockIdx.y * 32, bk = blockIdx.z;
+  for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+    const int j = j0 + i, d = d0 + threadIdx.x;
+    tile[i][threadIdx.x] = j < Skv ? v[((size_t)bk * Skv + j) * 128 + d] : (uint16_t)0;
+  }
+  __syncthreads();
+  for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+    const int d = d0 + i, j = j0 + threadIdx.x;
+    if (j < pitch) vt[((size_t)bk * 128 + d) * pitch + j] = tile[threadIdx.x][i];
+  }
+}
+
+typedef CUresult (*EncodeFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                             const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                             CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeFn attn_encode_fn() {
+  static EncodeFn fn = nullptr;
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeFn>(p);
+  }
+  return fn;
+}
+
+// [rows][cols] f16 at row pitch `pitch` elements, box {64, 128}, 128-byte swizzle.
+bool attn_tmap(CUtensorMap* m, const void* base, uint64_t cols, uint64_t rows, uint64_t pitch) {
+  EncodeFn enc = attn_encode_fn();
+  if (!enc) return false;
+  cuuint64_t gdim[2] = {cols, rows};
+  cuuint64_t gstride[1] = {pitch * 2};
+  cuuint32_t box[2] = {64, 128};
+  cuuint32_t es[2] = {1, 1};
+  return enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), gdim, gstride, box, es,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+}  // namespace
+
+size_t attn_fused_workspace(int64_t B, int64_t Hkv, int64_t Skv) {
+  const int64_t pitch = (Skv + 127) / 128 * 128;
+  return (size_t)(B * Hkv * 128 * pitch * 2 + 255) / 256 * 256;
+}
+
+bq4_status attn_fused(const uint16_t* q, const uint16_t* k, const uint16_t* v, int64_t B, int64_t Hq, int64_t Hkv,
+                      int64_t Sq, int64_t Skv, float scale, float* out, void* workspace, cudaStream_t s) {
+  const int64_t pitch = (Skv + 127) / 128 * 128;
+  uint16_t* vt = static_cast<uint16_t*>(workspace);
+  attn_vt_kernel<<<dim3((unsigned)(pitch / 32), 4, (unsigned)(B * Hkv)), dim3(32, 8), 0, s>>>(v, (int)Skv,
+                                                                                          (int)pitch, vt);
+  note_launch();
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return check_cuda(e, "attention v transpose launch");
+  CUtensorMap tq, tk, tvt;
+  if (!attn_tmap(&tq, q, 128, (uint64_t)(B * Hq * Sq), 128) || !attn_tmap(&tk, k, 128, (uint64_t)(B * Hkv * Skv), 128) ||
+      !attn_tmap(&tvt, vt, (uint64_t)pitch, (uint64_t)(B * Hkv * 128), (uint64_t)pitch))
+    return set_error(BQ4_ECUDA, "cuTensorMapEncodeTiled failed for the attention operands");
+  AttnArgs a;
+  a.out = out;
+  a.Sq = (int)Sq;
+  a.Skv = (int)Skv;
+  a.Hq = (int)Hq;
+  a.Hkv = (int)Hkv;
+  a.qtiles = (int)((Sq + 127) / 128);
+  a.nblk = (int)((Skv + 127) / 128);
+  a.c = scale * 1.4426950408889634f;  // log2(e): exp(x) = exp2(x log2 e)
+  a.err = device_error_word();
+  static bool attr_set[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !attr_set[dev]) {
+    e = cudaFuncSetAttribute(attn_fused_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kASmem);
+    if (e != cudaSuccess) return check_cuda(e, "attention shared-memory attribute");
+    attr_set[dev] = true;
+  }
+  attn_fused_kernel<<<(unsigned)(B * Hq * a.qtiles), kAThreads, kASmem, s>>>(tq, tk, tvt, a);
+  note_launch();
+  return check_cuda(cudaGetLastError(), "fused attention launch");
+}
+
+}  // namespace bq4

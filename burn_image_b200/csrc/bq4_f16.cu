@@ -18,6 +18,7 @@
 #include <cuda_runtime.h>
 
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
 #include <new>
 
@@ -766,6 +767,13 @@ bq4_status bq4_packed_f16_conv2d(const float* input, int64_t batch, int64_t in_c
 
 // ---------------------------------------------------------------- attention
 
+namespace bq4 {
+// fused attention for head_dim 128 (bq4_attn_fused.cu)
+size_t attn_fused_workspace(int64_t B, int64_t Hkv, int64_t Skv);
+bq4_status attn_fused(const uint16_t* q, const uint16_t* k, const uint16_t* v, int64_t B, int64_t Hq, int64_t Hkv,
+                      int64_t Sq, int64_t Skv, float scale, float* out, void* workspace, cudaStream_t s);
+}  // namespace bq4
+
 namespace {
 
 struct AttnLayout {
@@ -795,19 +803,31 @@ bq4_status attn_layout(int64_t Sq, int64_t Skv, int64_t D, int dev, AttnLayout* 
   return BQ4_OK;
 }
 
+bool attn_use_fused(int64_t D) { return D == 128 && !getenv("BQ4_ATTN_UNFUSED"); }
+
+bq4_status attn_check(int64_t B, int64_t Hq, int64_t Hkv) {
+  if (B <= 0 || Hq <= 0 || Hkv <= 0 || Hq % Hkv || B * Hq > (1 << 20))
+    return set_error(BQ4_EINVAL_SHAPE, "B=%lld Hq=%lld Hkv=%lld (Hq %% Hkv == 0)", (long long)B, (long long)Hq,
+                     (long long)Hkv);
+  return BQ4_OK;
+}
+
 }  // namespace
 
 extern "C" {
 
-bq4_status bq4_attention_workspace_size(int64_t Sq, int64_t Skv, int64_t D, size_t* bytes) {
+bq4_status bq4_attention_workspace_size(int64_t B, int64_t Hq, int64_t Hkv, int64_t Sq, int64_t Skv, int64_t D,
+                                        size_t* bytes) {
   if (!bytes) return set_error(BQ4_EINVAL_ARG, "bytes is NULL");
+  bq4_status st = attn_check(B, Hq, Hkv);
+  if (st) return st;
   int dev = 0;
   cudaGetDevice(&dev);
   AttnLayout L;
   GemmPlan ps, pv;
-  bq4_status st = attn_layout(Sq, Skv, D, dev, &L, &ps, &pv);
+  st = attn_layout(Sq, Skv, D, dev, &L, &ps, &pv);
   if (st) return st;
-  *bytes = L.total;
+  *bytes = attn_use_fused(D) ? attn_fused_workspace(B, Hkv, Skv) : L.total;
   return BQ4_OK;
 }
 
@@ -815,23 +835,28 @@ bq4_status bq4_attention(const uint32_t* q, const uint32_t* k, const uint32_t* v
                          int64_t Sq, int64_t Skv, int64_t D, float scale, float* out, void* workspace,
                          size_t workspace_bytes, bq4_stream_t stream) {
   if (!q || !k || !v || !out) return set_error(BQ4_EINVAL_ARG, "NULL pointer");
-  if (B <= 0 || Hq <= 0 || Hkv <= 0 || Hq % Hkv)
-    return set_error(BQ4_EINVAL_SHAPE, "B=%lld Hq=%lld Hkv=%lld (Hq %% Hkv == 0)", (long long)B, (long long)Hq,
-                     (long long)Hkv);
+  bq4_status st = attn_check(B, Hq, Hkv);
+  if (st) return st;
   if (!al(out, 16)) return set_error(BQ4_EALIGN, "out must be 16-byte aligned");
   int dev = 0;
   cudaGetDevice(&dev);
-  bq4_status st = need_sm100(dev);
+  st = need_sm100(dev);
   if (st) return st;
   AttnLayout L;
   GemmPlan ps, pv;
   st = attn_layout(Sq, Skv, D, dev, &L, &ps, &pv);
   if (st) return st;
-  if (!workspace || workspace_bytes < L.total)
-    return set_error(BQ4_EWORKSPACE, "workspace %zu < required %zu bytes", workspace_bytes, L.total);
+  const bool fused = attn_use_fused(D);
+  const size_t need = fused ? attn_fused_workspace(B, Hkv, Skv) : L.total;
+  if (!workspace || workspace_bytes < need)
+    return set_error(BQ4_EWORKSPACE, "workspace %zu < required %zu bytes", workspace_bytes, need);
   if (!al(workspace, 256)) return set_error(BQ4_EALIGN, "workspace not 256-byte aligned");
+  if (!al(q, 16) || !al(k, 16) || !al(v, 16)) return set_error(BQ4_EALIGN, "q/k/v must be 16-byte aligned");
   const float sc = scale > 0.0f ? scale : 1.0f / std::sqrt((float)D);
   const cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (fused)
+    return attn_fused(reinterpret_cast<const uint16_t*>(q), reinterpret_cast<const uint16_t*>(k),
+                      reinterpret_cast<const uint16_t*>(v), B, Hq, Hkv, Sq, Skv, sc, out, workspace, s);
   uint8_t* p = static_cast<uint8_t*>(workspace);
   float* q32 = reinterpret_cast<float*>(p);
   float* S = reinterpret_cast<float*>(p + L.q32);

@@ -247,7 +247,7 @@ def attention(query: torch.Tensor, key: torch.Tensor, value: torch.Tensor, scale
     Hkv, Skv = k.shape[1], k.shape[2]
     y = out if out is not None else torch.empty((B, Hq, Sq, D), dtype=torch.float32, device=q.device)
     n = ctypes.c_size_t()
-    check(L.lib().bq4_attention_workspace_size(Sq, Skv, D, ctypes.byref(n)))
+    check(L.lib().bq4_attention_workspace_size(B, Hq, Hkv, Sq, Skv, D, ctypes.byref(n)))
     ws = Workspace.get(q.device, n.value)
     check(L.lib().bq4_attention(_ptr(q), _ptr(k), _ptr(v), B, Hq, Hkv, Sq, Skv, D, float(scale or 0.0), _ptr(y),
                                 _ptr(ws), ws.numel(), _stream_ptr(q.device)))

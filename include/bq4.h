@@ -520,11 +520,15 @@ BQ4_API bq4_status bq4_packed_f16_conv2d(const float* input, int64_t batch, int6
  * [B][Hkv][Skv][D], binary16 (packed-F16 storage), contiguous; query head h
  * reads kv head h / (Hq / Hkv) (grouped-query attention, Hq % Hkv == 0).
  * out f32 [B][Hq][Sq][D], 16-byte aligned.  scale <= 0 means 1/sqrt(D).
- * D % 4 == 0.  Unfused: per head the scores q k^T and P v run as tf32 GEMMs
- * (k and v widened into the weight tiles, q and the f32 scores read in
- * place) with a row softmax between them; the scores of one head live in
- * the workspace. */
-BQ4_API bq4_status bq4_attention_workspace_size(int64_t Sq, int64_t Skv, int64_t D, size_t* bytes);
+ * D % 4 == 0; q, k, v 16-byte aligned.  D = 128 runs one fused kernel
+ * (scores in TMEM, softmax in registers, P through shared memory, O in
+ * TMEM; v transposed once into the workspace).  Other D run unfused: per
+ * head the scores q k^T and P v as tf32 GEMMs (k and v widened into the
+ * weight tiles, q and the f32 scores read in place) with a row softmax
+ * between them.  The environment variable BQ4_ATTN_UNFUSED=1 selects the
+ * unfused path for D = 128 too. */
+BQ4_API bq4_status bq4_attention_workspace_size(int64_t B, int64_t Hq, int64_t Hkv, int64_t Sq, int64_t Skv,
+                                                int64_t D, size_t* bytes);
 BQ4_API bq4_status bq4_attention(const uint32_t* q, const uint32_t* k, const uint32_t* v, int64_t B, int64_t Hq,
                                  int64_t Hkv, int64_t Sq, int64_t Skv, int64_t D, float scale, float* out,
                                  void* workspace, size_t workspace_bytes, bq4_stream_t stream);

@@ -7,6 +7,7 @@ add the tf32 rounding of the softmax probabilities and f32 accumulation.
 - the reference test's grouped-query fixture (4 query heads on 2 kv heads);
 - random shapes with grouped heads, the model's head_dim 120 and 128,
   sequence lengths off the tile sizes, an explicit scale;
+- head_dim 128 (the fused kernel) against the unfused composition;
 - a DiT-size head set (24 heads, 4352 tokens) checked on a slice of query rows;
 - repeated calls give the same bits; argument errors.
 """
@@ -62,6 +63,21 @@ def test_random_shapes(B, Hq, Hkv, Sq, Skv, D, scale):
     v = torch.randn((B, Hkv, Skv, D), generator=g, device=DEV).half()
     out, _ = _check(q, k, v, scale)
     assert torch.equal(out, F.attention(q, k, v, scale))
+
+
+def test_fused_matches_unfused(monkeypatch):
+    # head_dim 128 runs the fused kernel; BQ4_ATTN_UNFUSED=1 the GEMM + softmax composition
+    g = torch.Generator(device=DEV).manual_seed(5)
+    q = torch.randn((2, 4, 200, 128), generator=g, device=DEV).half()
+    k = torch.randn((2, 2, 333, 128), generator=g, device=DEV).half()
+    v = torch.randn((2, 2, 333, 128), generator=g, device=DEV).half()
+    fused = F.attention(q, k, v)
+    monkeypatch.setenv("BQ4_ATTN_UNFUSED", "1")
+    unfused = F.attention(q, k, v)
+    torch.cuda.synchronize()
+    q4.poll_device_error()
+    rel = (torch.linalg.norm(fused.double() - unfused.double()) / torch.linalg.norm(unfused.double())).item()
+    assert rel <= 3e-3, f"rel {rel}"
 
 
 def test_dit_size_slice():
