@@ -9,9 +9,11 @@
 //                     into the TMEM accumulator; S_{j+2} is issued as soon as
 //                     buffer j % 2 is released.
 //   warps 4..7        one query row per thread: the row max of S_j (scaled, in
-//                     log2 units), P = exp2(s - m) as f16 into shared memory
-//                     in the MMA operand layout, the running sum, and -- when
-//                     the max grew -- O rescaled in TMEM before the next P v.
+//                     log2 units), P = exp2(s - m) as f16 into one of two
+//                     shared-memory buffers in the MMA operand layout, the
+//                     running sum, and -- only when the max jumps by more than
+//                     2^8 -- O rescaled in TMEM once the previous P v is done,
+//                     so the softmax of block j overlaps P_{j-1} v_{j-1}.
 // At the end O / sum is written as f32.  Every wait is bounded: a timeout
 // records BQ4_ETIMEOUT and every role unwinds.
 #include <cuda.h>
@@ -29,7 +31,11 @@ namespace {
 constexpr int kAThreads = 256;
 constexpr uint32_t kASub = 128 * 128;       // one [128 rows][64] f16 sub-tile (16 KB)
 constexpr uint32_t kATileB = 2 * kASub;     // one [128][128] f16 operand
-constexpr uint32_t kASmem = 6 * kATileB + 1024 + 256;  // q, k[2], vt[2], p; alignment; barriers
+constexpr uint32_t kASmem = 7 * kATileB + 1024 + 256;  // q, k[2], vt[2], p[2]; alignment; barriers
+// A row keeps its running max until a block's max passes it by more than this
+// (log2 units): P = exp2(s - m) then stays <= 2^8, which f16 holds, and O is
+// rescaled -- after waiting for the previous P v -- only when the max jumps.
+constexpr float kRescaleLog2 = 8.0f;
 
 struct AttnArgs {
   float* out;     // [B*Hq][Sq][128] f32
@@ -56,8 +62,8 @@ __global__ void __launch_bounds__(kAThreads, 1)
   uint8_t* qs = smem;
   uint8_t* ks = qs + kATileB;          // [2] stages
   uint8_t* vs = ks + 2 * kATileB;      // [2] stages
-  uint8_t* ps = vs + 2 * kATileB;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(ps + kATileB);
+  uint8_t* ps = vs + 2 * kATileB;      // [2] P buffers
+  uint64_t* bars = reinterpret_cast<uint64_t*>(ps + 2 * kATileB);
   uint64_t* q_full = bars;
   uint64_t* k_full = bars + 1;   // [2]
   uint64_t* k_empty = bars + 3;  // [2]
@@ -66,8 +72,8 @@ __global__ void __launch_bounds__(kAThreads, 1)
   uint64_t* s_full = bars + 9;   // [2]
   uint64_t* s_free = bars + 11;  // [2]
   uint64_t* p_full = bars + 13;
-  uint64_t* pv_done = bars + 14;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 15);
+  uint64_t* p_free = bars + 14;  // [2]: P_j v_j has completed (P buffer j % 2 free, O holds it)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -85,9 +91,9 @@ __global__ void __launch_bounds__(kAThreads, 1)
       ptx::mbar_init(&v_empty[i], 1);
       ptx::mbar_init(&s_full[i], 1);
       ptx::mbar_init(&s_free[i], 4);
+      ptx::mbar_init(&p_free[i], 1);
     }
     ptx::mbar_init(p_full, 4);
-    ptx::mbar_init(pv_done, 1);
     *abort_flag = 0;
     ptx::fence_mbar_init();
   }
@@ -155,19 +161,22 @@ __global__ void __launch_bounds__(kAThreads, 1)
             !attn_wait(&v_full[st], (j >> 1) & 1, abort_flag, a.err)) break;
         ptx::tc_fence_after();
         const uint32_t v_a = ptx::smem_u32(vs + st * kATileB);
+        const uint32_t pb = p_a + st * kATileB;
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
           const uint32_t off = (uint32_t)(kk >> 2) * kASub + (uint32_t)(kk & 3) * 32;
-          ptx::mma_f16_ss(tmem + 256, ptx::umma_desc_sw128(p_a + off), ptx::umma_desc_sw128(v_a + off), idesc,
+          ptx::mma_f16_ss(tmem + 256, ptx::umma_desc_sw128(pb + off), ptx::umma_desc_sw128(v_a + off), idesc,
                           (j > 0 || kk > 0) ? 1u : 0u);
         }
-        ptx::mma_commit(pv_done);
         ptx::mma_commit(&v_empty[st]);
+        ptx::mma_commit(&p_free[st]);
         if (j + 2 < nblk && !issue_s(j + 2)) break;
       }
     }
   } else if (warp >= 4) {
     // ------------------------------------------------ softmax, one query row per thread
+    // (one warp per scheduler: eight independent partial max / sum chains and
+    // a row's eight TMEM loads in flight before one wait)
     const int wq = warp - 4;
     const int row = wq * 32 + lane;
     const uint32_t t_lane = tmem + ((uint32_t)(wq * 32) << 16);
@@ -180,36 +189,46 @@ __global__ void __launch_bounds__(kAThreads, 1)
       if (!ok) break;
       ptx::tc_fence_after();
       const int valid = a.Skv - j * 128;  // keys of this block (>= 1)
-      float mx = -INFINITY;
+      uint32_t r[128];
 #pragma unroll
       for (int cc = 0; cc < 8; ++cc) {
-        uint32_t r[16];
-        ptx::tmem_ld_32x32b_x16(t_lane + st * 128 + cc * 16, r);
-        ptx::tmem_ld_wait();
-#pragma unroll
-        for (int i = 0; i < 16; ++i)
-          if (cc * 16 + i < valid) mx = fmaxf(mx, __uint_as_float(r[i]) * c);
+        uint32_t (&rc)[16] = *reinterpret_cast<uint32_t(*)[16]>(r + cc * 16);
+        ptx::tmem_ld_32x32b_x16(t_lane + st * 128 + cc * 16, rc);
       }
-      const float m_new = fmaxf(m, mx);
-      const float alpha = exp2f(m - m_new);  // 0 on the first block (m = -inf)
-      if (j > 0) {
-        // P's buffer and O are free once P_{j-1} v_{j-1} has completed
-        ok = __all_sync(0xffffffffu, attn_wait(pv_done, (j - 1) & 1, abort_flag, a.err));
+      ptx::tmem_ld_wait();
+      // S_j is in registers: its TMEM buffer may take S_{j+2}
+      ptx::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) ptx::mbar_arrive(&s_free[st]);
+      float mp[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) mp[u] = -INFINITY;
+#pragma unroll
+      for (int i = 0; i < 128; ++i)
+        if (i < valid) mp[i & 7] = fmaxf(mp[i & 7], __uint_as_float(r[i]));
+      const float mx =
+          c * fmaxf(fmaxf(fmaxf(mp[0], mp[1]), fmaxf(mp[2], mp[3])), fmaxf(fmaxf(mp[4], mp[5]), fmaxf(mp[6], mp[7])));
+      const bool jump = j == 0 || mx > m + kRescaleLog2;
+      const float m_use = jump ? fmaxf(m, mx) : m;
+      const float alpha = (j > 0 && jump) ? exp2f(m - m_use) : 1.0f;
+      if (j >= 2) {
+        // P buffer j % 2 was last read by P_{j-2} v_{j-2}
+        ok = __all_sync(0xffffffffu, attn_wait(&p_free[st], ((j >> 1) - 1) & 1, abort_flag, a.err));
         if (!ok) break;
-        ptx::tc_fence_after();
       }
-      float sum = 0.0f;
+      uint8_t* pbuf = ps + st * kATileB;
+      float sp[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) sp[u] = 0.0f;
 #pragma unroll
       for (int cc = 0; cc < 8; ++cc) {
-        uint32_t r[16];
-        ptx::tmem_ld_32x32b_x16(t_lane + st * 128 + cc * 16, r);
-        ptx::tmem_ld_wait();
         uint32_t pk[8];
 #pragma unroll
         for (int i = 0; i < 16; i += 2) {
-          const float p0 = (cc * 16 + i < valid) ? exp2f(__uint_as_float(r[i]) * c - m_new) : 0.0f;
-          const float p1 = (cc * 16 + i + 1 < valid) ? exp2f(__uint_as_float(r[i + 1]) * c - m_new) : 0.0f;
-          sum += p0 + p1;
+          const int k0 = cc * 16 + i;
+          const float p0 = (k0 < valid) ? exp2f(fmaf(__uint_as_float(r[k0]), c, -m_use)) : 0.0f;
+          const float p1 = (k0 + 1 < valid) ? exp2f(fmaf(__uint_as_float(r[k0 + 1]), c, -m_use)) : 0.0f;
+          sp[i >> 1] += p0 + p1;
           const __half2 hp = __floats2half2_rn(p0, p1);
           pk[i >> 1] = *reinterpret_cast<const uint32_t*>(&hp);
         }
@@ -217,51 +236,58 @@ __global__ void __launch_bounds__(kAThreads, 1)
 #pragma unroll
         for (int hh = 0; hh < 2; ++hh) {
           const int ch = 2 * cc + hh;
-          uint8_t* dst = ps + (ch >> 3) * kASub + row * 128 + (((ch & 7) ^ (row & 7)) * 16);
+          uint8_t* dst = pbuf + (ch >> 3) * kASub + row * 128 + (((ch & 7) ^ (row & 7)) * 16);
           *reinterpret_cast<uint4*>(dst) = make_uint4(pk[4 * hh], pk[4 * hh + 1], pk[4 * hh + 2], pk[4 * hh + 3]);
         }
       }
-      // S_j has been read: its buffer may take S_{j+2}
-      ptx::tc_fence_before();
-      __syncwarp();
-      if (lane == 0) ptx::mbar_arrive(&s_free[st]);
-      l = l * alpha + sum;
-      if (j > 0 && __any_sync(0xffffffffu, alpha != 1.0f)) {
+      if (j > 0 && __any_sync(0xffffffffu, jump)) {
+        // O must hold P_{j-1} v_{j-1} before it is scaled (P_j v_j waits for p_full)
+        ok = __all_sync(0xffffffffu, attn_wait(&p_free[(j - 1) & 1], ((j - 1) >> 1) & 1, abort_flag, a.err));
+        if (!ok) break;
+        ptx::tc_fence_after();
+        uint32_t o[128];
 #pragma unroll
         for (int cc = 0; cc < 8; ++cc) {
-          uint32_t r[16];
-          ptx::tmem_ld_32x32b_x16(t_lane + 256 + cc * 16, r);
-          ptx::tmem_ld_wait();
+          uint32_t (&oc)[16] = *reinterpret_cast<uint32_t(*)[16]>(o + cc * 16);
+          ptx::tmem_ld_32x32b_x16(t_lane + 256 + cc * 16, oc);
+        }
+        ptx::tmem_ld_wait();
 #pragma unroll
-          for (int i = 0; i < 16; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
-          ptx::tmem_st_32x32b_x16(t_lane + 256 + cc * 16, r);
+        for (int i = 0; i < 128; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+#pragma unroll
+        for (int cc = 0; cc < 8; ++cc) {
+          const uint32_t (&oc)[16] = *reinterpret_cast<const uint32_t(*)[16]>(o + cc * 16);
+          ptx::tmem_st_32x32b_x16(t_lane + 256 + cc * 16, oc);
         }
         ptx::tmem_st_wait();
       }
-      m = m_new;
+      l = l * alpha + (((sp[0] + sp[1]) + (sp[2] + sp[3])) + ((sp[4] + sp[5]) + (sp[6] + sp[7])));
+      m = m_use;
       ptx::fence_proxy_async_smem();  // P's stores, for the MMA's reads
       ptx::tc_fence_before();
       __syncwarp();
       if (lane == 0) ptx::mbar_arrive(p_full);
     }
-    if (ok) ok = __all_sync(0xffffffffu, attn_wait(pv_done, (nblk - 1) & 1, abort_flag, a.err));
+    // the last P v's commit covers every earlier MMA
+    if (ok) ok = __all_sync(0xffffffffu, attn_wait(&p_free[(nblk - 1) & 1], ((nblk - 1) >> 1) & 1, abort_flag, a.err));
     if (ok) {
       ptx::tc_fence_after();
       const int qrow = qt * 128 + row;
       const float inv = 1.0f / l;
       float* o = a.out + ((size_t)bh * a.Sq + qrow) * 128;
+      uint32_t r[128];
 #pragma unroll
       for (int cc = 0; cc < 8; ++cc) {
-        uint32_t r[16];
-        ptx::tmem_ld_32x32b_x16(t_lane + 256 + cc * 16, r);
-        ptx::tmem_ld_wait();
-        if (qrow < a.Sq) {
+        uint32_t (&rc)[16] = *reinterpret_cast<uint32_t(*)[16]>(r + cc * 16);
+        ptx::tmem_ld_32x32b_x16(t_lane + 256 + cc * 16, rc);
+      }
+      ptx::tmem_ld_wait();
+      if (qrow < a.Sq) {
 #pragma unroll
-          for (int i = 0; i < 16; i += 4)
-            *reinterpret_cast<float4*>(o + cc * 16 + i) =
-                make_float4(__uint_as_float(r[i]) * inv, __uint_as_float(r[i + 1]) * inv,
-                            __uint_as_float(r[i + 2]) * inv, __uint_as_float(r[i + 3]) * inv);
-        }
+        for (int i = 0; i < 128; i += 4)
+          *reinterpret_cast<float4*>(o + i) =
+              make_float4(__uint_as_float(r[i]) * inv, __uint_as_float(r[i + 1]) * inv,
+                          __uint_as_float(r[i + 2]) * inv, __uint_as_float(r[i + 3]) * inv);
       }
     }
   }
