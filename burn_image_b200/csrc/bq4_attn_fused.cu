@@ -8,7 +8,7 @@
 //                     f32 out), and after the softmax of block j, O += P_j v_j
 //                     into the TMEM accumulator; S_{j+2} is issued as soon as
 //                     buffer j % 2 is released.
-//   warps 4..7        one query row per thread: the row max of S_j (scaled, in
+//   warps 4..11       two threads per query row (64 columns each): the row max of S_j (scaled, in
 //                     log2 units), P = exp2(s - m) as f16 into one of two
 //                     shared-memory buffers in the MMA operand layout, the
 //                     running sum, and -- only when the max jumps by more than
@@ -28,10 +28,14 @@
 namespace bq4 {
 namespace {
 
-constexpr int kAThreads = 256;
+constexpr int kAThreads = 384;  // warp 0 TMA, 1 MMA, 4..11 softmax (two per TMEM lane quarter)
 constexpr uint32_t kASub = 128 * 128;       // one [128 rows][64] f16 sub-tile (16 KB)
 constexpr uint32_t kATileB = 2 * kASub;     // one [128][128] f16 operand
-constexpr uint32_t kASmem = 7 * kATileB + 1024 + 256;  // q, k[2], vt[2], p[2]; alignment; barriers
+// q, k[2], vt[2], p[2]; the two softmax halves' row-max slots [2][2][128] f32;
+// barriers.  No alignment slack: the kernel checks that its dynamic shared
+// memory starts 1024-aligned (the operand tiles' swizzle needs it).
+constexpr uint32_t kAXchg = 2 * 2 * 128 * 4;
+constexpr uint32_t kASmem = 7 * kATileB + kAXchg + 256;
 // A row keeps its running max until a block's max passes it by more than this
 // (log2 units): P = exp2(s - m) then stays <= 2^8, which f16 holds, and O is
 // rescaled -- after waiting for the previous P v -- only when the max jumps.
@@ -56,14 +60,18 @@ __device__ __forceinline__ bool attn_wait(uint64_t* bar, uint32_t parity, volati
 __global__ void __launch_bounds__(kAThreads, 1)
     attn_fused_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                       const __grid_constant__ CUtensorMap tvt, const AttnArgs a) {
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
-                                             ~static_cast<uintptr_t>(1023));
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  if (ptx::smem_u32(smem_raw) & 1023) {  // uniform: every thread leaves before any barrier
+    if (threadIdx.x == 0 && a.err) atomicCAS(a.err, 0, (int)BQ4_EALIGN);
+    return;
+  }
+  uint8_t* smem = smem_raw;
   uint8_t* qs = smem;
   uint8_t* ks = qs + kATileB;          // [2] stages
   uint8_t* vs = ks + 2 * kATileB;      // [2] stages
   uint8_t* ps = vs + 2 * kATileB;      // [2] P buffers
-  uint64_t* bars = reinterpret_cast<uint64_t*>(ps + 2 * kATileB);
+  float* xmax = reinterpret_cast<float*>(ps + 2 * kATileB);  // [block parity][half][row]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(ps + 2 * kATileB + kAXchg);
   uint64_t* q_full = bars;
   uint64_t* k_full = bars + 1;   // [2]
   uint64_t* k_empty = bars + 3;  // [2]
@@ -73,7 +81,8 @@ __global__ void __launch_bounds__(kAThreads, 1)
   uint64_t* s_free = bars + 11;  // [2]
   uint64_t* p_full = bars + 13;
   uint64_t* p_free = bars + 14;  // [2]: P_j v_j has completed (P buffer j % 2 free, O holds it)
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
+  uint64_t* pair = bars + 16;    // [4]: both softmax warps of a lane quarter have posted their half's max
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 20);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -90,10 +99,11 @@ __global__ void __launch_bounds__(kAThreads, 1)
       ptx::mbar_init(&v_full[i], 1);
       ptx::mbar_init(&v_empty[i], 1);
       ptx::mbar_init(&s_full[i], 1);
-      ptx::mbar_init(&s_free[i], 4);
+      ptx::mbar_init(&s_free[i], 8);
       ptx::mbar_init(&p_free[i], 1);
     }
-    ptx::mbar_init(p_full, 4);
+    ptx::mbar_init(p_full, 8);
+    for (int i = 0; i < 4; ++i) ptx::mbar_init(&pair[i], 64);
     *abort_flag = 0;
     ptx::fence_mbar_init();
   }
@@ -174,12 +184,15 @@ __global__ void __launch_bounds__(kAThreads, 1)
       }
     }
   } else if (warp >= 4) {
-    // ------------------------------------------------ softmax, one query row per thread
-    // (one warp per scheduler: eight independent partial max / sum chains and
-    // a row's eight TMEM loads in flight before one wait)
+    // ------------------------------------------------ softmax: two threads per query row
+    // Warps w and w + 4 share TMEM lane quarter w % 4 (rows 32 (w % 4) ..);
+    // the first takes score / output columns 0..63, the second 64..127.  Per
+    // block the halves post their max to shared memory and meet on pair[q],
+    // so both use the same row max; each keeps its own partial sum.
     const int wq = warp - 4;
-    const int row = wq * 32 + lane;
-    const uint32_t t_lane = tmem + ((uint32_t)(wq * 32) << 16);
+    const int q = warp & 3, half = wq >> 2;
+    const int row = q * 32 + lane;
+    const uint32_t t_lane = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(half * 64);
     const float c = a.c;
     float m = -INFINITY, l = 0.0f;
     bool ok = true;
@@ -188,10 +201,10 @@ __global__ void __launch_bounds__(kAThreads, 1)
       ok = __all_sync(0xffffffffu, attn_wait(&s_full[st], (j >> 1) & 1, abort_flag, a.err));
       if (!ok) break;
       ptx::tc_fence_after();
-      const int valid = a.Skv - j * 128;  // keys of this block (>= 1)
-      uint32_t r[128];
+      const int valid = a.Skv - j * 128 - half * 64;  // keys of this half (may be <= 0)
+      uint32_t r[64];
 #pragma unroll
-      for (int cc = 0; cc < 8; ++cc) {
+      for (int cc = 0; cc < 4; ++cc) {
         uint32_t (&rc)[16] = *reinterpret_cast<uint32_t(*)[16]>(r + cc * 16);
         ptx::tmem_ld_32x32b_x16(t_lane + st * 128 + cc * 16, rc);
       }
@@ -204,10 +217,14 @@ __global__ void __launch_bounds__(kAThreads, 1)
 #pragma unroll
       for (int u = 0; u < 8; ++u) mp[u] = -INFINITY;
 #pragma unroll
-      for (int i = 0; i < 128; ++i)
+      for (int i = 0; i < 64; ++i)
         if (i < valid) mp[i & 7] = fmaxf(mp[i & 7], __uint_as_float(r[i]));
-      const float mx =
-          c * fmaxf(fmaxf(fmaxf(mp[0], mp[1]), fmaxf(mp[2], mp[3])), fmaxf(fmaxf(mp[4], mp[5]), fmaxf(mp[6], mp[7])));
+      const float pm = fmaxf(fmaxf(fmaxf(mp[0], mp[1]), fmaxf(mp[2], mp[3])), fmaxf(fmaxf(mp[4], mp[5]), fmaxf(mp[6], mp[7])));
+      xmax[(st * 2 + half) * 128 + row] = pm;
+      ptx::mbar_arrive(&pair[q]);
+      ok = __all_sync(0xffffffffu, attn_wait(&pair[q], j & 1, abort_flag, a.err));
+      if (!ok) break;
+      const float mx = c * fmaxf(pm, xmax[(st * 2 + (half ^ 1)) * 128 + row]);
       const bool jump = j == 0 || mx > m + kRescaleLog2;
       const float m_use = jump ? fmaxf(m, mx) : m;
       const float alpha = (j > 0 && jump) ? exp2f(m - m_use) : 1.0f;
@@ -216,12 +233,12 @@ __global__ void __launch_bounds__(kAThreads, 1)
         ok = __all_sync(0xffffffffu, attn_wait(&p_free[st], ((j >> 1) - 1) & 1, abort_flag, a.err));
         if (!ok) break;
       }
-      uint8_t* pbuf = ps + st * kATileB;
+      uint8_t* pbuf = ps + st * kATileB + half * kASub;  // this half's keys are one 64-key sub-tile
       float sp[8];
 #pragma unroll
       for (int u = 0; u < 8; ++u) sp[u] = 0.0f;
 #pragma unroll
-      for (int cc = 0; cc < 8; ++cc) {
+      for (int cc = 0; cc < 4; ++cc) {
         uint32_t pk[8];
 #pragma unroll
         for (int i = 0; i < 16; i += 2) {
@@ -232,11 +249,11 @@ __global__ void __launch_bounds__(kAThreads, 1)
           const __half2 hp = __floats2half2_rn(p0, p1);
           pk[i >> 1] = *reinterpret_cast<const uint32_t*>(&hp);
         }
-        // keys 16 cc .. 16 cc + 15 = 16-byte chunks 2 cc, 2 cc + 1 of row `row`
+        // keys 16 cc .. 16 cc + 15 of this half = 16-byte chunks 2 cc, 2 cc + 1 of the row
 #pragma unroll
         for (int hh = 0; hh < 2; ++hh) {
           const int ch = 2 * cc + hh;
-          uint8_t* dst = pbuf + (ch >> 3) * kASub + row * 128 + (((ch & 7) ^ (row & 7)) * 16);
+          uint8_t* dst = pbuf + row * 128 + ((ch ^ (row & 7)) * 16);
           *reinterpret_cast<uint4*>(dst) = make_uint4(pk[4 * hh], pk[4 * hh + 1], pk[4 * hh + 2], pk[4 * hh + 3]);
         }
       }
@@ -245,17 +262,17 @@ __global__ void __launch_bounds__(kAThreads, 1)
         ok = __all_sync(0xffffffffu, attn_wait(&p_free[(j - 1) & 1], ((j - 1) >> 1) & 1, abort_flag, a.err));
         if (!ok) break;
         ptx::tc_fence_after();
-        uint32_t o[128];
+        uint32_t o[64];
 #pragma unroll
-        for (int cc = 0; cc < 8; ++cc) {
+        for (int cc = 0; cc < 4; ++cc) {
           uint32_t (&oc)[16] = *reinterpret_cast<uint32_t(*)[16]>(o + cc * 16);
           ptx::tmem_ld_32x32b_x16(t_lane + 256 + cc * 16, oc);
         }
         ptx::tmem_ld_wait();
 #pragma unroll
-        for (int i = 0; i < 128; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+        for (int i = 0; i < 64; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
 #pragma unroll
-        for (int cc = 0; cc < 8; ++cc) {
+        for (int cc = 0; cc < 4; ++cc) {
           const uint32_t (&oc)[16] = *reinterpret_cast<const uint32_t(*)[16]>(o + cc * 16);
           ptx::tmem_st_32x32b_x16(t_lane + 256 + cc * 16, oc);
         }
@@ -271,20 +288,27 @@ __global__ void __launch_bounds__(kAThreads, 1)
     // the last P v's commit covers every earlier MMA
     if (ok) ok = __all_sync(0xffffffffu, attn_wait(&p_free[(nblk - 1) & 1], ((nblk - 1) >> 1) & 1, abort_flag, a.err));
     if (ok) {
+      // the row's sum: both halves post theirs in the slot of block nblk (free:
+      // block nblk - 2 used it, and both halves have passed block nblk - 1)
+      xmax[((nblk & 1) * 2 + half) * 128 + row] = l;
+      ptx::mbar_arrive(&pair[q]);
+      ok = __all_sync(0xffffffffu, attn_wait(&pair[q], nblk & 1, abort_flag, a.err));
+    }
+    if (ok) {
+      const float inv = 1.0f / (l + xmax[((nblk & 1) * 2 + (half ^ 1)) * 128 + row]);
       ptx::tc_fence_after();
       const int qrow = qt * 128 + row;
-      const float inv = 1.0f / l;
-      float* o = a.out + ((size_t)bh * a.Sq + qrow) * 128;
-      uint32_t r[128];
+      float* o = a.out + ((size_t)bh * a.Sq + qrow) * 128 + half * 64;
+      uint32_t r[64];
 #pragma unroll
-      for (int cc = 0; cc < 8; ++cc) {
+      for (int cc = 0; cc < 4; ++cc) {
         uint32_t (&rc)[16] = *reinterpret_cast<uint32_t(*)[16]>(r + cc * 16);
         ptx::tmem_ld_32x32b_x16(t_lane + 256 + cc * 16, rc);
       }
       ptx::tmem_ld_wait();
       if (qrow < a.Sq) {
 #pragma unroll
-        for (int i = 0; i < 128; i += 4)
+        for (int i = 0; i < 64; i += 4)
           *reinterpret_cast<float4*>(o + i) =
               make_float4(__uint_as_float(r[i]) * inv, __uint_as_float(r[i + 1]) * inv,
                           __uint_as_float(r[i + 2]) * inv, __uint_as_float(r[i + 3]) * inv);
