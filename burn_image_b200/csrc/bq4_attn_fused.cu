@@ -3,15 +3,16 @@
 //
 // The scores never leave the SM.  Per 128-key block j:
 //   warp 0 (TMA)      k_j [128 keys][128] f16 and v_j^T [128 d][128 keys] f16
-//                     into a 2-stage ring (128-byte swizzle); q once.
+//                     into a 3-stage ring (128-byte swizzle); q once.
 //   warp 1 (MMA)      S_j = q k_j^T into TMEM buffer j % 2 (tcgen05, f16 in,
 //                     f32 out), and after the softmax of block j, O += P_j v_j
-//                     into the TMEM accumulator; S_{j+2} is issued as soon as
-//                     buffer j % 2 is released.
+//                     into the TMEM accumulator with P_j read from TMEM (the
+//                     A-in-TMEM form); S_{j+2} is issued as soon as buffer
+//                     j % 2 is released.
 //   warps 4..11       two threads per query row (64 columns each): the row max of S_j (scaled, in
-//                     log2 units), P = exp2(s - m) as f16 into one of two
-//                     shared-memory buffers in the MMA operand layout, the
-//                     running sum, and -- only when the max jumps by more than
+//                     log2 units), P = exp2(s - m) as f16 pairs into one of
+//                     two TMEM P buffers (row i in lane i, two keys per
+//                     column), the running sum, and -- only when the max jumps by more than
 //                     2^8 -- O rescaled in TMEM once the previous P v is done,
 //                     so the softmax of block j overlaps P_{j-1} v_{j-1}.
 // At the end O / sum is written as f32.  Every wait is bounded: a timeout
@@ -29,13 +30,17 @@ namespace bq4 {
 namespace {
 
 constexpr int kAThreads = 384;  // warp 0 TMA, 1 MMA, 4..11 softmax (two per TMEM lane quarter)
+constexpr int kAKV = 3;         // k / v ring stages
 constexpr uint32_t kASub = 128 * 128;       // one [128 rows][64] f16 sub-tile (16 KB)
 constexpr uint32_t kATileB = 2 * kASub;     // one [128][128] f16 operand
-// q, k[2], vt[2], p[2]; the two softmax halves' row-max slots [2][2][128] f32;
-// barriers.  No alignment slack: the kernel checks that its dynamic shared
-// memory starts 1024-aligned (the operand tiles' swizzle needs it).
+// q, k[kAKV], vt[kAKV]; the two softmax halves' row-max slots [2][2][128]
+// f32; barriers.  No alignment slack: the kernel checks that its dynamic
+// shared memory starts 1024-aligned (the operand tiles' swizzle needs it).
 constexpr uint32_t kAXchg = 2 * 2 * 128 * 4;
-constexpr uint32_t kASmem = 7 * kATileB + kAXchg + 256;
+constexpr uint32_t kASmem = (1 + 2 * kAKV) * kATileB + kAXchg + 256;
+// TMEM columns: S buffers at 0 and 128 (f32), O at 256 (f32), P buffers at
+// 384 and 448 (128 keys as 64 columns of f16 pairs).
+constexpr uint32_t kATmemO = 256, kATmemP = 384;
 // A row keeps its running max until a block's max passes it by more than this
 // (log2 units): P = exp2(s - m) then stays <= 2^8, which f16 holds, and O is
 // rescaled -- after waiting for the previous P v -- only when the max jumps.
@@ -57,6 +62,54 @@ __device__ __forceinline__ bool attn_wait(uint64_t* bar, uint32_t parity, volati
   return false;
 }
 
+// 2^x by the PTX instruction ex2.approx.ftz.f32 (one MUFU op; relative error
+// near 2^-22, results below 2^-126 flush to 0 -- far under the smallest f16
+// probability the P operand can hold).
+__device__ __forceinline__ float attn_ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// Max of this thread's 64 raw scores; kFull: all 64 keys exist (every block
+// but a ragged last one), so no key is masked.
+template <bool kFull>
+__device__ __forceinline__ float attn_rowmax(const uint32_t (&r)[64], int valid) {
+  float mp[8];
+#pragma unroll
+  for (int u = 0; u < 8; ++u) mp[u] = -INFINITY;
+#pragma unroll
+  for (int i = 0; i < 64; ++i)
+    if (kFull || i < valid) mp[i & 7] = fmaxf(mp[i & 7], __uint_as_float(r[i]));
+  return fmaxf(fmaxf(fmaxf(mp[0], mp[1]), fmaxf(mp[2], mp[3])), fmaxf(fmaxf(mp[4], mp[5]), fmaxf(mp[6], mp[7])));
+}
+
+// P = 2^(s c - m) for this thread's 64 keys as f16 pairs into 32 TMEM
+// columns of its lane from t_p (key 2 i in the low half of column i, the
+// layout the A-in-TMEM MMA reads); returns the f32 sum of the probabilities.
+template <bool kFull>
+__device__ __forceinline__ float attn_p_store(const uint32_t (&r)[64], int valid, float c, float m_use,
+                                              uint32_t t_p) {
+  float sp[8];
+#pragma unroll
+  for (int u = 0; u < 8; ++u) sp[u] = 0.0f;
+#pragma unroll
+  for (int cc = 0; cc < 4; ++cc) {
+    uint32_t pk[8];
+#pragma unroll
+    for (int i = 0; i < 16; i += 2) {
+      const int k0 = cc * 16 + i;
+      const float p0 = (kFull || k0 < valid) ? attn_ex2(fmaf(__uint_as_float(r[k0]), c, -m_use)) : 0.0f;
+      const float p1 = (kFull || k0 + 1 < valid) ? attn_ex2(fmaf(__uint_as_float(r[k0 + 1]), c, -m_use)) : 0.0f;
+      sp[i >> 1] += p0 + p1;
+      const __half2 hp = __floats2half2_rn(p0, p1);
+      pk[i >> 1] = *reinterpret_cast<const uint32_t*>(&hp);
+    }
+    ptx::tmem_st_32x32b_x8(t_p + cc * 8, pk);
+  }
+  return ((sp[0] + sp[1]) + (sp[2] + sp[3])) + ((sp[4] + sp[5]) + (sp[6] + sp[7]));
+}
+
 __global__ void __launch_bounds__(kAThreads, 1)
     attn_fused_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                       const __grid_constant__ CUtensorMap tvt, const AttnArgs a) {
@@ -67,22 +120,21 @@ __global__ void __launch_bounds__(kAThreads, 1)
   }
   uint8_t* smem = smem_raw;
   uint8_t* qs = smem;
-  uint8_t* ks = qs + kATileB;          // [2] stages
-  uint8_t* vs = ks + 2 * kATileB;      // [2] stages
-  uint8_t* ps = vs + 2 * kATileB;      // [2] P buffers
-  float* xmax = reinterpret_cast<float*>(ps + 2 * kATileB);  // [block parity][half][row]
-  uint64_t* bars = reinterpret_cast<uint64_t*>(ps + 2 * kATileB + kAXchg);
+  uint8_t* ks = qs + kATileB;          // [kAKV] stages
+  uint8_t* vs = ks + kAKV * kATileB;   // [kAKV] stages
+  float* xmax = reinterpret_cast<float*>(vs + kAKV * kATileB);  // [block parity][half][row]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(vs + kAKV * kATileB + kAXchg);
   uint64_t* q_full = bars;
-  uint64_t* k_full = bars + 1;   // [2]
-  uint64_t* k_empty = bars + 3;  // [2]
-  uint64_t* v_full = bars + 5;   // [2]
-  uint64_t* v_empty = bars + 7;  // [2]
-  uint64_t* s_full = bars + 9;   // [2]
-  uint64_t* s_free = bars + 11;  // [2]
-  uint64_t* p_full = bars + 13;
-  uint64_t* p_free = bars + 14;  // [2]: P_j v_j has completed (P buffer j % 2 free, O holds it)
-  uint64_t* pair = bars + 16;    // [4]: both softmax warps of a lane quarter have posted their half's max
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 20);
+  uint64_t* k_full = bars + 1;          // [kAKV]
+  uint64_t* k_empty = k_full + kAKV;    // [kAKV]
+  uint64_t* v_full = k_empty + kAKV;    // [kAKV]
+  uint64_t* v_empty = v_full + kAKV;    // [kAKV]
+  uint64_t* s_full = v_empty + kAKV;    // [2]
+  uint64_t* s_free = s_full + 2;        // [2]
+  uint64_t* p_full = s_free + 2;
+  uint64_t* p_free = p_full + 1;  // [2]: P_j v_j has completed (P buffer j % 2 free, O holds it)
+  uint64_t* pair = p_free + 2;    // [4]: both softmax warps of a lane quarter have posted their half's max
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(pair + 4);  // 24 barriers: 192 of the 256 bytes
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -93,11 +145,13 @@ __global__ void __launch_bounds__(kAThreads, 1)
 
   if (threadIdx.x == 0) {
     ptx::mbar_init(q_full, 1);
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < kAKV; ++i) {
       ptx::mbar_init(&k_full[i], 1);
       ptx::mbar_init(&k_empty[i], 1);
       ptx::mbar_init(&v_full[i], 1);
       ptx::mbar_init(&v_empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
       ptx::mbar_init(&s_full[i], 1);
       ptx::mbar_init(&s_free[i], 8);
       ptx::mbar_init(&p_free[i], 1);
@@ -128,8 +182,8 @@ __global__ void __launch_bounds__(kAThreads, 1)
       ptx::tma_load_2d(qs, &tq, q_full, 0, qrow);
       ptx::tma_load_2d(qs + kASub, &tq, q_full, 64, qrow);
       for (int j = 0; j < nblk; ++j) {
-        const int st = j & 1;
-        const uint32_t ph = (j >> 1) & 1;
+        const int st = j % kAKV;
+        const uint32_t ph = (j / kAKV) & 1;
         if (!attn_wait(&k_empty[st], ph ^ 1, abort_flag, a.err)) break;
         const int krow = bkv * a.Skv + j * 128;
         ptx::mbar_arrive_expect_tx(&k_full[st], kATileB);
@@ -145,14 +199,14 @@ __global__ void __launch_bounds__(kAThreads, 1)
     if (lane == 0) {
       // ------------------------------------------------ MMA issuer
       constexpr uint32_t idesc = ptx::umma_idesc_f16(128, 128);
-      const uint32_t q_a = ptx::smem_u32(qs), p_a = ptx::smem_u32(ps);
+      const uint32_t q_a = ptx::smem_u32(qs);
       bool ok = attn_wait(q_full, 0, abort_flag, a.err);
       auto issue_s = [&](int j) -> bool {
-        const int st = j & 1;
-        if (!attn_wait(&k_full[st], (j >> 1) & 1, abort_flag, a.err)) return false;
+        const int st = j & 1, kst = j % kAKV;
+        if (!attn_wait(&k_full[kst], (j / kAKV) & 1, abort_flag, a.err)) return false;
         if (j >= 2 && !attn_wait(&s_free[st], ((j >> 1) - 1) & 1, abort_flag, a.err)) return false;
         ptx::tc_fence_after();
-        const uint32_t k_a = ptx::smem_u32(ks + st * kATileB);
+        const uint32_t k_a = ptx::smem_u32(ks + kst * kATileB);
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
           const uint32_t off = (uint32_t)(kk >> 2) * kASub + (uint32_t)(kk & 3) * 32;
@@ -160,25 +214,25 @@ __global__ void __launch_bounds__(kAThreads, 1)
                           kk > 0 ? 1u : 0u);
         }
         ptx::mma_commit(&s_full[st]);
-        ptx::mma_commit(&k_empty[st]);
+        ptx::mma_commit(&k_empty[kst]);
         return true;
       };
       if (ok) ok = issue_s(0);
       if (ok && nblk > 1) ok = issue_s(1);
       for (int j = 0; ok && j < nblk; ++j) {
-        const int st = j & 1;
+        const int st = j & 1, vst = j % kAKV;
         if (!attn_wait(p_full, j & 1, abort_flag, a.err) ||
-            !attn_wait(&v_full[st], (j >> 1) & 1, abort_flag, a.err)) break;
+            !attn_wait(&v_full[vst], (j / kAKV) & 1, abort_flag, a.err)) break;
         ptx::tc_fence_after();
-        const uint32_t v_a = ptx::smem_u32(vs + st * kATileB);
-        const uint32_t pb = p_a + st * kATileB;
+        const uint32_t v_a = ptx::smem_u32(vs + vst * kATileB);
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
+          // keys 16 kk .. 16 kk + 15: P columns 8 kk .. 8 kk + 7, v^T sub-tile kk / 4 at 32-byte step kk % 4
           const uint32_t off = (uint32_t)(kk >> 2) * kASub + (uint32_t)(kk & 3) * 32;
-          ptx::mma_f16_ss(tmem + 256, ptx::umma_desc_sw128(pb + off), ptx::umma_desc_sw128(v_a + off), idesc,
-                          (j > 0 || kk > 0) ? 1u : 0u);
+          ptx::mma_f16_ts(tmem + kATmemO, tmem + kATmemP + (uint32_t)st * 64 + (uint32_t)kk * 8,
+                          ptx::umma_desc_sw128(v_a + off), idesc, (j > 0 || kk > 0) ? 1u : 0u);
         }
-        ptx::mma_commit(&v_empty[st]);
+        ptx::mma_commit(&v_empty[vst]);
         ptx::mma_commit(&p_free[st]);
         if (j + 2 < nblk && !issue_s(j + 2)) break;
       }
@@ -213,13 +267,8 @@ __global__ void __launch_bounds__(kAThreads, 1)
       ptx::tc_fence_before();
       __syncwarp();
       if (lane == 0) ptx::mbar_arrive(&s_free[st]);
-      float mp[8];
-#pragma unroll
-      for (int u = 0; u < 8; ++u) mp[u] = -INFINITY;
-#pragma unroll
-      for (int i = 0; i < 64; ++i)
-        if (i < valid) mp[i & 7] = fmaxf(mp[i & 7], __uint_as_float(r[i]));
-      const float pm = fmaxf(fmaxf(fmaxf(mp[0], mp[1]), fmaxf(mp[2], mp[3])), fmaxf(fmaxf(mp[4], mp[5]), fmaxf(mp[6], mp[7])));
+      const bool full = valid >= 64;  // warp-uniform: valid depends on the block and the half
+      const float pm = full ? attn_rowmax<true>(r, valid) : attn_rowmax<false>(r, valid);
       xmax[(st * 2 + half) * 128 + row] = pm;
       ptx::mbar_arrive(&pair[q]);
       ok = __all_sync(0xffffffffu, attn_wait(&pair[q], j & 1, abort_flag, a.err));
@@ -233,30 +282,10 @@ __global__ void __launch_bounds__(kAThreads, 1)
         ok = __all_sync(0xffffffffu, attn_wait(&p_free[st], ((j >> 1) - 1) & 1, abort_flag, a.err));
         if (!ok) break;
       }
-      uint8_t* pbuf = ps + st * kATileB + half * kASub;  // this half's keys are one 64-key sub-tile
-      float sp[8];
-#pragma unroll
-      for (int u = 0; u < 8; ++u) sp[u] = 0.0f;
-#pragma unroll
-      for (int cc = 0; cc < 4; ++cc) {
-        uint32_t pk[8];
-#pragma unroll
-        for (int i = 0; i < 16; i += 2) {
-          const int k0 = cc * 16 + i;
-          const float p0 = (k0 < valid) ? exp2f(fmaf(__uint_as_float(r[k0]), c, -m_use)) : 0.0f;
-          const float p1 = (k0 + 1 < valid) ? exp2f(fmaf(__uint_as_float(r[k0 + 1]), c, -m_use)) : 0.0f;
-          sp[i >> 1] += p0 + p1;
-          const __half2 hp = __floats2half2_rn(p0, p1);
-          pk[i >> 1] = *reinterpret_cast<const uint32_t*>(&hp);
-        }
-        // keys 16 cc .. 16 cc + 15 of this half = 16-byte chunks 2 cc, 2 cc + 1 of the row
-#pragma unroll
-        for (int hh = 0; hh < 2; ++hh) {
-          const int ch = 2 * cc + hh;
-          uint8_t* dst = pbuf + row * 128 + ((ch ^ (row & 7)) * 16);
-          *reinterpret_cast<uint4*>(dst) = make_uint4(pk[4 * hh], pk[4 * hh + 1], pk[4 * hh + 2], pk[4 * hh + 3]);
-        }
-      }
+      // this half's 64 keys: 32 columns of P buffer j % 2
+      const uint32_t t_p = t_lane - (uint32_t)(half * 64) + kATmemP + (uint32_t)(st * 64 + half * 32);
+      const float psum = full ? attn_p_store<true>(r, valid, c, m_use, t_p)
+                              : attn_p_store<false>(r, valid, c, m_use, t_p);
       if (j > 0 && __any_sync(0xffffffffu, jump)) {
         // O must hold P_{j-1} v_{j-1} before it is scaled (P_j v_j waits for p_full)
         ok = __all_sync(0xffffffffu, attn_wait(&p_free[(j - 1) & 1], ((j - 1) >> 1) & 1, abort_flag, a.err));
@@ -266,7 +295,7 @@ __global__ void __launch_bounds__(kAThreads, 1)
 #pragma unroll
         for (int cc = 0; cc < 4; ++cc) {
           uint32_t (&oc)[16] = *reinterpret_cast<uint32_t(*)[16]>(o + cc * 16);
-          ptx::tmem_ld_32x32b_x16(t_lane + 256 + cc * 16, oc);
+          ptx::tmem_ld_32x32b_x16(t_lane + kATmemO + cc * 16, oc);
         }
         ptx::tmem_ld_wait();
 #pragma unroll
@@ -274,13 +303,13 @@ __global__ void __launch_bounds__(kAThreads, 1)
 #pragma unroll
         for (int cc = 0; cc < 4; ++cc) {
           const uint32_t (&oc)[16] = *reinterpret_cast<const uint32_t(*)[16]>(o + cc * 16);
-          ptx::tmem_st_32x32b_x16(t_lane + 256 + cc * 16, oc);
+          ptx::tmem_st_32x32b_x16(t_lane + kATmemO + cc * 16, oc);
         }
         ptx::tmem_st_wait();
       }
-      l = l * alpha + (((sp[0] + sp[1]) + (sp[2] + sp[3])) + ((sp[4] + sp[5]) + (sp[6] + sp[7])));
+      l = l * alpha + psum;
       m = m_use;
-      ptx::fence_proxy_async_smem();  // P's stores, for the MMA's reads
+      ptx::tmem_st_wait();  // P (and a rescaled O) in TMEM before the MMA reads them
       ptx::tc_fence_before();
       __syncwarp();
       if (lane == 0) ptx::mbar_arrive(p_full);
@@ -303,7 +332,7 @@ __global__ void __launch_bounds__(kAThreads, 1)
 #pragma unroll
       for (int cc = 0; cc < 4; ++cc) {
         uint32_t (&rc)[16] = *reinterpret_cast<uint32_t(*)[16]>(r + cc * 16);
-        ptx::tmem_ld_32x32b_x16(t_lane + 256 + cc * 16, rc);
+        ptx::tmem_ld_32x32b_x16(t_lane + kATmemO + cc * 16, rc);
       }
       ptx::tmem_ld_wait();
       if (qrow < a.Sq) {
