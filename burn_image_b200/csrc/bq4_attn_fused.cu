@@ -3,13 +3,13 @@
 //
 // The scores never leave the SM.  Per 128-key block j:
 //   warp 0 (TMA)      k_j [128 keys][128] f16 and v_j^T [128 d][128 keys] f16
-//                     into a 3-stage ring (128-byte swizzle); q once.
+//                     into a 2-stage ring (128-byte swizzle); q once.
 //   warp 1 (MMA)      S_j = q k_j^T into TMEM buffer j % 2 (tcgen05, f16 in,
 //                     f32 out), and after the softmax of block j, O += P_j v_j
 //                     into the TMEM accumulator with P_j read from TMEM (the
 //                     A-in-TMEM form); S_{j+2} is issued as soon as buffer
 //                     j % 2 is released.
-//   warps 4..11       two threads per query row (64 columns each): the row max of S_j (scaled, in
+//   warps 4..19       four threads per query row (32 columns each): the row max of S_j (scaled, in
 //                     log2 units), P = exp2(s - m) as f16 pairs into one of
 //                     two TMEM P buffers (row i in lane i, two keys per
 //                     column), the running sum, and -- only when the max jumps by more than
@@ -29,14 +29,17 @@
 namespace bq4 {
 namespace {
 
-constexpr int kAThreads = 384;  // warp 0 TMA, 1 MMA, 4..11 softmax (two per TMEM lane quarter)
-constexpr int kAKV = 3;         // k / v ring stages
+constexpr int kAParts = 4;                       // softmax threads per query row
+constexpr int kACols = 128 / kAParts;            // score / output columns per softmax thread
+constexpr int kASoftWarps = 4 * kAParts;         // kAParts warps per TMEM lane quarter
+constexpr int kAThreads = 128 + 32 * kASoftWarps;  // warp 0 TMA, 1 MMA, 4.. softmax
+constexpr int kAKV = 2;                          // k / v ring stages
 constexpr uint32_t kASub = 128 * 128;       // one [128 rows][64] f16 sub-tile (16 KB)
 constexpr uint32_t kATileB = 2 * kASub;     // one [128][128] f16 operand
-// q, k[kAKV], vt[kAKV]; the two softmax halves' row-max slots [2][2][128]
+// q, k[kAKV], vt[kAKV]; the softmax parts' row-max slots [2][kAParts][128]
 // f32; barriers.  No alignment slack: the kernel checks that its dynamic
 // shared memory starts 1024-aligned (the operand tiles' swizzle needs it).
-constexpr uint32_t kAXchg = 2 * 2 * 128 * 4;
+constexpr uint32_t kAXchg = 2 * kAParts * 128 * 4;
 constexpr uint32_t kASmem = (1 + 2 * kAKV) * kATileB + kAXchg + 256;
 // TMEM columns: S buffers at 0 and 128 (f32), O at 256 (f32), P buffers at
 // 384 and 448 (128 keys as 64 columns of f16 pairs).
@@ -71,43 +74,112 @@ __device__ __forceinline__ float attn_ex2(float x) {
   return y;
 }
 
-// Max of this thread's 64 raw scores; kFull: all 64 keys exist (every block
-// but a ragged last one), so no key is masked.
-template <bool kFull>
-__device__ __forceinline__ float attn_rowmax(const uint32_t (&r)[64], int valid) {
-  float mp[8];
-#pragma unroll
-  for (int u = 0; u < 8; ++u) mp[u] = -INFINITY;
-#pragma unroll
-  for (int i = 0; i < 64; ++i)
-    if (kFull || i < valid) mp[i & 7] = fmaxf(mp[i & 7], __uint_as_float(r[i]));
-  return fmaxf(fmaxf(fmaxf(mp[0], mp[1]), fmaxf(mp[2], mp[3])), fmaxf(fmaxf(mp[4], mp[5]), fmaxf(mp[6], mp[7])));
+// Blackwell's three-input max and packed two-lane f32 arithmetic (PTX
+// max.f32 with three sources; fma / add .f32x2 on a b64 pair, low lane first).
+__device__ __forceinline__ float attn_max3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t attn_pack2(float lo, float hi) {
+  uint64_t d;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(d) : "f"(lo), "f"(hi));
+  return d;
+}
+__device__ __forceinline__ void attn_unpack2(uint64_t v, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ uint64_t attn_fma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t attn_add2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
 }
 
-// P = 2^(s c - m) for this thread's 64 keys as f16 pairs into 32 TMEM
+// Max of this thread's kN raw scores; kFull: all kN keys exist (every block
+// but a ragged last one), so no key is masked.
+template <int kN, bool kFull>
+__device__ __forceinline__ float attn_rowmax(const uint32_t (&r)[kN], int valid) {
+  if constexpr (kFull && kN % 16 == 0) {
+    // eight running maxima, two new scores per three-input max
+    float mp[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) mp[u] = __uint_as_float(r[u]);
+#pragma unroll
+    for (int i = 8; i + 16 <= kN; i += 16)
+#pragma unroll
+      for (int u = 0; u < 8; ++u) mp[u] = attn_max3(mp[u], __uint_as_float(r[i + u]), __uint_as_float(r[i + 8 + u]));
+#pragma unroll
+    for (int u = 0; u < 8; ++u) mp[u] = fmaxf(mp[u], __uint_as_float(r[kN - 8 + u]));
+    return attn_max3(attn_max3(mp[0], mp[1], mp[2]), attn_max3(mp[3], mp[4], mp[5]), fmaxf(mp[6], mp[7]));
+  } else {
+    float mp[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) mp[u] = -INFINITY;
+#pragma unroll
+    for (int i = 0; i < kN; ++i)
+      if (kFull || i < valid) mp[i & 7] = fmaxf(mp[i & 7], __uint_as_float(r[i]));
+    return fmaxf(fmaxf(fmaxf(mp[0], mp[1]), fmaxf(mp[2], mp[3])), fmaxf(fmaxf(mp[4], mp[5]), fmaxf(mp[6], mp[7])));
+  }
+}
+
+// P = 2^(s c - m) for this thread's kN keys as f16 pairs into kN / 2 TMEM
 // columns of its lane from t_p (key 2 i in the low half of column i, the
 // layout the A-in-TMEM MMA reads); returns the f32 sum of the probabilities.
-template <bool kFull>
-__device__ __forceinline__ float attn_p_store(const uint32_t (&r)[64], int valid, float c, float m_use,
+template <int kN, bool kFull>
+__device__ __forceinline__ float attn_p_store(const uint32_t (&r)[kN], int valid, float c, float m_use,
                                               uint32_t t_p) {
-  float sp[8];
+  if constexpr (kFull) {
+    // s c - m two keys at a time, and four packed partial sums
+    const uint64_t c2 = attn_pack2(c, c), m2 = attn_pack2(-m_use, -m_use);
+    uint64_t acc[4] = {0, 0, 0, 0};  // zero bits: +0.0f in both lanes
 #pragma unroll
-  for (int u = 0; u < 8; ++u) sp[u] = 0.0f;
+    for (int cc = 0; cc < kN / 16; ++cc) {
+      uint32_t pk[8];
 #pragma unroll
-  for (int cc = 0; cc < 4; ++cc) {
-    uint32_t pk[8];
-#pragma unroll
-    for (int i = 0; i < 16; i += 2) {
-      const int k0 = cc * 16 + i;
-      const float p0 = (kFull || k0 < valid) ? attn_ex2(fmaf(__uint_as_float(r[k0]), c, -m_use)) : 0.0f;
-      const float p1 = (kFull || k0 + 1 < valid) ? attn_ex2(fmaf(__uint_as_float(r[k0 + 1]), c, -m_use)) : 0.0f;
-      sp[i >> 1] += p0 + p1;
-      const __half2 hp = __floats2half2_rn(p0, p1);
-      pk[i >> 1] = *reinterpret_cast<const uint32_t*>(&hp);
+      for (int i = 0; i < 16; i += 2) {
+        const int k0 = cc * 16 + i;
+        float x0, x1;
+        attn_unpack2(attn_fma2(attn_pack2(__uint_as_float(r[k0]), __uint_as_float(r[k0 + 1])), c2, m2), x0, x1);
+        const float p0 = attn_ex2(x0), p1 = attn_ex2(x1);
+        acc[(i >> 1) & 3] = attn_add2(acc[(i >> 1) & 3], attn_pack2(p0, p1));
+        const __half2 hp = __floats2half2_rn(p0, p1);
+        pk[i >> 1] = *reinterpret_cast<const uint32_t*>(&hp);
+      }
+      ptx::tmem_st_32x32b_x8(t_p + cc * 8, pk);
     }
-    ptx::tmem_st_32x32b_x8(t_p + cc * 8, pk);
+    float sum = 0.0f;
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      float lo, hi;
+      attn_unpack2(acc[u], lo, hi);
+      sum += lo + hi;
+    }
+    return sum;
+  } else {
+    float sp[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) sp[u] = 0.0f;
+#pragma unroll
+    for (int cc = 0; cc < kN / 16; ++cc) {
+      uint32_t pk[8];
+#pragma unroll
+      for (int i = 0; i < 16; i += 2) {
+        const int k0 = cc * 16 + i;
+        const float p0 = (kFull || k0 < valid) ? attn_ex2(fmaf(__uint_as_float(r[k0]), c, -m_use)) : 0.0f;
+        const float p1 = (kFull || k0 + 1 < valid) ? attn_ex2(fmaf(__uint_as_float(r[k0 + 1]), c, -m_use)) : 0.0f;
+        sp[i >> 1] += p0 + p1;
+        const __half2 hp = __floats2half2_rn(p0, p1);
+        pk[i >> 1] = *reinterpret_cast<const uint32_t*>(&hp);
+      }
+      ptx::tmem_st_32x32b_x8(t_p + cc * 8, pk);
+    }
+    return ((sp[0] + sp[1]) + (sp[2] + sp[3])) + ((sp[4] + sp[5]) + (sp[6] + sp[7]));
   }
-  return ((sp[0] + sp[1]) + (sp[2] + sp[3])) + ((sp[4] + sp[5]) + (sp[6] + sp[7]));
 }
 
 __global__ void __launch_bounds__(kAThreads, 1)
@@ -122,7 +194,7 @@ __global__ void __launch_bounds__(kAThreads, 1)
   uint8_t* qs = smem;
   uint8_t* ks = qs + kATileB;          // [kAKV] stages
   uint8_t* vs = ks + kAKV * kATileB;   // [kAKV] stages
-  float* xmax = reinterpret_cast<float*>(vs + kAKV * kATileB);  // [block parity][half][row]
+  float* xmax = reinterpret_cast<float*>(vs + kAKV * kATileB);  // [block parity][part][row]
   uint64_t* bars = reinterpret_cast<uint64_t*>(vs + kAKV * kATileB + kAXchg);
   uint64_t* q_full = bars;
   uint64_t* k_full = bars + 1;          // [kAKV]
@@ -153,11 +225,11 @@ __global__ void __launch_bounds__(kAThreads, 1)
     }
     for (int i = 0; i < 2; ++i) {
       ptx::mbar_init(&s_full[i], 1);
-      ptx::mbar_init(&s_free[i], 8);
+      ptx::mbar_init(&s_free[i], kASoftWarps);
       ptx::mbar_init(&p_free[i], 1);
     }
-    ptx::mbar_init(p_full, 8);
-    for (int i = 0; i < 4; ++i) ptx::mbar_init(&pair[i], 64);
+    ptx::mbar_init(p_full, kASoftWarps);
+    for (int i = 0; i < 4; ++i) ptx::mbar_init(&pair[i], kAParts);  // lane 0 of each part's warp
     *abort_flag = 0;
     ptx::fence_mbar_init();
   }
@@ -238,15 +310,15 @@ __global__ void __launch_bounds__(kAThreads, 1)
       }
     }
   } else if (warp >= 4) {
-    // ------------------------------------------------ softmax: two threads per query row
-    // Warps w and w + 4 share TMEM lane quarter w % 4 (rows 32 (w % 4) ..);
-    // the first takes score / output columns 0..63, the second 64..127.  Per
-    // block the halves post their max to shared memory and meet on pair[q],
-    // so both use the same row max; each keeps its own partial sum.
-    const int wq = warp - 4;
-    const int q = warp & 3, half = wq >> 2;
+    // ------------------------------------------------ softmax: kAParts threads per query row
+    // Warps w, w + 4, ... share TMEM lane quarter w % 4 (rows 32 (w % 4) ..);
+    // part p = (w - 4) / 4 takes score / output columns kACols p .. .  Per
+    // block the parts post their max to shared memory and meet on pair[q],
+    // so all use the same row max; each keeps its own partial sum.
+    const int q = warp & 3, part = (warp - 4) >> 2;
     const int row = q * 32 + lane;
-    const uint32_t t_lane = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(half * 64);
+    const uint32_t t_quarter = tmem + ((uint32_t)(q * 32) << 16);
+    const uint32_t t_lane = t_quarter + (uint32_t)(part * kACols);
     const float c = a.c;
     float m = -INFINITY, l = 0.0f;
     bool ok = true;
@@ -255,10 +327,10 @@ __global__ void __launch_bounds__(kAThreads, 1)
       ok = __all_sync(0xffffffffu, attn_wait(&s_full[st], (j >> 1) & 1, abort_flag, a.err));
       if (!ok) break;
       ptx::tc_fence_after();
-      const int valid = a.Skv - j * 128 - half * 64;  // keys of this half (may be <= 0)
-      uint32_t r[64];
+      const int valid = a.Skv - j * 128 - part * kACols;  // keys of this part (may be <= 0)
+      uint32_t r[kACols];
 #pragma unroll
-      for (int cc = 0; cc < 4; ++cc) {
+      for (int cc = 0; cc < kACols / 16; ++cc) {
         uint32_t (&rc)[16] = *reinterpret_cast<uint32_t(*)[16]>(r + cc * 16);
         ptx::tmem_ld_32x32b_x16(t_lane + st * 128 + cc * 16, rc);
       }
@@ -267,13 +339,17 @@ __global__ void __launch_bounds__(kAThreads, 1)
       ptx::tc_fence_before();
       __syncwarp();
       if (lane == 0) ptx::mbar_arrive(&s_free[st]);
-      const bool full = valid >= 64;  // warp-uniform: valid depends on the block and the half
-      const float pm = full ? attn_rowmax<true>(r, valid) : attn_rowmax<false>(r, valid);
-      xmax[(st * 2 + half) * 128 + row] = pm;
-      ptx::mbar_arrive(&pair[q]);
+      const bool full = valid >= kACols;  // warp-uniform: valid depends on the block and the part
+      const float pm = full ? attn_rowmax<kACols, true>(r, valid) : attn_rowmax<kACols, false>(r, valid);
+      xmax[(st * kAParts + part) * 128 + row] = pm;
+      __syncwarp();  // the warp's slots are written before its lane 0 arrives
+      if (lane == 0) ptx::mbar_arrive(&pair[q]);
       ok = __all_sync(0xffffffffu, attn_wait(&pair[q], j & 1, abort_flag, a.err));
       if (!ok) break;
-      const float mx = c * fmaxf(pm, xmax[(st * 2 + (half ^ 1)) * 128 + row]);
+      float rmax = pm;
+#pragma unroll
+      for (int p = 0; p < kAParts; ++p) rmax = fmaxf(rmax, xmax[(st * kAParts + p) * 128 + row]);
+      const float mx = c * rmax;
       const bool jump = j == 0 || mx > m + kRescaleLog2;
       const float m_use = jump ? fmaxf(m, mx) : m;
       const float alpha = (j > 0 && jump) ? exp2f(m - m_use) : 1.0f;
@@ -282,30 +358,29 @@ __global__ void __launch_bounds__(kAThreads, 1)
         ok = __all_sync(0xffffffffu, attn_wait(&p_free[st], ((j >> 1) - 1) & 1, abort_flag, a.err));
         if (!ok) break;
       }
-      // this half's 64 keys: 32 columns of P buffer j % 2
-      const uint32_t t_p = t_lane - (uint32_t)(half * 64) + kATmemP + (uint32_t)(st * 64 + half * 32);
-      const float psum = full ? attn_p_store<true>(r, valid, c, m_use, t_p)
-                              : attn_p_store<false>(r, valid, c, m_use, t_p);
+      // this part's keys: kACols / 2 columns of P buffer j % 2
+      const uint32_t t_p = t_quarter + kATmemP + (uint32_t)(st * 64 + part * (kACols / 2));
+      const float psum = full ? attn_p_store<kACols, true>(r, valid, c, m_use, t_p)
+                              : attn_p_store<kACols, false>(r, valid, c, m_use, t_p);
       if (j > 0 && __any_sync(0xffffffffu, jump)) {
         // O must hold P_{j-1} v_{j-1} before it is scaled (P_j v_j waits for p_full)
         ok = __all_sync(0xffffffffu, attn_wait(&p_free[(j - 1) & 1], ((j - 1) >> 1) & 1, abort_flag, a.err));
         if (!ok) break;
         ptx::tc_fence_after();
-        uint32_t o[64];
+        uint32_t o[kACols];
 #pragma unroll
-        for (int cc = 0; cc < 4; ++cc) {
+        for (int cc = 0; cc < kACols / 16; ++cc) {
           uint32_t (&oc)[16] = *reinterpret_cast<uint32_t(*)[16]>(o + cc * 16);
           ptx::tmem_ld_32x32b_x16(t_lane + kATmemO + cc * 16, oc);
         }
         ptx::tmem_ld_wait();
 #pragma unroll
-        for (int i = 0; i < 64; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+        for (int i = 0; i < kACols; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
 #pragma unroll
-        for (int cc = 0; cc < 4; ++cc) {
+        for (int cc = 0; cc < kACols / 16; ++cc) {
           const uint32_t (&oc)[16] = *reinterpret_cast<const uint32_t(*)[16]>(o + cc * 16);
           ptx::tmem_st_32x32b_x16(t_lane + kATmemO + cc * 16, oc);
         }
-        ptx::tmem_st_wait();
       }
       l = l * alpha + psum;
       m = m_use;
@@ -317,27 +392,31 @@ __global__ void __launch_bounds__(kAThreads, 1)
     // the last P v's commit covers every earlier MMA
     if (ok) ok = __all_sync(0xffffffffu, attn_wait(&p_free[(nblk - 1) & 1], ((nblk - 1) >> 1) & 1, abort_flag, a.err));
     if (ok) {
-      // the row's sum: both halves post theirs in the slot of block nblk (free:
-      // block nblk - 2 used it, and both halves have passed block nblk - 1)
-      xmax[((nblk & 1) * 2 + half) * 128 + row] = l;
-      ptx::mbar_arrive(&pair[q]);
+      // the row's sum: every part posts its own in the slot of block nblk (free:
+      // block nblk - 2 used it, and every part has passed block nblk - 1)
+      xmax[((nblk & 1) * kAParts + part) * 128 + row] = l;
+      __syncwarp();
+      if (lane == 0) ptx::mbar_arrive(&pair[q]);
       ok = __all_sync(0xffffffffu, attn_wait(&pair[q], nblk & 1, abort_flag, a.err));
     }
     if (ok) {
-      const float inv = 1.0f / (l + xmax[((nblk & 1) * 2 + (half ^ 1)) * 128 + row]);
+      float lsum = 0.0f;
+#pragma unroll
+      for (int p = 0; p < kAParts; ++p) lsum += xmax[((nblk & 1) * kAParts + p) * 128 + row];
+      const float inv = 1.0f / lsum;
       ptx::tc_fence_after();
       const int qrow = qt * 128 + row;
-      float* o = a.out + ((size_t)bh * a.Sq + qrow) * 128 + half * 64;
-      uint32_t r[64];
+      float* o = a.out + ((size_t)bh * a.Sq + qrow) * 128 + part * kACols;
+      uint32_t r[kACols];
 #pragma unroll
-      for (int cc = 0; cc < 4; ++cc) {
+      for (int cc = 0; cc < kACols / 16; ++cc) {
         uint32_t (&rc)[16] = *reinterpret_cast<uint32_t(*)[16]>(r + cc * 16);
         ptx::tmem_ld_32x32b_x16(t_lane + kATmemO + cc * 16, rc);
       }
       ptx::tmem_ld_wait();
       if (qrow < a.Sq) {
 #pragma unroll
-        for (int i = 0; i < 64; i += 4)
+        for (int i = 0; i < kACols; i += 4)
           *reinterpret_cast<float4*>(o + i) =
               make_float4(__uint_as_float(r[i]) * inv, __uint_as_float(r[i + 1]) * inv,
                           __uint_as_float(r[i + 2]) * inv, __uint_as_float(r[i + 3]) * inv);
