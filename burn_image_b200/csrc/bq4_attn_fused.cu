@@ -478,6 +478,17 @@ bool attn_tmap(CUtensorMap* m, const void* base, uint64_t cols, uint64_t rows, u
 
 }  // namespace
 
+// The fused kernel addresses rows of q ([B*Hq*Sq][128]) and k ([B*Hkv*Skv][128])
+// by 32-bit TMA coordinates, and the v transpose puts B*Hkv on grid z.
+bq4_status attn_fused_check(int64_t B, int64_t Hq, int64_t Hkv, int64_t Sq, int64_t Skv) {
+  constexpr int64_t kRowLimit = ((int64_t)1 << 31) - 256;
+  if (B * Hq * Sq > kRowLimit || B * Hkv * Skv > kRowLimit || B * Hkv > 65535)
+    return set_error(BQ4_EINVAL_SHAPE,
+                     "fused attention: B*Hq*Sq=%lld and B*Hkv*Skv=%lld must be < 2^31 - 256, B*Hkv=%lld <= 65535",
+                     (long long)(B * Hq * Sq), (long long)(B * Hkv * Skv), (long long)(B * Hkv));
+  return BQ4_OK;
+}
+
 size_t attn_fused_workspace(int64_t B, int64_t Hkv, int64_t Skv) {
   const int64_t pitch = (Skv + 127) / 128 * 128;
   return (size_t)(B * Hkv * 128 * pitch * 2 + 255) / 256 * 256;

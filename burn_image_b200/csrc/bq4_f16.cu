@@ -770,6 +770,7 @@ bq4_status bq4_packed_f16_conv2d(const float* input, int64_t batch, int64_t in_c
 namespace bq4 {
 // fused attention for head_dim 128 (bq4_attn_fused.cu)
 size_t attn_fused_workspace(int64_t B, int64_t Hkv, int64_t Skv);
+bq4_status attn_fused_check(int64_t B, int64_t Hq, int64_t Hkv, int64_t Sq, int64_t Skv);
 bq4_status attn_fused(const uint16_t* q, const uint16_t* k, const uint16_t* v, int64_t B, int64_t Hq, int64_t Hkv,
                       int64_t Sq, int64_t Skv, float scale, float* out, void* workspace, cudaStream_t s);
 }  // namespace bq4
@@ -827,6 +828,10 @@ bq4_status bq4_attention_workspace_size(int64_t B, int64_t Hq, int64_t Hkv, int6
   GemmPlan ps, pv;
   st = attn_layout(Sq, Skv, D, dev, &L, &ps, &pv);
   if (st) return st;
+  if (attn_use_fused(D)) {
+    st = attn_fused_check(B, Hq, Hkv, Sq, Skv);
+    if (st) return st;
+  }
   *bytes = attn_use_fused(D) ? attn_fused_workspace(B, Hkv, Skv) : L.total;
   return BQ4_OK;
 }
@@ -847,6 +852,10 @@ bq4_status bq4_attention(const uint32_t* q, const uint32_t* k, const uint32_t* v
   st = attn_layout(Sq, Skv, D, dev, &L, &ps, &pv);
   if (st) return st;
   const bool fused = attn_use_fused(D);
+  if (fused) {
+    st = attn_fused_check(B, Hq, Hkv, Sq, Skv);
+    if (st) return st;
+  }
   const size_t need = fused ? attn_fused_workspace(B, Hkv, Skv) : L.total;
   if (!workspace || workspace_bytes < need)
     return set_error(BQ4_EWORKSPACE, "workspace %zu < required %zu bytes", workspace_bytes, need);

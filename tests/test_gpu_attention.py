@@ -98,3 +98,7 @@ def test_argument_checks():
     k6 = torch.zeros((1, 2, 8, 6), device=DEV).half()
     with pytest.raises(Bq4Error, match="EINVAL_SHAPE"):
         F.attention(q6, k6, k6)  # head_dim not a multiple of 4
+    # the fused kernel's limits (32-bit row coordinates, B*Hkv on grid z) are checked before any launch
+    qw = torch.zeros((1, 65536, 1, 128), device=DEV).half()
+    with pytest.raises(Bq4Error, match="EINVAL_SHAPE"):
+        F.attention(qw, qw, qw)  # B*Hkv = 65536
