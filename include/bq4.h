@@ -521,8 +521,9 @@ BQ4_API bq4_status bq4_packed_f16_conv2d(const float* input, int64_t batch, int6
  * reads kv head h / (Hq / Hkv) (grouped-query attention, Hq % Hkv == 0).
  * out f32 [B][Hq][Sq][D], 16-byte aligned.  scale <= 0 means 1/sqrt(D).
  * D % 4 == 0; q, k, v 16-byte aligned.  D = 128 runs one fused kernel
- * (scores in TMEM, softmax in registers, P through shared memory, O in
- * TMEM; v transposed once into the workspace).  Other D run unfused: per
+ * (scores, P and O in TMEM, softmax in registers; v transposed once into
+ * the workspace); it needs B*Hq*Sq and B*Hkv*Skv below 2^31 - 256 and
+ * B*Hkv <= 65535, else BQ4_EINVAL_SHAPE from both calls.  Other D run unfused: per
  * head the scores q k^T and P v as tf32 GEMMs (k and v widened into the
  * weight tiles, q and the f32 scores read in place) with a row softmax
  * between them.  The environment variable BQ4_ATTN_UNFUSED=1 selects the
