@@ -415,13 +415,34 @@ def _select_row(dev, n, cols, rows, hbm):
             "frac": t_star / t, "sets": sets}
 
 
+def _attn_cpu_arm(S, D, rows=256):
+    """The oracle's attention (f64, all host threads) on one head: `rows`
+    query rows against all S keys; TFLOP/s of the 4 rows S D FLOPs."""
+    import time
+
+    import numpy as np
+
+    import oracle as O
+    rng = np.random.default_rng(5)
+    rows = min(rows, S)
+    q = (rng.standard_normal((1, 1, rows, D)) * 0.5).astype(np.float16).astype(np.float32)
+    k = (rng.standard_normal((1, 1, S, D)) * 0.5).astype(np.float16).astype(np.float32)
+    v = rng.standard_normal((1, 1, S, D)).astype(np.float16).astype(np.float32)
+    O.attention_f64(q[:, :, :8], k, v)
+    t0 = time.perf_counter()
+    O.attention_f64(q, k, v)
+    dt = time.perf_counter() - t0
+    return {"tflops": 4.0 * rows * S * D / dt / 1e12, "cores": O.cpu_threads(), "kind": "port",
+            "sample": f"1 head, {rows} of {S} query rows"}
+
+
 def _attn_row(dev, S, D, H, hbm, tfl):
     """Attention row: softmax(q k^T / sqrt(D)) v over H heads of S tokens,
     f16 q/k/v, f32 out, graph-replayed on two input sets.  head_dim 128 runs
     the fused kernel (f16 MMAs): roofline = the measured bf16 burst peak for
     the 4 S^2 D H FLOPs against q, k, v read once and out written once.  It
     also needs S^2 H exponentials, which bound it before the tensor core
-    does."""
+    does.  cpu: the oracle's attention on a one-head sample."""
     import torch
 
     from burn_image_b200 import f16 as F
@@ -444,9 +465,14 @@ def _attn_row(dev, S, D, H, hbm, tfl):
     t_star = max(nbytes / (hbm * 1e9), flops / (tfl * 1e12))
     del items
     torch.cuda.empty_cache()
-    return {"us": t * 1e6, "tflops": flops / t / 1e12, "gbs": nbytes / t / 1e9, "bound": "tensor",
-            "t_star_us": t_star * 1e6, "frac": t_star / t, "peak_tflops": tfl, "kernel": "fused (f16 MMA)",
-            "exp_per_s": H * S * S / t, "sets": 2}
+    row = {"us": t * 1e6, "tflops": flops / t / 1e12, "gbs": nbytes / t / 1e9, "bound": "tensor",
+           "t_star_us": t_star * 1e6, "frac": t_star / t, "peak_tflops": tfl, "kernel": "fused (f16 MMA)",
+           "exp_per_s": H * S * S / t, "sets": 2}
+    try:
+        row["cpu"] = _attn_cpu_arm(S, D)
+    except Exception as e:  # noqa: BLE001 -- the CPU arm is informational
+        row["cpu"] = {"tflops": None, "sample": f"failed: {e}"}
+    return row
 
 
 def _f16_row(dev, kind, M, K, N, hbm, tfl):
