@@ -70,7 +70,7 @@ def _worker(rank, world, port, layout, results):
 @pytest.mark.parametrize("layout", [0, 1])
 def test_tensor_parallel_decomposition_gloo(layout):
     world = 2
-    with mp.Manager() as mgr:
+    with mp.get_context("spawn").Manager() as mgr:  # no fork of this multi-threaded process
         results = mgr.dict()
         mp.spawn(_worker, args=(world, _free_port(), layout, results), nprocs=world, join=True)
         res = dict(results)
