@@ -21,6 +21,7 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <cstring>
 
 #include "bq4_internal.h"
@@ -452,14 +453,14 @@ typedef CUresult (*EncodeFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void
                              CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 
 EncodeFn attn_encode_fn() {
-  static EncodeFn fn = nullptr;
-  if (!fn) {
+  static const EncodeFn fn = [] {
     void* p = nullptr;
     cudaDriverEntryPointQueryResult q;
     if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
         q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<EncodeFn>(p);
-  }
+      return reinterpret_cast<EncodeFn>(p);
+    return static_cast<EncodeFn>(nullptr);
+  }();
   return fn;
 }
 
@@ -517,13 +518,13 @@ bq4_status attn_fused(const uint16_t* q, const uint16_t* k, const uint16_t* v, i
   a.nblk = (int)((Skv + 127) / 128);
   a.c = scale * 1.4426950408889634f;  // log2(e): exp(x) = exp2(x log2 e)
   a.err = device_error_word();
-  static bool attr_set[64] = {false};
+  static std::atomic<bool> attr_set[64];  // per-device function attribute, set once
   int dev = 0;
   cudaGetDevice(&dev);
-  if (dev >= 0 && dev < 64 && !attr_set[dev]) {
+  if (dev < 0 || dev >= 64 || !attr_set[dev].load(std::memory_order_relaxed)) {
     e = cudaFuncSetAttribute(attn_fused_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kASmem);
     if (e != cudaSuccess) return check_cuda(e, "attention shared-memory attribute");
-    attr_set[dev] = true;
+    if (dev >= 0 && dev < 64) attr_set[dev].store(true, std::memory_order_relaxed);
   }
   attn_fused_kernel<<<(unsigned)(B * Hq * a.qtiles), kAThreads, kASmem, s>>>(tq, tk, tvt, a);
   note_launch();

@@ -1121,16 +1121,15 @@ typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t,
                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 
 EncodeTiledFn encode_fn() {
-  static EncodeTiledFn fn = nullptr;
-  static bool tried = false;
-  if (!tried) {
-    tried = true;
+  // a function-local static: initialised once, and no caller sees it before that ends
+  static const EncodeTiledFn fn = [] {
     void* p = nullptr;
     cudaDriverEntryPointQueryResult q;
     if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
         q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<EncodeTiledFn>(p);
-  }
+      return reinterpret_cast<EncodeTiledFn>(p);
+    return static_cast<EncodeTiledFn>(nullptr);
+  }();
   return fn;
 }
 
@@ -1144,14 +1143,14 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 
 template <int BT, int NW, bool TA, bool QK = false, bool SC = false, bool CV = false, bool TF = false>
 cudaError_t prepare_ws_kernel(size_t smem_bytes, bool* ok_regs) {
   auto kern = q4_gemm_ws_kernel<BT, NW, TA, QK, SC, CV, TF>;
-  static int checked = 0;  // 0 unknown, 1 ok, -1 bad
-  if (checked == 0) {
+  static std::atomic<int> checked{0};  // 0 unknown, 1 ok, -1 bad
+  if (checked.load(std::memory_order_relaxed) == 0) {
     cudaFuncAttributes attr;
     cudaError_t e = cudaFuncGetAttributes(&attr, kern);
     if (e != cudaSuccess) return e;
-    checked = (attr.numRegs == kWsRegsLaunch) ? 1 : -1;
+    checked.store((attr.numRegs == kWsRegsLaunch) ? 1 : -1, std::memory_order_relaxed);
   }
-  *ok_regs = checked == 1;
+  *ok_regs = checked.load(std::memory_order_relaxed) == 1;
   // the shared-memory opt-in is a per-device function attribute
   static std::atomic<size_t> smem_set[64];
   int dev = 0;
@@ -1302,15 +1301,15 @@ int sm_budget() {
 void set_sm_budget(int sms) { g_sm_budget.store(sms > 0 ? sms : 0, std::memory_order_relaxed); }
 
 int device_sm_count(int device) {
-  static int cache[64] = {0};
+  static std::atomic<int> cache[64];
   if (device < 0 || device >= 64) return 148;
-  if (!cache[device]) {
-    int v = 0;
+  int v = cache[device].load(std::memory_order_relaxed);
+  if (!v) {
     if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, device) != cudaSuccess || v <= 0)
       v = 148;
-    cache[device] = v;
+    cache[device].store(v, std::memory_order_relaxed);
   }
-  return cache[device];
+  return v;
 }
 
 int device_is_sm100(int device) {
