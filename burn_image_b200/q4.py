@@ -495,6 +495,8 @@ def q_matmul(lhs: torch.Tensor, rhs: QuantizedTensor) -> torch.Tensor:
     Goes through the C ABI entry ``bq4_q_matmul`` (prepare + GEMM per call)."""
     if lhs.dtype != torch.float32:
         raise Bq4Error(L.EINVAL_ARG, f"lhs dtype {lhs.dtype} is not F32")
+    if not (lhs.is_cuda and rhs.values.is_cuda and rhs.scales.is_cuda):
+        raise Bq4Error(L.EINVAL_ARG, "q_matmul runs on the GPU only: lhs and the packed rhs must be CUDA tensors")
     if not rhs.scheme.eligible():
         raise Bq4Error(L.EINVAL_ARG, f"scheme {rhs.scheme} is not eligible for the packed-Q4 kernel")
     K, N = rhs.shape
