@@ -206,7 +206,7 @@ __global__ void __launch_bounds__(kAThreads, 1)
   uint64_t* s_free = s_full + 2;        // [2]
   uint64_t* p_full = s_free + 2;
   uint64_t* p_free = p_full + 1;  // [2]: P_j v_j has completed (P buffer j % 2 free, O holds it)
-  uint64_t* pair = p_free + 2;    // [4]: both softmax warps of a lane quarter have posted their half's max
+  uint64_t* pair = p_free + 2;    // [4]: every softmax warp of a lane quarter has posted its part's max
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(pair + 4);  // 24 barriers: 192 of the 256 bytes
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -241,7 +241,7 @@ __global__ void __launch_bounds__(kAThreads, 1)
   ptx::tc_fence_before();
   __syncthreads();
   ptx::tc_fence_after();
-  const uint32_t tmem = *tmem_slot;  // S buffers at columns 0 and 128, O at 256
+  const uint32_t tmem = *tmem_slot;  // S buffers at columns 0 and 128, O at 256, P buffers at 384 and 448
 
   if (warp == 0) {
     if (lane == 0) {
