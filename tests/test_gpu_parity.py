@@ -322,9 +322,15 @@ def test_error_status_on_bad_args(rng):
     pw = q4.PreparedQ4Weight(dev(w), dev(s), K, N, 128, O.LAYOUT_ROW, DEV)
     x = dev(gen_x(4, K, rng))
     y = torch.empty((4, N), dtype=torch.float32, device=DEV)
-    ws = q4.Workspace.get(DEV, pw.workspace_bytes(4))
     lib = L.lib()
-    assert lib.bq4_linear(pw.handle, p(x), 4, K, None, 0, None, p(y), p(ws), 16, stream()) == L.EWORKSPACE
+    import os
+    os.environ["BQ4_NO_SKINNY"] = "1"  # the tcgen05 plan, which needs a workspace (the few-token one needs none)
+    try:
+        ws = q4.Workspace.get(DEV, pw.workspace_bytes(4))
+        assert pw.workspace_bytes(4) > 16
+        assert lib.bq4_linear(pw.handle, p(x), 4, K, None, 0, None, p(y), p(ws), 16, stream()) == L.EWORKSPACE
+    finally:
+        os.environ.pop("BQ4_NO_SKINNY", None)
     assert lib.bq4_linear(pw.handle, p(x), 0, K, None, 0, None, p(y), p(ws), ws.numel(), stream()) == L.EINVAL_SHAPE
     assert lib.bq4_linear(pw.handle, p(x), 4, K - 8, None, 0, None, p(y), p(ws), ws.numel(), stream()) == L.EINVAL_SHAPE
     assert lib.bq4_linear(pw.handle, p(x), 4, K, None, 9, None, p(y), p(ws), ws.numel(), stream()) == L.EINVAL_ARG
@@ -333,11 +339,15 @@ def test_error_status_on_bad_args(rng):
 
 # ---------------------------------------------------------------- BASELINE sizes: torch fp32 reference
 
-@pytest.mark.parametrize("M,K,N,act", [(256, 2560, 2560, 0), (256, 9728, 2560, 0), (4352, 3072, 12288, 1),
-                                       (4352, 12288, 3072, 0)])
+@pytest.mark.parametrize("M,K,N,act", [(256, 2560, 2560, 0), (256, 2560, 512, 0), (256, 9728, 2560, 0),
+                                       (512, 2560, 9728, 0), (4352, 3072, 12288, 1), (4352, 12288, 3072, 0),
+                                       (18432, 3072, 9216, 0), (18432, 3072, 3072, 0)])
 def test_baseline_shapes_vs_torch_fp32(M, K, N, act):
-    """Full BASELINE shapes against a plain PyTorch fp32 reference of the same
-    op on the device (dequantized by the bit-exact kernel)."""
+    """Full BASELINE shapes against a PyTorch fp64 product of the same op on
+    the device (weights dequantized by the bit-exact kernel): configs 1-3 and
+    the 1536 px edit projections of config 4 (fused qkv 18432 x 3072 -> 9216,
+    o 18432 x 3072 -> 3072), which have more token tiles and different
+    split / stream-K plans than any smaller case."""
     g = torch.Generator(device=DEV).manual_seed(M * 7 + N)
     words = torch.randint(-2 ** 31, 2 ** 31 - 1, (K // 8, N), generator=g, device=DEV, dtype=torch.int64).to(torch.int32)
     scales = (torch.rand((K // 128, N), generator=g, device=DEV) * 0.019 + 0.001).contiguous()
@@ -353,3 +363,30 @@ def test_baseline_shapes_vs_torch_fp32(M, K, N, act):
     rf = (torch.linalg.norm((y.double() - ref)) / torch.linalg.norm(ref)).item()
     print(f"baseline M{M} K{K} N{N}: rel_frob={rf:.3e} max_abs={(y.double() - ref).abs().max().item():.3e}")
     assert rf <= TOL
+
+
+def test_baseline_gated_pair_vs_torch_fp64():
+    """Config 2's fused gate+up pair at full size (M=256, K=2560, N=2 x 9728,
+    SiLU(gate) * up, crates/burn_qwen3_vl/src/text.rs:46-52) against an fp64
+    product of the bit-exact dequantized weights."""
+    M, K, N = 256, 2560, 9728
+    g = torch.Generator(device=DEV).manual_seed(97281)
+    ws = []
+    for _ in range(2):
+        words = torch.randint(-2 ** 31, 2 ** 31 - 1, (N, K // 8), generator=g, device=DEV,
+                              dtype=torch.int64).to(torch.int32).contiguous()
+        scales = (torch.rand((N, K // 128), generator=g, device=DEV) * 0.019 + 0.001).contiguous()
+        ws.append(q4.PreparedQ4Weight(words, scales, K, N, 128, L.LAYOUT_COL, DEV))
+    x = torch.randn((M, K), generator=g, device=DEV)
+    bg = torch.randn(N, generator=g, device=DEV) * 0.02
+    bu = torch.randn(N, generator=g, device=DEV) * 0.02
+    y = q4.linear_gated(ws[0], ws[1], x, bg, bu)
+    q4.poll_device_error()
+    xd = x.double()
+    gate = torch.addmm(bg.double(), xd, ws[0].dequantize().double())
+    up = torch.addmm(bu.double(), xd, ws[1].dequantize().double())
+    ref = torch.nn.functional.silu(gate) * up
+    rf = (torch.linalg.norm(y.double() - ref) / torch.linalg.norm(ref)).item()
+    print(f"gated pair M{M} K{K} N2x{N}: rel_frob={rf:.3e} max_abs={(y.double() - ref).abs().max().item():.3e}")
+    assert rf <= TOL
+    assert torch.equal(y, q4.linear_gated(ws[0], ws[1], x, bg, bu))  # repeat calls: same bits
