@@ -299,10 +299,10 @@ bq4_status bq4_linear_plan_info(const bq4_weight* w, int64_t M, int32_t gated, i
   GemmPlan plan;
   st = plan_gemm(w, gated ? 2 : 1, M, w->device, &plan);
   if (st) return st;
-  const int32_t v[12] = {plan.bt, plan.ksplit, plan.grid, plan.exact, plan.ta, plan.stages, plan.sk_tiles,
+  const int32_t v[13] = {plan.bt, plan.ksplit, plan.grid, plan.exact, plan.ta, plan.stages, plan.sk_tiles,
                          plan.dp_tiles, (int32_t)(plan.workspace_bytes / 256), plan.wide, plan.tail_tiles,
-                         plan.tail_split};
-  for (int32_t i = 0; i < n && i < 12; ++i) info[i] = v[i];
+                         plan.tail_split, plan.skinny};
+  for (int32_t i = 0; i < n && i < 13; ++i) info[i] = v[i];
   return BQ4_OK;
 }
 
@@ -629,6 +629,11 @@ bq4_status bq4_peer_signal_wait(uint32_t* flags, uint32_t* const* peer_flags, in
   cudaError_t e = launch_peer_signal_wait(flags, peer_flags, nranks, rank, epoch, device_error_word(),
                                           reinterpret_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? BQ4_OK : check_cuda(e, "peer signal/wait launch");
+}
+
+bq4_status bq4_set_peer_wait_timeout_ns(uint64_t ns) {
+  set_peer_wait_ns(ns);
+  return BQ4_OK;
 }
 
 bq4_status bq4_reduce_slices(const float* recv, int32_t nranks, int64_t rows, int64_t H, int64_t ld, int32_t renorm,

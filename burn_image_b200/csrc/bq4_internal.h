@@ -81,6 +81,8 @@ cudaError_t launch_zero_flags(unsigned* flags, int nflags, cudaStream_t s);
 // Tensor-parallel exchange over peer memory (bq4_peer.cu).
 cudaError_t launch_peer_signal_wait(unsigned* local, unsigned* const* peers, int nranks, int rank, unsigned epoch,
                                     int* err, cudaStream_t s);
+// Bound of the peer signal/wait in ns for launches after the call (0 = the 10 s default).
+void set_peer_wait_ns(uint64_t ns);
 cudaError_t launch_reduce_slices(const float* recv, int P, int64_t R, int64_t H, int64_t ld, int renorm, float eps,
                                  void* out, int out_f16, int64_t ldo, cudaStream_t s);
 // QK-norm + RoPE over `heads` heads of hd (even, <= 256) per token; cos/sin
@@ -100,6 +102,23 @@ int* device_error_word();
 // Per-row RMS renormalisation (the layer-stack workload's between-block step).
 cudaError_t launch_rms_renorm(const void* x, int x_f16, int64_t M, int64_t H, int64_t ldx, void* out,
                               int out_f16, int64_t ldo, float eps, cudaStream_t s);
+
+// ------------------------------------------------------------ small-M linear (bq4_skinny.cu)
+// Launch plan of the few-token kernel: 8 * nt tokens per CTA (gz token
+// groups), one 128-row weight tile per CTA (gx CTAs along N; R = 8 row
+// groups), ks CTAs per cluster splitting K, a ring of `stages` 128-K weight
+// stages per CTA.  It needs no workspace.
+constexpr int64_t kSkMaxM = 256;             // calls above this many rows always use the tcgen05 GEMM
+constexpr int64_t kSkAutoMaxM = 16;          // the planner's default: the few-token kernel up to this many rows
+constexpr size_t kSkMaxSmem = 200 * 1024;    // dynamic shared memory limit of one CTA
+struct SkPlan {
+  int nt, nw, R, ks, gx, gz, exact, pdl, stages;
+  size_t smem_bytes;
+};
+// false when the weight or numerics do not fit the kernel (pre-expanded or
+// packed-F16 weights, exact numerics with blocks other than 128, M above
+// kSkMaxM, shared memory).
+bool plan_skinny(const bq4_weight* w, int nw, int64_t M, int device, bool exact, SkPlan* p);
 
 // ------------------------------------------------------------ GEMM (bq4_gemm_sm100.cu)
 struct GemmPlan {
@@ -130,6 +149,8 @@ struct GemmPlan {
   size_t partial_bytes;    // workspace part 1: split-K partial tiles (0 without split)
   size_t xh_bytes;         // workspace part 2: the f16 copy of x (unused with f16 x)
   size_t workspace_bytes;
+  int skinny;              // 1: the few-token kernel runs the call (plan in sk; no workspace)
+  SkPlan sk;
 };
 
 // allow_sk = false plans without the stream-K tail (smaller workspace);
@@ -176,6 +197,11 @@ struct GemmIo {
 bq4_status run_gemm(const GemmPlan& plan, const bq4_weight* const* ws, const void* x, int64_t M,
                     int64_t ldx, const float* const* bias, int act, const float* aux, void* y,
                     void* workspace, cudaStream_t stream, const GemmIo& io = GemmIo());
+
+// The few-token kernel (bq4_skinny.cu) for a plan with skinny = 1.
+bq4_status run_skinny(const SkPlan& p, const bq4_weight* const* ws, const void* x, int x_f16, int64_t M, int64_t ldx,
+                      const float* const* bias, int act, const float* aux, void* y, int y_f16, int64_t ldy,
+                      const GemmIo& io, cudaStream_t stream);
 
 // Operand staging policy (bq4_numerics); AUTO keeps exact weights up to
 // this many rows: the reference's own kernel test at M = 1 asks for a

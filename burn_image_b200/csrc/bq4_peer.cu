@@ -14,6 +14,7 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <cstring>
 
 #include "bq4_internal.h"
@@ -22,7 +23,8 @@
 namespace bq4 {
 namespace {
 
-constexpr uint64_t kPeerWaitNs = 10000000000ull;  // 10 s: ranks enqueue at their own pace
+constexpr uint64_t kPeerWaitNs = 10000000000ull;  // default 10 s: ranks enqueue at their own pace
+std::atomic<uint64_t> g_peer_wait_ns{kPeerWaitNs};
 
 __device__ __forceinline__ void st4(float* p, float4 v) { *reinterpret_cast<float4*>(p) = v; }
 __device__ __forceinline__ void st4(__half* p, float4 v) {  // round to nearest even, as the staging kernel
@@ -40,7 +42,7 @@ struct PeerFlags {
 // reads the flag with acquire), then wait until every peer has published
 // `epoch` into this rank's own array.
 __global__ void peer_signal_wait_kernel(unsigned* local, PeerFlags peers, int nranks, int rank, unsigned epoch,
-                                        int* err) {
+                                        uint64_t limit_ns, int* err) {
   if (threadIdx.x != 0 || blockIdx.x != 0) return;
   __threadfence_system();
   for (int r = 0; r < nranks; ++r)
@@ -53,7 +55,7 @@ __global__ void peer_signal_wait_kernel(unsigned* local, PeerFlags peers, int nr
       unsigned v;
       asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(local + r) : "memory");
       if ((int)(v - epoch) >= 0) break;
-      if (ptx::globaltimer() - t0 > kPeerWaitNs) {
+      if (ptx::globaltimer() - t0 > limit_ns) {
         if (err) atomicExch(err, (int)BQ4_ETIMEOUT);
         return;
       }
@@ -114,12 +116,15 @@ __global__ void reduce_slices_kernel(const float* __restrict__ recv, int P, int6
 
 }  // namespace
 
+void set_peer_wait_ns(uint64_t ns) { g_peer_wait_ns.store(ns ? ns : kPeerWaitNs, std::memory_order_relaxed); }
+
 cudaError_t launch_peer_signal_wait(unsigned* local, unsigned* const* peers, int nranks, int rank, unsigned epoch,
                                     int* err, cudaStream_t s) {
   PeerFlags pf;
   memset(&pf, 0, sizeof(pf));
   for (int r = 0; r < nranks && r < BQ4_MAX_PEERS; ++r) pf.p[r] = peers[r];
-  peer_signal_wait_kernel<<<1, 32, 0, s>>>(local, pf, nranks, rank, epoch, err);
+  peer_signal_wait_kernel<<<1, 32, 0, s>>>(local, pf, nranks, rank, epoch,
+                                           g_peer_wait_ns.load(std::memory_order_relaxed), err);
   note_launch();
   return cudaGetLastError();
 }

@@ -128,14 +128,18 @@ BQ4_API bq4_status bq4_linear_workspace_size(const bq4_weight* w, int64_t M, siz
 
 /*
  * The launch plan bq4_linear uses for this weight and M (diagnostics and
- * tests).  Writes min(n, 12) values to info: token tile (64/128/256),
+ * tests).  Writes min(n, 13) values to info: token tile (64/128/256; the
+ * tokens per CTA, 8..64, for the few-token kernel),
  * split-K factor (1 = none), grid size, exact numerics (0/1), weight tile in
  * TMEM (0/1), operand-ring stages, stream-K tiles (0 = whole tiles only),
  * whole tiles before them, workspace bytes / 256, 1 when a packed-F16
  * weight runs on 256 x 256 tiles (two N tiles per token tile), and the
  * split-K tail: tiles of the partial last wave run in a second launch, each
- * cut into the given number of K ranges (0, 0 = none).  gated = 1 plans the
- * SiLU-gated pair (bq4_linear_gated) with `w` as both weights.
+ * cut into the given number of K ranges (0, 0 = none), and 1 when the
+ * few-token kernel runs the call (weights streamed from HBM into registers,
+ * mma.sync tensor-core steps, split-K partials summed within a thread-block
+ * cluster; no workspace).  gated = 1 plans the SiLU-gated pair
+ * (bq4_linear_gated) with `w` as both weights.
  */
 BQ4_API bq4_status bq4_linear_plan_info(const bq4_weight* w, int64_t M, int32_t gated, int32_t* info,
                                         int32_t n);
@@ -210,15 +214,21 @@ BQ4_API bq4_status bq4_dequant_raw(const uint32_t* packed_words, const float* sc
  * allocator.  Some callers of this library have no way to hand it a
  * workspace -- a runtime whose allocator owns all device memory, code that
  * must not call the (device-synchronizing) cudaMalloc, or a process that may
- * not grow its device footprint after start-up.  This entry point computes
- * exactly what bq4_linear computes, with its scratch in a static device
- * array of BQ4_NOALLOC_SCRATCH_BYTES that every GPU loading the library
- * holds until exit; it allocates nothing.  When bq4_linear's workspace for
- * the same weight and M exceeds that size it plans without the stream-K
- * tail (whose partial slots need workspace); calls whose scratch need still
- * exceeds it return BQ4_EWORKSPACE.  The first call on a device looks up the array's
- * device address, so make it before any stream capture.  All calls on a
- * device share the array: calls that overlap on the GPU race.
+ * not grow its device footprint after start-up.  This entry point runs the
+ * GEMM of bq4_linear with its scratch in a static device array of
+ * BQ4_NOALLOC_SCRATCH_BYTES that every GPU loading the library holds until
+ * exit; it allocates nothing.  When bq4_linear's workspace for the same
+ * weight and M fits that size, both run the same plan and the result is
+ * bit-identical to bq4_linear's.  When it does not fit because of the
+ * stream-K tail (whose partial slots need workspace), this call plans whole
+ * tiles instead: the tiling then differs and the result agrees with
+ * bq4_linear's within the parity tolerance, not bit for bit.  Calls whose
+ * scratch need still exceeds the array return BQ4_EWORKSPACE.  The first
+ * call on a device looks up the array's device address, so make it before
+ * any stream capture.  The address is cached for the life of the process:
+ * do not call this entry point after a cudaDeviceReset (or any other
+ * teardown of the device's primary context) in the same process.  All calls
+ * on a device share the array: calls that overlap on the GPU race.
  */
 #define BQ4_NOALLOC_SCRATCH_BYTES (32u << 20)
 BQ4_API bq4_status bq4_linear_noalloc(const bq4_weight* w, const float* x, int64_t M, int64_t ldx,
@@ -412,6 +422,12 @@ BQ4_API bq4_status bq4_peer_buffer_free(void* ptr, int32_t device);
  * mapped here (peer_flags[rank] may be `flags`).  epoch grows by one per use. */
 BQ4_API bq4_status bq4_peer_signal_wait(uint32_t* flags, uint32_t* const* peer_flags, int32_t nranks, int32_t rank,
                                         uint32_t epoch, bq4_stream_t stream);
+/* Bound of bq4_peer_signal_wait for launches enqueued after this call, in
+ * nanoseconds of the GPU's global timer, process-wide; 0 restores the 10 s
+ * default.  A wait that runs out records BQ4_ETIMEOUT in the device error word
+ * (bq4_poll_device_error) and its kernel returns.  No counterpart in the
+ * reference, which has no cross-GPU wait. */
+BQ4_API bq4_status bq4_set_peer_wait_timeout_ns(uint64_t ns);
 /* out[r] = sum_s recv[s][r] (s = 0..nranks-1 in order) for rows r < rows of
  * H floats (recv pitch ld, H % 4 == 0, H <= 8192, 16-byte aligned), then
  * x / sqrt(mean(x^2) + eps) per row when renorm; out f32 or f16 at pitch ldo. */
