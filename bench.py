@@ -218,6 +218,12 @@ def run_reference(args):
 # "linear" = one fused linear (+bias), "gated" = silu(x.Wg+bg)*(x.Wu+bu).
 ROWS = [
     ("c1_cpu_linear_512x2560x9728", 512, 2560, 9728, "linear", 0),
+    # decode-shaped rows of the text encoder's largest projection (north star: the
+    # bandwidth-bound path for few tokens), where HBM is the binding roof
+    ("d_decode_1x2560x9728", 1, 2560, 9728, "linear", 0),
+    ("d_decode_16x2560x9728", 16, 2560, 9728, "linear", 0),
+    ("d_decode_gate_up_silu_16x2560x2x9728", 16, 2560, 9728, "gated", 0),
+    ("d_decode_down_16x9728x2560", 16, 9728, 2560, "linear", 0),
     ("c2_text_qo_256x2560x2560", 256, 2560, 2560, "linear", 0),
     ("c2_text_kv_256x2560x512", 256, 2560, 512, "linear", 0),
     ("c2_text_gate_up_silu_256x2560x2x9728", 256, 2560, 9728, "gated", 0),
@@ -345,6 +351,14 @@ def config_rows(dev, peaks, names=None):
             q4.qk_norm_rope(y[:, :heads * hd], heads, hd, gq, 1e-5, cs, sn, out=y[:, :heads * hd])
 
         t = _graph_time(dev, items, call)
+        t_gemm = None
+        if M <= 256 and kind in ("linear", "gated"):
+            # the same calls on the tcgen05 GEMM (the few-token kernel switched off)
+            os.environ["BQ4_NO_SKINNY"] = "1"
+            try:
+                t_gemm = _graph_time(dev, items, call)
+            finally:
+                os.environ.pop("BQ4_NO_SKINNY", None)
         t_unfused = _graph_time(dev, items, call_unfused) if kind == "qknorm" else None
         t_norm = _graph_time(dev, items, call_norm) if kind == "qknorm" else None
         q4.poll_device_error()
@@ -353,7 +367,10 @@ def config_rows(dev, peaks, names=None):
         t_star = max(nbytes / (hbm * 1e9), flops / (tfl * 1e12))
         bound = "hbm" if nbytes / (hbm * 1e9) > flops / (tfl * 1e12) else "tensor"
         out[name] = {"us": t * 1e6, "tflops": flops / t / 1e12, "gbs": nbytes / t / 1e9, "bound": bound,
-                     "t_star_us": t_star * 1e6, "frac": t_star / t, "sets": sets}
+                     "t_star_us": t_star * 1e6, "frac": t_star / t, "sets": sets,
+                     "kernel": "few-token (mma.sync)" if ws_plan_skinny(items[0][0][0], M, nw) else "tcgen05 GEMM"}
+        if t_gemm is not None:
+            out[name]["us_tcgen05_gemm"] = t_gemm * 1e6
         if t_unfused is not None:
             # the standalone pass: reads and writes M x heads x 128 f32 and reads the two tables
             norm_bytes = 2 * M * heads * hd * 4 + 2 * M * hd * 4
@@ -363,6 +380,11 @@ def config_rows(dev, peaks, names=None):
         del items
         torch.cuda.empty_cache()
     return out
+
+
+def ws_plan_skinny(pw, M, nw):
+    """1 when the planner sends this call to the few-token kernel."""
+    return pw.plan_info(M, gated=nw == 2)["skinny"] == 1
 
 
 def _select_row(dev, n, cols, rows, hbm):

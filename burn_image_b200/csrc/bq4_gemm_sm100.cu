@@ -1544,6 +1544,29 @@ bq4_status plan_gemm(const bq4_weight* w, int nw, int64_t M, int device, GemmPla
     const int v = atoi(f);
     if (v == 64 || v == 128 || (v == 256 && nw == 1)) forced = v;
   }
+  // Few-token calls (up to kSkAutoMaxM rows) take the bandwidth-bound
+  // small-M kernel: measured on B200 against this GEMM (graph-replayed, cold
+  // L2), 1 x 2560 x 9728: 12.4 vs 31.6 us; 16 x 2560 x 9728: 17.0 vs 34.0;
+  // 16 x 9728 x 2560: 16.9 vs 26.8; it loses from 64 rows (37.6 vs 34.6)
+  // and at 256 (k/v: 22.6 vs 14.3).  BQ4_NO_SKINNY=1 never takes it,
+  // BQ4_FORCE_SKINNY=1 takes it for every call that fits it (to 256 rows).
+  SkPlan skp;
+  const char* force_sk = getenv("BQ4_FORCE_SKINNY");
+  const bool want_sk = (force_sk && force_sk[0] == '1') || M <= kSkAutoMaxM;
+  const bool sk_ok = want_sk && !qk && !cv && !p->tf && !p->pre && !getenv("BQ4_NO_SKINNY") &&
+                     plan_skinny(w, nw, M, device, p->exact != 0, &skp);
+  if (sk_ok) {
+    p->skinny = 1;
+    p->sk = skp;
+    p->bt = 8 * skp.nt;
+    p->ksplit = p->cluster = skp.ks;
+    p->mtiles = skp.gz;
+    p->ntiles = (int)w->ntiles;
+    p->units = p->grid = skp.gx * skp.ks * skp.gz;
+    p->stages = skp.stages;
+    p->smem_bytes = skp.smem_bytes;
+    return BQ4_OK;  // no workspace
+  }
   const GemmPlan base = *p;
   double best = 1e300;
   bool have = false;
@@ -1595,6 +1618,8 @@ bq4_status plan_gemm(const bq4_weight* w, int nw, int64_t M, int device, GemmPla
 bq4_status run_gemm(const GemmPlan& plan, const bq4_weight* const* ws, const void* x, int64_t M,
                     int64_t ldx, const float* const* bias, int act, const float* aux, void* y,
                     void* workspace, cudaStream_t stream, const GemmIo& io) {
+  if (plan.skinny)
+    return run_skinny(plan.sk, ws, x, io.x_f16, M, ldx, bias, act, aux, y, io.y_f16, io.ldy, io, stream);
   const bq4_weight* w0 = ws[0];
   cudaError_t e = cudaSuccess;
   const void* xh = x;

@@ -1,0 +1,700 @@
+// bq4_skinny.cu -- the packed signed-Q4 linear for few tokens (decode-shaped
+// and text-encoder-shaped calls), where streaming the weights from HBM, not
+// the tensor core, sets the time.
+//
+// The tcgen05 GEMM (bq4_gemm_sm100.cu) is a persistent, warp-specialised
+// kernel built for many tokens; with a handful of tokens its fixed costs
+// (TMEM allocation, the activation staging launch, a split-K exchange through
+// L2) dwarf the few microseconds the weight bytes take.  This kernel is one
+// launch with no workspace:
+//   * weights stream from HBM straight into registers with 128-bit
+//     non-allocating loads, several 128-K stages in flight per warp;
+//   * each lane unpacks its own nibbles in registers into the A fragment of
+//     mma.sync.m16n8k16 (f16 x f16 -> f32): the K order inside an MMA is
+//     permuted so that the 32 K values of one 16-byte load of a prepared row
+//     are exactly the values that lane contributes, the same permutation is
+//     applied to the activations, and no shuffle is needed;
+//   * the f32 activations of the CTA's K range are read once, rounded to f16
+//     (round to nearest even, as the GEMM's staging does) into swizzled
+//     shared memory that every warp reads conflict-free;
+//   * split-K partials meet in shared memory (warps of a CTA) and then in
+//     distributed shared memory (CTAs of a cluster), summed in a fixed
+//     order, so repeated calls give the same bits;
+//   * the epilogue (bias, GELU-tanh, SiLU, aux, SiLU-gated pair, f16 output,
+//     row scatter) runs once per output element.
+// It is launched as a programmatic dependent of the kernel before it: the
+// weight loads start before that kernel has finished, and only the reads of
+// the activations (and every global write) wait for it.
+//
+// Numerics match the GEMM's: activations staged as f16; EXACT (block 128)
+// keeps q exact in f16 and multiplies each K block's f32 partial by its
+// scale; FOLDED stages f16(q * f16(scale)), the reference kernel's staging
+// (patches/burn-cubecl-0.21.0/src/kernel/matmul/quantized.rs:172-178).
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <atomic>
+#include <cstdlib>
+#include <cstring>
+
+#include "bq4_internal.h"
+#include "sm100_ptx.cuh"
+
+namespace bq4 {
+namespace {
+
+constexpr int kSkConsumers = 256;                 // 8 MMA warps, one 16-row group each
+constexpr int kSkThreads = kSkConsumers + 32;     // + 1 producer warp
+constexpr uint32_t kSkSeg = 2048;                 // one (chunk, half) of a 128-row tile: 128 rows x 16 B
+constexpr uint32_t kSkSegStride = kSkSeg + 32;    // padded so the four segments a warp reads fall in distinct banks
+constexpr uint32_t kSkWBytes = 4 * kSkSegStride;  // one weight's 128-K stage in the ring
+constexpr size_t kSkCtaSmem = 110 * 1024;         // ring budget: two CTAs fit on one SM
+
+struct SkArgs {
+  const uint32_t* q[2];
+  const float* s[2];
+  const float* bias[2];
+  const float* aux;
+  const void* x;
+  void* y;
+  float* sc_y[BQ4_MAX_PEERS];  // row scatter targets (sc_rows > 0)
+  int* err;                    // device error word (BQ4_ETIMEOUT on a wait that ran out)
+  int64_t ldx, ldy;
+  int M, N, K;
+  int nkc, nkb, nks, block;
+  int ks;         // CTAs per cluster along K (grid.y)
+  int stages;     // ring depth
+  uint32_t s_bytes;      // scale bytes of one weight's stage (128 / block rows of 128 scales)
+  uint32_t stage_bytes;  // ring bytes per stage (all weights)
+  int x_f16, y_f16, xvec, yvec;
+  int act;
+  int sc_rows, sc_rank;
+  uint32_t xs_pitch;     // bytes per token row of the staged activations
+  uint32_t xs_off;       // offsets in dynamic shared memory: staged activations,
+  uint32_t red_off;      //   the warps' partial tiles, the per-CTA sums,
+  uint32_t sum_off;      //   the mbarriers (ring at 0)
+  uint32_t bar_off;
+};
+
+__device__ __forceinline__ uint32_t lds32(uint32_t addr) {
+  uint32_t v;
+  asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(addr));
+  return v;
+}
+
+// The f16x2 pair (K 2i, 2i+1) of a prepared word (nibbles stored in K order
+// {0,2,4,6,1,3,5,7}): (w >> 4i) & 0x000F000F, XOR 0x6408 maps the
+// two's-complement nibble to f16 1024 + (q + 8), subtracting 1032 leaves q.
+__device__ __forceinline__ uint32_t nib_pair(uint32_t w, int i) {
+  const uint32_t magic = 0x64086408u;
+  uint32_t t;
+  asm("lop3.b32 %0, %1, %2, %3, 0x6a;" : "=r"(t) : "r"(w >> (4 * i)), "r"(0x000F000Fu), "r"(magic));
+  asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(t) : "r"(t), "r"(magic));
+  return t;
+}
+
+__device__ __forceinline__ uint32_t hmul2(uint32_t a, uint32_t b) {
+  uint32_t r;
+  asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+
+__device__ __forceinline__ uint32_t f16x2_of(float s) {
+  uint16_t h;
+  asm("cvt.rn.satfinite.f16.f32 %0, %1;" : "=h"(h) : "f"(s));
+  return static_cast<uint32_t>(h) | (static_cast<uint32_t>(h) << 16);
+}
+
+__device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                         uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};\n"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ uint4 lds128(uint32_t addr) {
+  uint4 v;
+  asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr));
+  return v;
+}
+
+// Barrier of the 8 MMA warps only (the producer warp keeps streaming).
+__device__ __forceinline__ void consumers_sync() { asm volatile("bar.sync 1, %0;" ::"n"(kSkConsumers) : "memory"); }
+
+__device__ __forceinline__ float sk_gelu_tanh(float v) {
+  // Burn Gelu::new_approximate: 0.5 v (1 + tanh(sqrt(2/pi) (v + 0.044715 v^3)))
+  const float u = 0.7978845608028654f * (v + 0.044715f * v * v * v);
+  float t;
+  asm("tanh.approx.f32 %0, %1;" : "=f"(t) : "f"(u));
+  return 0.5f * v * (1.0f + t);
+}
+
+__device__ __forceinline__ float sk_silu(float v) { return __fdividef(v, 1.0f + __expf(-v)); }
+
+// Byte offset of 16-byte chunk c (8 K values) in a staged token row: chunk
+// c ^ 2 when bit 3 of c is set, so that the four K quarters a warp reads at
+// once (chunks 4t + u, t = 0..3) fall in distinct banks; the row pitch is 16
+// bytes past a multiple of 128, so the two token rows of one access phase
+// use the other half of the banks.
+__device__ __forceinline__ uint32_t xs_chunk(int c) { return (uint32_t)((c ^ (((c >> 3) & 1) << 1)) << 4); }
+
+__device__ __forceinline__ void sk_fail(volatile int* abort_flag, int* err) {
+  if (!*abort_flag) {
+    *abort_flag = 1;
+    if (err) atomicCAS(err, 0, (int)BQ4_ETIMEOUT);
+  }
+}
+
+// One CTA: the 128-row prepared tile blockIdx.x, tokens [8 NT blockIdx.z,
+// +8 NT), the K stages of split blockIdx.y (its rank in a cluster of ks CTAs
+// along K).  Warp 8 streams the tile's stages (nibbles, and the scales of
+// their blocks) into a ring of `stages` slots with 1-D bulk copies,
+// independent of everything else; warps 0-7 stage the activations, then
+// warp w consumes rows 16 w .. 16 w + 15 of every stage.
+//
+// Lane (g = lane / 4, t = lane % 4) reads, per stage, the 16 bytes of rows
+// g and g + 8 of its row group that hold K = 32 t .. 32 t + 31 of the stage
+// (prepared chunk t / 2, half t % 2 = ring segment t).  MMA step (u, v)
+// (u = 0..3, v = 0..1) takes K = 32 t + 8 u + 4 v + {0,1} into k-slots 2t,
+// 2t + 1 and + {2,3} into 2t + 8, 2t + 9: every lane's A registers come from
+// its own words, and the B fragment of token g is the same four K values of
+// that token's row.
+// SPL: scales per lane row per stage -- 1 (exact numerics, or blocks of 32+:
+// a lane's 32 K lie in one block), 2 (blocks of 16), 4 (blocks of 8).
+template <int NT, int NW, bool EXACT, int SPL>
+__global__ void __launch_bounds__(kSkThreads, 2) q4_skinny_kernel(const SkArgs a) {
+  extern __shared__ __align__(128) unsigned char sk_smem[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int tile = blockIdx.x;
+  const int split = blockIdx.y;
+  const int m0 = blockIdx.z * 8 * NT;
+  const int S0 = (int)((int64_t)split * a.nks / a.ks), S1 = (int)((int64_t)(split + 1) * a.nks / a.ks);
+  const int ns = S1 - S0;
+  const int S = a.stages;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sk_smem + a.bar_off);
+  uint64_t* empty = full + S;
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + S);
+  const uint32_t ring = ptx::smem_u32(sk_smem);
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < S; ++i) {
+      ptx::mbar_init(&full[i], 1);
+      ptx::mbar_init(&empty[i], kSkConsumers / 32);
+    }
+    *abort_flag = 0;
+    ptx::fence_mbar_init();
+  }
+  __syncthreads();
+
+  if (warp == kSkConsumers / 32) {
+    // ---- producer: weights are immutable, so the stream starts before the
+    // kernel this one depends on has finished
+    if (lane == 0) {
+      const uint32_t wbytes = 4 * kSkSeg + a.s_bytes;
+      int i = 0;
+      for (; i < ns && !*abort_flag; ++i) {
+        const int slot = i % S;
+        if (i >= S && !ptx::mbar_wait(&empty[slot], ((i / S) - 1) & 1, abort_flag)) {
+          sk_fail(abort_flag, a.err);
+          break;
+        }
+        const int st = S0 + i;
+        ptx::mbar_arrive_expect_tx(&full[slot], NW * wbytes);
+        unsigned char* dst = sk_smem + (size_t)slot * a.stage_bytes;
+#pragma unroll
+        for (int w = 0; w < NW; ++w) {
+          const unsigned char* q = reinterpret_cast<const unsigned char*>(a.q[w]) +
+                                   ((size_t)tile * a.nkc + 2 * st) * 4096;
+#pragma unroll
+          for (int seg = 0; seg < 4; ++seg)
+            ptx::bulk_load(dst + w * (kSkWBytes + a.s_bytes) + seg * kSkSegStride, q + seg * kSkSeg, kSkSeg,
+                           &full[slot]);
+          const float* sc = a.s[w] + ((size_t)tile * a.nkb + (size_t)st * 128 / a.block) * 128;
+          ptx::bulk_load(dst + w * (kSkWBytes + a.s_bytes) + kSkWBytes, sc, a.s_bytes, &full[slot]);
+        }
+      }
+      // copies still in flight land before this CTA may exit (bounded)
+      for (int j = i - 1; j >= 0 && j >= i - S; --j)
+        if (!ptx::mbar_wait(&full[j % S], (j / S) & 1, abort_flag)) break;
+    }
+    __syncwarp();
+  } else {
+    const int g = lane >> 2, t = lane & 3;
+    const int row = warp * 16 + g;  // row of the tile (and row + 8)
+
+    // ---- activations of the CTA's K range -> f16, swizzled shared memory
+    ptx::griddep_launch_dependents();  // the next kernel may start its own weight stream
+    ptx::griddep_wait();               // x may be the output of the kernel before this one
+    {
+      // rows past M and K values past K are zeros; each thread issues the
+      // loads of kXB chunks before converting any, so their latencies overlap
+      constexpr int kXB = 4;
+      const int chunks = ns * 16;  // 8-K chunks per token row
+      const int K0 = S0 * 128;
+      const int total = 8 * NT * chunks;
+      unsigned char* xs = sk_smem + a.xs_off;
+      for (int base = threadIdx.x; base < total; base += kSkConsumers * kXB) {
+        float f[kXB][8];
+        uint4 hv[kXB];
+#pragma unroll
+        for (int b = 0; b < kXB; ++b) {
+          const int idx = base + b * kSkConsumers;
+          hv[b] = make_uint4(0, 0, 0, 0);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) f[b][i] = 0.0f;
+          if (idx >= total) continue;
+          const int tok = idx / chunks, c = idx - tok * chunks;
+          const int m = m0 + tok, k = K0 + c * 8;
+          if (m >= a.M) continue;
+          if (a.x_f16) {
+            const __half* xr = static_cast<const __half*>(a.x) + (size_t)m * a.ldx;
+            if (k + 8 <= a.K && a.xvec) {
+              hv[b] = *reinterpret_cast<const uint4*>(xr + k);
+            } else {
+              uint16_t e[8];
+#pragma unroll
+              for (int i = 0; i < 8; ++i) e[i] = k + i < a.K ? __half_as_ushort(xr[k + i]) : (uint16_t)0;
+              hv[b] = make_uint4(e[0] | (uint32_t)e[1] << 16, e[2] | (uint32_t)e[3] << 16,
+                                 e[4] | (uint32_t)e[5] << 16, e[6] | (uint32_t)e[7] << 16);
+            }
+          } else {
+            const float* xr = static_cast<const float*>(a.x) + (size_t)m * a.ldx;
+            if (k + 8 <= a.K && a.xvec) {
+              const float4 p0 = *reinterpret_cast<const float4*>(xr + k);
+              const float4 p1 = *reinterpret_cast<const float4*>(xr + k + 4);
+              f[b][0] = p0.x; f[b][1] = p0.y; f[b][2] = p0.z; f[b][3] = p0.w;
+              f[b][4] = p1.x; f[b][5] = p1.y; f[b][6] = p1.z; f[b][7] = p1.w;
+            } else {
+#pragma unroll
+              for (int i = 0; i < 8; ++i) f[b][i] = k + i < a.K ? xr[k + i] : 0.0f;
+            }
+          }
+        }
+#pragma unroll
+        for (int b = 0; b < kXB; ++b) {
+          const int idx = base + b * kSkConsumers;
+          if (idx >= total) continue;
+          const int tok = idx / chunks, c = idx - tok * chunks;
+          uint4 h = hv[b];
+          if (!a.x_f16) {
+            uint32_t p[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              const __half2 v = __floats2half2_rn(f[b][2 * i], f[b][2 * i + 1]);
+              p[i] = *reinterpret_cast<const uint32_t*>(&v);
+            }
+            h = make_uint4(p[0], p[1], p[2], p[3]);
+          }
+          *reinterpret_cast<uint4*>(xs + (size_t)tok * a.xs_pitch + xs_chunk(c)) = h;
+        }
+      }
+    }
+    consumers_sync();
+
+    // ---- main loop over the CTA's stages.  The 8 MMA steps of a stage go
+    // round-robin into CH independent accumulator chains (so that mma.sync
+    // latency, not a dependent chain, sets the pace: NW x NT x CH >= 8 chains per
+    // warp), summed in a fixed order at the end (folded) or per stage
+    // before the scale is applied (exact).
+    constexpr int CH = NT * NW >= 8 ? 1 : 8 / (NT * NW);
+    float acc[NW][NT][4];
+#pragma unroll
+    for (int i = 0; i < NW; ++i)
+#pragma unroll
+      for (int j = 0; j < NT; ++j) acc[i][j][0] = acc[i][j][1] = acc[i][j][2] = acc[i][j][3] = 0.0f;
+    float chain[CH][NW][NT][4];  // folded: running sums per chain; exact: the stage's partial per chain
+#pragma unroll
+    for (int c = 0; c < CH; ++c)
+#pragma unroll
+      for (int i = 0; i < NW; ++i)
+#pragma unroll
+        for (int j = 0; j < NT; ++j) chain[c][i][j][0] = chain[c][i][j][1] = chain[c][i][j][2] = chain[c][i][j][3] = 0.0f;
+    const uint32_t xs_base = ptx::smem_u32(sk_smem + a.xs_off) + (uint32_t)g * a.xs_pitch;
+    const uint32_t lane_w = (uint32_t)t * kSkSegStride + (uint32_t)row * 16;  // rows g, g + 8: + 0, + 128
+    const int sc0 = EXACT ? 0 : (32 * t) / a.block;  // the lane's first scale block within a stage
+    bool ok = true;
+    for (int i = 0; i < ns; ++i) {
+      const int slot = i % S;
+      if (!ptx::mbar_wait(&full[slot], (i / S) & 1, abort_flag)) {
+        ok = false;
+        break;
+      }
+      const uint32_t sbase = ring + (uint32_t)slot * a.stage_bytes;
+      uint4 w[NW][2];
+      float se[NW][SPL][2];
+#pragma unroll
+      for (int q = 0; q < NW; ++q) {
+        const uint32_t wb = sbase + (uint32_t)q * (kSkWBytes + a.s_bytes);
+        w[q][0] = lds128(wb + lane_w);
+        w[q][1] = lds128(wb + lane_w + 128);
+#pragma unroll
+        for (int j = 0; j < SPL; ++j) {
+          const uint32_t sa = wb + kSkWBytes + (uint32_t)(sc0 + j) * 512 + (uint32_t)row * 4;
+          se[q][j][0] = __uint_as_float(lds32(sa));
+          se[q][j][1] = __uint_as_float(lds32(sa + 32));
+        }
+      }
+      // every read of the slot is done: release it to the producer
+      __syncwarp();
+      if (lane == 0) ptx::mbar_arrive(&empty[slot]);
+      uint32_t sf[NW][4][2];
+      if constexpr (!EXACT) {
+#pragma unroll
+        for (int q = 0; q < NW; ++q)
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            sf[q][u][0] = f16x2_of(se[q][u * SPL / 4][0]);
+            sf[q][u][1] = f16x2_of(se[q][u * SPL / 4][1]);
+          }
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        uint32_t af[NW][2][4];
+#pragma unroll
+        for (int q = 0; q < NW; ++q) {
+          const uint32_t lo = (&w[q][0].x)[u], hi = (&w[q][1].x)[u];
+#pragma unroll
+          for (int v = 0; v < 2; ++v) {
+            af[q][v][0] = nib_pair(lo, 2 * v);
+            af[q][v][1] = nib_pair(hi, 2 * v);
+            af[q][v][2] = nib_pair(lo, 2 * v + 1);
+            af[q][v][3] = nib_pair(hi, 2 * v + 1);
+            if constexpr (!EXACT) {
+              af[q][v][0] = hmul2(af[q][v][0], sf[q][u][0]);
+              af[q][v][1] = hmul2(af[q][v][1], sf[q][u][1]);
+              af[q][v][2] = hmul2(af[q][v][2], sf[q][u][0]);
+              af[q][v][3] = hmul2(af[q][v][3], sf[q][u][1]);
+            }
+          }
+        }
+        const uint32_t xoff = xs_base + xs_chunk(i * 16 + 4 * t + u);
+#pragma unroll
+        for (int j = 0; j < NT; ++j) {
+          const uint4 xv = lds128(xoff + (uint32_t)(8 * j) * a.xs_pitch);
+#pragma unroll
+          for (int q = 0; q < NW; ++q) {
+            mma16816(chain[(2 * u) % CH][q][j], af[q][0][0], af[q][0][1], af[q][0][2], af[q][0][3], xv.x, xv.y);
+            mma16816(chain[(2 * u + 1) % CH][q][j], af[q][1][0], af[q][1][1], af[q][1][2], af[q][1][3], xv.z,
+                     xv.w);
+          }
+        }
+      }
+      if constexpr (EXACT) {
+#pragma unroll
+        for (int q = 0; q < NW; ++q)
+#pragma unroll
+          for (int j = 0; j < NT; ++j) {
+            float p[4];
+#pragma unroll
+            for (int r = 0; r < 4; ++r) {
+              p[r] = chain[0][q][j][r];
+              chain[0][q][j][r] = 0.0f;
+#pragma unroll
+              for (int c = 1; c < CH; ++c) {
+                p[r] += chain[c][q][j][r];
+                chain[c][q][j][r] = 0.0f;
+              }
+            }
+            acc[q][j][0] = fmaf(p[0], se[q][0][0], acc[q][j][0]);
+            acc[q][j][1] = fmaf(p[1], se[q][0][0], acc[q][j][1]);
+            acc[q][j][2] = fmaf(p[2], se[q][0][1], acc[q][j][2]);
+            acc[q][j][3] = fmaf(p[3], se[q][0][1], acc[q][j][3]);
+          }
+      }
+    }
+    if (!ok) sk_fail(abort_flag, a.err);
+    if constexpr (!EXACT) {
+#pragma unroll
+      for (int q = 0; q < NW; ++q)
+#pragma unroll
+        for (int j = 0; j < NT; ++j)
+#pragma unroll
+          for (int r = 0; r < 4; ++r) {
+            float v = chain[0][q][j][r];
+#pragma unroll
+            for (int c = 1; c < CH; ++c) v += chain[c][q][j][r];
+            acc[q][j][r] = v;
+          }
+    }
+
+    // ---- the warps' tiles -> [NW][8 NT tokens][128 + 4 rows] f32 (rows of
+    // token t contiguous, so the epilogue reads 4 rows at once), over the
+    // staged activations, which every warp has finished with
+    constexpr int RP = 132;
+    consumers_sync();
+    float* red = reinterpret_cast<float*>(sk_smem + a.red_off);
+#pragma unroll
+    for (int q = 0; q < NW; ++q)
+#pragma unroll
+      for (int j = 0; j < NT; ++j) {
+        float* base = red + ((size_t)q * 8 * NT + 8 * j + 2 * t) * RP + row;
+        base[0] = acc[q][j][0];
+        base[RP] = acc[q][j][1];
+        base[8] = acc[q][j][2];
+        base[RP + 8] = acc[q][j][3];
+      }
+  }
+  // ---- cluster sum (ranks in order) and the epilogue; rank r takes every
+  // ks-th element (the producer warp passes the barriers only)
+  if (a.ks > 1) ptx::cluster_sync();
+  else __syncthreads();
+  if (warp < kSkConsumers / 32) {
+    constexpr int RP = 132;
+    const float* red = reinterpret_cast<const float*>(sk_smem + a.red_off);
+    const int quads = 32, elems = 8 * NT * quads;
+    const int e_first = threadIdx.x * a.ks + split;
+    const int n0 = tile * 128;
+    float bpre[NW][4];
+#pragma unroll
+    for (int i = 0; i < NW; ++i)
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const int nc = n0 + 4 * (e_first % quads) + c;
+        bpre[i][c] = (a.bias[i] && e_first < elems && nc < a.N) ? __ldg(a.bias[i] + nc) : 0.0f;
+      }
+    for (int e = e_first; e < elems; e += kSkConsumers * a.ks) {
+      const int tok = e / quads, rq = e - tok * quads;
+      const int m = m0 + tok;
+      float v[NW][4];
+#pragma unroll
+      for (int i = 0; i < NW; ++i) {
+        v[i][0] = v[i][1] = v[i][2] = v[i][3] = 0.0f;
+        const float* src = red + ((size_t)i * 8 * NT + tok) * RP + 4 * rq;
+        for (int r = 0; r < a.ks; ++r) {
+          float4 p;
+          if (a.ks > 1) p = ptx::ld_shared_cluster_f4(ptx::mapa_shared(ptx::smem_u32(src), (uint32_t)r));
+          else p = *reinterpret_cast<const float4*>(src);
+          v[i][0] += p.x; v[i][1] += p.y; v[i][2] += p.z; v[i][3] += p.w;
+        }
+      }
+      if (m >= a.M) continue;
+      const int n = n0 + 4 * rq;
+      float o[4];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const int nc = n + c;
+        const bool in = nc < a.N;
+        float r0 = v[0][c];
+        if (a.bias[0] && in) r0 += e == e_first ? bpre[0][c] : __ldg(a.bias[0] + nc);
+        if constexpr (NW == 2) {
+          float r1 = v[1][c];
+          if (a.bias[1] && in) r1 += e == e_first ? bpre[1][c] : __ldg(a.bias[1] + nc);
+          r0 = sk_silu(r0) * r1;
+        } else {
+          if (a.act == BQ4_ACT_GELU_TANH) r0 = sk_gelu_tanh(r0);
+          else if (a.act == BQ4_ACT_SILU) r0 = sk_silu(r0);
+          if (a.aux && in) r0 *= __ldg(a.aux + (size_t)m * a.N + nc);
+        }
+        o[c] = r0;
+      }
+      if (a.sc_rows) {
+        const int owner = m / a.sc_rows;
+        float* yr = a.sc_y[owner] + (size_t)(a.sc_rank * a.sc_rows + (m - owner * a.sc_rows)) * a.ldy;
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+          if (n + c < a.N) yr[n + c] = o[c];
+      } else if (a.y_f16) {
+        __half* yr = static_cast<__half*>(a.y) + (size_t)m * a.ldy;
+        if (a.yvec && n + 4 <= a.N) {
+          const __half2 h0 = __floats2half2_rn(o[0], o[1]), h1 = __floats2half2_rn(o[2], o[3]);
+          *reinterpret_cast<uint2*>(yr + n) =
+              make_uint2(*reinterpret_cast<const uint32_t*>(&h0), *reinterpret_cast<const uint32_t*>(&h1));
+        } else {
+#pragma unroll
+          for (int c = 0; c < 4; ++c)
+            if (n + c < a.N) yr[n + c] = __float2half_rn(o[c]);
+        }
+      } else {
+        float* yr = static_cast<float*>(a.y) + (size_t)m * a.ldy;
+        if (a.yvec && n + 4 <= a.N) {
+          *reinterpret_cast<float4*>(yr + n) = make_float4(o[0], o[1], o[2], o[3]);
+        } else {
+#pragma unroll
+          for (int c = 0; c < 4; ++c)
+            if (n + c < a.N) yr[n + c] = o[c];
+        }
+      }
+    }
+  }
+  if (a.ks > 1) ptx::cluster_sync();  // keep this CTA's partials alive until every rank has read them
+}
+
+template <int NT, int NW, bool EXACT, int SPL>
+cudaError_t launch_sk(const SkPlan& p, const SkArgs& a, cudaStream_t stream) {
+  static std::atomic<int> ready[64];
+  int dev = 0;
+  cudaGetDevice(&dev);
+  auto kern = q4_skinny_kernel<NT, NW, EXACT, SPL>;
+  if (dev >= 0 && dev < 64 && !ready[dev].load(std::memory_order_acquire)) {
+    const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSkMaxSmem);
+    if (e != cudaSuccess) return e;
+    ready[dev].store(1, std::memory_order_release);
+  }
+  cudaLaunchConfig_t cfg;
+  memset(&cfg, 0, sizeof(cfg));
+  cfg.gridDim = dim3((unsigned)p.gx, (unsigned)p.ks, (unsigned)p.gz);
+  cfg.blockDim = dim3(kSkThreads, 1, 1);
+  cfg.dynamicSmemBytes = p.smem_bytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  int na = 0;
+  attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[na].val.programmaticStreamSerializationAllowed = p.pdl ? 1 : 0;
+  ++na;
+  if (p.ks > 1) {
+    attr[na].id = cudaLaunchAttributeClusterDimension;
+    attr[na].val.clusterDim.x = 1;
+    attr[na].val.clusterDim.y = (unsigned)p.ks;
+    attr[na].val.clusterDim.z = 1;
+    ++na;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = na;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, a);
+  note_launch();
+  return e;
+}
+
+// Shared-memory layout of one CTA (bytes): the ring of `stages` slots, the
+// staged activation rows (8 NT tokens x kcta stages x 128 K in f16, 16 bytes
+// of pitch padding) -- reused after the main loop for the warps' partial
+// tiles ([NW][8 NT][132] f32) -- the mbarriers and the abort flag.
+struct SkLayout {
+  uint32_t stage_bytes, s_bytes, xs_pitch, xs_off, red_off, bar_off;
+  size_t total;
+};
+
+SkLayout sk_layout(int nt, int nw, int block, int kcta, int stages) {
+  SkLayout L;
+  L.s_bytes = 512u * (uint32_t)(block >= 128 ? 1 : 128 / block);
+  L.stage_bytes = (uint32_t)nw * (kSkWBytes + L.s_bytes);
+  L.xs_pitch = (uint32_t)kcta * 256 + 16;
+  L.xs_off = (uint32_t)stages * L.stage_bytes;
+  L.red_off = L.xs_off;
+  const uint32_t xs_bytes = 8u * nt * L.xs_pitch, red_bytes = (uint32_t)nw * 8 * nt * 132 * 4;
+  L.bar_off = L.xs_off + (((xs_bytes > red_bytes ? xs_bytes : red_bytes) + 127) & ~127u);
+  L.total = (size_t)L.bar_off + (size_t)stages * 16 + 16;
+  return L;
+}
+
+}  // namespace
+
+bool plan_skinny(const bq4_weight* w, int nw, int64_t M, int device, bool exact, SkPlan* p) {
+  memset(p, 0, sizeof(*p));
+  if (w->h || w->tf32 || !w->q || !w->s) return false;       // pre-expanded / packed-F16 weights
+  if (exact && w->block != 128) return false;                // exact scale per 128-K stage only
+  if (M <= 0 || M > kSkMaxM) return false;
+  if (w->Kp % 128 != 0) return false;
+  int sms = device_sm_count(device);
+  if (sm_budget() > 0 && sm_budget() < sms) sms = sm_budget();
+  // token tile: the fewest 8-token MMA columns covering M (at most 64 per CTA)
+  int nt = 1;
+  while (nt < 8 && 8 * nt < M) nt *= 2;
+  if (nw == 2 && nt > 2) nt = 2;   // two weights' accumulators: at most 16 tokens per CTA
+  if (exact && nt > 4) nt = 4;     // the exact partials: at most 32 tokens per CTA
+  const int mgroups = (int)((M + 8 * nt - 1) / (8 * nt));
+  const int nks = (int)(w->Kp / 128);
+  const int gx = (int)w->ntiles;
+  // K splits across a cluster (<= 8): doubled while the grid is short of one
+  // CTA per SM and every CTA keeps at least two 128-K stages
+  int ks = 1;
+  while (ks < 8 && (int64_t)gx * mgroups * ks < sms && nks >= 4 * ks) ks *= 2;
+  if (const char* f = getenv("BQ4_SKINNY_KS")) {
+    const int v = atoi(f);
+    if (v >= 1 && v <= 8) ks = v;
+  }
+  if (ks > nks) ks = nks;
+  int kcta = (nks + ks - 1) / ks;
+  // ring: as many stages as fit next to the activations (at most the CTA's
+  // stage count), at least 2
+  int stages = 2;
+  while (stages < kcta && sk_layout(nt, nw, w->block, kcta, stages + 1).total <= kSkCtaSmem) ++stages;
+  if (const char* f = getenv("BQ4_SKINNY_STAGES")) {
+    const int v = atoi(f);
+    if (v >= 2 && v < stages) stages = v;
+  }
+  const SkLayout L = sk_layout(nt, nw, w->block, kcta, stages);
+  if (L.total > kSkMaxSmem) return false;
+  p->nt = nt;
+  p->nw = nw;
+  p->R = 8;
+  p->ks = ks;
+  p->gx = gx;
+  p->gz = mgroups;
+  p->stages = stages;
+  p->smem_bytes = L.total;
+  p->exact = exact ? 1 : 0;
+  p->pdl = getenv("BQ4_NO_PDL") ? 0 : 1;
+  return true;
+}
+
+bq4_status run_skinny(const SkPlan& p, const bq4_weight* const* ws, const void* x, int x_f16, int64_t M, int64_t ldx,
+                      const float* const* bias, int act, const float* aux, void* y, int y_f16, int64_t ldy,
+                      const GemmIo& io, cudaStream_t stream) {
+  const bq4_weight* w0 = ws[0];
+  SkArgs a;
+  memset(&a, 0, sizeof(a));
+  for (int i = 0; i < p.nw; ++i) {
+    a.q[i] = ws[i]->q;
+    a.s[i] = ws[i]->s;
+    a.bias[i] = bias ? bias[i] : nullptr;
+  }
+  a.aux = aux;
+  a.x = x;
+  a.y = y;
+  a.ldx = ldx;
+  a.ldy = ldy > 0 ? ldy : w0->N;
+  a.M = (int)M;
+  a.N = (int)w0->N;
+  a.K = (int)w0->K;
+  a.nkc = (int)w0->nkc;
+  a.nkb = (int)w0->nkb;
+  a.nks = (int)(w0->Kp / 128);
+  a.block = w0->block;
+  a.ks = p.ks;
+  a.stages = p.stages;
+  a.err = device_error_word();
+  a.x_f16 = x_f16;
+  a.y_f16 = y_f16;
+  a.xvec = x_f16 ? ((reinterpret_cast<uintptr_t>(x) & 15) == 0 && ldx % 8 == 0)
+                 : ((reinterpret_cast<uintptr_t>(x) & 15) == 0 && ldx % 4 == 0);
+  a.yvec = ((reinterpret_cast<uintptr_t>(y) & (y_f16 ? 7 : 15)) == 0 && a.ldy % 4 == 0) ? 1 : 0;
+  a.act = act;
+  if (io.sc_rows) {
+    if (y_f16 || io.sc_nranks < 1 || io.sc_nranks > BQ4_MAX_PEERS || !io.sc_y)
+      return set_error(BQ4_EINVAL_ARG, "row scatter needs f32 output and 1..%d ranks", BQ4_MAX_PEERS);
+    a.sc_rows = io.sc_rows;
+    a.sc_rank = io.sc_rank;
+    for (int r = 0; r < io.sc_nranks; ++r) a.sc_y[r] = io.sc_y[r];
+  }
+  const int kcta = (a.nks + p.ks - 1) / p.ks;
+  const SkLayout L = sk_layout(p.nt, p.nw, w0->block, kcta, p.stages);
+  a.s_bytes = L.s_bytes;
+  a.stage_bytes = L.stage_bytes;
+  a.xs_pitch = L.xs_pitch;
+  a.xs_off = L.xs_off;
+  a.red_off = L.red_off;
+  a.bar_off = L.bar_off;
+  cudaError_t e = cudaSuccess;
+#define BQ4_SK_CASE(NT_, NW_, EX_, SPL_)                           \
+  if (p.nt == NT_ && p.nw == NW_ && p.exact == EX_ && spl == SPL_) \
+    e = launch_sk<NT_, NW_, EX_, SPL_>(p, a, stream);               \
+  else
+  const int spl = p.exact || w0->block >= 32 ? 1 : 128 / 4 / w0->block;  // blocks of 16: 2, of 8: 4
+  BQ4_SK_CASE(1, 1, true, 1) BQ4_SK_CASE(2, 1, true, 1) BQ4_SK_CASE(4, 1, true, 1)
+  BQ4_SK_CASE(1, 1, false, 1) BQ4_SK_CASE(2, 1, false, 1) BQ4_SK_CASE(4, 1, false, 1) BQ4_SK_CASE(8, 1, false, 1)
+  BQ4_SK_CASE(1, 1, false, 2) BQ4_SK_CASE(2, 1, false, 2) BQ4_SK_CASE(4, 1, false, 2) BQ4_SK_CASE(8, 1, false, 2)
+  BQ4_SK_CASE(1, 1, false, 4) BQ4_SK_CASE(2, 1, false, 4) BQ4_SK_CASE(4, 1, false, 4) BQ4_SK_CASE(8, 1, false, 4)
+  BQ4_SK_CASE(1, 2, true, 1) BQ4_SK_CASE(2, 2, true, 1)
+  BQ4_SK_CASE(1, 2, false, 1) BQ4_SK_CASE(2, 2, false, 1) BQ4_SK_CASE(1, 2, false, 2) BQ4_SK_CASE(2, 2, false, 2)
+  BQ4_SK_CASE(1, 2, false, 4) BQ4_SK_CASE(2, 2, false, 4)
+  return set_error(BQ4_EUNSUPPORTED, "no small-M kernel for %d token columns x %d weights", 8 * p.nt, p.nw);
+#undef BQ4_SK_CASE
+  if (e != cudaSuccess) return check_cuda(e, "small-M q4 linear launch");
+  return BQ4_OK;
+}
+
+}  // namespace bq4

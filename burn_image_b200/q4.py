@@ -261,7 +261,7 @@ class PreparedQ4Weight:
         return n.value
 
     PLAN_FIELDS = ("bt", "ksplit", "grid", "exact", "ta", "stages", "sk_tiles", "dp_tiles", "workspace_256", "wide",
-                   "tail_tiles", "tail_split")
+                   "tail_tiles", "tail_split", "skinny")
 
     def plan_info(self, M: int, gated: bool = False) -> dict:
         """The launch plan of bq4_linear (or of the gated pair) for M rows."""
