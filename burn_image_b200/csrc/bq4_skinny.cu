@@ -7,24 +7,27 @@
 // (TMEM allocation, the activation staging launch, a split-K exchange through
 // L2) dwarf the few microseconds the weight bytes take.  This kernel is one
 // launch with no workspace:
-//   * weights stream from HBM straight into registers with 128-bit
-//     non-allocating loads, several 128-K stages in flight per warp;
+//   * every warp streams its own 16 weight rows of the next D 128-K stages
+//     from HBM into a private shared-memory ring with 16-byte cp.async
+//     copies (the load/store path; measured on B200 it sustains the full HBM
+//     rate for these per-CTA streams where small 1-D bulk copies did not),
+//     waiting only on its own copy groups -- no producer warp and no
+//     cross-warp barrier in the main loop;
 //   * each lane unpacks its own nibbles in registers into the A fragment of
 //     mma.sync.m16n8k16 (f16 x f16 -> f32): the K order inside an MMA is
-//     permuted so that the 32 K values of one 16-byte load of a prepared row
-//     are exactly the values that lane contributes, the same permutation is
-//     applied to the activations, and no shuffle is needed;
+//     permuted so that the 32 K values of one 16-byte row segment are exactly
+//     the values that lane contributes, the same permutation is applied to
+//     the activations, and no shuffle is needed;
 //   * the f32 activations of the CTA's K range are read once, rounded to f16
 //     (round to nearest even, as the GEMM's staging does) into swizzled
 //     shared memory that every warp reads conflict-free;
-//   * split-K partials meet in shared memory (warps of a CTA) and then in
-//     distributed shared memory (CTAs of a cluster), summed in a fixed
-//     order, so repeated calls give the same bits;
+//   * split-K partials meet in distributed shared memory (the CTAs of a
+//     cluster), summed in a fixed order, so repeated calls give the same bits;
 //   * the epilogue (bias, GELU-tanh, SiLU, aux, SiLU-gated pair, f16 output,
 //     row scatter) runs once per output element.
 // It is launched as a programmatic dependent of the kernel before it: the
-// weight loads start before that kernel has finished, and only the reads of
-// the activations (and every global write) wait for it.
+// weight copies start before that kernel has finished, and only the reads
+// of the activations (and every global write) wait for it.
 //
 // Numerics match the GEMM's: activations staged as f16; EXACT (block 128)
 // keeps q exact in f16 and multiplies each K block's f32 partial by its
@@ -44,12 +47,8 @@
 namespace bq4 {
 namespace {
 
-constexpr int kSkConsumers = 256;                 // 8 MMA warps, one 16-row group each
-constexpr int kSkThreads = kSkConsumers + 32;     // + 1 producer warp
-constexpr uint32_t kSkSeg = 2048;                 // one (chunk, half) of a 128-row tile: 128 rows x 16 B
-constexpr uint32_t kSkSegStride = kSkSeg + 32;    // padded so the four segments a warp reads fall in distinct banks
-constexpr uint32_t kSkWBytes = 4 * kSkSegStride;  // one weight's 128-K stage in the ring
-constexpr size_t kSkCtaSmem = 110 * 1024;         // ring budget: two CTAs fit on one SM
+constexpr int kSkThreads = 256;  // 8 warps, one 16-row group of the CTA's 128-row tile each
+constexpr size_t kSkCtaSmem = 110 * 1024;  // shared-memory budget: two CTAs fit on one SM
 
 struct SkArgs {
   const uint32_t* q[2];
@@ -59,22 +58,17 @@ struct SkArgs {
   const void* x;
   void* y;
   float* sc_y[BQ4_MAX_PEERS];  // row scatter targets (sc_rows > 0)
-  int* err;                    // device error word (BQ4_ETIMEOUT on a wait that ran out)
   int64_t ldx, ldy;
   int M, N, K;
   int nkc, nkb, nks, block;
   int ks;         // CTAs per cluster along K (grid.y)
-  int stages;     // ring depth
-  uint32_t s_bytes;      // scale bytes of one weight's stage (128 / block rows of 128 scales)
-  uint32_t stage_bytes;  // ring bytes per stage (all weights)
+  int stages;     // depth D of each warp's ring
+  uint32_t lane_bytes;  // ring bytes per lane per stage (weights, then scales)
   int x_f16, y_f16, xvec, yvec;
   int act;
   int sc_rows, sc_rank;
-  uint32_t xs_pitch;     // bytes per token row of the staged activations
-  uint32_t xs_off;       // offsets in dynamic shared memory: staged activations,
-  uint32_t red_off;      //   the warps' partial tiles, the per-CTA sums,
-  uint32_t sum_off;      //   the mbarriers (ring at 0)
-  uint32_t bar_off;
+  uint32_t xs_pitch;    // bytes per token row of the staged activations
+  uint32_t xs_off;      // offset of the staged activations (and, after the main loop, the partial tiles)
 };
 
 __device__ __forceinline__ uint32_t lds32(uint32_t addr) {
@@ -90,6 +84,19 @@ __device__ __forceinline__ uint32_t nib_pair(uint32_t w, int i) {
   const uint32_t magic = 0x64086408u;
   uint32_t t;
   asm("lop3.b32 %0, %1, %2, %3, 0x6a;" : "=r"(t) : "r"(w >> (4 * i)), "r"(0x000F000Fu), "r"(magic));
+  asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(t) : "r"(t), "r"(magic));
+  return t;
+}
+
+// Pair h (0 or 1) of the low byte of each half of w, unshifted: h = 0 gives
+// the f16x2 q of bits [0,4), as nib_pair(w, 0); h = 1 reads bits [4,8) in
+// place, which the XOR/subtract map to exactly 16 q (those bits are f16
+// mantissa bits 4-7, and 1024 + 16 (n ^ 8) is exact).
+__device__ __forceinline__ uint32_t nib_pair_at(uint32_t w, int h) {
+  const uint32_t mask = h ? 0x00F000F0u : 0x000F000Fu;
+  const uint32_t magic = h ? 0x64806480u : 0x64086408u;
+  uint32_t t;
+  asm("lop3.b32 %0, %1, %2, %3, 0x6a;" : "=r"(t) : "r"(w), "r"(mask), "r"(magic));
   asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(t) : "r"(t), "r"(magic));
   return t;
 }
@@ -115,14 +122,55 @@ __device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
+// d = A . B (accumulator input zero)
+__device__ __forceinline__ void mma16816_zc(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                            uint32_t b0, uint32_t b1) {
+  const float z = 0.0f;
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%10,%10,%10,%10};\n"
+      : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "f"(z));
+}
+
 __device__ __forceinline__ uint4 lds128(uint32_t addr) {
   uint4 v;
   asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr));
   return v;
 }
 
-// Barrier of the 8 MMA warps only (the producer warp keeps streaming).
-__device__ __forceinline__ void consumers_sync() { asm volatile("bar.sync 1, %0;" ::"n"(kSkConsumers) : "memory"); }
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async4(uint32_t dst, const void* src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+// Wait until at most n of this thread's copy groups are pending (n < 16).
+__device__ __forceinline__ void cp_async_wait_dyn(int n) {
+  switch (n) {
+    case 0: cp_async_wait<0>(); break;
+    case 1: cp_async_wait<1>(); break;
+    case 2: cp_async_wait<2>(); break;
+    case 3: cp_async_wait<3>(); break;
+    case 4: cp_async_wait<4>(); break;
+    case 5: cp_async_wait<5>(); break;
+    case 6: cp_async_wait<6>(); break;
+    case 7: cp_async_wait<7>(); break;
+    case 8: cp_async_wait<8>(); break;
+    case 9: cp_async_wait<9>(); break;
+    case 10: cp_async_wait<10>(); break;
+    case 11: cp_async_wait<11>(); break;
+    case 12: cp_async_wait<12>(); break;
+    case 13: cp_async_wait<13>(); break;
+    case 14: cp_async_wait<14>(); break;
+    default: cp_async_wait<15>(); break;
+  }
+}
 
 __device__ __forceinline__ float sk_gelu_tanh(float v) {
   // Burn Gelu::new_approximate: 0.5 v (1 + tanh(sqrt(2/pi) (v + 0.044715 v^3)))
@@ -141,23 +189,15 @@ __device__ __forceinline__ float sk_silu(float v) { return __fdividef(v, 1.0f + 
 // use the other half of the banks.
 __device__ __forceinline__ uint32_t xs_chunk(int c) { return (uint32_t)((c ^ (((c >> 3) & 1) << 1)) << 4); }
 
-__device__ __forceinline__ void sk_fail(volatile int* abort_flag, int* err) {
-  if (!*abort_flag) {
-    *abort_flag = 1;
-    if (err) atomicCAS(err, 0, (int)BQ4_ETIMEOUT);
-  }
-}
-
 // One CTA: the 128-row prepared tile blockIdx.x, tokens [8 NT blockIdx.z,
 // +8 NT), the K stages of split blockIdx.y (its rank in a cluster of ks CTAs
-// along K).  Warp 8 streams the tile's stages (nibbles, and the scales of
-// their blocks) into a ring of `stages` slots with 1-D bulk copies,
-// independent of everything else; warps 0-7 stage the activations, then
-// warp w consumes rows 16 w .. 16 w + 15 of every stage.
+// along K).  Warp w owns rows 16 w .. 16 w + 15 of the tile: it streams
+// them, stage by stage, into its own ring of D slots and consumes them.
 //
-// Lane (g = lane / 4, t = lane % 4) reads, per stage, the 16 bytes of rows
+// Lane (g = lane / 4, t = lane % 4) copies, per stage, the 16 bytes of rows
 // g and g + 8 of its row group that hold K = 32 t .. 32 t + 31 of the stage
-// (prepared chunk t / 2, half t % 2 = ring segment t).  MMA step (u, v)
+// (prepared chunk t / 2, half t % 2), and the scales of those rows, into its
+// own ring slot, and reads back only what it copied.  MMA step (u, v)
 // (u = 0..3, v = 0..1) takes K = 32 t + 8 u + 4 v + {0,1} into k-slots 2t,
 // 2t + 1 and + {2,3} into 2t + 8, 2t + 9: every lane's A registers come from
 // its own words, and the B fragment of token g is the same four K values of
@@ -168,294 +208,296 @@ template <int NT, int NW, bool EXACT, int SPL>
 __global__ void __launch_bounds__(kSkThreads, 2) q4_skinny_kernel(const SkArgs a) {
   extern __shared__ __align__(128) unsigned char sk_smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, t = lane & 3;
   const int tile = blockIdx.x;
   const int split = blockIdx.y;
   const int m0 = blockIdx.z * 8 * NT;
   const int S0 = (int)((int64_t)split * a.nks / a.ks), S1 = (int)((int64_t)(split + 1) * a.nks / a.ks);
   const int ns = S1 - S0;
-  const int S = a.stages;
-  uint64_t* full = reinterpret_cast<uint64_t*>(sk_smem + a.bar_off);
-  uint64_t* empty = full + S;
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + S);
-  const uint32_t ring = ptx::smem_u32(sk_smem);
+  const int D = a.stages;
+  const int row = warp * 16 + g;  // row of the tile (and row + 8)
 
-  if (threadIdx.x == 0) {
-    for (int i = 0; i < S; ++i) {
-      ptx::mbar_init(&full[i], 1);
-      ptx::mbar_init(&empty[i], kSkConsumers / 32);
+  // ---- weight stream: this lane's slots of the warp's ring; the first D
+  // stages are requested before anything else (weights are immutable, so
+  // before the kernel this one depends on has finished)
+  const uint32_t ring = ptx::smem_u32(sk_smem) + (uint32_t)(warp * D * 32 + lane) * a.lane_bytes;
+  const uint32_t slot_stride = 32u * a.lane_bytes;
+  const unsigned char* qsrc[NW];
+  const float* ssrc[NW];
+#pragma unroll
+  for (int q = 0; q < NW; ++q) {
+    qsrc[q] = reinterpret_cast<const unsigned char*>(a.q[q]) + (size_t)tile * a.nkc * 4096 + t * 2048 + row * 16;
+    ssrc[q] = a.s[q] + (size_t)tile * a.nkb * 128 + row;
+  }
+  const int sc0 = EXACT ? 0 : (32 * t) / a.block;  // the lane's first scale block within a stage
+  constexpr uint32_t kWStride = (32 + 8 * SPL + 15) & ~15u;  // one weight's bytes in a lane's slot (16-aligned)
+  auto issue = [&](int i) {  // stage S0 + i into slot i % D
+    const int st = S0 + i;
+    const uint32_t dst = ring + (uint32_t)(i % D) * slot_stride;
+    const int kb = EXACT ? st : st * 128 / a.block + sc0;
+#pragma unroll
+    for (int q = 0; q < NW; ++q) {
+      const uint32_t d = dst + (uint32_t)q * kWStride;
+      cp_async16(d, qsrc[q] + (size_t)st * 8192);
+      cp_async16(d + 16, qsrc[q] + (size_t)st * 8192 + 128);
+#pragma unroll
+      for (int j = 0; j < SPL; ++j) {
+        cp_async4(d + 32 + 8 * j, ssrc[q] + (size_t)(kb + j) * 128);
+        cp_async4(d + 36 + 8 * j, ssrc[q] + (size_t)(kb + j) * 128 + 8);
+      }
     }
-    *abort_flag = 0;
-    ptx::fence_mbar_init();
+  };
+  for (int i = 0; i < D; ++i) {
+    if (i < ns) issue(i);
+    cp_async_commit();  // one group per slot, empty past the CTA's range
+  }
+
+  // ---- activations of the CTA's K range -> f16, swizzled shared memory
+  ptx::griddep_launch_dependents();  // the next kernel may start its own weight stream
+  ptx::griddep_wait();               // x may be the output of the kernel before this one
+  // the bias of this thread's first epilogue element (see the epilogue),
+  // loaded now so that its latency hides behind the main loop
+  const int quads = 32, elems = 8 * NT * quads;
+  const int e_first = threadIdx.x * a.ks + split;
+  const int n0 = tile * 128;
+  float bpre[NW][4];
+#pragma unroll
+  for (int q = 0; q < NW; ++q)
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      const int nc = n0 + 4 * (e_first % quads) + c;
+      bpre[q][c] = (a.bias[q] && e_first < elems && nc < a.N) ? __ldg(a.bias[q] + nc) : 0.0f;
+    }
+  {
+    // rows past M and K values past K are zeros; each thread issues the
+    // loads of kXB chunks before converting any, so their latencies overlap
+    constexpr int kXB = 4;
+    const int chunks = ns * 16;  // 8-K chunks per token row
+    const int K0 = S0 * 128;
+    const int total = 8 * NT * chunks;
+    unsigned char* xs = sk_smem + a.xs_off;
+    for (int base = threadIdx.x; base < total; base += kSkThreads * kXB) {
+      float f[kXB][8];
+      uint4 hv[kXB];
+#pragma unroll
+      for (int b = 0; b < kXB; ++b) {
+        const int idx = base + b * kSkThreads;
+        hv[b] = make_uint4(0, 0, 0, 0);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) f[b][i] = 0.0f;
+        if (idx >= total) continue;
+        const int tok = idx / chunks, c = idx - tok * chunks;
+        const int m = m0 + tok, k = K0 + c * 8;
+        if (m >= a.M) continue;
+        if (a.x_f16) {
+          const __half* xr = static_cast<const __half*>(a.x) + (size_t)m * a.ldx;
+          if (k + 8 <= a.K && a.xvec) {
+            hv[b] = *reinterpret_cast<const uint4*>(xr + k);
+          } else {
+            uint16_t e[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) e[i] = k + i < a.K ? __half_as_ushort(xr[k + i]) : (uint16_t)0;
+            hv[b] = make_uint4(e[0] | (uint32_t)e[1] << 16, e[2] | (uint32_t)e[3] << 16,
+                               e[4] | (uint32_t)e[5] << 16, e[6] | (uint32_t)e[7] << 16);
+          }
+        } else {
+          const float* xr = static_cast<const float*>(a.x) + (size_t)m * a.ldx;
+          if (k + 8 <= a.K && a.xvec) {
+            const float4 p0 = *reinterpret_cast<const float4*>(xr + k);
+            const float4 p1 = *reinterpret_cast<const float4*>(xr + k + 4);
+            f[b][0] = p0.x; f[b][1] = p0.y; f[b][2] = p0.z; f[b][3] = p0.w;
+            f[b][4] = p1.x; f[b][5] = p1.y; f[b][6] = p1.z; f[b][7] = p1.w;
+          } else {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) f[b][i] = k + i < a.K ? xr[k + i] : 0.0f;
+          }
+        }
+      }
+#pragma unroll
+      for (int b = 0; b < kXB; ++b) {
+        const int idx = base + b * kSkThreads;
+        if (idx >= total) continue;
+        const int tok = idx / chunks, c = idx - tok * chunks;
+        uint4 h = hv[b];
+        if (!a.x_f16) {
+          uint32_t p[4];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const __half2 v = __floats2half2_rn(f[b][2 * i], f[b][2 * i + 1]);
+            p[i] = *reinterpret_cast<const uint32_t*>(&v);
+          }
+          h = make_uint4(p[0], p[1], p[2], p[3]);
+        }
+        *reinterpret_cast<uint4*>(xs + (size_t)tok * a.xs_pitch + xs_chunk(c)) = h;
+      }
+    }
   }
   __syncthreads();
 
-  if (warp == kSkConsumers / 32) {
-    // ---- producer: weights are immutable, so the stream starts before the
-    // kernel this one depends on has finished
-    if (lane == 0) {
-      const uint32_t wbytes = 4 * kSkSeg + a.s_bytes;
-      int i = 0;
-      for (; i < ns && !*abort_flag; ++i) {
-        const int slot = i % S;
-        if (i >= S && !ptx::mbar_wait(&empty[slot], ((i / S) - 1) & 1, abort_flag)) {
-          sk_fail(abort_flag, a.err);
-          break;
-        }
-        const int st = S0 + i;
-        ptx::mbar_arrive_expect_tx(&full[slot], NW * wbytes);
-        unsigned char* dst = sk_smem + (size_t)slot * a.stage_bytes;
+  // ---- main loop over the CTA's stages.  The 8 MMA steps of a stage go
+  // round-robin into CH independent accumulator chains, so that mma.sync
+  // latency, not one dependent chain, sets the pace.  Step (u, p) takes the
+  // nibble pairs p and p + 2 of the lane's word u (K = 8 u + 2 p + {0,1} and
+  // 8 u + 2 p + 4 + {0,1} of its 32), and chain (2 u + p) % CH; CH is even,
+  // so a chain only ever sees one p.
+  //   EXACT: pairs 1 and 3 are unpacked without a shift (their nibbles sit
+  //   in bits 4-7 of each f16 half, so they come out as exactly 16 q) and
+  //   their chains are scaled by 1/16 (exact) when the stage's partial is
+  //   summed; each chain restarts every stage (zero-accumulator MMA), and the
+  //   partial, summed in chain order, is multiplied by the block's f32 scale.
+  //   FOLDED: every pair is unpacked to q and multiplied by f16(scale); the
+  //   chains run over all stages and are summed in chain order at the end.
+  constexpr int CH = EXACT ? (NT * NW >= 4 ? 2 : 4 / (NT * NW)) : (NT * NW >= 8 ? 2 : 8 / (NT * NW));
+  float acc[NW][NT][4];
 #pragma unroll
-        for (int w = 0; w < NW; ++w) {
-          const unsigned char* q = reinterpret_cast<const unsigned char*>(a.q[w]) +
-                                   ((size_t)tile * a.nkc + 2 * st) * 4096;
+  for (int i = 0; i < NW; ++i)
 #pragma unroll
-          for (int seg = 0; seg < 4; ++seg)
-            ptx::bulk_load(dst + w * (kSkWBytes + a.s_bytes) + seg * kSkSegStride, q + seg * kSkSeg, kSkSeg,
-                           &full[slot]);
-          const float* sc = a.s[w] + ((size_t)tile * a.nkb + (size_t)st * 128 / a.block) * 128;
-          ptx::bulk_load(dst + w * (kSkWBytes + a.s_bytes) + kSkWBytes, sc, a.s_bytes, &full[slot]);
-        }
-      }
-      // copies still in flight land before this CTA may exit (bounded)
-      for (int j = i - 1; j >= 0 && j >= i - S; --j)
-        if (!ptx::mbar_wait(&full[j % S], (j / S) & 1, abort_flag)) break;
-    }
-    __syncwarp();
-  } else {
-    const int g = lane >> 2, t = lane & 3;
-    const int row = warp * 16 + g;  // row of the tile (and row + 8)
-
-    // ---- activations of the CTA's K range -> f16, swizzled shared memory
-    ptx::griddep_launch_dependents();  // the next kernel may start its own weight stream
-    ptx::griddep_wait();               // x may be the output of the kernel before this one
-    {
-      // rows past M and K values past K are zeros; each thread issues the
-      // loads of kXB chunks before converting any, so their latencies overlap
-      constexpr int kXB = 4;
-      const int chunks = ns * 16;  // 8-K chunks per token row
-      const int K0 = S0 * 128;
-      const int total = 8 * NT * chunks;
-      unsigned char* xs = sk_smem + a.xs_off;
-      for (int base = threadIdx.x; base < total; base += kSkConsumers * kXB) {
-        float f[kXB][8];
-        uint4 hv[kXB];
-#pragma unroll
-        for (int b = 0; b < kXB; ++b) {
-          const int idx = base + b * kSkConsumers;
-          hv[b] = make_uint4(0, 0, 0, 0);
-#pragma unroll
-          for (int i = 0; i < 8; ++i) f[b][i] = 0.0f;
-          if (idx >= total) continue;
-          const int tok = idx / chunks, c = idx - tok * chunks;
-          const int m = m0 + tok, k = K0 + c * 8;
-          if (m >= a.M) continue;
-          if (a.x_f16) {
-            const __half* xr = static_cast<const __half*>(a.x) + (size_t)m * a.ldx;
-            if (k + 8 <= a.K && a.xvec) {
-              hv[b] = *reinterpret_cast<const uint4*>(xr + k);
-            } else {
-              uint16_t e[8];
-#pragma unroll
-              for (int i = 0; i < 8; ++i) e[i] = k + i < a.K ? __half_as_ushort(xr[k + i]) : (uint16_t)0;
-              hv[b] = make_uint4(e[0] | (uint32_t)e[1] << 16, e[2] | (uint32_t)e[3] << 16,
-                                 e[4] | (uint32_t)e[5] << 16, e[6] | (uint32_t)e[7] << 16);
-            }
-          } else {
-            const float* xr = static_cast<const float*>(a.x) + (size_t)m * a.ldx;
-            if (k + 8 <= a.K && a.xvec) {
-              const float4 p0 = *reinterpret_cast<const float4*>(xr + k);
-              const float4 p1 = *reinterpret_cast<const float4*>(xr + k + 4);
-              f[b][0] = p0.x; f[b][1] = p0.y; f[b][2] = p0.z; f[b][3] = p0.w;
-              f[b][4] = p1.x; f[b][5] = p1.y; f[b][6] = p1.z; f[b][7] = p1.w;
-            } else {
-#pragma unroll
-              for (int i = 0; i < 8; ++i) f[b][i] = k + i < a.K ? xr[k + i] : 0.0f;
-            }
-          }
-        }
-#pragma unroll
-        for (int b = 0; b < kXB; ++b) {
-          const int idx = base + b * kSkConsumers;
-          if (idx >= total) continue;
-          const int tok = idx / chunks, c = idx - tok * chunks;
-          uint4 h = hv[b];
-          if (!a.x_f16) {
-            uint32_t p[4];
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-              const __half2 v = __floats2half2_rn(f[b][2 * i], f[b][2 * i + 1]);
-              p[i] = *reinterpret_cast<const uint32_t*>(&v);
-            }
-            h = make_uint4(p[0], p[1], p[2], p[3]);
-          }
-          *reinterpret_cast<uint4*>(xs + (size_t)tok * a.xs_pitch + xs_chunk(c)) = h;
-        }
-      }
-    }
-    consumers_sync();
-
-    // ---- main loop over the CTA's stages.  The 8 MMA steps of a stage go
-    // round-robin into CH independent accumulator chains (so that mma.sync
-    // latency, not a dependent chain, sets the pace: NW x NT x CH >= 8 chains per
-    // warp), summed in a fixed order at the end (folded) or per stage
-    // before the scale is applied (exact).
-    constexpr int CH = NT * NW >= 8 ? 1 : 8 / (NT * NW);
-    float acc[NW][NT][4];
-#pragma unroll
-    for (int i = 0; i < NW; ++i)
-#pragma unroll
-      for (int j = 0; j < NT; ++j) acc[i][j][0] = acc[i][j][1] = acc[i][j][2] = acc[i][j][3] = 0.0f;
-    float chain[CH][NW][NT][4];  // folded: running sums per chain; exact: the stage's partial per chain
+    for (int j = 0; j < NT; ++j) acc[i][j][0] = acc[i][j][1] = acc[i][j][2] = acc[i][j][3] = 0.0f;
+  float chain[CH][NW][NT][4];
+  if constexpr (!EXACT) {
 #pragma unroll
     for (int c = 0; c < CH; ++c)
 #pragma unroll
       for (int i = 0; i < NW; ++i)
 #pragma unroll
         for (int j = 0; j < NT; ++j) chain[c][i][j][0] = chain[c][i][j][1] = chain[c][i][j][2] = chain[c][i][j][3] = 0.0f;
-    const uint32_t xs_base = ptx::smem_u32(sk_smem + a.xs_off) + (uint32_t)g * a.xs_pitch;
-    const uint32_t lane_w = (uint32_t)t * kSkSegStride + (uint32_t)row * 16;  // rows g, g + 8: + 0, + 128
-    const int sc0 = EXACT ? 0 : (32 * t) / a.block;  // the lane's first scale block within a stage
-    bool ok = true;
-    for (int i = 0; i < ns; ++i) {
-      const int slot = i % S;
-      if (!ptx::mbar_wait(&full[slot], (i / S) & 1, abort_flag)) {
-        ok = false;
-        break;
-      }
-      const uint32_t sbase = ring + (uint32_t)slot * a.stage_bytes;
-      uint4 w[NW][2];
-      float se[NW][SPL][2];
+  }
+  const uint32_t xs_base = ptx::smem_u32(sk_smem + a.xs_off) + (uint32_t)g * a.xs_pitch;
+  for (int i = 0; i < ns; ++i) {
+    cp_async_wait_dyn(D - 1);  // this lane's copies of stage i have landed (one group per stage)
+    uint4 w[NW][2];
+    float se[NW][SPL][2];
+    const uint32_t src = ring + (uint32_t)(i % D) * slot_stride;
 #pragma unroll
-      for (int q = 0; q < NW; ++q) {
-        const uint32_t wb = sbase + (uint32_t)q * (kSkWBytes + a.s_bytes);
-        w[q][0] = lds128(wb + lane_w);
-        w[q][1] = lds128(wb + lane_w + 128);
+    for (int q = 0; q < NW; ++q) {
+      const uint32_t d = src + (uint32_t)q * kWStride;
+      w[q][0] = lds128(d);
+      w[q][1] = lds128(d + 16);
 #pragma unroll
-        for (int j = 0; j < SPL; ++j) {
-          const uint32_t sa = wb + kSkWBytes + (uint32_t)(sc0 + j) * 512 + (uint32_t)row * 4;
-          se[q][j][0] = __uint_as_float(lds32(sa));
-          se[q][j][1] = __uint_as_float(lds32(sa + 32));
-        }
-      }
-      // every read of the slot is done: release it to the producer
-      __syncwarp();
-      if (lane == 0) ptx::mbar_arrive(&empty[slot]);
-      uint32_t sf[NW][4][2];
-      if constexpr (!EXACT) {
-#pragma unroll
-        for (int q = 0; q < NW; ++q)
-#pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            sf[q][u][0] = f16x2_of(se[q][u * SPL / 4][0]);
-            sf[q][u][1] = f16x2_of(se[q][u * SPL / 4][1]);
-          }
-      }
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        uint32_t af[NW][2][4];
-#pragma unroll
-        for (int q = 0; q < NW; ++q) {
-          const uint32_t lo = (&w[q][0].x)[u], hi = (&w[q][1].x)[u];
-#pragma unroll
-          for (int v = 0; v < 2; ++v) {
-            af[q][v][0] = nib_pair(lo, 2 * v);
-            af[q][v][1] = nib_pair(hi, 2 * v);
-            af[q][v][2] = nib_pair(lo, 2 * v + 1);
-            af[q][v][3] = nib_pair(hi, 2 * v + 1);
-            if constexpr (!EXACT) {
-              af[q][v][0] = hmul2(af[q][v][0], sf[q][u][0]);
-              af[q][v][1] = hmul2(af[q][v][1], sf[q][u][1]);
-              af[q][v][2] = hmul2(af[q][v][2], sf[q][u][0]);
-              af[q][v][3] = hmul2(af[q][v][3], sf[q][u][1]);
-            }
-          }
-        }
-        const uint32_t xoff = xs_base + xs_chunk(i * 16 + 4 * t + u);
-#pragma unroll
-        for (int j = 0; j < NT; ++j) {
-          const uint4 xv = lds128(xoff + (uint32_t)(8 * j) * a.xs_pitch);
-#pragma unroll
-          for (int q = 0; q < NW; ++q) {
-            mma16816(chain[(2 * u) % CH][q][j], af[q][0][0], af[q][0][1], af[q][0][2], af[q][0][3], xv.x, xv.y);
-            mma16816(chain[(2 * u + 1) % CH][q][j], af[q][1][0], af[q][1][1], af[q][1][2], af[q][1][3], xv.z,
-                     xv.w);
-          }
-        }
-      }
-      if constexpr (EXACT) {
-#pragma unroll
-        for (int q = 0; q < NW; ++q)
-#pragma unroll
-          for (int j = 0; j < NT; ++j) {
-            float p[4];
-#pragma unroll
-            for (int r = 0; r < 4; ++r) {
-              p[r] = chain[0][q][j][r];
-              chain[0][q][j][r] = 0.0f;
-#pragma unroll
-              for (int c = 1; c < CH; ++c) {
-                p[r] += chain[c][q][j][r];
-                chain[c][q][j][r] = 0.0f;
-              }
-            }
-            acc[q][j][0] = fmaf(p[0], se[q][0][0], acc[q][j][0]);
-            acc[q][j][1] = fmaf(p[1], se[q][0][0], acc[q][j][1]);
-            acc[q][j][2] = fmaf(p[2], se[q][0][1], acc[q][j][2]);
-            acc[q][j][3] = fmaf(p[3], se[q][0][1], acc[q][j][3]);
-          }
+      for (int j = 0; j < SPL; ++j) {
+        se[q][j][0] = __uint_as_float(lds32(d + 32 + 8 * j));
+        se[q][j][1] = __uint_as_float(lds32(d + 36 + 8 * j));
       }
     }
-    if (!ok) sk_fail(abort_flag, a.err);
+    uint32_t sf[NW][4][2];
     if constexpr (!EXACT) {
 #pragma unroll
       for (int q = 0; q < NW; ++q)
 #pragma unroll
-        for (int j = 0; j < NT; ++j)
+        for (int u = 0; u < 4; ++u) {
+          sf[q][u][0] = f16x2_of(se[q][u * SPL / 4][0]);
+          sf[q][u][1] = f16x2_of(se[q][u * SPL / 4][1]);
+        }
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      // af[q][p] = {row g pair p, row g+8 pair p, row g pair p+2, row g+8 pair p+2}
+      uint32_t af[NW][2][4];
+#pragma unroll
+      for (int q = 0; q < NW; ++q) {
+        const uint32_t lo = (&w[q][0].x)[u], hi = (&w[q][1].x)[u];
+        if constexpr (EXACT) {
+          const uint32_t lo8 = lo >> 8, hi8 = hi >> 8;
+          af[q][0][0] = nib_pair_at(lo, 0);
+          af[q][0][1] = nib_pair_at(hi, 0);
+          af[q][0][2] = nib_pair_at(lo8, 0);
+          af[q][0][3] = nib_pair_at(hi8, 0);
+          af[q][1][0] = nib_pair_at(lo, 1);  // 16 q
+          af[q][1][1] = nib_pair_at(hi, 1);
+          af[q][1][2] = nib_pair_at(lo8, 1);
+          af[q][1][3] = nib_pair_at(hi8, 1);
+        } else {
+#pragma unroll
+          for (int pp = 0; pp < 2; ++pp) {
+            af[q][pp][0] = hmul2(nib_pair(lo, pp), sf[q][u][0]);
+            af[q][pp][1] = hmul2(nib_pair(hi, pp), sf[q][u][1]);
+            af[q][pp][2] = hmul2(nib_pair(lo, pp + 2), sf[q][u][0]);
+            af[q][pp][3] = hmul2(nib_pair(hi, pp + 2), sf[q][u][1]);
+          }
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < NT; ++j) {
+        // token g's K values 8 u + {0..7}: word k holds K 8 u + 2 k, + 1
+        const uint4 xv = lds128(xs_base + (uint32_t)(8 * j) * a.xs_pitch + xs_chunk(i * 16 + 4 * t + u));
+#pragma unroll
+        for (int q = 0; q < NW; ++q) {
+#pragma unroll
+          for (int pp = 0; pp < 2; ++pp) {
+            const int c = (2 * u + pp) % CH;
+            const uint32_t b0 = pp ? xv.y : xv.x, b1 = pp ? xv.w : xv.z;
+            if (EXACT && 2 * u + pp < CH)
+              mma16816_zc(chain[c][q][j], af[q][pp][0], af[q][pp][1], af[q][pp][2], af[q][pp][3], b0, b1);
+            else
+              mma16816(chain[c][q][j], af[q][pp][0], af[q][pp][1], af[q][pp][2], af[q][pp][3], b0, b1);
+          }
+        }
+      }
+    }
+    // the slot's data is in registers: refill it with stage i + D
+    if (i + D < ns) issue(i + D);
+    cp_async_commit();
+    if constexpr (EXACT) {
+#pragma unroll
+      for (int q = 0; q < NW; ++q)
+#pragma unroll
+        for (int j = 0; j < NT; ++j) {
+          float p[4];
 #pragma unroll
           for (int r = 0; r < 4; ++r) {
-            float v = chain[0][q][j][r];
+            float ev = chain[0][q][j][r], od = chain[1][q][j][r];
 #pragma unroll
-            for (int c = 1; c < CH; ++c) v += chain[c][q][j][r];
-            acc[q][j][r] = v;
+            for (int c = 2; c < CH; c += 2) {
+              ev += chain[c][q][j][r];
+              od += chain[c + 1][q][j][r];
+            }
+            p[r] = fmaf(od, 0.0625f, ev);
           }
+          acc[q][j][0] = fmaf(p[0], se[q][0][0], acc[q][j][0]);
+          acc[q][j][1] = fmaf(p[1], se[q][0][0], acc[q][j][1]);
+          acc[q][j][2] = fmaf(p[2], se[q][0][1], acc[q][j][2]);
+          acc[q][j][3] = fmaf(p[3], se[q][0][1], acc[q][j][3]);
+        }
     }
-
-    // ---- the warps' tiles -> [NW][8 NT tokens][128 + 4 rows] f32 (rows of
-    // token t contiguous, so the epilogue reads 4 rows at once), over the
-    // staged activations, which every warp has finished with
-    constexpr int RP = 132;
-    consumers_sync();
-    float* red = reinterpret_cast<float*>(sk_smem + a.red_off);
+  }
+  cp_async_wait<0>();  // no copy may land after this CTA's shared memory is reused or released
+  if constexpr (!EXACT) {
 #pragma unroll
     for (int q = 0; q < NW; ++q)
 #pragma unroll
-      for (int j = 0; j < NT; ++j) {
-        float* base = red + ((size_t)q * 8 * NT + 8 * j + 2 * t) * RP + row;
-        base[0] = acc[q][j][0];
-        base[RP] = acc[q][j][1];
-        base[8] = acc[q][j][2];
-        base[RP + 8] = acc[q][j][3];
-      }
+      for (int j = 0; j < NT; ++j)
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+          float v = chain[0][q][j][r];
+#pragma unroll
+          for (int c = 1; c < CH; ++c) v += chain[c][q][j][r];
+          acc[q][j][r] = v;
+        }
   }
+
+  // ---- the warps' tiles -> [NW][8 NT tokens][128 + 4 rows] f32 (rows of
+  // token t contiguous, so the epilogue reads 4 rows at once), over the
+  // staged activations, which every warp has finished with
+  constexpr int RP = 132;
+  __syncthreads();
+  float* red = reinterpret_cast<float*>(sk_smem + a.xs_off);
+#pragma unroll
+  for (int q = 0; q < NW; ++q)
+#pragma unroll
+    for (int j = 0; j < NT; ++j) {
+      float* base = red + ((size_t)q * 8 * NT + 8 * j + 2 * t) * RP + row;
+      base[0] = acc[q][j][0];
+      base[RP] = acc[q][j][1];
+      base[8] = acc[q][j][2];
+      base[RP + 8] = acc[q][j][3];
+    }
+
   // ---- cluster sum (ranks in order) and the epilogue; rank r takes every
-  // ks-th element (the producer warp passes the barriers only)
+  // ks-th element
   if (a.ks > 1) ptx::cluster_sync();
   else __syncthreads();
-  if (warp < kSkConsumers / 32) {
-    constexpr int RP = 132;
-    const float* red = reinterpret_cast<const float*>(sk_smem + a.red_off);
-    const int quads = 32, elems = 8 * NT * quads;
-    const int e_first = threadIdx.x * a.ks + split;
-    const int n0 = tile * 128;
-    float bpre[NW][4];
-#pragma unroll
-    for (int i = 0; i < NW; ++i)
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        const int nc = n0 + 4 * (e_first % quads) + c;
-        bpre[i][c] = (a.bias[i] && e_first < elems && nc < a.N) ? __ldg(a.bias[i] + nc) : 0.0f;
-      }
-    for (int e = e_first; e < elems; e += kSkConsumers * a.ks) {
+  {
+    for (int e = e_first; e < elems; e += kSkThreads * a.ks) {
       const int tok = e / quads, rq = e - tok * quads;
       const int m = m0 + tok;
       float v[NW][4];
@@ -558,25 +600,26 @@ cudaError_t launch_sk(const SkPlan& p, const SkArgs& a, cudaStream_t stream) {
   return e;
 }
 
-// Shared-memory layout of one CTA (bytes): the ring of `stages` slots, the
-// staged activation rows (8 NT tokens x kcta stages x 128 K in f16, 16 bytes
-// of pitch padding) -- reused after the main loop for the warps' partial
-// tiles ([NW][8 NT][132] f32) -- the mbarriers and the abort flag.
+// Shared-memory layout of one CTA (bytes): the eight warps' rings of
+// `stages` slots of 32 lanes x lane_bytes (weights, then scales; an odd
+// number of 16-byte units, so the lanes of one access phase hit distinct
+// banks), then the staged activation rows (8 NT tokens x kcta stages x 128 K
+// in f16, 16 bytes of pitch padding) -- reused after the main loop for the
+// warps' partial tiles ([NW][8 NT][132] f32).
 struct SkLayout {
-  uint32_t stage_bytes, s_bytes, xs_pitch, xs_off, red_off, bar_off;
+  uint32_t lane_bytes, xs_pitch, xs_off;
   size_t total;
 };
 
-SkLayout sk_layout(int nt, int nw, int block, int kcta, int stages) {
+SkLayout sk_layout(int nt, int nw, int spl, int kcta, int stages) {
   SkLayout L;
-  L.s_bytes = 512u * (uint32_t)(block >= 128 ? 1 : 128 / block);
-  L.stage_bytes = (uint32_t)nw * (kSkWBytes + L.s_bytes);
+  uint32_t lb = (uint32_t)nw * ((32 + 8 * spl + 15) & ~15u);
+  if (((lb >> 4) & 1) == 0) lb += 16;
+  L.lane_bytes = lb;
   L.xs_pitch = (uint32_t)kcta * 256 + 16;
-  L.xs_off = (uint32_t)stages * L.stage_bytes;
-  L.red_off = L.xs_off;
+  L.xs_off = (uint32_t)(kSkThreads / 32) * (uint32_t)stages * 32u * lb;
   const uint32_t xs_bytes = 8u * nt * L.xs_pitch, red_bytes = (uint32_t)nw * 8 * nt * 132 * 4;
-  L.bar_off = L.xs_off + (((xs_bytes > red_bytes ? xs_bytes : red_bytes) + 127) & ~127u);
-  L.total = (size_t)L.bar_off + (size_t)stages * 16 + 16;
+  L.total = (size_t)L.xs_off + (xs_bytes > red_bytes ? xs_bytes : red_bytes);
   return L;
 }
 
@@ -607,16 +650,17 @@ bool plan_skinny(const bq4_weight* w, int nw, int64_t M, int device, bool exact,
     if (v >= 1 && v <= 8) ks = v;
   }
   if (ks > nks) ks = nks;
-  int kcta = (nks + ks - 1) / ks;
-  // ring: as many stages as fit next to the activations (at most the CTA's
-  // stage count), at least 2
+  const int kcta = (nks + ks - 1) / ks;
+  const int spl = exact || w->block >= 32 ? 1 : 128 / 4 / w->block;  // blocks of 16: 2, of 8: 4
+  // each warp's ring: as many stages as fit next to the activations (at most
+  // the CTA's stage count and 15), at least 2
   int stages = 2;
-  while (stages < kcta && sk_layout(nt, nw, w->block, kcta, stages + 1).total <= kSkCtaSmem) ++stages;
+  while (stages < kcta && stages < 15 && sk_layout(nt, nw, spl, kcta, stages + 1).total <= kSkCtaSmem) ++stages;
   if (const char* f = getenv("BQ4_SKINNY_STAGES")) {
     const int v = atoi(f);
     if (v >= 2 && v < stages) stages = v;
   }
-  const SkLayout L = sk_layout(nt, nw, w->block, kcta, stages);
+  const SkLayout L = sk_layout(nt, nw, spl, kcta, stages);
   if (L.total > kSkMaxSmem) return false;
   p->nt = nt;
   p->nw = nw;
@@ -656,7 +700,6 @@ bq4_status run_skinny(const SkPlan& p, const bq4_weight* const* ws, const void* 
   a.block = w0->block;
   a.ks = p.ks;
   a.stages = p.stages;
-  a.err = device_error_word();
   a.x_f16 = x_f16;
   a.y_f16 = y_f16;
   a.xvec = x_f16 ? ((reinterpret_cast<uintptr_t>(x) & 15) == 0 && ldx % 8 == 0)
@@ -671,19 +714,16 @@ bq4_status run_skinny(const SkPlan& p, const bq4_weight* const* ws, const void* 
     for (int r = 0; r < io.sc_nranks; ++r) a.sc_y[r] = io.sc_y[r];
   }
   const int kcta = (a.nks + p.ks - 1) / p.ks;
-  const SkLayout L = sk_layout(p.nt, p.nw, w0->block, kcta, p.stages);
-  a.s_bytes = L.s_bytes;
-  a.stage_bytes = L.stage_bytes;
+  const int spl = p.exact || w0->block >= 32 ? 1 : 128 / 4 / w0->block;  // blocks of 16: 2, of 8: 4
+  const SkLayout L = sk_layout(p.nt, p.nw, spl, kcta, p.stages);
+  a.lane_bytes = L.lane_bytes;
   a.xs_pitch = L.xs_pitch;
   a.xs_off = L.xs_off;
-  a.red_off = L.red_off;
-  a.bar_off = L.bar_off;
   cudaError_t e = cudaSuccess;
 #define BQ4_SK_CASE(NT_, NW_, EX_, SPL_)                           \
   if (p.nt == NT_ && p.nw == NW_ && p.exact == EX_ && spl == SPL_) \
     e = launch_sk<NT_, NW_, EX_, SPL_>(p, a, stream);               \
   else
-  const int spl = p.exact || w0->block >= 32 ? 1 : 128 / 4 / w0->block;  // blocks of 16: 2, of 8: 4
   BQ4_SK_CASE(1, 1, true, 1) BQ4_SK_CASE(2, 1, true, 1) BQ4_SK_CASE(4, 1, true, 1)
   BQ4_SK_CASE(1, 1, false, 1) BQ4_SK_CASE(2, 1, false, 1) BQ4_SK_CASE(4, 1, false, 1) BQ4_SK_CASE(8, 1, false, 1)
   BQ4_SK_CASE(1, 1, false, 2) BQ4_SK_CASE(2, 1, false, 2) BQ4_SK_CASE(4, 1, false, 2) BQ4_SK_CASE(8, 1, false, 2)

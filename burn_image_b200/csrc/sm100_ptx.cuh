@@ -88,6 +88,34 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
   }
 }
 
+// Bounded wait that polls with the non-blocking test_wait instead of parking
+// the thread: for waiters that have nothing else to do and whose phase
+// completes within a few microseconds, it avoids the wake-up latency of a
+// suspended try_wait.  Same contract as mbar_wait.
+__device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+__device__ __forceinline__ bool mbar_wait_spin(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
+  if (mbar_test_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer();
+  for (uint32_t n = 1;; ++n) {
+    if (mbar_test_wait(bar, parity)) return true;
+    if ((n & 255) == 0) {
+      if (*abort_flag) return false;
+      if (globaltimer() - t0 > kWaitTimeoutNs) return false;
+    }
+  }
+}
+
 // ---------------------------------------------------------------- fences
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
