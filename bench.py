@@ -62,6 +62,10 @@ def parse():
                          "(f32 all-reduce of the partials); auto = p2p at 2 GPUs, where it was verified bit "
                          "for bit against nccl and measured faster, nccl at more")
     ap.add_argument("--rows-only", action="store_true", help="print only the per-config rows (1 GPU)")
+    ap.add_argument("--config", choices=["stack", "c4"], default="stack",
+                    help="c4: BASELINE configs[3], the 1536 px edit projections (M=18432: fused qkv 3072->9216 "
+                         "column-sharded, o 3072->3072 row-sharded + all-reduce) at N GPUs, with a parity check "
+                         "against the unsharded projections")
     ap.add_argument("--rows", default=None, help="comma-separated row names to run (with --rows-only)")
     return ap.parse_args()
 
@@ -181,6 +185,33 @@ def cpu_sample(tokens_sample: int, repeats: int, threads: int = 0):
     return flops / dt / 1e12, dt, threads
 
 
+def cpu_config1(repeats: int = 3, threads: int = 0):
+    """BASELINE configs[0] on the CPU restatement (the reference's CPU
+    linear, crates/burn_boogu/src/model/linear.rs:51-96): x f32 [512, 2560]
+    ~N(0,1), signed-int4 weights [2560 -> 9728] in [-8, 7], block 128,
+    |U(0.001, 0.02)| scales, bias ~N(0, 0.02).  Returns (TFLOP/s, seconds of
+    the median call, threads)."""
+    import numpy as np
+
+    import oracle as O
+    if threads <= 0:
+        threads = host_cores()
+    M, K, N = 512, 2560, 9728
+    rng = np.random.default_rng(1)
+    words = rng.integers(0, 2 ** 32, size=(K // 8, N), dtype=np.uint64).astype(np.uint32)
+    scales = rng.uniform(0.001, 0.02, size=(K // QBLOCK, N)).astype(np.float32)
+    bias = (rng.standard_normal(N) * 0.02).astype(np.float32)
+    x = rng.standard_normal((M, K), dtype=np.float32)
+    O.cpu_linear(words, scales, K, N, QBLOCK, O.LAYOUT_ROW, x, bias, 0, threads=threads)  # warm-up
+    ts = []
+    for _ in range(repeats):
+        t0 = time.perf_counter()
+        O.cpu_linear(words, scales, K, N, QBLOCK, O.LAYOUT_ROW, x, bias, 0, threads=threads)
+        ts.append(time.perf_counter() - t0)
+    t = statistics.median(ts)
+    return 2 * M * K * N / t / 1e12, t, threads
+
+
 def run_reference(args):
     rank, world, _ = dist_env()
     if rank != 0:
@@ -197,16 +228,25 @@ def run_reference(args):
         secs += dt
     value = statistics.median(vals)
     flops_step = (2 * TOKENS * (HIDDEN * QKV + HIDDEN * HIDDEN + HIDDEN * MLP + MLP * HIDDEN) * args.blocks)
+    flops_sample = 2 * tokens_sample * (HIDDEN * QKV + HIDDEN * HIDDEN + HIDDEN * MLP + MLP * HIDDEN)
+    c1_value, c1_s, c1_thr = cpu_config1()
     sample = (f"one block's 4 linears (qkv/o/up+gelu/down, block 128) at {tokens_sample} of {TOKENS} tokens per step; "
               "CPU restatement of the reference q_matmul (oracle/bq4_oracle.c: dequantize + AVX2 SGEMM, OpenMP)")
     print(json.dumps({
         "impl": "reference", "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": flops_step / (value * 1e12) * 1e3, "higher_is_better": True, "scaling": "strong",
+        "ms_per_step": secs / max(args.steps, 1) * 1e3, "higher_is_better": True, "scaling": "strong",
+        "ms_per_step_note": "measured time of one step's sample (see cpu_baseline.sample); the full step "
+                            "(all 24 blocks at 4352 tokens) at the same rate is ms_per_full_step_projected",
+        "ms_per_full_step_projected": flops_step / (value * 1e12) * 1e3,
         "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": {"workload": WORKLOAD, "tokens": TOKENS, "blocks": args.blocks, "sampled_tokens": tokens_sample,
                    "parallelism": "cpu"},
-        "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": thr, "kind": "port", "sample": sample},
+        "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": thr, "kind": "port", "sample": sample,
+                         "sample_gflop": flops_sample / 1e9,
+                         "config1": {"value": c1_value, "unit": "TFLOP/s", "ms": c1_s * 1e3, "cores": c1_thr,
+                                     "workload": "BASELINE configs[0]: one Q4 linear M=512, K=2560, N=9728, "
+                                                 "block 128, bias (median of 3 calls)"}},
         "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "note": "reference NdArray q_matmul unavailable on this box (Rust toolchain absent); oracle port timed",
     }))
@@ -721,6 +761,29 @@ def run_ours(args):
         value_tokens = flops_step / (t.item() / args.steps * 1e-3) / 1e12
         del local
 
+    # ---- multi-GPU correctness: the sharded stack against the unsharded one
+    # (every rank runs both on the same input; 2 blocks, same weights)
+    tp_parity = None
+    if world > 1:
+        nb = 2
+        sh = tp.DiTQ4Stack(nb, HIDDEN, QKV, MLP, dev, seed=7, block=QBLOCK, group=group, act_dtype=act_dtype,
+                           chunks=1, exchange=exchange)
+        un = tp.DiTQ4Stack(nb, HIDDEN, QKV, MLP, dev, seed=7, block=QBLOCK, group=tp.LOCAL, act_dtype=act_dtype,
+                           chunks=1)
+        ys = sh.forward(x0).clone()
+        yu = un.forward(x0).clone()
+        barrier()
+        d = (ys.double() - yu.double())
+        rel = (torch.linalg.norm(d) / torch.linalg.norm(yu.double())).item()
+        mx = torch.tensor([rel, d.abs().max().item()], device=dev, dtype=torch.float64)
+        dist.all_reduce(mx, op=dist.ReduceOp.MAX)
+        tp_parity = {"blocks": nb, "rel_frob": mx[0].item(), "max_abs": mx[1].item(), "bar": 5e-3,
+                     "ok": bool(mx[0].item() <= 5e-3),
+                     "what": "sharded stack (this run's exchange) vs the unsharded stack on every rank, same "
+                             "weights and input; max over ranks"}
+        sh.close()
+        del sh, un
+
     # ---- e2e: through the public API with host buffers.  Every step copies its
     # input from pinned host memory and reads its output back; the copies run
     # on a copy stream, double-buffered, so step i+1's upload and step i's
@@ -777,10 +840,19 @@ def run_ours(args):
         peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
     except Exception:
         pass
-    peak = peaks.get("bf16_tflops_sustained")
-    peak_src = "measured sustained bf16 (MEASURED_PEAKS.json)"
+    # The stack's linears are timed in a step of ~19 ms at the full SM clock
+    # (the bench's clock samples), so the denominator is the burst bf16 peak;
+    # the sustained peak was measured at 1380 MHz under the power cap.
+    peak = peaks.get("bf16_tflops")
+    peak_src = "measured burst bf16 (MEASURED_PEAKS.json)"
     if peak is None:
-        peak, peak_src = 1400.0, "fallback sustained"
+        peak, peak_src = 1590.0, "fallback burst"
+    # algorithmic bytes of one GEMM launch, mean over a block's four: f16 activations in and
+    # out (chained), Q4 nibbles + f32 scales, f32 bias (this rank's shard)
+    P = world
+    lin = [(TOKENS, HIDDEN, QKV // P, 0), (TOKENS, HIDDEN // P, HIDDEN, 1), (TOKENS, HIDDEN, MLP // P, 1),
+           (TOKENS, MLP // P, HIDDEN, 1)]
+    alg_bytes = sum(m * k * 2 + k * n // 2 + k // QBLOCK * n * 4 + m * n * 2 + b * n * 4 for m, k, n, b in lin) / 4
     traffic = None
     try:
         tj = json.load(open(os.path.join(ROOT, "profiles", "traffic.json")))
@@ -798,9 +870,13 @@ def run_ours(args):
             import oracle as O
             O.build()
             v, dt, thr = cpu_sample(64, 2)
+            c1_value, c1_s, c1_thr = cpu_config1()
             cpu = {"value": v, "unit": "TFLOP/s", "cores": thr, "kind": "port",
                    "sample": f"one block's 4 linears at 64 of {M} tokens, x2 ({dt:.1f} s); CPU restatement of the "
-                             "reference q_matmul (dequantize + AVX2 SGEMM, OpenMP)"}
+                             "reference q_matmul (dequantize + AVX2 SGEMM, OpenMP)",
+                   "config1": {"value": c1_value, "unit": "TFLOP/s", "ms": c1_s * 1e3, "cores": c1_thr,
+                               "workload": "BASELINE configs[0]: one Q4 linear M=512, K=2560, N=9728, block 128, "
+                                           "bias (median of 3 calls)"}}
         except Exception as e:  # pragma: no cover
             cpu = {"value": None, "unit": "TFLOP/s", "cores": 0, "kind": "port", "sample": f"failed: {e}"}
 
@@ -818,7 +894,10 @@ def run_ours(args):
                        "l2": "inputs larger than L2 (1.44 GB of Q4 weights streamed per step)"},
             "roofline": {"bound": "tensor", "achieved": achieved_tflops, "peak": peak, "unit": "TFLOP/s",
                          "frac": achieved_tflops / peak, "traffic": traffic,
+                         "algorithmic_bytes_per_gemm_launch": alg_bytes,
+                         "traffic_over_algorithmic": (traffic / alg_bytes) if traffic else None,
                          "peak_source": peak_src,
+
                          "kernel": "q4_gemm_ws_kernel (+ activation staging where a call has f32 input), CUDA "
                                    "events around every linear call in a separate pass, rank 0"},
             "numerics": "auto: f16(q*scale) staging (the reference kernel's) at this M; "
@@ -832,6 +911,7 @@ def run_ours(args):
             "cpu_baseline": cpu,
             "rows": rows,
             "value_token_parallel": value_tokens,
+            "tp_parity": tp_parity,
             "token_parallel": None if value_tokens is None else (
                 "the alternative to tensor parallelism: each GPU runs the unsharded stack on M/N tokens, no "
                 "collective; same metric and FLOPs, max over ranks"),
@@ -839,6 +919,118 @@ def run_ours(args):
         print(json.dumps(out))
     if world > 1:
         stack.close()
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def run_c4(args):
+    """per step, the fused qkv projection (column-parallel:
+    each rank its 9216/N output features) and the o projection (row-parallel:
+    each rank its 3072/N input features, the rank's v columns of the qkv
+    output, then an all-reduce of the f32 partials), M = 18432 f32 tokens.
+    Attention is not on the Q4 path, so the o projection reads the v section
+    of the qkv output directly.  FLOPs per step = 2 M 3072 (9216 + 3072)."""
+    import torch
+    import torch.distributed as dist
+
+    from burn_image_b200 import _lib as L
+    from burn_image_b200 import q4, tp
+
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    group = None
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    M, H, QN = 18432, HIDDEN, QKV
+    g = torch.Generator(device=dev).manual_seed(4)
+    wq, sq = tp._random_packed(H, QN, QBLOCK, g, dev)
+    wo, so = tp._random_packed(H, H, QBLOCK, g, dev)
+    bo = torch.randn(H, generator=g, device=dev) * 0.02
+    x = torch.randn((M, H), generator=g, device=dev)
+    if world > 1:
+        perm = tp._qkv_rank_order(H, QN, world, dev)
+        wq_s, sq_s = wq[:, perm].contiguous(), sq[:, perm].contiguous()
+    else:
+        wq_s, sq_s = wq, sq
+    qkv = tp.ColumnParallelQ4Linear(wq_s, sq_s, H, QN, QBLOCK, L.LAYOUT_ROW, dev, group=group)
+    o = tp.RowParallelQ4Linear(wo, so, H, H, QBLOCK, L.LAYOUT_ROW, dev, bo, group=group)
+    qn_l, h_l = QN // world, H // world
+    t = torch.empty((M, qn_l), device=dev)
+    y = torch.empty((M, H), device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        qkv.forward(x, out=t)
+        o.forward(t[:, qn_l - h_l:], out=y)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    barrier()
+    clocks = ClockSampler(local)
+    clocks.start()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    clocks.mark(True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        step()
+    e1.record(stream)
+    barrier()
+    clocks.mark(False)
+    clk = clocks.stop()
+    tt = torch.tensor([e0.elapsed_time(e1)], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+    ms = tt.item() / args.steps
+    flops = 2 * M * H * (QN + H)
+    # algorithmic bytes per step and rank: x f32 in, the Q4 shards, qkv f32 out, o's
+    # v-slice in and f32 partial out (the all-reduce traffic is reported apart)
+    nbytes = (M * H * 4 + H * qn_l // 2 + H // QBLOCK * qn_l * 4 + M * qn_l * 4 + M * h_l * 4 + h_l * H // 2 +
+              h_l // QBLOCK * H * 4 + M * H * 4)
+    peaks = {}
+    try:
+        peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
+    except Exception:
+        pass
+    tfl = peaks.get("bf16_tflops", 1590.0)
+    # parity: the unsharded projections of the same weights and input, on every rank
+    ref_q = q4.PreparedQ4Weight(wq, sq, H, QN, QBLOCK, L.LAYOUT_ROW, dev)
+    ref_o = q4.PreparedQ4Weight(wo, so, H, H, QBLOCK, L.LAYOUT_ROW, dev)
+    tr = ref_q.linear(x)
+    yr = ref_o.linear(tr[:, QN - H:], bo)
+    step()
+    barrier()
+    d = y.double() - yr.double()
+    par = torch.tensor([(torch.linalg.norm(d) / torch.linalg.norm(yr.double())).item(), d.abs().max().item()],
+                       device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(par, op=dist.ReduceOp.MAX)
+    if rank == 0:
+        value = flops / (ms * 1e-3) / 1e12
+        print(json.dumps({
+            "metric": "Q4 linear TFLOP/s, 1536 px edit projections (fused qkv + o, M=18432)", "value": value,
+            "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "f16 operands, f32 accumulate (Q4 weights)", "data": "synthetic",
+            "config": {"workload": "c4_edit_qkv18432x3072x9216_colTP+o18432x3072x3072_rowTP+allreduce_b128",
+                       "parallelism": f"tp{world}" if world > 1 else "single",
+                       "l2": "inputs larger than L2 (x 226 MB f32)"},
+            "gbs_per_rank": nbytes / (ms * 1e-3) / 1e9,
+            "allreduce_bytes_per_step": M * H * 4 if world > 1 else 0,
+            "roofline": {"bound": "tensor", "achieved_per_gpu": value / world, "peak": tfl, "unit": "TFLOP/s",
+                         "frac": value / world / tfl, "peak_source": "measured burst bf16 (MEASURED_PEAKS.json)"},
+            "parity": {"rel_frob": par[0].item(), "max_abs": par[1].item(), "bar": 5e-3,
+                       "ok": bool(par[0].item() <= 5e-3),
+                       "what": "sharded output vs the unsharded projections of the same weights, max over ranks"},
+            "clocks": clk}))
+    if world > 1:
         dist.barrier()
         dist.destroy_process_group()
 
@@ -908,6 +1100,8 @@ def main():
         print(json.dumps({"rows": config_rows(torch.device("cuda", 0), peaks, names)}))
     elif args.linear or args.gated:
         run_linear(args)
+    elif args.config == "c4":
+        run_c4(args)
     else:
         run_ours(args)
 
