@@ -275,6 +275,10 @@ ROWS = [
     # next row of the path: the packed-Q4 embedding lookup (q_select + dequantize), 256
     # prompt tokens from a 151936 x 2560 table (rows = table rows, K = row width)
     ("f1_q4_embedding_256_of_151936x2560", 256, 2560, 151936, "select", 0),
+    # the row-parallel exchange's two kernels at one rank (the multi-GPU path's
+    # GEMM with its row-scatter epilogue writing the owner's receive buffer, then
+    # the owner's rank-order sum + RMS renorm into f16 rows), down-projection shape
+    ("e_rowscatter_down_1rank_4352x12288x3072", 4352, 12288, 3072, "rowscatter", 0),
     # next row: the DiT qkv projection with QK-norm + RoPE on its q and k heads (24 + 24 + 24
     # heads of 128), fused into the GEMM epilogue; "us_unfused" = linear + two norm passes
     ("f3_qkv_qknorm_rope_4352x3072x9216", 4352, 3072, 9216, "qknorm", 0),
@@ -348,6 +352,9 @@ def config_rows(dev, peaks, names=None):
         if kind == "attn":
             out[name] = _attn_row(dev, M, K, N, hbm, tfl)
             continue
+        if kind == "rowscatter":
+            out[name] = _rowscatter_row(dev, M, K, N, hbm, tfl)
+            continue
         nw = 2 if kind == "gated" else 1
         wbytes = nw * (N * K // 2 + N * K // QBLOCK * 4)
         set_bytes = wbytes + M * K * 4 + M * N * 4
@@ -420,6 +427,65 @@ def config_rows(dev, peaks, names=None):
         del items
         torch.cuda.empty_cache()
     return out
+
+
+def _rowscatter_row(dev, M, K, N, hbm, tfl):
+    """One rank of the row-parallel peer exchange: bq4_linear_rowscatter
+    (f16 activations, f32 partial rows written by the epilogue into the
+    receive buffer) and bq4_reduce_slices (sum in rank order, RMS renorm,
+    f16 rows), graph-replayed over rotating sets; times of the two and of
+    the plain f16-in / f16-out linear of the same shape for comparison."""
+    import ctypes
+
+    import torch
+
+    from burn_image_b200 import _lib as L
+    from burn_image_b200 import q4, tp
+    g = torch.Generator(device=dev).manual_seed(17)
+    lib = L.lib()
+    sets = 2
+    items = []
+    for _ in range(sets):
+        pw = q4.PreparedQ4Weight(*tp._random_packed(K, N, QBLOCK, g, dev), K, N, QBLOCK, L.LAYOUT_ROW, dev)
+        x = torch.randn((M, K), generator=g, device=dev).half()
+        recv = torch.empty((M, N), device=dev)
+        y16 = torch.empty((M, N), dtype=torch.float16, device=dev)
+        items.append((pw, x, recv, y16))
+    n = ctypes.c_size_t()
+    L.check(lib.bq4_linear_ex_workspace_size(items[0][0].handle, M, L.DTYPE_F16, ctypes.byref(n)))
+    ws = q4.Workspace.get(dev, max(n.value, 256))
+
+    def stream():
+        return ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
+
+    def scatter(it):
+        pw, x, recv, _ = it
+        targets = (ctypes.c_void_p * 1)(ctypes.c_void_p(recv.data_ptr()))
+        L.check(lib.bq4_linear_rowscatter(pw.handle, ctypes.c_void_p(x.data_ptr()), L.DTYPE_F16, M, K, None,
+                                          L.ACT_NONE, targets, 1, 0, N, ctypes.c_void_p(ws.data_ptr()),
+                                          ws.numel(), stream()))
+
+    def reduce(it):
+        _, _, recv, y16 = it
+        L.check(lib.bq4_reduce_slices(ctypes.c_void_p(recv.data_ptr()), 1, M, N, N, 1, ctypes.c_float(1e-6),
+                                      ctypes.c_void_p(y16.data_ptr()), L.DTYPE_F16, N, stream()))
+
+    def plain(it):
+        pw, x, _, y16 = it
+        pw.linear_ex(x, out=y16)
+
+    t_sc = _graph_time(dev, items, scatter)
+    t_red = _graph_time(dev, items, reduce)
+    t_plain = _graph_time(dev, items, plain)
+    q4.poll_device_error()
+    flops = 2 * M * K * N
+    red_bytes = M * N * 4 + M * N * 2
+    t_star = max((K * N // 2 + K // QBLOCK * N * 4 + M * K * 2 + M * N * 4) / (hbm * 1e9), flops / (tfl * 1e12))
+    return {"us": t_sc * 1e6, "tflops": flops / t_sc / 1e12, "bound": "tensor", "t_star_us": t_star * 1e6,
+            "frac": t_star / t_sc, "sets": sets, "kernel": "tcgen05 GEMM, row-scatter epilogue",
+            "us_plain_f16_linear": t_plain * 1e6,
+            "reduce_slices": {"us": t_red * 1e6, "gbs": red_bytes / t_red / 1e9,
+                              "frac_hbm": red_bytes / t_red / 1e9 / hbm}}
 
 
 def ws_plan_skinny(pw, M, nw):
