@@ -22,6 +22,7 @@
 #include <cuda_runtime.h>
 
 #include <atomic>
+#include <cstdlib>
 #include <cstring>
 
 #include "bq4_internal.h"
@@ -101,6 +102,33 @@ __device__ __forceinline__ uint64_t attn_add2(uint64_t a, uint64_t b) {
   return d;
 }
 
+// 2^x for two lanes on the FMA pipe instead of the MUFU unit, which the
+// exponentials of both query tiles otherwise saturate.  Cody-Waite range
+// reduction x = n + f, n = round(x), f in [-1/2, 1/2]: adding 1.5 * 2^23
+// rounds x to an integer held in the low mantissa bits of the sum t, and
+// (t - 1.5 * 2^23) is n exactly.  2^f is a degree-3 polynomial fitted here
+// by the Remez exchange for minimal relative error on [-1/2, 1/2]: 7.5e-5 in
+// f32 Horner form, below the f16 rounding of the probability (2^-11).  2^n
+// is applied by adding n to the exponent field: the bits of t shifted left by
+// 23 are n << 23 (the rest of t's bits shift out).  x is clamped at -125 so
+// that the exponent of the result stays normal (2^-125 is 0 in f16).
+__device__ __forceinline__ void attn_exp2_poly2(float x0, float x1, float& p0, float& p1) {
+  constexpr float kRound = 12582912.0f;  // 1.5 * 2^23
+  constexpr float kC0 = 0x1.fff692p-1f, kC1 = 0x1.62f31ap-1f, kC2 = 0x1.f0de1ap-3f, kC3 = 0x1.c3f76p-5f;
+  const uint64_t x = attn_pack2(fmaxf(x0, -125.0f), fmaxf(x1, -125.0f));
+  const uint64_t t = attn_add2(x, attn_pack2(kRound, kRound));
+  const uint64_t n = attn_add2(t, attn_pack2(-kRound, -kRound));
+  const uint64_t f = attn_fma2(n, attn_pack2(-1.0f, -1.0f), x);
+  uint64_t p = attn_fma2(attn_pack2(kC3, kC3), f, attn_pack2(kC2, kC2));
+  p = attn_fma2(p, f, attn_pack2(kC1, kC1));
+  p = attn_fma2(p, f, attn_pack2(kC0, kC0));
+  float pl, ph, tl, th;
+  attn_unpack2(p, pl, ph);
+  attn_unpack2(t, tl, th);
+  p0 = __int_as_float(__float_as_int(pl) + (__float_as_int(tl) << 23));
+  p1 = __int_as_float(__float_as_int(ph) + (__float_as_int(th) << 23));
+}
+
 // Max of this thread's kN raw scores; kFull: all kN keys exist (every block
 // but a ragged last one), so no key is masked.
 template <int kN, bool kFull>
@@ -131,7 +159,9 @@ __device__ __forceinline__ float attn_rowmax(const uint32_t (&r)[kN], int valid)
 // P = 2^(s c - m) for this thread's kN keys as f16 pairs into kN / 2 TMEM
 // columns of its lane from t_p (key 2 i in the low half of column i, the
 // layout the A-in-TMEM MMA reads); returns the f32 sum of the probabilities.
-template <int kN, bool kFull>
+// kPolyQ (full blocks): of every four key pairs, the first kPolyQ take the
+// FMA-pipe exponential (attn_exp2_poly2), the rest ex2.approx.
+template <int kN, bool kFull, int kPolyQ = 0>
 __device__ __forceinline__ float attn_p_store(const uint32_t (&r)[kN], int valid, float c, float m_use,
                                               uint32_t t_p) {
   if constexpr (kFull) {
@@ -144,9 +174,14 @@ __device__ __forceinline__ float attn_p_store(const uint32_t (&r)[kN], int valid
 #pragma unroll
       for (int i = 0; i < 16; i += 2) {
         const int k0 = cc * 16 + i;
-        float x0, x1;
+        float x0, x1, p0, p1;
         attn_unpack2(attn_fma2(attn_pack2(__uint_as_float(r[k0]), __uint_as_float(r[k0 + 1])), c2, m2), x0, x1);
-        const float p0 = attn_ex2(x0), p1 = attn_ex2(x1);
+        if (((i >> 1) & 3) < kPolyQ) {
+          attn_exp2_poly2(x0, x1, p0, p1);
+        } else {
+          p0 = attn_ex2(x0);
+          p1 = attn_ex2(x1);
+        }
         acc[(i >> 1) & 3] = attn_add2(acc[(i >> 1) & 3], attn_pack2(p0, p1));
         const __half2 hp = __floats2half2_rn(p0, p1);
         pk[i >> 1] = *reinterpret_cast<const uint32_t*>(&hp);
@@ -432,6 +467,283 @@ __global__ void __launch_bounds__(kAThreads, 1)
   }
 }
 
+// ---------------------------------------------------------------------------
+// Two query tiles per CTA (256 query rows), ping-ponging on the tensor core.
+//
+// With one tile, the tensor core waits for the softmax of every block: the
+// scores of block j + 1 are ready early, but P_j v_j can only start once the
+// softmax has finished block j, and the softmax's chain (TMEM load, row max,
+// exponentials, P store) is about three times as long as the two MMAs of a
+// block.  With two tiles A and B the MMA warp issues, per 128-key block j,
+//     P_A(j) v_j,  S_A(j+1) = q_A k_{j+1}^T,  P_B(j) v_j,  S_B(j+1)
+// so the tensor core runs one tile's MMAs while the other tile's softmax
+// runs, and both tiles' exponentials share the MUFU unit.
+//
+//   warp 0        TMA: q_A, q_B once; k_j, v_j^T into a 2-stage ring.
+//   warp 1        MMA issuer (one thread).
+//   warps 4..7    softmax of tile A, warps 8..11 of tile B: one thread per
+//                 query row (warp % 4 is the TMEM lane quarter), so the row
+//                 max needs no exchange between threads.
+// TMEM (512 columns): S_A 0..127, S_B 128..255 (f32), O_A 256..383, O_B
+// 384..511.  P_t (f16 pairs, 64 columns) is written into columns 64..127 of
+// S_t after the softmax has read them: keys 64..127 (in registers from the
+// max pass) into columns 96..127, then keys 0..63 (read again from columns
+// 0..63) into 64..95.
+// Ordering, all from the issue order of one thread's tcgen05.mma (they
+// execute in order) and from commits, which track every earlier MMA:
+//   * S_t(j+1) overwrites P_t(j) only after P_t(j) v_j in issue order;
+//   * s_full[t] completing for S_t(j) means P_t(j-1) v_{j-1} is done, so the
+//     softmax may rescale O_t and overwrite the P_t columns right away;
+//   * the MMA waits p_full[t] (phase j) before P_t(j) v_j; the softmax only
+//     waits s_full[t] (phase j) after arriving at p_full[t] phase j-1, so
+//     neither barrier runs more than one phase ahead of its waiter.
+// ---------------------------------------------------------------------------
+constexpr int kPThreads = 384;
+constexpr uint32_t kPSmem = 6 * kATileB + 256;  // q_A, q_B, k[2], vt[2], barriers
+constexpr uint32_t kPColO = 256;
+// Default share of the polynomial exponentials: none.  Measured at 24 heads x
+// 4352 tokens (two tiles per CTA): 272.8 us with every exponential on
+// ex2.approx, 278.8 / 286.4 / 299.3 us with one to three quarters on the FMA
+// pipe -- the MUFU unit is not what limits the kernel.
+constexpr int kAttnPolyQ = 0;
+
+// Bounded wait that ignores the abort flag: for draining this CTA's own
+// copies and MMAs before its shared memory and TMEM are released.
+__device__ __forceinline__ void attn_drain(uint64_t* bar, uint32_t parity) {
+  volatile int never = 0;
+  (void)ptx::mbar_wait(bar, parity, &never);
+}
+
+__device__ __forceinline__ void attn_ld64(uint32_t taddr, uint32_t (&r)[64]) {
+  ptx::tmem_ld_32x32b_x32(taddr, *reinterpret_cast<uint32_t(*)[32]>(r));
+  ptx::tmem_ld_32x32b_x32(taddr + 32, *reinterpret_cast<uint32_t(*)[32]>(r + 32));
+  ptx::tmem_ld_wait();
+}
+
+// kPolyQ: quarters of each full block's exponentials taken on the FMA pipe.
+template <int kPolyQ>
+__global__ void __launch_bounds__(kPThreads, 1)
+    attn_pp_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
+                   const __grid_constant__ CUtensorMap tvt, const AttnArgs a) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  if (ptx::smem_u32(smem_raw) & 1023) {  // uniform: every thread leaves before any barrier
+    if (threadIdx.x == 0 && a.err) atomicCAS(a.err, 0, (int)BQ4_EALIGN);
+    return;
+  }
+  uint8_t* qs = smem_raw;                // [2] query tiles
+  uint8_t* ks = qs + 2 * kATileB;        // [kAKV]
+  uint8_t* vs = ks + kAKV * kATileB;     // [kAKV]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(vs + kAKV * kATileB);
+  uint64_t* q_full = bars;
+  uint64_t* k_full = bars + 1;           // [kAKV]
+  uint64_t* k_empty = k_full + kAKV;     // [kAKV]
+  uint64_t* v_full = k_empty + kAKV;     // [kAKV]
+  uint64_t* v_empty = v_full + kAKV;     // [kAKV]
+  uint64_t* s_full = v_empty + kAKV;     // [tile]
+  uint64_t* p_full = s_full + 2;         // [tile]: lane 0 of each of the tile's 4 softmax warps
+  uint64_t* o_done = p_full + 2;         // the last P_B v (and with it every MMA) has completed
+  uint64_t* drain = o_done + 1;          // the MMA issuer's own end-of-work commit
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);  // 15 barriers: 120 of the 256 bytes
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int bh = blockIdx.x / a.qtiles, qt = blockIdx.x - bh * a.qtiles;
+  const int b = bh / a.Hq, h = bh - b * a.Hq;
+  const int bkv = b * a.Hkv + h / (a.Hq / a.Hkv);
+  const int nblk = a.nblk;
+
+  if (threadIdx.x == 0) {
+    ptx::mbar_init(q_full, 1);
+    for (int i = 0; i < kAKV; ++i) {
+      ptx::mbar_init(&k_full[i], 1);
+      ptx::mbar_init(&k_empty[i], 1);
+      ptx::mbar_init(&v_full[i], 1);
+      ptx::mbar_init(&v_empty[i], 1);
+    }
+    for (int t = 0; t < 2; ++t) {
+      ptx::mbar_init(&s_full[t], 1);
+      ptx::mbar_init(&p_full[t], 4);
+    }
+    ptx::mbar_init(o_done, 1);
+    ptx::mbar_init(drain, 1);
+    *abort_flag = 0;
+    ptx::fence_mbar_init();
+  }
+  if (warp == 1) {
+    ptx::tmem_alloc(tmem_slot, 512);
+    ptx::tmem_relinquish();
+  }
+  ptx::tc_fence_before();
+  __syncthreads();
+  ptx::tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ------------------------------------------------ TMA producer
+      ptx::prefetch_tmap(&tq);
+      ptx::prefetch_tmap(&tk);
+      ptx::prefetch_tmap(&tvt);
+      ptx::griddep_wait();
+      const int qrow = bh * a.Sq + qt * 256;
+      ptx::mbar_arrive_expect_tx(q_full, 2 * kATileB);
+      for (int t = 0; t < 2; ++t) {
+        ptx::tma_load_2d(qs + t * kATileB, &tq, q_full, 0, qrow + t * 128);
+        ptx::tma_load_2d(qs + t * kATileB + kASub, &tq, q_full, 64, qrow + t * 128);
+      }
+      int k_issued = 0, v_issued = 0;  // blocks whose k / v loads were issued
+      for (int j = 0; j < nblk; ++j) {
+        const int st = j % kAKV;
+        const uint32_t ph = (j / kAKV) & 1;
+        if (!attn_wait(&k_empty[st], ph ^ 1, abort_flag, a.err)) break;
+        const int krow = bkv * a.Skv + j * 128;
+        ptx::mbar_arrive_expect_tx(&k_full[st], kATileB);
+        ptx::tma_load_2d(ks + st * kATileB, &tk, &k_full[st], 0, krow);
+        ptx::tma_load_2d(ks + st * kATileB + kASub, &tk, &k_full[st], 64, krow);
+        k_issued = j + 1;
+        if (!attn_wait(&v_empty[st], ph ^ 1, abort_flag, a.err)) break;
+        ptx::mbar_arrive_expect_tx(&v_full[st], kATileB);
+        ptx::tma_load_2d(vs + st * kATileB, &tvt, &v_full[st], j * 128, bkv * 128);
+        ptx::tma_load_2d(vs + st * kATileB + kASub, &tvt, &v_full[st], j * 128 + 64, bkv * 128);
+        v_issued = j + 1;
+      }
+      // every copy this thread started has landed before the CTA may exit
+      // (on the normal path the MMAs consumed them all: these return at once)
+      attn_drain(q_full, 0);
+      for (int j = (k_issued > kAKV ? k_issued - kAKV : 0); j < k_issued; ++j)
+        attn_drain(&k_full[j % kAKV], (j / kAKV) & 1);
+      for (int j = (v_issued > kAKV ? v_issued - kAKV : 0); j < v_issued; ++j)
+        attn_drain(&v_full[j % kAKV], (j / kAKV) & 1);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ------------------------------------------------ MMA issuer
+      constexpr uint32_t idesc = ptx::umma_idesc_f16(128, 128);
+      const uint32_t q_a = ptx::smem_u32(qs);
+      bool ok = attn_wait(q_full, 0, abort_flag, a.err);
+      // S_t(j) = q_t k_j^T into columns 128 t; tile A is k_j's first reader, tile B its last
+      auto issue_s = [&](int t, int j) -> bool {
+        const int kst = j % kAKV;
+        if (t == 0 && !attn_wait(&k_full[kst], (j / kAKV) & 1, abort_flag, a.err)) return false;
+        ptx::tc_fence_after();
+        const uint32_t k_a = ptx::smem_u32(ks + kst * kATileB), qa = q_a + (uint32_t)t * kATileB;
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          const uint32_t off = (uint32_t)(kk >> 2) * kASub + (uint32_t)(kk & 3) * 32;
+          ptx::mma_f16_ss(tmem + (uint32_t)t * 128, ptx::umma_desc_sw128(qa + off), ptx::umma_desc_sw128(k_a + off),
+                          idesc, kk > 0 ? 1u : 0u);
+        }
+        ptx::mma_commit(&s_full[t]);
+        if (t == 1) ptx::mma_commit(&k_empty[kst]);
+        return true;
+      };
+      // O_t (+)= P_t(j) v_j with P_t read from columns 128 t + 64 .. 127
+      auto issue_pv = [&](int t, int j) -> bool {
+        const int vst = j % kAKV;
+        if (!attn_wait(&p_full[t], j & 1, abort_flag, a.err)) return false;
+        if (t == 0 && !attn_wait(&v_full[vst], (j / kAKV) & 1, abort_flag, a.err)) return false;
+        ptx::tc_fence_after();
+        const uint32_t v_a = ptx::smem_u32(vs + vst * kATileB);
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          const uint32_t off = (uint32_t)(kk >> 2) * kASub + (uint32_t)(kk & 3) * 32;
+          ptx::mma_f16_ts(tmem + kPColO + (uint32_t)t * 128, tmem + (uint32_t)t * 128 + 64 + (uint32_t)kk * 8,
+                          ptx::umma_desc_sw128(v_a + off), idesc, (j > 0 || kk > 0) ? 1u : 0u);
+        }
+        if (t == 1) {
+          ptx::mma_commit(&v_empty[vst]);
+          if (j == nblk - 1) ptx::mma_commit(o_done);
+        }
+        return true;
+      };
+      if (ok) ok = issue_s(0, 0);
+      if (ok) ok = issue_s(1, 0);
+      for (int j = 0; ok && j < nblk; ++j) {
+        ok = issue_pv(0, j);
+        if (ok && j + 1 < nblk) ok = issue_s(0, j + 1);
+        if (ok) ok = issue_pv(1, j);
+        if (ok && j + 1 < nblk) ok = issue_s(1, j + 1);
+      }
+      // every MMA this thread issued has completed before TMEM is released
+      ptx::mma_commit(drain);
+      attn_drain(drain, 0);
+    }
+  } else if (warp >= 4) {
+    // ------------------------------------------------ softmax: one thread per query row of tile t
+    const int t = (warp - 4) >> 2, q = warp & 3;
+    const int row = q * 32 + lane;
+    const uint32_t t_lane = tmem + ((uint32_t)(q * 32) << 16);
+    const uint32_t t_s = t_lane + (uint32_t)t * 128, t_o = t_lane + kPColO + (uint32_t)t * 128;
+    const float c = a.c;
+    float m = -INFINITY, l = 0.0f;
+    bool ok = true;
+    uint32_t r[64];
+    for (int j = 0; j < nblk && ok; ++j) {
+      ok = __all_sync(0xffffffffu, attn_wait(&s_full[t], j & 1, abort_flag, a.err));
+      if (!ok) break;
+      ptx::tc_fence_after();
+      const int valid0 = a.Skv - j * 128, valid1 = valid0 - 64;  // keys present in each 64-key half
+      const bool full = valid0 >= 128;                           // warp-uniform
+      attn_ld64(t_s, r);
+      float pm = full ? attn_rowmax<64, true>(r, valid0) : attn_rowmax<64, false>(r, valid0);
+      attn_ld64(t_s + 64, r);  // kept for the P pass
+      pm = fmaxf(pm, full ? attn_rowmax<64, true>(r, valid1) : attn_rowmax<64, false>(r, valid1));
+      const float mx = c * pm;
+      const bool jump = j == 0 || mx > m + kRescaleLog2;
+      const float m_use = jump ? fmaxf(m, mx) : m;
+      const float alpha = (j > 0 && jump) ? exp2f(m - m_use) : 1.0f;
+      // keys 64..127 -> P columns 96..127 (S columns already read), then keys 0..63 -> 64..95
+      float psum = full ? attn_p_store<64, true, kPolyQ>(r, valid1, c, m_use, t_s + 96)
+                        : attn_p_store<64, false>(r, valid1, c, m_use, t_s + 96);
+      attn_ld64(t_s, r);
+      psum += full ? attn_p_store<64, true, kPolyQ>(r, valid0, c, m_use, t_s + 64)
+                   : attn_p_store<64, false>(r, valid0, c, m_use, t_s + 64);
+      if (j > 0 && __any_sync(0xffffffffu, jump)) {
+        // O_t holds P_t(j-1) v_{j-1}: s_full's commit for S_t(j) covered it
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+          attn_ld64(t_o + half * 64, r);
+#pragma unroll
+          for (int i = 0; i < 64; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
+#pragma unroll
+          for (int cc = 0; cc < 4; ++cc)
+            ptx::tmem_st_32x32b_x16(t_o + half * 64 + cc * 16, *reinterpret_cast<const uint32_t(*)[16]>(r + cc * 16));
+        }
+      }
+      l = l * alpha + psum;
+      m = m_use;
+      ptx::tmem_st_wait();  // P (and a rescaled O) in TMEM before the MMA reads them
+      ptx::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) ptx::mbar_arrive(&p_full[t]);
+    }
+    if (ok) ok = __all_sync(0xffffffffu, attn_wait(o_done, 0, abort_flag, a.err));
+    if (ok) {
+      ptx::tc_fence_after();
+      const float inv = 1.0f / l;
+      const int qrow = qt * 256 + t * 128 + row;
+      float* o = a.out + ((size_t)bh * a.Sq + qrow) * 128;
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        attn_ld64(t_o + half * 64, r);
+        if (qrow < a.Sq) {
+#pragma unroll
+          for (int i = 0; i < 64; i += 4)
+            *reinterpret_cast<float4*>(o + half * 64 + i) =
+                make_float4(__uint_as_float(r[i]) * inv, __uint_as_float(r[i + 1]) * inv,
+                            __uint_as_float(r[i + 2]) * inv, __uint_as_float(r[i + 3]) * inv);
+        }
+      }
+    }
+  }
+  ptx::tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    ptx::tc_fence_after();
+    ptx::tmem_dealloc(tmem, 512);
+  }
+}
+
 // v [B*Hkv][Skv][128] f16 -> v^T [B*Hkv][128][pitch] f16, zero for keys >= Skv;
 // 32 x 32 tiles through shared memory.
 __global__ void attn_vt_kernel(const uint16_t* __restrict__ v, int Skv, int pitch, uint16_t* __restrict__ vt) {
@@ -508,25 +820,41 @@ bq4_status attn_fused(const uint16_t* q, const uint16_t* k, const uint16_t* v, i
   if (!attn_tmap(&tq, q, 128, (uint64_t)(B * Hq * Sq), 128) || !attn_tmap(&tk, k, 128, (uint64_t)(B * Hkv * Skv), 128) ||
       !attn_tmap(&tvt, vt, (uint64_t)pitch, (uint64_t)(B * Hkv * 128), (uint64_t)pitch))
     return set_error(BQ4_ECUDA, "cuTensorMapEncodeTiled failed for the attention operands");
+  // Two query tiles per CTA whenever a head has more than one 128-row tile
+  // (BQ4_ATTN_ONE_TILE=1 keeps one tile per CTA); BQ4_ATTN_POLY=0..3 sets how
+  // many quarters of its exponentials take the FMA-pipe polynomial.
+  const bool two = Sq > 128 && !getenv("BQ4_ATTN_ONE_TILE");
+  int poly = kAttnPolyQ;
+  if (const char* f = getenv("BQ4_ATTN_POLY")) {
+    const int v = atoi(f);
+    if (v >= 0 && v <= 3) poly = v;
+  }
+  auto pp = poly == 0 ? attn_pp_kernel<0> : poly == 1 ? attn_pp_kernel<1> : poly == 2 ? attn_pp_kernel<2>
+                                                                                       : attn_pp_kernel<3>;
   AttnArgs a;
   a.out = out;
   a.Sq = (int)Sq;
   a.Skv = (int)Skv;
   a.Hq = (int)Hq;
   a.Hkv = (int)Hkv;
-  a.qtiles = (int)((Sq + 127) / 128);
+  a.qtiles = (int)(two ? (Sq + 255) / 256 : (Sq + 127) / 128);
   a.nblk = (int)((Skv + 127) / 128);
   a.c = scale * 1.4426950408889634f;  // log2(e): exp(x) = exp2(x log2 e)
   a.err = device_error_word();
-  static std::atomic<bool> attr_set[64];  // per-device function attribute, set once
+  static std::atomic<int> attr_set[64];  // per-device function attributes (bit 0 one tile, 1 + poly two), set once
   int dev = 0;
   cudaGetDevice(&dev);
-  if (dev < 0 || dev >= 64 || !attr_set[dev].load(std::memory_order_relaxed)) {
-    e = cudaFuncSetAttribute(attn_fused_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kASmem);
+  const int bit = two ? 2 << poly : 1;
+  if (dev < 0 || dev >= 64 || !(attr_set[dev].load(std::memory_order_relaxed) & bit)) {
+    e = two ? cudaFuncSetAttribute(pp, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kPSmem)
+            : cudaFuncSetAttribute(attn_fused_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kASmem);
     if (e != cudaSuccess) return check_cuda(e, "attention shared-memory attribute");
-    if (dev >= 0 && dev < 64) attr_set[dev].store(true, std::memory_order_relaxed);
+    if (dev >= 0 && dev < 64) attr_set[dev].fetch_or(bit, std::memory_order_relaxed);
   }
-  attn_fused_kernel<<<(unsigned)(B * Hq * a.qtiles), kAThreads, kASmem, s>>>(tq, tk, tvt, a);
+  if (two)
+    pp<<<(unsigned)(B * Hq * a.qtiles), kPThreads, kPSmem, s>>>(tq, tk, tvt, a);
+  else
+    attn_fused_kernel<<<(unsigned)(B * Hq * a.qtiles), kAThreads, kASmem, s>>>(tq, tk, tvt, a);
   note_launch();
   return check_cuda(cudaGetLastError(), "fused attention launch");
 }

@@ -61,6 +61,7 @@ struct SkArgs {
   int64_t ldx, ldy;
   int M, N, K;
   int nkc, nkb, nks, block;
+  int kb_stage;   // scale blocks per 128-K stage (128 / block)
   int ks;         // CTAs per cluster along K (grid.y)
   int stages;     // depth D of each warp's ring
   uint32_t lane_bytes;  // ring bytes per lane per stage (weights, then scales)
@@ -231,10 +232,14 @@ __global__ void __launch_bounds__(kSkThreads, 2) q4_skinny_kernel(const SkArgs a
   }
   const int sc0 = EXACT ? 0 : (32 * t) / a.block;  // the lane's first scale block within a stage
   constexpr uint32_t kWStride = (32 + 8 * SPL + 15) & ~15u;  // one weight's bytes in a lane's slot (16-aligned)
-  auto issue = [&](int i) {  // stage S0 + i into slot i % D
+  uint32_t fill = ring;  // the slot the next stage is copied into (the ring wraps after D slots)
+  const uint32_t ring_end = ring + (uint32_t)D * slot_stride;
+  auto issue = [&](int i) {  // stage S0 + i into the next slot (slot i % D)
     const int st = S0 + i;
-    const uint32_t dst = ring + (uint32_t)(i % D) * slot_stride;
-    const int kb = EXACT ? st : st * 128 / a.block + sc0;
+    const uint32_t dst = fill;
+    fill += slot_stride;
+    if (fill == ring_end) fill = ring;
+    const int kb = EXACT ? st : st * a.kb_stage + sc0;
 #pragma unroll
     for (int q = 0; q < NW; ++q) {
       const uint32_t d = dst + (uint32_t)q * kWStride;
@@ -362,12 +367,18 @@ __global__ void __launch_bounds__(kSkThreads, 2) q4_skinny_kernel(const SkArgs a
 #pragma unroll
         for (int j = 0; j < NT; ++j) chain[c][i][j][0] = chain[c][i][j][1] = chain[c][i][j][2] = chain[c][i][j][3] = 0.0f;
   }
+  // token g's row of staged activations; stage i's chunk 4 t + u sits at
+  // i * 256 + xs_chunk(4 t + u) (the swizzle only moves bit 1 of the chunk
+  // index within each 16-chunk stage)
   const uint32_t xs_base = ptx::smem_u32(sk_smem + a.xs_off) + (uint32_t)g * a.xs_pitch;
+  uint32_t xoff[4];
+#pragma unroll
+  for (int u = 0; u < 4; ++u) xoff[u] = xs_chunk(4 * t + u);
+  uint32_t src = ring;  // the slot of stage i
   for (int i = 0; i < ns; ++i) {
     cp_async_wait_dyn(D - 1);  // this lane's copies of stage i have landed (one group per stage)
     uint4 w[NW][2];
     float se[NW][SPL][2];
-    const uint32_t src = ring + (uint32_t)(i % D) * slot_stride;
 #pragma unroll
     for (int q = 0; q < NW; ++q) {
       const uint32_t d = src + (uint32_t)q * kWStride;
@@ -419,7 +430,7 @@ __global__ void __launch_bounds__(kSkThreads, 2) q4_skinny_kernel(const SkArgs a
 #pragma unroll
       for (int j = 0; j < NT; ++j) {
         // token g's K values 8 u + {0..7}: word k holds K 8 u + 2 k, + 1
-        const uint4 xv = lds128(xs_base + (uint32_t)(8 * j) * a.xs_pitch + xs_chunk(i * 16 + 4 * t + u));
+        const uint4 xv = lds128(xs_base + (uint32_t)(8 * j) * a.xs_pitch + (uint32_t)i * 256u + xoff[u]);
 #pragma unroll
         for (int q = 0; q < NW; ++q) {
 #pragma unroll
@@ -437,6 +448,8 @@ __global__ void __launch_bounds__(kSkThreads, 2) q4_skinny_kernel(const SkArgs a
     // the slot's data is in registers: refill it with stage i + D
     if (i + D < ns) issue(i + D);
     cp_async_commit();
+    src += slot_stride;
+    if (src == ring_end) src = ring;
     if constexpr (EXACT) {
 #pragma unroll
       for (int q = 0; q < NW; ++q)
@@ -698,6 +711,7 @@ bq4_status run_skinny(const SkPlan& p, const bq4_weight* const* ws, const void* 
   a.nkb = (int)w0->nkb;
   a.nks = (int)(w0->Kp / 128);
   a.block = w0->block;
+  a.kb_stage = 128 / w0->block;
   a.ks = p.ks;
   a.stages = p.stages;
   a.x_f16 = x_f16;

@@ -80,6 +80,46 @@ def test_fused_matches_unfused(monkeypatch):
     assert rel <= 3e-3, f"rel {rel}"
 
 
+@pytest.mark.parametrize("Sq,Skv", [(512, 384), (256, 40), (384, 64), (640, 129), (129, 200)])
+def test_two_query_tiles(Sq, Skv, monkeypatch):
+    # more than 128 query rows: two 128-row tiles per CTA (the last CTA's second tile may be
+    # partly or wholly past Sq); full key blocks, one block of fewer than 64 keys, the 64- and
+    # 128-key edges.  Against the oracle, and against one tile per CTA (BQ4_ATTN_ONE_TILE=1),
+    # which sums the probabilities in another order and takes every exponential from
+    # ex2.approx: the two-tile kernel's polynomial exponentials (relative error 7.5e-5) move
+    # about 1 % of those f16 probabilities by one ulp.
+    g = torch.Generator(device=DEV).manual_seed(Sq * 7 + Skv)
+    q = torch.randn((1, 4, Sq, 128), generator=g, device=DEV).half()
+    k = torch.randn((1, 2, Skv, 128), generator=g, device=DEV).half()
+    v = torch.randn((1, 2, Skv, 128), generator=g, device=DEV).half()
+    two, _ = _check(q, k, v)
+    monkeypatch.setenv("BQ4_ATTN_ONE_TILE", "1")
+    one, _ = _check(q, k, v)
+    rel = (torch.linalg.norm(two.double() - one.double()) / torch.linalg.norm(one.double())).item()
+    assert rel <= 2e-4, f"rel {rel}"
+    if Sq == 512:
+        # every polynomial share gives the oracle's result; without it the tiles match one tile per CTA closely
+        monkeypatch.delenv("BQ4_ATTN_ONE_TILE")
+        for poly in ("0", "2", "3"):
+            monkeypatch.setenv("BQ4_ATTN_POLY", poly)
+            out, _ = _check(q, k, v)
+            if poly == "0":
+                rel0 = (torch.linalg.norm(out.double() - one.double()) / torch.linalg.norm(one.double())).item()
+                assert rel0 <= 1e-5, f"rel {rel0}"
+
+
+def test_running_max_jumps():
+    # scores grow along the keys, so a row's block max passes its running max by more than
+    # the 2^8 margin in later blocks: O is rescaled in TMEM between blocks
+    g = torch.Generator(device=DEV).manual_seed(3)
+    Sq, Skv = 300, 1000
+    q = (torch.randn((1, 2, Sq, 128), generator=g, device=DEV) * 0.25 + 1.0).half()
+    ramp = torch.linspace(0.0, 3.0, Skv, device=DEV)[:, None]
+    k = ((torch.randn((1, 1, Skv, 128), generator=g, device=DEV) * 0.25 + 1.0) * ramp).half()
+    v = torch.randn((1, 1, Skv, 128), generator=g, device=DEV).half()
+    _check(q, k, v)
+
+
 def test_dit_size_slice():
     # 24 heads of 128 over 4352 tokens (the DiT block at 1024 px); query rows sampled
     g = torch.Generator(device=DEV).manual_seed(11)
