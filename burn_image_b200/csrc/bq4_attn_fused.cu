@@ -477,7 +477,13 @@ __global__ void __launch_bounds__(kAThreads, 1)
 // block.  With two tiles A and B the MMA warp issues, per 128-key block j,
 //     P_A(j) v_j,  S_A(j+1) = q_A k_{j+1}^T,  P_B(j) v_j,  S_B(j+1)
 // so the tensor core runs one tile's MMAs while the other tile's softmax
-// runs, and both tiles' exponentials share the MUFU unit.
+// runs, and both tiles' exponentials share the MUFU unit.  Each P_t(j) v_j
+// goes in two halves: keys 64..127 once the softmax has stored their
+// probabilities (p_half), keys 0..63 once it has stored the rest (p_full),
+// so half of the P v MMAs overlap the softmax's second exponential pass.
+// (Measured on B200, one 128x128x16 tcgen05.mma takes about 108 cycles with
+// both operands in shared memory and 95 with A in TMEM, against 64 of
+// arithmetic: the S and P v MMAs of a tile's block take about 1600 cycles.)
 //
 //   warp 0        TMA: q_A, q_B once; k_j, v_j^T into a 2-stage ring.
 //   warp 1        MMA issuer (one thread).
@@ -494,9 +500,12 @@ __global__ void __launch_bounds__(kAThreads, 1)
 //   * S_t(j+1) overwrites P_t(j) only after P_t(j) v_j in issue order;
 //   * s_full[t] completing for S_t(j) means P_t(j-1) v_{j-1} is done, so the
 //     softmax may rescale O_t and overwrite the P_t columns right away;
-//   * the MMA waits p_full[t] (phase j) before P_t(j) v_j; the softmax only
-//     waits s_full[t] (phase j) after arriving at p_full[t] phase j-1, so
-//     neither barrier runs more than one phase ahead of its waiter.
+//   * the MMA waits p_half[t] / p_full[t] (phase j) before the halves of
+//     P_t(j) v_j; the softmax only waits s_full[t] (phase j) after arriving
+//     at both for phase j-1, so no barrier runs more than one phase ahead of
+//     its waiter;
+//   * a rescale of O_t (a jump of the row max) is stored before p_half, so
+//     no half of P_t(j) v_j adds into O_t before it is scaled.
 // ---------------------------------------------------------------------------
 constexpr int kPThreads = 384;
 constexpr uint32_t kPSmem = 6 * kATileB + 256;  // q_A, q_B, k[2], vt[2], barriers
@@ -540,10 +549,11 @@ __global__ void __launch_bounds__(kPThreads, 1)
   uint64_t* v_full = k_empty + kAKV;     // [kAKV]
   uint64_t* v_empty = v_full + kAKV;     // [kAKV]
   uint64_t* s_full = v_empty + kAKV;     // [tile]
-  uint64_t* p_full = s_full + 2;         // [tile]: lane 0 of each of the tile's 4 softmax warps
+  uint64_t* p_half = s_full + 2;         // [tile]: P of keys 64..127 stored (lane 0 of the tile's 4 softmax warps)
+  uint64_t* p_full = p_half + 2;         // [tile]: P of keys 0..63 stored
   uint64_t* o_done = p_full + 2;         // the last P_B v (and with it every MMA) has completed
   uint64_t* drain = o_done + 1;          // the MMA issuer's own end-of-work commit
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);  // 15 barriers: 120 of the 256 bytes
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);  // 17 barriers: 136 of the 256 bytes
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -562,6 +572,7 @@ __global__ void __launch_bounds__(kPThreads, 1)
     }
     for (int t = 0; t < 2; ++t) {
       ptx::mbar_init(&s_full[t], 1);
+      ptx::mbar_init(&p_half[t], 4);
       ptx::mbar_init(&p_full[t], 4);
     }
     ptx::mbar_init(o_done, 1);
@@ -637,20 +648,24 @@ __global__ void __launch_bounds__(kPThreads, 1)
         if (t == 1) ptx::mma_commit(&k_empty[kst]);
         return true;
       };
-      // O_t (+)= P_t(j) v_j with P_t read from columns 128 t + 64 .. 127
-      auto issue_pv = [&](int t, int j) -> bool {
+      // O_t (+)= P_t(j) v_j with P_t read from columns 128 t + 64 .. 127, in
+      // two halves: keys 64..127 (P columns 96..127, K steps 4..7; the first
+      // MMA of block 0 starts the accumulator) after p_half, keys 0..63
+      // (columns 64..95) after p_full
+      auto issue_pv = [&](int t, int j, int half) -> bool {
         const int vst = j % kAKV;
-        if (!attn_wait(&p_full[t], j & 1, abort_flag, a.err)) return false;
-        if (t == 0 && !attn_wait(&v_full[vst], (j / kAKV) & 1, abort_flag, a.err)) return false;
+        if (!attn_wait(half ? &p_full[t] : &p_half[t], j & 1, abort_flag, a.err)) return false;
+        if (t == 0 && !half && !attn_wait(&v_full[vst], (j / kAKV) & 1, abort_flag, a.err)) return false;
         ptx::tc_fence_after();
         const uint32_t v_a = ptx::smem_u32(vs + vst * kATileB);
 #pragma unroll
-        for (int kk = 0; kk < 8; ++kk) {
+        for (int i = 0; i < 4; ++i) {
+          const int kk = half ? i : 4 + i;
           const uint32_t off = (uint32_t)(kk >> 2) * kASub + (uint32_t)(kk & 3) * 32;
           ptx::mma_f16_ts(tmem + kPColO + (uint32_t)t * 128, tmem + (uint32_t)t * 128 + 64 + (uint32_t)kk * 8,
-                          ptx::umma_desc_sw128(v_a + off), idesc, (j > 0 || kk > 0) ? 1u : 0u);
+                          ptx::umma_desc_sw128(v_a + off), idesc, (j > 0 || half || i > 0) ? 1u : 0u);
         }
-        if (t == 1) {
+        if (t == 1 && half) {
           ptx::mma_commit(&v_empty[vst]);
           if (j == nblk - 1) ptx::mma_commit(o_done);
         }
@@ -659,9 +674,9 @@ __global__ void __launch_bounds__(kPThreads, 1)
       if (ok) ok = issue_s(0, 0);
       if (ok) ok = issue_s(1, 0);
       for (int j = 0; ok && j < nblk; ++j) {
-        ok = issue_pv(0, j);
+        ok = issue_pv(0, j, 0) && issue_pv(0, j, 1);
         if (ok && j + 1 < nblk) ok = issue_s(0, j + 1);
-        if (ok) ok = issue_pv(1, j);
+        if (ok) ok = issue_pv(1, j, 0) && issue_pv(1, j, 1);
         if (ok && j + 1 < nblk) ok = issue_s(1, j + 1);
       }
       // every MMA this thread issued has completed before TMEM is released
@@ -692,27 +707,33 @@ __global__ void __launch_bounds__(kPThreads, 1)
       const bool jump = j == 0 || mx > m + kRescaleLog2;
       const float m_use = jump ? fmaxf(m, mx) : m;
       const float alpha = (j > 0 && jump) ? exp2f(m - m_use) : 1.0f;
-      // keys 64..127 -> P columns 96..127 (S columns already read), then keys 0..63 -> 64..95
+      if (j > 0 && __any_sync(0xffffffffu, jump)) {
+        // O_t holds P_t(j-1) v_{j-1} (s_full's commit for S_t(j) covered it);
+        // scaled 16 columns at a time, before any half of P_t(j) v_j is issued
+#pragma unroll
+        for (int cc = 0; cc < 8; ++cc) {
+          uint32_t o[16];
+          ptx::tmem_ld_32x32b_x16(t_o + cc * 16, o);
+          ptx::tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 16; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+          ptx::tmem_st_32x32b_x16(t_o + cc * 16, o);
+        }
+      }
+      // keys 64..127 -> P columns 96..127 (S columns already read): their half of P v may start
       float psum = full ? attn_p_store<64, true, kPolyQ>(r, valid1, c, m_use, t_s + 96)
                         : attn_p_store<64, false>(r, valid1, c, m_use, t_s + 96);
+      ptx::tmem_st_wait();  // P (and a rescaled O) in TMEM before the MMA reads them
+      ptx::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) ptx::mbar_arrive(&p_half[t]);
+      // keys 0..63 (read again) -> P columns 64..95
       attn_ld64(t_s, r);
       psum += full ? attn_p_store<64, true, kPolyQ>(r, valid0, c, m_use, t_s + 64)
                    : attn_p_store<64, false>(r, valid0, c, m_use, t_s + 64);
-      if (j > 0 && __any_sync(0xffffffffu, jump)) {
-        // O_t holds P_t(j-1) v_{j-1}: s_full's commit for S_t(j) covered it
-#pragma unroll
-        for (int half = 0; half < 2; ++half) {
-          attn_ld64(t_o + half * 64, r);
-#pragma unroll
-          for (int i = 0; i < 64; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
-#pragma unroll
-          for (int cc = 0; cc < 4; ++cc)
-            ptx::tmem_st_32x32b_x16(t_o + half * 64 + cc * 16, *reinterpret_cast<const uint32_t(*)[16]>(r + cc * 16));
-        }
-      }
       l = l * alpha + psum;
       m = m_use;
-      ptx::tmem_st_wait();  // P (and a rescaled O) in TMEM before the MMA reads them
+      ptx::tmem_st_wait();
       ptx::tc_fence_before();
       __syncwarp();
       if (lane == 0) ptx::mbar_arrive(&p_full[t]);
@@ -744,19 +765,32 @@ __global__ void __launch_bounds__(kPThreads, 1)
   }
 }
 
-// v [B*Hkv][Skv][128] f16 -> v^T [B*Hkv][128][pitch] f16, zero for keys >= Skv;
-// 32 x 32 tiles through shared memory.
-__global__ void attn_vt_kernel(const uint16_t* __restrict__ v, int Skv, int pitch, uint16_t* __restrict__ vt) {
-  __shared__ uint16_t tile[32][33];
-  const int j0 = blockIdx.x * 32, d0 = blockIdx.y * 32, bk = blockIdx.z;
-  for (int i = threadIdx.y; i < 32; i += blockDim.y) {
-    const int j = j0 + i, d = d0 + threadIdx.x;
-    tile[i][threadIdx.x] = j < Skv ? v[((size_t)bk * Skv + j) * 128 + d] : (uint16_t)0;
+// v [B*Hkv][Skv][128] f16 -> v^T [B*Hkv][128][pitch] f16, zero for keys >= Skv
+// (pitch a multiple of 128; v 16-byte aligned, rows of 256 bytes).  One CTA
+// per 64 keys of one kv head: 16-byte loads of whole key rows into shared
+// memory, then each thread gathers 16 keys of one d column and writes them as
+// two adjacent 16-byte stores (a full 32-byte sector); the lanes of a warp
+// read 32 consecutive d of one key row, which fall in distinct banks.
+__global__ void __launch_bounds__(256) attn_vt_kernel(const uint16_t* __restrict__ v, int Skv, int pitch,
+                                                      uint16_t* __restrict__ vt) {
+  __shared__ __align__(16) uint16_t tile[64][136];  // [key][d], rows padded to 272 bytes
+  const int j0 = blockIdx.x * 64, bk = blockIdx.y;
+  for (int i = threadIdx.x; i < 64 * 16; i += 256) {
+    const int key = i >> 4, c = i & 15;
+    uint4 val = make_uint4(0, 0, 0, 0);
+    if (j0 + key < Skv) val = __ldg(reinterpret_cast<const uint4*>(v + ((size_t)bk * Skv + j0 + key) * 128) + c);
+    *reinterpret_cast<uint4*>(&tile[key][c * 8]) = val;
   }
   __syncthreads();
-  for (int i = threadIdx.y; i < 32; i += blockDim.y) {
-    const int d = d0 + i, j = j0 + threadIdx.x;
-    if (j < pitch) vt[((size_t)bk * 128 + d) * pitch + j] = tile[threadIdx.x][i];
+  for (int i = threadIdx.x; i < 128 * 4; i += 256) {
+    const int d = (i & 31) + 32 * ((i >> 5) & 3), p = i >> 7;  // keys 16 p .. 16 p + 15 of column d
+    uint32_t w[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u)
+      w[u] = (uint32_t)tile[16 * p + 2 * u][d] | ((uint32_t)tile[16 * p + 2 * u + 1][d] << 16);
+    uint4* dst = reinterpret_cast<uint4*>(vt + ((size_t)bk * 128 + d) * pitch + j0 + 16 * p);
+    dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
+    dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
   }
 }
 
@@ -792,7 +826,7 @@ bool attn_tmap(CUtensorMap* m, const void* base, uint64_t cols, uint64_t rows, u
 }  // namespace
 
 // The fused kernel addresses rows of q ([B*Hq*Sq][128]) and k ([B*Hkv*Skv][128])
-// by 32-bit TMA coordinates, and the v transpose puts B*Hkv on grid z.
+// by 32-bit TMA coordinates, and the v transpose puts B*Hkv on grid y.
 bq4_status attn_fused_check(int64_t B, int64_t Hq, int64_t Hkv, int64_t Sq, int64_t Skv) {
   constexpr int64_t kRowLimit = ((int64_t)1 << 31) - 256;
   if (B * Hq * Sq > kRowLimit || B * Hkv * Skv > kRowLimit || B * Hkv > 65535)
@@ -811,8 +845,7 @@ bq4_status attn_fused(const uint16_t* q, const uint16_t* k, const uint16_t* v, i
                       int64_t Sq, int64_t Skv, float scale, float* out, void* workspace, cudaStream_t s) {
   const int64_t pitch = (Skv + 127) / 128 * 128;
   uint16_t* vt = static_cast<uint16_t*>(workspace);
-  attn_vt_kernel<<<dim3((unsigned)(pitch / 32), 4, (unsigned)(B * Hkv)), dim3(32, 8), 0, s>>>(v, (int)Skv,
-                                                                                          (int)pitch, vt);
+  attn_vt_kernel<<<dim3((unsigned)(pitch / 64), (unsigned)(B * Hkv)), 256, 0, s>>>(v, (int)Skv, (int)pitch, vt);
   note_launch();
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return check_cuda(e, "attention v transpose launch");
