@@ -59,8 +59,8 @@ def parse():
     ap.add_argument("--tp-exchange", choices=["auto", "p2p", "nccl"], default="auto",
                     help="row-parallel exchange at N > 1: p2p (GEMM epilogue writes each row's partial to its "
                          "owner over NVLink peer memory, owner sums + renormalises, f16 all-gather) or nccl "
-                         "(f32 all-reduce of the partials); auto = p2p at 2 GPUs, where it was verified bit "
-                         "for bit against nccl and measured faster, nccl at more")
+                         "(f32 all-reduce of the partials); auto = p2p (checked against nccl and the unsharded "
+                         "stack on B200 at 2 and 4 ranks, and faster at both; the same code path serves 8)")
     ap.add_argument("--rows-only", action="store_true", help="print only the per-config rows (1 GPU)")
     ap.add_argument("--config", choices=["stack", "c4"], default="stack",
                     help="c4: BASELINE configs[3], the 1536 px edit projections (M=18432: fused qkv 3072->9216 "
@@ -716,7 +716,7 @@ def run_ours(args):
         _q.set_sm_budget(args.sm_budget)
     exchange = args.tp_exchange
     if exchange == "auto":
-        exchange = "p2p" if world == 2 else "nccl"
+        exchange = "p2p"
     if not (world > 1 and args.act_dtype == "f16" and chunks == 1):
         exchange = "nccl"
     stack = tp.DiTQ4Stack(args.blocks, HIDDEN, QKV, MLP, dev, seed=1, block=QBLOCK, group=group,

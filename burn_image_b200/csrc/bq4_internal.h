@@ -113,6 +113,7 @@ constexpr int64_t kSkAutoMaxM = 16;          // the planner's default: the few-t
 constexpr size_t kSkMaxSmem = 200 * 1024;    // dynamic shared memory limit of one CTA
 struct SkPlan {
   int nt, nw, R, ks, gx, gz, exact, pdl, stages;
+  int minb;  // CTAs the kernel is compiled to fit on one SM (2, or 3 for the one-weight few-token cases)
   size_t smem_bytes;
 };
 // false when the weight or numerics do not fit the kernel (pre-expanded or

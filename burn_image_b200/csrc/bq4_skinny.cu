@@ -49,6 +49,7 @@ namespace {
 
 constexpr int kSkThreads = 256;  // 8 warps, one 16-row group of the CTA's 128-row tile each
 constexpr size_t kSkCtaSmem = 110 * 1024;  // shared-memory budget: two CTAs fit on one SM
+constexpr size_t kSkCtaSmem3 = 73 * 1024;  // three CTAs on one SM
 
 struct SkArgs {
   const uint32_t* q[2];
@@ -205,8 +206,8 @@ __device__ __forceinline__ uint32_t xs_chunk(int c) { return (uint32_t)((c ^ (((
 // that token's row.
 // SPL: scales per lane row per stage -- 1 (exact numerics, or blocks of 32+:
 // a lane's 32 K lie in one block), 2 (blocks of 16), 4 (blocks of 8).
-template <int NT, int NW, bool EXACT, int SPL>
-__global__ void __launch_bounds__(kSkThreads, 2) q4_skinny_kernel(const SkArgs a) {
+template <int NT, int NW, bool EXACT, int SPL, int MINB = 2>
+__global__ void __launch_bounds__(kSkThreads, MINB) q4_skinny_kernel(const SkArgs a) {
   extern __shared__ __align__(128) unsigned char sk_smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, t = lane & 3;
@@ -252,9 +253,14 @@ __global__ void __launch_bounds__(kSkThreads, 2) q4_skinny_kernel(const SkArgs a
       }
     }
   };
-  for (int i = 0; i < D; ++i) {
+  // The first kSkEarly stages are requested before the activation loads and
+  // the rest after them, so that those loads do not queue behind the whole
+  // ring.  One commit group per slot (empty past the CTA's range), in stage
+  // order, so the main loop's wait counts stay as for one batch of D.
+  constexpr int kSkEarly = 2;
+  for (int i = 0; i < kSkEarly && i < D; ++i) {
     if (i < ns) issue(i);
-    cp_async_commit();  // one group per slot, empty past the CTA's range
+    cp_async_commit();
   }
 
   // ---- activations of the CTA's K range -> f16, swizzled shared memory
@@ -336,6 +342,10 @@ __global__ void __launch_bounds__(kSkThreads, 2) q4_skinny_kernel(const SkArgs a
         *reinterpret_cast<uint4*>(xs + (size_t)tok * a.xs_pitch + xs_chunk(c)) = h;
       }
     }
+  }
+  for (int i = kSkEarly; i < D; ++i) {
+    if (i < ns) issue(i);
+    cp_async_commit();
   }
   __syncthreads();
 
@@ -513,6 +523,7 @@ __global__ void __launch_bounds__(kSkThreads, 2) q4_skinny_kernel(const SkArgs a
     for (int e = e_first; e < elems; e += kSkThreads * a.ks) {
       const int tok = e / quads, rq = e - tok * quads;
       const int m = m0 + tok;
+      if (m >= a.M) continue;  // a padding token column: nothing to read or write
       float v[NW][4];
 #pragma unroll
       for (int i = 0; i < NW; ++i) {
@@ -525,7 +536,6 @@ __global__ void __launch_bounds__(kSkThreads, 2) q4_skinny_kernel(const SkArgs a
           v[i][0] += p.x; v[i][1] += p.y; v[i][2] += p.z; v[i][3] += p.w;
         }
       }
-      if (m >= a.M) continue;
       const int n = n0 + 4 * rq;
       float o[4];
 #pragma unroll
@@ -577,12 +587,12 @@ __global__ void __launch_bounds__(kSkThreads, 2) q4_skinny_kernel(const SkArgs a
   if (a.ks > 1) ptx::cluster_sync();  // keep this CTA's partials alive until every rank has read them
 }
 
-template <int NT, int NW, bool EXACT, int SPL>
+template <int NT, int NW, bool EXACT, int SPL, int MINB = 2>
 cudaError_t launch_sk(const SkPlan& p, const SkArgs& a, cudaStream_t stream) {
   static std::atomic<int> ready[64];
   int dev = 0;
   cudaGetDevice(&dev);
-  auto kern = q4_skinny_kernel<NT, NW, EXACT, SPL>;
+  auto kern = q4_skinny_kernel<NT, NW, EXACT, SPL, MINB>;
   if (dev >= 0 && dev < 64 && !ready[dev].load(std::memory_order_acquire)) {
     const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSkMaxSmem);
     if (e != cudaSuccess) return e;
@@ -667,8 +677,15 @@ bool plan_skinny(const bq4_weight* w, int nw, int64_t M, int device, bool exact,
   const int spl = exact || w->block >= 32 ? 1 : 128 / 4 / w->block;  // blocks of 16: 2, of 8: 4
   // each warp's ring: as many stages as fit next to the activations (at most
   // the CTA's stage count and 15), at least 2
+  // Three CTAs per SM (BQ4_SKINNY_MINB=3; one weight, up to 16 tokens): a
+  // smaller register and shared-memory budget, for grids of up to three CTAs
+  // per SM in one wave.
+  int minb = 2;
+  if (const char* f = getenv("BQ4_SKINNY_MINB"))
+    if (atoi(f) == 3 && nw == 1 && nt <= 2 && spl == 1) minb = 3;
+  const size_t budget = minb == 3 ? kSkCtaSmem3 : kSkCtaSmem;
   int stages = 2;
-  while (stages < kcta && stages < 15 && sk_layout(nt, nw, spl, kcta, stages + 1).total <= kSkCtaSmem) ++stages;
+  while (stages < kcta && stages < 15 && sk_layout(nt, nw, spl, kcta, stages + 1).total <= budget) ++stages;
   if (const char* f = getenv("BQ4_SKINNY_STAGES")) {
     const int v = atoi(f);
     if (v >= 2 && v < stages) stages = v;
@@ -685,6 +702,8 @@ bool plan_skinny(const bq4_weight* w, int nw, int64_t M, int device, bool exact,
   p->smem_bytes = L.total;
   p->exact = exact ? 1 : 0;
   p->pdl = getenv("BQ4_NO_PDL") ? 0 : 1;
+  p->minb = minb;
+  if (minb == 3 && L.total > kSkCtaSmem3) p->minb = 2;
   return true;
 }
 
@@ -738,6 +757,11 @@ bq4_status run_skinny(const SkPlan& p, const bq4_weight* const* ws, const void* 
   if (p.nt == NT_ && p.nw == NW_ && p.exact == EX_ && spl == SPL_) \
     e = launch_sk<NT_, NW_, EX_, SPL_>(p, a, stream);               \
   else
+#define BQ4_SK_CASE3(NT_, EX_)                                                       \
+  if (p.minb == 3 && p.nt == NT_ && p.nw == 1 && p.exact == EX_ && spl == 1) \
+    e = launch_sk<NT_, 1, EX_, 1, 3>(p, a, stream);                          \
+  else
+  BQ4_SK_CASE3(1, true) BQ4_SK_CASE3(2, true) BQ4_SK_CASE3(1, false) BQ4_SK_CASE3(2, false)
   BQ4_SK_CASE(1, 1, true, 1) BQ4_SK_CASE(2, 1, true, 1) BQ4_SK_CASE(4, 1, true, 1)
   BQ4_SK_CASE(1, 1, false, 1) BQ4_SK_CASE(2, 1, false, 1) BQ4_SK_CASE(4, 1, false, 1) BQ4_SK_CASE(8, 1, false, 1)
   BQ4_SK_CASE(1, 1, false, 2) BQ4_SK_CASE(2, 1, false, 2) BQ4_SK_CASE(4, 1, false, 2) BQ4_SK_CASE(8, 1, false, 2)
@@ -747,6 +771,7 @@ bq4_status run_skinny(const SkPlan& p, const bq4_weight* const* ws, const void* 
   BQ4_SK_CASE(1, 2, false, 4) BQ4_SK_CASE(2, 2, false, 4)
   return set_error(BQ4_EUNSUPPORTED, "no small-M kernel for %d token columns x %d weights", 8 * p.nt, p.nw);
 #undef BQ4_SK_CASE
+#undef BQ4_SK_CASE3
   if (e != cudaSuccess) return check_cuda(e, "small-M q4 linear launch");
   return BQ4_OK;
 }

@@ -112,6 +112,33 @@ def test_skinny_linear_parity(M, K, N, block, layout, act, with_bias, with_aux, 
     assert rel(y, ref_s) <= tight
 
 
+@pytest.mark.parametrize("M,exact,KS", [(1, 1, 4), (5, 0, 4), (12, 1, 3), (16, 0, 2), (9, 1, 1)])
+def test_skinny_three_ctas_per_sm(M, exact, KS, rng):
+    """The variant compiled for three CTAs per SM (BQ4_SKINNY_MINB=3: one
+    weight, up to 16 tokens, a smaller register and shared-memory budget)
+    gives the oracle's result, deterministically, at every K split."""
+    K, N, block = 2560, 640, 128
+    w, s = gen_q4(K, N, block, O.LAYOUT_ROW, rng)
+    x = gen_x(M, K, rng)
+    bias = gen_bias(N, rng)
+    ref = O.linear_f64(x, O.unpack(w, s, K, N, block, O.LAYOUT_ROW), bias)
+    pw = q4.PreparedQ4Weight(dev(w), dev(s), K, N, block, O.LAYOUT_ROW, DEV)
+    xd, bd = dev(x), dev(bias)
+    q4.set_numerics(L.NUMERICS_EXACT if exact else L.NUMERICS_FOLDED)
+    try:
+        with env(BQ4_SKINNY_MINB=3, BQ4_SKINNY_KS=KS):
+            info = pw.plan_info(M)
+            assert info["skinny"] == 1 and info["ksplit"] == KS and info["exact"] == exact, info
+            a = pw.linear(xd, bd).clone()
+            b = pw.linear(xd, bd).clone()
+    finally:
+        q4.set_numerics(L.NUMERICS_AUTO)
+    torch.cuda.synchronize()
+    q4.poll_device_error()
+    assert torch.equal(a, b)
+    assert rel(a.cpu().numpy(), ref) <= TOL
+
+
 @pytest.mark.parametrize("KS,STAGES", [(1, 0), (2, 2), (4, 3), (8, 0), (3, 2), (1, 2)])
 def test_skinny_ring_depths_and_cluster_splits(KS, STAGES, rng):
     """Every cluster K split and weight-ring depth gives the same result

@@ -1,10 +1,15 @@
-"""GPU, 2 devices: the tensor-parallel DiT stack with the row-parallel exchange
-over NVLink peer memory (GEMM epilogue scatters each output row's partial to
-its owner, the owner sums and renormalises its rows, f16 all-gather) against
-the same stack with an NCCL float32 all-reduce, and against the unsharded
-stack.  With two ranks both exchanges add the same two partials, so the
-outputs must be bit-identical; repeated calls (advancing barrier epochs)
-must give the same bits.  Skipped on hosts with fewer than 2 GPUs.
+"""GPU, 2 / 4 / 8 devices: the tensor-parallel DiT stack with the row-parallel
+exchange over NVLink peer memory (GEMM epilogue scatters each output row's
+partial to its owner, the owner sums and renormalises its rows, f16
+all-gather) against the same stack with an NCCL float32 all-reduce, and
+against the unsharded stack.  With two ranks both exchanges add the same two
+partials, so the outputs must be bit-identical; with more, the all-reduce
+adds them in its own order and each f32 sum is then rounded to f16 for the
+next linear, so a last-bit difference can flip an f16 rounding and travel
+through the later layers: the two agree within 2e-3 there, and both stay
+within 5e-3 of the unsharded stack; repeated calls (advancing barrier
+epochs) must give the same bits.  Each rank count runs
+when the host has that many GPUs.
 """
 import os
 import socket
@@ -14,7 +19,6 @@ import pytest
 import torch
 
 pytestmark = pytest.mark.gpu
-WORLD = 2
 
 
 def _free_port():
@@ -33,7 +37,7 @@ def _worker(rank, world, port, results):
     torch.cuda.set_device(dev)
     dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60), device_id=dev)
     try:
-        M, H, QKV, MLP = 300, 512, 1536, 2048
+        M, H, QKV, MLP = 304, 512, 1536, 2048  # M divisible by 2, 4, 8
         g = torch.Generator(device=dev).manual_seed(7)
         x = torch.randn((M, H), generator=g, device=dev)
         p2p = tp.DiTQ4Stack(2, H, QKV, MLP, dev, seed=3, act_dtype=torch.float16, exchange="p2p")
@@ -46,16 +50,19 @@ def _worker(rank, world, port, results):
         torch.cuda.synchronize(dev)
         q4.poll_device_error()
         rel = (torch.linalg.norm(a.double() - c.double()) / torch.linalg.norm(c.double())).item()
-        results[rank] = (bool(torch.equal(a, b)), bool(torch.equal(a, a2)), rel, None)
+        d_ar = (torch.linalg.norm(a.double() - b.double()) / torch.linalg.norm(b.double())).item()
+        same = bool(torch.equal(a, b)) if world == 2 else d_ar <= 2e-3
+        results[rank] = (same, bool(torch.equal(a, a2)), rel, d_ar, None)
         p2p.close()
     except Exception as e:  # reported to the parent
-        results[rank] = (False, False, float("nan"), repr(e))
+        results[rank] = (False, False, float("nan"), float("nan"), repr(e))
     finally:
         dist.barrier()
         dist.destroy_process_group()
 
 
-def test_p2p_exchange_matches_allreduce():
+@pytest.mark.parametrize("WORLD", [2, 4, 8])
+def test_p2p_exchange_matches_allreduce(WORLD):
     if torch.cuda.device_count() < WORLD:
         pytest.skip(f"needs {WORLD} GPUs")
     import torch.multiprocessing as mp
@@ -74,8 +81,9 @@ def test_p2p_exchange_matches_allreduce():
     assert not alive, "a rank did not finish"
     assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
     for r in range(WORLD):
-        same, repeat, rel, err = results[r]
+        same, repeat, rel, d_ar, err = results[r]
+        print(f"world {WORLD} rank {r}: p2p vs all-reduce {d_ar:.3e}, p2p vs unsharded {rel:.3e}")
         assert err is None, f"rank {r}: {err}"
-        assert same, f"rank {r}: p2p exchange differs from the all-reduce"
+        assert same, f"rank {r}: p2p exchange differs from the all-reduce ({d_ar:.3e})"
         assert repeat, f"rank {r}: repeated calls differ"
         assert rel <= 5e-3, f"rank {r}: rel to unsharded {rel}"
