@@ -781,9 +781,10 @@ __global__ void __launch_bounds__(kPThreads, 1)
 // v [B*Hkv][Skv][128] f16 -> v^T [B*Hkv][128][pitch] f16, zero for keys >= Skv
 // (pitch a multiple of 128; v 16-byte aligned, rows of 256 bytes).  One CTA
 // per 64 keys of one kv head: 16-byte loads of whole key rows into shared
-// memory, then each thread gathers 16 keys of one d column and writes them as
-// two adjacent 16-byte stores (a full 32-byte sector); the lanes of a warp
-// read 32 consecutive d of one key row, which fall in distinct banks.
+// memory; then thread i takes the column pair d = 2 (i % 64), d + 1 and keys
+// 16 (i / 64) .. + 15: it reads each key's (d, d + 1) pair as one 32-bit word
+// (the lanes of a warp read 128 consecutive bytes of a key row), splits the
+// pairs with byte permutes, and writes 32 bytes to each of the two v^T rows.
 __global__ void __launch_bounds__(256) attn_vt_kernel(const uint16_t* __restrict__ v, int Skv, int pitch,
                                                       uint16_t* __restrict__ vt) {
   __shared__ __align__(16) uint16_t tile[64][136];  // [key][d], rows padded to 272 bytes
@@ -795,16 +796,21 @@ __global__ void __launch_bounds__(256) attn_vt_kernel(const uint16_t* __restrict
     *reinterpret_cast<uint4*>(&tile[key][c * 8]) = val;
   }
   __syncthreads();
-  for (int i = threadIdx.x; i < 128 * 4; i += 256) {
-    const int d = (i & 31) + 32 * ((i >> 5) & 3), p = i >> 7;  // keys 16 p .. 16 p + 15 of column d
-    uint32_t w[8];
+  const int d = 2 * (threadIdx.x & 63), k0 = 16 * (threadIdx.x >> 6);
+  uint32_t lo[8], hi[8];  // keys k0 + 2 u, + 1 of column d (lo) and d + 1 (hi)
 #pragma unroll
-    for (int u = 0; u < 8; ++u)
-      w[u] = (uint32_t)tile[16 * p + 2 * u][d] | ((uint32_t)tile[16 * p + 2 * u + 1][d] << 16);
-    uint4* dst = reinterpret_cast<uint4*>(vt + ((size_t)bk * 128 + d) * pitch + j0 + 16 * p);
-    dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
-    dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
+  for (int u = 0; u < 8; ++u) {
+    const uint32_t a = *reinterpret_cast<const uint32_t*>(&tile[k0 + 2 * u][d]);
+    const uint32_t b = *reinterpret_cast<const uint32_t*>(&tile[k0 + 2 * u + 1][d]);
+    lo[u] = __byte_perm(a, b, 0x5410);
+    hi[u] = __byte_perm(a, b, 0x7632);
   }
+  uint4* d0 = reinterpret_cast<uint4*>(vt + ((size_t)bk * 128 + d) * pitch + j0 + k0);
+  uint4* d1 = reinterpret_cast<uint4*>(vt + ((size_t)bk * 128 + d + 1) * pitch + j0 + k0);
+  d0[0] = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+  d0[1] = make_uint4(lo[4], lo[5], lo[6], lo[7]);
+  d1[0] = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+  d1[1] = make_uint4(hi[4], hi[5], hi[6], hi[7]);
 }
 
 typedef CUresult (*EncodeFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,

@@ -1073,7 +1073,30 @@ __global__ void __launch_bounds__(kWsThreads, 1)
             continue;
           }
         }
-        if (n < a.N) {
+        if (SC && n < a.N) {
+          // row scatter: token m's partial goes to row (sc_rank sc_rows + m - owner sc_rows)
+          // of its owner's receive buffer; the owner and the row address advance with m
+          // (this thread's tokens are consecutive) instead of a division per element
+          const float b0 = a.bias[0] ? __ldg(a.bias[0] + n) : 0.0f;
+          const int act = a.act;
+          int owner = m0 / a.sc_rows;
+          int next = (owner + 1) * a.sc_rows;
+          float* dst = a.sc_y[owner] + (size_t)(a.sc_rank * a.sc_rows + (m0 - owner * a.sc_rows)) * a.ldy + n;
+  #pragma unroll
+          for (int j = 0; j < kCols; ++j) {
+            const int m = m0 + j;
+            if (m >= a.M) break;
+            if (m == next) {
+              ++owner;
+              next += a.sc_rows;
+              dst = a.sc_y[owner] + (size_t)a.sc_rank * a.sc_rows * a.ldy + n;
+            }
+            float v = apply_act(acc[0][j] + b0, act);
+            if (a.aux) v *= __ldg(a.aux + (size_t)m * a.N + n);
+            *dst = v;
+            dst += a.ldy;
+          }
+        } else if (n < a.N) {
           const float b0 = a.bias[0] ? __ldg(a.bias[0] + n) : 0.0f;
           const float b1 = (NW == 2 && a.bias[1]) ? __ldg(a.bias[1] + n) : 0.0f;
           const int act = a.act;

@@ -253,14 +253,12 @@ __global__ void __launch_bounds__(kSkThreads, MINB) q4_skinny_kernel(const SkArg
       }
     }
   };
-  // The first kSkEarly stages are requested before the activation loads and
-  // the rest after them, so that those loads do not queue behind the whole
-  // ring.  One commit group per slot (empty past the CTA's range), in stage
-  // order, so the main loop's wait counts stay as for one batch of D.
-  constexpr int kSkEarly = 2;
-  for (int i = 0; i < kSkEarly && i < D; ++i) {
+  // (Requesting only the first two stages before the activation loads, so
+  // that those loads do not queue behind the whole ring, measured slower:
+  // 13.1 against 10.9 us at 1 x 2560 -> 9728.)
+  for (int i = 0; i < D; ++i) {
     if (i < ns) issue(i);
-    cp_async_commit();
+    cp_async_commit();  // one group per slot, empty past the CTA's range
   }
 
   // ---- activations of the CTA's K range -> f16, swizzled shared memory
@@ -342,10 +340,6 @@ __global__ void __launch_bounds__(kSkThreads, MINB) q4_skinny_kernel(const SkArg
         *reinterpret_cast<uint4*>(xs + (size_t)tok * a.xs_pitch + xs_chunk(c)) = h;
       }
     }
-  }
-  for (int i = kSkEarly; i < D; ++i) {
-    if (i < ns) issue(i);
-    cp_async_commit();
   }
   __syncthreads();
 
@@ -664,33 +658,55 @@ bool plan_skinny(const bq4_weight* w, int nw, int64_t M, int device, bool exact,
   const int mgroups = (int)((M + 8 * nt - 1) / (8 * nt));
   const int nks = (int)(w->Kp / 128);
   const int gx = (int)w->ntiles;
-  // K splits across a cluster (<= 8): doubled while the grid is short of one
-  // CTA per SM and every CTA keeps at least two 128-K stages
-  int ks = 1;
-  while (ks < 8 && (int64_t)gx * mgroups * ks < sms && nks >= 4 * ks) ks *= 2;
-  if (const char* f = getenv("BQ4_SKINNY_KS")) {
-    const int v = atoi(f);
-    if (v >= 1 && v <= 8) ks = v;
-  }
-  if (ks > nks) ks = nks;
-  const int kcta = (nks + ks - 1) / ks;
   const int spl = exact || w->block >= 32 ? 1 : 128 / 4 / w->block;  // blocks of 16: 2, of 8: 4
-  // each warp's ring: as many stages as fit next to the activations (at most
-  // the CTA's stage count and 15), at least 2
-  // Three CTAs per SM (BQ4_SKINNY_MINB=3; one weight, up to 16 tokens): a
-  // smaller register and shared-memory budget, for grids of up to three CTAs
-  // per SM in one wave.
-  int minb = 2;
-  if (const char* f = getenv("BQ4_SKINNY_MINB"))
-    if (atoi(f) == 3 && nw == 1 && nt <= 2 && spl == 1) minb = 3;
-  const size_t budget = minb == 3 ? kSkCtaSmem3 : kSkCtaSmem;
-  int stages = 2;
-  while (stages < kcta && stages < 15 && sk_layout(nt, nw, spl, kcta, stages + 1).total <= budget) ++stages;
-  if (const char* f = getenv("BQ4_SKINNY_STAGES")) {
+  // K splits across a cluster (<= 8): as many as one wave of minb CTAs per
+  // SM holds, each CTA keeping at least two 128-K stages.  The build for
+  // three CTAs per SM (one weight, up to 16 tokens: 80 registers, a smaller
+  // shared-memory budget) is taken when it allows more splits than two CTAs
+  // per SM do.  Measured on B200 (graph-replayed): 76 weight tiles,
+  // 1 x 2560 -> 9728: 2 splits 10.9 us, 3 splits 10.8, 5 splits at three
+  // CTAs per SM 9.6; 16 x 2560 -> 9728: 15.9 / 14.3 / 13.4; 16 x 2560 ->
+  // 2 x 9728 gated: 24.6 / 20.0 (two weights: two CTAs per SM); 20 tiles
+  // (16 x 9728 -> 2560) keep 8 splits at two CTAs per SM (17.6 us; 21.0 at
+  // three).  BQ4_SKINNY_MINB=2|3 pins the choice.
+  auto splits = [&](int per_sm) {
+    int k = (int)((int64_t)per_sm * sms / ((int64_t)gx * mgroups));
+    if (k > 8) k = 8;
+    if (k > nks / 2) k = nks / 2;
+    return k < 1 ? 1 : k;
+  };
+  const bool can3 = nw == 1 && nt <= 2 && spl == 1;
+  int minb = can3 && splits(3) > splits(2) ? 3 : 2;
+  if (const char* f = getenv("BQ4_SKINNY_MINB")) {
     const int v = atoi(f);
-    if (v >= 2 && v < stages) stages = v;
+    if (v == 2 || (v == 3 && can3)) minb = v;
   }
-  const SkLayout L = sk_layout(nt, nw, spl, kcta, stages);
+  int ks = 1, kcta = 1, stages = 2;
+  SkLayout L;
+  for (;;) {
+    ks = splits(minb);
+    if (const char* f = getenv("BQ4_SKINNY_KS")) {
+      const int v = atoi(f);
+      if (v >= 1 && v <= 8) ks = v;
+    }
+    if (ks > nks) ks = nks;
+    kcta = (nks + ks - 1) / ks;
+    // each warp's ring: as many stages as fit next to the activations (at
+    // most the CTA's stage count and 15), at least 2
+    const size_t budget = minb == 3 ? kSkCtaSmem3 : kSkCtaSmem;
+    stages = 2;
+    while (stages < kcta && stages < 15 && sk_layout(nt, nw, spl, kcta, stages + 1).total <= budget) ++stages;
+    if (const char* f = getenv("BQ4_SKINNY_STAGES")) {
+      const int v = atoi(f);
+      if (v >= 2 && v < stages) stages = v;
+    }
+    L = sk_layout(nt, nw, spl, kcta, stages);
+    if (minb == 3 && L.total > kSkCtaSmem3) {  // three CTAs do not fit one SM's shared memory
+      minb = 2;
+      continue;
+    }
+    break;
+  }
   if (L.total > kSkMaxSmem) return false;
   p->nt = nt;
   p->nw = nw;
@@ -703,7 +719,6 @@ bool plan_skinny(const bq4_weight* w, int nw, int64_t M, int device, bool exact,
   p->exact = exact ? 1 : 0;
   p->pdl = getenv("BQ4_NO_PDL") ? 0 : 1;
   p->minb = minb;
-  if (minb == 3 && L.total > kSkCtaSmem3) p->minb = 2;
   return true;
 }
 

@@ -1,0 +1,65 @@
+"""GPU, one device: the row-scatter GEMM (bq4_linear_rowscatter), the
+row-parallel layer's epilogue that writes each output row's partial product
+into the receive buffer of the rank that owns the row.
+
+The receive buffers of all "ranks" are plain buffers on this one device, so
+the kernel's addressing is checked without peer memory: owner r of rows
+[r R, (r+1) R) (R = M / nranks) must hold, at rows [rank R, (rank+1) R) of its
+buffer, exactly the rows the plain linear (bq4_linear_ex, f32 output) computes
+for them, and no other row of any buffer may change.  Row-slice sizes that are
+not multiples of the token tile put owner boundaries inside tiles.
+"""
+import ctypes
+
+import numpy as np
+import pytest
+import torch
+
+import oracle as O
+from burn_image_b200 import _lib as L
+from burn_image_b200 import q4
+from conftest import gen_bias, gen_q4
+
+pytestmark = pytest.mark.gpu
+DEV = torch.device("cuda", 0)
+
+
+def dev(a):
+    a = np.ascontiguousarray(a)
+    if a.dtype == np.uint32:
+        a = a.view(np.int32)
+    return torch.from_numpy(a).to(DEV)
+
+
+@pytest.mark.parametrize("M,K,N,nranks,rank,x_f16", [(520, 1024, 768, 4, 2, True), (600, 768, 384, 8, 5, True),
+                                                     (264, 512, 640, 2, 0, False), (4352, 3072, 3072, 4, 3, True)])
+def test_rowscatter_rows_land_at_their_owner(M, K, N, nranks, rank, x_f16, rng):
+    w, s = gen_q4(K, N, 128, O.LAYOUT_ROW, rng)
+    bias = dev(gen_bias(N, rng))
+    pw = q4.PreparedQ4Weight(dev(w), dev(s), K, N, 128, O.LAYOUT_ROW, DEV)
+    x = torch.randn((M, K), generator=torch.Generator(device=DEV).manual_seed(M + K), device=DEV)
+    if x_f16:
+        x = x.half()
+    ref = pw.linear_ex(x, bias)  # f32 [M, N]
+    R = M // nranks
+    sentinel = float("nan")
+    bufs = [torch.full((M, N), sentinel, device=DEV) for _ in range(nranks)]
+    targets = (ctypes.c_void_p * L.MAX_PEERS)(*[b.data_ptr() for b in bufs], *([None] * (L.MAX_PEERS - nranks)))
+    dt = L.DTYPE_F16 if x_f16 else L.DTYPE_F32
+    n = ctypes.c_size_t()
+    L.check(L.lib().bq4_linear_ex_workspace_size(pw.handle, M, dt, ctypes.byref(n)))
+    ws = torch.empty(max(n.value, 256), dtype=torch.uint8, device=DEV)
+    stream = ctypes.c_void_p(torch.cuda.current_stream(DEV).cuda_stream)
+    for _ in range(2):  # a repeated call writes the same bits
+        L.check(L.lib().bq4_linear_rowscatter(pw.handle, ctypes.c_void_p(x.data_ptr()), dt, M, x.stride(0),
+                                              ctypes.c_void_p(bias.data_ptr()), L.ACT_NONE, targets, nranks, rank, N,
+                                              ctypes.c_void_p(ws.data_ptr()), ws.numel(), stream))
+        torch.cuda.synchronize()
+        q4.poll_device_error()
+        for r in range(nranks):
+            got = bufs[r][rank * R:(rank + 1) * R]
+            want = ref[r * R:(r + 1) * R]
+            rel = (torch.linalg.norm(got.double() - want.double()) / torch.linalg.norm(want.double())).item()
+            assert rel <= 1e-6, f"owner {r}: rel {rel}"
+            others = torch.cat([bufs[r][:rank * R], bufs[r][(rank + 1) * R:]])
+            assert bool(torch.isnan(others).all()), f"owner {r}: rows outside this rank's slot were written"
