@@ -789,11 +789,17 @@ __global__ void __launch_bounds__(256) attn_vt_kernel(const uint16_t* __restrict
                                                       uint16_t* __restrict__ vt) {
   __shared__ __align__(16) uint16_t tile[64][136];  // [key][d], rows padded to 272 bytes
   const int j0 = blockIdx.x * 64, bk = blockIdx.y;
-  for (int i = threadIdx.x; i < 64 * 16; i += 256) {
-    const int key = i >> 4, c = i & 15;
-    uint4 val = make_uint4(0, 0, 0, 0);
-    if (j0 + key < Skv) val = __ldg(reinterpret_cast<const uint4*>(v + ((size_t)bk * Skv + j0 + key) * 128) + c);
-    *reinterpret_cast<uint4*>(&tile[key][c * 8]) = val;
+  uint4 val[4];  // all four loads in flight before the first store
+#pragma unroll
+  for (int r = 0; r < 4; ++r) {
+    const int i = (int)threadIdx.x + 256 * r, key = i >> 4, c = i & 15;
+    val[r] = make_uint4(0, 0, 0, 0);
+    if (j0 + key < Skv) val[r] = __ldg(reinterpret_cast<const uint4*>(v + ((size_t)bk * Skv + j0 + key) * 128) + c);
+  }
+#pragma unroll
+  for (int r = 0; r < 4; ++r) {
+    const int i = (int)threadIdx.x + 256 * r;
+    *reinterpret_cast<uint4*>(&tile[i >> 4][(i & 15) * 8]) = val[r];
   }
   __syncthreads();
   const int d = 2 * (threadIdx.x & 63), k0 = 16 * (threadIdx.x >> 6);
