@@ -37,7 +37,7 @@ def _worker(rank, world, port, results):
     torch.cuda.set_device(dev)
     dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60), device_id=dev)
     try:
-        M, H, QKV, MLP = 304, 512, 1536, 2048  # M divisible by 2, 4, 8
+        M, H, QKV, MLP = 304, 1024, 3072, 2048  # M and the row shards (H/P, MLP/P) divide by 2, 4, 8 on block-128 boundaries
         g = torch.Generator(device=dev).manual_seed(7)
         x = torch.randn((M, H), generator=g, device=dev)
         p2p = tp.DiTQ4Stack(2, H, QKV, MLP, dev, seed=3, act_dtype=torch.float16, exchange="p2p")
