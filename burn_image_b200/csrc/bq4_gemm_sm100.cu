@@ -1369,7 +1369,8 @@ static bq4_status plan_for_bt(const bq4_weight* w, int nw, int64_t M, int device
   // Exact numerics need two TMEM partials, which leave room for A slots only
   // at 128-token tiles (BQ4_EXACT_TA=1 enables that combination).
   p->ta = (!p->pre && nw == 1 && !getenv("BQ4_NO_TA") &&
-           ((!p->exact && p->bt == 256) || (p->exact && p->bt == 128 && getenv("BQ4_EXACT_TA"))))
+           ((!p->exact && p->bt == 256) || (p->exact && p->bt == 128 && getenv("BQ4_EXACT_TA")) ||
+            (p->exact && p->bt == 256 && getenv("BQ4_EXACT_TA256"))))
               ? 1 : 0;
   // operand rows: 128 bytes, or 64 for the tf32 linear (whose stages are then
   // small enough for up to 8 in flight)

@@ -92,3 +92,35 @@ def test_unit_order_does_not_change_results(M, K, N, monkeypatch):
         torch.cuda.synchronize()
         q4.poll_device_error()
     assert torch.equal(outs[0], outs[1])
+
+
+@pytest.mark.parametrize("M,K,N,S", [(1024, 3072, 1024, 1), (4352, 3072, 3072, 1), (256, 2560, 2560, 5), (600, 1536, 768, 2)])
+def test_exact_with_a_in_tmem_at_256_tokens(M, K, N, S, monkeypatch):
+    """Exact numerics with the dequantized weight tile in TMEM and 256-token
+    tiles (BQ4_EXACT_TA256=1: one TMEM partial, drained by the scaler before
+    the next K block's MMAs): the same products and summation order as the
+    plan with A in shared memory, so the results agree to the last bits."""
+    block = 128
+    words, scales, x = problem(M, K, N, block)
+    pw = q4.PreparedQ4Weight(words, scales, K, N, block, L.LAYOUT_ROW, DEV)
+    ref = x.half().double() @ pw.dequantize().double()
+    monkeypatch.setenv("BQ4_FORCE_KSPLIT", str(S))
+    monkeypatch.setenv("BQ4_FORCE_BT", "256")
+    monkeypatch.setenv("BQ4_NO_STREAMK", "1")
+    q4.set_numerics(L.NUMERICS_EXACT)
+    try:
+        smem = pw.linear(x).clone()
+        monkeypatch.setenv("BQ4_EXACT_TA256", "1")
+        info = pw.plan_info(M)
+        assert info["exact"] == 1 and info["ta"] == 1 and info["bt"] == 256, info
+        a = pw.linear(x).clone()
+        b = pw.linear(x).clone()
+    finally:
+        q4.set_numerics(L.NUMERICS_AUTO)
+    torch.cuda.synchronize()
+    q4.poll_device_error()
+    assert torch.equal(a, b)
+    rf = (torch.linalg.norm(a.double() - ref) / torch.linalg.norm(ref)).item()
+    assert rf < 5e-5, f"rel_frob {rf}"
+    rs = (torch.linalg.norm(a.double() - smem.double()) / torch.linalg.norm(smem.double())).item()
+    assert rs < 1e-6, f"rel to the shared-memory plan {rs}"
