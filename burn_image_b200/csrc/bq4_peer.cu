@@ -5,9 +5,12 @@
 // epilogue straight into the buffer of the rank that owns each output row
 // (bq4_linear_rowscatter); ranks then pass a cross-GPU signal/wait
 // (bq4_peer_signal_wait) and each owner sums the partials of its rows in
-// rank order, optionally RMS-renormalising them (bq4_reduce_slices).  The
-// shared buffers are plain cudaMalloc allocations exported with CUDA IPC
-// handles (bq4_peer_buffer_*): plain peer loads and stores between GPUs.
+// rank order, optionally RMS-renormalising them (bq4_reduce_slices).  In the
+// pull form each rank's GEMM writes its whole partial product into its own
+// shared buffer, and after the signal/wait each owner reads its rows from
+// every rank's buffer (bq4_reduce_slices_peer).  The shared buffers are
+// plain cudaMalloc allocations exported with CUDA IPC handles
+// (bq4_peer_buffer_*): plain peer loads and stores between GPUs.
 //
 // Every wait is bounded: a signal/wait that times out records BQ4_ETIMEOUT
 // in the device error word and returns.
@@ -64,13 +67,23 @@ __global__ void peer_signal_wait_kernel(unsigned* local, PeerFlags peers, int nr
   }
 }
 
-// out[r] = sum over s = 0..P-1 (in that order) of recv[s][r], for the R
-// rows this rank owns (recv: [P][R] rows of H floats at pitch ld), then
-// optionally the per-row RMS renorm with the thread mapping and arithmetic
-// of rms_renorm_vec4_kernel (so the result matches an all-reduce followed
-// by that kernel bit for bit when the summation orders agree).  H % 4 == 0.
+// The P partial slices of a reduction: slice s, row r is src.p[s] + (row0 + r) * ld.
+struct SliceSrc {
+  const float* p[BQ4_MAX_PEERS];
+};
+
+// out[r] = sum over s = 0..P-1 (in that order) of slice s, row r, for the R
+// rows this rank owns (rows of H floats at pitch ld), then optionally the
+// per-row RMS renorm with the thread mapping and arithmetic of
+// rms_renorm_vec4_kernel (so the result matches an all-reduce followed by
+// that kernel bit for bit when the summation orders agree).  H % 4 == 0.
+// The slices are one local receive buffer (the push exchange: [P][R] rows)
+// or the ranks' own partial buffers read over peer memory (the pull
+// exchange: rank s's full [M] rows, this rank's R starting at row0); a
+// thread issues the loads of all P slices of its columns before adding, so
+// P remote reads are in flight together.
 template <typename TO, bool kRenorm>
-__global__ void reduce_slices_kernel(const float* __restrict__ recv, int P, int64_t R, int64_t H, int64_t ld,
+__global__ void reduce_slices_kernel(const SliceSrc src, int P, int64_t row0, int64_t R, int64_t H, int64_t ld,
                                      float eps, TO* __restrict__ out, int64_t ldo) {
   constexpr int kMaxVec = 8;  // H <= 8 * 4 * blockDim.x
   __shared__ float part[32];
@@ -83,7 +96,7 @@ __global__ void reduce_slices_kernel(const float* __restrict__ recv, int P, int6
       v[i] = make_float4(0.f, 0.f, 0.f, 0.f);
       if (h < H) {
         for (int s = 0; s < P; ++s) {
-          const float4 t = *reinterpret_cast<const float4*>(recv + ((int64_t)s * R + r) * ld + h);
+          const float4 t = *reinterpret_cast<const float4*>(src.p[s] + (row0 + r) * ld + h);
           v[i].x += t.x; v[i].y += t.y; v[i].z += t.z; v[i].w += t.w;
         }
         ss = fmaf(v[i].x, v[i].x, ss); ss = fmaf(v[i].y, v[i].y, ss);
@@ -129,22 +142,41 @@ cudaError_t launch_peer_signal_wait(unsigned* local, unsigned* const* peers, int
   return cudaGetLastError();
 }
 
-cudaError_t launch_reduce_slices(const float* recv, int P, int64_t R, int64_t H, int64_t ld, int renorm, float eps,
-                                 void* out, int out_f16, int64_t ldo, cudaStream_t s) {
+namespace {
+cudaError_t launch_reduce(const SliceSrc& src, int P, int64_t row0, int64_t R, int64_t H, int64_t ld, int renorm,
+                          float eps, void* out, int out_f16, int64_t ldo, cudaStream_t s) {
   const int grid = R < 148 * 8 ? (int)R : 148 * 8;
   if (out_f16) {
     if (renorm)
-      reduce_slices_kernel<__half, true><<<grid, 256, 0, s>>>(recv, P, R, H, ld, eps, static_cast<__half*>(out), ldo);
+      reduce_slices_kernel<__half, true><<<grid, 256, 0, s>>>(src, P, row0, R, H, ld, eps, static_cast<__half*>(out), ldo);
     else
-      reduce_slices_kernel<__half, false><<<grid, 256, 0, s>>>(recv, P, R, H, ld, eps, static_cast<__half*>(out), ldo);
+      reduce_slices_kernel<__half, false><<<grid, 256, 0, s>>>(src, P, row0, R, H, ld, eps, static_cast<__half*>(out), ldo);
   } else {
     if (renorm)
-      reduce_slices_kernel<float, true><<<grid, 256, 0, s>>>(recv, P, R, H, ld, eps, static_cast<float*>(out), ldo);
+      reduce_slices_kernel<float, true><<<grid, 256, 0, s>>>(src, P, row0, R, H, ld, eps, static_cast<float*>(out), ldo);
     else
-      reduce_slices_kernel<float, false><<<grid, 256, 0, s>>>(recv, P, R, H, ld, eps, static_cast<float*>(out), ldo);
+      reduce_slices_kernel<float, false><<<grid, 256, 0, s>>>(src, P, row0, R, H, ld, eps, static_cast<float*>(out), ldo);
   }
   note_launch();
   return cudaGetLastError();
+}
+}  // namespace
+
+cudaError_t launch_reduce_slices(const float* recv, int P, int64_t R, int64_t H, int64_t ld, int renorm, float eps,
+                                 void* out, int out_f16, int64_t ldo, cudaStream_t s) {
+  SliceSrc src;
+  memset(&src, 0, sizeof(src));
+  for (int r = 0; r < P && r < BQ4_MAX_PEERS; ++r) src.p[r] = recv + (int64_t)r * R * ld;
+  return launch_reduce(src, P, 0, R, H, ld, renorm, eps, out, out_f16, ldo, s);
+}
+
+cudaError_t launch_reduce_slices_peer(const float* const* src_ranks, int P, int64_t row0, int64_t R, int64_t H,
+                                      int64_t ld, int renorm, float eps, void* out, int out_f16, int64_t ldo,
+                                      cudaStream_t s) {
+  SliceSrc src;
+  memset(&src, 0, sizeof(src));
+  for (int r = 0; r < P && r < BQ4_MAX_PEERS; ++r) src.p[r] = src_ranks[r];
+  return launch_reduce(src, P, row0, R, H, ld, renorm, eps, out, out_f16, ldo, s);
 }
 
 }  // namespace bq4

@@ -130,6 +130,22 @@ class RowParallelQ4Linear:
                                               _ptr(ws), ws.numel() if ws is not None else 0, _stream_ptr(w.device)))
         ex.signal_wait()
 
+    def forward_local(self, x_local: torch.Tensor, ex: "PeerExchange", b: int) -> None:
+        """The pull form: this rank's whole partial product [M, H] f32 goes
+        into its own shared buffer b (a plain bq4_linear_ex, local HBM
+        stores), then the cross-rank signal/wait; afterwards every owner can
+        read its rows from every rank's buffer (PeerExchange.reduce_pull)."""
+        w = self.weight
+        M = x_local.shape[0]
+        dt = {torch.float32: L.DTYPE_F32, torch.float16: L.DTYPE_F16}
+        n = ctypes.c_size_t()
+        L.check(L.lib().bq4_linear_ex_workspace_size(w.handle, M, dt[x_local.dtype], ctypes.byref(n)))
+        ws = Workspace.get(w.device, n.value) if n.value else None
+        L.check(L.lib().bq4_linear_ex(w.handle, _ptr(x_local), dt[x_local.dtype], M, x_local.stride(0),
+                                      _ptr(self.bias), L.ACT_NONE, None, ctypes.c_void_p(ex.local[b]), L.DTYPE_F32,
+                                      ex.H, _ptr(ws), ws.numel() if ws is not None else 0, _stream_ptr(w.device)))
+        ex.signal_wait()
+
     def forward_ex(self, x_local: torch.Tensor, out: torch.Tensor, async_op: bool = False):
         """Same, with float16 or float32 activations; the partial sums are
         reduced in ``out``'s dtype.  With ``async_op`` the all-reduce is only
@@ -197,6 +213,16 @@ class PeerExchange:
                                           1 if renorm else 0, ctypes.c_float(eps), _ptr(out), dt[out.dtype],
                                           out.stride(0), _stream_ptr(self.device)))
 
+    def reduce_pull(self, b: int, out: torch.Tensor, renorm: bool, eps: float = 1e-6):
+        """As reduce, reading this rank's rows of every rank's buffer b (each
+        rank's whole partial product, written by forward_local) over peer
+        memory."""
+        dt = {torch.float32: L.DTYPE_F32, torch.float16: L.DTYPE_F16}
+        src = (ctypes.c_void_p * self.size)(*self.peer[b])
+        L.check(L.lib().bq4_reduce_slices_peer(src, self.size, self.rank * self.rows, self.rows, self.H, self.H,
+                                               1 if renorm else 0, ctypes.c_float(eps), _ptr(out), dt[out.dtype],
+                                               out.stride(0), _stream_ptr(self.device)))
+
     def close(self):
         torch.cuda.synchronize(self.device)
         dist.barrier(group=self.group)
@@ -231,7 +257,10 @@ class DiTQ4Stack:
         # partials go to each row's owner through the GEMM epilogue over NVLink
         # peer memory, the owner sums (and renormalises) its rows, and an NCCL
         # all-gather of float16 rows rebuilds the replicated activations
-        # (_forward_p2p); "nccl": a float32 all-reduce of the partials.
+        # (_forward_p2p); "pull": each rank's GEMM writes its partials into
+        # its own shared buffer and each owner reads its rows from every
+        # rank's buffer (same sums in the same order); "nccl": a float32
+        # all-reduce of the partials.
         self.exchange = exchange
         self.group = group
         self._peer = None
@@ -285,7 +314,7 @@ class DiTQ4Stack:
         """The stack on x [M, hidden]; the renormalised float32 output goes to
         ``out`` when given (else an internal buffer reused by the next call)."""
         if self.act_dtype == torch.float16:
-            if self.exchange == "p2p" and self.size > 1:
+            if self.exchange in ("p2p", "pull") and self.size > 1:
                 return self._forward_p2p(x, on_linear, out)
             return self._forward_chained(x, on_linear, out)
         M = x.shape[0]
@@ -389,17 +418,26 @@ class DiTQ4Stack:
             out = self._buf("out32", (M, self.hidden), torch.float32)
         mine = slice(r * R, (r + 1) * R)
         n = len(self.layers)
+        pull = self.exchange == "pull"
         for i, layer in enumerate(self.layers):
             xc = x if i == 0 else xin
             _timed(on_linear, "qkv", lambda: layer["qkv"].forward_ex(xc, out=t))
             v = t[:, qkv_local - hid_local:]
-            _timed(on_linear, "o", lambda: layer["o"].forward_scatter(v, ex, 0))
-            ex.reduce(0, o16[mine], renorm=False)
+            dst = out if i == n - 1 else xin
+            if pull:
+                _timed(on_linear, "o", lambda: layer["o"].forward_local(v, ex, 0))
+                ex.reduce_pull(0, o16[mine], renorm=False)
+            else:
+                _timed(on_linear, "o", lambda: layer["o"].forward_scatter(v, ex, 0))
+                ex.reduce(0, o16[mine], renorm=False)
             dist.all_gather_into_tensor(o16, o16[mine], group=self.group)
             _timed(on_linear, "up", lambda: layer["up"].forward_ex(o16, out=u))
-            _timed(on_linear, "down", lambda: layer["down"].forward_scatter(u, ex, 1))
-            dst = out if i == n - 1 else xin
-            ex.reduce(1, dst[mine], renorm=True)
+            if pull:
+                _timed(on_linear, "down", lambda: layer["down"].forward_local(u, ex, 1))
+                ex.reduce_pull(1, dst[mine], renorm=True)
+            else:
+                _timed(on_linear, "down", lambda: layer["down"].forward_scatter(u, ex, 1))
+                ex.reduce(1, dst[mine], renorm=True)
             dist.all_gather_into_tensor(dst, dst[mine], group=self.group)
         return out
 

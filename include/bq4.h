@@ -434,6 +434,17 @@ BQ4_API bq4_status bq4_set_peer_wait_timeout_ns(uint64_t ns);
 BQ4_API bq4_status bq4_reduce_slices(const float* recv, int32_t nranks, int64_t rows, int64_t H, int64_t ld,
                                      int32_t renorm, float eps, void* out, bq4_dtype out_dtype, int64_t ldo,
                                      bq4_stream_t stream);
+/* The pull form of the exchange: out[r] = sum_s src_ranks[s][(row0 + r) ld ..]
+ * over s = 0..nranks-1 in order, for rows r < rows of H floats (H % 4 == 0,
+ * H <= 8192, ld % 4 == 0, every src_ranks[s] 16-byte aligned), then the
+ * optional renorm, as bq4_reduce_slices.  src_ranks[s] is rank s's own f32
+ * partial product [M][ld] (written by a plain bq4_linear_ex into a buffer
+ * shared with bq4_peer_buffer_alloc / _open), read over peer memory after a
+ * bq4_peer_signal_wait; row0 = rank * rows.  No counterpart in the
+ * reference, which has no multi-GPU code. */
+BQ4_API bq4_status bq4_reduce_slices_peer(const float* const* src_ranks, int32_t nranks, int64_t row0, int64_t rows,
+                                          int64_t H, int64_t ld, int32_t renorm, float eps, void* out,
+                                          bq4_dtype out_dtype, int64_t ldo, bq4_stream_t stream);
 /* bq4_linear_ex with f32 output scattered by row owner (see above):
  * y_ranks[r] = rank r's receive buffer [nranks][M/nranks][ldy] f32 as mapped
  * here; M % nranks == 0.  Workspace as bq4_linear_ex. */

@@ -63,3 +63,35 @@ def test_rowscatter_rows_land_at_their_owner(M, K, N, nranks, rank, x_f16, rng):
             assert rel <= 1e-6, f"owner {r}: rel {rel}"
             others = torch.cat([bufs[r][:rank * R], bufs[r][(rank + 1) * R:]])
             assert bool(torch.isnan(others).all()), f"owner {r}: rows outside this rank's slot were written"
+
+
+@pytest.mark.parametrize("nranks,rank,renorm,f16", [(4, 1, False, True), (8, 7, True, True), (2, 0, True, False)])
+def test_reduce_slices_peer_matches_reduce_slices(nranks, rank, renorm, f16):
+    """bq4_reduce_slices_peer (the pull exchange: rank s's slice is rows
+    [rank R, (rank+1) R) of rank s's own [M][H] partial buffer) against
+    bq4_reduce_slices on the same rows gathered into one [P][R][H] receive
+    buffer: the same sums in the same order, so the same bits.  All "ranks"
+    are buffers on this one device."""
+    R, H = 40, 3072
+    M = nranks * R
+    g = torch.Generator(device=DEV).manual_seed(nranks * 10 + rank)
+    parts = [torch.randn((M, H), generator=g, device=DEV) * 100 for _ in range(nranks)]
+    recv = torch.stack([p[rank * R:(rank + 1) * R] for p in parts]).contiguous()  # [P][R][H]
+    odt = torch.float16 if f16 else torch.float32
+    dt = L.DTYPE_F16 if f16 else L.DTYPE_F32
+    a = torch.empty((R, H), dtype=odt, device=DEV)
+    b = torch.empty((R, H), dtype=odt, device=DEV)
+    stream = ctypes.c_void_p(torch.cuda.current_stream(DEV).cuda_stream)
+    L.check(L.lib().bq4_reduce_slices(ctypes.c_void_p(recv.data_ptr()), nranks, R, H, H, 1 if renorm else 0,
+                                      ctypes.c_float(1e-6), ctypes.c_void_p(a.data_ptr()), dt, H, stream))
+    src = (ctypes.c_void_p * nranks)(*[p.data_ptr() for p in parts])
+    L.check(L.lib().bq4_reduce_slices_peer(src, nranks, rank * R, R, H, H, 1 if renorm else 0, ctypes.c_float(1e-6),
+                                           ctypes.c_void_p(b.data_ptr()), dt, H, stream))
+    torch.cuda.synchronize()
+    q4.poll_device_error()
+    assert torch.equal(a, b)
+    want = sum(p[rank * R:(rank + 1) * R].double() for p in parts)
+    if renorm:
+        want = want / torch.sqrt((want * want).mean(dim=1, keepdim=True) + 1e-6)
+    rel = (torch.linalg.norm(b.double() - want) / torch.linalg.norm(want)).item()
+    assert rel <= (1e-3 if f16 else 1e-6), rel

@@ -8,8 +8,10 @@ adds them in its own order and each f32 sum is then rounded to f16 for the
 next linear, so a last-bit difference can flip an f16 rounding and travel
 through the later layers: the two agree within 2e-3 there, and both stay
 within 5e-3 of the unsharded stack; repeated calls (advancing barrier
-epochs) must give the same bits.  Each rank count runs
-when the host has that many GPUs.
+epochs) must give the same bits.  The pull form of the exchange (each
+rank's GEMM writes its partials locally, each owner reads its rows from
+every rank) agrees with the push form within 2e-3 and repeats its bits.
+Each rank count runs when the host has that many GPUs.
 """
 import os
 import socket
@@ -42,9 +44,12 @@ def _worker(rank, world, port, results):
         x = torch.randn((M, H), generator=g, device=dev)
         p2p = tp.DiTQ4Stack(2, H, QKV, MLP, dev, seed=3, act_dtype=torch.float16, exchange="p2p")
         ar = tp.DiTQ4Stack(2, H, QKV, MLP, dev, seed=3, act_dtype=torch.float16, exchange="nccl")
+        pull = tp.DiTQ4Stack(2, H, QKV, MLP, dev, seed=3, act_dtype=torch.float16, exchange="pull")
         a = p2p.forward(x).clone()
         a2 = p2p.forward(x).clone()
         b = ar.forward(x).clone()
+        pl = pull.forward(x).clone()
+        pl2 = pull.forward(x).clone()
         local = tp.DiTQ4Stack(2, H, QKV, MLP, dev, seed=3, act_dtype=torch.float16, group=tp.LOCAL)
         c = local.forward(x).clone()
         torch.cuda.synchronize(dev)
@@ -52,8 +57,14 @@ def _worker(rank, world, port, results):
         rel = (torch.linalg.norm(a.double() - c.double()) / torch.linalg.norm(c.double())).item()
         d_ar = (torch.linalg.norm(a.double() - b.double()) / torch.linalg.norm(b.double())).item()
         same = bool(torch.equal(a, b)) if world == 2 else d_ar <= 2e-3
+        # the pull exchange adds the partials in the same (rank) order as the push one; its
+        # GEMM is the plain kernel, whose plan may split tiles differently from the row-scatter
+        # one, so a partial's last bits (and through f16 rounding, later layers) may differ
+        d_pull = (torch.linalg.norm(pl.double() - a.double()) / torch.linalg.norm(a.double())).item()
+        same = same and d_pull <= 2e-3 and bool(torch.equal(pl, pl2))
         results[rank] = (same, bool(torch.equal(a, a2)), rel, d_ar, None)
         p2p.close()
+        pull.close()
     except Exception as e:  # reported to the parent
         results[rank] = (False, False, float("nan"), float("nan"), repr(e))
     finally:
@@ -84,6 +95,6 @@ def test_p2p_exchange_matches_allreduce(WORLD):
         same, repeat, rel, d_ar, err = results[r]
         print(f"world {WORLD} rank {r}: p2p vs all-reduce {d_ar:.3e}, p2p vs unsharded {rel:.3e}")
         assert err is None, f"rank {r}: {err}"
-        assert same, f"rank {r}: p2p exchange differs from the all-reduce ({d_ar:.3e})"
+        assert same, f"rank {r}: p2p exchange differs from the all-reduce ({d_ar:.3e}) or from the pull exchange"
         assert repeat, f"rank {r}: repeated calls differ"
         assert rel <= 5e-3, f"rank {r}: rel to unsharded {rel}"
