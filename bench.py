@@ -60,8 +60,9 @@ def parse():
                     help="row-parallel exchange at N > 1: p2p (GEMM epilogue writes each row's partial to its "
                          "owner over NVLink peer memory, owner sums + renormalises, f16 all-gather) or nccl "
                          "(f32 all-reduce of the partials); pull: each rank's GEMM writes its partials locally and "
-                         "each owner reads its rows from every rank over NVLink; auto = p2p (checked against nccl and the unsharded "
-                         "stack on B200 at 2 and 4 ranks, and faster at both; the same code path serves 8)")
+                         "each owner reads its rows from every rank over NVLink; auto = p2p at 2 GPUs and pull "
+                         "above (each the faster one measured on B200; both checked against nccl and the "
+                         "unsharded stack)")
     ap.add_argument("--rows-only", action="store_true", help="print only the per-config rows (1 GPU)")
     ap.add_argument("--config", choices=["stack", "c4"], default="stack",
                     help="c4: BASELINE configs[3], the 1536 px edit projections (M=18432: fused qkv 3072->9216 "
@@ -717,7 +718,9 @@ def run_ours(args):
         _q.set_sm_budget(args.sm_budget)
     exchange = args.tp_exchange
     if exchange == "auto":
-        exchange = "p2p"
+        # measured on B200 (stack, TFLOP/s): 2 GPUs p2p 1531 / pull 1451-1475; 4 GPUs 1671 / 1691;
+        # 8 GPUs 1762 / 1788
+        exchange = "p2p" if world == 2 else "pull"
     if not (world > 1 and args.act_dtype == "f16" and chunks == 1):
         exchange = "nccl"
     stack = tp.DiTQ4Stack(args.blocks, HIDDEN, QKV, MLP, dev, seed=1, block=QBLOCK, group=group,
