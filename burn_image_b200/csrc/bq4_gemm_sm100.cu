@@ -556,24 +556,8 @@ __device__ __forceinline__ void split_reduce_epilogue(const WsArgs& a) {
     }
   const float* part = a.partials + (size_t)tile * SPL * NW * BT * 128;
   const int act = a.act;
-  for (int col = c0 + (int)(threadIdx.x >> 5); col < c1; col += 16) {
-    const int m = mtile * BT + col;
-    if (m >= a.M) break;
-    float v[NW][4];
-#pragma unroll
-    for (int w = 0; w < NW; ++w) {
-      float4 t[kMaxSplit];
-#pragma unroll
-      for (int p = 0; p < kMaxSplit; ++p)
-        if (p < SPL)
-          t[p] = __ldcg(reinterpret_cast<const float4*>(part + (((size_t)p * NW + w) * BT + col) * 128 + r4));
-      v[w][0] = v[w][1] = v[w][2] = v[w][3] = 0.0f;
-#pragma unroll
-      for (int p = 0; p < kMaxSplit; ++p)
-        if (p < SPL) {
-          v[w][0] += t[p].x; v[w][1] += t[p].y; v[w][2] += t[p].z; v[w][3] += t[p].w;
-        }
-    }
+  // bias, activation (or the gated pair) and the store of token m's four features
+  auto emit = [&](int m, const float (&v)[NW][4]) {
     float o[4];
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
@@ -598,6 +582,50 @@ __device__ __forceinline__ void split_reduce_epilogue(const WsArgs& a) {
       for (int i = 0; i < 4; ++i)
         if (n + i < a.N) store_out<SC>(a, m, n + i, o[i]);
     }
+  };
+  int col = c0 + (int)(threadIdx.x >> 5);
+  if constexpr (NW == 1) {
+    // two of the warp's columns (col, col + 16) per round: every split's
+    // loads of both are in flight before either is summed (one L2 latency
+    // per two columns; the sums keep the split order)
+    for (; col + 16 < c1 && mtile * BT + col + 16 < a.M; col += 32) {
+      float4 t0[kMaxSplit], t1[kMaxSplit];
+#pragma unroll
+      for (int p = 0; p < kMaxSplit; ++p)
+        if (p < SPL) {
+          t0[p] = __ldcg(reinterpret_cast<const float4*>(part + ((size_t)p * BT + col) * 128 + r4));
+          t1[p] = __ldcg(reinterpret_cast<const float4*>(part + ((size_t)p * BT + col + 16) * 128 + r4));
+        }
+      float v0[1][4] = {{0.0f, 0.0f, 0.0f, 0.0f}}, v1[1][4] = {{0.0f, 0.0f, 0.0f, 0.0f}};
+#pragma unroll
+      for (int p = 0; p < kMaxSplit; ++p)
+        if (p < SPL) {
+          v0[0][0] += t0[p].x; v0[0][1] += t0[p].y; v0[0][2] += t0[p].z; v0[0][3] += t0[p].w;
+          v1[0][0] += t1[p].x; v1[0][1] += t1[p].y; v1[0][2] += t1[p].z; v1[0][3] += t1[p].w;
+        }
+      emit(mtile * BT + col, v0);
+      emit(mtile * BT + col + 16, v1);
+    }
+  }
+  for (; col < c1; col += 16) {
+    const int m = mtile * BT + col;
+    if (m >= a.M) break;
+    float v[NW][4];
+#pragma unroll
+    for (int w = 0; w < NW; ++w) {
+      float4 t[kMaxSplit];
+#pragma unroll
+      for (int p = 0; p < kMaxSplit; ++p)
+        if (p < SPL)
+          t[p] = __ldcg(reinterpret_cast<const float4*>(part + (((size_t)p * NW + w) * BT + col) * 128 + r4));
+      v[w][0] = v[w][1] = v[w][2] = v[w][3] = 0.0f;
+#pragma unroll
+      for (int p = 0; p < kMaxSplit; ++p)
+        if (p < SPL) {
+          v[w][0] += t[p].x; v[w][1] += t[p].y; v[w][2] += t[p].z; v[w][3] += t[p].w;
+        }
+    }
+    emit(m, v);
   }
 }
 
