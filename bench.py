@@ -56,11 +56,13 @@ def parse():
     ap.add_argument("--chunks", type=int, default=1, help="token chunks of the stack pipeline (each chunk's "
                                                           "all-reduces overlap the other chunks' GEMMs)")
     ap.add_argument("--sm-budget", type=int, default=0, help="cap the SMs a GEMM occupies (0: all)")
-    ap.add_argument("--tp-exchange", choices=["auto", "p2p", "pull", "nccl"], default="auto",
+    ap.add_argument("--tp-exchange", choices=["auto", "p2p", "pull", "bcast", "nccl"], default="auto",
                     help="row-parallel exchange at N > 1: p2p (GEMM epilogue writes each row's partial to its "
                          "owner over NVLink peer memory, owner sums + renormalises, f16 all-gather) or nccl "
                          "(f32 all-reduce of the partials); pull: each rank's GEMM writes its partials locally and "
-                         "each owner reads its rows from every rank over NVLink; auto = p2p at 2 GPUs and pull "
+                         "each owner reads its rows from every rank over NVLink; bcast: pull, with each owner "
+                         "writing its reduced rows into every rank's activations instead of an all-gather; "
+                         "auto = p2p at 2 GPUs and pull "
                          "above (each the faster one measured on B200; both checked against nccl and the "
                          "unsharded stack)")
     ap.add_argument("--rows-only", action="store_true", help="print only the per-config rows (1 GPU)")

@@ -72,6 +72,8 @@ SIGNATURES = {
     "bq4_set_peer_wait_timeout_ns": (_st, [_u64]),
     "bq4_reduce_slices": (_st, [_p, _i32, _i64, _i64, _i64, _i32, ctypes.c_float, _p, _i32, _i64, _p]),
     "bq4_reduce_slices_peer": (_st, [_p, _i32, _i64, _i64, _i64, _i64, _i32, ctypes.c_float, _p, _i32, _i64, _p]),
+    "bq4_reduce_slices_peer_bcast": (_st, [_p, _i32, _i64, _i64, _i64, _i64, _i32, ctypes.c_float, _p, _i32, _i64,
+                                           _p]),
     "bq4_linear_rowscatter": (_st, [_p, _p, _i32, _i64, _i64, _p, _i32, _p, _i32, _i32, _i64, _p, _sz, _p]),
     "bq4_linear_qk_norm_rope": (_st, [_p, _p, _i32, _i64, _i64, _p, _i64, _i64, _i64, _p, _p, ctypes.c_float, _p, _p,
                                       _i64, _p, _i32, _i64, _p, _sz, _p]),

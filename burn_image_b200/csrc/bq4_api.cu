@@ -666,9 +666,31 @@ bq4_status bq4_reduce_slices_peer(const float* const* src_ranks, int32_t nranks,
     if (!src_ranks[r] || !aligned(src_ranks[r], 16))
       return set_error(BQ4_EALIGN, "src_ranks[%d] is NULL or not 16-byte aligned", r);
   if (!aligned(out, out_dtype == BQ4_DTYPE_F16 ? 8 : 16)) return set_error(BQ4_EALIGN, "out misaligned");
-  cudaError_t e = launch_reduce_slices_peer(src_ranks, nranks, row0, rows, H, ld, renorm, eps, out,
+  cudaError_t e = launch_reduce_slices_peer(src_ranks, nranks, row0, rows, H, ld, renorm, eps, out, nullptr,
                                             out_dtype == BQ4_DTYPE_F16, ldo, reinterpret_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? BQ4_OK : check_cuda(e, "reduce_slices_peer launch");
+}
+
+bq4_status bq4_reduce_slices_peer_bcast(const float* const* src_ranks, int32_t nranks, int64_t row0, int64_t rows,
+                                        int64_t H, int64_t ld, int32_t renorm, float eps, void* const* out_ranks,
+                                        bq4_dtype out_dtype, int64_t ldo, bq4_stream_t stream) {
+  if (!src_ranks || !out_ranks) return set_error(BQ4_EINVAL_ARG, "src_ranks/out_ranks is NULL");
+  if (out_dtype != BQ4_DTYPE_F32 && out_dtype != BQ4_DTYPE_F16) return set_error(BQ4_EINVAL_ARG, "dtype unknown");
+  if (nranks < 1 || nranks > BQ4_MAX_PEERS || row0 < 0 || rows <= 0 || H <= 0 || H % 4 || H > 8192 || ld < H ||
+      ld % 4 || ldo < H || ldo % 4)
+    return set_error(BQ4_EINVAL_SHAPE, "nranks=%d row0=%lld rows=%lld H=%lld (H %% 4 == 0, <= 8192) ld=%lld ldo=%lld",
+                     (int)nranks, (long long)row0, (long long)rows, (long long)H, (long long)ld, (long long)ldo);
+  if (renorm && !(eps > 0.0f)) return set_error(BQ4_EINVAL_ARG, "eps must be positive");
+  for (int r = 0; r < nranks; ++r) {
+    if (!src_ranks[r] || !aligned(src_ranks[r], 16))
+      return set_error(BQ4_EALIGN, "src_ranks[%d] is NULL or not 16-byte aligned", r);
+    if (!out_ranks[r] || !aligned(out_ranks[r], out_dtype == BQ4_DTYPE_F16 ? 8 : 16))
+      return set_error(BQ4_EALIGN, "out_ranks[%d] is NULL or misaligned", r);
+  }
+  cudaError_t e = launch_reduce_slices_peer(src_ranks, nranks, row0, rows, H, ld, renorm, eps, out_ranks[0],
+                                            out_ranks, out_dtype == BQ4_DTYPE_F16, ldo,
+                                            reinterpret_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? BQ4_OK : check_cuda(e, "reduce_slices_peer_bcast launch");
 }
 
 bq4_status bq4_linear_rowscatter(const bq4_weight* w, const void* x, bq4_dtype x_dtype, int64_t M, int64_t ldx,

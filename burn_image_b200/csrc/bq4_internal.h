@@ -85,10 +85,12 @@ cudaError_t launch_peer_signal_wait(unsigned* local, unsigned* const* peers, int
 void set_peer_wait_ns(uint64_t ns);
 cudaError_t launch_reduce_slices(const float* recv, int P, int64_t R, int64_t H, int64_t ld, int renorm, float eps,
                                  void* out, int out_f16, int64_t ldo, cudaStream_t s);
-// As launch_reduce_slices with slice s = rows [row0, row0 + R) of src_ranks[s] (pitch ld).
+// As launch_reduce_slices with slice s = rows [row0, row0 + R) of src_ranks[s]
+// (pitch ld); with out_ranks (P pointers), row r of the result goes to
+// out_ranks[q] + (row0 + r) * ldo for every q instead of out.
 cudaError_t launch_reduce_slices_peer(const float* const* src_ranks, int P, int64_t row0, int64_t R, int64_t H,
-                                      int64_t ld, int renorm, float eps, void* out, int out_f16, int64_t ldo,
-                                      cudaStream_t s);
+                                      int64_t ld, int renorm, float eps, void* out, void* const* out_ranks,
+                                      int out_f16, int64_t ldo, cudaStream_t s);
 // QK-norm + RoPE over `heads` heads of hd (even, <= 256) per token; cos/sin
 // NULL skips the rotation, gamma NULL means ones.
 cudaError_t launch_qk_norm_rope(const void* x, int x_f16, int64_t M, int heads, int hd, int64_t ldx,

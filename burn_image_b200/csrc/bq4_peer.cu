@@ -71,6 +71,14 @@ __global__ void peer_signal_wait_kernel(unsigned* local, PeerFlags peers, int nr
 struct SliceSrc {
   const float* p[BQ4_MAX_PEERS];
 };
+// Where the reduced rows go: n == 0: out + r * ldo; else row r of the result
+// to p[q] + (row0 + r) * ldo for every q < n (every rank's copy of the
+// activations, over peer memory).
+struct RowDst {
+  void* p[BQ4_MAX_PEERS];
+  int n;
+  int64_t row0;
+};
 
 // out[r] = sum over s = 0..P-1 (in that order) of slice s, row r, for the R
 // rows this rank owns (rows of H floats at pitch ld), then optionally the
@@ -84,7 +92,7 @@ struct SliceSrc {
 // P remote reads are in flight together.
 template <typename TO, bool kRenorm>
 __global__ void reduce_slices_kernel(const SliceSrc src, int P, int64_t row0, int64_t R, int64_t H, int64_t ld,
-                                     float eps, TO* __restrict__ out, int64_t ldo) {
+                                     float eps, TO* __restrict__ out, int64_t ldo, const RowDst dst) {
   constexpr int kMaxVec = 8;  // H <= 8 * 4 * blockDim.x
   __shared__ float part[32];
   for (int64_t r = blockIdx.x; r < R; r += gridDim.x) {
@@ -122,7 +130,13 @@ __global__ void reduce_slices_kernel(const SliceSrc src, int P, int64_t row0, in
 #pragma unroll
     for (int i = 0; i < kMaxVec; ++i) {
       const int64_t h = ((int64_t)threadIdx.x + (int64_t)i * blockDim.x) * 4;
-      if (h < H) st4(out + r * ldo + h, make_float4(v[i].x * rs, v[i].y * rs, v[i].z * rs, v[i].w * rs));
+      if (h >= H) continue;
+      const float4 o = make_float4(v[i].x * rs, v[i].y * rs, v[i].z * rs, v[i].w * rs);
+      if (dst.n == 0) {
+        st4(out + r * ldo + h, o);
+      } else {
+        for (int q = 0; q < dst.n; ++q) st4(static_cast<TO*>(dst.p[q]) + (dst.row0 + r) * ldo + h, o);
+      }
     }
   }
 }
@@ -144,18 +158,20 @@ cudaError_t launch_peer_signal_wait(unsigned* local, unsigned* const* peers, int
 
 namespace {
 cudaError_t launch_reduce(const SliceSrc& src, int P, int64_t row0, int64_t R, int64_t H, int64_t ld, int renorm,
-                          float eps, void* out, int out_f16, int64_t ldo, cudaStream_t s) {
+                          float eps, void* out, int out_f16, int64_t ldo, const RowDst& dst, cudaStream_t s) {
   const int grid = R < 148 * 8 ? (int)R : 148 * 8;
   if (out_f16) {
+    __half* o = static_cast<__half*>(out);
     if (renorm)
-      reduce_slices_kernel<__half, true><<<grid, 256, 0, s>>>(src, P, row0, R, H, ld, eps, static_cast<__half*>(out), ldo);
+      reduce_slices_kernel<__half, true><<<grid, 256, 0, s>>>(src, P, row0, R, H, ld, eps, o, ldo, dst);
     else
-      reduce_slices_kernel<__half, false><<<grid, 256, 0, s>>>(src, P, row0, R, H, ld, eps, static_cast<__half*>(out), ldo);
+      reduce_slices_kernel<__half, false><<<grid, 256, 0, s>>>(src, P, row0, R, H, ld, eps, o, ldo, dst);
   } else {
+    float* o = static_cast<float*>(out);
     if (renorm)
-      reduce_slices_kernel<float, true><<<grid, 256, 0, s>>>(src, P, row0, R, H, ld, eps, static_cast<float*>(out), ldo);
+      reduce_slices_kernel<float, true><<<grid, 256, 0, s>>>(src, P, row0, R, H, ld, eps, o, ldo, dst);
     else
-      reduce_slices_kernel<float, false><<<grid, 256, 0, s>>>(src, P, row0, R, H, ld, eps, static_cast<float*>(out), ldo);
+      reduce_slices_kernel<float, false><<<grid, 256, 0, s>>>(src, P, row0, R, H, ld, eps, o, ldo, dst);
   }
   note_launch();
   return cudaGetLastError();
@@ -167,16 +183,25 @@ cudaError_t launch_reduce_slices(const float* recv, int P, int64_t R, int64_t H,
   SliceSrc src;
   memset(&src, 0, sizeof(src));
   for (int r = 0; r < P && r < BQ4_MAX_PEERS; ++r) src.p[r] = recv + (int64_t)r * R * ld;
-  return launch_reduce(src, P, 0, R, H, ld, renorm, eps, out, out_f16, ldo, s);
+  RowDst dst;
+  memset(&dst, 0, sizeof(dst));
+  return launch_reduce(src, P, 0, R, H, ld, renorm, eps, out, out_f16, ldo, dst, s);
 }
 
 cudaError_t launch_reduce_slices_peer(const float* const* src_ranks, int P, int64_t row0, int64_t R, int64_t H,
-                                      int64_t ld, int renorm, float eps, void* out, int out_f16, int64_t ldo,
-                                      cudaStream_t s) {
+                                      int64_t ld, int renorm, float eps, void* out, void* const* out_ranks,
+                                      int out_f16, int64_t ldo, cudaStream_t s) {
   SliceSrc src;
   memset(&src, 0, sizeof(src));
   for (int r = 0; r < P && r < BQ4_MAX_PEERS; ++r) src.p[r] = src_ranks[r];
-  return launch_reduce(src, P, row0, R, H, ld, renorm, eps, out, out_f16, ldo, s);
+  RowDst dst;
+  memset(&dst, 0, sizeof(dst));
+  if (out_ranks) {
+    for (int r = 0; r < P && r < BQ4_MAX_PEERS; ++r) dst.p[r] = out_ranks[r];
+    dst.n = P;
+    dst.row0 = row0;
+  }
+  return launch_reduce(src, P, row0, R, H, ld, renorm, eps, out, out_f16, ldo, dst, s);
 }
 
 }  // namespace bq4

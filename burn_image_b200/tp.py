@@ -159,6 +159,16 @@ class RowParallelQ4Linear:
         return None if async_op else out
 
 
+class _DeviceArray:
+    """A device pointer presented through the CUDA array interface, so that
+    torch can view memory it did not allocate (the shared buffers)."""
+
+    def __init__(self, ptr: int, shape, dtype: torch.dtype):
+        typestr = {torch.float16: "<f2", torch.float32: "<f4"}[dtype]
+        self.__cuda_array_interface__ = {"shape": shape, "typestr": typestr, "data": (ptr, False), "version": 3,
+                                         "strides": None}
+
+
 class PeerExchange:
     """Receive buffers and flags shared between the ranks of `group` through
     CUDA IPC (bq4_peer_buffer_*), for the row-parallel exchange over NVLink
@@ -167,12 +177,14 @@ class PeerExchange:
     before it), and one [P] u32 flag array per rank for bq4_peer_signal_wait.
     """
 
-    def __init__(self, device: torch.device, group, rows: int, H: int):
+    def __init__(self, device: torch.device, group, rows: int, H: int, acts: int = 0):
         self.device, self.group = device, group
         self.rank, self.size = _world(group)
         self.rows, self.H = rows, H
         lib = L.lib()
-        sizes = [self.size * rows * H * 4] * 2 + [4 * L.MAX_PEERS]
+        # buffers 0, 1: f32 partials; 2: flags; 3, 3 + acts: [M][H] f16 activation copies that
+        # peers write into (reduce_bcast)
+        sizes = [self.size * rows * H * 4] * 2 + [4 * L.MAX_PEERS] + [self.size * rows * H * 2] * acts
         self.local, handles = [], []
         for n in sizes:
             ptr, h = ctypes.c_void_p(), (ctypes.c_uint8 * L.IPC_HANDLE_BYTES)()
@@ -212,6 +224,20 @@ class PeerExchange:
         L.check(L.lib().bq4_reduce_slices(ctypes.c_void_p(self.local[b]), self.size, self.rows, self.H, self.H,
                                           1 if renorm else 0, ctypes.c_float(eps), _ptr(out), dt[out.dtype],
                                           out.stride(0), _stream_ptr(self.device)))
+
+    def view(self, b: int, shape, dtype: torch.dtype) -> torch.Tensor:
+        """This rank's buffer b as a tensor (no copy; valid until close)."""
+        return torch.as_tensor(_DeviceArray(self.local[b], tuple(shape), dtype), device=self.device)
+
+    def reduce_bcast(self, b: int, dst: int, renorm: bool, eps: float = 1e-6):
+        """As reduce_pull, writing this rank's rows of the result (f16) into
+        every rank's activation buffer dst over peer memory (in place of an
+        all-gather); a signal_wait afterwards makes every rank's copy whole."""
+        src = (ctypes.c_void_p * self.size)(*self.peer[b])
+        outs = (ctypes.c_void_p * self.size)(*self.peer[dst])
+        L.check(L.lib().bq4_reduce_slices_peer_bcast(src, self.size, self.rank * self.rows, self.rows, self.H, self.H,
+                                                     1 if renorm else 0, ctypes.c_float(eps), outs, L.DTYPE_F16,
+                                                     self.H, _stream_ptr(self.device)))
 
     def reduce_pull(self, b: int, out: torch.Tensor, renorm: bool, eps: float = 1e-6):
         """As reduce, reading this rank's rows of every rank's buffer b (each
@@ -259,8 +285,10 @@ class DiTQ4Stack:
         # all-gather of float16 rows rebuilds the replicated activations
         # (_forward_p2p); "pull": each rank's GEMM writes its partials into
         # its own shared buffer and each owner reads its rows from every
-        # rank's buffer (same sums in the same order); "nccl": a float32
-        # all-reduce of the partials.
+        # rank's buffer (same sums in the same order); "bcast": "pull" with
+        # each owner writing its reduced rows into every rank's copy of the
+        # activations instead of an all-gather; "nccl": a float32 all-reduce
+        # of the partials.
         self.exchange = exchange
         self.group = group
         self._peer = None
@@ -314,7 +342,7 @@ class DiTQ4Stack:
         """The stack on x [M, hidden]; the renormalised float32 output goes to
         ``out`` when given (else an internal buffer reused by the next call)."""
         if self.act_dtype == torch.float16:
-            if self.exchange in ("p2p", "pull") and self.size > 1:
+            if self.exchange in ("p2p", "pull", "bcast") and self.size > 1:
                 return self._forward_p2p(x, on_linear, out)
             return self._forward_chained(x, on_linear, out)
         M = x.shape[0]
@@ -403,22 +431,27 @@ class DiTQ4Stack:
         if M % P:
             raise ValueError(f"p2p exchange: M={M} not divisible by {P} ranks")
         R = M // P
+        bcast = self.exchange == "bcast"
+        pull = self.exchange in ("pull", "bcast")
         if self._peer is None or self._peer.rows != R:
             if self._peer is not None:
                 self._peer.close()
-            self._peer = PeerExchange(self.device, self.group, R, self.hidden)
+            self._peer = PeerExchange(self.device, self.group, R, self.hidden, acts=2 if bcast else 0)
         ex = self._peer
         qkv_local, hid_local, mlp_local = self.qkv // P, self.hidden // P, self.mlp // P
         f16 = torch.float16
-        xin = self._buf("x16", (M, self.hidden), f16)
         t = self._buf("qkv16", (M, qkv_local), f16)
-        o16 = self._buf("o16", (M, self.hidden), f16)
+        if bcast:  # peers write their rows of o and of the next block's input straight into these
+            o16 = ex.view(3, (M, self.hidden), f16)
+            xin = ex.view(4, (M, self.hidden), f16)
+        else:
+            o16 = self._buf("o16", (M, self.hidden), f16)
+            xin = self._buf("x16", (M, self.hidden), f16)
         u = self._buf("up16", (M, mlp_local), f16)
         if out is None:
             out = self._buf("out32", (M, self.hidden), torch.float32)
         mine = slice(r * R, (r + 1) * R)
         n = len(self.layers)
-        pull = self.exchange == "pull"
         for i, layer in enumerate(self.layers):
             xc = x if i == 0 else xin
             _timed(on_linear, "qkv", lambda: layer["qkv"].forward_ex(xc, out=t))
@@ -426,19 +459,29 @@ class DiTQ4Stack:
             dst = out if i == n - 1 else xin
             if pull:
                 _timed(on_linear, "o", lambda: layer["o"].forward_local(v, ex, 0))
-                ex.reduce_pull(0, o16[mine], renorm=False)
+                if bcast:
+                    ex.reduce_bcast(0, 3, renorm=False)
+                    ex.signal_wait()
+                else:
+                    ex.reduce_pull(0, o16[mine], renorm=False)
             else:
                 _timed(on_linear, "o", lambda: layer["o"].forward_scatter(v, ex, 0))
                 ex.reduce(0, o16[mine], renorm=False)
-            dist.all_gather_into_tensor(o16, o16[mine], group=self.group)
+            if not bcast:
+                dist.all_gather_into_tensor(o16, o16[mine], group=self.group)
             _timed(on_linear, "up", lambda: layer["up"].forward_ex(o16, out=u))
             if pull:
                 _timed(on_linear, "down", lambda: layer["down"].forward_local(u, ex, 1))
-                ex.reduce_pull(1, dst[mine], renorm=True)
+                if bcast and i < n - 1:
+                    ex.reduce_bcast(1, 4, renorm=True)
+                    ex.signal_wait()
+                else:
+                    ex.reduce_pull(1, dst[mine], renorm=True)
             else:
                 _timed(on_linear, "down", lambda: layer["down"].forward_scatter(u, ex, 1))
                 ex.reduce(1, dst[mine], renorm=True)
-            dist.all_gather_into_tensor(dst, dst[mine], group=self.group)
+            if not (bcast and i < n - 1):
+                dist.all_gather_into_tensor(dst, dst[mine], group=self.group)
         return out
 
     def close(self):

@@ -445,6 +445,17 @@ BQ4_API bq4_status bq4_reduce_slices(const float* recv, int32_t nranks, int64_t 
 BQ4_API bq4_status bq4_reduce_slices_peer(const float* const* src_ranks, int32_t nranks, int64_t row0, int64_t rows,
                                           int64_t H, int64_t ld, int32_t renorm, float eps, void* out,
                                           bq4_dtype out_dtype, int64_t ldo, bq4_stream_t stream);
+/* bq4_reduce_slices_peer that writes the reduced rows into every rank's copy
+ * of the activations instead of one local output: row r of the result goes
+ * to out_ranks[q] + (row0 + r) * ldo for q = 0..nranks-1 (rank q's [M][ldo]
+ * buffer, shared with bq4_peer_buffer_alloc / _open), which replaces the
+ * all-gather that follows the reduction; a bq4_peer_signal_wait afterwards
+ * tells every rank that its copy is complete.  No counterpart in the
+ * reference, which has no multi-GPU code. */
+BQ4_API bq4_status bq4_reduce_slices_peer_bcast(const float* const* src_ranks, int32_t nranks, int64_t row0,
+                                                int64_t rows, int64_t H, int64_t ld, int32_t renorm, float eps,
+                                                void* const* out_ranks, bq4_dtype out_dtype, int64_t ldo,
+                                                bq4_stream_t stream);
 /* bq4_linear_ex with f32 output scattered by row owner (see above):
  * y_ranks[r] = rank r's receive buffer [nranks][M/nranks][ldy] f32 as mapped
  * here; M % nranks == 0.  Workspace as bq4_linear_ex. */

@@ -95,3 +95,28 @@ def test_reduce_slices_peer_matches_reduce_slices(nranks, rank, renorm, f16):
         want = want / torch.sqrt((want * want).mean(dim=1, keepdim=True) + 1e-6)
     rel = (torch.linalg.norm(b.double() - want) / torch.linalg.norm(want)).item()
     assert rel <= (1e-3 if f16 else 1e-6), rel
+
+
+@pytest.mark.parametrize("nranks,rank,renorm", [(4, 2, False), (8, 0, True)])
+def test_reduce_slices_peer_bcast_writes_every_copy(nranks, rank, renorm):
+    """bq4_reduce_slices_peer_bcast writes this rank's reduced rows into every
+    rank's [M][H] f16 activation copy at rows [rank R, (rank+1) R), with the
+    bits bq4_reduce_slices_peer gives, and leaves every other row alone."""
+    R, H = 24, 1024
+    M = nranks * R
+    g = torch.Generator(device=DEV).manual_seed(nranks + 100 * rank)
+    parts = [torch.randn((M, H), generator=g, device=DEV) for _ in range(nranks)]
+    src = (ctypes.c_void_p * nranks)(*[p.data_ptr() for p in parts])
+    stream = ctypes.c_void_p(torch.cuda.current_stream(DEV).cuda_stream)
+    ref = torch.empty((R, H), dtype=torch.float16, device=DEV)
+    L.check(L.lib().bq4_reduce_slices_peer(src, nranks, rank * R, R, H, H, 1 if renorm else 0, ctypes.c_float(1e-6),
+                                           ctypes.c_void_p(ref.data_ptr()), L.DTYPE_F16, H, stream))
+    copies = [torch.full((M, H), float("nan"), dtype=torch.float16, device=DEV) for _ in range(nranks)]
+    outs = (ctypes.c_void_p * nranks)(*[c.data_ptr() for c in copies])
+    L.check(L.lib().bq4_reduce_slices_peer_bcast(src, nranks, rank * R, R, H, H, 1 if renorm else 0,
+                                                 ctypes.c_float(1e-6), outs, L.DTYPE_F16, H, stream))
+    torch.cuda.synchronize()
+    q4.poll_device_error()
+    for c in copies:
+        assert torch.equal(c[rank * R:(rank + 1) * R], ref)
+        assert bool(torch.isnan(torch.cat([c[:rank * R], c[(rank + 1) * R:]])).all())

@@ -10,7 +10,9 @@ through the later layers: the two agree within 2e-3 there, and both stay
 within 5e-3 of the unsharded stack; repeated calls (advancing barrier
 epochs) must give the same bits.  The pull form of the exchange (each
 rank's GEMM writes its partials locally, each owner reads its rows from
-every rank) agrees with the push form within 2e-3 and repeats its bits.
+every rank) agrees with the push form within 2e-3 and repeats its bits;
+with the owners writing their rows into every rank's activations in place
+of the all-gather ("bcast") it gives the pull form's bits.
 Each rank count runs when the host has that many GPUs.
 """
 import os
@@ -50,6 +52,9 @@ def _worker(rank, world, port, results):
         b = ar.forward(x).clone()
         pl = pull.forward(x).clone()
         pl2 = pull.forward(x).clone()
+        bc = tp.DiTQ4Stack(2, H, QKV, MLP, dev, seed=3, act_dtype=torch.float16, exchange="bcast")
+        bo = bc.forward(x).clone()
+        bo2 = bc.forward(x).clone()
         local = tp.DiTQ4Stack(2, H, QKV, MLP, dev, seed=3, act_dtype=torch.float16, group=tp.LOCAL)
         c = local.forward(x).clone()
         torch.cuda.synchronize(dev)
@@ -62,9 +67,12 @@ def _worker(rank, world, port, results):
         # one, so a partial's last bits (and through f16 rounding, later layers) may differ
         d_pull = (torch.linalg.norm(pl.double() - a.double()) / torch.linalg.norm(a.double())).item()
         same = same and d_pull <= 2e-3 and bool(torch.equal(pl, pl2))
+        # the broadcasting reduction only replaces the all-gather: the same bits as pull
+        same = same and bool(torch.equal(bo, pl)) and bool(torch.equal(bo, bo2))
         results[rank] = (same, bool(torch.equal(a, a2)), rel, d_ar, None)
         p2p.close()
         pull.close()
+        bc.close()
     except Exception as e:  # reported to the parent
         results[rank] = (False, False, float("nan"), float("nan"), repr(e))
     finally:
