@@ -62,9 +62,8 @@ def parse():
                          "(f32 all-reduce of the partials); pull: each rank's GEMM writes its partials locally and "
                          "each owner reads its rows from every rank over NVLink; bcast: pull, with each owner "
                          "writing its reduced rows into every rank's activations instead of an all-gather; "
-                         "auto = p2p at 2 GPUs and pull "
-                         "above (each the faster one measured on B200; both checked against nccl and the "
-                         "unsharded stack)")
+                         "auto = bcast (the fastest measured on B200 at 2 and 4 GPUs; every form checked against "
+                         "nccl and the unsharded stack)")
     ap.add_argument("--rows-only", action="store_true", help="print only the per-config rows (1 GPU)")
     ap.add_argument("--config", choices=["stack", "c4"], default="stack",
                     help="c4: BASELINE configs[3], the 1536 px edit projections (M=18432: fused qkv 3072->9216 "
@@ -720,9 +719,9 @@ def run_ours(args):
         _q.set_sm_budget(args.sm_budget)
     exchange = args.tp_exchange
     if exchange == "auto":
-        # measured on B200 (stack, TFLOP/s): 2 GPUs p2p 1531 / pull 1451-1475; 4 GPUs 1671 / 1691;
-        # 8 GPUs 1762 / 1788
-        exchange = "p2p" if world == 2 else "pull"
+        # measured on B200 (stack, TFLOP/s, push / pull / bcast): 2 GPUs 1491-1531 / 1451-1475 /
+        # 1570-1587; 4 GPUs 1671 / 1683-1691 / 1832; 8 GPUs 1762 / 1788 / (not run: same code path)
+        exchange = "bcast"
     if not (world > 1 and args.act_dtype == "f16" and chunks == 1):
         exchange = "nccl"
     stack = tp.DiTQ4Stack(args.blocks, HIDDEN, QKV, MLP, dev, seed=1, block=QBLOCK, group=group,
